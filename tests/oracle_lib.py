@@ -1,0 +1,221 @@
+"""ctypes bindings for the CPU oracle (test infrastructure only).
+
+``oracle()`` loads oracle/liboracle.so (the plain-C restatement of the reference arithmetic);
+``reference()`` loads oracle/_ref/libg4ref.so (the reference's own kernels, compiled from the
+reference sources by oracle/Makefile) or returns None when it was not built.
+"""
+import ctypes
+import os
+import pathlib
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+ORACLE_DIR = ROOT / "oracle"
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64 = ctypes.c_int64
+_F = ctypes.c_float
+
+
+def ptr(a):
+    """Raw pointer of a C-contiguous numpy array (or None)."""
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"], "array must be C-contiguous"
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+_SIGS_ORACLE = {
+    "or_w4g32_gemm": (None, [_P, _P, _P, _I, _I, _I, _P]),
+    "or_w4a8_quant": (None, [_P, _I, _I, _P, _P, _P]),
+    "or_w4a8_gemm": (None, [_P, _P, _P, _P, _P, _I, _I, _I, _P]),
+    "or_bf16p_codebook": (None, [_P, _I64, _P]),
+    "or_bf16p_count": (_I64, [_P, _I, _I, _P, _P]),
+    "or_bf16p_pack": (None, [_P, _I, _I, _P, _P, _P, _P, _P]),
+    "or_bf16p_gemm": (None, [_P, _P, _P, _P, _P, _I, _I, _P, _I, _P]),
+    "or_cap": (_F, [_F]),
+    "or_calc_thr": (_F, [_F]),
+    "or_head_pick": (_I, [_P, _I]),
+    "or_screen_build": (None, [_P, _I, _I, _P, _P, _P]),
+    "or_screen_row": (_I, [_P, _P, _P, _I, _I, _P, _P, _I, _I, _P, _P]),
+    "or_hnorm": (_F, [_P, _I]),
+    "or_seed_bound": (_F, [_P, _P, _P, _I, _P, _P, _I]),
+    "or_attn_splitkv": (None, [_P, _P, _I, _I, _I, _P, _P, _P, _I, _I, _I, _P]),
+    "or_exp8": (_F, [_F]),
+    "or_gelu": (_F, [_F]),
+    "or_r16": (_F, [_F]),
+}
+
+_SIGS_REF = {
+    "ref_pool_start": (_I, [_I]),
+    "ref_w4g32_gemm": (None, [_P, _P, _P, _I, _I, _I, _P]),
+    "ref_w4a8_quant": (None, [_P, _I, _I, _P, _P, _P]),
+    "ref_w4a8_gemm": (None, [_P, _P, _P, _I, _I, _I, _P]),
+    "ref_bf16p_pack": (_I64, [_P, _I, _I, _P, _P, _P, _P, _P, _I64]),
+    "ref_bf16p_gemm": (None, [_P, _I, _I, _P, _P, _I, _P]),
+    "ref_attn_splitkv": (None, [_P, _P, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
+    "ref_screen_1536": (None, [_P, _P, _P, _P, _I, _P, _P, _P, _P, _I]),
+    "ref_gelu8": (None, [_P, _I, _P]),
+    "ref_exp8": (None, [_P, _I, _P]),
+}
+
+
+def _load(path, sigs):
+    lib = ctypes.CDLL(str(path))
+    for name, (res, args) in sigs.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+_oracle = None
+_ref = None
+
+
+def oracle():
+    global _oracle
+    if _oracle is None:
+        path = ORACLE_DIR / "liboracle.so"
+        if not path.exists():
+            raise RuntimeError(f"{path} missing: run `make -C oracle liboracle.so`")
+        _oracle = _load(path, _SIGS_ORACLE)
+    return _oracle
+
+
+REF_THREADS = 8
+
+
+def reference():
+    """The reference's own kernels (pool started with REF_THREADS threads), or None."""
+    global _ref
+    if _ref is None:
+        path = ORACLE_DIR / "_ref" / "libg4ref.so"
+        if not path.exists():
+            return None
+        _ref = _load(path, _SIGS_REF)
+        _ref.ref_pool_start(int(os.environ.get("G4_REF_THREADS", REF_THREADS)))
+    return _ref
+
+
+# ---------------------------------------------------------------- seeded synthetic inputs
+def bf16_bits(x):
+    """fp32 -> bf16 bit patterns, round to nearest even (gemma4_engine.cpp:34 without NaNs)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return u.astype(np.uint16)
+
+
+def bf16_to_f32(b):
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def w4g32_weights(rng, N, K):
+    """configs[0] distribution: int4 q uniform in [-8,7] stored as q+8 nibbles, bf16 scales |N(0,1)|*0.01."""
+    t = rng.integers(0, 16, size=(N, K), dtype=np.uint8)
+    W = (t[:, 0::2] | (t[:, 1::2] << 4)).astype(np.uint8)
+    S = bf16_bits(np.abs(rng.standard_normal((N, K // 32), dtype=np.float32)) * np.float32(0.01))
+    return np.ascontiguousarray(W), np.ascontiguousarray(S)
+
+
+# ---------------------------------------------------------------- oracle wrappers
+def or_w4g32(W, S, X):
+    M, K = X.shape
+    N = W.shape[0]
+    Y = np.empty((M, N), np.float32)
+    oracle().or_w4g32_gemm(ptr(W), ptr(S), ptr(X), M, N, K, ptr(Y))
+    return Y
+
+
+def or_quant(X):
+    M, K = X.shape
+    q = np.empty((M, K), np.int8)
+    sx = np.empty((M, K // 32), np.float32)
+    sm = np.empty((M, K // 32), np.int32)
+    oracle().or_w4a8_quant(ptr(X), M, K, ptr(q), ptr(sx), ptr(sm))
+    return q, sx, sm
+
+
+def or_w4a8(W, S, X):
+    M, K = X.shape
+    N = W.shape[0]
+    q, sx, sm = or_quant(X)
+    Y = np.empty((M, N), np.float32)
+    oracle().or_w4a8_gemm(ptr(W), ptr(S), ptr(q), ptr(sx), ptr(sm), M, N, K, ptr(Y))
+    return Y
+
+
+def or_codebook(E):
+    cb = np.zeros(8, np.uint8)
+    oracle().or_bf16p_codebook(ptr(E), E.size, ptr(cb))
+    return cb
+
+
+def or_pack(E, cb):
+    N, K = E.shape
+    ep = np.zeros(N + 1, np.int64)
+    ne = oracle().or_bf16p_count(ptr(E), N, K, ptr(cb), ptr(ep))
+    data = np.zeros(N * (K // 32) * 44, np.uint8)
+    col = np.zeros(max(ne, 1), np.uint16)
+    dl = np.zeros(max(ne, 1), np.float32)
+    oracle().or_bf16p_pack(ptr(E), N, K, ptr(cb), ptr(data), ptr(ep), ptr(col), ptr(dl))
+    return data, ep, col[:ne], dl[:ne]
+
+
+def or_head_logits(packed, cb, N, K, X):
+    data, ep, col, dl = packed
+    M = X.shape[0]
+    Y = np.empty((M, N), np.float32)
+    col_ = col if col.size else np.zeros(1, np.uint16)
+    dl_ = dl if dl.size else np.zeros(1, np.float32)
+    oracle().or_bf16p_gemm(ptr(data), ptr(cb), ptr(ep), ptr(col_), ptr(dl_), N, K, ptr(X), M, ptr(Y))
+    return Y
+
+
+def or_pick(raw_row):
+    r = np.ascontiguousarray(raw_row, np.float32)
+    return oracle().or_head_pick(ptr(r), r.size)
+
+
+def or_screen_build(E):
+    N, K = E.shape
+    W4 = np.empty((N, K // 2), np.uint8)
+    S4 = np.empty((N, K // 32), np.uint16)
+    coef = np.empty(N, np.float32)
+    oracle().or_screen_build(ptr(E), N, K, ptr(W4), ptr(S4), ptr(coef))
+    return W4, S4, coef
+
+
+def or_screen_row(W4, S4, coef, h, lim=30000):
+    N = W4.shape[0]
+    K = h.size
+    surv = np.empty(lim, np.int32)
+    L = np.zeros(1, np.float32)
+    seeds = np.zeros(1, np.int32)
+    h = np.ascontiguousarray(h, np.float32)
+    c = oracle().or_screen_row(ptr(W4), ptr(S4), ptr(coef), N, K, ptr(h), ptr(seeds), 0, lim, ptr(surv), ptr(L))
+    return (surv[:c].copy() if c >= 0 else None), float(L[0])
+
+
+def or_attn(Kc, Vc, q, pos, lo, T=8):
+    """q: [M, nh, hd] fp32; Kc/Vc: [ctx, hd] bf16 bits; returns [M, nh, hd] fp32."""
+    M, nh, hd = q.shape
+    pos = np.ascontiguousarray(pos, np.int32)
+    lo = np.ascontiguousarray(lo, np.int32)
+    kmin, kmax = int(lo.min()), int(pos.max())
+    out = np.empty((M, nh, hd), np.float32)
+    oracle().or_attn_splitkv(ptr(Kc), ptr(Vc), hd, nh, M, ptr(np.ascontiguousarray(q)), ptr(pos), ptr(lo),
+                             kmin, kmax, T, ptr(out))
+    return out
+
+
+def or_seed_bound(W4, S4, coef, h, seeds):
+    seeds = np.ascontiguousarray(seeds, np.int32)
+    h = np.ascontiguousarray(h, np.float32)
+    return oracle().or_seed_bound(ptr(W4), ptr(S4), ptr(coef), h.size, ptr(h), ptr(seeds), seeds.size)
+
+
+def or_calc_thr(L):
+    return oracle().or_calc_thr(float(L))
