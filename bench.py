@@ -1,0 +1,349 @@
+"""Benchmark driver (one JSON line on stdout from rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl g4|reference] [--workload NAME]
+
+Workloads:
+  gemv   configs[0]: one W4G32 GEMV, 8192 x 2048 int4 weights, x ~ N(0,1), M = 1.  A step is one
+         GEMV over the next of 64 rotating weight copies (604 MB, > 4x the 126 MB L2), so every
+         step streams its weights from HBM.
+
+The g4 arm times the sm_100a kernels with CUDA events on the launching stream (inputs resident
+in HBM); its `e2e` key repeats the workload through the C ABI from pinned host buffers, with the
+host->device copy of x and the device->host read of y inside every step.  `--impl reference`
+times the reference's own AVX2 kernels (oracle/_ref, compiled from the reference sources) on the
+host's cores for the same workload.  Under torchrun every rank runs its own replica (no data-path
+collective); the value is the sum over ranks and the time the max over ranks.
+"""
+import argparse
+import ctypes
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "gemma4-e2b-laptop-cpu_b200"))
+sys.path.insert(0, str(ROOT / "tests"))
+
+METRIC = "greedy spec-decode tok/s @6.8k ctx; W4G32 GEMV HBM GB/s vs B200 peak"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<name>.md, or None."""
+    p = ROOT / "profiles" / f"{name}.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples (every 200 ms) during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = None
+
+    def __enter__(self):
+        self.out = tempfile.TemporaryFile(mode="w+")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        if self.proc is None:
+            return None
+        self.out.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- distributed
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_pg(world, local):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    if world > 1 and not dist.is_initialized():
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return dist if world > 1 else None
+
+
+def max_over_ranks(x, dist_):
+    if dist_ is None:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist_.all_reduce(t, op=dist_.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist_):
+    if dist_ is not None:
+        dist_.barrier()
+
+
+# --------------------------------------------------------------------------- gemv workload
+N_CFG0, K_CFG0, NCOPY = 8192, 2048, 64
+GEMV_BYTES = N_CFG0 * K_CFG0 // 2 + N_CFG0 * (K_CFG0 // 32) * 2 + K_CFG0 * 4 + N_CFG0 * 4  # 9,478,144
+
+
+def gemv_inputs(seed=0):
+    from oracle_lib import w4g32_weights
+    rng = np.random.default_rng(seed)
+    W, S = w4g32_weights(rng, N_CFG0, K_CFG0)
+    X = rng.standard_normal((1, K_CFG0), dtype=np.float32)
+    return W, S, X
+
+
+def run_gemv_g4(args, world, rank, local):
+    import torch
+    import g4
+    torch.cuda.set_device(local)
+    dist_ = init_pg(world, local)
+    W, S, X = gemv_inputs(rank)
+    Wd = torch.from_numpy(W).cuda()
+    Wp0 = g4.w4_pack(Wd)
+    Sd0 = torch.from_numpy(S).cuda()
+    Wps = [Wp0] + [Wp0.clone() for _ in range(NCOPY - 1)]
+    Sds = [Sd0] + [Sd0.clone() for _ in range(NCOPY - 1)]
+    Xd = torch.from_numpy(X).cuda()
+    Y = torch.empty((1, N_CFG0), device="cuda")
+    lib = g4.lib()
+    stream = torch.cuda.Stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    xp, yp = ctypes.c_void_p(Xd.data_ptr()), ctypes.c_void_p(Y.data_ptr())
+    wps = [ctypes.c_void_p(t.data_ptr()) for t in Wps]
+    sps = [ctypes.c_void_p(t.data_ptr()) for t in Sds]
+
+    def step(i):
+        rc = lib.g4_w4g32_gemm(wps[i % NCOPY], sps[i % NCOPY], xp, None, 1, N_CFG0, K_CFG0, yp, N_CFG0, sp)
+        if rc:
+            raise RuntimeError(lib.g4_last_error().decode())
+
+    # the K timed steps are launched as one CUDA graph (no host launch gaps between kernels)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(args.steps):
+            step(i)
+    with torch.cuda.stream(stream):
+        graph.replay()  # warm replay
+    torch.cuda.synchronize()
+    barrier(dist_)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # nvidia-smi samples every 200 ms, so the timed replay sits in the middle of a ~1.2 s window of
+    # back-to-back replays of the same graph, and the clock record covers that window.
+    t_one = time.perf_counter()
+    with torch.cuda.stream(stream):
+        graph.replay()
+    torch.cuda.synchronize()
+    t_one = max(time.perf_counter() - t_one, 1e-5)
+    roll = max(1, int(0.6 / t_one))
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            for _ in range(roll):
+                graph.replay()
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            for _ in range(roll):
+                graph.replay()
+        torch.cuda.synchronize()
+    barrier(dist_)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms, dist_)
+    del graph
+
+    # e2e: the same GEMV through the C ABI from pinned host buffers, H2D x + D2H y every step
+    xh = torch.from_numpy(X).pin_memory()
+    yh = torch.empty((1, N_CFG0), dtype=torch.float32).pin_memory()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            Xd.copy_(xh, non_blocking=True)
+            step(i)
+            yh.copy_(Y, non_blocking=True)
+            stream.synchronize()
+        barrier(dist_)
+        t0 = time.perf_counter()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for i in range(args.steps):
+            Xd.copy_(xh, non_blocking=True)
+            step(i)
+            yh.copy_(Y, non_blocking=True)
+            stream.synchronize()
+        f1.record(stream)
+        torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), dist_)
+    wall_ms = (time.perf_counter() - t0) * 1e3
+    ok = np.array_equal(yh.numpy(), Y.cpu().numpy())
+    out = None
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        per_gpu_gbs = GEMV_BYTES * args.steps / (ms / 1e3) / 1e9
+        out = {
+            "metric": METRIC, "value": GEMV_BYTES * args.steps * world / (ms_max / 1e3) / 1e9, "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded int4 weights uniform in [-8,7], bf16 scales |N(0,1)|*0.01, x ~ N(0,1))",
+            "config": {"workload": "configs[0] W4G32 GEMV 8192x2048, M=1", "N": N_CFG0, "K": K_CFG0,
+                       "timing": "K launches replayed as one CUDA graph, CUDA events on its stream",
+                       "bytes_per_step": GEMV_BYTES, "l2": f"{NCOPY} rotating weight copies "
+                       f"({NCOPY * GEMV_BYTES / 1e6:.0f} MB > L2)", "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "achieved": per_gpu_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": per_gpu_gbs / peak, "peak_kind": peak_kind,
+                         "traffic": profile_traffic("w4g32_gemv_cfg0"), "kernel": "k_w4g32<1>"},
+            "e2e": {"value": GEMV_BYTES * args.steps * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": K_CFG0 * 4, "d2h_bytes_per_step": N_CFG0 * 4,
+                    "wall_ms": wall_ms, "result_matches_device": bool(ok)},
+            "gpu_launches": args.steps,
+            "clocks": dict(clk.summary() or {}, window="1.2 s of back-to-back replays around the timed one"),
+        }
+    return out, dist_
+
+
+def ref_lib():
+    from oracle_lib import reference
+    return reference()
+
+
+def cpu_gemv_reference(seconds=10.0, max_calls=2000):
+    """The reference's own W4G32 path (lin_task over its thread pool) on the host's cores, over
+    rotating weight copies larger than the last-level cache."""
+    from oracle_lib import ptr
+    os.environ.setdefault("G4_REF_THREADS", str(min(16, os.cpu_count())))
+    ref = ref_lib()
+    if ref is None:
+        return None
+    W, S, X = gemv_inputs(0)
+    ncopy = 32
+    Ws = [W.copy() for _ in range(ncopy)]
+    Ss = [S.copy() for _ in range(ncopy)]
+    Y = np.empty((1, N_CFG0), np.float32)
+    for i in range(5):
+        ref.ref_w4g32_gemm(ptr(Ws[i % ncopy]), ptr(Ss[i % ncopy]), ptr(X), 1, N_CFG0, K_CFG0, ptr(Y))
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_calls and time.perf_counter() - t0 < seconds:
+        ref.ref_w4g32_gemm(ptr(Ws[n % ncopy]), ptr(Ss[n % ncopy]), ptr(X), 1, N_CFG0, K_CFG0, ptr(Y))
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": GEMV_BYTES * n / dt / 1e9, "unit": "GB/s", "cores": int(os.environ["G4_REF_THREADS"]),
+            "kind": "reference", "calls": n, "ms_per_call": dt / n * 1e3,
+            "sample": f"{n} GEMV calls over {ncopy} rotating weight copies ({ncopy * GEMV_BYTES / 1e6:.0f} MB), "
+                      f"reference lin_task via its pool (oracle/_ref, AVX2)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
+    ap.add_argument("--workload", default="gemv", choices=["gemv"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup()
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        os.environ.setdefault("G4_REF_THREADS", str(min(16, os.cpu_count())))
+        per_step = []
+        res = None
+        for i in range(args.warmup + args.steps):
+            r = cpu_gemv_reference(seconds=1.0, max_calls=50)
+            if r is None:
+                print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libg4ref.so was not built "
+                                  "(needs the reference sources at build time)"}))
+                return
+            if i >= args.warmup:
+                per_step.append(r)
+            res = r
+        value = statistics.median(r["value"] for r in per_step)
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(r["ms_per_call"] for r in per_step),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "configs[0] W4G32 GEMV 8192x2048, M=1", "N": N_CFG0,
+                                            "K": K_CFG0, "bytes_per_step": GEMV_BYTES},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": res["cores"], "kind": "reference",
+                             "sample": res["sample"]},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    out, dist_ = run_gemv_g4(args, world, rank, local)
+    if rank == 0:
+        if not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_gemv_reference()
+        print(json.dumps(out))
+    if dist_ is not None:
+        dist_.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,39 @@
+// Error reporting and version for the C ABI (include/g4.h).
+#include "g4_api.h"
+#include <cstring>
+
+namespace g4 {
+static thread_local char g_msg[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof g_msg, fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return G4_OK;
+}
+}  // namespace g4
+
+extern "C" const char* g4_last_error(void) { return g4::g_msg; }
+extern "C" int g4_abi_version(void) { return 1; }
+
+namespace g4 {
+unsigned status_read_linear(bool reset);
+}
+
+// OR of the device status words of all kernel files on the current device; reset clears them.
+extern "C" int g4_device_status(unsigned* out, int reset) {
+  if (!out) return g4::set_error(G4_ERR_INVALID, "g4_device_status: null pointer");
+  unsigned v = 0;
+  v |= g4::status_read_linear(reset != 0);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return g4::set_error(G4_ERR_CUDA, "g4_device_status: %s", cudaGetErrorString(e));
+  *out = v;
+  return G4_OK;
+}

@@ -1,0 +1,18 @@
+// Host-side helpers shared by the C-ABI entry points: thread-local error message and the checks
+// every entry point runs before it launches anything.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdarg>
+#include <cstdio>
+#include "g4.h"
+
+namespace g4 {
+int set_error(int code, const char* fmt, ...);
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+// After a launch: turn a launch error into G4_ERR_CUDA with the kernel's name.
+int check_launch(const char* what);
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+}  // namespace g4
+
+#define G4_REQUIRE(cond, ...) \
+  do { if (!(cond)) return ::g4::set_error(G4_ERR_INVALID, __VA_ARGS__); } while (0)

@@ -1,0 +1,472 @@
+// W4G32 and W4A8 linears for decode and draft verification (M <= 8 activation rows).
+//
+// Both GEMVs stream the int4 weights once from HBM in the device layout made by g4_w4_pack
+// (per 32-group, byte b holds element b in its low nibble and element 16+b in its high
+// nibble).  That one layout serves both kernels:
+//   * float path: lane j of a row needs elements 2j, 16+2j, 2j+1, 17+2j of every group, which
+//     are the four nibbles of the little-endian u16 at byte 2j, in exactly the order in which
+//     the reference's lane j multiplies them (w4g32_avx2.h:74-91);
+//   * int8 path: the low nibbles of word k are elements 4k..4k+3 and the high nibbles elements
+//     16+4k..16+4k+3, so each masked word pairs with a natural-order word of int8 activations
+//     in one dp4a.
+#include "g4_api.h"
+#include "g4_common.cuh"
+#include "g4_async.cuh"
+#include <cstdlib>
+#include <cstdio>
+
+namespace g4 {
+
+// ---------------------------------------------------------------------------------- relayout
+// Reference layout byte b = element 2b | element 2b+1 << 4  ->  device layout byte b =
+// element b | element 16+b << 4.  One thread per 32-group.
+__global__ void k_w4_pack(const uint8_t* __restrict__ W, long long groups, uint8_t* __restrict__ Wp) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= groups) return;
+  const uint4 v = reinterpret_cast<const uint4*>(W)[i];
+  const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+  uint32_t t[32];
+#pragma unroll
+  for (int b = 0; b < 16; ++b) {
+    const uint32_t byte = (in[b >> 2] >> (8 * (b & 3))) & 0xFFu;
+    t[2 * b] = byte & 15u;
+    t[2 * b + 1] = byte >> 4;
+  }
+  uint32_t out[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int b = 0; b < 16; ++b) out[b >> 2] |= (t[b] | (t[16 + b] << 4)) << (8 * (b & 3));
+  reinterpret_cast<uint4*>(Wp)[i] = make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// ---------------------------------------------------------------------------- group sums
+// gsum[m][g] = ((x0 + x1) + x2) + ... + x31 starting from 0 (w4g32_avx2.h:22; XP::prep
+// gemma4_engine.cpp:191).  One thread per (m, g).
+__global__ void k_gsum(const float* __restrict__ X, int MG, int G, float* __restrict__ gs) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= MG) return;
+  const float* x = X + (size_t)(i / G) * G * 32 + (size_t)(i % G) * 32;
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) s = __fadd_rn(s, x[k]);
+  gs[i] = s;
+}
+
+// ------------------------------------------------------------------------- W4G32 float GEMV
+// Each CTA owns ROWS = 8*R weight rows.  Thread 0 streams the rows into shared memory with 1D
+// bulk copies (the TMA engine), CH groups per chunk, NB chunk buffers in a ring; every row is
+// padded by 16 bytes so the octets' reads fall in different banks.  One octet (8 lanes) works on
+// R rows, lane j owning the reference's AVX lane j: per group
+//   a = t(2j)x(2j); a = fma(t(16+2j), x(16+2j), a); a = fma(t(2j+1), ...); a = fma(t(17+2j), ...)
+//   row = fma(a, scale, row); off = fma(scale, gsum, off)   (the reference build fuses this one)
+// and finally y = hsum8(row) - 8*off.  With R = 2 the two rows' chains run as packed f32x2
+// operations (each half an IEEE fp32 op, so the results are the same bits).
+struct GemvGeom {
+  int G, CH, nchunk, NB, rowb;
+};
+__host__ __device__ inline GemvGeom gemv_geom(int K, int CH, int NB) {
+  GemvGeom g;
+  g.G = K >> 5;
+  g.CH = CH;
+  g.nchunk = g.G / CH;
+  g.NB = NB < g.nchunk ? NB : g.nchunk;
+  g.rowb = CH * 16 + 16;
+  return g;
+}
+
+// 4 int4 values (nibbles of v, low first) -> exact floats via the 2^23 bias.
+__device__ __forceinline__ void nib4_to_f(uint32_t v, float& t0, float& t1, float& t2, float& t3) {
+  const uint32_t lo = v & 0x0F0Fu, hi = (v >> 4) & 0x0F0Fu;
+  const float2 a = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7650)),
+                                          __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7650))),
+                              make_float2(-8388608.0f, -8388608.0f));
+  const float2 b = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7651)),
+                                          __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7651))),
+                              make_float2(-8388608.0f, -8388608.0f));
+  t0 = a.x; t1 = a.y; t2 = b.x; t3 = b.y;
+}
+
+template <int M, int R, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
+k_w4g32(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const float* __restrict__ X,
+        const float* __restrict__ gsum_in, int N, int K, float* __restrict__ Y, int ldy, int CH, int NBmax) {
+  constexpr int T = WARPS * 32;
+  constexpr int ROWS = WARPS * 4 * R;
+  const GemvGeom geo = gemv_geom(K, CH, NBmax);
+  const int G = geo.G;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint8_t* wbuf = smem + 128;
+  uint16_t* sc = reinterpret_cast<uint16_t*>(wbuf + (size_t)geo.NB * ROWS * geo.rowb);
+  float* gs = reinterpret_cast<float*>(sc + (size_t)ROWS * G);
+  const int n0 = blockIdx.x * ROWS;
+  const int nvalid = min(ROWS, N - n0);
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < geo.NB; ++b) mbar_init(&bars[b], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int c) {
+    const int b = c % geo.NB;
+    const uint32_t wbytes = (uint32_t)geo.CH * 16;
+    mbar_expect_tx(&bars[b], nvalid * wbytes + (c == 0 ? (uint32_t)nvalid * G * 2 : 0u));
+    for (int r = 0; r < nvalid; ++r)
+      bulk_g2s(wbuf + ((size_t)b * ROWS + r) * geo.rowb, Wp + (size_t)(n0 + r) * (K >> 1) + (size_t)c * wbytes, wbytes,
+               &bars[b]);
+    if (c == 0) bulk_g2s(sc, S + (size_t)n0 * G, (uint32_t)nvalid * G * 2, &bars[b]);
+  };
+  if (threadIdx.x == 0)
+    for (int c = 0; c < geo.NB; ++c) issue(c);
+
+  // group sums (given, or ((x0 + x1) + ...) + x31 from 0, w4g32_avx2.h:22) while the copies fly
+  if (gsum_in != nullptr) {
+    for (int i = threadIdx.x; i < M * G; i += T) gs[i] = gsum_in[i];
+  } else {
+    for (int i = threadIdx.x; i < M * G; i += T) {
+      const float4* x4 = reinterpret_cast<const float4*>(X + (size_t)(i / G) * K + (size_t)(i % G) * 32);
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float4 v = __ldg(x4 + k);
+        s = __fadd_rn(s, v.x); s = __fadd_rn(s, v.y); s = __fadd_rn(s, v.z); s = __fadd_rn(s, v.w);
+      }
+      gs[i] = s;
+    }
+  }
+  __syncthreads();
+
+  const int oct = threadIdx.x >> 3, j = threadIdx.x & 7;
+  float2 row[M], off[M];  // .x = row oct*R, .y = row oct*R+1 (unused when R == 1)
+#pragma unroll
+  for (int m = 0; m < M; ++m) { row[m] = make_float2(0.f, 0.f); off[m] = make_float2(0.f, 0.f); }
+  const int r0 = oct * R;
+
+  for (int c = 0; c < geo.nchunk; ++c) {
+    const int b = c % geo.NB;
+    if (!cta_wait(&bars[b], (uint32_t)(c / geo.NB) & 1u)) return;
+    const uint8_t* wb = wbuf + (size_t)b * ROWS * geo.rowb;
+    for (int gl = 0; gl < geo.CH; gl += 8) {
+      const int gbase = c * geo.CH + gl;
+      uint4 s4[R];
+#pragma unroll
+      for (int i = 0; i < R; ++i) s4[i] = *reinterpret_cast<const uint4*>(sc + (size_t)(r0 + i) * G + gbase);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int g = gbase + u;
+        float t[R][4], scl[R];
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+          const uint32_t v = *reinterpret_cast<const uint16_t*>(wb + (size_t)(r0 + i) * geo.rowb + (gl + u) * 16 + 2 * j);
+          nib4_to_f(v, t[i][0], t[i][1], t[i][2], t[i][3]);
+          const uint32_t sw = (u < 2 ? s4[i].x : u < 4 ? s4[i].y : u < 6 ? s4[i].z : s4[i].w);
+          scl[i] = bf2f((u & 1) ? (sw >> 16) : (sw & 0xFFFFu));
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          const float* xg = X + (size_t)m * K + (size_t)g * 32;
+          const float2 xa = __ldg(reinterpret_cast<const float2*>(xg + 2 * j));
+          const float2 xb = __ldg(reinterpret_cast<const float2*>(xg + 16 + 2 * j));
+          const float gsv = gs[m * G + g];
+          if constexpr (R == 2) {
+            float2 a = __fmul2_rn(make_float2(t[0][0], t[1][0]), make_float2(xa.x, xa.x));
+            a = __ffma2_rn(make_float2(t[0][1], t[1][1]), make_float2(xb.x, xb.x), a);
+            a = __ffma2_rn(make_float2(t[0][2], t[1][2]), make_float2(xa.y, xa.y), a);
+            a = __ffma2_rn(make_float2(t[0][3], t[1][3]), make_float2(xb.y, xb.y), a);
+            const float2 s2 = make_float2(scl[0], scl[1]);
+            row[m] = __ffma2_rn(a, s2, row[m]);
+            off[m] = __ffma2_rn(s2, make_float2(gsv, gsv), off[m]);
+          } else {
+            float a = __fmul_rn(t[0][0], xa.x);
+            a = fmaf(t[0][1], xb.x, a);
+            a = fmaf(t[0][2], xa.y, a);
+            a = fmaf(t[0][3], xb.y, a);
+            row[m].x = fmaf(a, scl[0], row[m].x);
+            off[m].x = fmaf(scl[0], gsv, off[m].x);
+          }
+        }
+      }
+    }
+    if (c + geo.NB < geo.nchunk) {
+      __syncthreads();
+      if (threadIdx.x == 0) { fence_proxy_async_smem(); issue(c + geo.NB); }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const float h0 = hsum8_octet(row[m].x);
+    if (j == 0 && r0 < nvalid) Y[(size_t)m * ldy + n0 + r0] = __fsub_rn(h0, __fmul_rn(8.f, off[m].x));
+    if constexpr (R == 2) {
+      const float h1 = hsum8_octet(row[m].y);
+      if (j == 0 && r0 + 1 < nvalid) Y[(size_t)m * ldy + n0 + r0 + 1] = __fsub_rn(h1, __fmul_rn(8.f, off[m].y));
+    }
+  }
+}
+
+// ------------------------------------------------------------------------ W4A8 quantisation
+// One warp per (row, 32-group), lane i owning element i: amax, sx = amax/127, inv = sx>0 ? 1/sx
+// : 0, r = RNE(x*inv) (x86 cvtps_epi32 semantics: out of range or NaN -> INT32_MIN), sum of the
+// unsaturated r, q = r saturated to int16 then int8 (w4a8_avx2.h:30-42).
+__global__ void k_w4a8_quant(const float* __restrict__ X, int MG, int G, int8_t* __restrict__ q,
+                             float* __restrict__ sx, int32_t* __restrict__ sum) {
+  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= MG) return;
+  const size_t base = (size_t)wid * 32;  // [m][K] with K = 32G: group wid starts at 32*wid
+  const float x = X[base + lane];
+  float amax = fabsf(x);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, o));
+  const float s = __fdiv_rn(amax, 127.0f);
+  const float inv = s > 0.f ? __fdiv_rn(1.0f, s) : 0.0f;
+  const float v = __fmul_rn(x, inv);
+  const int32_t r = (v > -2147483648.f && v < 2147483648.f) ? __float2int_rn(v) : INT32_MIN;
+  int32_t tot = r;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(FULL, tot, o);
+  const int32_t r16 = r < -32768 ? -32768 : (r > 32767 ? 32767 : r);
+  q[base + lane] = (int8_t)(r16 < -128 ? -128 : (r16 > 127 ? 127 : r16));
+  if (lane == 0) { sx[wid] = s; sum[wid] = tot; }
+  (void)G;
+}
+
+// ------------------------------------------------------------------------------ W4A8 GEMV
+// Each CTA owns 8 weight rows streamed into shared memory as in k_w4g32.  Per chunk, phase 1
+// has each thread take one group for all 8 rows (its int8 activations, scale and sum are loaded
+// once and reused across the rows): the integer-exact group dot a32 = sum t*xq - 8*sum (eight
+// dp4a per activation row) and the scale sw*sx go to shared memory.  Phase 2 runs the fp32
+// chain row = fma(float(a32), sw*sx, row) over the groups in order (w4a8_avx2.h:57-58).
+constexpr int kW4A8Rows = 8;
+
+template <int M, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
+k_w4a8(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const int8_t* __restrict__ q,
+       const float* __restrict__ sx, const int32_t* __restrict__ sum, int N, int K, float* __restrict__ Y, int ldy,
+       int CH, int NBmax) {
+  constexpr int T = WARPS * 32;
+  constexpr int ROWS = kW4A8Rows;
+  const GemvGeom geo = gemv_geom(K, CH, NBmax);
+  const int G = geo.G;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint8_t* wbuf = smem + 128;
+  uint16_t* sc = reinterpret_cast<uint16_t*>(wbuf + (size_t)geo.NB * ROWS * geo.rowb);
+  float2* ac = reinterpret_cast<float2*>(sc + (size_t)ROWS * G);  // [ROWS*M][CH+1]
+  const int n0 = blockIdx.x * ROWS;
+  const int nvalid = min(ROWS, N - n0);
+  const int acs = geo.CH + 1;
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < geo.NB; ++b) mbar_init(&bars[b], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int c) {
+    const int b = c % geo.NB;
+    const uint32_t wbytes = (uint32_t)geo.CH * 16;
+    mbar_expect_tx(&bars[b], nvalid * wbytes + (c == 0 ? (uint32_t)nvalid * G * 2 : 0u));
+    for (int r = 0; r < nvalid; ++r)
+      bulk_g2s(wbuf + ((size_t)b * ROWS + r) * geo.rowb, Wp + (size_t)(n0 + r) * (K >> 1) + (size_t)c * wbytes, wbytes,
+               &bars[b]);
+    if (c == 0) bulk_g2s(sc, S + (size_t)n0 * G, (uint32_t)nvalid * G * 2, &bars[b]);
+  };
+  if (threadIdx.x == 0)
+    for (int c = 0; c < geo.NB; ++c) issue(c);
+
+  // chain slots: thread t owns (row, activation row) pairs t, t+T, ... of the ROWS*M chains
+  constexpr int CPT = (ROWS * M + T - 1) / T;
+  float row[CPT];
+#pragma unroll
+  for (int k = 0; k < CPT; ++k) row[k] = 0.f;
+  for (int c = 0; c < geo.nchunk; ++c) {
+    const int b = c % geo.NB;
+    if (!cta_wait(&bars[b], (uint32_t)(c / geo.NB) & 1u)) return;
+    const uint8_t* wb = wbuf + (size_t)b * ROWS * geo.rowb;
+    for (int gl = threadIdx.x; gl < geo.CH; gl += T) {
+      const int g = c * geo.CH + gl;
+      int4 qa[M], qb[M];
+      int bias[M];
+      float sxm[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const int4* qp = reinterpret_cast<const int4*>(q + (size_t)m * K + (size_t)g * 32);
+        qa[m] = __ldg(qp);
+        qb[m] = __ldg(qp + 1);
+        bias[m] = -8 * __ldg(sum + (size_t)m * G + g);
+        sxm[m] = __ldg(sx + (size_t)m * G + g);
+      }
+#pragma unroll 2
+      for (int r = 0; r < ROWS; ++r) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(wb + (size_t)r * geo.rowb + gl * 16);
+        const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { lo[k] = w4[k] & 0x0F0F0F0Fu; hi[k] = (w4[k] >> 4) & 0x0F0F0F0Fu; }
+        const float sw = bf2f(sc[(size_t)r * G + g]);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          int acc = bias[m];
+          acc = __dp4a((int)lo[0], qa[m].x, acc);
+          acc = __dp4a((int)lo[1], qa[m].y, acc);
+          acc = __dp4a((int)lo[2], qa[m].z, acc);
+          acc = __dp4a((int)lo[3], qa[m].w, acc);
+          acc = __dp4a((int)hi[0], qb[m].x, acc);
+          acc = __dp4a((int)hi[1], qb[m].y, acc);
+          acc = __dp4a((int)hi[2], qb[m].z, acc);
+          acc = __dp4a((int)hi[3], qb[m].w, acc);
+          ac[(size_t)(r * M + m) * acs + gl] = make_float2((float)acc, __fmul_rn(sw, sxm[m]));
+        }
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < CPT; ++k) {
+      const int ci = threadIdx.x + k * T;  // = r*M + m
+      if (ci < ROWS * M) {
+        const float2* a = ac + (size_t)ci * acs;
+#pragma unroll 8
+        for (int gl = 0; gl < geo.CH; ++gl) {
+          const float2 v = a[gl];
+          row[k] = fmaf(v.x, v.y, row[k]);
+        }
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && c + geo.NB < geo.nchunk) { fence_proxy_async_smem(); issue(c + geo.NB); }
+  }
+#pragma unroll
+  for (int k = 0; k < CPT; ++k) {
+    const int ci = threadIdx.x + k * T, cr = ci / M, cm = ci % M;
+    if (ci < ROWS * M && cr < nvalid) Y[(size_t)cm * ldy + n0 + cr] = row[k];
+  }
+}
+
+}  // namespace g4
+
+G4_STATUS_READER(linear)
+
+using namespace g4;
+
+extern "C" int g4_w4_pack(const uint8_t* W, int N, int K, uint8_t* Wp, void* stream) {
+  G4_REQUIRE(W && Wp && N > 0 && K > 0 && K % 32 == 0, "g4_w4_pack: bad arguments N=%d K=%d", N, K);
+  G4_REQUIRE(aligned(W, 16) && aligned(Wp, 16), "g4_w4_pack: W and Wp must be 16-byte aligned");
+  const long long groups = (long long)N * (K / 32);
+  k_w4_pack<<<(unsigned)((groups + 255) / 256), 256, 0, as_stream(stream)>>>(W, groups, Wp);
+  return check_launch("k_w4_pack");
+}
+
+extern "C" int g4_w4g32_gsum(const float* X, int M, int K, float* gsum, void* stream) {
+  G4_REQUIRE(X && gsum && M > 0 && K > 0 && K % 32 == 0, "g4_w4g32_gsum: bad arguments M=%d K=%d", M, K);
+  const int MG = M * (K / 32);
+  k_gsum<<<(MG + 255) / 256, 256, 0, as_stream(stream)>>>(X, MG, K / 32, gsum);
+  return check_launch("k_gsum");
+}
+
+// Launch geometry: CH groups per chunk (64, or the largest of 32/16/8 dividing G), up to NB
+// chunk buffers in flight.  Rows per CTA: 16 (R = 2 packed rows per octet) when that still gives
+// at least two CTAs per SM, else 8.  G4_GEMV_CFG="R,WARPS,CH,NB" overrides this (tuning knob).
+static int pick_ch(int G) { return G % 64 == 0 ? 64 : G % 32 == 0 ? 32 : G % 16 == 0 ? 16 : 8; }
+
+struct GemvCfg { int R, WARPS, CH, NB; };
+static GemvCfg gemv_cfg(int N, int G) {
+  GemvCfg c{2, 2, pick_ch(G), 3};
+  if ((N + 15) / 16 < 296) c.R = 1;
+  if (const char* e = getenv("G4_GEMV_CFG")) sscanf(e, "%d,%d,%d,%d", &c.R, &c.WARPS, &c.CH, &c.NB);
+  return c;
+}
+static size_t w4g32_smem(int M, int rows, const GemvGeom& g) {
+  return 128 + (size_t)g.NB * rows * g.rowb + (size_t)rows * g.G * 2 + (size_t)M * g.G * 4;
+}
+
+template <int M, int R, int WARPS>
+static int launch_w4g32_t(const uint8_t* Wp, const uint16_t* S, const float* X, const float* gsum, int N, int K,
+                          float* Y, int ldy, int CH, int NB, cudaStream_t st) {
+  constexpr int ROWS = WARPS * 4 * R;
+  const GemvGeom g = gemv_geom(K, CH, NB);
+  const size_t smem = w4g32_smem(M, ROWS, g);
+  if (smem > 227 * 1024) return set_error(G4_ERR_UNSUPPORTED, "g4_w4g32_gemm: %zu B of shared memory", smem);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k_w4g32<M, R, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_w4g32<M, R, WARPS><<<(N + ROWS - 1) / ROWS, WARPS * 32, smem, st>>>(Wp, S, X, gsum, N, K, Y, ldy, CH, NB);
+  return check_launch("k_w4g32");
+}
+
+template <int M>
+static int launch_w4g32(const uint8_t* Wp, const uint16_t* S, const float* X, const float* gsum, int N, int K,
+                        float* Y, int ldy, cudaStream_t st) {
+  const GemvCfg c = gemv_cfg(N, K / 32);
+  if (c.R == 2 && c.WARPS == 2) return launch_w4g32_t<M, 2, 2>(Wp, S, X, gsum, N, K, Y, ldy, c.CH, c.NB, st);
+  if (c.R == 2 && c.WARPS == 4) return launch_w4g32_t<M, 2, 4>(Wp, S, X, gsum, N, K, Y, ldy, c.CH, c.NB, st);
+  if (c.R == 1 && c.WARPS == 4) return launch_w4g32_t<M, 1, 4>(Wp, S, X, gsum, N, K, Y, ldy, c.CH, c.NB, st);
+  return launch_w4g32_t<M, 1, 2>(Wp, S, X, gsum, N, K, Y, ldy, c.CH, c.NB, st);
+}
+
+extern "C" int g4_w4g32_gemm(const uint8_t* Wp, const uint16_t* S, const float* X, const float* gsum, int M, int N,
+                             int K, float* Y, int ldy, void* stream) {
+  G4_REQUIRE(Wp && S && X && Y, "g4_w4g32_gemm: null pointer");
+  G4_REQUIRE(M >= 1 && M <= 8 && N > 0 && K > 0 && K % 256 == 0 && ldy >= N,
+             "g4_w4g32_gemm: unsupported shape M=%d N=%d K=%d ldy=%d (K must be a multiple of 256)", M, N, K, ldy);
+  G4_REQUIRE(aligned(Wp, 16) && aligned(S, 16) && aligned(X, 16) && (gsum == nullptr || aligned(gsum, 4)),
+             "g4_w4g32_gemm: Wp, S and X must be 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  switch (M) {
+    case 1: return launch_w4g32<1>(Wp, S, X, gsum, N, K, Y, ldy, st);
+    case 2: return launch_w4g32<2>(Wp, S, X, gsum, N, K, Y, ldy, st);
+    case 3: return launch_w4g32<3>(Wp, S, X, gsum, N, K, Y, ldy, st);
+    case 4: return launch_w4g32<4>(Wp, S, X, gsum, N, K, Y, ldy, st);
+    case 5: return launch_w4g32<5>(Wp, S, X, gsum, N, K, Y, ldy, st);
+    case 6: return launch_w4g32<6>(Wp, S, X, gsum, N, K, Y, ldy, st);
+    case 7: return launch_w4g32<7>(Wp, S, X, gsum, N, K, Y, ldy, st);
+    default: return launch_w4g32<8>(Wp, S, X, gsum, N, K, Y, ldy, st);
+  }
+}
+
+extern "C" int g4_w4a8_quant(const float* X, int M, int K, int8_t* q, float* sx, int32_t* sum, void* stream) {
+  G4_REQUIRE(X && q && sx && sum && M > 0 && K > 0 && K % 32 == 0, "g4_w4a8_quant: bad arguments M=%d K=%d", M, K);
+  const int MG = M * (K / 32);
+  const int threads = 256, per_block = threads / 32;
+  k_w4a8_quant<<<(MG + per_block - 1) / per_block, threads, 0, as_stream(stream)>>>(X, MG, K / 32, q, sx, sum);
+  return check_launch("k_w4a8_quant");
+}
+
+static size_t w4a8_smem(int M, const GemvGeom& g) {
+  return 128 + (size_t)g.NB * kW4A8Rows * g.rowb + (size_t)kW4A8Rows * g.G * 2 + (size_t)kW4A8Rows * M * (g.CH + 1) * 8;
+}
+
+template <int M, int WARPS>
+static int launch_w4a8_t(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
+                         int N, int K, float* Y, int ldy, int CH, int NB, cudaStream_t st) {
+  const GemvGeom g = gemv_geom(K, CH, NB);
+  const size_t smem = w4a8_smem(M, g);
+  if (smem > 227 * 1024) return set_error(G4_ERR_UNSUPPORTED, "g4_w4a8_gemm: %zu B of shared memory", smem);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k_w4a8<M, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_w4a8<M, WARPS><<<(N + kW4A8Rows - 1) / kW4A8Rows, WARPS * 32, smem, st>>>(Wp, S, q, sx, sum, N, K, Y, ldy, CH, NB);
+  return check_launch("k_w4a8");
+}
+
+template <int M>
+static int launch_w4a8(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
+                       int N, int K, float* Y, int ldy, cudaStream_t st) {
+  int WARPS = 2, CH = pick_ch(K / 32), NB = 3;
+  if (const char* e = getenv("G4_W4A8_CFG")) sscanf(e, "%d,%d,%d", &WARPS, &CH, &NB);
+  if (WARPS == 1) return launch_w4a8_t<M, 1>(Wp, S, q, sx, sum, N, K, Y, ldy, CH, NB, st);
+  if (WARPS == 4) return launch_w4a8_t<M, 4>(Wp, S, q, sx, sum, N, K, Y, ldy, CH, NB, st);
+  return launch_w4a8_t<M, 2>(Wp, S, q, sx, sum, N, K, Y, ldy, CH, NB, st);
+}
+
+extern "C" int g4_w4a8_gemm(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx,
+                            const int32_t* sum, int M, int N, int K, float* Y, int ldy, void* stream) {
+  G4_REQUIRE(Wp && S && q && sx && sum && Y, "g4_w4a8_gemm: null pointer");
+  G4_REQUIRE(M >= 1 && M <= 8 && N > 0 && K > 0 && K % 256 == 0 && ldy >= N,
+             "g4_w4a8_gemm: unsupported shape M=%d N=%d K=%d ldy=%d (K must be a multiple of 256)", M, N, K, ldy);
+  G4_REQUIRE(aligned(Wp, 16) && aligned(S, 16) && aligned(q, 16), "g4_w4a8_gemm: Wp, S and q must be 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  switch (M) {
+    case 1: return launch_w4a8<1>(Wp, S, q, sx, sum, N, K, Y, ldy, st);
+    case 2: return launch_w4a8<2>(Wp, S, q, sx, sum, N, K, Y, ldy, st);
+    case 3: return launch_w4a8<3>(Wp, S, q, sx, sum, N, K, Y, ldy, st);
+    case 4: return launch_w4a8<4>(Wp, S, q, sx, sum, N, K, Y, ldy, st);
+    case 5: return launch_w4a8<5>(Wp, S, q, sx, sum, N, K, Y, ldy, st);
+    case 6: return launch_w4a8<6>(Wp, S, q, sx, sum, N, K, Y, ldy, st);
+    case 7: return launch_w4a8<7>(Wp, S, q, sx, sum, N, K, Y, ldy, st);
+    default: return launch_w4a8<8>(Wp, S, q, sx, sum, N, K, Y, ldy, st);
+  }
+}

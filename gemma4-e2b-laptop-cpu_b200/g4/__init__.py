@@ -1,0 +1,136 @@
+"""Python binding of libg4.so, the C ABI declared in include/g4.h.
+
+This is the host-side mirror of the reference's kernel-header operator surface
+(engine/w4g32_avx2.h, engine/w4a8_avx2.h, engine/bf16_exp3_head.h and the engine tasks of
+engine/gemma4_engine.cpp): the same operations under the same names, taking torch CUDA tensors
+(device memory and the current stream are torch's; the arithmetic is the library's sm_100a
+kernels).  There is no CPU fallback: loading fails loudly when libg4.so is missing.
+"""
+import ctypes
+import pathlib
+
+PKG_ROOT = pathlib.Path(__file__).resolve().parent.parent
+LIB_PATH = PKG_ROOT / "libg4.so"
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64 = ctypes.c_int64
+_SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes); every entry point of include/g4.h
+SIGNATURES = {
+    "g4_last_error": (ctypes.c_char_p, []),
+    "g4_abi_version": (_I, []),
+    "g4_device_status": (_I, [ctypes.POINTER(ctypes.c_uint), _I]),
+    "g4_w4_pack": (_I, [_P, _I, _I, _P, _P]),
+    "g4_w4g32_gsum": (_I, [_P, _I, _I, _P, _P]),
+    "g4_w4g32_gemm": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _I, _P]),
+    "g4_w4a8_quant": (_I, [_P, _I, _I, _P, _P, _P, _P]),
+    "g4_w4a8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _P]),
+}
+
+
+class G4Error(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def lib():
+    """The loaded libg4.so with argument types set; raises when it was not built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise G4Error(f"{LIB_PATH} is missing: build it with __graft_entry__.build() "
+                          f"(make -C {PKG_ROOT}); g4 has no CPU fallback")
+        lib_ = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib_, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib_
+    return _lib
+
+
+def check(rc, what):
+    if rc != 0:
+        raise G4Error(f"{what} failed ({rc}): {lib().g4_last_error().decode()}")
+
+
+def device_status(reset=True):
+    """OR of the device status words (bit 0: a bounded device wait gave up)."""
+    v = ctypes.c_uint(0)
+    check(lib().g4_device_status(ctypes.byref(v), int(reset)), "g4_device_status")
+    return v.value
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _dev(t, name):
+    if not t.is_cuda or not t.is_contiguous():
+        raise G4Error(f"{name} must be a contiguous CUDA tensor")
+    return t
+
+
+# ------------------------------------------------------------------ W4G32 / W4A8 operators
+def w4_pack(W):
+    """Reference W4 layout uint8 [N, K/2] -> device layout (load-time, like w4a8::repack_tiles)."""
+    import torch
+    _dev(W, "W")
+    N, Kh = W.shape
+    Wp = torch.empty_like(W)
+    check(lib().g4_w4_pack(_ptr(W), N, 2 * Kh, _ptr(Wp), _stream()), "g4_w4_pack")
+    return Wp
+
+
+def w4g32_gsum(X):
+    import torch
+    _dev(X, "X")
+    M, K = X.shape
+    gs = torch.empty((M, K // 32), dtype=torch.float32, device=X.device)
+    check(lib().g4_w4g32_gsum(_ptr(X), M, K, _ptr(gs), _stream()), "g4_w4g32_gsum")
+    return gs
+
+
+def w4g32_gemm(Wp, S, X, gsum=None, out=None):
+    """Y[M, N] = W4G32(Wp, S) @ X[M, K]^T, fp32 order of w4::gemm_rows_tile<MT>."""
+    import torch
+    for t, n in ((Wp, "Wp"), (S, "S"), (X, "X")):
+        _dev(t, n)
+    M, K = X.shape
+    N = Wp.shape[0]
+    Y = out if out is not None else torch.empty((M, N), dtype=torch.float32, device=X.device)
+    check(lib().g4_w4g32_gemm(_ptr(Wp), _ptr(S), _ptr(X), _ptr(gsum), M, N, K, _ptr(Y), Y.stride(0), _stream()),
+          "g4_w4g32_gemm")
+    return Y
+
+
+def w4a8_quant(X):
+    """(q int8 [M, K], sx fp32 [M, K/32], sum int32 [M, K/32]) exactly as w4a8::quant."""
+    import torch
+    _dev(X, "X")
+    M, K = X.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=X.device)
+    sx = torch.empty((M, K // 32), dtype=torch.float32, device=X.device)
+    sm = torch.empty((M, K // 32), dtype=torch.int32, device=X.device)
+    check(lib().g4_w4a8_quant(_ptr(X), M, K, _ptr(q), _ptr(sx), _ptr(sm), _stream()), "g4_w4a8_quant")
+    return q, sx, sm
+
+
+def w4a8_gemm(Wp, S, q, sx, sm, out=None):
+    """Y[M, N] with integer-exact group dots and the fp32 scale chain of w4a8::tile<MT>."""
+    import torch
+    M, K = q.shape
+    N = Wp.shape[0]
+    Y = out if out is not None else torch.empty((M, N), dtype=torch.float32, device=q.device)
+    check(lib().g4_w4a8_gemm(_ptr(Wp), _ptr(S), _ptr(q), _ptr(sx), _ptr(sm), M, N, K, _ptr(Y), Y.stride(0),
+                             _stream()), "g4_w4a8_gemm")
+    return Y

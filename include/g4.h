@@ -1,0 +1,77 @@
+/* g4: B200-native (sm_100a) speculative greedy-decode hot path behind a thin C ABI.
+ *
+ * Drop-in boundary for the kernel-header operator surface of gemma4-e2b-laptop-cpu
+ * (engine/w4g32_avx2.h, engine/w4a8_avx2.h, engine/bf16_exp3_head.h and the engine tasks in
+ * engine/gemma4_engine.cpp).  Every entry point takes plain pointers and sizes, returns an int
+ * status (G4_OK or a negative G4_ERR_*; g4_last_error() gives the message), never allocates,
+ * and enqueues its work on the CUDA stream passed as `stream` (NULL = the legacy default
+ * stream).  Pointers marked "dev" are device memory; all others are host memory.
+ *
+ * Layouts (identical to the reference unless stated):
+ *   W4 weights   uint8  [N][K/2]   two int4 values (q+8) per byte; the reference layout has low
+ *                                  nibble = even k (w4g32_avx2.h:1-6); the device layout made by
+ *                                  g4_w4_pack has, per 32-group, byte b = element b (low nibble)
+ *                                  and element 16+b (high nibble).
+ *   W4 scales    bf16   [N][K/32]
+ *   activations  fp32   [M][K]     row m at X + m*K; outputs Y[m*ldy + n]
+ *   int8 acts    int8   [M][K], scales fp32 [M][K/32], sums int32 [M][K/32]  (w4a8_avx2.h:29)
+ *   bf16-exp3    44 B per 32-group (bf16_exp3_head.h:1-4) + CSR exceptions (exc_ptr int64[N+1],
+ *                exc_col uint16, exc_delta fp32)
+ *   KV cache     bf16   [ctx][hd]  one KV head (gemma4_engine.cpp:1248)
+ * K must be a multiple of 32 everywhere (256 for the GEMMs).
+ */
+#ifndef G4_H
+#define G4_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define G4_OK 0
+#define G4_ERR_INVALID (-1)     /* bad argument (size, alignment, null pointer) */
+#define G4_ERR_CUDA (-2)        /* a CUDA call failed */
+#define G4_ERR_TIMEOUT (-3)     /* a device-side wait gave up (status word set by the kernel) */
+#define G4_ERR_NOMEM (-4)       /* caller-provided workspace too small */
+#define G4_ERR_UNSUPPORTED (-5) /* shape outside what this build supports */
+
+/* Message of the last failed call on this host thread. */
+const char* g4_last_error(void);
+/* ABI version of this library (bumped on any signature change). */
+int g4_abi_version(void);
+/* Device status word (OR over the library's kernels on the current device): bit 0 set when a
+ * device-side bounded wait gave up.  Synchronous; reset != 0 clears it. */
+int g4_device_status(unsigned* out, int reset);
+
+/* ---------------------------------------------------------------- W4G32 / W4A8 linears */
+
+/* Load-time relayout of reference W4 weights (the role of w4a8::repack_tiles,
+ * w4a8_avx2.h:20-27): W dev [N][K/2] reference layout -> Wp dev [N][K/2] device layout. */
+int g4_w4_pack(const uint8_t* W, int N, int K, uint8_t* Wp, void* stream);
+
+/* Per-32-group sequential sums of X (the gsum half of w4::prep_x, w4g32_avx2.h:20-23):
+ * X dev [M][K] -> gsum dev [M][K/32]. */
+int g4_w4g32_gsum(const float* X, int M, int K, float* gsum, void* stream);
+
+/* Float-activation int4 GEMM, Y[m*ldy+n] = sum_g s[n,g]*(sum_i t*x - 8*gsum) in the exact fp32
+ * order of w4::gemm_rows_tile<MT> (w4g32_avx2.h:65-96) as dispatched by lin_task/lin_multi
+ * (gemma4_engine.cpp:243-255, 310-317).  Wp dev (device layout), S dev, X dev, gsum dev or NULL
+ * (then computed in-kernel), Y dev.  1 <= M <= 8, K % 256 == 0. */
+int g4_w4g32_gemm(const uint8_t* Wp, const uint16_t* S, const float* X, const float* gsum, int M, int N,
+                  int K, float* Y, int ldy, void* stream);
+
+/* Per-(row, 32-group) symmetric int8 quantisation, bit-exact to w4a8::quant (w4a8_avx2.h:30-42).
+ * X dev [M][K] -> q dev [M][K], sx dev [M][K/32], sum dev [M][K/32]. */
+int g4_w4a8_quant(const float* X, int M, int K, int8_t* q, float* sx, int32_t* sum, void* stream);
+
+/* Int8-activation int4 GEMM, integer-exact group dots and the fp32 scale chain of
+ * w4a8::tile<MT> (w4a8_avx2.h:46-60) / i8_task (gemma4_engine.cpp:304-309).
+ * Wp dev (device layout), S dev, q/sx/sum dev (from g4_w4a8_quant), Y dev.  1 <= M <= 8. */
+int g4_w4a8_gemm(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
+                 int M, int N, int K, float* Y, int ldy, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
