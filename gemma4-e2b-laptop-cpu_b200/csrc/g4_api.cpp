@@ -25,6 +25,7 @@ extern "C" int g4_abi_version(void) { return 1; }
 
 namespace g4 {
 unsigned status_read_linear(bool reset);
+unsigned status_read_attn(bool reset);
 }
 
 // OR of the device status words of all kernel files on the current device; reset clears them.
@@ -32,6 +33,7 @@ extern "C" int g4_device_status(unsigned* out, int reset) {
   if (!out) return g4::set_error(G4_ERR_INVALID, "g4_device_status: null pointer");
   unsigned v = 0;
   v |= g4::status_read_linear(reset != 0);
+  v |= g4::status_read_attn(reset != 0);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return g4::set_error(G4_ERR_CUDA, "g4_device_status: %s", cudaGetErrorString(e));
   *out = v;

@@ -27,6 +27,8 @@ SIGNATURES = {
     "g4_w4g32_gemm": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _I, _P]),
     "g4_w4a8_quant": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "g4_w4a8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _P]),
+    "g4_attn_splitkv_ws_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "g4_attn_splitkv": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
 }
 
 
@@ -134,3 +136,22 @@ def w4a8_gemm(Wp, S, q, sx, sm, out=None):
     check(lib().g4_w4a8_gemm(_ptr(Wp), _ptr(S), _ptr(q), _ptr(sx), _ptr(sm), M, N, K, _ptr(Y), Y.stride(0),
                              _stream()), "g4_w4a8_gemm")
     return Y
+
+
+# ------------------------------------------------------------------ split-KV attention
+def attn_splitkv(Kc, Vc, q, pos, lo, T=8, ws=None, out=None):
+    """q [M, nh, hd] fp32 CUDA; Kc/Vc [ctx, hd] int16 (bf16 bits) CUDA; pos/lo host int lists."""
+    import torch
+    M, nh, hd = q.shape
+    pos = list(map(int, pos))
+    lo = list(map(int, lo))
+    kmin, kmax = min(lo), max(pos)
+    need = lib().g4_attn_splitkv_ws_bytes(M, nh, hd, kmin, kmax, T)
+    if ws is None:
+        ws = torch.empty(need // 4 + 4, dtype=torch.float32, device=q.device)
+    out = out if out is not None else torch.empty_like(q)
+    ia = (ctypes.c_int * 4)(*pos)
+    la = (ctypes.c_int * 4)(*lo)
+    check(lib().g4_attn_splitkv(_ptr(Kc), _ptr(Vc), _ptr(q), ia, la, M, nh, hd, kmin, kmax, T, _ptr(out), _ptr(ws),
+                                ws.numel() * ws.element_size(), _stream()), "g4_attn_splitkv")
+    return out

@@ -71,6 +71,20 @@ int g4_w4a8_quant(const float* X, int M, int K, int8_t* q, float* sx, int32_t* s
 int g4_w4a8_gemm(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
                  int M, int N, int K, float* Y, int ldy, void* stream);
 
+/* ---------------------------------------------------------------- split-KV decode attention */
+
+/* Workspace bytes g4_attn_splitkv needs for these sizes. */
+size_t g4_attn_splitkv_ws_bytes(int M, int nh, int hd, int kmin, int kmax, int T);
+
+/* Decode/verify attention of M <= 4 query rows, nh <= 8 query heads over one bf16 KV head, keys
+ * kmin..kmax split into T chunks as the reference's pool threads split them (attn_task,
+ * gemma4_engine.cpp:743-877) and merged with its exact log-sum-exp rescale (attn_merge
+ * :1019-1059).  Row m attends keys lo[m]..pos[m] (host arrays).  Kc, Vc dev bf16 [ctx][hd];
+ * q dev fp32 [M][nh][hd] (softmax scale already folded in); out dev fp32 [M][nh][hd], values
+ * rounded to bf16; ws dev scratch of g4_attn_splitkv_ws_bytes(); hd % 32 == 0, hd <= 512. */
+int g4_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, const float* q, const int* pos, const int* lo, int M,
+                    int nh, int hd, int kmin, int kmax, int T, float* out, void* ws, size_t ws_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
