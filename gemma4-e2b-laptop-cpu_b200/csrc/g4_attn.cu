@@ -205,3 +205,69 @@ extern "C" int g4_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, const flo
   k_attn_merge<<<(M * nh * hd + 255) / 256, 256, 0, st>>>(d, w, out);
   return check_launch("k_attn_merge");
 }
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free variant of g4_attn_splitkv.
+//
+// Some callers cannot hand this library a workspace: code embedded in a host that owns every
+// byte of device memory through its own arena and forbids foreign allocations, or a decode loop
+// on a latency-critical thread where a cudaMalloc/cudaFree could stall on a device-wide
+// synchronisation.  This entry point takes only inputs and outputs; its scratch is the fixed
+// array below, a file-scope device global of kAttnNoAllocFloats floats (1,312,768 bytes) that every
+// GPU which loads libg4.so holds until the process exits.  It serves M <= 4 rows, nh <= 8 heads,
+// hd <= 256, T <= 8 chunks and up to 8,192 keys (kmax - kmin + 1); larger calls are rejected.
+//
+// In host code the name g_attn_scratch only stands for the array; the device address comes from
+// cudaGetSymbolAddress, looked up once per device (with that device current) by the first call on
+// it, so make that first call before any stream capture.  All calls on a device share the array
+// and it keeps the previous call's contents; every word a call reads is written earlier in the
+// same call, so nothing needs clearing, but two calls whose kernels overlap on the GPU (two
+// streams, or two host threads) race on it and must be serialised by the caller.
+constexpr size_t kAttnNoAllocFloats = (size_t)8192 * 4 * 8 + 2 * (size_t)8 * 4 * 8 + (size_t)8 * 4 * 8 * 256;
+static __device__ __align__(256) float g_attn_scratch[kAttnNoAllocFloats];
+
+#include <mutex>
+static std::mutex g_attn_scratch_mu;
+static float* g_attn_scratch_dev[128];
+
+static int attn_scratch_for_current_device(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "g4_attn_splitkv_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 128) return set_error(G4_ERR_UNSUPPORTED, "g4_attn_splitkv_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lk(g_attn_scratch_mu);
+  if (g_attn_scratch_dev[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(G4_ERR_CUDA, "g4_attn_splitkv_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_attn_scratch_dev[dev] = static_cast<float*>(p);
+  }
+  *out = g_attn_scratch_dev[dev];
+  return G4_OK;
+}
+
+extern "C" int g4_attn_splitkv_noalloc(const uint16_t* Kc, const uint16_t* Vc, const float* q, const int* pos,
+                                       const int* lo, int M, int nh, int hd, int kmin, int kmax, int T, float* out,
+                                       void* stream) {
+  G4_REQUIRE(Kc && Vc && q && out, "g4_attn_splitkv_noalloc: null pointer");
+  AttnDesc d;
+  if (int rc = fill_desc(d, M, nh, hd, pos, lo, kmin, kmax, T)) return rc;
+  const int len = kmax - kmin + 1;
+  if (hd > 256 || T > 8 || len > 8192 || attn_ws_floats(M, nh, hd, len, T) > kAttnNoAllocFloats)
+    return set_error(G4_ERR_UNSUPPORTED,
+                     "g4_attn_splitkv_noalloc: M=%d nh=%d hd=%d T=%d keys=%d exceed the fixed scratch "
+                     "(hd <= 256, T <= 8, keys <= 8192); use g4_attn_splitkv with a workspace",
+                     M, nh, hd, T, len);
+  float* w = nullptr;
+  if (int rc = attn_scratch_for_current_device(&w)) return rc;
+  cudaStream_t st = as_stream(stream);
+  k_attn_scores<<<dim3((len + kScoreKeys - 1) / kScoreKeys, (M * nh + 15) / 16), 256, 0, st>>>(Kc, q, d, w);
+  if (int rc = check_launch("k_attn_scores")) return rc;
+  k_attn_stats<<<(T * M * nh * 32 + 255) / 256, 256, 0, st>>>(d, w);
+  if (int rc = check_launch("k_attn_stats")) return rc;
+  k_attn_accum<<<dim3(T, (hd + 31) / 32), M * nh * 32, 0, st>>>(Vc, d, w);
+  if (int rc = check_launch("k_attn_accum")) return rc;
+  k_attn_merge<<<(M * nh * hd + 255) / 256, 256, 0, st>>>(d, w, out);
+  return check_launch("k_attn_merge");
+}

@@ -29,6 +29,7 @@ SIGNATURES = {
     "g4_w4a8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _P]),
     "g4_attn_splitkv_ws_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "g4_attn_splitkv": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
+    "g4_attn_splitkv_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
 }
 
 

@@ -85,6 +85,18 @@ size_t g4_attn_splitkv_ws_bytes(int M, int nh, int hd, int kmin, int kmax, int T
 int g4_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, const float* q, const int* pos, const int* lo, int M,
                     int nh, int hd, int kmin, int kmax, int T, float* out, void* ws, size_t ws_bytes, void* stream);
 
+/* Same computation as g4_attn_splitkv for callers that cannot allocate device memory or hand over
+ * a workspace (an embedding host whose arena owns all device memory, or a latency-critical decode
+ * thread that must not risk the device-wide synchronisation a cudaMalloc/cudaFree can cause).
+ * No counterpart in the reference.  Scratch is a fixed device global inside libg4.so (1,312,768
+ * bytes, held by every GPU that loads the library until exit); limits: hd <= 256, T <= 8,
+ * kmax - kmin + 1 <= 8192 keys (plus M <= 4, nh <= 8), larger calls return G4_ERR_UNSUPPORTED.
+ * The first call on a device looks up the scratch address (cudaGetSymbolAddress) with that device
+ * current: make it before any stream capture.  Calls share the scratch, so calls that overlap on
+ * the GPU race; serialise them. */
+int g4_attn_splitkv_noalloc(const uint16_t* Kc, const uint16_t* Vc, const float* q, const int* pos, const int* lo,
+                            int M, int nh, int hd, int kmin, int kmax, int T, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
