@@ -26,6 +26,7 @@ extern "C" int g4_abi_version(void) { return 1; }
 namespace g4 {
 unsigned status_read_linear(bool reset);
 unsigned status_read_attn(bool reset);
+unsigned status_read_head(bool reset);
 }
 
 // OR of the device status words of all kernel files on the current device; reset clears them.
@@ -34,6 +35,7 @@ extern "C" int g4_device_status(unsigned* out, int reset) {
   unsigned v = 0;
   v |= g4::status_read_linear(reset != 0);
   v |= g4::status_read_attn(reset != 0);
+  v |= g4::status_read_head(reset != 0);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return g4::set_error(G4_ERR_CUDA, "g4_device_status: %s", cudaGetErrorString(e));
   *out = v;

@@ -1,0 +1,620 @@
+// Output head: the bf16-exp3 packed exact head (engine/bf16_exp3_head.h), the certified int4
+// head screen (gemma4_engine.cpp:1235-1244, 454-538, 1409-1497) and the greedy pick with the
+// softcap tie rule, all on the device.
+//
+// Logits stay exact: each packed row is decoded to its bf16 weights and dotted with h in the
+// reference's fp32 order (lane j: weights j, 16+j, 8+j, 24+j of every group; hsum8; then the CSR
+// exception patches y = y + delta*x, not fused, as the reference compiles under Zen 3 tuning).
+// The screen finds the same survivor set as the reference's eval_row: lower/upper bounds s -+ c|h|
+// (fused), L = max lower, survivors = {n : upper >= calc_thr(L)}.  Survivors are collected in any
+// order: the pick (max of the rescored bf16 logits, then the lowest index whose capped value
+// equals the max's) does not depend on it.  More than `lim` survivors means the full head runs,
+// as the reference's fallback does.  The softcap r16(30*tanh(s/30)) is only ever applied to bf16
+// values, so it is a 65,536-entry table built on the host with the same libm (g4_device_init).
+#include "g4_api.h"
+#include "g4_async.cuh"
+#include "g4_common.cuh"
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+namespace g4 {
+
+__device__ float g_cap_table[65536];  // cap(bf16 value with these bits), as float
+
+__device__ __forceinline__ float cap_bf(float v) { return g_cap_table[__float_as_uint(v) >> 16]; }  // v bf16-valued
+
+// calc_thr (gemma4_engine.cpp:1455-1459): lowest z (40-step bisection on [r16(L)-64, r16(L)])
+// whose capped bf16 value equals cap(r16(L)), minus 0.25.
+__device__ float calc_thr(float L) {
+  const float Lr = r16(L), cmL = cap_bf(Lr);
+  float lo = __fsub_rn(Lr, 64.0f), hi = Lr;
+  for (int it = 0; it < 40; ++it) {
+    const float mid = __fmul_rn(0.5f, __fadd_rn(lo, hi));
+    if (cap_bf(r16(mid)) == cmL) hi = mid; else lo = mid;
+  }
+  return __fsub_rn(hi, 0.25f);
+}
+
+// float <-> order-preserving int for atomicMax
+__device__ __forceinline__ int f2ord(float f) { const int i = __float_as_int(f); return i >= 0 ? i : i ^ 0x7FFFFFFF; }
+__device__ __forceinline__ float ord2f(int i) { return __int_as_float(i >= 0 ? i : i ^ 0x7FFFFFFF); }
+
+// ------------------------------------------------------------------------------- packing
+// exponent histogram for the codebook (gemma4_engine.cpp:1232)
+__global__ void k_exp_hist(const uint16_t* __restrict__ E, long long count, unsigned long long* __restrict__ hist) {
+  __shared__ unsigned int h[256];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) h[i] = 0;
+  __syncthreads();
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (long long)gridDim.x * blockDim.x)
+    atomicAdd(&h[(E[i] >> 7) & 0xFF], 1u);
+  __syncthreads();
+  for (int i = threadIdx.x; i < 256; i += blockDim.x)
+    if (h[i]) atomicAdd(&hist[i], (unsigned long long)h[i]);
+}
+
+struct Codebook { uint8_t e[8]; };
+
+// index of exponent e in the codebook; not found -> nearest (first on ties), exc = 1 (bf16_exp3_head.h:33-40)
+__device__ __forceinline__ int cb_index(const Codebook& cb, int e, int& exc) {
+  for (int i = 0; i < 8; ++i) if (cb.e[i] == e) { exc = 0; return i; }
+  int best = 0, bd = 1 << 30;
+  for (int i = 0; i < 8; ++i) { const int dd = abs((int)cb.e[i] - e); if (dd < bd) { bd = dd; best = i; } }
+  exc = 1;
+  return best;
+}
+
+// exceptions per row -> cnt[n] (block per row)
+__global__ void k_bf16p_count(const uint16_t* __restrict__ E, int K, Codebook cb, long long* __restrict__ cnt) {
+  const int n = blockIdx.x;
+  int c = 0;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    int exc;
+    cb_index(cb, (E[(size_t)n * K + k] >> 7) & 0xFF, exc);
+    c += exc;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(FULL, c, o);
+  __shared__ int ws[32];
+  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < (int)(blockDim.x + 31) / 32; ++w) t += ws[w];
+    cnt[n] = t;
+  }
+}
+
+// exclusive scan of cnt[0..N) into ptr[0..N] (ptr[0] = 0); one block of 1024 threads, chunked.
+__global__ void __launch_bounds__(1024) k_scan_rows(const long long* __restrict__ cnt, int N, long long* __restrict__ ptr) {
+  __shared__ long long part[1024];
+  const int per = (N + 1023) / 1024;
+  const int a = threadIdx.x * per, b = min(N, a + per);
+  long long s = 0;
+  for (int i = a; i < b; ++i) s += cnt[i];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long run = 0;
+    for (int i = 0; i < 1024; ++i) { const long long v = part[i]; part[i] = run; run += v; }
+  }
+  __syncthreads();
+  long long run = part[threadIdx.x];
+  if (threadIdx.x == 0) ptr[0] = 0;
+  for (int i = a; i < b; ++i) { run += cnt[i]; ptr[i + 1] = run; }
+}
+
+// fill the 44-byte groups and the exceptions of one row (block per row, thread per group);
+// exceptions in (group, element) order at exc_ptr[n] + (exceptions of earlier groups) + rank.
+__global__ void k_bf16p_fill(const uint16_t* __restrict__ E, int K, Codebook cb, uint8_t* __restrict__ data,
+                             const long long* __restrict__ exc_ptr, uint16_t* __restrict__ exc_col,
+                             float* __restrict__ exc_delta) {
+  extern __shared__ int gcount[];  // [G] then scanned
+  const int n = blockIdx.x, G = K >> 5;
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    int c = 0;
+    for (int j = 0; j < 32; ++j) {
+      int exc;
+      cb_index(cb, (E[(size_t)n * K + g * 32 + j] >> 7) & 0xFF, exc);
+      c += exc;
+    }
+    gcount[g] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int g = 0; g < G; ++g) { const int v = gcount[g]; gcount[g] = run; run += v; }
+  }
+  __syncthreads();
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    uint32_t sm[8] = {0, 0, 0, 0, 0, 0, 0, 0}, pl[3] = {0, 0, 0};
+    long long e_out = exc_ptr[n] + gcount[g];
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t w = E[(size_t)n * K + g * 32 + j];
+      const uint32_t sign = w >> 15, e = (w >> 7) & 0xFF, m = w & 0x7F;
+      int exc;
+      const int idx = cb_index(cb, (int)e, exc);
+      if (exc) {
+        const uint32_t dec = (sign << 15) | ((uint32_t)cb.e[idx] << 7) | m;
+        exc_col[e_out] = (uint16_t)(g * 32 + j);
+        exc_delta[e_out] = __fsub_rn(bf2f(w), bf2f(dec));
+        ++e_out;
+      }
+      sm[j >> 2] |= ((sign << 7) | m) << (8 * (j & 3));
+      for (int k = 0; k < 3; ++k) pl[k] |= (uint32_t)((idx >> k) & 1) << j;
+    }
+    uint32_t* d = reinterpret_cast<uint32_t*>(data + ((size_t)n * G + g) * 44);
+    for (int k = 0; k < 8; ++k) d[k] = sm[k];
+    for (int k = 0; k < 3; ++k) d[8 + k] = pl[k];
+  }
+}
+
+// ------------------------------------------------------------------------- exact head dot
+struct HeadPacked {
+  const uint8_t* data;
+  const long long* exc_ptr;
+  const uint16_t* exc_col;
+  const float* exc_delta;
+  uint32_t cb_lo, cb_hi;  // codebook bytes 0-3 and 4-7
+  int N, K;
+};
+
+// weight e (0..31) of a packed group held as sign/mant bytes and 3 planes
+__device__ __forceinline__ float bf16p_w(const uint8_t* g, uint32_t p0, uint32_t p1, uint32_t p2, int e,
+                                         uint32_t cb_lo, uint32_t cb_hi) {
+  const uint32_t idx = ((p0 >> e) & 1u) | (((p1 >> e) & 1u) << 1) | (((p2 >> e) & 1u) << 2);
+  const uint32_t ex = __byte_perm(cb_lo, cb_hi, idx) & 0xFFu;
+  const uint32_t sm = g[e];
+  return __uint_as_float((((sm & 0x80u) << 8) | (ex << 7) | (sm & 0x7Fu)) << 16);
+}
+
+// Row dot for one octet lane: returns the lane's partial sum over all groups (rows_tile order).
+__device__ __forceinline__ float bf16p_lane_dot(const uint8_t* __restrict__ row, int G, const float* __restrict__ x,
+                                                int j, uint32_t cb_lo, uint32_t cb_hi) {
+  float acc = 0.f;
+#pragma unroll 2
+  for (int g = 0; g < G; ++g) {
+    const uint8_t* gp = row + (size_t)g * 44;
+    const uint32_t* pw = reinterpret_cast<const uint32_t*>(gp + 32);
+    const uint32_t p0 = pw[0], p1 = pw[1], p2 = pw[2];
+    const float* xg = x + g * 32;
+    acc = fmaf(bf16p_w(gp, p0, p1, p2, j, cb_lo, cb_hi), xg[j], acc);
+    acc = fmaf(bf16p_w(gp, p0, p1, p2, 16 + j, cb_lo, cb_hi), xg[16 + j], acc);
+    acc = fmaf(bf16p_w(gp, p0, p1, p2, 8 + j, cb_lo, cb_hi), xg[8 + j], acc);
+    acc = fmaf(bf16p_w(gp, p0, p1, p2, 24 + j, cb_lo, cb_hi), xg[24 + j], acc);
+  }
+  return acc;
+}
+
+// exception patches of row n against x, in CSR order, unfused (bf16_exp3_head.h:103)
+__device__ __forceinline__ float bf16p_patch(const HeadPacked& P, int n, const float* __restrict__ x, float y) {
+  for (long long e = P.exc_ptr[n]; e < P.exc_ptr[n + 1]; ++e) y = __fadd_rn(y, __fmul_rn(P.exc_delta[e], x[P.exc_col[e]]));
+  return y;
+}
+
+// Y[m*ldy + n] = raw logit (before r16).  Octet per row; 256 threads = 32 rows.  If `gate` is
+// non-null the kernel does nothing unless *gate != 0 (device-side fallback decision).
+template <int M>
+__global__ void __launch_bounds__(256) k_bf16p_gemv(HeadPacked P, const float* __restrict__ X, float* __restrict__ Y,
+                                                    int ldy, const int* __restrict__ gate) {
+  if (gate != nullptr && *gate == 0) return;
+  const int j = threadIdx.x & 7;
+  const int n_raw = blockIdx.x * 32 + (threadIdx.x >> 3);
+  const bool live = n_raw < P.N;
+  const int n = live ? n_raw : P.N - 1;
+  const int G = P.K >> 5;
+  const uint8_t* row = P.data + (size_t)n * G * 44;
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const float* x = X + (size_t)m * P.K;
+    const float acc = bf16p_lane_dot(row, G, x, j, P.cb_lo, P.cb_hi);
+    const float y = hsum8_octet(acc);
+    if (live && j == 0) Y[(size_t)m * ldy + n] = bf16p_patch(P, n, x, y);
+  }
+}
+
+// ------------------------------------------------------------------------------ greedy pick
+// Slots per row m: [0] ordered-int max of r16 logits, [1] winner index.
+__global__ void k_pick_init(int* __restrict__ slots, int M) {
+  const int m = threadIdx.x;
+  if (m < M) { slots[2 * m] = f2ord(-1e30f); slots[2 * m + 1] = 0x7FFFFFFF; }
+}
+__global__ void k_pick_max(const float* __restrict__ Y, int N, int ldy, int* __restrict__ slots, const int* __restrict__ gate) {
+  if (gate != nullptr && *gate == 0) return;
+  const int m = blockIdx.y;
+  float mx = -1e30f;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < N; i += gridDim.x * blockDim.x) mx = fmaxf(mx, r16(Y[(size_t)m * ldy + i]));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(&slots[2 * m], f2ord(mx));
+}
+// lowest index with v >= mx - 2 and cap(v) == cap(mx) (gemma4_engine.cpp:1496)
+__global__ void k_pick_idx(const float* __restrict__ Y, int N, int ldy, int* __restrict__ slots, const int* __restrict__ gate) {
+  if (gate != nullptr && *gate == 0) return;
+  const int m = blockIdx.y;
+  const float mx = ord2f(slots[2 * m]);
+  const float cm = cap_bf(mx), lim = __fsub_rn(mx, 2.0f);
+  int best = 0x7FFFFFFF;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < N; i += gridDim.x * blockDim.x) {
+    const float v = r16(Y[(size_t)m * ldy + i]);
+    if (v >= lim && cap_bf(v) == cm) { best = i; break; }  // grid-stride: later i only larger
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) best = min(best, __shfl_xor_sync(FULL, best, o));
+  if ((threadIdx.x & 31) == 0 && best != 0x7FFFFFFF) atomicMin(&slots[2 * m + 1], best);
+}
+__global__ void k_pick_out(const int* __restrict__ slots, int M, int* __restrict__ out, const int* __restrict__ gate) {
+  if (gate != nullptr && *gate == 0) return;
+  const int m = threadIdx.x;
+  if (m < M) out[m] = slots[2 * m + 1] == 0x7FFFFFFF ? -1 : slots[2 * m + 1];
+}
+
+// ---------------------------------------------------------------------------- screen build
+// Block per row, thread per group for the int4 copy (device nibble layout: byte b = q[b] |
+// q[16+b] << 4); then one thread sums e^2 and w^2 in double in the reference's (group, element)
+// order and writes coef = fma(1e-4, sqrt(w2), sqrt(e2)) (gemma4_engine.cpp:1236-1243).
+__global__ void k_screen_build(const uint16_t* __restrict__ E, int K, uint8_t* __restrict__ W4, uint16_t* __restrict__ S4,
+                               float* __restrict__ coef) {
+  extern __shared__ float scl[];  // [G] scale per group
+  const int n = blockIdx.x, G = K >> 5;
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    float amax = 0.f, w[32];
+    for (int i = 0; i < 32; ++i) { w[i] = bf2f(E[(size_t)n * K + g * 32 + i]); amax = fmaxf(amax, fabsf(w[i])); }
+    const uint32_t sb = f2bf(__fdiv_rn(amax, 7.0f));
+    const float sc = bf2f(sb);
+    S4[(size_t)n * G + g] = (uint16_t)sb;
+    scl[g] = sc;
+    uint32_t qv[32];
+    for (int i = 0; i < 32; ++i) {
+      int v = sc > 0.f ? __float2int_rn(__fdiv_rn(w[i], sc)) : 0;
+      v = max(-8, min(7, v));
+      qv[i] = (uint32_t)(v + 8);
+    }
+    uint32_t out[4] = {0, 0, 0, 0};
+    for (int b = 0; b < 16; ++b) out[b >> 2] |= (qv[b] | (qv[16 + b] << 4)) << (8 * (b & 3));
+    reinterpret_cast<uint4*>(W4 + (size_t)n * (K >> 1))[g] = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double e2 = 0, w2 = 0;
+    for (int g = 0; g < G; ++g) {
+      const float sc = scl[g];
+      for (int i = 0; i < 32; ++i) {
+        const float w = bf2f(E[(size_t)n * K + g * 32 + i]);
+        int v = sc > 0.f ? __float2int_rn(__fdiv_rn(w, sc)) : 0;
+        v = max(-8, min(7, v));
+        const double d = fma(-(double)v, (double)sc, (double)w);  // exact either way: v*sc is exact
+        e2 = fma(d, d, e2);
+        w2 = fma((double)w, (double)w, w2);
+      }
+    }
+    coef[n] = (float)fma(1e-4, sqrt(w2), sqrt(e2));
+  }
+}
+
+// ------------------------------------------------------------------------------------ screen
+struct ScreenWs {
+  float* s;      // [M][N] screen dots, later the fallback logits
+  float* hn;     // [M]
+  int* Lord;     // [M] ordered-int L
+  float* thr;    // [M]
+  int* cnt;      // [M] survivors
+  int* fb;       // [1] fallback flag
+  int* surv;     // [M][lim]
+  float* fval;   // [M][lim]
+  int* slots;    // [2M] pick slots
+};
+static size_t screen_ws_layout(int M, int N, int lim, ScreenWs* w, char* base) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) { char* p = base ? base + off : nullptr; off += (bytes + 255) & ~(size_t)255; return p; };
+  char* s = take(sizeof(float) * (size_t)M * N);
+  char* hn = take(sizeof(float) * M);
+  char* L = take(sizeof(int) * M);
+  char* thr = take(sizeof(float) * M);
+  char* cnt = take(sizeof(int) * M);
+  char* fb = take(sizeof(int));
+  char* surv = take(sizeof(int) * (size_t)M * lim);
+  char* fval = take(sizeof(float) * (size_t)M * lim);
+  char* slots = take(sizeof(int) * 2 * M);
+  if (w) {
+    w->s = (float*)s; w->hn = (float*)hn; w->Lord = (int*)L; w->thr = (float*)thr; w->cnt = (int*)cnt; w->fb = (int*)fb;
+    w->surv = (int*)surv; w->fval = (float*)fval; w->slots = (int*)slots;
+  }
+  return off;
+}
+
+// |h| per row in double, in the order of ss_avx2 (gemma4_engine.cpp:326-343); one warp per row.
+__global__ void k_screen_init(const float* __restrict__ H, int K, int M, ScreenWs w) {
+  const int m = blockIdx.x, lane = threadIdx.x;
+  double s = 0;
+  if (lane < 16) {
+    for (int i = 0; i < K; i += 16) { const double d = H[(size_t)m * K + i + lane]; s = fma(d, d, s); }
+  }
+  // lane l = 4a + b holds s[a][b]; t_b = (s0_b + s1_b) + (s2_b + s3_b); total = (t0 + t2) + (t1 + t3)
+  double v[16];
+#pragma unroll
+  for (int l = 0; l < 16; ++l) v[l] = __shfl_sync(FULL, s, l);
+  if (lane == 0) {
+    double t[4];
+    for (int b = 0; b < 4; ++b) t[b] = (v[b] + v[4 + b]) + (v[8 + b] + v[12 + b]);
+    w.hn[m] = (float)sqrt((t[0] + t[2]) + (t[1] + t[3]));
+    w.Lord[m] = f2ord(-1e30f);
+    w.cnt[m] = 0;
+    if (m == 0) *w.fb = 0;
+  }
+}
+// L = max over rows of fma(-c, hn, s) (screen_task :484, vmx)
+__global__ void k_screen_L(const float* __restrict__ coef, int N, ScreenWs w) {
+  const int m = blockIdx.y;
+  const float hn = w.hn[m];
+  float mx = -1e30f;
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < N; n += gridDim.x * blockDim.x)
+    mx = fmaxf(mx, fmaf(-coef[n], hn, w.s[(size_t)m * N + n]));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(&w.Lord[m], f2ord(mx));
+}
+__global__ void k_screen_thr(int M, ScreenWs w) {
+  const int m = threadIdx.x;
+  if (m < M) w.thr[m] = calc_thr(ord2f(w.Lord[m]));
+}
+// survivors: upper = fma(c, hn, s) >= thr (eval_row :1461); more than lim -> fallback flag.
+// Warp-uniform iteration with one atomic per warp; the order of the list is irrelevant.
+__global__ void k_screen_collect(const float* __restrict__ coef, int N, int lim, ScreenWs w) {
+  const int m = blockIdx.y, lane = threadIdx.x & 31;
+  const float hn = w.hn[m], thr = w.thr[m];
+  const int wstride = gridDim.x * blockDim.x;
+  for (int base = (blockIdx.x * blockDim.x + threadIdx.x) & ~31; base < N; base += wstride) {
+    const int n = base + lane;
+    const bool pass = n < N && fmaf(coef[n], hn, w.s[(size_t)m * N + n]) >= thr;
+    const unsigned mask = __ballot_sync(FULL, pass);
+    if (mask == 0u) continue;
+    int k0 = 0;
+    if (lane == 0) k0 = atomicAdd(&w.cnt[m], __popc(mask));
+    k0 = __shfl_sync(FULL, k0, 0);
+    if (pass) {
+      const int k = k0 + __popc(mask & ((1u << lane) - 1u));
+      if (k < lim) w.surv[(size_t)m * lim + k] = n;
+      else *w.fb = 1;
+    }
+  }
+}
+// rescore survivors with the exact head (octet per survivor, resc_task :540-571): fval = r16(y)
+__global__ void __launch_bounds__(256) k_screen_rescore(HeadPacked P, const float* __restrict__ H, int lim, ScreenWs w) {
+  if (*w.fb) return;
+  const int m = blockIdx.y;
+  const int count = min(w.cnt[m], lim);
+  const int j = threadIdx.x & 7;
+  const int k_raw = blockIdx.x * 32 + (threadIdx.x >> 3);
+  if (blockIdx.x * 32 >= count) return;  // whole block past the survivors (uniform)
+  const bool live = k_raw < count;
+  const int k = live ? k_raw : 0;
+  const int n = w.surv[(size_t)m * lim + k];
+  const int G = P.K >> 5;
+  const float* x = H + (size_t)m * P.K;
+  const float acc = bf16p_lane_dot(P.data + (size_t)n * G * 44, G, x, j, P.cb_lo, P.cb_hi);
+  const float y = hsum8_octet(acc);
+  if (live && j == 0) w.fval[(size_t)m * lim + k] = r16(bf16p_patch(P, n, x, y));
+}
+// pick among survivors: max value, then lowest index with the tie rule (eval_row :1469-1471 with
+// ties to the lowest index).  One block per row.
+__global__ void k_screen_pick(int lim, ScreenWs w, int* __restrict__ out, int* __restrict__ nsurv) {
+  const int m = blockIdx.x;
+  const int count = min(w.cnt[m], lim);
+  if (threadIdx.x == 0) nsurv[m] = *w.fb ? -1 : count;
+  if (*w.fb) return;
+  __shared__ float smx[32];
+  __shared__ int sidx[32];
+  float mx = -1e30f;
+  for (int k = threadIdx.x; k < count; k += blockDim.x) mx = fmaxf(mx, w.fval[(size_t)m * lim + k]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+  if ((threadIdx.x & 31) == 0) smx[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = -1e30f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, smx[i]);
+  const float cm = cap_bf(mx), lo = __fsub_rn(mx, 2.0f);
+  int best = 0x7FFFFFFF;
+  for (int k = threadIdx.x; k < count; k += blockDim.x) {
+    const float v = w.fval[(size_t)m * lim + k];
+    if (v >= lo && cap_bf(v) == cm) best = min(best, w.surv[(size_t)m * lim + k]);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) best = min(best, __shfl_xor_sync(FULL, best, o));
+  if ((threadIdx.x & 31) == 0) sidx[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) best = min(best, sidx[i]);
+    out[m] = best == 0x7FFFFFFF ? -1 : best;
+  }
+}
+// fallback pick writes the winners (only when the flag is set)
+__global__ void k_screen_fb_out(const int* __restrict__ slots, int M, const ScreenWs w, int* __restrict__ out) {
+  if (!*w.fb) return;
+  const int m = threadIdx.x;
+  if (m < M) out[m] = slots[2 * m + 1] == 0x7FFFFFFF ? -1 : slots[2 * m + 1];
+}
+
+}  // namespace g4
+
+G4_STATUS_READER(head)
+
+using namespace g4;
+
+// ---------------------------------------------------------------------------- device init
+static std::mutex g_init_mu;
+static bool g_init_done[128];
+
+static bool device_ready() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return false;
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  return g_init_done[dev];
+}
+
+extern "C" int g4_device_init(void) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "g4_device_init: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 128) return set_error(G4_ERR_UNSUPPORTED, "g4_device_init: device %d", dev);
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  if (g_init_done[dev]) return G4_OK;
+  // softcap of every bf16 value: r16(30 * tanhf(s / 30)) with the host libm (gemma4_engine.cpp:1410)
+  std::vector<float> tab(65536);
+  for (uint32_t b = 0; b < 65536; ++b) {
+    uint32_t u = b << 16;
+    float s;
+    std::memcpy(&s, &u, 4);
+    float c = 30.0f * tanhf(s / 30.0f);
+    uint32_t cu;
+    std::memcpy(&cu, &c, 4);
+    if ((cu & 0x7fffffffu) > 0x7f800000u) cu = ((cu >> 16) | 0x40u) << 16;
+    else cu = ((cu + 0x7fffu + ((cu >> 16) & 1u)) >> 16) << 16;
+    std::memcpy(&tab[b], &cu, 4);
+  }
+  e = cudaMemcpyToSymbol(g_cap_table, tab.data(), sizeof(float) * 65536);
+  if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "g4_device_init: %s", cudaGetErrorString(e));
+  g_init_done[dev] = true;
+  return G4_OK;
+}
+
+#define G4_NEED_INIT(fn) \
+  G4_REQUIRE(device_ready(), fn ": call g4_device_init() on this device first")
+
+// ------------------------------------------------------------------------------ packing ABI
+extern "C" int g4_bf16p_codebook(const uint16_t* E, long long count, uint8_t* cb8, void* ws, size_t ws_bytes,
+                                 void* stream) {
+  G4_REQUIRE(E && cb8 && ws && count > 0, "g4_bf16p_codebook: bad arguments");
+  if (ws_bytes < 256 * sizeof(unsigned long long)) return set_error(G4_ERR_NOMEM, "g4_bf16p_codebook: workspace < 2048 B");
+  cudaStream_t st = as_stream(stream);
+  unsigned long long* hist = static_cast<unsigned long long*>(ws);
+  cudaMemsetAsync(hist, 0, 256 * sizeof(unsigned long long), st);
+  k_exp_hist<<<1184, 256, 0, st>>>(E, count, hist);
+  if (int rc = check_launch("k_exp_hist")) return rc;
+  unsigned long long h[256];
+  cudaError_t e = cudaMemcpyAsync(h, hist, sizeof h, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "g4_bf16p_codebook: %s", cudaGetErrorString(e));
+  int ord[256];
+  for (int i = 0; i < 256; ++i) ord[i] = i;
+  std::stable_sort(ord, ord + 256, [&](int a, int b) { return h[a] > h[b]; });
+  for (int i = 0; i < 8; ++i) cb8[i] = (uint8_t)ord[i];
+  return G4_OK;
+}
+
+static Codebook make_cb(const uint8_t* cb8) { Codebook c; std::memcpy(c.e, cb8, 8); return c; }
+
+extern "C" int g4_bf16p_count(const uint16_t* E, int N, int K, const uint8_t* cb8, long long* exc_ptr, void* ws,
+                              size_t ws_bytes, long long* total, void* stream) {
+  G4_REQUIRE(E && cb8 && exc_ptr && ws && total && N > 0 && K > 0 && K % 32 == 0, "g4_bf16p_count: bad arguments");
+  if (ws_bytes < sizeof(long long) * (size_t)N) return set_error(G4_ERR_NOMEM, "g4_bf16p_count: workspace < 8*N bytes");
+  cudaStream_t st = as_stream(stream);
+  long long* cnt = static_cast<long long*>(ws);
+  k_bf16p_count<<<N, 256, 0, st>>>(E, K, make_cb(cb8), cnt);
+  if (int rc = check_launch("k_bf16p_count")) return rc;
+  k_scan_rows<<<1, 1024, 0, st>>>(cnt, N, exc_ptr);
+  if (int rc = check_launch("k_scan_rows")) return rc;
+  cudaError_t e = cudaMemcpyAsync(total, exc_ptr + N, sizeof(long long), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "g4_bf16p_count: %s", cudaGetErrorString(e));
+  return G4_OK;
+}
+
+extern "C" int g4_bf16p_pack(const uint16_t* E, int N, int K, const uint8_t* cb8, uint8_t* data,
+                             const long long* exc_ptr, uint16_t* exc_col, float* exc_delta, void* stream) {
+  G4_REQUIRE(E && cb8 && data && exc_ptr && N > 0 && K > 0 && K % 32 == 0, "g4_bf16p_pack: bad arguments");
+  G4_REQUIRE(aligned(data, 4), "g4_bf16p_pack: data must be 4-byte aligned");
+  const int G = K / 32;
+  k_bf16p_fill<<<N, 64, sizeof(int) * G, as_stream(stream)>>>(E, K, make_cb(cb8), data, exc_ptr, exc_col, exc_delta);
+  return check_launch("k_bf16p_fill");
+}
+
+static HeadPacked make_head(const uint8_t* data, const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col,
+                            const float* exc_delta, int N, int K) {
+  HeadPacked P;
+  P.data = data; P.exc_ptr = exc_ptr; P.exc_col = exc_col; P.exc_delta = exc_delta; P.N = N; P.K = K;
+  std::memcpy(&P.cb_lo, cb8, 4);
+  std::memcpy(&P.cb_hi, cb8 + 4, 4);
+  return P;
+}
+
+template <int M>
+static void launch_head_gemv(const HeadPacked& P, const float* X, float* Y, int ldy, const int* gate, cudaStream_t st) {
+  k_bf16p_gemv<M><<<(P.N + 31) / 32, 256, 0, st>>>(P, X, Y, ldy, gate);
+}
+static int head_gemv(const HeadPacked& P, const float* X, int M, float* Y, int ldy, const int* gate, cudaStream_t st) {
+  switch (M) {
+    case 1: launch_head_gemv<1>(P, X, Y, ldy, gate, st); break;
+    case 2: launch_head_gemv<2>(P, X, Y, ldy, gate, st); break;
+    case 3: launch_head_gemv<3>(P, X, Y, ldy, gate, st); break;
+    default: launch_head_gemv<4>(P, X, Y, ldy, gate, st); break;
+  }
+  return check_launch("k_bf16p_gemv");
+}
+
+extern "C" int g4_bf16p_gemm(const uint8_t* data, const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col,
+                             const float* exc_delta, int N, int K, const float* X, int M, float* Y, int ldy,
+                             void* stream) {
+  G4_REQUIRE(data && cb8 && exc_ptr && X && Y && N > 0 && K > 0 && K % 32 == 0 && M >= 1 && M <= 4 && ldy >= N,
+             "g4_bf16p_gemm: bad arguments N=%d K=%d M=%d", N, K, M);
+  return head_gemv(make_head(data, cb8, exc_ptr, exc_col, exc_delta, N, K), X, M, Y, ldy, nullptr, as_stream(stream));
+}
+
+static int pick(const float* Y, int M, int N, int ldy, int* slots, int* out, const int* gate, cudaStream_t st) {
+  k_pick_init<<<1, 32, 0, st>>>(slots, M);
+  k_pick_max<<<dim3(296, M), 256, 0, st>>>(Y, N, ldy, slots, gate);
+  k_pick_idx<<<dim3(296, M), 256, 0, st>>>(Y, N, ldy, slots, gate);
+  if (out) k_pick_out<<<1, 32, 0, st>>>(slots, M, out, gate);
+  return check_launch("head pick");
+}
+
+extern "C" int g4_head_argmax(const float* Y, int M, int N, int ldy, int* out_idx, void* ws, size_t ws_bytes,
+                              void* stream) {
+  G4_REQUIRE(Y && out_idx && ws && M >= 1 && M <= 16 && N > 0 && ldy >= N, "g4_head_argmax: bad arguments");
+  G4_NEED_INIT("g4_head_argmax");
+  if (ws_bytes < sizeof(int) * 2 * (size_t)M) return set_error(G4_ERR_NOMEM, "g4_head_argmax: workspace < 8*M bytes");
+  return pick(Y, M, N, ldy, static_cast<int*>(ws), out_idx, nullptr, as_stream(stream));
+}
+
+extern "C" int g4_screen_build(const uint16_t* E, int N, int K, uint8_t* W4p, uint16_t* S4, float* coef, void* stream) {
+  G4_REQUIRE(E && W4p && S4 && coef && N > 0 && K > 0 && K % 32 == 0, "g4_screen_build: bad arguments");
+  G4_REQUIRE(aligned(W4p, 16), "g4_screen_build: W4p must be 16-byte aligned");
+  k_screen_build<<<N, 64, sizeof(float) * (K / 32), as_stream(stream)>>>(E, K, W4p, S4, coef);
+  return check_launch("k_screen_build");
+}
+
+extern "C" size_t g4_head_screen_ws_bytes(int M, int N, int lim) { return screen_ws_layout(M, N, lim, nullptr, nullptr); }
+
+extern "C" int g4_head_screen(const uint8_t* W4p, const uint16_t* S4, const float* coef, const uint8_t* data,
+                              const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col,
+                              const float* exc_delta, int N, int K, const float* H, int M, int lim, int* out_idx,
+                              int* out_nsurv, void* ws, size_t ws_bytes, void* stream) {
+  G4_REQUIRE(W4p && S4 && coef && data && cb8 && exc_ptr && H && out_idx && out_nsurv && ws,
+             "g4_head_screen: null pointer");
+  G4_REQUIRE(M >= 1 && M <= 4 && N > 0 && K > 0 && K % 256 == 0 && lim > 0, "g4_head_screen: bad shape M=%d N=%d K=%d", M,
+             N, K);
+  G4_NEED_INIT("g4_head_screen");
+  const size_t need = screen_ws_layout(M, N, lim, nullptr, nullptr);
+  if (ws_bytes < need) return set_error(G4_ERR_NOMEM, "g4_head_screen: workspace %zu < %zu bytes", ws_bytes, need);
+  G4_REQUIRE(aligned(ws, 256), "g4_head_screen: workspace must be 256-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  ScreenWs w;
+  screen_ws_layout(M, N, lim, &w, static_cast<char*>(ws));
+  const HeadPacked P = make_head(data, cb8, exc_ptr, exc_col, exc_delta, N, K);
+  k_screen_init<<<M, 32, 0, st>>>(H, K, M, w);
+  if (int rc = check_launch("k_screen_init")) return rc;
+  if (int rc = g4_w4g32_gemm(W4p, S4, H, nullptr, M, N, K, w.s, N, stream)) return rc;
+  k_screen_L<<<dim3(296, M), 256, 0, st>>>(coef, N, w);
+  k_screen_thr<<<1, 32, 0, st>>>(M, w);
+  k_screen_collect<<<dim3(296, M), 256, 0, st>>>(coef, N, lim, w);
+  k_screen_rescore<<<dim3((lim + 31) / 32, M), 256, 0, st>>>(P, H, lim, w);
+  k_screen_pick<<<M, 256, 0, st>>>(lim, w, out_idx, out_nsurv);
+  if (int rc = check_launch("screen")) return rc;
+  // fallback: full exact head for all rows, gated on the device flag
+  if (int rc = head_gemv(P, H, M, w.s, N, w.fb, st)) return rc;
+  if (int rc = pick(w.s, M, N, N, w.slots, nullptr, w.fb, st)) return rc;
+  k_screen_fb_out<<<1, 32, 0, st>>>(w.slots, M, w, out_idx);
+  return check_launch("k_screen_fb_out");
+}

@@ -27,6 +27,15 @@ SIGNATURES = {
     "g4_w4g32_gemm": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _I, _P]),
     "g4_w4a8_quant": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "g4_w4a8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _P]),
+    "g4_device_init": (_I, []),
+    "g4_bf16p_codebook": (_I, [_P, ctypes.c_longlong, _P, _P, _SZ, _P]),
+    "g4_bf16p_count": (_I, [_P, _I, _I, _P, _P, _P, _SZ, ctypes.POINTER(ctypes.c_longlong), _P]),
+    "g4_bf16p_pack": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _P]),
+    "g4_bf16p_gemm": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _I, _P, _I, _P]),
+    "g4_head_argmax": (_I, [_P, _I, _I, _I, _P, _P, _SZ, _P]),
+    "g4_screen_build": (_I, [_P, _I, _I, _P, _P, _P, _P]),
+    "g4_head_screen_ws_bytes": (_SZ, [_I, _I, _I]),
+    "g4_head_screen": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _SZ, _P]),
     "g4_attn_splitkv_ws_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "g4_attn_splitkv": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
     "g4_attn_splitkv_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
@@ -156,3 +165,78 @@ def attn_splitkv(Kc, Vc, q, pos, lo, T=8, ws=None, out=None):
     check(lib().g4_attn_splitkv(_ptr(Kc), _ptr(Vc), _ptr(q), ia, la, M, nh, hd, kmin, kmax, T, _ptr(out), _ptr(ws),
                                 ws.numel() * ws.element_size(), _stream()), "g4_attn_splitkv")
     return out
+
+
+# ------------------------------------------------------------------ output head
+def device_init():
+    check(lib().g4_device_init(), "g4_device_init")
+
+
+class PackedHead:
+    """bf16-exp3 packed head on the device (bf16p::Packed): data, codebook, CSR exceptions."""
+
+    def __init__(self, E):
+        import torch
+        _dev(E, "E")
+        N, K = E.shape
+        self.N, self.K = N, K
+        ws = torch.empty(max(2048, 8 * N), dtype=torch.uint8, device=E.device)
+        cb = (ctypes.c_uint8 * 8)()
+        check(lib().g4_bf16p_codebook(_ptr(E), E.numel(), cb, _ptr(ws), ws.numel(), _stream()), "g4_bf16p_codebook")
+        self.cb_host = bytes(cb)
+        self.cb = ctypes.create_string_buffer(self.cb_host, 8)
+        self.exc_ptr = torch.empty(N + 1, dtype=torch.int64, device=E.device)
+        total = ctypes.c_longlong(0)
+        check(lib().g4_bf16p_count(_ptr(E), N, K, self.cb, _ptr(self.exc_ptr), _ptr(ws), ws.numel(), ctypes.byref(total),
+                                   _stream()), "g4_bf16p_count")
+        self.n_exc = total.value
+        self.data = torch.empty(N * (K // 32) * 44, dtype=torch.uint8, device=E.device)
+        self.exc_col = torch.empty(max(1, self.n_exc), dtype=torch.int16, device=E.device)
+        self.exc_delta = torch.empty(max(1, self.n_exc), dtype=torch.float32, device=E.device)
+        check(lib().g4_bf16p_pack(_ptr(E), N, K, self.cb, _ptr(self.data), _ptr(self.exc_ptr), _ptr(self.exc_col),
+                                  _ptr(self.exc_delta), _stream()), "g4_bf16p_pack")
+
+    def args(self):
+        return (_ptr(self.data), self.cb, _ptr(self.exc_ptr), _ptr(self.exc_col), _ptr(self.exc_delta))
+
+    def logits(self, X, out=None):
+        import torch
+        M = X.shape[0]
+        Y = out if out is not None else torch.empty((M, self.N), dtype=torch.float32, device=X.device)
+        check(lib().g4_bf16p_gemm(*self.args(), self.N, self.K, _ptr(X), M, _ptr(Y), Y.stride(0), _stream()),
+              "g4_bf16p_gemm")
+        return Y
+
+
+def head_argmax(Y):
+    import torch
+    M, N = Y.shape
+    out = torch.empty(M, dtype=torch.int32, device=Y.device)
+    ws = torch.empty(2 * M, dtype=torch.int32, device=Y.device)
+    check(lib().g4_head_argmax(_ptr(Y), M, N, Y.stride(0), _ptr(out), _ptr(ws), ws.numel() * 4, _stream()),
+          "g4_head_argmax")
+    return out
+
+
+def screen_build(E):
+    import torch
+    N, K = E.shape
+    W4 = torch.empty((N, K // 2), dtype=torch.uint8, device=E.device)
+    S4 = torch.empty((N, K // 32), dtype=torch.int16, device=E.device)
+    coef = torch.empty(N, dtype=torch.float32, device=E.device)
+    check(lib().g4_screen_build(_ptr(E), N, K, _ptr(W4), _ptr(S4), _ptr(coef), _stream()), "g4_screen_build")
+    return W4, S4, coef
+
+
+def head_screen(screen, head, H, lim=30000):
+    """Certified screen + rescoring + pick for hidden rows H [M, K]; returns (idx, nsurv)."""
+    import torch
+    W4, S4, coef = screen
+    M, K = H.shape
+    need = lib().g4_head_screen_ws_bytes(M, head.N, lim)
+    ws = torch.empty(need, dtype=torch.uint8, device=H.device)
+    idx = torch.empty(M, dtype=torch.int32, device=H.device)
+    ns = torch.empty(M, dtype=torch.int32, device=H.device)
+    check(lib().g4_head_screen(_ptr(W4), _ptr(S4), _ptr(coef), *head.args(), head.N, K, _ptr(H), M, lim, _ptr(idx),
+                               _ptr(ns), _ptr(ws), need, _stream()), "g4_head_screen")
+    return idx, ns

@@ -71,6 +71,43 @@ int g4_w4a8_quant(const float* X, int M, int K, int8_t* q, float* sx, int32_t* s
 int g4_w4a8_gemm(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
                  int M, int N, int K, float* Y, int ldy, void* stream);
 
+/* ---------------------------------------------------------------- output head */
+
+/* Once per device, before any stream capture: uploads the softcap table (r16(30*tanh(s/30)) of
+ * every bf16 value, computed with the host libm) that the head entry points use. */
+int g4_device_init(void);
+
+/* Codebook of the bf16-exp3 head: the 8 most frequent exponents of E (stable order by count),
+ * gemma4_engine.cpp:1232-1234.  E dev bf16 [count]; cb8 host [8]; ws dev >= 2048 B.  Synchronous. */
+int g4_bf16p_codebook(const uint16_t* E, long long count, uint8_t* cb8, void* ws, size_t ws_bytes, void* stream);
+/* First half of bf16p::pack (bf16_exp3_head.h:26-49): exceptions per row, exclusive-scanned into
+ * exc_ptr dev [N+1]; *total (host) = exception count.  ws dev >= 8*N B.  Synchronous. */
+int g4_bf16p_count(const uint16_t* E, int N, int K, const uint8_t* cb8, long long* exc_ptr, void* ws, size_t ws_bytes,
+                   long long* total, void* stream);
+/* Second half: the 44-byte groups (data dev [N*K/32*44]) and the CSR exceptions (exc_col dev,
+ * exc_delta dev, sized by g4_bf16p_count), byte-identical to bf16p::pack. */
+int g4_bf16p_pack(const uint16_t* E, int N, int K, const uint8_t* cb8, uint8_t* data, const long long* exc_ptr,
+                  uint16_t* exc_col, float* exc_delta, void* stream);
+/* Raw head logits Y[m*ldy+n] (before bf16 rounding) in the fp32 order of bf16p::rows_tile
+ * (bf16_exp3_head.h:84-107) / head_task (gemma4_engine.cpp:574-579).  X dev [M][K], M <= 4. */
+int g4_bf16p_gemm(const uint8_t* data, const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col,
+                  const float* exc_delta, int N, int K, const float* X, int M, float* Y, int ldy, void* stream);
+/* Greedy pick over raw logits: r16, max, then the lowest index whose softcapped value equals the
+ * max's (gemma4_engine.cpp:1491-1497).  out_idx dev [M]; ws dev >= 8*M B. */
+int g4_head_argmax(const float* Y, int M, int N, int ldy, int* out_idx, void* ws, size_t ws_bytes, void* stream);
+/* Int4 screen copy of the head: device W4 layout (see g4_w4_pack), bf16 scales f2bf(amax/7) and
+ * the per-row error coefficient (gemma4_engine.cpp:1235-1244, for any K). */
+int g4_screen_build(const uint16_t* E, int N, int K, uint8_t* W4p, uint16_t* S4, float* coef, void* stream);
+size_t g4_head_screen_ws_bytes(int M, int N, int lim);
+/* Certified screen + exact rescoring + pick for M <= 4 hidden rows H dev [M][K]
+ * (screen_task :460-538, eval_row :1453-1474, resc_task :540-571), all on the device; more than
+ * lim survivors (the reference uses 30000) falls back to the full exact head, as the reference
+ * does.  out_idx dev [M] winners; out_nsurv dev [M] survivor counts (-1 = fallback). */
+int g4_head_screen(const uint8_t* W4p, const uint16_t* S4, const float* coef, const uint8_t* data, const uint8_t* cb8,
+                   const long long* exc_ptr, const uint16_t* exc_col, const float* exc_delta, int N, int K,
+                   const float* H, int M, int lim, int* out_idx, int* out_nsurv, void* ws, size_t ws_bytes,
+                   void* stream);
+
 /* ---------------------------------------------------------------- split-KV decode attention */
 
 /* Workspace bytes g4_attn_splitkv needs for these sizes. */

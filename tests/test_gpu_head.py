@@ -1,0 +1,142 @@
+"""Output head on the GPU against the oracle (pinned to the reference's bf16p::pack / rows_tile /
+head_task / screen_task by tests/test_oracle_golden.py): codebook, pack bytes, exact logits,
+greedy pick with the softcap tie rule, int4 screen build, and the certified screen with
+rescoring and fallback.  Argmax indices and survivor sets must be bit-exact (north_star)."""
+import pathlib
+
+import numpy as np
+import pytest
+
+from oracle_lib import (bf16_bits, bf16_to_f32, or_codebook, or_head_logits, or_pack, or_pick, or_screen_build,
+                        or_screen_row)
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from g4pkg import g4  # noqa: E402
+
+GOLD = pathlib.Path(__file__).resolve().parent / "golden"
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def to_device_layout(W):
+    N, Kh = W.shape
+    t = np.empty((N, 2 * Kh), np.uint8)
+    t[:, 0::2] = W & 15
+    t[:, 1::2] = W >> 4
+    t = t.reshape(N, -1, 32)
+    return (t[:, :, :16] | (t[:, :, 16:] << 4)).reshape(N, Kh)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _init():
+    g4.device_init()
+
+
+def test_pack_and_logits_golden():
+    d = np.load(GOLD / "bf16p.npz")
+    E = d["E"]
+    N, K = E.shape
+    head = g4.PackedHead(dev(E.view(np.int16)))
+    assert head.cb_host == bytes(d["cb"])
+    assert np.array_equal(head.data.cpu().numpy(), d["data"])
+    assert np.array_equal(head.exc_ptr.cpu().numpy(), d["exc_ptr"])
+    ne = len(d["exc_col"])
+    assert head.n_exc == ne
+    assert np.array_equal(head.exc_col.cpu().numpy()[:ne].view(np.uint16), d["exc_col"])
+    assert np.array_equal(bits(head.exc_delta.cpu().numpy()[:ne]), bits(d["exc_delta"]))
+    Y = head.logits(dev(d["X"])).cpu().numpy()
+    assert np.array_equal(bits(Y), bits(d["Y"]))
+    idx = g4.head_argmax(dev(Y)).cpu().numpy()
+    assert list(idx) == [or_pick(Y[m]) for m in range(Y.shape[0])]
+
+
+def test_pick_tie_rule():
+    raw = np.zeros((2, 4096), np.float32)
+    raw[0, [70, 900, 3000]] = [5.0, 5.0009766, 5.0]  # equal after bf16 rounding: lowest index wins
+    raw[1, [11, 12]] = [-1.0, 7.0]
+    raw[1, 4000] = 7.01  # bf16(7.01) == 7.0
+    idx = g4.head_argmax(dev(raw)).cpu().numpy()
+    assert list(idx) == [or_pick(raw[0]), or_pick(raw[1])] == [70, 12]
+
+
+@pytest.fixture(scope="module")
+def full_head():
+    """262144 x 2048 bf16 head ~ N(0, 0.02), packed and screened on the GPU and by the oracle."""
+    rng = np.random.default_rng(262144)
+    N, K = 262144, 2048
+    E = bf16_bits(rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+    Ed = dev(E.view(np.int16))
+    head = g4.PackedHead(Ed)
+    screen = g4.screen_build(Ed)
+    torch.cuda.synchronize()
+    return E, head, screen, rng, or_screen_build(E)
+
+
+def test_full_pack_and_screen_build(full_head):
+    E, head, screen, _, oscreen = full_head
+    cb = or_codebook(E)
+    assert head.cb_host == bytes(cb)
+    data, ep, col, dl = or_pack(E, cb)
+    assert head.n_exc == len(col)
+    assert np.array_equal(head.exc_ptr.cpu().numpy(), ep)
+    assert np.array_equal(head.data.cpu().numpy(), data)
+    W4, S4, coef = oscreen
+    assert np.array_equal(screen[0].cpu().numpy(), to_device_layout(W4))
+    assert np.array_equal(screen[1].cpu().numpy().view(np.uint16), S4)
+    assert np.array_equal(bits(screen[2].cpu().numpy()), bits(coef))
+
+
+def test_screen_random_rows_fall_back_to_exact_argmax(full_head):
+    """configs[2] as specified: h ~ N(0,1)/sqrt(2048), M = 4.  Every row survives the bound, so the
+    screen falls back to the full exact head, whose argmax must equal the oracle's."""
+    E, head, screen, rng, _ = full_head
+    N, K = E.shape
+    H = (rng.standard_normal((4, K), dtype=np.float32) / np.float32(np.sqrt(K))).astype(np.float32)
+    idx, ns = g4.head_screen(screen, head, dev(H))
+    idx, ns = idx.cpu().numpy(), ns.cpu().numpy()
+    assert list(ns) == [-1, -1, -1, -1]
+    Y = head.logits(dev(H)).cpu().numpy()
+    packed = (head.data.cpu().numpy(), head.exc_ptr.cpu().numpy(),
+              head.exc_col.cpu().numpy()[:head.n_exc].view(np.uint16), head.exc_delta.cpu().numpy()[:head.n_exc])
+    sub = slice(0, 32768)  # exact logits for a slice (the oracle dot over the full head is slow)
+    Yo = or_head_logits((packed[0][: 32768 * (K // 32) * 44], packed[1][: 32769], packed[2], packed[3]),
+                        np.frombuffer(head.cb_host, np.uint8), 32768, K, H)
+    assert np.array_equal(bits(Y[:, sub]), bits(Yo))
+    assert list(idx) == [or_pick(Y[m]) for m in range(4)]
+    assert list(g4.head_argmax(dev(Y)).cpu().numpy()) == list(idx)
+
+
+def test_screen_planted_winners(full_head):
+    """Planted hidden states (h along a head row): the screen keeps few rows, the survivor count
+    equals the oracle's, and the winner is the exact-head winner."""
+    E, head, screen, rng, (W4, S4, coef) = full_head
+    N, K = E.shape
+    H = []
+    for j, (a, b) in zip([123457, 5], [(24.0, 8.0), (2.4, 7.6)]):
+        w = bf16_to_f32(E[j])
+        u = w / np.float32(np.linalg.norm(w))
+        noise = rng.standard_normal(K, dtype=np.float32) / np.float32(np.sqrt(K))
+        H.append((np.float32(a) * u + np.float32(b) * noise).astype(np.float32))
+    H = np.stack(H)
+    idx, ns = g4.head_screen(screen, head, dev(H))
+    idx, ns = idx.cpu().numpy(), ns.cpu().numpy()
+    Y = head.logits(dev(H)).cpu().numpy()
+    survs = [or_screen_row(W4, S4, coef, H[m])[0] for m in range(2)]
+    # the batch falls back as a whole when any row has more than lim survivors (as the reference
+    # falls back for the whole verify group when any evaluated row overflows)
+    fallback = any(sv is None for sv in survs)
+    for m in range(2):
+        assert ns[m] == (-1 if fallback else len(survs[m])), (m, ns[m], [None if v is None else len(v) for v in survs])
+        assert idx[m] == or_pick(Y[m])
+    assert idx[0] == 123457 and survs[0] is not None and list(survs[0]) == [123457]
+    # the strong plant alone never falls back: one survivor
+    idx1, ns1 = g4.head_screen(screen, head, dev(H[:1]))
+    assert int(ns1.cpu()[0]) == 1 and int(idx1.cpu()[0]) == 123457
