@@ -1,0 +1,550 @@
+// The speculative greedy-decode engine on one GPU: the synthetic E2B target (g4_model.cuh), its
+// MTP drafter, prompt lookup, batched verification and greedy acceptance.  The control flow is the
+// reference's run_req spec loop (gemma4_engine.cpp:1582-1663) in chain mode; the forward pass is
+// its fwd lambda (:1256-1502) and the draft step its draft_step (:1534-1563), both at the
+// synthetic dimensions.  Every kernel launch goes to the engine's stream.
+#include "g4_api.h"
+#include "g4_layers.cuh"
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+namespace g4 {
+
+#define ECK(call)                                                                                  \
+  do {                                                                                             \
+    cudaError_t e_ = (call);                                                                       \
+    if (e_ != cudaSuccess) return set_error(G4_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+#define RCK(call)              \
+  do {                         \
+    int rc_ = (call);          \
+    if (rc_ != G4_OK) return rc_; \
+  } while (0)
+
+struct Lin {  // one int4 W4G32 matrix in device layout
+  uint8_t* w = nullptr;
+  uint16_t* s = nullptr;
+  int N = 0, K = 0;
+};
+struct TLayer {
+  Lin qkv, o, gu, down;
+  float *in_ln, *post_attn, *pre_ff, *post_ff, *qn, *kn;
+  bool global;
+};
+struct DLayerW {
+  Lin q, o, gu, down;
+  float *in_ln, *post_attn, *pre_ff, *post_ff, *qn;
+  bool global;
+};
+
+}  // namespace g4
+
+struct g4_engine {
+  g4_engine_config cfg;
+  g4::ModelDims d;
+  cudaStream_t st = nullptr;
+  std::vector<void*> allocs;
+  // weights
+  std::vector<g4::TLayer> L;
+  std::vector<g4::DLayerW> DL;
+  g4::Lin dpre, dpost, dcent;
+  float *fnorm = nullptr, *dnorm = nullptr;
+  uint16_t* E = nullptr;
+  // head
+  uint8_t *hdata = nullptr, *sW4 = nullptr;
+  uint16_t* sS4 = nullptr;
+  float* scoef = nullptr;
+  long long* hexc_ptr = nullptr;
+  uint16_t* hexc_col = nullptr;
+  float* hexc_delta = nullptr;
+  uint8_t cb8[8];
+  // caches and tables
+  uint16_t *Kc = nullptr, *Vc = nullptr;  // [NL][ctx][HD]
+  float* rope[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [type][cos|sin] [ctx][HD/2]
+  // activations (M <= MMAX)
+  int MMAX = 32;
+  float *x, *a, *qkv, *att, *o, *gu, *act, *hbuf, *mlp_in, *qs;
+  int8_t* xq;
+  float* xsx;
+  int32_t* xsum;
+  int* toks;
+  int* G;
+  void* attn_ws = nullptr;
+  size_t attn_ws_bytes = 0;
+  void* head_ws = nullptr;
+  size_t head_ws_bytes = 0;
+  int* head_ns = nullptr;
+  // drafter activations
+  float *dcomb, *dx, *da, *dq, *dopt, *dgu, *dact, *dh, *bcur, *dscore, *cscore, *hprev, *hnext;
+  int *cand, *dtok;
+  bool i8_active = false;
+  g4_engine_stats stats{};
+};
+
+using namespace g4;
+
+extern "C" int g4_engine_default_config(g4_engine_config* c) {
+  if (!c) return set_error(G4_ERR_INVALID, "g4_engine_default_config: null pointer");
+  std::memset(c, 0, sizeof *c);
+  c->hidden = 2048; c->n_layers = 30; c->mlp = 8192; c->vocab = 262144; c->ctx_max = 8192;
+  c->prefill_block = 32; c->k_draft = 3; c->ngram = 2; c->ngram_len = 3; c->prefill_int8 = 1; c->decode_int8 = 1;
+  c->head_screen = 1; c->screen_lim = 30000; c->attn_chunks = 8; c->att_par = 192; c->drafter = 1; c->seed = 20261201ull;
+  return G4_OK;
+}
+
+static int ealloc(g4_engine* e, void** p, size_t bytes) {
+  cudaError_t r = cudaMalloc(p, bytes < 256 ? 256 : bytes);
+  if (r != cudaSuccess) return set_error(G4_ERR_CUDA, "g4_engine: cudaMalloc(%zu): %s", bytes, cudaGetErrorString(r));
+  e->allocs.push_back(*p);
+  return G4_OK;
+}
+template <class T>
+static int ealloc_t(g4_engine* e, T** p, size_t count) { return ealloc(e, reinterpret_cast<void**>(p), count * sizeof(T)); }
+
+static unsigned gridfor(long long n, int block = 256) { return (unsigned)std::min<long long>((n + block - 1) / block, 1 << 20); }
+
+// Generate a stack of int4 matrices (ids, row counts) as one device-layout matrix of K columns.
+static int gen_lin(g4_engine* e, Lin& lin, const std::vector<std::pair<uint64_t, int>>& parts, int K, uint8_t* tmp) {
+  int N = 0;
+  for (auto& p : parts) N += p.second;
+  lin.N = N; lin.K = K;
+  RCK(ealloc_t(e, &lin.w, (size_t)N * K / 2));
+  RCK(ealloc_t(e, &lin.s, (size_t)N * K / 32));
+  size_t roff = 0, soff = 0;
+  for (auto& p : parts) {
+    const long long nb = (long long)p.second * K / 2, ns = (long long)p.second * K / 32;
+    k_gen_w4<<<gridfor(nb), 256, 0, e->st>>>(e->cfg.seed, p.first, nb, tmp + roff);
+    k_gen_scales<<<gridfor(ns), 256, 0, e->st>>>(e->cfg.seed, p.first | T_SCALES, ns, lin.s + soff);
+    roff += nb; soff += ns;
+  }
+  RCK(g4_w4_pack(tmp, N, K, lin.w, e->st));
+  return check_launch("gen_lin");
+}
+static int gen_norm(g4_engine* e, float** p, uint64_t id, int n, float mul) {
+  RCK(ealloc_t(e, p, n));
+  k_gen_norm<<<gridfor(n), 256, 0, e->st>>>(e->cfg.seed, id, n, mul, *p);
+  return check_launch("gen_norm");
+}
+
+extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
+  if (!cfg || !out) return set_error(G4_ERR_INVALID, "g4_engine_create: null pointer");
+  const g4_engine_config c = *cfg;
+  G4_REQUIRE(c.hidden % 256 == 0 && c.hidden >= 256 && c.mlp % 256 == 0 && c.n_layers >= 1 && c.vocab % 128 == 0 &&
+                 c.vocab <= (1 << 18) && (c.vocab & (c.vocab - 1)) == 0 && c.ctx_max >= 64 && c.ctx_max <= 32768 &&
+                 c.prefill_block >= 1 && c.prefill_block <= 32 && c.k_draft >= 0 && c.k_draft <= 3 && c.attn_chunks >= 1 &&
+                 c.attn_chunks <= 16,
+             "g4_engine_create: unsupported configuration");
+  RCK(g4_device_init());
+  g4_engine* e = new g4_engine();
+  e->cfg = c;
+  ModelDims& d = e->d;
+  d.H = c.hidden; d.NL = c.n_layers; d.I = c.mlp; d.V = c.vocab; d.DCENT = c.vocab / d.DPER;
+  d.DTOP = std::min(32, d.DCENT);
+  auto fail = [&](int rc) { g4_engine_destroy(e); return rc; };
+  if (cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking) != cudaSuccess) return fail(set_error(G4_ERR_CUDA, "stream"));
+  const int H = d.H, QD = d.NQ * d.HD, I = d.I;
+  uint8_t* tmp = nullptr;
+  const size_t tmp_bytes = (size_t)std::max({(size_t)(QD + 2 * d.HD) * H / 2, (size_t)2 * I * H / 2, (size_t)I * H / 2,
+                                              (size_t)QD * H / 2, (size_t)d.DCENT * H / 2, (size_t)H * 2 * H / 2});
+  if (ealloc_t(e, &tmp, tmp_bytes)) return fail(G4_ERR_CUDA);
+  e->L.resize(d.NL);
+  for (int l = 0; l < d.NL; ++l) {
+    TLayer& t = e->L[l];
+    t.global = d.global_layer(l);
+    int rc = gen_lin(e, t.qkv, {{layer_id(l, T_Q), QD}, {layer_id(l, T_K), d.HD}, {layer_id(l, T_V), d.HD}}, H, tmp);
+    if (!rc) rc = gen_lin(e, t.o, {{layer_id(l, T_O), H}}, QD, tmp);
+    if (!rc) rc = gen_lin(e, t.gu, {{layer_id(l, T_GATE), I}, {layer_id(l, T_UP), I}}, H, tmp);
+    if (!rc) rc = gen_lin(e, t.down, {{layer_id(l, T_DOWN), H}}, I, tmp);
+    if (!rc) rc = gen_norm(e, &t.in_ln, layer_id(l, T_IN_LN), H, 1.f);
+    if (!rc) rc = gen_norm(e, &t.post_attn, layer_id(l, T_POST_ATTN), H, 1.f);
+    if (!rc) rc = gen_norm(e, &t.pre_ff, layer_id(l, T_PRE_FF), H, 1.f);
+    if (!rc) rc = gen_norm(e, &t.post_ff, layer_id(l, T_POST_FF), H, 1.f);
+    if (!rc) rc = gen_norm(e, &t.qn, layer_id(l, T_QN), d.HD, 0.0625f);
+    if (!rc) rc = gen_norm(e, &t.kn, layer_id(l, T_KN), d.HD, 1.f);
+    if (rc) return fail(rc);
+  }
+  if (gen_norm(e, &e->fnorm, T_FNORM, H, 1.f)) return fail(G4_ERR_CUDA);
+  // embedding / tied head, packed exact head, screen
+  const long long EV = (long long)d.V * H;
+  if (ealloc_t(e, &e->E, (size_t)EV)) return fail(G4_ERR_CUDA);
+  k_gen_embed<<<gridfor(EV), 256, 0, e->st>>>(c.seed, EV, e->E);
+  {
+    void* ws = nullptr;
+    if (ealloc(e, &ws, std::max<size_t>(2048, 8 * (size_t)d.V))) return fail(G4_ERR_CUDA);
+    int rc = g4_bf16p_codebook(e->E, EV, e->cb8, ws, std::max<size_t>(2048, 8 * (size_t)d.V), e->st);
+    long long total = 0;
+    if (!rc && ealloc_t(e, &e->hexc_ptr, (size_t)d.V + 1)) rc = G4_ERR_CUDA;
+    if (!rc) rc = g4_bf16p_count(e->E, d.V, H, e->cb8, e->hexc_ptr, ws, 8 * (size_t)d.V, &total, e->st);
+    if (!rc && ealloc_t(e, &e->hdata, (size_t)d.V * (H / 32) * 44)) rc = G4_ERR_CUDA;
+    if (!rc && ealloc_t(e, &e->hexc_col, (size_t)std::max(1LL, total))) rc = G4_ERR_CUDA;
+    if (!rc && ealloc_t(e, &e->hexc_delta, (size_t)std::max(1LL, total))) rc = G4_ERR_CUDA;
+    if (!rc) rc = g4_bf16p_pack(e->E, d.V, H, e->cb8, e->hdata, e->hexc_ptr, e->hexc_col, e->hexc_delta, e->st);
+    if (!rc && ealloc_t(e, &e->sW4, (size_t)d.V * H / 2)) rc = G4_ERR_CUDA;
+    if (!rc && ealloc_t(e, &e->sS4, (size_t)d.V * H / 32)) rc = G4_ERR_CUDA;
+    if (!rc && ealloc_t(e, &e->scoef, (size_t)d.V)) rc = G4_ERR_CUDA;
+    if (!rc) rc = g4_screen_build(e->E, d.V, H, e->sW4, e->sS4, e->scoef, e->st);
+    if (rc) return fail(rc);
+  }
+  // drafter
+  if (c.drafter) {
+    int rc = gen_lin(e, e->dpre, {{T_DPRE, H}}, 2 * H, tmp);
+    if (!rc) rc = gen_lin(e, e->dpost, {{T_DPOST, H}}, H, tmp);
+    if (!rc) rc = gen_lin(e, e->dcent, {{T_DCENT, d.DCENT}}, H, tmp);
+    if (!rc) rc = gen_norm(e, &e->dnorm, T_DNORM, H, 1.f);
+    e->DL.resize(d.DL);
+    for (int l = 0; l < d.DL && !rc; ++l) {
+      DLayerW& t = e->DL[l];
+      t.global = (l == d.DL - 1);
+      rc = gen_lin(e, t.q, {{dlayer_id(l, T_Q), QD}}, H, tmp);
+      if (!rc) rc = gen_lin(e, t.o, {{dlayer_id(l, T_O), H}}, QD, tmp);
+      if (!rc) rc = gen_lin(e, t.gu, {{dlayer_id(l, T_GATE), I}, {dlayer_id(l, T_UP), I}}, H, tmp);
+      if (!rc) rc = gen_lin(e, t.down, {{dlayer_id(l, T_DOWN), H}}, I, tmp);
+      if (!rc) rc = gen_norm(e, &t.in_ln, dlayer_id(l, T_IN_LN), H, 1.f);
+      if (!rc) rc = gen_norm(e, &t.post_attn, dlayer_id(l, T_POST_ATTN), H, 1.f);
+      if (!rc) rc = gen_norm(e, &t.pre_ff, dlayer_id(l, T_PRE_FF), H, 1.f);
+      if (!rc) rc = gen_norm(e, &t.post_ff, dlayer_id(l, T_POST_FF), H, 1.f);
+      if (!rc) rc = gen_norm(e, &t.qn, dlayer_id(l, T_QN), d.HD, 0.0625f);
+    }
+    if (rc) return fail(rc);
+  }
+  // KV cache and RoPE tables (host, double -> float, as gemma4_engine.cpp:1246-1247)
+  const size_t kvn = (size_t)d.NL * c.ctx_max * d.HD;
+  if (ealloc_t(e, &e->Kc, kvn) || ealloc_t(e, &e->Vc, kvn)) return fail(G4_ERR_CUDA);
+  cudaMemsetAsync(e->Kc, 0, kvn * 2, e->st);
+  cudaMemsetAsync(e->Vc, 0, kvn * 2, e->st);
+  {
+    const int hh = d.HD / 2;
+    std::vector<float> cs((size_t)c.ctx_max * hh), sn((size_t)c.ctx_max * hh);
+    for (int ty = 0; ty < 2; ++ty) {
+      const double theta = ty ? 1e6 : 1e4;
+      for (int p = 0; p < c.ctx_max; ++p)
+        for (int j = 0; j < hh; ++j) {
+          const double inv = 1.0 / pow(theta, (2.0 * j) / d.HD);
+          const double ang = p * inv;
+          cs[(size_t)p * hh + j] = (float)cos(ang);
+          sn[(size_t)p * hh + j] = (float)sin(ang);
+        }
+      if (ealloc_t(e, &e->rope[ty][0], cs.size()) || ealloc_t(e, &e->rope[ty][1], sn.size())) return fail(G4_ERR_CUDA);
+      if (cudaMemcpy(e->rope[ty][0], cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+          cudaMemcpy(e->rope[ty][1], sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail(set_error(G4_ERR_CUDA, "rope tables"));
+    }
+  }
+  // activations
+  const int MM = e->MMAX;
+  int rc = ealloc_t(e, &e->x, (size_t)MM * H);
+  if (!rc) rc = ealloc_t(e, &e->a, (size_t)MM * std::max(H, I));
+  if (!rc) rc = ealloc_t(e, &e->qkv, (size_t)MM * (QD + 2 * d.HD));
+  if (!rc) rc = ealloc_t(e, &e->att, (size_t)MM * QD);
+  if (!rc) rc = ealloc_t(e, &e->qs, (size_t)4 * QD);
+  if (!rc) rc = ealloc_t(e, &e->o, (size_t)MM * H);
+  if (!rc) rc = ealloc_t(e, &e->gu, (size_t)MM * 2 * I);
+  if (!rc) rc = ealloc_t(e, &e->act, (size_t)MM * I);
+  if (!rc) rc = ealloc_t(e, &e->hbuf, (size_t)MM * H);
+  if (!rc) rc = ealloc_t(e, &e->mlp_in, (size_t)MM * H);
+  const size_t kmax = (size_t)std::max({2 * H, I, QD});  // widest linear input
+  if (!rc) rc = ealloc_t(e, &e->xq, (size_t)MM * kmax);
+  if (!rc) rc = ealloc_t(e, &e->xsx, (size_t)MM * kmax / 32);
+  if (!rc) rc = ealloc_t(e, &e->xsum, (size_t)MM * kmax / 32);
+  if (!rc) rc = ealloc_t(e, &e->toks, (size_t)MM);
+  if (!rc) rc = ealloc_t(e, &e->G, (size_t)MM);
+  e->attn_ws_bytes = g4_attn_splitkv_ws_bytes(4, d.NQ, d.HD, 0, c.ctx_max - 1, c.attn_chunks);
+  if (!rc) rc = ealloc(e, &e->attn_ws, e->attn_ws_bytes);
+  e->head_ws_bytes = g4_head_screen_ws_bytes(4, d.V, c.screen_lim);
+  if (!rc) rc = ealloc(e, &e->head_ws, e->head_ws_bytes);
+  if (!rc) rc = ealloc_t(e, &e->head_ns, 4);
+  if (!rc) rc = ealloc_t(e, &e->dcomb, (size_t)2 * H);
+  if (!rc) rc = ealloc_t(e, &e->dx, (size_t)H);
+  if (!rc) rc = ealloc_t(e, &e->da, (size_t)std::max({H, I, QD}));
+  if (!rc) rc = ealloc_t(e, &e->dq, (size_t)QD);
+  if (!rc) rc = ealloc_t(e, &e->dopt, (size_t)QD);
+  if (!rc) rc = ealloc_t(e, &e->dgu, (size_t)2 * I);
+  if (!rc) rc = ealloc_t(e, &e->dact, (size_t)I);
+  if (!rc) rc = ealloc_t(e, &e->dh, (size_t)H);
+  if (!rc) rc = ealloc_t(e, &e->bcur, (size_t)H);
+  if (!rc) rc = ealloc_t(e, &e->hprev, (size_t)H);
+  if (!rc) rc = ealloc_t(e, &e->hnext, (size_t)H);
+  if (!rc) rc = ealloc_t(e, &e->dscore, (size_t)d.DCENT);
+  if (!rc) rc = ealloc_t(e, &e->cscore, (size_t)d.DTOP * d.DPER);
+  if (!rc) rc = ealloc_t(e, &e->cand, (size_t)d.DTOP * d.DPER);
+  if (!rc) rc = ealloc_t(e, &e->dtok, 4);
+  if (rc) return fail(rc);
+  if (cudaStreamSynchronize(e->st) != cudaSuccess) return fail(set_error(G4_ERR_CUDA, "g4_engine_create: %s", cudaGetErrorString(cudaGetLastError())));
+  *out = e;
+  return G4_OK;
+}
+
+extern "C" void g4_engine_destroy(g4_engine* e) {
+  if (!e) return;
+  if (e->st) cudaStreamSynchronize(e->st);
+  for (void* p : e->allocs) cudaFree(p);
+  if (e->st) cudaStreamDestroy(e->st);
+  delete e;
+}
+
+// int4 linear: W4A8 when int8 activations are active and M >= 2 (lin_multi :311), or always for the
+// drafter (force_i8); otherwise the float W4G32 path.
+static int lin(g4_engine* e, const Lin& w, const float* X, int M, float* Y, bool force_i8 = false) {
+  if ((e->i8_active && M >= 2) || force_i8) {
+    RCK(g4_w4a8_quant(X, M, w.K, e->xq, e->xsx, e->xsum, e->st));
+    int m0 = 0;
+    while (m0 < M) {  // the GEMV serves up to 8 activation rows per launch; rows are independent
+      const int mm = std::min(8, M - m0);
+      RCK(g4_w4a8_gemm(w.w, w.s, e->xq + (size_t)m0 * w.K, e->xsx + (size_t)m0 * (w.K / 32),
+                       e->xsum + (size_t)m0 * (w.K / 32), mm, w.N, w.K, Y + (size_t)m0 * w.N, w.N, e->st));
+      m0 += mm;
+    }
+    return G4_OK;
+  }
+  int m0 = 0;
+  while (m0 < M) {
+    const int mm = std::min(8, M - m0);
+    RCK(g4_w4g32_gemm(w.w, w.s, X + (size_t)m0 * w.K, nullptr, mm, w.N, w.K, Y + (size_t)m0 * w.N, w.N, e->st));
+    m0 += mm;
+  }
+  return G4_OK;
+}
+
+// One target forward over M tokens at positions pos0.. (fwd, :1256-1502).  toks are device ints;
+// when want, rows hf.. get the final-normed hidden in hbuf and the greedy next token in G.
+static int forward(g4_engine* e, int M, int pos0, bool want, int hf) {
+  const ModelDims& d = e->d;
+  const int H = d.H, QD = d.NQ * d.HD, ld = QD + 2 * d.HD;
+  const float sqrtH = sqrtf((float)H);
+  k_embed<<<M, 256, 0, e->st>>>(e->E, e->toks, H, sqrtH, e->x);
+  for (int l = 0; l < d.NL; ++l) {
+    const TLayer& t = e->L[l];
+    const int ty = t.global ? 1 : 0;
+    k_rmsnorm<<<M, 256, 0, e->st>>>(e->x, t.in_ln, H, e->a, 0);
+    RCK(lin(e, t.qkv, e->a, M, e->qkv));
+    uint16_t* Kc = e->Kc + (size_t)l * e->cfg.ctx_max * d.HD;
+    uint16_t* Vc = e->Vc + (size_t)l * e->cfg.ctx_max * d.HD;
+    k_qkv_post<<<dim3(M, d.NQ + 2), 256, 0, e->st>>>(e->qkv, ld, d.NQ, d.HD, pos0, t.qn, t.kn, e->rope[ty][0],
+                                                     e->rope[ty][1], Kc, Vc);
+    RCK(check_launch("k_qkv_post"));
+    if (M <= 4 && pos0 + M > e->cfg.att_par) {
+      // split-KV (:1305-1327): rows' q are rows of the qkv buffer (stride ld); gather into att first
+      int pos[4], lo[4], kmin = 1 << 30;
+      for (int m = 0; m < M; ++m) {
+        pos[m] = pos0 + m;
+        lo[m] = t.global ? 0 : std::max(0, pos[m] - (d.WINDOW - 1));
+        kmin = std::min(kmin, lo[m]);
+      }
+      ECK(cudaMemcpy2DAsync(e->qs, sizeof(float) * QD, e->qkv, sizeof(float) * ld, sizeof(float) * QD, M,
+                            cudaMemcpyDeviceToDevice, e->st));
+      RCK(g4_attn_splitkv(Kc, Vc, e->qs, pos, lo, M, d.NQ, d.HD, kmin, pos0 + M - 1, e->cfg.attn_chunks, e->att, e->attn_ws,
+                          e->attn_ws_bytes, e->st));
+    } else {
+      const int variant = (M >= 4 && pos0 + M > 64) ? 0 : 1;  // attn_tile, else per-(row, head) (:1328-1355)
+      const int len_max = (t.global ? pos0 + M : std::min(pos0 + M, d.WINDOW));
+      k_attn_rows<<<dim3(M, d.NQ), 256, sizeof(float) * len_max, e->st>>>(Kc, Vc, e->qkv, ld, d.NQ, d.HD, pos0,
+                                                                           t.global ? 0 : d.WINDOW, variant, e->att, QD);
+      RCK(check_launch("k_attn_rows"));
+    }
+    RCK(lin(e, t.o, e->att, M, e->o));
+    k_post_attn<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_attn, t.pre_ff, e->mlp_in, H);
+    RCK(lin(e, t.gu, e->mlp_in, M, e->gu));
+    k_act<<<gridfor((long long)M * d.I), 256, 0, e->st>>>(e->gu, d.I, M, e->act);
+    RCK(lin(e, t.down, e->act, M, e->o));
+    k_post_ff<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_ff, 1.0f, H);
+    RCK(check_launch("layer"));
+  }
+  if (!want) return G4_OK;
+  const int Mh = M - hf;
+  k_rmsnorm<<<Mh, 256, 0, e->st>>>(e->x + (size_t)hf * H, e->fnorm, H, e->hbuf + (size_t)hf * H, 1);
+  RCK(check_launch("final norm"));
+  // head in groups of 4 rows (:1500)
+  for (int r0 = hf; r0 < M; r0 += 4) {
+    const int mh = std::min(4, M - r0);
+    if (e->cfg.head_screen) {
+      RCK(g4_head_screen(e->sW4, e->sS4, e->scoef, e->hdata, e->cb8, e->hexc_ptr, e->hexc_col, e->hexc_delta, d.V, H,
+                         e->hbuf + (size_t)r0 * H, mh, e->cfg.screen_lim, e->G + r0, e->head_ns, e->head_ws,
+                         e->head_ws_bytes, e->st));
+    } else {
+      float* logits = static_cast<float*>(e->head_ws);
+      RCK(g4_bf16p_gemm(e->hdata, e->cb8, e->hexc_ptr, e->hexc_col, e->hexc_delta, d.V, H, e->hbuf + (size_t)r0 * H, mh,
+                        logits, d.V, e->st));
+      RCK(g4_head_argmax(logits, mh, d.V, d.V, e->G + r0, static_cast<char*>(e->head_ws) + sizeof(float) * (size_t)4 * d.V,
+                         64, e->st));
+    }
+  }
+  return G4_OK;
+}
+
+// One draft step (draft_step, :1534-1563): token *dtok_in, hidden h (device), query position pos,
+// last valid target position P; writes the drafted token to *dtok_out and the next hidden to bcur.
+static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos, int P, int* dtok_out) {
+  const ModelDims& d = e->d;
+  const int H = d.H, QD = d.NQ * d.HD;
+  k_draft_in<<<8, 256, 0, e->st>>>(e->E, dtok_in, h, H, sqrtf((float)H), e->dcomb);
+  RCK(lin(e, e->dpre, e->dcomb, 1, e->dx, true));
+  k_round<<<gridfor(H), 256, 0, e->st>>>(e->dx, H);
+  for (int l = 0; l < d.DL; ++l) {
+    const DLayerW& t = e->DL[l];
+    const int ty = t.global ? 1 : 0;
+    // target layer whose KV the drafter reads: the last global layer, or the last sliding layer
+    int tl = -1;
+    for (int l2 = d.NL - 1; l2 >= 0; --l2)
+      if (d.global_layer(l2) == t.global) { tl = l2; break; }
+    if (tl < 0) return set_error(G4_ERR_UNSUPPORTED, "draft_step: the target has no %s layer", t.global ? "global" : "sliding");
+    k_rmsnorm<<<1, 256, 0, e->st>>>(e->dx, t.in_ln, H, e->da, 0);
+    RCK(lin(e, t.q, e->da, 1, e->dq, true));
+    k_q_post<<<d.NQ, 256, 0, e->st>>>(e->dq, d.HD, pos, t.qn, e->rope[ty][0], e->rope[ty][1]);
+    const int lo = t.global ? 0 : std::max(0, pos - (d.WINDOW - 1));
+    const int pp = P;
+    RCK(g4_attn_splitkv(e->Kc + (size_t)tl * e->cfg.ctx_max * d.HD, e->Vc + (size_t)tl * e->cfg.ctx_max * d.HD, e->dq,
+                        &pp, &lo, 1, d.NQ, d.HD, lo, P, e->cfg.attn_chunks, e->dopt, e->attn_ws, e->attn_ws_bytes, e->st));
+    RCK(lin(e, t.o, e->dopt, 1, e->da, true));
+    k_resid_norm<<<1, 256, 0, e->st>>>(e->da, e->dx, t.post_attn, H);
+    k_rmsnorm<<<1, 256, 0, e->st>>>(e->dx, t.pre_ff, H, e->da, 1);
+    RCK(lin(e, t.gu, e->da, 1, e->dgu, true));
+    k_act<<<gridfor(d.I), 256, 0, e->st>>>(e->dgu, d.I, 1, e->dact);
+    RCK(lin(e, t.down, e->dact, 1, e->da, true));
+    k_resid_norm<<<1, 256, 0, e->st>>>(e->da, e->dx, t.post_ff, H);
+    k_scale_round<<<gridfor(H), 256, 0, e->st>>>(e->dx, H, 1.0f);
+    RCK(check_launch("draft layer"));
+  }
+  k_rmsnorm<<<1, 256, 0, e->st>>>(e->dx, e->dnorm, H, e->dh, 1);
+  RCK(lin(e, e->dpost, e->dh, 1, e->bcur, true));
+  RCK(lin(e, e->dcent, e->dh, 1, e->dscore, true));
+  k_round<<<gridfor(H), 256, 0, e->st>>>(e->bcur, H);
+  const int nc = d.DTOP * d.DPER;
+  k_topk_cand<<<1, 1024, sizeof(float) * d.DCENT, e->st>>>(e->dscore, d.DCENT, d.DTOP, d.DPER, d.V, e->cand);
+  k_cand_scores<<<(nc * 16 + 255) / 256, 256, 0, e->st>>>(e->E, e->cand, nc, e->dh, H, e->cscore);
+  k_cand_best<<<1, 1024, 0, e->st>>>(e->cscore, e->cand, nc, dtok_out);
+  return check_launch("draft_step");
+}
+
+extern "C" int g4_engine_forward(g4_engine* e, const int32_t* toks, int M, int pos0, int want, int hf, int int8,
+                                 int32_t* G, float* hbuf) {
+  G4_REQUIRE(e && toks && M >= 1 && M <= e->MMAX && pos0 >= 0 && pos0 + M <= e->cfg.ctx_max && hf >= 0 && hf < M,
+             "g4_engine_forward: bad arguments");
+  e->i8_active = int8 != 0;
+  ECK(cudaMemcpyAsync(e->toks, toks, sizeof(int) * M, cudaMemcpyHostToDevice, e->st));
+  RCK(forward(e, M, pos0, want != 0, hf));
+  if (want && G) ECK(cudaMemcpyAsync(G + hf, e->G + hf, sizeof(int) * (M - hf), cudaMemcpyDeviceToHost, e->st));
+  if (want && hbuf)
+    ECK(cudaMemcpyAsync(hbuf + (size_t)hf * e->d.H, e->hbuf + (size_t)hf * e->d.H, sizeof(float) * (M - hf) * e->d.H,
+                        cudaMemcpyDeviceToHost, e->st));
+  ECK(cudaStreamSynchronize(e->st));
+  return G4_OK;
+}
+
+extern "C" int g4_engine_draft(g4_engine* e, int32_t tok, const float* h, int pos, int P, int32_t* out_tok, float* h_next) {
+  G4_REQUIRE(e && h && out_tok && e->cfg.drafter && pos < e->cfg.ctx_max && P >= 0, "g4_engine_draft: bad arguments");
+  ECK(cudaMemcpyAsync(e->dtok, &tok, sizeof(int), cudaMemcpyHostToDevice, e->st));
+  ECK(cudaMemcpyAsync(e->hbuf, h, sizeof(float) * e->d.H, cudaMemcpyHostToDevice, e->st));
+  RCK(draft_step(e, e->dtok, e->hbuf, pos, P, e->dtok + 1));
+  ECK(cudaMemcpyAsync(out_tok, e->dtok + 1, sizeof(int), cudaMemcpyDeviceToHost, e->st));
+  if (h_next) ECK(cudaMemcpyAsync(h_next, e->bcur, sizeof(float) * e->d.H, cudaMemcpyDeviceToHost, e->st));
+  ECK(cudaStreamSynchronize(e->st));
+  return G4_OK;
+}
+
+static bool is_stop(int t) { return t == 106 || t == 1; }
+
+// run_req (:1582-1680) in chain mode: prefill in blocks, then rounds of (prompt lookup or k MTP
+// drafts) -> one verify forward -> greedy acceptance.
+extern "C" int g4_engine_generate(g4_engine* e, const int32_t* prompt, int n, int n_new, int32_t* out, int* n_out,
+                                  g4_engine_stats* stats) {
+  G4_REQUIRE(e && prompt && out && n_out && n >= 1 && n_new >= 1 && n + n_new + 4 <= e->cfg.ctx_max,
+             "g4_engine_generate: bad arguments (n=%d n_new=%d ctx_max=%d)", n, n_new, e->cfg.ctx_max);
+  const ModelDims& d = e->d;
+  const int H = d.H;
+  g4_engine_stats s{};
+  auto t0 = std::chrono::steady_clock::now();
+  // prefill (int8 per ENGINE_PREFILL_INT8, :1595)
+  e->i8_active = e->cfg.prefill_int8 != 0;
+  int done = 0, last_M = 0;
+  while (done < n) {
+    const int M = std::min(e->cfg.prefill_block, n - done);
+    const bool last = done + M == n;
+    ECK(cudaMemcpyAsync(e->toks, prompt + done, sizeof(int) * M, cudaMemcpyHostToDevice, e->st));
+    RCK(forward(e, M, done, last, last ? M - 1 : 0));
+    done += M;
+    last_M = M;
+  }
+  int first = 0;
+  ECK(cudaMemcpyAsync(&first, e->G + (last_M - 1), sizeof(int), cudaMemcpyDeviceToHost, e->st));
+  ECK(cudaStreamSynchronize(e->st));
+  auto t1 = std::chrono::steady_clock::now();
+  s.prefill_ms = std::chrono::duration<double, std::milli>(t1 - t0).count();
+  s.prefill_tokens = n;
+  // decode (ENGINE_DECODE_INT8 on requires PREFILL_INT8, :1600)
+  e->i8_active = e->cfg.decode_int8 && e->cfg.prefill_int8;
+  std::vector<int> gen{first};
+  std::vector<int> seq(prompt, prompt + n);
+  seq.push_back(first);
+  // hprev (the final-normed hidden of the last committed row) stays on the device; hbuf is
+  // overwritten by every forward, so it is copied out
+  ECK(cudaMemcpyAsync(e->hprev, e->hbuf + (size_t)(last_M - 1) * H, sizeof(float) * H, cudaMemcpyDeviceToDevice, e->st));
+  int P = n - 1, conf = first;
+  bool stopped = is_stop(first);
+  int block[8];
+  std::vector<int> G(8);
+  while ((int)gen.size() < n_new && !stopped) {
+    block[0] = conf;
+    int nd = 0;
+    bool used_ng = false;
+    if (e->cfg.ngram > 0) {  // prompt lookup (:1624-1628)
+      const int Ls = (int)seq.size(), NG = e->cfg.ngram;
+      if (Ls > NG)
+        for (int i = Ls - NG - 1; i >= 0; --i) {
+          bool eq = true;
+          for (int t = 0; t < NG; ++t)
+            if (seq[i + t] != seq[Ls - NG + t]) { eq = false; break; }
+          if (eq) {
+            for (int j = 0; j < e->cfg.ngram_len && j < 7 && i + NG + j < Ls; ++j) block[1 + nd++] = seq[i + NG + j];
+            break;
+          }
+        }
+      if (nd > 0) { used_ng = true; s.ngram_rounds++; }
+    }
+    if (!used_ng && e->cfg.drafter && e->cfg.k_draft > 0) {
+      // MTP drafts: token conf with hidden hprev, then each draft with the drafter's next hidden
+      ECK(cudaMemcpyAsync(e->dtok, &conf, sizeof(int), cudaMemcpyHostToDevice, e->st));
+      const float* hcur = e->hprev;
+      for (int j = 0; j < e->cfg.k_draft; ++j) {
+        RCK(draft_step(e, e->dtok + (j & 1), hcur, P + 1 + j, P, e->dtok + ((j + 1) & 1)));
+        ECK(cudaMemcpyAsync(e->toks + 1 + j, e->dtok + ((j + 1) & 1), sizeof(int), cudaMemcpyDeviceToDevice, e->st));
+        ECK(cudaMemcpyAsync(e->hnext, e->bcur, sizeof(float) * H, cudaMemcpyDeviceToDevice, e->st));
+        hcur = e->hnext;
+      }
+      int dr[3];
+      ECK(cudaMemcpyAsync(dr, e->toks + 1, sizeof(int) * e->cfg.k_draft, cudaMemcpyDeviceToHost, e->st));
+      ECK(cudaStreamSynchronize(e->st));
+      for (int j = 0; j < e->cfg.k_draft; ++j) block[1 + nd++] = dr[j];
+      s.drafted += nd;
+    }
+    const int M = nd + 1;
+    ECK(cudaMemcpyAsync(e->toks, block, sizeof(int) * M, cudaMemcpyHostToDevice, e->st));
+    RCK(forward(e, M, P + 1, true, 0));
+    ECK(cudaMemcpyAsync(G.data(), e->G, sizeof(int) * M, cudaMemcpyDeviceToHost, e->st));
+    ECK(cudaStreamSynchronize(e->st));
+    s.rounds++;
+    int nacc = 0;
+    while (nacc < nd && block[nacc + 1] == G[nacc]) ++nacc;
+    s.accepted += nacc;
+    for (int i = 0; i <= nacc; ++i) {
+      gen.push_back(G[i]);
+      seq.push_back(G[i]);
+      if (is_stop(G[i])) { stopped = true; break; }
+    }
+    conf = G[nacc];
+    ECK(cudaMemcpyAsync(e->hprev, e->hbuf + (size_t)nacc * H, sizeof(float) * H, cudaMemcpyDeviceToDevice, e->st));
+    P += nacc + 1;
+  }
+  auto t2 = std::chrono::steady_clock::now();
+  s.decode_ms = std::chrono::duration<double, std::milli>(t2 - t1).count();
+  if ((int)gen.size() > n_new) gen.resize(n_new);
+  for (size_t i = 0; i < gen.size(); ++i)
+    if (is_stop(gen[i])) { gen.resize(i + 1); break; }
+  for (size_t i = 0; i < gen.size(); ++i) out[i] = gen[i];
+  *n_out = (int)gen.size();
+  s.decode_tokens = (int)gen.size() - 1;
+  if (stats) *stats = s;
+  return G4_OK;
+}

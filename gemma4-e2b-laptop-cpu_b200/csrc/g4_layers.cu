@@ -1,0 +1,326 @@
+// Row-wise kernels of the decoder layer (norms, RoPE, KV write, residual adds, GeGLU), the
+// embedding, the non-split attention paths used for prefill and short contexts, the drafter's
+// candidate scoring, and the seeded weight generator.  Each follows the rounding points of the
+// reference's fwd (gemma4_engine.cpp:1262-1404) operation for operation.
+#include "g4_layers.cuh"
+
+namespace g4 {
+
+// ---- RMS scale in the reference's order: sum of squares in double over 16 partial sums
+// (element i + 4a + b goes to partial (a, b), i in steps of 16), combined as ss_avx2 does
+// (gemma4_engine.cpp:326-343); r = 1 / sqrtf((float)(ss / n) + eps).  Block-wide, >= 16 threads;
+// every thread gets r.
+__device__ float block_rms_scale(const float* __restrict__ x, int n, double* red) {
+  if (threadIdx.x < 16) {
+    double s = 0;
+    for (int i = 0; i < n; i += 16) { const double d = x[i + threadIdx.x]; s = fma(d, d, s); }
+    red[threadIdx.x] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t[4];
+    for (int b = 0; b < 4; ++b) t[b] = (red[b] + red[4 + b]) + (red[8 + b] + red[12 + b]);
+    const double ss = (t[0] + t[2]) + (t[1] + t[3]);
+    red[16] = (double)__fdiv_rn(1.0f, sqrtf(__fadd_rn((float)(ss / (double)n), 1e-6f)));
+  }
+  __syncthreads();
+  const float r = (float)red[16];
+  __syncthreads();
+  return r;
+}
+
+// y[m] = (x[m]*r)*w, optionally rounded to bf16 (rms / rms_prep_x, :344-352, :365-381).
+__global__ void k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w, int n, float* __restrict__ y, int round) {
+  __shared__ double red[17];
+  const float* xm = x + (size_t)blockIdx.x * n;
+  float* ym = y + (size_t)blockIdx.x * n;
+  const float r = block_rms_scale(xm, n, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = __fmul_rn(__fmul_rn(xm[i], r), w[i]);
+    ym[i] = round ? r16(v) : v;
+  }
+}
+
+// x[m] = r16(E[tok[m]] * sqrt(H))   (embed, :1264)
+__global__ void k_embed(const uint16_t* __restrict__ E, const int* __restrict__ toks, int H, float sqrtH, float* __restrict__ x) {
+  const int m = blockIdx.x;
+  const uint16_t* er = E + (size_t)toks[m] * H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) x[(size_t)m * H + i] = r16(__fmul_rn(bf2f(er[i]), sqrtH));
+}
+
+// q/k/v after the qkv projection (:1290-1303, :1314-1323).  Block (m, part): part < nq is query
+// head `part`: rms_r16 with q_norm, then RoPE (fp32, not rounded); part == nq is k: rms_r16 with
+// k_norm, RoPE, bf16 store at cache position pos0+m; part == nq+1 is v: rms_r16 without weight,
+// bf16 store.  RoPE (rope_avx2 :394-402): h[j] = fma(u, c, -(w*s)), h[j+hd/2] = fma(w, c, u*s).
+__global__ void k_qkv_post(float* __restrict__ qkv, int ldqkv, int nq, int hd, int pos0, const float* __restrict__ qn,
+                           const float* __restrict__ kn, const float* __restrict__ cosT, const float* __restrict__ sinT,
+                           uint16_t* __restrict__ Kc, uint16_t* __restrict__ Vc) {
+  __shared__ double red[17];
+  __shared__ float hbuf[512];
+  const int m = blockIdx.x, part = blockIdx.y, pos = pos0 + m, hh = hd >> 1;
+  float* src = qkv + (size_t)m * ldqkv + (size_t)part * hd;  // q heads, then k, then v
+  const float* w = part < nq ? qn : (part == nq ? kn : nullptr);
+  const float r = block_rms_scale(src, hd, red);
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+    const float v = w ? __fmul_rn(__fmul_rn(src[i], r), w[i]) : __fmul_rn(src[i], r);
+    hbuf[i] = r16(v);
+  }
+  __syncthreads();
+  if (part == nq + 1) {
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) Vc[(size_t)pos * hd + i] = (uint16_t)f2bf(hbuf[i]);
+    return;
+  }
+  const float* cs = cosT + (size_t)pos * hh;
+  const float* sn = sinT + (size_t)pos * hh;
+  for (int j = threadIdx.x; j < hh; j += blockDim.x) {
+    const float u = hbuf[j], ww = hbuf[j + hh], c = cs[j], s = sn[j];
+    const float a = fmaf(u, c, -__fmul_rn(ww, s));
+    const float b = fmaf(ww, c, __fmul_rn(u, s));
+    if (part == nq) {
+      Kc[(size_t)pos * hd + j] = (uint16_t)f2bf(a);
+      Kc[(size_t)pos * hd + j + hh] = (uint16_t)f2bf(b);
+    } else {
+      src[j] = a;
+      src[j + hh] = b;
+    }
+  }
+}
+
+// Query-only variant for the drafter (and any caller whose k/v are not written): heads of q in
+// place, rms_r16 with q_norm then RoPE at position pos.
+__global__ void k_q_post(float* __restrict__ q, int hd, int pos, const float* __restrict__ qn, const float* __restrict__ cosT,
+                         const float* __restrict__ sinT) {
+  __shared__ double red[17];
+  __shared__ float hbuf[512];
+  const int h = blockIdx.x, hh = hd >> 1;
+  float* src = q + (size_t)h * hd;
+  const float r = block_rms_scale(src, hd, red);
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) hbuf[i] = r16(__fmul_rn(__fmul_rn(src[i], r), qn[i]));
+  __syncthreads();
+  const float* cs = cosT + (size_t)pos * hh;
+  const float* sn = sinT + (size_t)pos * hh;
+  for (int j = threadIdx.x; j < hh; j += blockDim.x) {
+    const float u = hbuf[j], ww = hbuf[j + hh], c = cs[j], s = sn[j];
+    src[j] = fmaf(u, c, -__fmul_rn(ww, s));
+    src[j + hh] = fmaf(ww, c, __fmul_rn(u, s));
+  }
+}
+
+// After o_proj (:1358-1361): o = r16(o); x = r16(x + r16((o*r)*w_post_attn)); then the pre-MLP
+// input mlp_in = r16((x*r')*w_pre_ff) (rms_prep_x with rounding, :1360).
+__global__ void k_post_attn(float* __restrict__ o, float* __restrict__ x, const float* __restrict__ w_post,
+                            const float* __restrict__ w_pre, float* __restrict__ mlp_in, int n) {
+  __shared__ double red[17];
+  float* om = o + (size_t)blockIdx.x * n;
+  float* xm = x + (size_t)blockIdx.x * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) om[i] = r16(om[i]);
+  __syncthreads();
+  const float r = block_rms_scale(om, n, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    xm[i] = r16(__fadd_rn(xm[i], r16(__fmul_rn(__fmul_rn(om[i], r), w_post[i]))));
+  __syncthreads();
+  const float r2 = block_rms_scale(xm, n, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) mlp_in[(size_t)blockIdx.x * n + i] = r16(__fmul_rn(__fmul_rn(xm[i], r2), w_pre[i]));
+}
+
+// After down_proj (:1375-1378) and the layer scalar (:1395): o = r16(o);
+// x = r16(x + r16((o*r)*w_post_ff)); x = r16(x * scalar).
+__global__ void k_post_ff(float* __restrict__ o, float* __restrict__ x, const float* __restrict__ w_post, float scalar, int n) {
+  __shared__ double red[17];
+  float* om = o + (size_t)blockIdx.x * n;
+  float* xm = x + (size_t)blockIdx.x * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) om[i] = r16(om[i]);
+  __syncthreads();
+  const float r = block_rms_scale(om, n, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = r16(__fadd_rn(xm[i], r16(__fmul_rn(__fmul_rn(om[i], r), w_post[i]))));
+    xm[i] = r16(__fmul_rn(v, scalar));
+  }
+}
+
+// GeGLU: act = r16(r16(gelu(r16 g)) * r16 u), gate in columns [0, I), up in [I, 2I) (:1370).
+__global__ void k_act(const float* __restrict__ gu, int I, int M, float* __restrict__ act) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)M * I) return;
+  const int m = (int)(idx / I), i = (int)(idx % I);
+  const float g = r16(gu[(size_t)m * 2 * I + i]), u = r16(gu[(size_t)m * 2 * I + I + i]);
+  act[idx] = r16(__fmul_rn(r16(gelu(g)), u));
+}
+
+// o_drafter residual (:1548): x = r16(x + r16((o*r)*w)) after o = r16(o); no second norm.
+__global__ void k_resid_norm(float* __restrict__ o, float* __restrict__ x, const float* __restrict__ w, int n) {
+  __shared__ double red[17];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = r16(o[i]);
+  __syncthreads();
+  const float r = block_rms_scale(o, n, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = r16(__fadd_rn(x[i], r16(__fmul_rn(__fmul_rn(o[i], r), w[i]))));
+}
+
+// elementwise helpers
+__global__ void k_round(float* __restrict__ p, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = r16(p[i]);
+}
+__global__ void k_scale_round(float* __restrict__ p, long long n, float s) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = r16(__fmul_rn(p[i], s));
+}
+// drafter input [r16(E[tok]*sqrt(H)) | h]
+__global__ void k_draft_in(const uint16_t* __restrict__ E, const int* __restrict__ tok, const float* __restrict__ h, int H,
+                           float sqrtH, float* __restrict__ out) {
+  const uint16_t* er = E + (size_t)(*tok) * H;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) {
+    out[i] = r16(__fmul_rn(bf2f(er[i]), sqrtH));
+    out[H + i] = h[i];
+  }
+}
+
+// ---- non-split attention (prefill blocks and short contexts), one block per (row m, head h).
+// Keys lo..pos in order, pos = pos0+m, lo = pos-511 clamped for sliding layers.
+//   variant 0 (attn_tile, :1061-1083): scores by the 16-partial dot (s0/s1 of stride 16 and hsum),
+//     weights exp8(s - max), den in key order, O = fma(w, v, O), out = r16(O * (1/den)).
+//   variant 1 (per-(m,h) path, :1337-1355): scores by the 8-partial dot (stride 8, hsum),
+//     weights expf(s - max) (correctly rounded here), den in key order, O = fma(w/den, v, O),
+//     out = r16(O).
+__global__ void __launch_bounds__(256) k_attn_rows(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
+                                                   const float* __restrict__ q, int ldq, int nh, int hd, int pos0,
+                                                   int window, int variant, float* __restrict__ out, int ldo) {
+  extern __shared__ float sc[];
+  __shared__ float s_red[32];
+  const int m = blockIdx.x, h = blockIdx.y;
+  const int pos = pos0 + m, lo = window > 0 ? max(0, pos - (window - 1)) : 0, len = pos - lo + 1;
+  const float* qh = q + (size_t)m * ldq + (size_t)h * hd;
+  const int hw = threadIdx.x >> 4, c = threadIdx.x & 15;
+  // scores: one half-warp per key; the two half-warps of a warp take keys pb and pb+1
+  float qr[32];
+  if (variant == 0) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) qr[i] = (i < (hd >> 4)) ? qh[c + 16 * i] : 0.f;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) qr[i] = (c < 8 && i < (hd >> 3)) ? qh[c + 8 * i] : 0.f;
+  }
+  for (int pb = lo + (hw & ~1); pb <= pos; pb += 16) {
+    const int p = min(pb + (hw & 1), pos);
+    const uint16_t* kr = Kc + (size_t)p * hd;
+    float acc = 0.f, s;
+    if (variant == 0) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < (hd >> 4)) acc = fmaf(qr[i], bf2f(kr[c + 16 * i]), acc);
+      s = hsum8_octet(__fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8)));
+    } else {
+      if (c < 8) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < (hd >> 3)) acc = fmaf(qr[i], bf2f(kr[c + 8 * i]), acc);
+      }
+      s = hsum8_octet(acc);
+    }
+    if (c == 0 && pb + (hw & 1) <= pos) sc[p - lo] = s;
+  }
+  __syncthreads();
+  float mx = -1e30f;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) mx = fmaxf(mx, sc[i]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = -1e30f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, s_red[i]);
+  __syncthreads();
+  for (int i = threadIdx.x; i < len; i += blockDim.x) {
+    const float d = __fsub_rn(sc[i], mx);
+    sc[i] = variant == 0 ? exp8(d) : exp_cr(d);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float den = 0.f;
+    for (int i = 0; i < len; ++i) den = __fadd_rn(den, sc[i]);
+    s_red[0] = den;
+  }
+  __syncthreads();
+  const float den = s_red[0];
+  if (variant == 1) {
+    for (int i = threadIdx.x; i < len; i += blockDim.x) sc[i] = __fdiv_rn(sc[i], den);
+    __syncthreads();
+  }
+  const float inv = __fdiv_rn(1.0f, den);
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+    float o = 0.f;
+    for (int p = 0; p < len; ++p) o = fmaf(sc[p], bf2f(Vc[(size_t)(lo + p) * hd + i]), o);
+    out[(size_t)m * ldo + (size_t)h * hd + i] = variant == 0 ? r16(__fmul_rn(o, inv)) : r16(o);
+  }
+}
+
+// ---- drafter candidates (dcand_task :675-722): score c = hsum(a + b) of the two 8-lane chains
+// of stride 16 (the same shape as the attention score), against the tied embedding; then the
+// first maximum in candidate order (:1557-1558).  One half-warp per candidate.
+__global__ void k_cand_scores(const uint16_t* __restrict__ E, const int* __restrict__ cand, int nc, const float* __restrict__ dh,
+                              int H, float* __restrict__ score) {
+  const int hw = (blockIdx.x * blockDim.x + threadIdx.x) >> 4, c = threadIdx.x & 15;
+  const int base = hw & ~1;  // warp-uniform
+  if (base >= nc) return;
+  const int k = min(hw, nc - 1);
+  const uint16_t* er = E + (size_t)cand[k] * H;
+  float acc = 0.f;
+  for (int i = c; i < H; i += 16) acc = fmaf(dh[i], bf2f(er[i]), acc);
+  const float s = hsum8_octet(__fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8)));
+  if (c == 0 && hw < nc) score[hw] = s;
+}
+// Top-T centroids by score (stable: ties keep the lower centroid first, as the insertion sort of
+// :1554-1555 does) and the candidate list cand[t*per + j] = perm((top t)*per + j).
+__global__ void k_topk_cand(const float* __restrict__ score, int n, int T, int per, int vocab, int* __restrict__ cand) {
+  extern __shared__ float s[];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = score[i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = s[i];
+    int rank = 0;
+    for (int j = 0; j < n; ++j) rank += (s[j] > v) || (s[j] == v && j < i);
+    if (rank < T)
+      for (int k = 0; k < per; ++k) cand[rank * per + k] = (int)perm_token((uint32_t)(i * per + k), (uint32_t)vocab);
+  }
+}
+// first argmax in candidate order -> *best (one block)
+__global__ void k_cand_best(const float* __restrict__ score, const int* __restrict__ cand, int nc, int* __restrict__ best) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  float bv = -1e30f;
+  int bi = 0x7FFFFFFF;
+  for (int i = threadIdx.x; i < nc; i += blockDim.x)
+    if (score[i] > bv) { bv = score[i]; bi = i; }  // per thread: increasing i, strict > keeps the first
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(FULL, bv, o);
+    const int oi = __shfl_xor_sync(FULL, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+    *best = bi < nc ? cand[bi] : -1;
+  }
+}
+
+// ---- seeded weights ("g4-e2b-synth v1", g4_model.cuh)
+__global__ void k_gen_w4(uint64_t seed, uint64_t id, long long nbytes, uint8_t* __restrict__ out) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nbytes; i += (long long)gridDim.x * blockDim.x)
+    out[i] = (uint8_t)(wh(seed, id, (uint64_t)i) & 0xFF);
+}
+__global__ void k_gen_scales(uint64_t seed, uint64_t id, long long n, uint16_t* __restrict__ out) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    out[i] = (uint16_t)f2bf(__fmul_rn(fabsf(wnorm(wh(seed, id, (uint64_t)i))), 0.01f));
+}
+__global__ void k_gen_norm(uint64_t seed, uint64_t id, int n, float mul, float* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = bf2f(f2bf(__fmul_rn(__fadd_rn(1.0f, __fmul_rn(0.1f, wnorm(wh(seed, id, (uint64_t)i)))), mul)));
+}
+__global__ void k_gen_embed(uint64_t seed, long long n, uint16_t* __restrict__ out) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    out[i] = (uint16_t)f2bf(__fmul_rn(0.02f, wnorm(wh(seed, T_EMBED, (uint64_t)i))));
+}
+
+}  // namespace g4

@@ -1,0 +1,28 @@
+// Declarations of the decoder-layer kernels (g4_layers.cu) used by the engine (g4_engine.cu).
+#pragma once
+#include "g4_common.cuh"
+#include "g4_model.cuh"
+
+namespace g4 {
+__global__ void k_rmsnorm(const float* x, const float* w, int n, float* y, int round);
+__global__ void k_embed(const uint16_t* E, const int* toks, int H, float sqrtH, float* x);
+__global__ void k_qkv_post(float* qkv, int ldqkv, int nq, int hd, int pos0, const float* qn, const float* kn,
+                           const float* cosT, const float* sinT, uint16_t* Kc, uint16_t* Vc);
+__global__ void k_q_post(float* q, int hd, int pos, const float* qn, const float* cosT, const float* sinT);
+__global__ void k_post_attn(float* o, float* x, const float* w_post, const float* w_pre, float* mlp_in, int n);
+__global__ void k_post_ff(float* o, float* x, const float* w_post, float scalar, int n);
+__global__ void k_act(const float* gu, int I, int M, float* act);
+__global__ void k_resid_norm(float* o, float* x, const float* w, int n);
+__global__ void k_round(float* p, long long n);
+__global__ void k_scale_round(float* p, long long n, float s);
+__global__ void k_draft_in(const uint16_t* E, const int* tok, const float* h, int H, float sqrtH, float* out);
+__global__ void k_attn_rows(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0,
+                            int window, int variant, float* out, int ldo);
+__global__ void k_cand_scores(const uint16_t* E, const int* cand, int nc, const float* dh, int H, float* score);
+__global__ void k_topk_cand(const float* score, int n, int T, int per, int vocab, int* cand);
+__global__ void k_cand_best(const float* score, const int* cand, int nc, int* best);
+__global__ void k_gen_w4(uint64_t seed, uint64_t id, long long nbytes, uint8_t* out);
+__global__ void k_gen_scales(uint64_t seed, uint64_t id, long long n, uint16_t* out);
+__global__ void k_gen_norm(uint64_t seed, uint64_t id, int n, float mul, float* out);
+__global__ void k_gen_embed(uint64_t seed, long long n, uint16_t* out);
+}  // namespace g4

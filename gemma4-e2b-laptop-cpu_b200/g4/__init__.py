@@ -36,6 +36,12 @@ SIGNATURES = {
     "g4_screen_build": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "g4_head_screen_ws_bytes": (_SZ, [_I, _I, _I]),
     "g4_head_screen": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _SZ, _P]),
+    "g4_engine_default_config": (_I, [_P]),
+    "g4_engine_create": (_I, [_P, _P]),
+    "g4_engine_destroy": (None, [_P]),
+    "g4_engine_forward": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "g4_engine_draft": (_I, [_P, _I, _P, _I, _I, _P, _P]),
+    "g4_engine_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "g4_attn_splitkv_ws_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "g4_attn_splitkv": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
     "g4_attn_splitkv_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
@@ -240,3 +246,72 @@ def head_screen(screen, head, H, lim=30000):
     check(lib().g4_head_screen(_ptr(W4), _ptr(S4), _ptr(coef), *head.args(), head.N, K, _ptr(H), M, lim, _ptr(idx),
                                _ptr(ns), _ptr(ws), need, _stream()), "g4_head_screen")
     return idx, ns
+
+
+# ------------------------------------------------------------------ speculative decode engine
+class EngineConfig(ctypes.Structure):
+    """g4_engine_config (include/g4.h)."""
+    _fields_ = [(n, ctypes.c_int) for n in ("hidden", "n_layers", "mlp", "vocab", "ctx_max", "prefill_block", "k_draft",
+                                            "ngram", "ngram_len", "prefill_int8", "decode_int8", "head_screen",
+                                            "screen_lim", "attn_chunks", "att_par", "drafter")] + [
+        ("seed", ctypes.c_ulonglong)]
+
+
+class EngineStats(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("rounds", "ngram_rounds", "drafted", "accepted", "prefill_tokens",
+                                            "decode_tokens")] + [("prefill_ms", ctypes.c_double),
+                                                                 ("decode_ms", ctypes.c_double)]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+def engine_config(**kw):
+    c = EngineConfig()
+    check(lib().g4_engine_default_config(ctypes.byref(c)), "g4_engine_default_config")
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+class Engine:
+    """The speculative greedy-decode engine (g4_engine_* in include/g4.h)."""
+
+    def __init__(self, cfg=None, **kw):
+        self.cfg = cfg if cfg is not None else engine_config(**kw)
+        self.h = ctypes.c_void_p()
+        check(lib().g4_engine_create(ctypes.byref(self.cfg), ctypes.byref(self.h)), "g4_engine_create")
+
+    def close(self):
+        if self.h:
+            lib().g4_engine_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def forward(self, toks, pos0, want=True, hf=0, int8=True):
+        import numpy as np
+        toks = np.ascontiguousarray(toks, np.int32)
+        M = toks.size
+        G = np.full(M, -1, np.int32)
+        hb = np.zeros((M, self.cfg.hidden), np.float32)
+        check(lib().g4_engine_forward(self.h, toks.ctypes.data_as(_P), M, pos0, int(want), hf, int(int8),
+                                      G.ctypes.data_as(_P), hb.ctypes.data_as(_P)), "g4_engine_forward")
+        return G, hb
+
+    def draft(self, tok, h, pos, P):
+        import numpy as np
+        h = np.ascontiguousarray(h, np.float32)
+        out = np.zeros(1, np.int32)
+        hn = np.zeros(self.cfg.hidden, np.float32)
+        check(lib().g4_engine_draft(self.h, int(tok), h.ctypes.data_as(_P), pos, P, out.ctypes.data_as(_P),
+                                    hn.ctypes.data_as(_P)), "g4_engine_draft")
+        return int(out[0]), hn
+
+    def generate(self, prompt, n_new):
+        import numpy as np
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(n_new + 8, np.int32)
+        n_out = ctypes.c_int(0)
+        st = EngineStats()
+        check(lib().g4_engine_generate(self.h, prompt.ctypes.data_as(_P), prompt.size, n_new, out.ctypes.data_as(_P),
+                                       ctypes.byref(n_out), ctypes.byref(st)), "g4_engine_generate")
+        return out[: n_out.value].copy(), st.as_dict()

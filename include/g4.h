@@ -134,6 +134,47 @@ int g4_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, const float* q, cons
 int g4_attn_splitkv_noalloc(const uint16_t* Kc, const uint16_t* Vc, const float* q, const int* pos, const int* lo,
                             int M, int nh, int hd, int kmin, int kmax, int T, float* out, void* stream);
 
+/* ---------------------------------------------------------------- speculative decode engine */
+
+/* The synthetic Gemma-style E2B model of BASELINE.json configs[4] (dimensions and seeded weights
+ * in gemma4-e2b-laptop-cpu_b200/csrc/g4_model.cuh) with its MTP drafter, prompt lookup, batched
+ * verification and greedy acceptance: the reference's run_req / fwd / draft_step
+ * (gemma4_engine.cpp:1582-1663, 1256-1502, 1534-1563) in chain mode. */
+typedef struct g4_engine g4_engine;
+typedef struct {
+  int hidden, n_layers, mlp, vocab;  /* 2048, 30, 8192, 262144 (vocab a power of two, = 128 x centroids) */
+  int ctx_max;                       /* KV cache positions */
+  int prefill_block;                 /* ENGINE_PREFILL_BLOCK (32) */
+  int k_draft;                       /* ENGINE_K (3) */
+  int ngram, ngram_len;              /* ENGINE_NGRAM (2), ENGINE_NGLEN (3) */
+  int prefill_int8, decode_int8;     /* ENGINE_PREFILL_INT8 (1), ENGINE_DECODE_INT8 (1) */
+  int head_screen, screen_lim;       /* ENGINE_HEAD_SCREEN (1), survivor limit (30000) */
+  int attn_chunks;                   /* split-KV key chunks = the reference's pool threads (8) */
+  int att_par;                       /* ENGINE_ATT_PAR (192) */
+  int drafter;                       /* build the MTP drafter (1) */
+  unsigned long long seed;           /* weight seed */
+} g4_engine_config;
+typedef struct {
+  int rounds, ngram_rounds, drafted, accepted, prefill_tokens, decode_tokens;
+  double prefill_ms, decode_ms;
+} g4_engine_stats;
+
+int g4_engine_default_config(g4_engine_config* cfg);
+/* Allocates the weights (generated on the device from cfg->seed), KV cache and buffers. */
+int g4_engine_create(const g4_engine_config* cfg, g4_engine** out);
+void g4_engine_destroy(g4_engine* e);
+/* One target forward (fwd) over M <= 32 host tokens at positions pos0..; int8 selects the W4A8
+ * path for M >= 2.  When want, rows hf.. get the greedy next token G (host [M]) and, if hbuf is
+ * non-null, the final-normed hidden (host [M][hidden]). */
+int g4_engine_forward(g4_engine* e, const int32_t* toks, int M, int pos0, int want, int hf, int int8, int32_t* G,
+                      float* hbuf);
+/* One MTP draft step: token, hidden h (host [hidden]), query position, last target position P. */
+int g4_engine_draft(g4_engine* e, int32_t tok, const float* h, int pos, int P, int32_t* out_tok, float* h_next);
+/* run_req: prefill the prompt, then speculative greedy decode until n_new tokens (the first from
+ * the prefill) or a stop token (1 or 106).  out host [n_new]. */
+int g4_engine_generate(g4_engine* e, const int32_t* prompt, int n, int n_new, int32_t* out, int* n_out,
+                       g4_engine_stats* stats);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,530 @@
+/* CPU oracle, end to end (TEST INFRASTRUCTURE ONLY): the synthetic Gemma-style E2B model of
+ * BASELINE.json configs[4] with its MTP drafter and the chain-mode speculative loop, restated in
+ * plain C on top of the kernel restatements of g4_oracle.c.  The model and its seeded weights are
+ * defined in gemma4-e2b-laptop-cpu_b200/csrc/g4_model.cuh ("g4-e2b-synth v1"); the layer is the
+ * reference's fwd (gemma4_engine.cpp:1256-1502) without PLE, the draft step its draft_step
+ * (:1534-1563) at the target's width, the loop its run_req (:1582-1663) in chain mode.
+ *
+ * The head is evaluated over the full exact head: the certified screen provably keeps every row
+ * that can win, so the screened pick equals the full pick (tested separately).
+ */
+#include "g4_oracle.h"
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---- weight generator (g4_model.cuh) */
+static uint64_t smix(uint64_t x) {
+  uint64_t z = x + 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+static uint64_t wh(uint64_t seed, uint64_t id, uint64_t i) { return smix((seed * 0x100000001B3ull) ^ (id << 40) ^ i); }
+static float wnorm(uint64_t h) {
+  const int s = (int)(h & 0xFFFF) + (int)((h >> 16) & 0xFFFF) + (int)((h >> 32) & 0xFFFF) + (int)(h >> 48) - 131070;
+  return (float)s * 2.642868e-5f;
+}
+/* int4 byte: both nibbles uniform in [0, 15], i.e. q = t - 8 uniform in [-8, 7] */
+static uint8_t w4_byte(uint64_t h) { return (uint8_t)(h & 0xFF); }
+static uint32_t perm_token(uint32_t i, uint32_t vocab) { return (uint32_t)(((uint64_t)i * 0x9E3779B1ull + 12345ull) & (uint64_t)(vocab - 1)); }
+enum { T_Q = 0, T_K = 1, T_V = 2, T_O = 3, T_GATE = 4, T_UP = 5, T_DOWN = 6, T_IN_LN = 8, T_POST_ATTN = 9, T_PRE_FF = 10,
+       T_POST_FF = 11, T_QN = 12, T_KN = 13 };
+#define T_SCALES 0x100000ull
+#define T_EMBED 1000ull
+#define T_FNORM 1001ull
+#define T_DPRE 2000ull
+#define T_DPOST 2001ull
+#define T_DCENT 2002ull
+#define T_DNORM 2003ull
+static uint64_t layer_id(int l, uint64_t w) { return 16ull * (uint64_t)l + w; }
+static uint64_t dlayer_id(int l, uint64_t w) { return 2100ull + 16ull * (uint64_t)l + w; }
+
+typedef struct { uint8_t* w; uint16_t* s; int N, K; } Lin;
+typedef struct { Lin qkv, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff, *qn, *kn; int global; } TLayer;
+typedef struct { Lin q, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff, *qn; int global; } DLayer;
+
+typedef struct {
+  int H, NL, I, V, NQ, HD, WINDOW, DL, DCENT, DTOP, DPER;
+  int ctx_max, prefill_block, k_draft, ngram, ngram_len, prefill_int8, decode_int8, attn_chunks, att_par, drafter;
+  uint64_t seed;
+  TLayer* L;
+  DLayer* D;
+  Lin dpre, dpost, dcent;
+  float *fnorm, *dnorm;
+  uint16_t* E;
+  uint8_t cb[8];
+  uint8_t* hdata;
+  int64_t* exc_ptr;
+  uint16_t* exc_col;
+  float* exc_delta;
+  uint16_t *Kc, *Vc;
+  float *rc[2], *rs[2];
+  int i8;
+} Model;
+
+static void gen_lin(Model* m, Lin* lin, const uint64_t* ids, const int* rows, int parts, int K) {
+  int N = 0;
+  for (int p = 0; p < parts; ++p) N += rows[p];
+  lin->N = N; lin->K = K;
+  lin->w = (uint8_t*)malloc((size_t)N * K / 2);
+  lin->s = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)N * K / 32);
+  size_t ro = 0, so = 0;
+  for (int p = 0; p < parts; ++p) {
+    const long long nb = (long long)rows[p] * K / 2, ns = (long long)rows[p] * K / 32;
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < nb; ++i) lin->w[ro + i] = w4_byte(wh(m->seed, ids[p], (uint64_t)i));
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < ns; ++i)
+      lin->s[so + i] = or_f2bf(fabsf(wnorm(wh(m->seed, ids[p] | T_SCALES, (uint64_t)i))) * 0.01f);
+    ro += nb; so += ns;
+  }
+}
+static float* gen_norm(Model* m, uint64_t id, int n, float mul) {
+  float* p = (float*)malloc(sizeof(float) * n);
+  for (int i = 0; i < n; ++i) p[i] = or_bf2f(or_f2bf((1.0f + 0.1f * wnorm(wh(m->seed, id, (uint64_t)i))) * mul));
+  return p;
+}
+
+typedef struct {
+  int hidden, n_layers, mlp, vocab, ctx_max, prefill_block, k_draft, ngram, ngram_len, prefill_int8, decode_int8;
+  int head_screen, screen_lim, attn_chunks, att_par, drafter;
+  unsigned long long seed;
+} or_e2e_config;  /* field order of g4_engine_config */
+
+void* or_e2e_create(const or_e2e_config* c) {
+  Model* m = (Model*)calloc(1, sizeof(Model));
+  m->H = c->hidden; m->NL = c->n_layers; m->I = c->mlp; m->V = c->vocab; m->NQ = 8; m->HD = 256; m->WINDOW = 512;
+  m->DL = 4; m->DPER = 128; m->DCENT = c->vocab / 128; m->DTOP = m->DCENT < 32 ? m->DCENT : 32;
+  m->ctx_max = c->ctx_max; m->prefill_block = c->prefill_block; m->k_draft = c->k_draft; m->ngram = c->ngram;
+  m->ngram_len = c->ngram_len; m->prefill_int8 = c->prefill_int8; m->decode_int8 = c->decode_int8;
+  m->attn_chunks = c->attn_chunks; m->att_par = c->att_par; m->drafter = c->drafter; m->seed = c->seed;
+  const int H = m->H, QD = m->NQ * m->HD, I = m->I;
+  m->L = (TLayer*)calloc(m->NL, sizeof(TLayer));
+  for (int l = 0; l < m->NL; ++l) {
+    TLayer* t = &m->L[l];
+    t->global = (l % 5 == 4);
+    { uint64_t ids[3] = {layer_id(l, T_Q), layer_id(l, T_K), layer_id(l, T_V)}; int rows[3] = {QD, m->HD, m->HD}; gen_lin(m, &t->qkv, ids, rows, 3, H); }
+    { uint64_t ids[1] = {layer_id(l, T_O)}; int rows[1] = {H}; gen_lin(m, &t->o, ids, rows, 1, QD); }
+    { uint64_t ids[2] = {layer_id(l, T_GATE), layer_id(l, T_UP)}; int rows[2] = {I, I}; gen_lin(m, &t->gu, ids, rows, 2, H); }
+    { uint64_t ids[1] = {layer_id(l, T_DOWN)}; int rows[1] = {H}; gen_lin(m, &t->down, ids, rows, 1, I); }
+    t->in_ln = gen_norm(m, layer_id(l, T_IN_LN), H, 1.f);
+    t->post_attn = gen_norm(m, layer_id(l, T_POST_ATTN), H, 1.f);
+    t->pre_ff = gen_norm(m, layer_id(l, T_PRE_FF), H, 1.f);
+    t->post_ff = gen_norm(m, layer_id(l, T_POST_FF), H, 1.f);
+    t->qn = gen_norm(m, layer_id(l, T_QN), m->HD, 0.0625f);
+    t->kn = gen_norm(m, layer_id(l, T_KN), m->HD, 1.f);
+  }
+  m->fnorm = gen_norm(m, T_FNORM, H, 1.f);
+  const long long EV = (long long)m->V * H;
+  m->E = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)EV);
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < EV; ++i) m->E[i] = or_f2bf(0.02f * wnorm(wh(m->seed, T_EMBED, (uint64_t)i)));
+  or_bf16p_codebook(m->E, EV, m->cb);
+  m->exc_ptr = (int64_t*)malloc(sizeof(int64_t) * (m->V + 1));
+  const int64_t ne = or_bf16p_count(m->E, m->V, H, m->cb, m->exc_ptr);
+  m->hdata = (uint8_t*)malloc((size_t)m->V * (H / 32) * 44);
+  m->exc_col = (uint16_t*)malloc(sizeof(uint16_t) * (ne > 0 ? ne : 1));
+  m->exc_delta = (float*)malloc(sizeof(float) * (ne > 0 ? ne : 1));
+  or_bf16p_pack(m->E, m->V, H, m->cb, m->hdata, m->exc_ptr, m->exc_col, m->exc_delta);
+  if (m->drafter) {
+    { uint64_t ids[1] = {T_DPRE}; int rows[1] = {H}; gen_lin(m, &m->dpre, ids, rows, 1, 2 * H); }
+    { uint64_t ids[1] = {T_DPOST}; int rows[1] = {H}; gen_lin(m, &m->dpost, ids, rows, 1, H); }
+    { uint64_t ids[1] = {T_DCENT}; int rows[1] = {m->DCENT}; gen_lin(m, &m->dcent, ids, rows, 1, H); }
+    m->dnorm = gen_norm(m, T_DNORM, H, 1.f);
+    m->D = (DLayer*)calloc(m->DL, sizeof(DLayer));
+    for (int l = 0; l < m->DL; ++l) {
+      DLayer* t = &m->D[l];
+      t->global = (l == m->DL - 1);
+      { uint64_t ids[1] = {dlayer_id(l, T_Q)}; int rows[1] = {QD}; gen_lin(m, &t->q, ids, rows, 1, H); }
+      { uint64_t ids[1] = {dlayer_id(l, T_O)}; int rows[1] = {H}; gen_lin(m, &t->o, ids, rows, 1, QD); }
+      { uint64_t ids[2] = {dlayer_id(l, T_GATE), dlayer_id(l, T_UP)}; int rows[2] = {I, I}; gen_lin(m, &t->gu, ids, rows, 2, H); }
+      { uint64_t ids[1] = {dlayer_id(l, T_DOWN)}; int rows[1] = {H}; gen_lin(m, &t->down, ids, rows, 1, I); }
+      t->in_ln = gen_norm(m, dlayer_id(l, T_IN_LN), H, 1.f);
+      t->post_attn = gen_norm(m, dlayer_id(l, T_POST_ATTN), H, 1.f);
+      t->pre_ff = gen_norm(m, dlayer_id(l, T_PRE_FF), H, 1.f);
+      t->post_ff = gen_norm(m, dlayer_id(l, T_POST_FF), H, 1.f);
+      t->qn = gen_norm(m, dlayer_id(l, T_QN), m->HD, 0.0625f);
+    }
+  }
+  const size_t kvn = (size_t)m->NL * m->ctx_max * m->HD;
+  m->Kc = (uint16_t*)calloc(kvn, sizeof(uint16_t));
+  m->Vc = (uint16_t*)calloc(kvn, sizeof(uint16_t));
+  const int hh = m->HD / 2;
+  for (int ty = 0; ty < 2; ++ty) {
+    const double theta = ty ? 1e6 : 1e4;
+    m->rc[ty] = (float*)malloc(sizeof(float) * (size_t)m->ctx_max * hh);
+    m->rs[ty] = (float*)malloc(sizeof(float) * (size_t)m->ctx_max * hh);
+    for (int p = 0; p < m->ctx_max; ++p)
+      for (int j = 0; j < hh; ++j) {
+        const double inv = 1.0 / pow(theta, (2.0 * j) / m->HD);
+        const double ang = p * inv;
+        m->rc[ty][(size_t)p * hh + j] = (float)cos(ang);
+        m->rs[ty][(size_t)p * hh + j] = (float)sin(ang);
+      }
+  }
+  return m;
+}
+
+static void free_lin(Lin* l) { free(l->w); free(l->s); }
+void or_e2e_destroy(void* mp) {
+  Model* m = (Model*)mp;
+  if (!m) return;
+  for (int l = 0; l < m->NL; ++l) {
+    TLayer* t = &m->L[l];
+    free_lin(&t->qkv); free_lin(&t->o); free_lin(&t->gu); free_lin(&t->down);
+    free(t->in_ln); free(t->post_attn); free(t->pre_ff); free(t->post_ff); free(t->qn); free(t->kn);
+  }
+  free(m->L);
+  if (m->D) {
+    for (int l = 0; l < m->DL; ++l) {
+      DLayer* t = &m->D[l];
+      free_lin(&t->q); free_lin(&t->o); free_lin(&t->gu); free_lin(&t->down);
+      free(t->in_ln); free(t->post_attn); free(t->pre_ff); free(t->post_ff); free(t->qn);
+    }
+    free(m->D);
+    free_lin(&m->dpre); free_lin(&m->dpost); free_lin(&m->dcent); free(m->dnorm);
+  }
+  free(m->fnorm); free(m->E); free(m->hdata); free(m->exc_ptr); free(m->exc_col); free(m->exc_delta);
+  free(m->Kc); free(m->Vc);
+  for (int t = 0; t < 2; ++t) { free(m->rc[t]); free(m->rs[t]); }
+  free(m);
+}
+
+/* ---- row operations (gemma4_engine.cpp:326-402) */
+static float rms_scale(const float* x, int n) {
+  double s[4][4] = {{0}};
+  for (int i = 0; i < n; i += 16)
+    for (int a = 0; a < 4; ++a)
+      for (int b = 0; b < 4; ++b) { const double d = x[i + 4 * a + b]; s[a][b] = fma(d, d, s[a][b]); }
+  double t[4];
+  for (int b = 0; b < 4; ++b) t[b] = (s[0][b] + s[1][b]) + (s[2][b] + s[3][b]);
+  const double ss = (t[0] + t[2]) + (t[1] + t[3]);
+  return 1.0f / sqrtf((float)(ss / n) + 1e-6f);
+}
+static void rmsnorm(const float* x, const float* w, int n, float* y, int round) {
+  const float r = rms_scale(x, n);
+  for (int i = 0; i < n; ++i) { const float v = (x[i] * r) * w[i]; y[i] = round ? or_r16(v) : v; }
+}
+static void rope(float* h, const float* cs, const float* sn, int hd) {
+  const int hh = hd / 2;
+  for (int j = 0; j < hh; ++j) {
+    const float u = h[j], w = h[j + hh];
+    h[j] = fmaf(u, cs[j], -(w * sn[j]));
+    h[j + hh] = fmaf(w, cs[j], u * sn[j]);
+  }
+}
+static void rms_r16_w(float* x, const float* w, int n) {
+  const float r = rms_scale(x, n);
+  for (int i = 0; i < n; ++i) x[i] = or_r16(w ? (x[i] * r) * w[i] : x[i] * r);
+}
+
+static void lin(Model* m, const Lin* w, const float* X, int M, float* Y, int force_i8) {
+  if ((m->i8 && M >= 2) || force_i8) {
+    int8_t* q = (int8_t*)malloc((size_t)M * w->K);
+    float* sx = (float*)malloc(sizeof(float) * (size_t)M * (w->K / 32));
+    int32_t* sm = (int32_t*)malloc(sizeof(int32_t) * (size_t)M * (w->K / 32));
+    or_w4a8_quant(X, M, w->K, q, sx, sm);
+    or_w4a8_gemm(w->w, w->s, q, sx, sm, M, w->N, w->K, Y);
+    free(q); free(sx); free(sm);
+  } else {
+    or_w4g32_gemm(w->w, w->s, X, M, w->N, w->K, Y);
+  }
+}
+
+/* non-split attention for row m: variant 0 = attn_tile (:1061-1083), 1 = per-(m,h) (:1337-1355) */
+static void attn_row(const Model* m, const uint16_t* Kc, const uint16_t* Vc, const float* q, int lo, int pos, int variant,
+                     float* out) {
+  const int hd = m->HD, len = pos - lo + 1;
+  float* sc = (float*)malloc(sizeof(float) * len);
+  for (int h = 0; h < m->NQ; ++h) {
+    const float* qh = q + (size_t)h * hd;
+    float mx = -1e30f;
+    for (int p = lo; p <= pos; ++p) {
+      const uint16_t* kr = Kc + (size_t)p * hd;
+      float s;
+      if (variant == 0) {
+        float s0[8] = {0}, s1[8] = {0}, t[8];
+        for (int i = 0; i < hd; i += 16)
+          for (int l = 0; l < 8; ++l) { s0[l] = fmaf(qh[i + l], or_bf2f(kr[i + l]), s0[l]); s1[l] = fmaf(qh[i + 8 + l], or_bf2f(kr[i + 8 + l]), s1[l]); }
+        for (int l = 0; l < 8; ++l) t[l] = s0[l] + s1[l];
+        s = ((t[0] + t[4]) + (t[1] + t[5])) + ((t[2] + t[6]) + (t[3] + t[7]));
+      } else {
+        float sv[8] = {0};
+        for (int i = 0; i < hd; i += 8)
+          for (int l = 0; l < 8; ++l) sv[l] = fmaf(qh[i + l], or_bf2f(kr[i + l]), sv[l]);
+        s = ((sv[0] + sv[4]) + (sv[1] + sv[5])) + ((sv[2] + sv[6]) + (sv[3] + sv[7]));
+      }
+      sc[p - lo] = s;
+      mx = mx < s ? s : mx;
+    }
+    float den = 0.f;
+    for (int p = 0; p < len; ++p) { sc[p] = variant == 0 ? or_exp8(sc[p] - mx) : expf(sc[p] - mx); den += sc[p]; }
+    float* o = out + (size_t)h * hd;
+    for (int i = 0; i < hd; ++i) o[i] = 0.f;
+    if (variant == 0) {
+      for (int p = 0; p < len; ++p)
+        for (int i = 0; i < hd; ++i) o[i] = fmaf(sc[p], or_bf2f(Vc[(size_t)(lo + p) * hd + i]), o[i]);
+      const float inv = 1.0f / den;
+      for (int i = 0; i < hd; ++i) o[i] = or_r16(o[i] * inv);
+    } else {
+      for (int p = 0; p < len; ++p) {
+        const float w = sc[p] / den;
+        for (int i = 0; i < hd; ++i) o[i] = fmaf(w, or_bf2f(Vc[(size_t)(lo + p) * hd + i]), o[i]);
+      }
+      for (int i = 0; i < hd; ++i) o[i] = or_r16(o[i]);
+    }
+  }
+  free(sc);
+}
+
+/* One target forward over M tokens at pos0 (fwd).  G[hf..] = greedy tokens, hbuf[hf..] = hidden. */
+static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf, int* G, float* hbuf) {
+  const int H = m->H, QD = m->NQ * m->HD, ld = QD + 2 * m->HD, I = m->I, hd = m->HD;
+  float* x = (float*)malloc(sizeof(float) * (size_t)M * H);
+  float* a = (float*)malloc(sizeof(float) * (size_t)M * H);
+  float* qkv = (float*)malloc(sizeof(float) * (size_t)M * ld);
+  float* att = (float*)malloc(sizeof(float) * (size_t)M * QD);
+  float* o = (float*)malloc(sizeof(float) * (size_t)M * H);
+  float* gu = (float*)malloc(sizeof(float) * (size_t)M * 2 * I);
+  float* act = (float*)malloc(sizeof(float) * (size_t)M * I);
+  float* mlp_in = (float*)malloc(sizeof(float) * (size_t)M * H);
+  const float sqrtH = sqrtf((float)H);
+  for (int r = 0; r < M; ++r)
+    for (int i = 0; i < H; ++i) x[(size_t)r * H + i] = or_r16(or_bf2f(m->E[(size_t)toks[r] * H + i]) * sqrtH);
+  for (int l = 0; l < m->NL; ++l) {
+    TLayer* t = &m->L[l];
+    const int ty = t->global ? 1 : 0;
+    for (int r = 0; r < M; ++r) rmsnorm(x + (size_t)r * H, t->in_ln, H, a + (size_t)r * H, 0);
+    lin(m, &t->qkv, a, M, qkv, 0);
+    uint16_t* Kc = m->Kc + (size_t)l * m->ctx_max * hd;
+    uint16_t* Vc = m->Vc + (size_t)l * m->ctx_max * hd;
+    for (int r = 0; r < M; ++r) {
+      const int pos = pos0 + r;
+      const float* cs = m->rc[ty] + (size_t)pos * (hd / 2);
+      const float* sn = m->rs[ty] + (size_t)pos * (hd / 2);
+      float* qr = qkv + (size_t)r * ld;
+      for (int h = 0; h < m->NQ; ++h) { rms_r16_w(qr + (size_t)h * hd, t->qn, hd); rope(qr + (size_t)h * hd, cs, sn, hd); }
+      float* kr = qr + QD;
+      float* vr = qr + QD + hd;
+      rms_r16_w(kr, t->kn, hd); rope(kr, cs, sn, hd);
+      rms_r16_w(vr, NULL, hd);
+      for (int i = 0; i < hd; ++i) { Kc[(size_t)pos * hd + i] = or_f2bf(kr[i]); Vc[(size_t)pos * hd + i] = or_f2bf(vr[i]); }
+    }
+    if (M <= 4 && pos0 + M > m->att_par) {
+      int pos[4], lo[4], kmin = 1 << 30;
+      float* q = (float*)malloc(sizeof(float) * (size_t)M * QD);
+      for (int r = 0; r < M; ++r) {
+        pos[r] = pos0 + r;
+        lo[r] = t->global ? 0 : (pos[r] - 511 > 0 ? pos[r] - 511 : 0);
+        kmin = lo[r] < kmin ? lo[r] : kmin;
+        memcpy(q + (size_t)r * QD, qkv + (size_t)r * ld, sizeof(float) * QD);
+      }
+      or_attn_splitkv(Kc, Vc, hd, m->NQ, M, q, pos, lo, kmin, pos0 + M - 1, m->attn_chunks, att);
+      free(q);
+    } else {
+      const int variant = (M >= 4 && pos0 + M > 64) ? 0 : 1;
+#pragma omp parallel for schedule(dynamic)
+      for (int r = 0; r < M; ++r) {
+        const int pos = pos0 + r, lo = t->global ? 0 : (pos - 511 > 0 ? pos - 511 : 0);
+        attn_row(m, Kc, Vc, qkv + (size_t)r * ld, lo, pos, variant, att + (size_t)r * QD);
+      }
+    }
+    lin(m, &t->o, att, M, o, 0);
+    for (int r = 0; r < M; ++r) {
+      float* om = o + (size_t)r * H;
+      float* xm = x + (size_t)r * H;
+      for (int i = 0; i < H; ++i) om[i] = or_r16(om[i]);
+      const float rr = rms_scale(om, H);
+      for (int i = 0; i < H; ++i) xm[i] = or_r16(xm[i] + or_r16((om[i] * rr) * t->post_attn[i]));
+      rmsnorm(xm, t->pre_ff, H, mlp_in + (size_t)r * H, 1);
+    }
+    lin(m, &t->gu, mlp_in, M, gu, 0);
+    for (int r = 0; r < M; ++r)
+      for (int i = 0; i < I; ++i) {
+        const float g = or_r16(gu[(size_t)r * 2 * I + i]), u = or_r16(gu[(size_t)r * 2 * I + I + i]);
+        act[(size_t)r * I + i] = or_r16(or_r16(or_gelu(g)) * u);
+      }
+    lin(m, &t->down, act, M, o, 0);
+    for (int r = 0; r < M; ++r) {
+      float* om = o + (size_t)r * H;
+      float* xm = x + (size_t)r * H;
+      for (int i = 0; i < H; ++i) om[i] = or_r16(om[i]);
+      const float rr = rms_scale(om, H);
+      for (int i = 0; i < H; ++i) xm[i] = or_r16(or_r16(xm[i] + or_r16((om[i] * rr) * t->post_ff[i])) * 1.0f);
+    }
+  }
+  if (want) {
+    float* logits = (float*)malloc(sizeof(float) * (size_t)m->V);
+    for (int r = hf; r < M; ++r) {
+      rmsnorm(x + (size_t)r * H, m->fnorm, H, hbuf + (size_t)r * H, 1);
+      or_bf16p_gemm(m->hdata, m->cb, m->exc_ptr, m->exc_col, m->exc_delta, m->V, H, hbuf + (size_t)r * H, 1, logits);
+      G[r] = or_head_pick(logits, m->V);
+    }
+    free(logits);
+  }
+  free(x); free(a); free(qkv); free(att); free(o); free(gu); free(act); free(mlp_in);
+}
+
+/* One draft step (draft_step :1534-1563): returns the drafted token; next hidden into h_next. */
+static int draft(Model* m, int tok, const float* h, int pos, int P, float* h_next) {
+  const int H = m->H, QD = m->NQ * m->HD, I = m->I, hd = m->HD;
+  float* comb = (float*)malloc(sizeof(float) * 2 * H);
+  float* dx = (float*)malloc(sizeof(float) * H);
+  float* da = (float*)malloc(sizeof(float) * (H > I ? H : I));
+  float* dq = (float*)malloc(sizeof(float) * QD);
+  float* dopt = (float*)malloc(sizeof(float) * QD);
+  float* dgu = (float*)malloc(sizeof(float) * 2 * I);
+  float* dact = (float*)malloc(sizeof(float) * I);
+  float* dh = (float*)malloc(sizeof(float) * H);
+  float* score = (float*)malloc(sizeof(float) * m->DCENT);
+  const float sqrtH = sqrtf((float)H);
+  for (int i = 0; i < H; ++i) { comb[i] = or_r16(or_bf2f(m->E[(size_t)tok * H + i]) * sqrtH); comb[H + i] = h[i]; }
+  lin(m, &m->dpre, comb, 1, dx, 1);
+  for (int i = 0; i < H; ++i) dx[i] = or_r16(dx[i]);
+  for (int l = 0; l < m->DL; ++l) {
+    DLayer* t = &m->D[l];
+    const int ty = t->global ? 1 : 0;
+    int tl = -1;
+    for (int l2 = m->NL - 1; l2 >= 0; --l2)
+      if ((l2 % 5 == 4) == t->global) { tl = l2; break; }
+    rmsnorm(dx, t->in_ln, H, da, 0);
+    lin(m, &t->q, da, 1, dq, 1);
+    const float* cs = m->rc[ty] + (size_t)pos * (hd / 2);
+    const float* sn = m->rs[ty] + (size_t)pos * (hd / 2);
+    for (int hh = 0; hh < m->NQ; ++hh) { rms_r16_w(dq + (size_t)hh * hd, t->qn, hd); rope(dq + (size_t)hh * hd, cs, sn, hd); }
+    const int lo = t->global ? 0 : (pos - 511 > 0 ? pos - 511 : 0);
+    int pp = P, ll = lo;
+    or_attn_splitkv(m->Kc + (size_t)tl * m->ctx_max * hd, m->Vc + (size_t)tl * m->ctx_max * hd, hd, m->NQ, 1, dq, &pp, &ll, lo,
+                    P, m->attn_chunks, dopt);
+    lin(m, &t->o, dopt, 1, da, 1);
+    for (int i = 0; i < H; ++i) da[i] = or_r16(da[i]);
+    { const float r = rms_scale(da, H); for (int i = 0; i < H; ++i) dx[i] = or_r16(dx[i] + or_r16((da[i] * r) * t->post_attn[i])); }
+    rmsnorm(dx, t->pre_ff, H, da, 1);
+    lin(m, &t->gu, da, 1, dgu, 1);
+    for (int i = 0; i < I; ++i) dact[i] = or_r16(or_r16(or_gelu(or_r16(dgu[i]))) * or_r16(dgu[I + i]));
+    lin(m, &t->down, dact, 1, da, 1);
+    for (int i = 0; i < H; ++i) da[i] = or_r16(da[i]);
+    { const float r = rms_scale(da, H); for (int i = 0; i < H; ++i) dx[i] = or_r16(dx[i] + or_r16((da[i] * r) * t->post_ff[i])); }
+    for (int i = 0; i < H; ++i) dx[i] = or_r16(dx[i] * 1.0f);
+  }
+  rmsnorm(dx, m->dnorm, H, dh, 1);
+  lin(m, &m->dpost, dh, 1, h_next, 1);
+  lin(m, &m->dcent, dh, 1, score, 1);
+  for (int i = 0; i < H; ++i) h_next[i] = or_r16(h_next[i]);
+  /* top DTOP centroids (insertion sort, :1554-1555), candidates, scores, first max */
+  int top[32];
+  float thr[32];
+  int cnt = 0;
+  for (int c = 0; c < m->DCENT; ++c) {
+    const float s = score[c];
+    if (cnt < m->DTOP) { int j = cnt++; while (j > 0 && thr[j - 1] < s) { thr[j] = thr[j - 1]; top[j] = top[j - 1]; --j; } thr[j] = s; top[j] = c; }
+    else if (s > thr[m->DTOP - 1]) { int j = m->DTOP - 1; while (j > 0 && thr[j - 1] < s) { thr[j] = thr[j - 1]; top[j] = top[j - 1]; --j; } thr[j] = s; top[j] = c; }
+  }
+  int best = -1;
+  float bs = -1e30f;
+  for (int t = 0; t < m->DTOP; ++t)
+    for (int j = 0; j < m->DPER; ++j) {
+      const int c = (int)perm_token((uint32_t)(top[t] * m->DPER + j), (uint32_t)m->V);
+      const uint16_t* er = m->E + (size_t)c * H;
+      float a0[8] = {0}, b0[8] = {0}, tt[8];
+      for (int k = 0; k < H; k += 16)
+        for (int l = 0; l < 8; ++l) { a0[l] = fmaf(or_bf2f(er[k + l]), dh[k + l], a0[l]); b0[l] = fmaf(or_bf2f(er[k + 8 + l]), dh[k + 8 + l], b0[l]); }
+      for (int l = 0; l < 8; ++l) tt[l] = a0[l] + b0[l];
+      const float s = ((tt[0] + tt[4]) + (tt[1] + tt[5])) + ((tt[2] + tt[6]) + (tt[3] + tt[7]));
+      if (best < 0 || s > bs) { bs = s; best = c; }
+    }
+  free(comb); free(dx); free(da); free(dq); free(dopt); free(dgu); free(dact); free(dh); free(score);
+  return best;
+}
+
+int or_e2e_forward(void* mp, const int32_t* toks, int M, int pos0, int want, int hf, int int8, int32_t* G, float* hbuf) {
+  Model* m = (Model*)mp;
+  m->i8 = int8;
+  float* hb = hbuf ? hbuf : (float*)malloc(sizeof(float) * (size_t)M * m->H);
+  forward(m, toks, M, pos0, want, hf, G, hb);
+  if (!hbuf) free(hb);
+  return 0;
+}
+int or_e2e_draft(void* mp, int32_t tok, const float* h, int pos, int P, int32_t* out_tok, float* h_next) {
+  Model* m = (Model*)mp;
+  float* hn = h_next ? h_next : (float*)malloc(sizeof(float) * m->H);
+  *out_tok = draft(m, tok, h, pos, P, hn);
+  if (!h_next) free(hn);
+  return 0;
+}
+
+static int is_stop(int t) { return t == 106 || t == 1; }
+
+/* run_req in chain mode (:1582-1663). stats[0..5] = rounds, ngram_rounds, drafted, accepted. */
+int or_e2e_generate(void* mp, const int32_t* prompt, int n, int n_new, int32_t* out, int* n_out, int* stats) {
+  Model* m = (Model*)mp;
+  const int H = m->H;
+  int* G = (int*)malloc(sizeof(int) * 64);
+  float* hbuf = (float*)malloc(sizeof(float) * 64 * H);
+  m->i8 = m->prefill_int8;
+  int done = 0, lastM = 0;
+  while (done < n) {
+    const int M = m->prefill_block < n - done ? m->prefill_block : n - done;
+    const int last = done + M == n;
+    forward(m, prompt + done, M, done, last, last ? M - 1 : 0, G, hbuf);
+    done += M; lastM = M;
+  }
+  m->i8 = m->decode_int8 && m->prefill_int8;
+  int* gen = (int*)malloc(sizeof(int) * (n_new + 8));
+  int* seq = (int*)malloc(sizeof(int) * (n + n_new + 8));
+  memcpy(seq, prompt, sizeof(int) * n);
+  int ng = 0, L = n;
+  gen[ng++] = G[lastM - 1];
+  seq[L++] = G[lastM - 1];
+  float* hprev = (float*)malloc(sizeof(float) * H);
+  float* hcur = (float*)malloc(sizeof(float) * H);
+  float* hnext = (float*)malloc(sizeof(float) * H);
+  memcpy(hprev, hbuf + (size_t)(lastM - 1) * H, sizeof(float) * H);
+  int P = n - 1, conf = gen[0], stopped = is_stop(conf);
+  int rounds = 0, ngr = 0, drafted = 0, accepted = 0;
+  while (ng < n_new && !stopped) {
+    int block[8], nd = 0, used_ng = 0;
+    block[0] = conf;
+    if (m->ngram > 0 && L > m->ngram) {
+      for (int i = L - m->ngram - 1; i >= 0; --i) {
+        int eq = 1;
+        for (int t = 0; t < m->ngram; ++t) if (seq[i + t] != seq[L - m->ngram + t]) { eq = 0; break; }
+        if (eq) { for (int j = 0; j < m->ngram_len && j < 7 && i + m->ngram + j < L; ++j) block[1 + nd++] = seq[i + m->ngram + j]; break; }
+      }
+      if (nd > 0) { used_ng = 1; ngr++; }
+    }
+    if (!used_ng && m->drafter && m->k_draft > 0) {
+      int cur = conf;
+      memcpy(hcur, hprev, sizeof(float) * H);
+      for (int j = 0; j < m->k_draft; ++j) {
+        const int dtok = draft(m, cur, hcur, P + 1 + j, P, hnext);
+        block[1 + nd++] = dtok;
+        cur = dtok;
+        memcpy(hcur, hnext, sizeof(float) * H);
+      }
+      drafted += nd;
+    }
+    forward(m, block, nd + 1, P + 1, 1, 0, G, hbuf);
+    rounds++;
+    int nacc = 0;
+    while (nacc < nd && block[nacc + 1] == G[nacc]) ++nacc;
+    accepted += nacc;
+    for (int i = 0; i <= nacc; ++i) { gen[ng++] = G[i]; seq[L++] = G[i]; if (is_stop(G[i])) { stopped = 1; break; } }
+    conf = G[nacc];
+    memcpy(hprev, hbuf + (size_t)nacc * H, sizeof(float) * H);
+    P += nacc + 1;
+  }
+  if (ng > n_new) ng = n_new;
+  for (int i = 0; i < ng; ++i) if (is_stop(gen[i])) { ng = i + 1; break; }
+  memcpy(out, gen, sizeof(int) * ng);
+  *n_out = ng;
+  if (stats) { stats[0] = rounds; stats[1] = ngr; stats[2] = drafted; stats[3] = accepted; }
+  free(G); free(hbuf); free(gen); free(seq); free(hprev); free(hcur); free(hnext);
+  return 0;
+}
+
+/* raw weight bytes for cross-checking the generator: tensor `id`, first n bytes (reference layout) */
+void or_e2e_gen_bytes(unsigned long long seed, unsigned long long id, long long n, uint8_t* out) {
+  for (long long i = 0; i < n; ++i) out[i] = (uint8_t)(wh(seed, id, (uint64_t)i) & 0xFF);
+}

@@ -46,6 +46,12 @@ _SIGS_ORACLE = {
     "or_exp8": (_F, [_F]),
     "or_gelu": (_F, [_F]),
     "or_r16": (_F, [_F]),
+    "or_e2e_create": (_P, [_P]),
+    "or_e2e_destroy": (None, [_P]),
+    "or_e2e_forward": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "or_e2e_draft": (_I, [_P, _I, _P, _I, _I, _P, _P]),
+    "or_e2e_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+    "or_e2e_gen_bytes": (None, [ctypes.c_ulonglong, ctypes.c_ulonglong, ctypes.c_longlong, _P]),
 }
 
 _SIGS_REF = {
@@ -219,3 +225,87 @@ def or_seed_bound(W4, S4, coef, h, seeds):
 
 def or_calc_thr(L):
     return oracle().or_calc_thr(float(L))
+
+
+# ---------------------------------------------------------------- end-to-end oracle
+class E2EConfig(ctypes.Structure):
+    """Field order of g4_engine_config (include/g4.h)."""
+    _fields_ = [(n, ctypes.c_int) for n in ("hidden", "n_layers", "mlp", "vocab", "ctx_max", "prefill_block", "k_draft",
+                                            "ngram", "ngram_len", "prefill_int8", "decode_int8", "head_screen",
+                                            "screen_lim", "attn_chunks", "att_par", "drafter")] + [
+        ("seed", ctypes.c_ulonglong)]
+
+
+def e2e_config(**kw):
+    c = E2EConfig(hidden=2048, n_layers=30, mlp=8192, vocab=262144, ctx_max=8192, prefill_block=32, k_draft=3, ngram=2,
+                  ngram_len=3, prefill_int8=1, decode_int8=1, head_screen=1, screen_lim=30000, attn_chunks=8, att_par=192,
+                  drafter=1, seed=20261201)
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+class OracleModel:
+    def __init__(self, cfg):
+        self.cfg = cfg
+        self.h = oracle().or_e2e_create(ctypes.byref(cfg))
+
+    def close(self):
+        if self.h:
+            oracle().or_e2e_destroy(self.h)
+            self.h = None
+
+    def forward(self, toks, pos0, want=True, hf=0, int8=True):
+        toks = np.ascontiguousarray(toks, np.int32)
+        M = toks.size
+        G = np.full(M, -1, np.int32)
+        hb = np.zeros((M, self.cfg.hidden), np.float32)
+        oracle().or_e2e_forward(self.h, ptr(toks), M, pos0, int(want), hf, int(int8), ptr(G), ptr(hb))
+        return G, hb
+
+    def draft(self, tok, h, pos, P):
+        out = np.zeros(1, np.int32)
+        hn = np.zeros(self.cfg.hidden, np.float32)
+        oracle().or_e2e_draft(self.h, int(tok), ptr(np.ascontiguousarray(h, np.float32)), pos, P, ptr(out), ptr(hn))
+        return int(out[0]), hn
+
+    def generate(self, prompt, n_new):
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(n_new + 8, np.int32)
+        n_out = np.zeros(1, np.int32)
+        st = np.zeros(8, np.int32)
+        oracle().or_e2e_generate(self.h, ptr(prompt), prompt.size, n_new, ptr(out), ptr(n_out), ptr(st))
+        return out[: n_out[0]].copy(), {"rounds": int(st[0]), "ngram_rounds": int(st[1]), "drafted": int(st[2]),
+                                        "accepted": int(st[3])}
+
+
+def gen_bytes(seed, tid, n):
+    out = np.zeros(n, np.uint8)
+    oracle().or_e2e_gen_bytes(seed, tid, n, ptr(out))
+    return out
+
+
+def make_prompt(seed, n, vocab=262144, copy_frac=0.2):
+    """configs[4] prompt: Zipf(1.1) token ranks over the vocab (mapped through a fixed permutation),
+    with about copy_frac of the positions copied from earlier 8-32-token spans so that prompt lookup
+    finds matches.  Deterministic for a seed."""
+    rng = np.random.default_rng(seed)
+    ranks = np.arange(1, vocab + 1, dtype=np.float64)
+    p = ranks ** -1.1
+    cdf = np.cumsum(p / p.sum())
+    perm = rng.permutation(vocab).astype(np.int32)
+    out = np.empty(n, np.int32)
+    i = 0
+    while i < n:
+        if i >= 64 and rng.random() < copy_frac / 20.0 * 1.0:
+            L = int(rng.integers(8, 33))
+            src = int(rng.integers(0, i - L)) if i - L > 0 else 0
+            for k in range(L):
+                if i >= n:
+                    break
+                out[i] = out[src + k]
+                i += 1
+        else:
+            out[i] = perm[min(int(np.searchsorted(cdf, rng.random())), vocab - 1)]
+            i += 1
+    return out
