@@ -23,7 +23,32 @@ namespace g4 {
 struct AttnDesc {
   int M, nh, hd, kmin, kmax, T;
   int pos[4], lo[4];
+  // Positions read on the device (a captured decode step whose position changes between replays):
+  // when dynP is set, row m's last key is *dynP + base_add + m and its first key is
+  // max(0, *dynP + q_add + m - (window - 1)) (0 for window == 0); kmin/kmax follow from them.
+  const int* dynP;
+  int base_add, q_add, window;
 };
+
+__device__ __forceinline__ AttnDesc resolve(const AttnDesc& d0) {
+  AttnDesc d = d0;
+  if (d.dynP != nullptr) {
+    const int P = *d.dynP;
+    d.kmin = 1 << 30;
+    for (int m = 0; m < 4; ++m) {
+      if (m < d.M) {
+        d.pos[m] = P + d.base_add + m;
+        d.lo[m] = d.window ? max(0, P + d.q_add + m - (d.window - 1)) : 0;
+        d.kmin = min(d.kmin, d.lo[m]);
+      } else {
+        d.pos[m] = -1;
+        d.lo[m] = 0;
+      }
+    }
+    d.kmax = P + d.base_add + d.M - 1;
+  }
+  return d;
+}
 
 __device__ __forceinline__ bool allowed(const AttnDesc& d, int m, int p) { return p >= d.lo[m] && p <= d.pos[m]; }
 __device__ __forceinline__ int chunk_lo(const AttnDesc& d, int t) {
@@ -31,8 +56,8 @@ __device__ __forceinline__ int chunk_lo(const AttnDesc& d, int t) {
   return d.kmin + (int)((long long)t * len / d.T);
 }
 
-// Workspace layout (floats): S [len][M][nh] scores then weights, AM [T][M][nh], AL [T][M][nh],
-// AO [T][M][nh][hd].
+// Workspace layout (floats): S [M*nh][len] scores then weights (one contiguous run of keys per
+// (row, head)), AM [T][M*nh], AL [T][M*nh], AO [T][M*nh][hd].
 struct AttnWs {
   float *S, *AM, *AL, *AO;
 };
@@ -49,117 +74,234 @@ __device__ __forceinline__ AttnWs attn_ws(float* base, const AttnDesc& d) {
   return w;
 }
 
-// ---- scores.  Block = 256 threads = 16 half-warps; half-warp (m, h) pairs are spread over the
-// blocks' y dimension.  Each block walks KB keys; K rows come from L1/L2 (each row is read by the
-// M*nh half-warps of the key).  q for the half-warp's (m, h) stays in registers (16 floats/lane).
+// ---- scores.  A block takes kScoreKeys consecutive keys, copies their K rows into shared memory
+// (one bulk copy), and gives each (row, head) pair one half-warp: lane c runs the reference's AVX
+// partial sum c (elements c, c+16, ...; q for the pair stays in registers), then the two 8-lane
+// halves are added and reduced with the 8-lane tree of hsum (:786-797).
 constexpr int kScoreKeys = 32;
-__global__ void __launch_bounds__(256) k_attn_scores(const uint16_t* __restrict__ Kc, const float* __restrict__ q,
-                                                     AttnDesc d, float* __restrict__ ws) {
+template <int STEPS>  // hd / 16
+__global__ void __launch_bounds__(512) k_attn_scores(const uint16_t* __restrict__ Kc, const float* __restrict__ q,
+                                                     AttnDesc d0, float* __restrict__ ws) {
+  extern __shared__ __align__(128) uint8_t sm_raw[];
+  const AttnDesc d = resolve(d0);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm_raw);
+  const uint16_t* kt = reinterpret_cast<const uint16_t*>(sm_raw + 128);
   const AttnWs w = attn_ws(ws, d);
+  const int len = d.kmax - d.kmin + 1;
+  const int p0 = d.kmin + blockIdx.x * kScoreKeys;
+  if (p0 > d.kmax) return;  // grid sized for the longest key range (positions read on the device)
+  const int nk = min(kScoreKeys, d.kmax + 1 - p0);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t bytes = (uint32_t)nk * d.hd * 2;
+    mbar_expect_tx(bar, bytes);
+    bulk_g2s(sm_raw + 128, Kc + (size_t)p0 * d.hd, bytes, bar);
+  }
   const int hw = threadIdx.x >> 4, c = threadIdx.x & 15;
-  const int mh = blockIdx.y * 16 + hw;  // (m, h) pair of this half-warp
-  const bool live_mh = mh < d.M * d.nh;
-  const int m = live_mh ? mh / d.nh : 0, h = live_mh ? mh % d.nh : 0;
-  const int steps = d.hd >> 4;  // <= 32 (hd <= 512)
-  float qr[32];
+  const bool live_mh = hw < d.M * d.nh;
+  const int m = live_mh ? hw / d.nh : 0, h = live_mh ? hw % d.nh : 0;
+  float qr[STEPS];
   const float* qh = q + ((size_t)m * d.nh + h) * d.hd;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) qr[i] = (i < steps) ? qh[c + 16 * i] : 0.f;
-  const int p0 = d.kmin + blockIdx.x * kScoreKeys;
-  const int p1 = min(p0 + kScoreKeys, d.kmax + 1);
-  for (int p = p0; p < p1; ++p) {
-    const uint16_t* kr = Kc + (size_t)p * d.hd;
+  for (int i = 0; i < STEPS; ++i) qr[i] = qh[c + 16 * i];
+  if (!cta_wait(bar, 0)) return;
+  float* srow = w.S + (size_t)hw * len + (p0 - d.kmin);
+  int k = 0;
+  for (; k + 4 <= nk; k += 4) {  // four keys at a time: independent chains for latency hiding
+    float acc[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint16_t* kr = kt + (size_t)(k + u) * d.hd;
+      acc[u] = 0.f;
+#pragma unroll
+      for (int i = 0; i < STEPS; ++i) acc[u] = fmaf(qr[i], bf2f(kr[c + 16 * i]), acc[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float sc = hsum8_octet(__fadd_rn(acc[u], __shfl_xor_sync(FULL, acc[u], 8)));
+      if (c == 0 && live_mh && allowed(d, m, p0 + k + u)) srow[k + u] = sc;
+    }
+  }
+  for (; k < nk; ++k) {
+    const uint16_t* kr = kt + (size_t)k * d.hd;
     float acc = 0.f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (i < steps) acc = fmaf(qr[i], bf2f(__ldg(kr + c + 16 * i)), acc);
-    // t_l = s0_l + s1_l (lanes l and l+8 of the half-warp), then the 8-lane hsum tree.
-    const float t = __fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8));
-    const float sc = hsum8_octet(t);
-    if (c == 0 && live_mh && allowed(d, m, p)) w.S[((size_t)(p - d.kmin) * d.M + m) * d.nh + h] = sc;
+    for (int i = 0; i < STEPS; ++i) acc = fmaf(qr[i], bf2f(kr[c + 16 * i]), acc);
+    const float sc = hsum8_octet(__fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8)));
+    if (c == 0 && live_mh && allowed(d, m, p0 + k)) srow[k] = sc;
   }
 }
 
-// ---- chunk statistics: one warp per (t, m, h).  max is order-free; the weights exp8(s - max)
-// are elementwise; their sum runs in key order in lane 0 (a batch of 32 keys at a time).
-__global__ void __launch_bounds__(256) k_attn_stats(AttnDesc d, float* __restrict__ ws) {
+// ---- chunk statistics: block = (chunk t, 8 (row, head) pairs), one warp per pair.  The warp holds the
+// chunk's allowed scores in registers (key c0 + 32*j + lane in slot j); max is order-free; the
+// weights exp8(s - max) are elementwise and overwrite the scores; their sum runs in key order
+// (each slot's 32 keys are handed over by shuffles).  Longer chunks run in segments of
+// 32*kStatSlots keys.
+constexpr int kStatSlots = 32;
+__global__ void __launch_bounds__(256) k_attn_stats(AttnDesc d0, float* __restrict__ ws) {
+  const AttnDesc d = resolve(d0);
   const AttnWs w = attn_ws(ws, d);
-  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (wid >= d.T * d.M * d.nh) return;
-  const int t = wid / (d.M * d.nh), m = (wid / d.nh) % d.M, h = wid % d.nh;
-  const int c0 = chunk_lo(d, t), c1 = chunk_lo(d, t + 1);
+  const int mh = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31, t = blockIdx.x;
+  if (mh >= d.M * d.nh) return;
+  const int m = mh / d.nh, len = d.kmax - d.kmin + 1;
+  const int c0 = max(chunk_lo(d, t), d.lo[m]), c1 = min(chunk_lo(d, t + 1), d.pos[m] + 1);  // allowed keys of the chunk
+  float* srow = w.S + (size_t)mh * len - d.kmin;
+  constexpr int SEG = 32 * kStatSlots;
+  const bool one = c1 - c0 <= SEG;  // the whole chunk fits the registers: load it once
+  float v[kStatSlots];
   float mx = -1e30f;
-  for (int p = c0 + lane; p < c1; p += 32)
-    if (allowed(d, m, p)) mx = fmaxf(mx, w.S[((size_t)(p - d.kmin) * d.M + m) * d.nh + h]);
+  for (int sb = c0; sb < c1; sb += SEG) {
+#pragma unroll
+    for (int j = 0; j < kStatSlots; ++j) {
+      const int p = sb + 32 * j + lane;
+      v[j] = p < c1 ? srow[p] : -1e30f;
+      mx = fmaxf(mx, v[j]);
+    }
+  }
 #pragma unroll
   for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
   float l8 = 0.f;
-  for (int pb = c0; pb < c1; pb += 32) {
-    const int p = pb + lane;
-    float wt = 0.f;
-    const bool ok = p < c1 && allowed(d, m, p);
-    if (ok) {
-      float* sp = &w.S[((size_t)(p - d.kmin) * d.M + m) * d.nh + h];
-      wt = exp8(__fsub_rn(*sp, mx));
-      *sp = wt;
+  for (int sb = c0; sb < c1; sb += SEG) {
+    if (!one) {
+#pragma unroll
+      for (int j = 0; j < kStatSlots; ++j) {
+        const int p = sb + 32 * j + lane;
+        v[j] = p < c1 ? srow[p] : -1e30f;
+      }
     }
-    const unsigned okm = __ballot_sync(FULL, ok);
-    for (int k = 0; k < 32; ++k) {  // lane 0 adds the batch in key order
-      const float v = __shfl_sync(FULL, wt, k);
-      if ((okm >> k) & 1u) l8 = __fadd_rn(l8, v);
+#pragma unroll
+    for (int j = 0; j < kStatSlots; ++j) {
+      const int pb = sb + 32 * j;
+      if (pb >= c1) break;  // warp-uniform
+      const int p = pb + lane;
+      float wt = 0.f;
+      if (p < c1) {
+        wt = exp8(__fsub_rn(v[j], mx));
+        srow[p] = wt;
+      }
+      const int nb = min(32, c1 - pb);
+      if (nb == 32) {
+        float x[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) x[k] = __shfl_sync(FULL, wt, k);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) l8 = __fadd_rn(l8, x[k]);  // every lane adds in key order
+      } else {
+        for (int k = 0; k < nb; ++k) l8 = __fadd_rn(l8, __shfl_sync(FULL, wt, k));
+      }
     }
   }
   if (lane == 0) {
-    const size_t ix = ((size_t)t * d.M + m) * d.nh + h;
+    const size_t ix = (size_t)t * d.M * d.nh + mh;
     w.AM[ix] = mx;
     w.AL[ix] = (d.lo[m] > d.pos[m]) ? 0.0f : l8;
   }
 }
 
-// ---- O accumulation: block = (chunk t, 32-dim slice); thread = (m, h, dim).  Each thread runs
-// its fma chain over the chunk's keys in order; a warp shares (m, h), so the weight load is a
-// broadcast and the V loads are one 64-byte row segment shared by all warps of the block.
-__global__ void __launch_bounds__(1024) k_attn_accum(const uint16_t* __restrict__ Vc, AttnDesc d,
-                                                     float* __restrict__ ws) {
+// cp.async (Ampere-style asynchronous copy) of 4 / 16 bytes global -> shared, grouped.
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// ---- O accumulation: block = (chunk t, 16-dim slice, group of 8 (row, head) pairs).  Thread =
+// (pair g of the group, dim pair dp): one packed f32x2 fma chain over the chunk's allowed keys in
+// order.  V slices and weights of kAccKeys keys at a time are staged in shared memory with
+// asynchronous copies, double-buffered so that the next tile loads while this one is consumed.
+constexpr int kAccKeys = 128;
+__global__ void __launch_bounds__(64) k_attn_accum(const uint16_t* __restrict__ Vc, AttnDesc d0, float* __restrict__ ws) {
+  const AttnDesc d = resolve(d0);
+  __shared__ __align__(16) uint32_t vs[2][kAccKeys][8];    // 16 bf16 dims per key
+  __shared__ __align__(16) float wsm[2][8][kAccKeys + 1];  // weights [pair][key], padded against bank conflicts
   const AttnWs w = attn_ws(ws, d);
-  const int t = blockIdx.x, i = blockIdx.y * 32 + (threadIdx.x & 31);
-  const int mh = threadIdx.x >> 5;
-  if (mh >= d.M * d.nh || i >= d.hd) return;
-  const int m = mh / d.nh, h = mh % d.nh;
+  const int t = blockIdx.x, i0 = blockIdx.y * 16, mhb = blockIdx.z * 8;
+  const int nmh = d.M * d.nh, len = d.kmax - d.kmin + 1;
+  const int g = threadIdx.x >> 3, dp = threadIdx.x & 7;
+  const int ng = min(8, nmh - mhb);  // live pairs in this group
+  const bool live = g < ng;
+  const int mh = mhb + (live ? g : 0), m = mh / d.nh;
   const int c0 = chunk_lo(d, t), c1 = chunk_lo(d, t + 1);
   const int a = max(c0, d.lo[m]), b = min(c1 - 1, d.pos[m]);
-  float o = 0.f;
-  const float* wp = w.S + (size_t)m * d.nh + h;
-  const size_t wstride = (size_t)d.M * d.nh;
+  auto stage = [&](int buf, int pb) {
+    const int nk = min(kAccKeys, c1 - pb);
+    for (int e = threadIdx.x; e < nk * 2; e += 64)  // V: 2 x 16 B per key
+      cp_async16(&vs[buf][e >> 1][(e & 1) * 4], Vc + (size_t)(pb + (e >> 1)) * d.hd + i0 + (e & 1) * 8);
+    for (int r = 0; r < ng; ++r) {
+      const float* src = w.S + (size_t)(mhb + r) * len + (pb - d.kmin);
+      for (int k = threadIdx.x; k < nk; k += 64) cp_async4(&wsm[buf][r][k], src + k);
+    }
+  };
+  float2 o = make_float2(0.f, 0.f);
+  stage(0, c0);
+  cp_async_commit();
+  for (int pb = c0, it = 0; pb < c1; pb += kAccKeys, ++it) {
+    if (pb + kAccKeys < c1) stage((it + 1) & 1, pb + kAccKeys);
+    cp_async_commit();  // possibly empty group: keeps the wait count uniform
+    cp_async_wait_1();
+    __syncthreads();
+    const int buf = it & 1;
+    if (live) {
+      const int nk = min(kAccKeys, c1 - pb);
+      const int ka = max(a, pb) - pb, kb = min(b, pb + nk - 1) - pb;
 #pragma unroll 4
-  for (int p = a; p <= b; ++p) o = fmaf(wp[(size_t)(p - d.kmin) * wstride], bf2f(__ldg(Vc + (size_t)p * d.hd + i)), o);
-  w.AO[(((size_t)t * d.M + m) * d.nh + h) * d.hd + i] = o;
+      for (int k = ka; k <= kb; ++k) {
+        const uint32_t vv = vs[buf][k][dp];
+        const float wt = wsm[buf][g][k];
+        o = __ffma2_rn(make_float2(wt, wt), make_float2(__uint_as_float(vv << 16), __uint_as_float(vv & 0xFFFF0000u)), o);
+      }
+    }
+    __syncthreads();
+  }
+  if (live) {
+    float* ao = w.AO + ((size_t)t * nmh + mh) * d.hd + i0 + 2 * dp;
+    ao[0] = o.x;
+    ao[1] = o.y;
+  }
 }
 
-// ---- merge: thread per (m, h, dim).  M0 = max of the chunk maxima with L > 0; sc_t =
-// expf(M_t - M0) (correctly rounded here); l = sum L_t*sc_t in double (each product exact);
-// out = r16((sum_t fma(O_t, sc_t)) * (float)(1/l)).
-__global__ void __launch_bounds__(256) k_attn_merge(AttnDesc d, const float* __restrict__ ws, float* __restrict__ out) {
+// ---- merge: block per (row, head), thread per dim.  M0 = max of the chunk maxima with L > 0;
+// sc_t = expf(M_t - M0) (correctly rounded here); l = sum L_t*sc_t in double in chunk order (each
+// product exact); out = r16((sum_t fma(O_t, sc_t)) * (float)(1/l)).  The per-chunk factors are
+// computed once per block.
+__global__ void __launch_bounds__(512) k_attn_merge(AttnDesc d0, const float* __restrict__ ws, float* __restrict__ out) {
+  const AttnDesc d = resolve(d0);
+  __shared__ float sc[64];
+  __shared__ float inv_l;
   const AttnWs w = attn_ws(const_cast<float*>(ws), d);
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= d.M * d.nh * d.hd) return;
-  const int i = idx % d.hd, mh = idx / d.hd, m = mh / d.nh, h = mh % d.nh;
-  float M0 = -1e30f;
-  for (int t = 0; t < d.T; ++t) {
-    const size_t ix = ((size_t)t * d.M + m) * d.nh + h;
-    if (w.AL[ix] > 0) M0 = fmaxf(M0, w.AM[ix]);
+  const int mh = blockIdx.x, i = threadIdx.x, nmh = d.M * d.nh;
+  if (i == 0) {
+    float M0 = -1e30f;
+    for (int t = 0; t < d.T; ++t) {
+      const size_t ix = (size_t)t * nmh + mh;
+      if (w.AL[ix] > 0) M0 = fmaxf(M0, w.AM[ix]);
+    }
+    double l = 0;
+    for (int t = 0; t < d.T; ++t) {
+      const size_t ix = (size_t)t * nmh + mh;
+      sc[t] = 0.f;
+      if (!(w.AL[ix] > 0)) continue;
+      sc[t] = exp_cr(__fsub_rn(w.AM[ix], M0));
+      l = fma((double)w.AL[ix], (double)sc[t], l);
+    }
+    inv_l = (float)(1.0 / l);
   }
-  double l = 0;
+  __syncthreads();
+  if (i >= d.hd) return;
   float acc = 0.f;
   for (int t = 0; t < d.T; ++t) {
-    const size_t ix = ((size_t)t * d.M + m) * d.nh + h;
+    const size_t ix = (size_t)t * nmh + mh;
     if (!(w.AL[ix] > 0)) continue;
-    const float sc = exp_cr(__fsub_rn(w.AM[ix], M0));
-    l = fma((double)w.AL[ix], (double)sc, l);
-    acc = fmaf(w.AO[ix * d.hd + i], sc, acc);
+    acc = fmaf(w.AO[ix * d.hd + i], sc[t], acc);
   }
-  const float inv = (float)(1.0 / l);
-  out[idx] = r16(__fmul_rn(acc, inv));
+  out[(size_t)mh * d.hd + i] = r16(__fmul_rn(acc, inv_l));
 }
 
 }  // namespace g4
@@ -168,16 +310,36 @@ G4_STATUS_READER(attn)
 
 using namespace g4;
 
-static int fill_desc(AttnDesc& d, int M, int nh, int hd, const int* pos, const int* lo, int kmin, int kmax, int T) {
+static int fill_desc(AttnDesc& d, const uint16_t* Kc, const uint16_t* Vc, int M, int nh, int hd, const int* pos,
+                     const int* lo, int kmin, int kmax, int T) {
+  G4_REQUIRE(aligned(Kc, 16) && aligned(Vc, 16), "attention: K and V caches must be 16-byte aligned");
   G4_REQUIRE(M >= 1 && M <= 4 && nh >= 1 && nh <= 8 && hd >= 16 && hd <= 512 && hd % 32 == 0 && T >= 1 && T <= 64,
              "attention: unsupported shape M=%d nh=%d hd=%d T=%d", M, nh, hd, T);
   G4_REQUIRE(pos && lo && kmin >= 0 && kmax >= kmin, "attention: bad key range [%d, %d]", kmin, kmax);
   d.M = M; d.nh = nh; d.hd = hd; d.kmin = kmin; d.kmax = kmax; d.T = T;
+  d.dynP = nullptr; d.base_add = d.q_add = d.window = 0;
   for (int m = 0; m < 4; ++m) { d.pos[m] = m < M ? pos[m] : -1; d.lo[m] = m < M ? lo[m] : 0; }
   for (int m = 0; m < M; ++m)
     G4_REQUIRE(lo[m] >= kmin && pos[m] <= kmax, "attention: row %d range [%d, %d] outside [%d, %d]", m, lo[m], pos[m],
                kmin, kmax);
   return G4_OK;
+}
+
+static int launch_attn(const uint16_t* Kc, const uint16_t* Vc, const float* q, const AttnDesc& d, float* w, float* out,
+                       cudaStream_t st, int max_len = 0) {
+  const int len = max_len > 0 ? max_len : d.kmax - d.kmin + 1, nmh = d.M * d.nh;
+  const size_t ssm = 128 + (size_t)kScoreKeys * d.hd * 2;
+  if (d.hd == 256) k_attn_scores<16><<<(len + kScoreKeys - 1) / kScoreKeys, nmh * 16, ssm, st>>>(Kc, q, d, w);
+  else if (d.hd == 512) k_attn_scores<32><<<(len + kScoreKeys - 1) / kScoreKeys, nmh * 16, ssm, st>>>(Kc, q, d, w);
+  else if (d.hd == 128) k_attn_scores<8><<<(len + kScoreKeys - 1) / kScoreKeys, nmh * 16, ssm, st>>>(Kc, q, d, w);
+  else return set_error(G4_ERR_UNSUPPORTED, "attention: hd=%d (supported: 128, 256, 512)", d.hd);
+  if (int rc = check_launch("k_attn_scores")) return rc;
+  k_attn_stats<<<dim3(d.T, (nmh + 7) / 8), 256, 0, st>>>(d, w);
+  if (int rc = check_launch("k_attn_stats")) return rc;
+  k_attn_accum<<<dim3(d.T, d.hd / 16, (nmh + 7) / 8), 64, 0, st>>>(Vc, d, w);
+  if (int rc = check_launch("k_attn_accum")) return rc;
+  k_attn_merge<<<nmh, (d.hd + 31) / 32 * 32, 0, st>>>(d, w, out);
+  return check_launch("k_attn_merge");
 }
 
 extern "C" size_t g4_attn_splitkv_ws_bytes(int M, int nh, int hd, int kmin, int kmax, int T) {
@@ -189,21 +351,30 @@ extern "C" int g4_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, const flo
                                void* stream) {
   G4_REQUIRE(Kc && Vc && q && out && ws, "g4_attn_splitkv: null pointer");
   AttnDesc d;
-  if (int rc = fill_desc(d, M, nh, hd, pos, lo, kmin, kmax, T)) return rc;
+  if (int rc = fill_desc(d, Kc, Vc, M, nh, hd, pos, lo, kmin, kmax, T)) return rc;
   const size_t need = g4_attn_splitkv_ws_bytes(M, nh, hd, kmin, kmax, T);
   if (ws_bytes < need) return set_error(G4_ERR_NOMEM, "g4_attn_splitkv: workspace %zu < %zu bytes", ws_bytes, need);
   G4_REQUIRE(aligned(ws, 16), "g4_attn_splitkv: workspace must be 16-byte aligned");
   cudaStream_t st = as_stream(stream);
   float* w = static_cast<float*>(ws);
-  const int len = kmax - kmin + 1;
-  k_attn_scores<<<dim3((len + kScoreKeys - 1) / kScoreKeys, (M * nh + 15) / 16), 256, 0, st>>>(Kc, q, d, w);
-  if (int rc = check_launch("k_attn_scores")) return rc;
-  k_attn_stats<<<(T * M * nh * 32 + 255) / 256, 256, 0, st>>>(d, w);
-  if (int rc = check_launch("k_attn_stats")) return rc;
-  k_attn_accum<<<dim3(T, (hd + 31) / 32), M * nh * 32, 0, st>>>(Vc, d, w);
-  if (int rc = check_launch("k_attn_accum")) return rc;
-  k_attn_merge<<<(M * nh * hd + 255) / 256, 256, 0, st>>>(d, w, out);
-  return check_launch("k_attn_merge");
+  return launch_attn(Kc, Vc, q, d, w, out, st);
+}
+
+// Engine-internal form for captured decode steps: the key ranges come from the position *dP on the
+// device (see AttnDesc::dynP); max_len bounds kmax - kmin + 1 over every position the capture will
+// see and sizes the score grid (blocks past kmax return at once).  ws must hold max_len keys.
+int g4::attn_splitkv_dev(const uint16_t* Kc, const uint16_t* Vc, const float* q, int M, int nh, int hd, const int* dP,
+                         int base_add, int q_add, int window, int max_len, int T, float* out, void* ws, size_t ws_bytes,
+                         cudaStream_t st) {
+  G4_REQUIRE(Kc && Vc && q && out && ws && dP && max_len >= 1, "attn_splitkv_dev: bad arguments");
+  int pos[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
+  for (int m = 0; m < M && m < 4; ++m) pos[m] = m;
+  AttnDesc d;
+  if (int rc = fill_desc(d, Kc, Vc, M, nh, hd, pos, lo, 0, M - 1, T)) return rc;
+  d.dynP = dP; d.base_add = base_add; d.q_add = q_add; d.window = window;
+  const size_t need = g4_attn_splitkv_ws_bytes(M, nh, hd, 0, max_len - 1, T);
+  if (ws_bytes < need) return set_error(G4_ERR_NOMEM, "attn_splitkv_dev: workspace %zu < %zu bytes", ws_bytes, need);
+  return launch_attn(Kc, Vc, q, d, static_cast<float*>(ws), out, st, max_len);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -252,7 +423,7 @@ extern "C" int g4_attn_splitkv_noalloc(const uint16_t* Kc, const uint16_t* Vc, c
                                        void* stream) {
   G4_REQUIRE(Kc && Vc && q && out, "g4_attn_splitkv_noalloc: null pointer");
   AttnDesc d;
-  if (int rc = fill_desc(d, M, nh, hd, pos, lo, kmin, kmax, T)) return rc;
+  if (int rc = fill_desc(d, Kc, Vc, M, nh, hd, pos, lo, kmin, kmax, T)) return rc;
   const int len = kmax - kmin + 1;
   if (hd > 256 || T > 8 || len > 8192 || attn_ws_floats(M, nh, hd, len, T) > kAttnNoAllocFloats)
     return set_error(G4_ERR_UNSUPPORTED,
@@ -262,12 +433,5 @@ extern "C" int g4_attn_splitkv_noalloc(const uint16_t* Kc, const uint16_t* Vc, c
   float* w = nullptr;
   if (int rc = attn_scratch_for_current_device(&w)) return rc;
   cudaStream_t st = as_stream(stream);
-  k_attn_scores<<<dim3((len + kScoreKeys - 1) / kScoreKeys, (M * nh + 15) / 16), 256, 0, st>>>(Kc, q, d, w);
-  if (int rc = check_launch("k_attn_scores")) return rc;
-  k_attn_stats<<<(T * M * nh * 32 + 255) / 256, 256, 0, st>>>(d, w);
-  if (int rc = check_launch("k_attn_stats")) return rc;
-  k_attn_accum<<<dim3(T, (hd + 31) / 32), M * nh * 32, 0, st>>>(Vc, d, w);
-  if (int rc = check_launch("k_attn_accum")) return rc;
-  k_attn_merge<<<(M * nh * hd + 255) / 256, 256, 0, st>>>(d, w, out);
-  return check_launch("k_attn_merge");
+  return launch_attn(Kc, Vc, q, d, w, out, st);
 }

@@ -40,6 +40,36 @@ struct DLayerW {
   bool global;
 };
 
+// Phase timer: CUDA events at op boundaries on the engine stream; the time between an event and the
+// next one is charged to the category recorded with the first (the reference's DECODE_STAGE /
+// STAGE_PROF breakdown, gemma4_engine.cpp:1672, 1691).
+enum Phase { PH_EMBED_NORM = 0, PH_LINEAR, PH_ATTN, PH_HEAD, PH_DRAFT, PH_COPY, PH_N };
+struct PhaseTimer {
+  bool on = false;
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> cat;
+  size_t used = 0;
+  double acc[PH_N] = {0, 0, 0, 0, 0, 0};
+  long long launches[PH_N] = {0, 0, 0, 0, 0, 0};
+  void mark(cudaStream_t st, int c) {
+    if (!on) return;
+    if (used == ev.size()) { cudaEvent_t e; cudaEventCreate(&e); ev.push_back(e); cat.push_back(0); }
+    cudaEventRecord(ev[used], st);
+    cat[used] = c;
+    ++used;
+  }
+  void flush() {  // after a stream sync
+    if (!on || used < 2) { used = 0; return; }
+    for (size_t i = 0; i + 1 < used; ++i) {
+      float ms = 0;
+      cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+      acc[cat[i]] += ms;
+      launches[cat[i]]++;
+    }
+    used = 0;
+  }
+};
+
 }  // namespace g4
 
 struct g4_engine {
@@ -82,6 +112,11 @@ struct g4_engine {
   int *cand, *dtok;
   bool i8_active = false;
   g4_engine_stats stats{};
+  g4::PhaseTimer prof;
+  // decode state between g4_engine_decode calls
+  std::vector<int> seq;  // prompt + committed tokens (prompt-lookup history)
+  int P = -1, conf = 0;
+  bool stopped = false;
 };
 
 using namespace g4;
@@ -314,17 +349,23 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf) {
   const ModelDims& d = e->d;
   const int H = d.H, QD = d.NQ * d.HD, ld = QD + 2 * d.HD;
   const float sqrtH = sqrtf((float)H);
+  PhaseTimer& pf = e->prof;
+  pf.mark(e->st, PH_EMBED_NORM);
   k_embed<<<M, 256, 0, e->st>>>(e->E, e->toks, H, sqrtH, e->x);
   for (int l = 0; l < d.NL; ++l) {
     const TLayer& t = e->L[l];
     const int ty = t.global ? 1 : 0;
+    pf.mark(e->st, PH_EMBED_NORM);
     k_rmsnorm<<<M, 256, 0, e->st>>>(e->x, t.in_ln, H, e->a, 0);
+    pf.mark(e->st, PH_LINEAR);
     RCK(lin(e, t.qkv, e->a, M, e->qkv));
     uint16_t* Kc = e->Kc + (size_t)l * e->cfg.ctx_max * d.HD;
     uint16_t* Vc = e->Vc + (size_t)l * e->cfg.ctx_max * d.HD;
+    pf.mark(e->st, PH_EMBED_NORM);
     k_qkv_post<<<dim3(M, d.NQ + 2), 256, 0, e->st>>>(e->qkv, ld, d.NQ, d.HD, pos0, t.qn, t.kn, e->rope[ty][0],
                                                      e->rope[ty][1], Kc, Vc);
     RCK(check_launch("k_qkv_post"));
+    pf.mark(e->st, PH_ATTN);
     if (M <= 4 && pos0 + M > e->cfg.att_par) {
       // split-KV (:1305-1327): rows' q are rows of the qkv buffer (stride ld); gather into att first
       int pos[4], lo[4], kmin = 1 << 30;
@@ -344,14 +385,21 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf) {
                                                                            t.global ? 0 : d.WINDOW, variant, e->att, QD);
       RCK(check_launch("k_attn_rows"));
     }
+    pf.mark(e->st, PH_LINEAR);
     RCK(lin(e, t.o, e->att, M, e->o));
+    pf.mark(e->st, PH_EMBED_NORM);
     k_post_attn<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_attn, t.pre_ff, e->mlp_in, H);
+    pf.mark(e->st, PH_LINEAR);
     RCK(lin(e, t.gu, e->mlp_in, M, e->gu));
+    pf.mark(e->st, PH_EMBED_NORM);
     k_act<<<gridfor((long long)M * d.I), 256, 0, e->st>>>(e->gu, d.I, M, e->act);
+    pf.mark(e->st, PH_LINEAR);
     RCK(lin(e, t.down, e->act, M, e->o));
+    pf.mark(e->st, PH_EMBED_NORM);
     k_post_ff<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_ff, 1.0f, H);
     RCK(check_launch("layer"));
   }
+  pf.mark(e->st, PH_HEAD);
   if (!want) return G4_OK;
   const int Mh = M - hf;
   k_rmsnorm<<<Mh, 256, 0, e->st>>>(e->x + (size_t)hf * H, e->fnorm, H, e->hbuf + (size_t)hf * H, 1);
@@ -371,6 +419,7 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf) {
                          64, e->st));
     }
   }
+  pf.mark(e->st, PH_COPY);
   return G4_OK;
 }
 
@@ -379,6 +428,8 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf) {
 static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos, int P, int* dtok_out) {
   const ModelDims& d = e->d;
   const int H = d.H, QD = d.NQ * d.HD;
+  (void)QD;
+  e->prof.mark(e->st, PH_DRAFT);
   k_draft_in<<<8, 256, 0, e->st>>>(e->E, dtok_in, h, H, sqrtf((float)H), e->dcomb);
   RCK(lin(e, e->dpre, e->dcomb, 1, e->dx, true));
   k_round<<<gridfor(H), 256, 0, e->st>>>(e->dx, H);
@@ -415,6 +466,7 @@ static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos,
   k_topk_cand<<<1, 1024, sizeof(float) * d.DCENT, e->st>>>(e->dscore, d.DCENT, d.DTOP, d.DPER, d.V, e->cand);
   k_cand_scores<<<(nc * 16 + 255) / 256, 256, 0, e->st>>>(e->E, e->cand, nc, e->dh, H, e->cscore);
   k_cand_best<<<1, 1024, 0, e->st>>>(e->cscore, e->cand, nc, dtok_out);
+  e->prof.mark(e->st, PH_COPY);
   return check_launch("draft_step");
 }
 
@@ -446,17 +498,14 @@ extern "C" int g4_engine_draft(g4_engine* e, int32_t tok, const float* h, int po
 
 static bool is_stop(int t) { return t == 106 || t == 1; }
 
-// run_req (:1582-1680) in chain mode: prefill in blocks, then rounds of (prompt lookup or k MTP
-// drafts) -> one verify forward -> greedy acceptance.
-extern "C" int g4_engine_generate(g4_engine* e, const int32_t* prompt, int n, int n_new, int32_t* out, int* n_out,
-                                  g4_engine_stats* stats) {
-  G4_REQUIRE(e && prompt && out && n_out && n >= 1 && n_new >= 1 && n + n_new + 4 <= e->cfg.ctx_max,
-             "g4_engine_generate: bad arguments (n=%d n_new=%d ctx_max=%d)", n, n_new, e->cfg.ctx_max);
-  const ModelDims& d = e->d;
-  const int H = d.H;
-  g4_engine_stats s{};
+// run_req (:1582-1680), split in two: prefill in blocks (int8 per ENGINE_PREFILL_INT8, :1595), then
+// resumable decode rounds (chain mode): prompt lookup or k MTP drafts -> one verify forward ->
+// greedy acceptance.  The committed sequence stays on the host (it is the prompt-lookup history).
+extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int32_t* first_token) {
+  G4_REQUIRE(e && prompt && n >= 1 && n + 8 <= e->cfg.ctx_max, "g4_engine_prefill: bad arguments (n=%d ctx_max=%d)", n,
+             e->cfg.ctx_max);
+  const int H = e->d.H;
   auto t0 = std::chrono::steady_clock::now();
-  // prefill (int8 per ENGINE_PREFILL_INT8, :1595)
   e->i8_active = e->cfg.prefill_int8 != 0;
   int done = 0, last_M = 0;
   while (done < n) {
@@ -469,26 +518,39 @@ extern "C" int g4_engine_generate(g4_engine* e, const int32_t* prompt, int n, in
   }
   int first = 0;
   ECK(cudaMemcpyAsync(&first, e->G + (last_M - 1), sizeof(int), cudaMemcpyDeviceToHost, e->st));
-  ECK(cudaStreamSynchronize(e->st));
-  auto t1 = std::chrono::steady_clock::now();
-  s.prefill_ms = std::chrono::duration<double, std::milli>(t1 - t0).count();
-  s.prefill_tokens = n;
-  // decode (ENGINE_DECODE_INT8 on requires PREFILL_INT8, :1600)
-  e->i8_active = e->cfg.decode_int8 && e->cfg.prefill_int8;
-  std::vector<int> gen{first};
-  std::vector<int> seq(prompt, prompt + n);
-  seq.push_back(first);
-  // hprev (the final-normed hidden of the last committed row) stays on the device; hbuf is
-  // overwritten by every forward, so it is copied out
   ECK(cudaMemcpyAsync(e->hprev, e->hbuf + (size_t)(last_M - 1) * H, sizeof(float) * H, cudaMemcpyDeviceToDevice, e->st));
-  int P = n - 1, conf = first;
-  bool stopped = is_stop(first);
+  ECK(cudaStreamSynchronize(e->st));
+  e->seq.assign(prompt, prompt + n);
+  e->seq.push_back(first);
+  e->P = n - 1;
+  e->conf = first;
+  e->stopped = is_stop(first);
+  e->stats = g4_engine_stats{};
+  e->stats.prefill_tokens = n;
+  e->stats.prefill_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  if (first_token) *first_token = first;
+  return G4_OK;
+}
+
+extern "C" int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, int32_t* out, int* n_out,
+                                g4_engine_stats* stats) {
+  G4_REQUIRE(e && n_out && max_rounds >= 0 && max_tokens >= 0 && !e->seq.empty(), "g4_engine_decode: call g4_engine_prefill first");
+  const int H = e->d.H;
+  auto t0 = std::chrono::steady_clock::now();
+  cudaEvent_t ev0, ev1;
+  ECK(cudaEventCreate(&ev0));
+  ECK(cudaEventCreate(&ev1));
+  ECK(cudaEventRecord(ev0, e->st));
+  e->i8_active = e->cfg.decode_int8 && e->cfg.prefill_int8;  // (:1600)
+  int produced = 0, rounds = 0;
   int block[8];
-  std::vector<int> G(8);
-  while ((int)gen.size() < n_new && !stopped) {
-    block[0] = conf;
+  int G[8];
+  while (rounds < max_rounds && produced < max_tokens && !e->stopped) {
+    if (e->P + 1 + 4 >= e->cfg.ctx_max) return set_error(G4_ERR_UNSUPPORTED, "g4_engine_decode: context full (%d)", e->cfg.ctx_max);
+    block[0] = e->conf;
     int nd = 0;
     bool used_ng = false;
+    const std::vector<int>& seq = e->seq;
     if (e->cfg.ngram > 0) {  // prompt lookup (:1624-1628)
       const int Ls = (int)seq.size(), NG = e->cfg.ngram;
       if (Ls > NG)
@@ -501,14 +563,14 @@ extern "C" int g4_engine_generate(g4_engine* e, const int32_t* prompt, int n, in
             break;
           }
         }
-      if (nd > 0) { used_ng = true; s.ngram_rounds++; }
+      if (nd > 0) { used_ng = true; e->stats.ngram_rounds++; }
     }
     if (!used_ng && e->cfg.drafter && e->cfg.k_draft > 0) {
       // MTP drafts: token conf with hidden hprev, then each draft with the drafter's next hidden
-      ECK(cudaMemcpyAsync(e->dtok, &conf, sizeof(int), cudaMemcpyHostToDevice, e->st));
+      ECK(cudaMemcpyAsync(e->dtok, &e->conf, sizeof(int), cudaMemcpyHostToDevice, e->st));
       const float* hcur = e->hprev;
       for (int j = 0; j < e->cfg.k_draft; ++j) {
-        RCK(draft_step(e, e->dtok + (j & 1), hcur, P + 1 + j, P, e->dtok + ((j + 1) & 1)));
+        RCK(draft_step(e, e->dtok + (j & 1), hcur, e->P + 1 + j, e->P, e->dtok + ((j + 1) & 1)));
         ECK(cudaMemcpyAsync(e->toks + 1 + j, e->dtok + ((j + 1) & 1), sizeof(int), cudaMemcpyDeviceToDevice, e->st));
         ECK(cudaMemcpyAsync(e->hnext, e->bcur, sizeof(float) * H, cudaMemcpyDeviceToDevice, e->st));
         hcur = e->hnext;
@@ -516,35 +578,73 @@ extern "C" int g4_engine_generate(g4_engine* e, const int32_t* prompt, int n, in
       int dr[3];
       ECK(cudaMemcpyAsync(dr, e->toks + 1, sizeof(int) * e->cfg.k_draft, cudaMemcpyDeviceToHost, e->st));
       ECK(cudaStreamSynchronize(e->st));
+      e->prof.flush();
       for (int j = 0; j < e->cfg.k_draft; ++j) block[1 + nd++] = dr[j];
-      s.drafted += nd;
+      e->stats.drafted += nd;
     }
     const int M = nd + 1;
     ECK(cudaMemcpyAsync(e->toks, block, sizeof(int) * M, cudaMemcpyHostToDevice, e->st));
-    RCK(forward(e, M, P + 1, true, 0));
-    ECK(cudaMemcpyAsync(G.data(), e->G, sizeof(int) * M, cudaMemcpyDeviceToHost, e->st));
+    RCK(forward(e, M, e->P + 1, true, 0));
+    ECK(cudaMemcpyAsync(G, e->G, sizeof(int) * M, cudaMemcpyDeviceToHost, e->st));
     ECK(cudaStreamSynchronize(e->st));
-    s.rounds++;
+    e->prof.flush();
+    e->stats.rounds++;
+    ++rounds;
     int nacc = 0;
     while (nacc < nd && block[nacc + 1] == G[nacc]) ++nacc;
-    s.accepted += nacc;
+    e->stats.accepted += nacc;
     for (int i = 0; i <= nacc; ++i) {
-      gen.push_back(G[i]);
-      seq.push_back(G[i]);
-      if (is_stop(G[i])) { stopped = true; break; }
+      e->seq.push_back(G[i]);
+      if (out && produced < max_tokens) out[produced] = G[i];
+      ++produced;
+      if (is_stop(G[i])) { e->stopped = true; break; }
     }
-    conf = G[nacc];
+    e->conf = G[nacc];
     ECK(cudaMemcpyAsync(e->hprev, e->hbuf + (size_t)nacc * H, sizeof(float) * H, cudaMemcpyDeviceToDevice, e->st));
-    P += nacc + 1;
+    e->P += nacc + 1;
   }
-  auto t2 = std::chrono::steady_clock::now();
-  s.decode_ms = std::chrono::duration<double, std::milli>(t2 - t1).count();
-  if ((int)gen.size() > n_new) gen.resize(n_new);
-  for (size_t i = 0; i < gen.size(); ++i)
-    if (is_stop(gen[i])) { gen.resize(i + 1); break; }
-  for (size_t i = 0; i < gen.size(); ++i) out[i] = gen[i];
-  *n_out = (int)gen.size();
-  s.decode_tokens = (int)gen.size() - 1;
-  if (stats) *stats = s;
+  ECK(cudaEventRecord(ev1, e->st));
+  ECK(cudaEventSynchronize(ev1));
+  float gms = 0;
+  cudaEventElapsedTime(&gms, ev0, ev1);
+  cudaEventDestroy(ev0);
+  cudaEventDestroy(ev1);
+  e->stats.decode_gpu_ms += gms;
+  e->stats.decode_tokens += std::min(produced, max_tokens);
+  e->stats.decode_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  *n_out = std::min(produced, max_tokens);
+  if (stats) *stats = e->stats;
+  return G4_OK;
+}
+
+extern "C" int g4_engine_generate(g4_engine* e, const int32_t* prompt, int n, int n_new, int32_t* out, int* n_out,
+                                  g4_engine_stats* stats) {
+  G4_REQUIRE(e && prompt && out && n_out && n >= 1 && n_new >= 1 && n + n_new + 8 <= e->cfg.ctx_max,
+             "g4_engine_generate: bad arguments (n=%d n_new=%d ctx_max=%d)", n, n_new, e->cfg.ctx_max);
+  int first = 0;
+  RCK(g4_engine_prefill(e, prompt, n, &first));
+  out[0] = first;
+  int got = 0;
+  if (n_new > 1 && !e->stopped) RCK(g4_engine_decode(e, 1 << 30, n_new - 1, out + 1, &got, nullptr));
+  int total = 1 + got;
+  for (int i = 0; i < total; ++i)
+    if (is_stop(out[i])) { total = i + 1; break; }
+  *n_out = total;
+  if (stats) *stats = e->stats;
+  return G4_OK;
+}
+
+// Phase times (ms) accumulated while profiling is on: [0] embed/norms/rope/residual, [1] linears,
+// [2] attention, [3] head, [4] drafter, [5] copies between phases; enable != 0 turns it on and
+// clears the totals, enable == 0 turns it off.  out may be NULL.
+extern "C" int g4_engine_phase_times(g4_engine* e, int enable, double* out_ms, long long* out_marks) {
+  G4_REQUIRE(e, "g4_engine_phase_times: null engine");
+  if (out_ms) for (int i = 0; i < PH_N; ++i) out_ms[i] = e->prof.acc[i];
+  if (out_marks) for (int i = 0; i < PH_N; ++i) out_marks[i] = e->prof.launches[i];
+  if (enable >= 0) {
+    e->prof.on = enable != 0;
+    for (int i = 0; i < PH_N; ++i) { e->prof.acc[i] = 0; e->prof.launches[i] = 0; }
+    e->prof.used = 0;
+  }
   return G4_OK;
 }

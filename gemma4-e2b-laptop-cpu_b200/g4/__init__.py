@@ -42,6 +42,9 @@ SIGNATURES = {
     "g4_engine_forward": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "g4_engine_draft": (_I, [_P, _I, _P, _I, _I, _P, _P]),
     "g4_engine_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+    "g4_engine_prefill": (_I, [_P, _P, _I, _P]),
+    "g4_engine_decode": (_I, [_P, _I, _I, _P, _P, _P]),
+    "g4_engine_phase_times": (_I, [_P, _I, _P, _P]),
     "g4_attn_splitkv_ws_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "g4_attn_splitkv": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
     "g4_attn_splitkv_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
@@ -260,7 +263,8 @@ class EngineConfig(ctypes.Structure):
 class EngineStats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in ("rounds", "ngram_rounds", "drafted", "accepted", "prefill_tokens",
                                             "decode_tokens")] + [("prefill_ms", ctypes.c_double),
-                                                                 ("decode_ms", ctypes.c_double)]
+                                                                 ("decode_ms", ctypes.c_double),
+                                                                 ("decode_gpu_ms", ctypes.c_double)]
 
     def as_dict(self):
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -305,6 +309,31 @@ class Engine:
         check(lib().g4_engine_draft(self.h, int(tok), h.ctypes.data_as(_P), pos, P, out.ctypes.data_as(_P),
                                     hn.ctypes.data_as(_P)), "g4_engine_draft")
         return int(out[0]), hn
+
+    def prefill(self, prompt):
+        import numpy as np
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        first = ctypes.c_int(0)
+        check(lib().g4_engine_prefill(self.h, prompt.ctypes.data_as(_P), prompt.size, ctypes.byref(first)),
+              "g4_engine_prefill")
+        return first.value
+
+    def decode(self, max_rounds, max_tokens, out=None):
+        import numpy as np
+        n = ctypes.c_int(0)
+        st = EngineStats()
+        optr = out.ctypes.data_as(_P) if out is not None else None
+        check(lib().g4_engine_decode(self.h, max_rounds, max_tokens, optr, ctypes.byref(n), ctypes.byref(st)),
+              "g4_engine_decode")
+        return n.value, st.as_dict()
+
+    PHASES = ("embed_norm_rope", "linear", "attention", "head", "drafter", "copies")
+
+    def phase_times(self, enable=-1):
+        ms = (ctypes.c_double * 6)()
+        marks = (ctypes.c_longlong * 6)()
+        check(lib().g4_engine_phase_times(self.h, enable, ms, marks), "g4_engine_phase_times")
+        return {n: (ms[i], marks[i]) for i, n in enumerate(self.PHASES)}
 
     def generate(self, prompt, n_new):
         import numpy as np

@@ -156,7 +156,8 @@ typedef struct {
 } g4_engine_config;
 typedef struct {
   int rounds, ngram_rounds, drafted, accepted, prefill_tokens, decode_tokens;
-  double prefill_ms, decode_ms;
+  double prefill_ms, decode_ms; /* host wall clock */
+  double decode_gpu_ms;         /* CUDA events on the engine stream around the decode calls */
 } g4_engine_stats;
 
 int g4_engine_default_config(g4_engine_config* cfg);
@@ -170,6 +171,17 @@ int g4_engine_forward(g4_engine* e, const int32_t* toks, int M, int pos0, int wa
                       float* hbuf);
 /* One MTP draft step: token, hidden h (host [hidden]), query position, last target position P. */
 int g4_engine_draft(g4_engine* e, int32_t tok, const float* h, int pos, int P, int32_t* out_tok, float* h_next);
+/* Prefill a prompt (host [n]) in blocks of prefill_block and reset the decode state; *first_token =
+ * the greedy token after the prompt. */
+int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int32_t* first_token);
+/* Continue speculative greedy decode for up to max_rounds rounds or max_tokens committed tokens
+ * (whichever comes first) or a stop token; out host [max_tokens] (may be NULL), *n_out = tokens
+ * committed by this call; stats (may be NULL) accumulate since the prefill. */
+int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, int32_t* out, int* n_out, g4_engine_stats* stats);
+/* Per-phase device time (CUDA events on the engine stream) while profiling is on: out_ms[6] =
+ * embed+norms+RoPE+residual, linears, attention, head, drafter, copies; out_marks[6] = intervals.
+ * enable = 1 starts (and clears), 0 stops, -1 only reads.  Outputs may be NULL. */
+int g4_engine_phase_times(g4_engine* e, int enable, double* out_ms, long long* out_marks);
 /* run_req: prefill the prompt, then speculative greedy decode until n_new tokens (the first from
  * the prefill) or a stop token (1 or 106).  out host [n_new]. */
 int g4_engine_generate(g4_engine* e, const int32_t* prompt, int n, int n_new, int32_t* out, int* n_out,

@@ -456,9 +456,27 @@ int or_e2e_draft(void* mp, int32_t tok, const float* h, int pos, int P, int32_t*
 
 static int is_stop(int t) { return t == 106 || t == 1; }
 
+/* ENGINE_FAKE_CTX (gemma4_engine.cpp:1249-1250): fill positions [0, n) of every layer's K and V with
+ * the reference's seeded LCG values, so that decode can be timed at a long context without a long
+ * prefill; the prompt then starts at position n. */
+static int g_fake_n = 0;
+void or_e2e_fake_ctx(void* mp, int n) {
+  Model* m = (Model*)mp;
+  uint32_t rs = 12345;
+  for (int l = 0; l < m->NL; ++l)
+    for (size_t i = 0; i < (size_t)n * m->HD; ++i) {
+      rs = rs * 1664525u + 1013904223u;
+      m->Kc[(size_t)l * m->ctx_max * m->HD + i] = or_f2bf(((int)(rs >> 9) % 2001 - 1000) / 700.0f);
+      rs = rs * 1664525u + 1013904223u;
+      m->Vc[(size_t)l * m->ctx_max * m->HD + i] = or_f2bf(((int)(rs >> 9) % 2001 - 1000) / 700.0f);
+    }
+  g_fake_n = n;
+}
+
 /* run_req in chain mode (:1582-1663). stats[0..5] = rounds, ngram_rounds, drafted, accepted. */
 int or_e2e_generate(void* mp, const int32_t* prompt, int n, int n_new, int32_t* out, int* n_out, int* stats) {
   Model* m = (Model*)mp;
+  const int FN = g_fake_n;
   const int H = m->H;
   int* G = (int*)malloc(sizeof(int) * 64);
   float* hbuf = (float*)malloc(sizeof(float) * 64 * H);
@@ -467,7 +485,7 @@ int or_e2e_generate(void* mp, const int32_t* prompt, int n, int n_new, int32_t* 
   while (done < n) {
     const int M = m->prefill_block < n - done ? m->prefill_block : n - done;
     const int last = done + M == n;
-    forward(m, prompt + done, M, done, last, last ? M - 1 : 0, G, hbuf);
+    forward(m, prompt + done, M, FN + done, last, last ? M - 1 : 0, G, hbuf);
     done += M; lastM = M;
   }
   m->i8 = m->decode_int8 && m->prefill_int8;
@@ -481,7 +499,7 @@ int or_e2e_generate(void* mp, const int32_t* prompt, int n, int n_new, int32_t* 
   float* hcur = (float*)malloc(sizeof(float) * H);
   float* hnext = (float*)malloc(sizeof(float) * H);
   memcpy(hprev, hbuf + (size_t)(lastM - 1) * H, sizeof(float) * H);
-  int P = n - 1, conf = gen[0], stopped = is_stop(conf);
+  int P = FN + n - 1, conf = gen[0], stopped = is_stop(conf);
   int rounds = 0, ngr = 0, drafted = 0, accepted = 0;
   while (ng < n_new && !stopped) {
     int block[8], nd = 0, used_ng = 0;

@@ -52,6 +52,7 @@ _SIGS_ORACLE = {
     "or_e2e_draft": (_I, [_P, _I, _P, _I, _I, _P, _P]),
     "or_e2e_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "or_e2e_gen_bytes": (None, [ctypes.c_ulonglong, ctypes.c_ulonglong, ctypes.c_longlong, _P]),
+    "or_e2e_fake_ctx": (None, [_P, _I]),
 }
 
 _SIGS_REF = {
@@ -268,6 +269,9 @@ class OracleModel:
         hn = np.zeros(self.cfg.hidden, np.float32)
         oracle().or_e2e_draft(self.h, int(tok), ptr(np.ascontiguousarray(h, np.float32)), pos, P, ptr(out), ptr(hn))
         return int(out[0]), hn
+
+    def fake_ctx(self, n):
+        oracle().or_e2e_fake_ctx(self.h, n)
 
     def generate(self, prompt, n_new):
         prompt = np.ascontiguousarray(prompt, np.int32)

@@ -75,3 +75,26 @@ def test_attention_workspace_too_small():
     kv = torch.zeros((16, 256), dtype=torch.int16, device="cuda")
     with pytest.raises(g4.G4Error):
         g4.attn_splitkv(kv, kv, q, [15], [0], ws=torch.zeros(4, device="cuda"))
+
+
+@pytest.mark.parametrize("ctx,M,nh,T", [(9000, 2, 8, 8), (3000, 4, 3, 2), (777, 1, 5, 7)])
+def test_attention_long_chunks_and_odd_head_counts(ctx, M, nh, T):
+    """Chunks longer than the statistics kernel's register tile (9,000 keys in 8 chunks; 3,000 in
+    2), head counts that leave (row, head) groups partly empty, and an odd chunk count."""
+    rng = np.random.default_rng(ctx + nh)
+    hd = 256
+    Kc = bf16_bits(rng.standard_normal((ctx, hd), dtype=np.float32))
+    Vc = bf16_bits(rng.standard_normal((ctx, hd), dtype=np.float32))
+    q = (rng.standard_normal((M, nh, hd), dtype=np.float32) * np.float32(0.0625)).astype(np.float32)
+    pos = np.arange(ctx - M, ctx, dtype=np.int32)
+    lo = np.zeros(M, np.int32)
+    out = g4.attn_splitkv(dev(Kc.view(np.int16)), dev(Vc.view(np.int16)), dev(q), pos, lo, T=T).cpu().numpy()
+    check(out, or_attn(Kc, Vc, q, pos, lo, T))
+    assert g4.device_status() == 0
+
+
+def test_attention_rejects_unaligned_cache():
+    kv = torch.zeros((17, 256), dtype=torch.int16, device="cuda")
+    q = torch.zeros((1, 8, 256), device="cuda")
+    with pytest.raises(g4.G4Error):
+        g4.attn_splitkv(kv.view(-1)[1:].view(-1)[: 16 * 256].view(16, 256), kv, q, [15], [0])
