@@ -100,8 +100,10 @@ struct g4_engine {
   int8_t* xq;
   float* xsx;
   int32_t* xsum;
-  int* toks;
+  int* ctl;   // device: [0] = P (last committed target position), [8, 8 + MMAX) = the rows' tokens
+  int* toks;  // = ctl + 8
   int* G;
+  int* hio = nullptr;  // pinned host mirror: ctl [8 + MMAX], then G [MMAX], then drafts [8]
   void* attn_ws = nullptr;
   size_t attn_ws_bytes = 0;
   void* head_ws = nullptr;
@@ -113,6 +115,12 @@ struct g4_engine {
   bool i8_active = false;
   g4_engine_stats stats{};
   g4::PhaseTimer prof;
+  // CUDA graphs of a decode round: the verify pass for M = 1..4 rows and the chain of k drafts;
+  // positions are read from ctl[0] on the device, so one capture serves every round
+  cudaGraphExec_t gverify[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+  cudaGraphExec_t gdraft = nullptr;
+  cudaEvent_t tev[4] = {nullptr, nullptr, nullptr, nullptr};  // draft start/end, verify start/end
+  int fake_n = 0;
   // decode state between g4_engine_decode calls
   std::vector<int> seq;  // prompt + committed tokens (prompt-lookup history)
   int P = -1, conf = 0;
@@ -127,6 +135,7 @@ extern "C" int g4_engine_default_config(g4_engine_config* c) {
   c->hidden = 2048; c->n_layers = 30; c->mlp = 8192; c->vocab = 262144; c->ctx_max = 8192;
   c->prefill_block = 32; c->k_draft = 3; c->ngram = 2; c->ngram_len = 3; c->prefill_int8 = 1; c->decode_int8 = 1;
   c->head_screen = 1; c->screen_lim = 30000; c->attn_chunks = 8; c->att_par = 192; c->drafter = 1; c->seed = 20261201ull;
+  c->graphs = 1;
   return G4_OK;
 }
 
@@ -284,7 +293,14 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
   if (!rc) rc = ealloc_t(e, &e->xq, (size_t)MM * kmax);
   if (!rc) rc = ealloc_t(e, &e->xsx, (size_t)MM * kmax / 32);
   if (!rc) rc = ealloc_t(e, &e->xsum, (size_t)MM * kmax / 32);
-  if (!rc) rc = ealloc_t(e, &e->toks, (size_t)MM);
+  if (!rc) rc = ealloc_t(e, &e->ctl, (size_t)MM + 8);
+  if (!rc) {
+    e->toks = e->ctl + 8;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&e->hio), sizeof(int) * (2 * (size_t)MM + 16), cudaHostAllocDefault) != cudaSuccess)
+      rc = set_error(G4_ERR_CUDA, "g4_engine_create: pinned host buffer");
+  }
+  for (int i = 0; i < 4 && !rc; ++i)
+    if (cudaEventCreate(&e->tev[i]) != cudaSuccess) rc = set_error(G4_ERR_CUDA, "g4_engine_create: events");
   if (!rc) rc = ealloc_t(e, &e->G, (size_t)MM);
   e->attn_ws_bytes = g4_attn_splitkv_ws_bytes(4, d.NQ, d.HD, 0, c.ctx_max - 1, c.attn_chunks);
   if (!rc) rc = ealloc(e, &e->attn_ws, e->attn_ws_bytes);
@@ -315,6 +331,12 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
 extern "C" void g4_engine_destroy(g4_engine* e) {
   if (!e) return;
   if (e->st) cudaStreamSynchronize(e->st);
+  for (auto& g : e->gverify)
+    if (g) cudaGraphExecDestroy(g);
+  if (e->gdraft) cudaGraphExecDestroy(e->gdraft);
+  for (auto& ev : e->tev)
+    if (ev) cudaEventDestroy(ev);
+  if (e->hio) cudaFreeHost(e->hio);
   for (void* p : e->allocs) cudaFree(p);
   if (e->st) cudaStreamDestroy(e->st);
   delete e;
@@ -344,8 +366,11 @@ static int lin(g4_engine* e, const Lin& w, const float* X, int M, float* Y, bool
 }
 
 // One target forward over M tokens at positions pos0.. (fwd, :1256-1502).  toks are device ints;
-// when want, rows hf.. get the final-normed hidden in hbuf and the greedy next token in G.
-static int forward(g4_engine* e, int M, int pos0, bool want, int hf) {
+// when want, rows hf.. get the final-normed hidden in hbuf and the greedy next token in G.  With
+// dyn the positions are ctl[0] + 1.. read on the device (pos0 unused; M <= 4 and the split-KV path,
+// i.e. position + M > att_par, which the caller guarantees), so that the launches can be captured
+// once and replayed at every position.
+static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = false) {
   const ModelDims& d = e->d;
   const int H = d.H, QD = d.NQ * d.HD, ld = QD + 2 * d.HD;
   const float sqrtH = sqrtf((float)H);
@@ -362,11 +387,17 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf) {
     uint16_t* Kc = e->Kc + (size_t)l * e->cfg.ctx_max * d.HD;
     uint16_t* Vc = e->Vc + (size_t)l * e->cfg.ctx_max * d.HD;
     pf.mark(e->st, PH_EMBED_NORM);
-    k_qkv_post<<<dim3(M, d.NQ + 2), 256, 0, e->st>>>(e->qkv, ld, d.NQ, d.HD, pos0, t.qn, t.kn, e->rope[ty][0],
-                                                     e->rope[ty][1], Kc, Vc);
+    k_qkv_post<<<dim3(M, d.NQ + 2), 256, 0, e->st>>>(e->qkv, ld, d.NQ, d.HD, dyn ? 1 : pos0, dyn ? e->ctl : nullptr,
+                                                     t.qn, t.kn, e->rope[ty][0], e->rope[ty][1], Kc, Vc);
     RCK(check_launch("k_qkv_post"));
     pf.mark(e->st, PH_ATTN);
-    if (M <= 4 && pos0 + M > e->cfg.att_par) {
+    if (dyn) {
+      ECK(cudaMemcpy2DAsync(e->qs, sizeof(float) * QD, e->qkv, sizeof(float) * ld, sizeof(float) * QD, M,
+                            cudaMemcpyDeviceToDevice, e->st));
+      const int max_len = t.global ? e->cfg.ctx_max : std::min(e->cfg.ctx_max, d.WINDOW + 4);
+      RCK(attn_splitkv_dev(Kc, Vc, e->qs, M, d.NQ, d.HD, e->ctl, 1, 1, t.global ? 0 : d.WINDOW, max_len,
+                           e->cfg.attn_chunks, e->att, e->attn_ws, e->attn_ws_bytes, e->st));
+    } else if (M <= 4 && pos0 + M > e->cfg.att_par) {
       // split-KV (:1305-1327): rows' q are rows of the qkv buffer (stride ld); gather into att first
       int pos[4], lo[4], kmin = 1 << 30;
       for (int m = 0; m < M; ++m) {
@@ -425,7 +456,9 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf) {
 
 // One draft step (draft_step, :1534-1563): token *dtok_in, hidden h (device), query position pos,
 // last valid target position P; writes the drafted token to *dtok_out and the next hidden to bcur.
-static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos, int P, int* dtok_out) {
+// With dyn, P is ctl[0] on the device and pos = P + 1 + j (pos and P unused).
+static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos, int P, int* dtok_out, bool dyn = false,
+                      int j = 0) {
   const ModelDims& d = e->d;
   const int H = d.H, QD = d.NQ * d.HD;
   (void)QD;
@@ -443,11 +476,20 @@ static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos,
     if (tl < 0) return set_error(G4_ERR_UNSUPPORTED, "draft_step: the target has no %s layer", t.global ? "global" : "sliding");
     k_rmsnorm<<<1, 256, 0, e->st>>>(e->dx, t.in_ln, H, e->da, 0);
     RCK(lin(e, t.q, e->da, 1, e->dq, true));
-    k_q_post<<<d.NQ, 256, 0, e->st>>>(e->dq, d.HD, pos, t.qn, e->rope[ty][0], e->rope[ty][1]);
-    const int lo = t.global ? 0 : std::max(0, pos - (d.WINDOW - 1));
-    const int pp = P;
-    RCK(g4_attn_splitkv(e->Kc + (size_t)tl * e->cfg.ctx_max * d.HD, e->Vc + (size_t)tl * e->cfg.ctx_max * d.HD, e->dq,
-                        &pp, &lo, 1, d.NQ, d.HD, lo, P, e->cfg.attn_chunks, e->dopt, e->attn_ws, e->attn_ws_bytes, e->st));
+    k_q_post<<<d.NQ, 256, 0, e->st>>>(e->dq, d.HD, dyn ? 1 + j : pos, dyn ? e->ctl : nullptr, t.qn, e->rope[ty][0],
+                                      e->rope[ty][1]);
+    const uint16_t* Kt = e->Kc + (size_t)tl * e->cfg.ctx_max * d.HD;
+    const uint16_t* Vt = e->Vc + (size_t)tl * e->cfg.ctx_max * d.HD;
+    if (dyn) {
+      const int max_len = t.global ? e->cfg.ctx_max : std::min(e->cfg.ctx_max, d.WINDOW);
+      RCK(attn_splitkv_dev(Kt, Vt, e->dq, 1, d.NQ, d.HD, e->ctl, 0, 1 + j, t.global ? 0 : d.WINDOW, max_len,
+                           e->cfg.attn_chunks, e->dopt, e->attn_ws, e->attn_ws_bytes, e->st));
+    } else {
+      const int lo = t.global ? 0 : std::max(0, pos - (d.WINDOW - 1));
+      const int pp = P;
+      RCK(g4_attn_splitkv(Kt, Vt, e->dq, &pp, &lo, 1, d.NQ, d.HD, lo, P, e->cfg.attn_chunks, e->dopt, e->attn_ws,
+                          e->attn_ws_bytes, e->st));
+    }
     RCK(lin(e, t.o, e->dopt, 1, e->da, true));
     k_resid_norm<<<1, 256, 0, e->st>>>(e->da, e->dx, t.post_attn, H);
     k_rmsnorm<<<1, 256, 0, e->st>>>(e->dx, t.pre_ff, H, e->da, 1);
@@ -498,13 +540,42 @@ extern "C" int g4_engine_draft(g4_engine* e, int32_t tok, const float* h, int po
 
 static bool is_stop(int t) { return t == 106 || t == 1; }
 
+extern "C" int g4_engine_fake_ctx(g4_engine* e, int n) {
+  G4_REQUIRE(e && n >= 0 && n + 16 <= e->cfg.ctx_max, "g4_engine_fake_ctx: bad arguments (n=%d ctx_max=%d)", n,
+             e ? e->cfg.ctx_max : 0);
+  const int HD = e->d.HD;
+  std::vector<uint16_t> kb((size_t)n * HD), vb((size_t)n * HD);
+  uint32_t rs = 12345;
+  auto rnd = [&]() {
+    rs = rs * 1664525u + 1013904223u;
+    const float f = ((int)(rs >> 9) % 2001 - 1000) / 700.0f;
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    u += 0x7fffu + ((u >> 16) & 1u);  // round to nearest even (finite values)
+    return (uint16_t)(u >> 16);
+  };
+  ECK(cudaStreamSynchronize(e->st));
+  for (int l = 0; l < e->d.NL; ++l) {
+    for (size_t i = 0; i < (size_t)n * HD; ++i) {
+      kb[i] = rnd();
+      vb[i] = rnd();
+    }
+    const size_t off = (size_t)l * e->cfg.ctx_max * HD;
+    ECK(cudaMemcpy(e->Kc + off, kb.data(), kb.size() * 2, cudaMemcpyHostToDevice));
+    ECK(cudaMemcpy(e->Vc + off, vb.data(), vb.size() * 2, cudaMemcpyHostToDevice));
+  }
+  e->fake_n = n;
+  return G4_OK;
+}
+
 // run_req (:1582-1680), split in two: prefill in blocks (int8 per ENGINE_PREFILL_INT8, :1595), then
 // resumable decode rounds (chain mode): prompt lookup or k MTP drafts -> one verify forward ->
 // greedy acceptance.  The committed sequence stays on the host (it is the prompt-lookup history).
 extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int32_t* first_token) {
-  G4_REQUIRE(e && prompt && n >= 1 && n + 8 <= e->cfg.ctx_max, "g4_engine_prefill: bad arguments (n=%d ctx_max=%d)", n,
-             e->cfg.ctx_max);
-  const int H = e->d.H;
+  G4_REQUIRE(e && prompt && n >= 1 && e->fake_n + n + 8 <= e->cfg.ctx_max,
+             "g4_engine_prefill: bad arguments (n=%d fake context %d ctx_max=%d)", n, e ? e->fake_n : 0,
+             e ? e->cfg.ctx_max : 0);
+  const int H = e->d.H, FN = e->fake_n;
   auto t0 = std::chrono::steady_clock::now();
   e->i8_active = e->cfg.prefill_int8 != 0;
   int done = 0, last_M = 0;
@@ -512,7 +583,7 @@ extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int
     const int M = std::min(e->cfg.prefill_block, n - done);
     const bool last = done + M == n;
     ECK(cudaMemcpyAsync(e->toks, prompt + done, sizeof(int) * M, cudaMemcpyHostToDevice, e->st));
-    RCK(forward(e, M, done, last, last ? M - 1 : 0));
+    RCK(forward(e, M, FN + done, last, last ? M - 1 : 0));
     done += M;
     last_M = M;
   }
@@ -520,9 +591,10 @@ extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int
   ECK(cudaMemcpyAsync(&first, e->G + (last_M - 1), sizeof(int), cudaMemcpyDeviceToHost, e->st));
   ECK(cudaMemcpyAsync(e->hprev, e->hbuf + (size_t)(last_M - 1) * H, sizeof(float) * H, cudaMemcpyDeviceToDevice, e->st));
   ECK(cudaStreamSynchronize(e->st));
+  e->prof.flush();
   e->seq.assign(prompt, prompt + n);
   e->seq.push_back(first);
-  e->P = n - 1;
+  e->P = FN + n - 1;
   e->conf = first;
   e->stopped = is_stop(first);
   e->stats = g4_engine_stats{};
@@ -532,21 +604,56 @@ extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int
   return G4_OK;
 }
 
+// Record the launches of body() on the engine stream into an executable graph.
+template <class F>
+static int capture(g4_engine* e, cudaGraphExec_t* out, F body) {
+  ECK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+  const int rc = body();
+  cudaGraph_t g = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(e->st, &g);
+  if (rc != G4_OK) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ce != cudaSuccess) return set_error(G4_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+  const cudaError_t ie = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) return set_error(G4_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ie));
+  return G4_OK;
+}
+
+// The k MTP drafts of a round from ctl (tokens[0] = the confirmed token, ctl[0] = P) and hprev:
+// draft j reads the drafter hidden of draft j-1 and writes its token to tokens[1 + j].
+static int draft_chain(g4_engine* e, bool dyn) {
+  const int H = e->d.H;
+  ECK(cudaMemcpyAsync(e->dtok, e->toks, sizeof(int), cudaMemcpyDeviceToDevice, e->st));
+  const float* hcur = e->hprev;
+  for (int j = 0; j < e->cfg.k_draft; ++j) {
+    RCK(draft_step(e, e->dtok + (j & 1), hcur, e->P + 1 + j, e->P, e->dtok + ((j + 1) & 1), dyn, j));
+    ECK(cudaMemcpyAsync(e->toks + 1 + j, e->dtok + ((j + 1) & 1), sizeof(int), cudaMemcpyDeviceToDevice, e->st));
+    ECK(cudaMemcpyAsync(e->hnext, e->bcur, sizeof(float) * H, cudaMemcpyDeviceToDevice, e->st));
+    hcur = e->hnext;
+  }
+  return G4_OK;
+}
+
 extern "C" int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, int32_t* out, int* n_out,
                                 g4_engine_stats* stats) {
   G4_REQUIRE(e && n_out && max_rounds >= 0 && max_tokens >= 0 && !e->seq.empty(), "g4_engine_decode: call g4_engine_prefill first");
-  const int H = e->d.H;
+  const int H = e->d.H, MM = e->MMAX;
   auto t0 = std::chrono::steady_clock::now();
   cudaEvent_t ev0, ev1;
   ECK(cudaEventCreate(&ev0));
   ECK(cudaEventCreate(&ev1));
   ECK(cudaEventRecord(ev0, e->st));
   e->i8_active = e->cfg.decode_int8 && e->cfg.prefill_int8;  // (:1600)
+  int* hctl = e->hio;                  // [0] = P, [8..] = tokens
+  int* hG = e->hio + 8 + MM;           // verified tokens
+  int* hdr = e->hio + 8 + 2 * MM;      // drafts read back
   int produced = 0, rounds = 0;
   int block[8];
-  int G[8];
   while (rounds < max_rounds && produced < max_tokens && !e->stopped) {
-    if (e->P + 1 + 4 >= e->cfg.ctx_max) return set_error(G4_ERR_UNSUPPORTED, "g4_engine_decode: context full (%d)", e->cfg.ctx_max);
+    if (e->P + 1 + 8 >= e->cfg.ctx_max) return set_error(G4_ERR_UNSUPPORTED, "g4_engine_decode: context full (%d)", e->cfg.ctx_max);
     block[0] = e->conf;
     int nd = 0;
     bool used_ng = false;
@@ -565,41 +672,69 @@ extern "C" int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, in
         }
       if (nd > 0) { used_ng = true; e->stats.ngram_rounds++; }
     }
-    if (!used_ng && e->cfg.drafter && e->cfg.k_draft > 0) {
-      // MTP drafts: token conf with hidden hprev, then each draft with the drafter's next hidden
-      ECK(cudaMemcpyAsync(e->dtok, &e->conf, sizeof(int), cudaMemcpyHostToDevice, e->st));
-      const float* hcur = e->hprev;
-      for (int j = 0; j < e->cfg.k_draft; ++j) {
-        RCK(draft_step(e, e->dtok + (j & 1), hcur, e->P + 1 + j, e->P, e->dtok + ((j + 1) & 1)));
-        ECK(cudaMemcpyAsync(e->toks + 1 + j, e->dtok + ((j + 1) & 1), sizeof(int), cudaMemcpyDeviceToDevice, e->st));
-        ECK(cudaMemcpyAsync(e->hnext, e->bcur, sizeof(float) * H, cudaMemcpyDeviceToDevice, e->st));
-        hcur = e->hnext;
+    const bool drafting = !used_ng && e->cfg.drafter && e->cfg.k_draft > 0;
+    const int M = (drafting ? e->cfg.k_draft : nd) + 1;
+    // replay captured graphs once the split-KV path applies to every row (positions > att_par)
+    const bool use_g = e->cfg.graphs && !e->prof.on && M <= 4 && e->P + 1 > e->cfg.att_par;
+    hctl[0] = e->P;
+    for (int i = 0; i <= nd; ++i) hctl[8 + i] = block[i];
+    const int nsend = 8 + (drafting ? 1 : M);
+    ECK(cudaMemcpyAsync(e->ctl, hctl, sizeof(int) * nsend, cudaMemcpyHostToDevice, e->st));
+    e->stats.h2d_bytes += sizeof(int) * nsend;
+    if (drafting) {
+      ECK(cudaEventRecord(e->tev[0], e->st));
+      if (use_g) {
+        if (!e->gdraft) RCK(capture(e, &e->gdraft, [&] { return draft_chain(e, true); }));
+        ECK(cudaGraphLaunch(e->gdraft, e->st));
+      } else {
+        RCK(draft_chain(e, false));
       }
-      int dr[3];
-      ECK(cudaMemcpyAsync(dr, e->toks + 1, sizeof(int) * e->cfg.k_draft, cudaMemcpyDeviceToHost, e->st));
-      ECK(cudaStreamSynchronize(e->st));
-      e->prof.flush();
-      for (int j = 0; j < e->cfg.k_draft; ++j) block[1 + nd++] = dr[j];
-      e->stats.drafted += nd;
+      ECK(cudaEventRecord(e->tev[1], e->st));
+      e->stats.drafted += e->cfg.k_draft;
+      e->stats.draft_steps += e->cfg.k_draft;
+      nd = e->cfg.k_draft;
     }
-    const int M = nd + 1;
-    ECK(cudaMemcpyAsync(e->toks, block, sizeof(int) * M, cudaMemcpyHostToDevice, e->st));
-    RCK(forward(e, M, e->P + 1, true, 0));
-    ECK(cudaMemcpyAsync(G, e->G, sizeof(int) * M, cudaMemcpyDeviceToHost, e->st));
+    ECK(cudaEventRecord(e->tev[2], e->st));
+    if (use_g) {
+      if (!e->gverify[M]) RCK(capture(e, &e->gverify[M], [&] { return forward(e, M, 0, true, 0, true); }));
+      ECK(cudaGraphLaunch(e->gverify[M], e->st));
+    } else {
+      RCK(forward(e, M, e->P + 1, true, 0));
+    }
+    ECK(cudaEventRecord(e->tev[3], e->st));
+    ECK(cudaMemcpyAsync(hG, e->G, sizeof(int) * M, cudaMemcpyDeviceToHost, e->st));
+    e->stats.d2h_bytes += sizeof(int) * M;
+    if (drafting) {
+      ECK(cudaMemcpyAsync(hdr, e->toks + 1, sizeof(int) * nd, cudaMemcpyDeviceToHost, e->st));
+      e->stats.d2h_bytes += sizeof(int) * nd;
+    }
     ECK(cudaStreamSynchronize(e->st));
     e->prof.flush();
+    if (drafting) {
+      for (int j = 0; j < nd; ++j) block[1 + j] = hdr[j];
+      float ms = 0;
+      cudaEventElapsedTime(&ms, e->tev[0], e->tev[1]);
+      e->stats.draft_gpu_ms += ms;
+    }
+    {
+      float ms = 0;
+      cudaEventElapsedTime(&ms, e->tev[2], e->tev[3]);
+      e->stats.verify_gpu_ms += ms;
+      e->stats.verify_passes++;
+      e->stats.verify_rows += M;
+    }
     e->stats.rounds++;
     ++rounds;
     int nacc = 0;
-    while (nacc < nd && block[nacc + 1] == G[nacc]) ++nacc;
+    while (nacc < nd && block[nacc + 1] == hG[nacc]) ++nacc;
     e->stats.accepted += nacc;
     for (int i = 0; i <= nacc; ++i) {
-      e->seq.push_back(G[i]);
-      if (out && produced < max_tokens) out[produced] = G[i];
+      e->seq.push_back(hG[i]);
+      if (out && produced < max_tokens) out[produced] = hG[i];
       ++produced;
-      if (is_stop(G[i])) { e->stopped = true; break; }
+      if (is_stop(hG[i])) { e->stopped = true; break; }
     }
-    e->conf = G[nacc];
+    e->conf = hG[nacc];
     ECK(cudaMemcpyAsync(e->hprev, e->hbuf + (size_t)nacc * H, sizeof(float) * H, cudaMemcpyDeviceToDevice, e->st));
     e->P += nacc + 1;
   }

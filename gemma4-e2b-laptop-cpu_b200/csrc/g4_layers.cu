@@ -52,11 +52,12 @@ __global__ void k_embed(const uint16_t* __restrict__ E, const int* __restrict__ 
 // head `part`: rms_r16 with q_norm, then RoPE (fp32, not rounded); part == nq is k: rms_r16 with
 // k_norm, RoPE, bf16 store at cache position pos0+m; part == nq+1 is v: rms_r16 without weight,
 // bf16 store.  RoPE (rope_avx2 :394-402): h[j] = fma(u, c, -(w*s)), h[j+hd/2] = fma(w, c, u*s).
-__global__ void k_qkv_post(float* __restrict__ qkv, int ldqkv, int nq, int hd, int pos0, const float* __restrict__ qn,
-                           const float* __restrict__ kn, const float* __restrict__ cosT, const float* __restrict__ sinT,
-                           uint16_t* __restrict__ Kc, uint16_t* __restrict__ Vc) {
+__global__ void k_qkv_post(float* __restrict__ qkv, int ldqkv, int nq, int hd, int pos0, const int* __restrict__ dpos,
+                           const float* __restrict__ qn, const float* __restrict__ kn, const float* __restrict__ cosT,
+                           const float* __restrict__ sinT, uint16_t* __restrict__ Kc, uint16_t* __restrict__ Vc) {
   __shared__ double red[17];
   __shared__ float hbuf[512];
+  if (dpos) pos0 += *dpos;  // position read on the device (captured decode steps)
   const int m = blockIdx.x, part = blockIdx.y, pos = pos0 + m, hh = hd >> 1;
   float* src = qkv + (size_t)m * ldqkv + (size_t)part * hd;  // q heads, then k, then v
   const float* w = part < nq ? qn : (part == nq ? kn : nullptr);
@@ -88,10 +89,11 @@ __global__ void k_qkv_post(float* __restrict__ qkv, int ldqkv, int nq, int hd, i
 
 // Query-only variant for the drafter (and any caller whose k/v are not written): heads of q in
 // place, rms_r16 with q_norm then RoPE at position pos.
-__global__ void k_q_post(float* __restrict__ q, int hd, int pos, const float* __restrict__ qn, const float* __restrict__ cosT,
-                         const float* __restrict__ sinT) {
+__global__ void k_q_post(float* __restrict__ q, int hd, int pos, const int* __restrict__ dpos, const float* __restrict__ qn,
+                         const float* __restrict__ cosT, const float* __restrict__ sinT) {
   __shared__ double red[17];
   __shared__ float hbuf[512];
+  if (dpos) pos += *dpos;
   const int h = blockIdx.x, hh = hd >> 1;
   float* src = q + (size_t)h * hd;
   const float r = block_rms_scale(src, hd, red);

@@ -6,9 +6,10 @@
 namespace g4 {
 __global__ void k_rmsnorm(const float* x, const float* w, int n, float* y, int round);
 __global__ void k_embed(const uint16_t* E, const int* toks, int H, float sqrtH, float* x);
-__global__ void k_qkv_post(float* qkv, int ldqkv, int nq, int hd, int pos0, const float* qn, const float* kn,
-                           const float* cosT, const float* sinT, uint16_t* Kc, uint16_t* Vc);
-__global__ void k_q_post(float* q, int hd, int pos, const float* qn, const float* cosT, const float* sinT);
+// dpos (device, may be NULL) is added to the position argument: pos0 / pos is then an offset.
+__global__ void k_qkv_post(float* qkv, int ldqkv, int nq, int hd, int pos0, const int* dpos, const float* qn,
+                           const float* kn, const float* cosT, const float* sinT, uint16_t* Kc, uint16_t* Vc);
+__global__ void k_q_post(float* q, int hd, int pos, const int* dpos, const float* qn, const float* cosT, const float* sinT);
 __global__ void k_post_attn(float* o, float* x, const float* w_post, const float* w_pre, float* mlp_in, int n);
 __global__ void k_post_ff(float* o, float* x, const float* w_post, float scalar, int n);
 __global__ void k_act(const float* gu, int I, int M, float* act);

@@ -42,6 +42,7 @@ SIGNATURES = {
     "g4_engine_forward": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "g4_engine_draft": (_I, [_P, _I, _P, _I, _I, _P, _P]),
     "g4_engine_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+    "g4_engine_fake_ctx": (_I, [_P, _I]),
     "g4_engine_prefill": (_I, [_P, _P, _I, _P]),
     "g4_engine_decode": (_I, [_P, _I, _I, _P, _P, _P]),
     "g4_engine_phase_times": (_I, [_P, _I, _P, _P]),
@@ -257,14 +258,17 @@ class EngineConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in ("hidden", "n_layers", "mlp", "vocab", "ctx_max", "prefill_block", "k_draft",
                                             "ngram", "ngram_len", "prefill_int8", "decode_int8", "head_screen",
                                             "screen_lim", "attn_chunks", "att_par", "drafter")] + [
-        ("seed", ctypes.c_ulonglong)]
+        ("seed", ctypes.c_ulonglong), ("graphs", ctypes.c_int)]
 
 
 class EngineStats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in ("rounds", "ngram_rounds", "drafted", "accepted", "prefill_tokens",
                                             "decode_tokens")] + [("prefill_ms", ctypes.c_double),
                                                                  ("decode_ms", ctypes.c_double),
-                                                                 ("decode_gpu_ms", ctypes.c_double)]
+                                                                 ("decode_gpu_ms", ctypes.c_double)] + [
+        (n, ctypes.c_int) for n in ("verify_passes", "verify_rows", "draft_steps")] + [
+        ("verify_gpu_ms", ctypes.c_double), ("draft_gpu_ms", ctypes.c_double), ("h2d_bytes", ctypes.c_longlong),
+        ("d2h_bytes", ctypes.c_longlong)]
 
     def as_dict(self):
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -309,6 +313,11 @@ class Engine:
         check(lib().g4_engine_draft(self.h, int(tok), h.ctypes.data_as(_P), pos, P, out.ctypes.data_as(_P),
                                     hn.ctypes.data_as(_P)), "g4_engine_draft")
         return int(out[0]), hn
+
+    def fake_ctx(self, n):
+        """Fill KV positions [0, n) with the reference's ENGINE_FAKE_CTX values; the next prefill
+        starts at position n."""
+        check(lib().g4_engine_fake_ctx(self.h, int(n)), "g4_engine_fake_ctx")
 
     def prefill(self, prompt):
         import numpy as np

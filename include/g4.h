@@ -153,11 +153,15 @@ typedef struct {
   int att_par;                       /* ENGINE_ATT_PAR (192) */
   int drafter;                       /* build the MTP drafter (1) */
   unsigned long long seed;           /* weight seed */
+  int graphs;                        /* replay decode rounds as CUDA graphs (1); 0 = eager launches */
 } g4_engine_config;
 typedef struct {
   int rounds, ngram_rounds, drafted, accepted, prefill_tokens, decode_tokens;
   double prefill_ms, decode_ms; /* host wall clock */
   double decode_gpu_ms;         /* CUDA events on the engine stream around the decode calls */
+  int verify_passes, verify_rows, draft_steps;
+  double verify_gpu_ms, draft_gpu_ms; /* CUDA events around each verify pass / each round's drafts */
+  long long h2d_bytes, d2h_bytes;     /* host<->device copies made by the decode calls */
 } g4_engine_stats;
 
 int g4_engine_default_config(g4_engine_config* cfg);
@@ -171,6 +175,10 @@ int g4_engine_forward(g4_engine* e, const int32_t* toks, int M, int pos0, int wa
                       float* hbuf);
 /* One MTP draft step: token, hidden h (host [hidden]), query position, last target position P. */
 int g4_engine_draft(g4_engine* e, int32_t tok, const float* h, int pos, int P, int32_t* out_tok, float* h_next);
+/* ENGINE_FAKE_CTX (gemma4_engine.cpp:1249-1250): fill positions [0, n) of every layer's K and V
+ * with the reference's seeded LCG values (K then V per element, one stream over the layers); the
+ * next prefill then starts at position n.  n = 0 turns it off. */
+int g4_engine_fake_ctx(g4_engine* e, int n);
 /* Prefill a prompt (host [n]) in blocks of prefill_block and reset the decode state; *first_token =
  * the greedy token after the prompt. */
 int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int32_t* first_token);

@@ -61,6 +61,7 @@ typedef struct {
   uint16_t *Kc, *Vc;
   float *rc[2], *rs[2];
   int i8;
+  int fake_n; /* ENGINE_FAKE_CTX positions before the prompt */
 } Model;
 
 static void gen_lin(Model* m, Lin* lin, const uint64_t* ids, const int* rows, int parts, int K) {
@@ -459,7 +460,6 @@ static int is_stop(int t) { return t == 106 || t == 1; }
 /* ENGINE_FAKE_CTX (gemma4_engine.cpp:1249-1250): fill positions [0, n) of every layer's K and V with
  * the reference's seeded LCG values, so that decode can be timed at a long context without a long
  * prefill; the prompt then starts at position n. */
-static int g_fake_n = 0;
 void or_e2e_fake_ctx(void* mp, int n) {
   Model* m = (Model*)mp;
   uint32_t rs = 12345;
@@ -470,13 +470,13 @@ void or_e2e_fake_ctx(void* mp, int n) {
       rs = rs * 1664525u + 1013904223u;
       m->Vc[(size_t)l * m->ctx_max * m->HD + i] = or_f2bf(((int)(rs >> 9) % 2001 - 1000) / 700.0f);
     }
-  g_fake_n = n;
+  m->fake_n = n;
 }
 
 /* run_req in chain mode (:1582-1663). stats[0..5] = rounds, ngram_rounds, drafted, accepted. */
 int or_e2e_generate(void* mp, const int32_t* prompt, int n, int n_new, int32_t* out, int* n_out, int* stats) {
   Model* m = (Model*)mp;
-  const int FN = g_fake_n;
+  const int FN = m->fake_n;
   const int H = m->H;
   int* G = (int*)malloc(sizeof(int) * 64);
   float* hbuf = (float*)malloc(sizeof(float) * 64 * H);

@@ -87,3 +87,40 @@ def test_generate_matches_oracle(pair):
     to, so = om.generate(prompt, 40)
     assert list(tg) == list(to)
     assert sg["rounds"] == so["rounds"] and sg["accepted"] == so["accepted"]
+
+
+@pytest.mark.parametrize("ngram,graphs", [(0, 1), (0, 0), (2, 0)])
+def test_generate_graph_replay_and_eager_agree_with_oracle(ngram, graphs):
+    """Decode rounds replayed from captured graphs (positions read on the device) and launched
+    eagerly give the oracle's tokens, with MTP drafts (ngram 0) and with prompt lookup."""
+    om = OracleModel(e2e_config(**SMALL, ngram=ngram))
+    eng = g4.Engine(g4.engine_config(**SMALL, ngram=ngram, graphs=graphs))
+    try:
+        prompt = make_prompt(6, 300, vocab=4096)
+        tg, sg = eng.generate(prompt, 32)
+        to, so = om.generate(prompt, 32)
+        assert list(tg) == list(to)
+        assert sg["rounds"] == so["rounds"] and sg["accepted"] == so["accepted"]
+        assert sg["verify_passes"] == sg["rounds"] and sg["verify_rows"] >= sg["rounds"]
+        if ngram == 0:
+            assert sg["draft_steps"] == 3 * sg["rounds"] and sg["draft_gpu_ms"] > 0
+        assert sg["h2d_bytes"] > 0 and sg["d2h_bytes"] > 0
+    finally:
+        eng.close()
+        om.close()
+
+
+def test_fake_context_generate_matches_oracle():
+    """ENGINE_FAKE_CTX: a 600-position LCG context, then a short prompt and decode on top of it."""
+    om = OracleModel(e2e_config(**SMALL))
+    eng = g4.Engine(g4.engine_config(**SMALL))
+    try:
+        om.fake_ctx(600)
+        eng.fake_ctx(600)
+        prompt = make_prompt(7, 40, vocab=4096)
+        tg, _ = eng.generate(prompt, 24)
+        to, _ = om.generate(prompt, 24)
+        assert list(tg) == list(to)
+    finally:
+        eng.close()
+        om.close()
