@@ -28,6 +28,7 @@ struct AttnDesc {
   // max(0, *dynP + q_add + m - (window - 1)) (0 for window == 0); kmin/kmax follow from them.
   const int* dynP;
   int base_add, q_add, window;
+  QuantOut qo;  // when qo.q is set, the merge also quantises each row of out for a W4A8 linear
 };
 
 __device__ __forceinline__ AttnDesc resolve(const AttnDesc& d0) {
@@ -301,7 +302,162 @@ __global__ void __launch_bounds__(512) k_attn_merge(AttnDesc d0, const float* __
     if (!(w.AL[ix] > 0)) continue;
     acc = fmaf(w.AO[ix * d.hd + i], sc[t], acc);
   }
-  out[(size_t)mh * d.hd + i] = r16(__fmul_rn(acc, inv_l));
+  const float v = r16(__fmul_rn(acc, inv_l));
+  out[(size_t)mh * d.hd + i] = v;
+  if (d.qo.q) {  // blockDim == hd, a multiple of 32: warp w holds group w of this head's dims
+    int8_t qv;
+    float sx;
+    int32_t tot;
+    quant_group32(v, qv, sx, tot);
+    const size_t flat = (size_t)mh * d.hd + i;
+    d.qo.q[flat] = qv;
+    if ((threadIdx.x & 31) == 0) {
+      d.qo.sx[flat >> 5] = sx;
+      d.qo.sum[flat >> 5] = tot;
+    }
+  }
+}
+
+// ---- one-kernel split-KV: block = (chunk t, (row, head) pair).  The block computes its chunk's
+// scores (half-warp per key, as k_attn_scores) into shared memory, the chunk max, the exp8 weights
+// and their in-order sum (as k_attn_stats), and O for every dim over the chunk's keys in order (as
+// k_attn_accum); the last of the T blocks of a pair to finish (a counter per pair, zeroed before
+// the launch) merges the chunks (as k_attn_merge) and quantises the row when asked.  Same values
+// as the four-kernel path.
+template <int STEPS>
+__global__ void __launch_bounds__(256) k_attn_fused(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
+                                                    const float* __restrict__ q, AttnDesc d0, float* __restrict__ ws,
+                                                    int* __restrict__ counters, float* __restrict__ out) {
+  extern __shared__ __align__(16) float sc[];  // chunk scores, then weights
+  __shared__ float red_f[8];
+  __shared__ float msc[64];
+  __shared__ float s_l8, s_inv;
+  __shared__ int s_last;
+  const AttnDesc d = resolve(d0);
+  const AttnWs w = attn_ws(ws, d);
+  const int t = blockIdx.x, mh = blockIdx.y, nmh = d.M * d.nh;
+  const int m = mh / d.nh, h = mh % d.nh;
+  const int c0 = max(chunk_lo(d, t), d.lo[m]), c1 = min(chunk_lo(d, t + 1), d.pos[m] + 1);
+  const int n = max(0, c1 - c0);
+  const int hw = threadIdx.x >> 4, c = threadIdx.x & 15, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  // scores
+  {
+    float qr[STEPS];
+    const float* qh = q + ((size_t)m * d.nh + h) * d.hd;
+#pragma unroll
+    for (int i = 0; i < STEPS; ++i) qr[i] = qh[c + 16 * i];
+    const int nk2 = (n + 15) / 16 * 16;  // keep half-warp pairs together for the shuffles
+    for (int k = hw; k < nk2; k += 16) {
+      const int kk = min(k, n - 1);
+      float acc = 0.f;
+      if (n > 0) {
+        const uint16_t* kr = Kc + (size_t)(c0 + kk) * d.hd;
+#pragma unroll
+        for (int i = 0; i < STEPS; ++i) acc = fmaf(qr[i], bf2f(__ldg(kr + c + 16 * i)), acc);
+      }
+      const float sv = hsum8_octet(__fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8)));
+      if (c == 0 && k < n) sc[k] = sv;
+    }
+  }
+  __syncthreads();
+  // chunk max (order-free), then the weights
+  float mx = -1e30f;
+  for (int k = threadIdx.x; k < n; k += blockDim.x) mx = fmaxf(mx, sc[k]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+  if (lane == 0) red_f[wid] = mx;
+  __syncthreads();
+  mx = red_f[0];
+  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, red_f[i]);
+  for (int k = threadIdx.x; k < n; k += blockDim.x) sc[k] = exp8(__fsub_rn(sc[k], mx));
+  __syncthreads();
+  // in-order sum of the weights (warp 0: 32 keys per step, handed over by shuffles)
+  if (wid == 0) {
+    float l8 = 0.f;
+    for (int kb = 0; kb < n; kb += 32) {
+      const float wt = kb + lane < n ? sc[kb + lane] : 0.f;
+      const int nb = min(32, n - kb);
+      if (nb == 32) {
+        float x[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) x[k] = __shfl_sync(FULL, wt, k);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) l8 = __fadd_rn(l8, x[k]);
+      } else {
+        for (int k = 0; k < nb; ++k) l8 = __fadd_rn(l8, __shfl_sync(FULL, wt, k));
+      }
+    }
+    if (lane == 0) s_l8 = l8;
+  }
+  // O over the chunk's keys in order, thread per dim
+  const size_t ix = (size_t)t * nmh + mh;
+  for (int i = threadIdx.x; i < d.hd; i += blockDim.x) {
+    float o = 0.f;
+    const uint16_t* vp = Vc + (size_t)c0 * d.hd + i;
+    int k = 0;
+    for (; k + 8 <= n; k += 8) {
+      uint16_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(vp + (size_t)(k + u) * d.hd);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o = fmaf(sc[k + u], bf2f(v[u]), o);
+    }
+    for (; k < n; ++k) o = fmaf(sc[k], bf2f(__ldg(vp + (size_t)k * d.hd)), o);
+    w.AO[ix * d.hd + i] = o;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    w.AM[ix] = mx;
+    w.AL[ix] = (d.lo[m] > d.pos[m]) ? 0.0f : s_l8;
+  }
+  __threadfence();  // every thread's partial results are visible device-wide before the count
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&counters[mh], 1) == d.T - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // merge (k_attn_merge) by the last block of the pair
+  if (threadIdx.x == 0) {
+    float M0 = -1e30f;
+    for (int tt = 0; tt < d.T; ++tt) {
+      const size_t jx = (size_t)tt * nmh + mh;
+      if (__ldcg(&w.AL[jx]) > 0) M0 = fmaxf(M0, __ldcg(&w.AM[jx]));
+    }
+    double l = 0;
+    for (int tt = 0; tt < d.T; ++tt) {
+      const size_t jx = (size_t)tt * nmh + mh;
+      msc[tt] = 0.f;
+      const float al = __ldcg(&w.AL[jx]);
+      if (!(al > 0)) continue;
+      msc[tt] = exp_cr(__fsub_rn(__ldcg(&w.AM[jx]), M0));
+      l = fma((double)al, (double)msc[tt], l);
+    }
+    s_inv = (float)(1.0 / l);
+    counters[mh] = 0;  // ready for the next launch
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < d.hd; i += blockDim.x) {
+    float acc = 0.f;
+    for (int tt = 0; tt < d.T; ++tt) {
+      const size_t jx = (size_t)tt * nmh + mh;
+      if (!(__ldcg(&w.AL[jx]) > 0)) continue;
+      acc = fmaf(__ldcg(&w.AO[jx * d.hd + i]), msc[tt], acc);
+    }
+    const float v = r16(__fmul_rn(acc, s_inv));
+    out[(size_t)mh * d.hd + i] = v;
+    if (d.qo.q) {
+      int8_t qv;
+      float sxv;
+      int32_t tot;
+      quant_group32(v, qv, sxv, tot);
+      const size_t flat = (size_t)mh * d.hd + i;
+      d.qo.q[flat] = qv;
+      if (lane == 0) {
+        d.qo.sx[flat >> 5] = sxv;
+        d.qo.sum[flat >> 5] = tot;
+      }
+    }
+  }
 }
 
 }  // namespace g4
@@ -318,6 +474,7 @@ static int fill_desc(AttnDesc& d, const uint16_t* Kc, const uint16_t* Vc, int M,
   G4_REQUIRE(pos && lo && kmin >= 0 && kmax >= kmin, "attention: bad key range [%d, %d]", kmin, kmax);
   d.M = M; d.nh = nh; d.hd = hd; d.kmin = kmin; d.kmax = kmax; d.T = T;
   d.dynP = nullptr; d.base_add = d.q_add = d.window = 0;
+  d.qo = QuantOut{nullptr, nullptr, nullptr};
   for (int m = 0; m < 4; ++m) { d.pos[m] = m < M ? pos[m] : -1; d.lo[m] = m < M ? lo[m] : 0; }
   for (int m = 0; m < M; ++m)
     G4_REQUIRE(lo[m] >= kmin && pos[m] <= kmax, "attention: row %d range [%d, %d] outside [%d, %d]", m, lo[m], pos[m],
@@ -338,13 +495,42 @@ static int launch_attn(const uint16_t* Kc, const uint16_t* Vc, const float* q, c
   if (int rc = check_launch("k_attn_stats")) return rc;
   k_attn_accum<<<dim3(d.T, d.hd / 16, (nmh + 7) / 8), 64, 0, st>>>(Vc, d, w);
   if (int rc = check_launch("k_attn_accum")) return rc;
-  k_attn_merge<<<nmh, (d.hd + 31) / 32 * 32, 0, st>>>(d, w, out);
+  k_attn_merge<<<nmh, d.hd, 0, st>>>(d, w, out);
   return check_launch("k_attn_merge");
 }
 
-extern "C" size_t g4_attn_splitkv_ws_bytes(int M, int nh, int hd, int kmin, int kmax, int T) {
-  return sizeof(float) * attn_ws_floats(M, nh, hd, kmax - kmin + 1, T);
+// Workspace of g4_attn_splitkv: the partial results (attn_ws_floats), then one int counter per
+// (row, head) pair for the one-kernel path.
+static size_t attn_counter_offset(int M, int nh, int hd, int len, int T) {
+  return (sizeof(float) * attn_ws_floats(M, nh, hd, len, T) + 15) / 16 * 16;
 }
+extern "C" size_t g4_attn_splitkv_ws_bytes(int M, int nh, int hd, int kmin, int kmax, int T) {
+  return attn_counter_offset(M, nh, hd, kmax - kmin + 1, T) + sizeof(int) * (size_t)M * nh;
+}
+
+// One-kernel path (k_attn_fused) when a chunk's scores fit in shared memory; max_len bounds the
+// key range (the device may pick a shorter one) and sizes the workspace.
+static int launch_attn_fused(const uint16_t* Kc, const uint16_t* Vc, const float* q, const AttnDesc& d, void* ws,
+                             float* out, cudaStream_t st, int max_len) {
+  const int nmh = d.M * d.nh;
+  const int max_chunk = (max_len + d.T - 1) / d.T + 1;
+  const size_t smem = sizeof(float) * (size_t)max_chunk;
+  int* counters = reinterpret_cast<int*>(static_cast<char*>(ws) + attn_counter_offset(d.M, d.nh, d.hd, max_len, d.T));
+  cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int) * (size_t)nmh, st);
+  if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "attention: counter reset: %s", cudaGetErrorString(e));
+  float* w = static_cast<float*>(ws);
+  const dim3 grid(d.T, nmh);
+  auto launch = [&](auto kern) {
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<grid, 256, smem, st>>>(Kc, Vc, q, d, w, counters, out);
+  };
+  if (d.hd == 256) launch(k_attn_fused<16>);
+  else if (d.hd == 512) launch(k_attn_fused<32>);
+  else if (d.hd == 128) launch(k_attn_fused<8>);
+  else return set_error(G4_ERR_UNSUPPORTED, "attention: hd=%d (supported: 128, 256, 512)", d.hd);
+  return check_launch("k_attn_fused");
+}
+static bool fused_fits(int max_len, int T) { return (size_t)sizeof(float) * ((max_len + T - 1) / T + 1) <= 200 * 1024; }
 
 extern "C" int g4_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, const float* q, const int* pos, const int* lo,
                                int M, int nh, int hd, int kmin, int kmax, int T, float* out, void* ws, size_t ws_bytes,
@@ -356,8 +542,9 @@ extern "C" int g4_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, const flo
   if (ws_bytes < need) return set_error(G4_ERR_NOMEM, "g4_attn_splitkv: workspace %zu < %zu bytes", ws_bytes, need);
   G4_REQUIRE(aligned(ws, 16), "g4_attn_splitkv: workspace must be 16-byte aligned");
   cudaStream_t st = as_stream(stream);
-  float* w = static_cast<float*>(ws);
-  return launch_attn(Kc, Vc, q, d, w, out, st);
+  const int len = kmax - kmin + 1;
+  if (fused_fits(len, T)) return launch_attn_fused(Kc, Vc, q, d, ws, out, st, len);
+  return launch_attn(Kc, Vc, q, d, static_cast<float*>(ws), out, st);
 }
 
 // Engine-internal form for captured decode steps: the key ranges come from the position *dP on the
@@ -365,15 +552,17 @@ extern "C" int g4_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, const flo
 // see and sizes the score grid (blocks past kmax return at once).  ws must hold max_len keys.
 int g4::attn_splitkv_dev(const uint16_t* Kc, const uint16_t* Vc, const float* q, int M, int nh, int hd, const int* dP,
                          int base_add, int q_add, int window, int max_len, int T, float* out, void* ws, size_t ws_bytes,
-                         cudaStream_t st) {
+                         cudaStream_t st, QuantOut qo) {
   G4_REQUIRE(Kc && Vc && q && out && ws && dP && max_len >= 1, "attn_splitkv_dev: bad arguments");
   int pos[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
   for (int m = 0; m < M && m < 4; ++m) pos[m] = m;
   AttnDesc d;
   if (int rc = fill_desc(d, Kc, Vc, M, nh, hd, pos, lo, 0, M - 1, T)) return rc;
   d.dynP = dP; d.base_add = base_add; d.q_add = q_add; d.window = window;
+  d.qo = qo;
   const size_t need = g4_attn_splitkv_ws_bytes(M, nh, hd, 0, max_len - 1, T);
   if (ws_bytes < need) return set_error(G4_ERR_NOMEM, "attn_splitkv_dev: workspace %zu < %zu bytes", ws_bytes, need);
+  if (fused_fits(max_len, T)) return launch_attn_fused(Kc, Vc, q, d, ws, out, st, max_len);
   return launch_attn(Kc, Vc, q, d, static_cast<float*>(ws), out, st, max_len);
 }
 

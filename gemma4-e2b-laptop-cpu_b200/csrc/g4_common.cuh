@@ -25,6 +25,33 @@ __device__ __forceinline__ float r16(float f) { return bf2f(f2bf(f)); }
 // Exact small-integer to float: 0x4B000000 | t is the float 2^23 + t for 0 <= t < 2^23.
 __device__ __forceinline__ float u4f(uint32_t t) { return __fsub_rn(__uint_as_float(0x4B000000u | t), 8388608.0f); }
 
+// W4A8 quantisation of one 32-group, lane i owning element x (w4a8_avx2.h:30-42): amax,
+// sx = amax/127, inv = sx > 0 ? 1/sx : 0, r = RNE(x*inv) (x86 cvtps_epi32: out of range or NaN ->
+// INT32_MIN), tot = sum of the unsaturated r, q = r saturated to int16 then int8.  All 32 lanes.
+__device__ __forceinline__ void quant_group32(float x, int8_t& q, float& sx, int32_t& tot) {
+  float amax = fabsf(x);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, o));
+  const float s = __fdiv_rn(amax, 127.0f);
+  const float inv = s > 0.f ? __fdiv_rn(1.0f, s) : 0.0f;
+  const float v = __fmul_rn(x, inv);
+  const int32_t r = (v > -2147483648.f && v < 2147483648.f) ? __float2int_rn(v) : INT32_MIN;
+  int32_t t = r;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(FULL, t, o);
+  const int32_t r16v = r < -32768 ? -32768 : (r > 32767 ? 32767 : r);
+  q = (int8_t)(r16v < -128 ? -128 : (r16v > 127 ? 127 : r16v));
+  sx = s;
+  tot = t;
+}
+
+// Destination of a fused W4A8 quantisation: rows of q [M][K], sx and sum [M][K/32] (NULL q = none).
+struct QuantOut {
+  int8_t* q;
+  float* sx;
+  int32_t* sum;
+};
+
 // Horizontal sum over the 8 consecutive lanes of an octet (lane j holds v_j), in the order of the
 // AVX2 hsum (w4g32_avx2.h:41-44): ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7)).  Every lane of the octet
 // ends with the same value; all 32 lanes of the warp must call it together.

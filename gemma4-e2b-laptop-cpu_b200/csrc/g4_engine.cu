@@ -176,7 +176,7 @@ static int gen_norm(g4_engine* e, float** p, uint64_t id, int n, float mul) {
 extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
   if (!cfg || !out) return set_error(G4_ERR_INVALID, "g4_engine_create: null pointer");
   const g4_engine_config c = *cfg;
-  G4_REQUIRE(c.hidden % 256 == 0 && c.hidden >= 256 && c.mlp % 256 == 0 && c.n_layers >= 1 && c.vocab % 128 == 0 &&
+  G4_REQUIRE(c.hidden % 256 == 0 && c.hidden >= 256 && c.hidden <= 2048 && c.mlp % 256 == 0 && c.n_layers >= 1 && c.vocab % 128 == 0 &&
                  c.vocab <= (1 << 18) && (c.vocab & (c.vocab - 1)) == 0 && c.ctx_max >= 64 && c.ctx_max <= 32768 &&
                  c.prefill_block >= 1 && c.prefill_block <= 32 && c.k_draft >= 0 && c.k_draft <= 3 && c.attn_chunks >= 1 &&
                  c.attn_chunks <= 16,
@@ -343,10 +343,15 @@ extern "C" void g4_engine_destroy(g4_engine* e) {
 }
 
 // int4 linear: W4A8 when int8 activations are active and M >= 2 (lin_multi :311), or always for the
-// drafter (force_i8); otherwise the float W4G32 path.
-static int lin(g4_engine* e, const Lin& w, const float* X, int M, float* Y, bool force_i8 = false) {
-  if ((e->i8_active && M >= 2) || force_i8) {
-    RCK(g4_w4a8_quant(X, M, w.K, e->xq, e->xsx, e->xsum, e->st));
+// drafter (force_i8); otherwise the float W4G32 path.  prequant: the producer of X already wrote its
+// quantisation to xq/xsx/xsum (fused row kernels, attention merge).
+static bool i8_path(const g4_engine* e, int M, bool force_i8) { return (e->i8_active && M >= 2) || force_i8; }
+static QuantOut quant_out(g4_engine* e, int M, bool force_i8) {
+  return i8_path(e, M, force_i8) ? QuantOut{e->xq, e->xsx, e->xsum} : QuantOut{nullptr, nullptr, nullptr};
+}
+static int lin(g4_engine* e, const Lin& w, const float* X, int M, float* Y, bool force_i8 = false, bool prequant = false) {
+  if (i8_path(e, M, force_i8)) {
+    if (!prequant) RCK(g4_w4a8_quant(X, M, w.K, e->xq, e->xsx, e->xsum, e->st));
     int m0 = 0;
     while (m0 < M) {  // the GEMV serves up to 8 activation rows per launch; rows are independent
       const int mm = std::min(8, M - m0);
@@ -369,44 +374,48 @@ static int lin(g4_engine* e, const Lin& w, const float* X, int M, float* Y, bool
 // when want, rows hf.. get the final-normed hidden in hbuf and the greedy next token in G.  With
 // dyn the positions are ctl[0] + 1.. read on the device (pos0 unused; M <= 4 and the split-KV path,
 // i.e. position + M > att_par, which the caller guarantees), so that the launches can be captured
-// once and replayed at every position.
+// once and replayed at every position.  Per layer: norm(+quant) -> qkv -> q/k norms, RoPE, KV
+// write -> attention(+quant) -> o -> residual + pre-MLP norm(+quant) -> gate/up -> GeGLU(+quant)
+// -> down -> residual + the next layer's input norm(+quant) (the final norm after the last layer).
 static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = false) {
   const ModelDims& d = e->d;
   const int H = d.H, QD = d.NQ * d.HD, ld = QD + 2 * d.HD;
   const float sqrtH = sqrtf((float)H);
   PhaseTimer& pf = e->prof;
+  const QuantOut qo = quant_out(e, M, false);
   pf.mark(e->st, PH_EMBED_NORM);
   k_embed<<<M, 256, 0, e->st>>>(e->E, e->toks, H, sqrtH, e->x);
+  k_norm_q<<<M, 256, 0, e->st>>>(e->x, e->L[0].in_ln, H, e->a, 0, qo);
+  RCK(check_launch("k_norm_q"));
   for (int l = 0; l < d.NL; ++l) {
     const TLayer& t = e->L[l];
     const int ty = t.global ? 1 : 0;
-    pf.mark(e->st, PH_EMBED_NORM);
-    k_rmsnorm<<<M, 256, 0, e->st>>>(e->x, t.in_ln, H, e->a, 0);
     pf.mark(e->st, PH_LINEAR);
-    RCK(lin(e, t.qkv, e->a, M, e->qkv));
+    RCK(lin(e, t.qkv, e->a, M, e->qkv, false, true));
     uint16_t* Kc = e->Kc + (size_t)l * e->cfg.ctx_max * d.HD;
     uint16_t* Vc = e->Vc + (size_t)l * e->cfg.ctx_max * d.HD;
     pf.mark(e->st, PH_EMBED_NORM);
+    const bool split = dyn || (M <= 4 && pos0 + M > e->cfg.att_par);
+    // split-KV reads the rotated queries from qs ([M][QD]); the per-row paths read them in place
     k_qkv_post<<<dim3(M, d.NQ + 2), 256, 0, e->st>>>(e->qkv, ld, d.NQ, d.HD, dyn ? 1 : pos0, dyn ? e->ctl : nullptr,
-                                                     t.qn, t.kn, e->rope[ty][0], e->rope[ty][1], Kc, Vc);
+                                                     t.qn, t.kn, e->rope[ty][0], e->rope[ty][1], Kc, Vc,
+                                                     split ? e->qs : e->qkv, split ? QD : ld);
     RCK(check_launch("k_qkv_post"));
     pf.mark(e->st, PH_ATTN);
+    bool att_q = false;
     if (dyn) {
-      ECK(cudaMemcpy2DAsync(e->qs, sizeof(float) * QD, e->qkv, sizeof(float) * ld, sizeof(float) * QD, M,
-                            cudaMemcpyDeviceToDevice, e->st));
       const int max_len = t.global ? e->cfg.ctx_max : std::min(e->cfg.ctx_max, d.WINDOW + 4);
       RCK(attn_splitkv_dev(Kc, Vc, e->qs, M, d.NQ, d.HD, e->ctl, 1, 1, t.global ? 0 : d.WINDOW, max_len,
-                           e->cfg.attn_chunks, e->att, e->attn_ws, e->attn_ws_bytes, e->st));
-    } else if (M <= 4 && pos0 + M > e->cfg.att_par) {
-      // split-KV (:1305-1327): rows' q are rows of the qkv buffer (stride ld); gather into att first
+                           e->cfg.attn_chunks, e->att, e->attn_ws, e->attn_ws_bytes, e->st, qo));
+      att_q = true;
+    } else if (split) {
+      // split-KV (:1305-1327)
       int pos[4], lo[4], kmin = 1 << 30;
       for (int m = 0; m < M; ++m) {
         pos[m] = pos0 + m;
         lo[m] = t.global ? 0 : std::max(0, pos[m] - (d.WINDOW - 1));
         kmin = std::min(kmin, lo[m]);
       }
-      ECK(cudaMemcpy2DAsync(e->qs, sizeof(float) * QD, e->qkv, sizeof(float) * ld, sizeof(float) * QD, M,
-                            cudaMemcpyDeviceToDevice, e->st));
       RCK(g4_attn_splitkv(Kc, Vc, e->qs, pos, lo, M, d.NQ, d.HD, kmin, pos0 + M - 1, e->cfg.attn_chunks, e->att, e->attn_ws,
                           e->attn_ws_bytes, e->st));
     } else {
@@ -417,24 +426,25 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
       RCK(check_launch("k_attn_rows"));
     }
     pf.mark(e->st, PH_LINEAR);
-    RCK(lin(e, t.o, e->att, M, e->o));
+    RCK(lin(e, t.o, e->att, M, e->o, false, att_q));
     pf.mark(e->st, PH_EMBED_NORM);
-    k_post_attn<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_attn, t.pre_ff, e->mlp_in, H);
+    k_post_attn_q<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_attn, t.pre_ff, e->mlp_in, H, qo);
     pf.mark(e->st, PH_LINEAR);
-    RCK(lin(e, t.gu, e->mlp_in, M, e->gu));
+    RCK(lin(e, t.gu, e->mlp_in, M, e->gu, false, true));
     pf.mark(e->st, PH_EMBED_NORM);
-    k_act<<<gridfor((long long)M * d.I), 256, 0, e->st>>>(e->gu, d.I, M, e->act);
+    k_act_q<<<(unsigned)((long long)M * d.I / 256), 256, 0, e->st>>>(e->gu, d.I, M, e->act, qo);
     pf.mark(e->st, PH_LINEAR);
-    RCK(lin(e, t.down, e->act, M, e->o));
+    RCK(lin(e, t.down, e->act, M, e->o, false, true));
     pf.mark(e->st, PH_EMBED_NORM);
-    k_post_ff<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_ff, 1.0f, H);
+    if (l + 1 < d.NL)  // residual (layer scalar 1) and the next layer's input norm
+      k_resid_norm_q<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_ff, 1.0f, H, e->L[l + 1].in_ln, e->a, 0, qo);
+    else  // residual and the final norm (rounded) of every row into hbuf
+      k_resid_norm_q<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_ff, 1.0f, H, e->fnorm, e->hbuf, 1,
+                                           QuantOut{nullptr, nullptr, nullptr});
     RCK(check_launch("layer"));
   }
   pf.mark(e->st, PH_HEAD);
   if (!want) return G4_OK;
-  const int Mh = M - hf;
-  k_rmsnorm<<<Mh, 256, 0, e->st>>>(e->x + (size_t)hf * H, e->fnorm, H, e->hbuf + (size_t)hf * H, 1);
-  RCK(check_launch("final norm"));
   // head in groups of 4 rows (:1500)
   for (int r0 = hf; r0 < M; r0 += 4) {
     const int mh = std::min(4, M - r0);
@@ -456,16 +466,18 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
 
 // One draft step (draft_step, :1534-1563): token *dtok_in, hidden h (device), query position pos,
 // last valid target position P; writes the drafted token to *dtok_out and the next hidden to bcur.
-// With dyn, P is ctl[0] on the device and pos = P + 1 + j (pos and P unused).
+// With dyn, P is ctl[0] on the device and pos = P + 1 + j (pos and P unused).  Every drafter linear
+// runs W4A8 at M = 1, its input quantised by the kernel that produces it.
 static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos, int P, int* dtok_out, bool dyn = false,
                       int j = 0) {
   const ModelDims& d = e->d;
-  const int H = d.H, QD = d.NQ * d.HD;
-  (void)QD;
+  const int H = d.H;
+  const QuantOut qo{e->xq, e->xsx, e->xsum};
   e->prof.mark(e->st, PH_DRAFT);
   k_draft_in<<<8, 256, 0, e->st>>>(e->E, dtok_in, h, H, sqrtf((float)H), e->dcomb);
   RCK(lin(e, e->dpre, e->dcomb, 1, e->dx, true));
   k_round<<<gridfor(H), 256, 0, e->st>>>(e->dx, H);
+  k_norm_q<<<1, 256, 0, e->st>>>(e->dx, e->DL[0].in_ln, H, e->da, 0, qo);
   for (int l = 0; l < d.DL; ++l) {
     const DLayerW& t = e->DL[l];
     const int ty = t.global ? 1 : 0;
@@ -474,38 +486,41 @@ static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos,
     for (int l2 = d.NL - 1; l2 >= 0; --l2)
       if (d.global_layer(l2) == t.global) { tl = l2; break; }
     if (tl < 0) return set_error(G4_ERR_UNSUPPORTED, "draft_step: the target has no %s layer", t.global ? "global" : "sliding");
-    k_rmsnorm<<<1, 256, 0, e->st>>>(e->dx, t.in_ln, H, e->da, 0);
-    RCK(lin(e, t.q, e->da, 1, e->dq, true));
+    RCK(lin(e, t.q, e->da, 1, e->dq, true, true));
     k_q_post<<<d.NQ, 256, 0, e->st>>>(e->dq, d.HD, dyn ? 1 + j : pos, dyn ? e->ctl : nullptr, t.qn, e->rope[ty][0],
                                       e->rope[ty][1]);
     const uint16_t* Kt = e->Kc + (size_t)tl * e->cfg.ctx_max * d.HD;
     const uint16_t* Vt = e->Vc + (size_t)tl * e->cfg.ctx_max * d.HD;
+    bool att_q = false;
     if (dyn) {
       const int max_len = t.global ? e->cfg.ctx_max : std::min(e->cfg.ctx_max, d.WINDOW);
       RCK(attn_splitkv_dev(Kt, Vt, e->dq, 1, d.NQ, d.HD, e->ctl, 0, 1 + j, t.global ? 0 : d.WINDOW, max_len,
-                           e->cfg.attn_chunks, e->dopt, e->attn_ws, e->attn_ws_bytes, e->st));
+                           e->cfg.attn_chunks, e->dopt, e->attn_ws, e->attn_ws_bytes, e->st, qo));
+      att_q = true;
     } else {
       const int lo = t.global ? 0 : std::max(0, pos - (d.WINDOW - 1));
       const int pp = P;
       RCK(g4_attn_splitkv(Kt, Vt, e->dq, &pp, &lo, 1, d.NQ, d.HD, lo, P, e->cfg.attn_chunks, e->dopt, e->attn_ws,
                           e->attn_ws_bytes, e->st));
     }
-    RCK(lin(e, t.o, e->dopt, 1, e->da, true));
-    k_resid_norm<<<1, 256, 0, e->st>>>(e->da, e->dx, t.post_attn, H);
-    k_rmsnorm<<<1, 256, 0, e->st>>>(e->dx, t.pre_ff, H, e->da, 1);
-    RCK(lin(e, t.gu, e->da, 1, e->dgu, true));
-    k_act<<<gridfor(d.I), 256, 0, e->st>>>(e->dgu, d.I, 1, e->dact);
-    RCK(lin(e, t.down, e->dact, 1, e->da, true));
-    k_resid_norm<<<1, 256, 0, e->st>>>(e->da, e->dx, t.post_ff, H);
-    k_scale_round<<<gridfor(H), 256, 0, e->st>>>(e->dx, H, 1.0f);
+    RCK(lin(e, t.o, e->dopt, 1, e->da, true, att_q));
+    // o residual (no layer scalar), then the pre-MLP norm (rounded)
+    k_resid_norm_q<<<1, 256, 0, e->st>>>(e->da, e->dx, t.post_attn, 0.0f, H, t.pre_ff, e->da, 1, qo);
+    RCK(lin(e, t.gu, e->da, 1, e->dgu, true, true));
+    k_act_q<<<(unsigned)(d.I / 256), 256, 0, e->st>>>(e->dgu, d.I, 1, e->dact, qo);
+    RCK(lin(e, t.down, e->dact, 1, e->da, true, true));
+    // MLP residual with the layer scalar 1, then the next layer's input norm or the final norm
+    if (l + 1 < d.DL)
+      k_resid_norm_q<<<1, 256, 0, e->st>>>(e->da, e->dx, t.post_ff, 1.0f, H, e->DL[l + 1].in_ln, e->da, 0, qo);
+    else
+      k_resid_norm_q<<<1, 256, 0, e->st>>>(e->da, e->dx, t.post_ff, 1.0f, H, e->dnorm, e->dh, 1, qo);
     RCK(check_launch("draft layer"));
   }
-  k_rmsnorm<<<1, 256, 0, e->st>>>(e->dx, e->dnorm, H, e->dh, 1);
-  RCK(lin(e, e->dpost, e->dh, 1, e->bcur, true));
-  RCK(lin(e, e->dcent, e->dh, 1, e->dscore, true));
+  RCK(lin(e, e->dpost, e->dh, 1, e->bcur, true, true));
+  RCK(lin(e, e->dcent, e->dh, 1, e->dscore, true, true));
   k_round<<<gridfor(H), 256, 0, e->st>>>(e->bcur, H);
   const int nc = d.DTOP * d.DPER;
-  k_topk_cand<<<1, 1024, sizeof(float) * d.DCENT, e->st>>>(e->dscore, d.DCENT, d.DTOP, d.DPER, d.V, e->cand);
+  k_topk_cand<<<(d.DCENT + 31) / 32, 256, sizeof(float) * d.DCENT, e->st>>>(e->dscore, d.DCENT, d.DTOP, d.DPER, d.V, e->cand);
   k_cand_scores<<<(nc * 16 + 255) / 256, 256, 0, e->st>>>(e->E, e->cand, nc, e->dh, H, e->cscore);
   k_cand_best<<<1, 1024, 0, e->st>>>(e->cscore, e->cand, nc, dtok_out);
   e->prof.mark(e->st, PH_COPY);

@@ -215,6 +215,127 @@ __global__ void __launch_bounds__(256) k_bf16p_gemv(HeadPacked P, const float* _
   }
 }
 
+// Staged variant for K % 256 == 0 and K <= 2048 (the head widths of this model): a persistent
+// grid, one CTA per SM, takes blocks of 32 rows in turn.  Each block's 32 packed rows arrive in
+// shared memory by one bulk copy per row (issued by the lanes of warp 0), double-buffered against
+// the previous block's arithmetic; rows sit 16 bytes further apart than in memory so that the four
+// octets of a warp (four rows) read different banks.  The activations sit in shared memory as
+// (row m, row m+1) pairs so
+// that each decoded weight feeds two rows per packed f32x2 FMA.  Every octet lane runs exactly
+// the chains of bf16p_lane_dot (per row m: elements j, 16+j, 8+j, 24+j of each group in group
+// order), so the logits are those of k_bf16p_gemv.
+constexpr int kHeadBlkRows = 32;
+__host__ __device__ inline int head_row_stride(int K) { return (K / 32) * 44 + 16; }
+__host__ __device__ inline size_t head_stage_bytes(int K) { return (size_t)kHeadBlkRows * head_row_stride(K); }
+__host__ __device__ inline size_t head_smem_bytes(int M, int K) {
+  return 128 + (size_t)((M + 1) / 2) * K * 8 + 2 * head_stage_bytes(K);
+}
+
+template <int M>
+__global__ void __launch_bounds__(256) k_bf16p_gemv_staged(HeadPacked P, const float* __restrict__ X,
+                                                           float* __restrict__ Y, int ldy,
+                                                           const int* __restrict__ gate) {
+  constexpr int NP = (M + 1) / 2;
+  if (gate != nullptr && *gate == 0) return;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  const int K = P.K, G = K >> 5;
+  float2* xs = reinterpret_cast<float2*>(smem + 128);  // [NP][K]
+  uint8_t* stage = smem + 128 + (size_t)NP * K * 8;
+  const size_t sbytes = head_stage_bytes(K);
+  const int nblk = (P.N + kHeadBlkRows - 1) / kHeadBlkRows;
+  const int rowb = G * 44, rs = head_row_stride(K);
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int blk, int s) {  // warp 0, all lanes
+    const int lane = threadIdx.x & 31;
+    const int r0 = blk * kHeadBlkRows, nr = min(kHeadBlkRows, P.N - r0);
+    if (lane == 0) mbar_expect_tx(&bars[s], (uint32_t)nr * rowb);
+    __syncwarp();
+    if (lane < nr)
+      bulk_g2s(stage + s * sbytes + (size_t)lane * rs, P.data + (size_t)(r0 + lane) * rowb, (uint32_t)rowb, &bars[s]);
+  };
+  if (threadIdx.x < 32) {
+    if ((int)blockIdx.x < nblk) issue(blockIdx.x, 0);
+    if ((int)(blockIdx.x + gridDim.x) < nblk) issue(blockIdx.x + gridDim.x, 1);
+  }
+  for (int i = threadIdx.x; i < NP * K; i += blockDim.x) {
+    const int p = i / K, k = i % K;
+    const float a = X[(size_t)(2 * p) * K + k];
+    const float b = (2 * p + 1 < M) ? X[(size_t)(2 * p + 1) * K + k] : 0.f;
+    xs[i] = make_float2(a, b);
+  }
+  __syncthreads();
+  const int j = threadIdx.x & 7, rl = threadIdx.x >> 3;  // octet lane, row in block
+  const uint32_t cb_lo = P.cb_lo, cb_hi = P.cb_hi;
+  int it = 0;
+  for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x, ++it) {
+    const int s = it & 1;
+    if (!cta_wait(&bars[s], (uint32_t)(it >> 1) & 1u)) return;
+    const int n = blk * kHeadBlkRows + rl;
+    const bool live = n < P.N;
+    const uint8_t* row = stage + s * sbytes + (size_t)(live ? rl : 0) * rs;
+    float2 acc[NP];
+#pragma unroll
+    for (int p = 0; p < NP; ++p) acc[p] = make_float2(0.f, 0.f);
+#pragma unroll 2
+    for (int g = 0; g < G; ++g) {
+      const uint8_t* gp = row + g * 44;
+      const uint32_t* pw = reinterpret_cast<const uint32_t*>(gp + 32);
+      // exponent codes of elements j, 8+j, 16+j, 24+j sit at bits j, j+8, j+16, j+24 of the planes
+      const uint32_t c = ((pw[0] >> j) & 0x01010101u) | (((pw[1] >> j) & 0x01010101u) << 1) |
+                         (((pw[2] >> j) & 0x01010101u) << 2);
+      const uint32_t sel = (c & 7u) | ((c >> 4) & 0x70u) | ((c >> 8) & 0x700u) | ((c >> 12) & 0x7000u);
+      const uint32_t ex4 = __byte_perm(cb_lo, cb_hi, sel);  // exponent of element j + 8i in byte i
+      float w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t sm = gp[j + 8 * i];
+        const uint32_t ex = (ex4 >> (8 * i)) & 0xFFu;
+        w[i] = __uint_as_float((((sm & 0x80u) << 8) | (ex << 7) | (sm & 0x7Fu)) << 16);
+      }
+      const float2* xg = xs + g * 32 + j;
+      // chain order of bf16p_lane_dot: elements j, 16+j, 8+j, 24+j
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        const float2* xp = xg + (size_t)p * K;
+        acc[p] = __ffma2_rn(make_float2(w[0], w[0]), xp[0], acc[p]);
+        acc[p] = __ffma2_rn(make_float2(w[2], w[2]), xp[16], acc[p]);
+        acc[p] = __ffma2_rn(make_float2(w[1], w[1]), xp[8], acc[p]);
+        acc[p] = __ffma2_rn(make_float2(w[3], w[3]), xp[24], acc[p]);
+      }
+    }
+    float y[M];
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      y[2 * p] = hsum8_octet(acc[p].x);
+      if (2 * p + 1 < M) y[2 * p + 1] = hsum8_octet(acc[p].y);
+    }
+    if (live && j == 0) {
+      for (long long e = P.exc_ptr[n]; e < P.exc_ptr[n + 1]; ++e) {  // CSR order, unfused (bf16_exp3_head.h:103)
+        const float dl = P.exc_delta[e];
+        const int col = P.exc_col[e];
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          const float2 xv = xs[(size_t)(m >> 1) * K + col];
+          y[m] = __fadd_rn(y[m], __fmul_rn(dl, (m & 1) ? xv.y : xv.x));
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) Y[(size_t)m * ldy + n] = y[m];
+    }
+    __syncthreads();  // every octet is done with this stage
+    if (threadIdx.x < 32 && blk + 2 * (int)gridDim.x < nblk) {
+      fence_proxy_async_smem();  // this stage's reads happen before the next bulk copies rewrite it
+      issue(blk + 2 * gridDim.x, s);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------ greedy pick
 // Slots per row m: [0] ordered-int max of r16 logits, [1] winner index.
 __global__ void k_pick_init(int* __restrict__ slots, int M) {
@@ -540,9 +661,26 @@ static HeadPacked make_head(const uint8_t* data, const uint8_t* cb8, const long 
   return P;
 }
 
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
+
 template <int M>
 static void launch_head_gemv(const HeadPacked& P, const float* X, float* Y, int ldy, const int* gate, cudaStream_t st) {
-  k_bf16p_gemv<M><<<(P.N + 31) / 32, 256, 0, st>>>(P, X, Y, ldy, gate);
+  const size_t smem = head_smem_bytes(M, P.K);
+  if (P.K % 256 == 0 && smem <= 227 * 1024 && aligned(P.data, 16)) {
+    cudaFuncSetAttribute(k_bf16p_gemv_staged<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int nblk = (P.N + kHeadBlkRows - 1) / kHeadBlkRows;
+    k_bf16p_gemv_staged<M><<<std::min(nblk, num_sms()), 256, smem, st>>>(P, X, Y, ldy, gate);
+  } else {
+    k_bf16p_gemv<M><<<(P.N + 31) / 32, 256, 0, st>>>(P, X, Y, ldy, gate);
+  }
 }
 static int head_gemv(const HeadPacked& P, const float* X, int M, float* Y, int ldy, const int* gate, cudaStream_t st) {
   switch (M) {

@@ -13,7 +13,15 @@ namespace g4 {
 __device__ float block_rms_scale(const float* __restrict__ x, int n, double* red) {
   if (threadIdx.x < 16) {
     double s = 0;
-    for (int i = 0; i < n; i += 16) { const double d = x[i + threadIdx.x]; s = fma(d, d, s); }
+    int i = 0;
+    for (; i + 128 <= n; i += 128) {  // 8 loads in flight, then the chain in element order
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = x[i + 16 * u + threadIdx.x];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) { const double d = v[u]; s = fma(d, d, s); }
+    }
+    for (; i < n; i += 16) { const double d = x[i + threadIdx.x]; s = fma(d, d, s); }
     red[threadIdx.x] = s;
   }
   __syncthreads();
@@ -28,6 +36,17 @@ __device__ float block_rms_scale(const float* __restrict__ x, int n, double* red
   __syncthreads();
   return r;
 }
+
+// Copy a row into shared memory (float4 when n % 4 == 0 and both ends are 16-byte aligned).
+__device__ __forceinline__ void stage_row(float* dst, const float* __restrict__ src, int n) {
+  if ((n & 3) == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+    for (int i = threadIdx.x; i < (n >> 2); i += blockDim.x)
+      reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
 
 // y[m] = (x[m]*r)*w, optionally rounded to bf16 (rms / rms_prep_x, :344-352, :365-381).
 __global__ void k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w, int n, float* __restrict__ y, int round) {
@@ -52,18 +71,22 @@ __global__ void k_embed(const uint16_t* __restrict__ E, const int* __restrict__ 
 // head `part`: rms_r16 with q_norm, then RoPE (fp32, not rounded); part == nq is k: rms_r16 with
 // k_norm, RoPE, bf16 store at cache position pos0+m; part == nq+1 is v: rms_r16 without weight,
 // bf16 store.  RoPE (rope_avx2 :394-402): h[j] = fma(u, c, -(w*s)), h[j+hd/2] = fma(w, c, u*s).
-__global__ void k_qkv_post(float* __restrict__ qkv, int ldqkv, int nq, int hd, int pos0, const int* __restrict__ dpos,
-                           const float* __restrict__ qn, const float* __restrict__ kn, const float* __restrict__ cosT,
-                           const float* __restrict__ sinT, uint16_t* __restrict__ Kc, uint16_t* __restrict__ Vc) {
+__global__ void k_qkv_post(const float* __restrict__ qkv, int ldqkv, int nq, int hd, int pos0,
+                           const int* __restrict__ dpos, const float* __restrict__ qn, const float* __restrict__ kn,
+                           const float* __restrict__ cosT, const float* __restrict__ sinT, uint16_t* __restrict__ Kc,
+                           uint16_t* __restrict__ Vc, float* __restrict__ qdst, int ldq) {
   __shared__ double red[17];
-  __shared__ float hbuf[512];
+  __shared__ __align__(16) float hbuf[512];
   if (dpos) pos0 += *dpos;  // position read on the device (captured decode steps)
   const int m = blockIdx.x, part = blockIdx.y, pos = pos0 + m, hh = hd >> 1;
-  float* src = qkv + (size_t)m * ldqkv + (size_t)part * hd;  // q heads, then k, then v
+  const float* src = qkv + (size_t)m * ldqkv + (size_t)part * hd;  // q heads, then k, then v
+  float* dst = qdst + (size_t)m * ldq + (size_t)part * hd;
   const float* w = part < nq ? qn : (part == nq ? kn : nullptr);
-  const float r = block_rms_scale(src, hd, red);
+  stage_row(hbuf, src, hd);
+  __syncthreads();
+  const float r = block_rms_scale(hbuf, hd, red);
   for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-    const float v = w ? __fmul_rn(__fmul_rn(src[i], r), w[i]) : __fmul_rn(src[i], r);
+    const float v = w ? __fmul_rn(__fmul_rn(hbuf[i], r), w[i]) : __fmul_rn(hbuf[i], r);
     hbuf[i] = r16(v);
   }
   __syncthreads();
@@ -81,8 +104,8 @@ __global__ void k_qkv_post(float* __restrict__ qkv, int ldqkv, int nq, int hd, i
       Kc[(size_t)pos * hd + j] = (uint16_t)f2bf(a);
       Kc[(size_t)pos * hd + j + hh] = (uint16_t)f2bf(b);
     } else {
-      src[j] = a;
-      src[j + hh] = b;
+      dst[j] = a;
+      dst[j + hh] = b;
     }
   }
 }
@@ -92,12 +115,14 @@ __global__ void k_qkv_post(float* __restrict__ qkv, int ldqkv, int nq, int hd, i
 __global__ void k_q_post(float* __restrict__ q, int hd, int pos, const int* __restrict__ dpos, const float* __restrict__ qn,
                          const float* __restrict__ cosT, const float* __restrict__ sinT) {
   __shared__ double red[17];
-  __shared__ float hbuf[512];
+  __shared__ __align__(16) float hbuf[512];
   if (dpos) pos += *dpos;
   const int h = blockIdx.x, hh = hd >> 1;
   float* src = q + (size_t)h * hd;
-  const float r = block_rms_scale(src, hd, red);
-  for (int i = threadIdx.x; i < hd; i += blockDim.x) hbuf[i] = r16(__fmul_rn(__fmul_rn(src[i], r), qn[i]));
+  stage_row(hbuf, src, hd);
+  __syncthreads();
+  const float r = block_rms_scale(hbuf, hd, red);
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) hbuf[i] = r16(__fmul_rn(__fmul_rn(hbuf[i], r), qn[i]));
   __syncthreads();
   const float* cs = cosT + (size_t)pos * hh;
   const float* sn = sinT + (size_t)pos * hh;
@@ -156,6 +181,148 @@ __global__ void k_resid_norm(float* __restrict__ o, float* __restrict__ x, const
   __syncthreads();
   const float r = block_rms_scale(o, n, red);
   for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = r16(__fadd_rn(x[i], r16(__fmul_rn(__fmul_rn(o[i], r), w[i]))));
+}
+
+// ---- fused row kernels: one block (256 threads) per activation row.  The row is first staged in
+// shared memory (one coalesced pass), so the RMS partial sums run from shared memory; each kernel
+// then writes its float outputs and, when qo.q is set, the W4A8 quantisation of the row that the
+// next linear consumes (quant_group32 per 32-group, identical to g4_w4a8_quant).  They replace
+// norm -> quantise pairs of launches with one and compute the same values as the unfused kernels.
+constexpr int kRowMax = 2048;
+
+// quantise row ys (shared memory, n % 32 == 0) into row m of qo (row length n); needs a barrier
+// between the writes of ys and this call
+__device__ __forceinline__ void quant_row(const float* ys, int n, int m, const QuantOut& qo) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5, G = n >> 5;
+  for (int g = w; g < G; g += nw) {
+    int8_t qv;
+    float sx;
+    int32_t tot;
+    quant_group32(ys[g * 32 + lane], qv, sx, tot);
+    qo.q[(size_t)m * n + g * 32 + lane] = qv;
+    if (lane == 0) {
+      qo.sx[(size_t)m * G + g] = sx;
+      qo.sum[(size_t)m * G + g] = tot;
+    }
+  }
+}
+
+// y[m] = (x[m]*r)*w, optionally rounded to bf16 (rms / rms_prep_x, :344-352, :365-381).
+__global__ void __launch_bounds__(256) k_norm_q(const float* __restrict__ x, const float* __restrict__ w, int n,
+                                                float* __restrict__ y, int round, QuantOut qo) {
+  __shared__ __align__(16) float xs[kRowMax];
+  __shared__ double red[17];
+  const int m = blockIdx.x;
+  stage_row(xs, x + (size_t)m * n, n);
+  __syncthreads();
+  const float r = block_rms_scale(xs, n, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = __fmul_rn(__fmul_rn(xs[i], r), w[i]);
+    if (round) v = r16(v);
+    y[(size_t)m * n + i] = v;
+    xs[i] = v;
+  }
+  if (qo.q) {
+    __syncthreads();
+    quant_row(xs, n, m, qo);
+  }
+}
+
+// k_post_attn with the pre-MLP input quantised: o = r16(o); x = r16(x + r16((o*r)*w_post));
+// mlp_in = r16((x*r')*w_pre).
+__global__ void __launch_bounds__(256) k_post_attn_q(const float* __restrict__ o, float* __restrict__ x,
+                                                     const float* __restrict__ w_post, const float* __restrict__ w_pre,
+                                                     float* __restrict__ mlp_in, int n, QuantOut qo) {
+  __shared__ __align__(16) float os[kRowMax];
+  __shared__ __align__(16) float xs[kRowMax];
+  __shared__ double red[17];
+  const int m = blockIdx.x;
+  float* xm = x + (size_t)m * n;
+  stage_row(os, o + (size_t)m * n, n);
+  stage_row(xs, xm, n);
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) os[i] = r16(os[i]);
+  __syncthreads();
+  const float r = block_rms_scale(os, n, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = r16(__fadd_rn(xs[i], r16(__fmul_rn(__fmul_rn(os[i], r), w_post[i]))));
+    xs[i] = v;
+    xm[i] = v;
+  }
+  __syncthreads();
+  const float r2 = block_rms_scale(xs, n, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = r16(__fmul_rn(__fmul_rn(xs[i], r2), w_pre[i]));
+    mlp_in[(size_t)m * n + i] = v;
+    os[i] = v;
+  }
+  if (qo.q) {
+    __syncthreads();
+    quant_row(os, n, m, qo);
+  }
+}
+
+// Residual after the MLP (or the drafter's attention / MLP), then the next norm:
+//   o = r16(o); x = r16(x + r16((o*r)*w_post)); if (scalar != 0) x = r16(x*scalar)
+//   (k_post_ff / k_resid_norm + k_scale_round); then, when w_next is set,
+//   a = (x*r')*w_next (rounded when round_next) and its quantisation.
+__global__ void __launch_bounds__(256) k_resid_norm_q(const float* __restrict__ o, float* __restrict__ x,
+                                                      const float* __restrict__ w_post, float scalar, int n,
+                                                      const float* __restrict__ w_next, float* __restrict__ a,
+                                                      int round_next, QuantOut qo) {
+  __shared__ __align__(16) float os[kRowMax];
+  __shared__ __align__(16) float xs[kRowMax];
+  __shared__ double red[17];
+  const int m = blockIdx.x;
+  float* xm = x + (size_t)m * n;
+  stage_row(os, o + (size_t)m * n, n);
+  stage_row(xs, xm, n);
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) os[i] = r16(os[i]);
+  __syncthreads();
+  const float r = block_rms_scale(os, n, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = r16(__fadd_rn(xs[i], r16(__fmul_rn(__fmul_rn(os[i], r), w_post[i]))));
+    if (scalar != 0.f) v = r16(__fmul_rn(v, scalar));
+    xs[i] = v;
+    xm[i] = v;
+  }
+  if (w_next == nullptr) return;
+  __syncthreads();
+  const float r2 = block_rms_scale(xs, n, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = __fmul_rn(__fmul_rn(xs[i], r2), w_next[i]);
+    if (round_next) v = r16(v);
+    a[(size_t)m * n + i] = v;
+    os[i] = v;
+  }
+  if (qo.q) {
+    __syncthreads();
+    quant_row(os, n, m, qo);
+  }
+}
+
+// GeGLU with the down-projection input quantised: one warp per 32-group of a row (I % 32 == 0,
+// blockDim 256, grid M*I/256).
+__global__ void __launch_bounds__(256) k_act_q(const float* __restrict__ gu, int I, int M, float* __restrict__ act,
+                                               QuantOut qo) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)M * I) return;  // warp-uniform (M*I is a multiple of 32)
+  const int m = (int)(idx / I), i = (int)(idx % I);
+  const float g = r16(gu[(size_t)m * 2 * I + i]), u = r16(gu[(size_t)m * 2 * I + I + i]);
+  const float v = r16(__fmul_rn(r16(gelu(g)), u));
+  act[idx] = v;
+  if (qo.q) {
+    int8_t qv;
+    float sx;
+    int32_t tot;
+    quant_group32(v, qv, sx, tot);
+    qo.q[idx] = qv;
+    if ((threadIdx.x & 31) == 0) {
+      qo.sx[idx >> 5] = sx;
+      qo.sum[idx >> 5] = tot;
+    }
+  }
 }
 
 // elementwise helpers
@@ -266,22 +433,41 @@ __global__ void k_cand_scores(const uint16_t* __restrict__ E, const int* __restr
   const int k = min(hw, nc - 1);
   const uint16_t* er = E + (size_t)cand[k] * H;
   float acc = 0.f;
-  for (int i = c; i < H; i += 16) acc = fmaf(dh[i], bf2f(er[i]), acc);
+#pragma unroll 16
+  for (int i = c; i < H; i += 16) acc = fmaf(__ldg(dh + i), bf2f(__ldg(er + i)), acc);
   const float s = hsum8_octet(__fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8)));
   if (c == 0 && hw < nc) score[hw] = s;
 }
 // Top-T centroids by score (stable: ties keep the lower centroid first, as the insertion sort of
 // :1554-1555 does) and the candidate list cand[t*per + j] = perm((top t)*per + j).
-__global__ void k_topk_cand(const float* __restrict__ score, int n, int T, int per, int vocab, int* __restrict__ cand) {
+__global__ void __launch_bounds__(256) k_topk_cand(const float* __restrict__ score, int n, int T, int per, int vocab,
+                                                   int* __restrict__ cand) {
+  // block of 32 scores (one per lane); the 8 warps each count the higher-ranked scores in one
+  // eighth of the list, and the partial ranks are summed (rank = #(s_j > v) + #(s_j == v, j < i))
   extern __shared__ float s[];
+  __shared__ int part[8][32];
   for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = score[i];
   __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = s[i];
-    int rank = 0;
-    for (int j = 0; j < n; ++j) rank += (s[j] > v) || (s[j] == v && j < i);
-    if (rank < T)
-      for (int k = 0; k < per; ++k) cand[rank * per + k] = (int)perm_token((uint32_t)(i * per + k), (uint32_t)vocab);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int i = blockIdx.x * 32 + lane;
+  const float v = i < n ? s[i] : 0.f;
+  const int span = (n + 7) / 8, j0 = w * span, j1 = min(n, j0 + span);
+  int rank = 0;
+#pragma unroll 8
+  for (int j = j0; j < j1; ++j) rank += (s[j] > v) || (s[j] == v && j < i);
+  part[w][lane] = rank;
+  __syncthreads();
+  __shared__ int rk[32];
+  if (w == 0) {
+    int r = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) r += part[k][lane];
+    rk[lane] = (i < n) ? r : 0x7FFFFFFF;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < 32 * per; e += blockDim.x) {
+    const int l = e / per, k = e % per, r = rk[l];
+    if (r < T) cand[r * per + k] = (int)perm_token((uint32_t)((blockIdx.x * 32 + l) * per + k), (uint32_t)vocab);
   }
 }
 // first argmax in candidate order -> *best (one block)

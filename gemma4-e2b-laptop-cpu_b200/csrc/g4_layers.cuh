@@ -7,13 +7,23 @@ namespace g4 {
 __global__ void k_rmsnorm(const float* x, const float* w, int n, float* y, int round);
 __global__ void k_embed(const uint16_t* E, const int* toks, int H, float sqrtH, float* x);
 // dpos (device, may be NULL) is added to the position argument: pos0 / pos is then an offset.
-__global__ void k_qkv_post(float* qkv, int ldqkv, int nq, int hd, int pos0, const int* dpos, const float* qn,
-                           const float* kn, const float* cosT, const float* sinT, uint16_t* Kc, uint16_t* Vc);
+// The rotated query heads go to qdst (row m at qdst + m*ldq; qdst = qkv, ldq = ldqkv for in place).
+__global__ void k_qkv_post(const float* qkv, int ldqkv, int nq, int hd, int pos0, const int* dpos, const float* qn,
+                           const float* kn, const float* cosT, const float* sinT, uint16_t* Kc, uint16_t* Vc,
+                           float* qdst, int ldq);
 __global__ void k_q_post(float* q, int hd, int pos, const int* dpos, const float* qn, const float* cosT, const float* sinT);
 __global__ void k_post_attn(float* o, float* x, const float* w_post, const float* w_pre, float* mlp_in, int n);
 __global__ void k_post_ff(float* o, float* x, const float* w_post, float scalar, int n);
 __global__ void k_act(const float* gu, int I, int M, float* act);
 __global__ void k_resid_norm(float* o, float* x, const float* w, int n);
+// Fused row kernels (one 256-thread block per row, rows up to kRowMax = 2048 wide) that also
+// quantise their output for the next W4A8 linear when qo.q is set.
+__global__ void k_norm_q(const float* x, const float* w, int n, float* y, int round, QuantOut qo);
+__global__ void k_post_attn_q(const float* o, float* x, const float* w_post, const float* w_pre, float* mlp_in, int n,
+                              QuantOut qo);
+__global__ void k_resid_norm_q(const float* o, float* x, const float* w_post, float scalar, int n, const float* w_next,
+                               float* a, int round_next, QuantOut qo);
+__global__ void k_act_q(const float* gu, int I, int M, float* act, QuantOut qo);
 __global__ void k_round(float* p, long long n);
 __global__ void k_scale_round(float* p, long long n, float s);
 __global__ void k_draft_in(const uint16_t* E, const int* tok, const float* h, int H, float sqrtH, float* out);

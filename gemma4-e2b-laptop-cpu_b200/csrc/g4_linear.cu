@@ -212,19 +212,11 @@ __global__ void k_w4a8_quant(const float* __restrict__ X, int MG, int G, int8_t*
   const int lane = threadIdx.x & 31;
   if (wid >= MG) return;
   const size_t base = (size_t)wid * 32;  // [m][K] with K = 32G: group wid starts at 32*wid
-  const float x = X[base + lane];
-  float amax = fabsf(x);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, o));
-  const float s = __fdiv_rn(amax, 127.0f);
-  const float inv = s > 0.f ? __fdiv_rn(1.0f, s) : 0.0f;
-  const float v = __fmul_rn(x, inv);
-  const int32_t r = (v > -2147483648.f && v < 2147483648.f) ? __float2int_rn(v) : INT32_MIN;
-  int32_t tot = r;
-#pragma unroll
-  for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(FULL, tot, o);
-  const int32_t r16 = r < -32768 ? -32768 : (r > 32767 ? 32767 : r);
-  q[base + lane] = (int8_t)(r16 < -128 ? -128 : (r16 > 127 ? 127 : r16));
+  int8_t qv;
+  float s;
+  int32_t tot;
+  quant_group32(X[base + lane], qv, s, tot);
+  q[base + lane] = qv;
   if (lane == 0) { sx[wid] = s; sum[wid] = tot; }
   (void)G;
 }
@@ -340,6 +332,99 @@ k_w4a8(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const int
   }
 }
 
+// W4A8 GEMV, whole-block variant: a CTA requests all of its ROWS weight rows (every chunk, one
+// mbarrier per chunk) and their scales at once, so that the whole matrix is in flight across the
+// grid; phase 1 turns each chunk into (a32, sw*sx) pairs as it lands, kept for every group of the
+// row in shared memory; phase 2 runs the ROWS*M fp32 chains over all groups in order.  The values
+// are those of k_w4a8 (same integer dot, same product, same chain order).
+template <int M, int ROWS, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
+k_w4a8_all(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const int8_t* __restrict__ q,
+           const float* __restrict__ sx, const int32_t* __restrict__ sum, int N, int K, float* __restrict__ Y, int ldy,
+           int CH) {
+  constexpr int T = WARPS * 32;
+  const int G = K >> 5, nchunk = G / CH;
+  const int wrs = (K >> 1) + 16;  // shared-memory row stride (16 B of padding against bank conflicts)
+  const int acs = G + 1;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);  // [nchunk] (<= 16)
+  uint8_t* wbuf = smem + 128;
+  uint16_t* sc = reinterpret_cast<uint16_t*>(wbuf + (size_t)ROWS * wrs);
+  float2* ac = reinterpret_cast<float2*>(sc + (size_t)ROWS * G);  // [ROWS*M][G+1]
+  const int n0 = blockIdx.x * ROWS;
+  const int nvalid = min(ROWS, N - n0);
+
+  if (threadIdx.x == 0) {
+    for (int c = 0; c < nchunk; ++c) mbar_init(&bars[c], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {  // warp 0: lane r issues row r's copies
+    const int lane = threadIdx.x;
+    const uint32_t wbytes = (uint32_t)CH * 16;
+    if (lane == 0)
+      for (int c = 0; c < nchunk; ++c) mbar_expect_tx(&bars[c], nvalid * wbytes + (c == 0 ? (uint32_t)nvalid * G * 2 : 0u));
+    __syncwarp();
+    for (int r = lane; r < nvalid; r += 32)
+      for (int c = 0; c < nchunk; ++c)
+        bulk_g2s(wbuf + (size_t)r * wrs + (size_t)c * wbytes, Wp + (size_t)(n0 + r) * (K >> 1) + (size_t)c * wbytes, wbytes,
+                 &bars[c]);
+    if (lane == 0) bulk_g2s(sc, S + (size_t)n0 * G, (uint32_t)nvalid * G * 2, &bars[0]);
+  }
+  for (int c = 0; c < nchunk; ++c) {
+    if (!cta_wait(&bars[c], 0)) return;
+    for (int gl = threadIdx.x; gl < CH; gl += T) {
+      const int g = c * CH + gl;
+      int4 qa[M], qb[M];
+      int bias[M];
+      float sxm[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const int4* qp = reinterpret_cast<const int4*>(q + (size_t)m * K + (size_t)g * 32);
+        qa[m] = __ldg(qp);
+        qb[m] = __ldg(qp + 1);
+        bias[m] = -8 * __ldg(sum + (size_t)m * G + g);
+        sxm[m] = __ldg(sx + (size_t)m * G + g);
+      }
+#pragma unroll 2
+      for (int r = 0; r < ROWS; ++r) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(wbuf + (size_t)r * wrs + (size_t)g * 16);
+        const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { lo[k] = w4[k] & 0x0F0F0F0Fu; hi[k] = (w4[k] >> 4) & 0x0F0F0F0Fu; }
+        const float sw = bf2f(sc[(size_t)r * G + g]);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          int acc = bias[m];
+          acc = __dp4a((int)lo[0], qa[m].x, acc);
+          acc = __dp4a((int)lo[1], qa[m].y, acc);
+          acc = __dp4a((int)lo[2], qa[m].z, acc);
+          acc = __dp4a((int)lo[3], qa[m].w, acc);
+          acc = __dp4a((int)hi[0], qb[m].x, acc);
+          acc = __dp4a((int)hi[1], qb[m].y, acc);
+          acc = __dp4a((int)hi[2], qb[m].z, acc);
+          acc = __dp4a((int)hi[3], qb[m].w, acc);
+          ac[(size_t)(r * M + m) * acs + g] = make_float2((float)acc, __fmul_rn(sw, sxm[m]));
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int ci = threadIdx.x;  // chain (row, activation row) = (ci / M, ci % M); T >= ROWS*M
+  if (ci < ROWS * M) {
+    const int cr = ci / M, cm = ci % M;
+    const float2* a = ac + (size_t)ci * acs;
+    float row = 0.f;
+#pragma unroll 8
+    for (int g = 0; g < G; ++g) {
+      const float2 v = a[g];
+      row = fmaf(v.x, v.y, row);
+    }
+    if (cr < nvalid) Y[(size_t)cm * ldy + n0 + cr] = row;
+  }
+}
+
 }  // namespace g4
 
 G4_STATUS_READER(linear)
@@ -442,9 +527,39 @@ static int launch_w4a8_t(const uint8_t* Wp, const uint16_t* S, const int8_t* q, 
   return check_launch("k_w4a8");
 }
 
+static size_t w4a8_all_smem(int M, int rows, int K) {
+  const int G = K / 32;
+  return 128 + (size_t)rows * (K / 2 + 16) + (size_t)rows * G * 2 + (size_t)rows * M * (G + 1) * 8;
+}
+
+template <int M, int ROWS, int WARPS>
+static int launch_w4a8_all_t(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
+                             int N, int K, float* Y, int ldy, int CH, cudaStream_t st) {
+  const size_t smem = w4a8_all_smem(M, ROWS, K);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k_w4a8_all<M, ROWS, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_w4a8_all<M, ROWS, WARPS><<<(N + ROWS - 1) / ROWS, WARPS * 32, smem, st>>>(Wp, S, q, sx, sum, N, K, Y, ldy, CH);
+  return check_launch("k_w4a8_all");
+}
+
 template <int M>
 static int launch_w4a8(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
                        int N, int K, float* Y, int ldy, cudaStream_t st) {
+  // whole-block variant (all rows of a CTA in flight at once) when its shared memory fits;
+  // 16 rows per CTA for the widest matrices, threads >= chains
+  int AR = (N >= 8192 && M <= 4) ? 16 : 8, AW = 2;
+  if (const char* e = getenv("G4_W4A8_ALL")) sscanf(e, "%d,%d", &AR, &AW);
+  if (AR != 16) AR = AR > 0 ? 8 : 0;
+  if (AW != 4) AW = 2;
+  if (AW * 32 < AR * M) AW = 4;
+  const int G = K / 32, ACH = pick_ch(G);
+  if (AR > 0 && AW * 32 >= AR * M && G / ACH <= 16 && w4a8_all_smem(M, AR, K) <= 200 * 1024) {
+    if (AR == 16) {
+      if (AW == 4) return launch_w4a8_all_t<M, 16, 4>(Wp, S, q, sx, sum, N, K, Y, ldy, ACH, st);
+      return launch_w4a8_all_t<M, 16, 2>(Wp, S, q, sx, sum, N, K, Y, ldy, ACH, st);
+    }
+    if (AW == 4) return launch_w4a8_all_t<M, 8, 4>(Wp, S, q, sx, sum, N, K, Y, ldy, ACH, st);
+    return launch_w4a8_all_t<M, 8, 2>(Wp, S, q, sx, sum, N, K, Y, ldy, ACH, st);
+  }
   int WARPS = 2, CH = pick_ch(K / 32), NB = 3;
   if (const char* e = getenv("G4_W4A8_CFG")) sscanf(e, "%d,%d,%d", &WARPS, &CH, &NB);
   if (WARPS == 1) return launch_w4a8_t<M, 1>(Wp, S, q, sx, sum, N, K, Y, ldy, CH, NB, st);

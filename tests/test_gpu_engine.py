@@ -124,3 +124,19 @@ def test_fake_context_generate_matches_oracle():
     finally:
         eng.close()
         om.close()
+
+
+def test_generate_cfg4_golden():
+    """configs[4] at full size: the seeded 6,841-token prompt, 256 greedy tokens, against the
+    oracle's tokens and round statistics stored by tests/golden/make_golden_e2e.py."""
+    import pathlib
+    d = np.load(pathlib.Path(__file__).resolve().parent / "golden" / "e2e_cfg4.npz")
+    eng = g4.Engine(g4.engine_config())
+    try:
+        assert eng.cfg.seed == int(d["seed"])
+        toks, st = eng.generate(d["prompt"], 256)
+        assert list(toks) == list(d["tokens"])
+        assert (st["rounds"], st["ngram_rounds"], st["accepted"]) == (int(d["rounds"]), int(d["ngram_rounds"]),
+                                                                       int(d["accepted"]))
+    finally:
+        eng.close()
