@@ -273,34 +273,38 @@ __global__ void __launch_bounds__(64) k_attn_accum(const uint16_t* __restrict__ 
 // product exact); out = r16((sum_t fma(O_t, sc_t)) * (float)(1/l)).  The per-chunk factors are
 // computed once per block.
 __global__ void __launch_bounds__(512) k_attn_merge(AttnDesc d0, const float* __restrict__ ws, float* __restrict__ out) {
+  __shared__ float sc[64], al[64];
+  __shared__ float inv_l, s_m0;
   const AttnDesc d = resolve(d0);
-  __shared__ float sc[64];
-  __shared__ float inv_l;
   const AttnWs w = attn_ws(const_cast<float*>(ws), d);
   const int mh = blockIdx.x, i = threadIdx.x, nmh = d.M * d.nh;
+  // chunk factors: maxima and sums loaded in parallel, M0 and l (in chunk order) by thread 0
+  if (i < d.T) {
+    const size_t ix = (size_t)i * nmh + mh;
+    al[i] = w.AL[ix];
+    sc[i] = al[i] > 0 ? w.AM[ix] : -1e30f;
+  }
+  __syncthreads();
   if (i == 0) {
     float M0 = -1e30f;
-    for (int t = 0; t < d.T; ++t) {
-      const size_t ix = (size_t)t * nmh + mh;
-      if (w.AL[ix] > 0) M0 = fmaxf(M0, w.AM[ix]);
-    }
+    for (int t = 0; t < d.T; ++t) M0 = fmaxf(M0, sc[t]);
+    s_m0 = M0;
+  }
+  __syncthreads();
+  if (i < d.T) sc[i] = al[i] > 0 ? exp_cr(__fsub_rn(sc[i], s_m0)) : 0.f;
+  __syncthreads();
+  if (i == 0) {
     double l = 0;
-    for (int t = 0; t < d.T; ++t) {
-      const size_t ix = (size_t)t * nmh + mh;
-      sc[t] = 0.f;
-      if (!(w.AL[ix] > 0)) continue;
-      sc[t] = exp_cr(__fsub_rn(w.AM[ix], M0));
-      l = fma((double)w.AL[ix], (double)sc[t], l);
-    }
+    for (int t = 0; t < d.T; ++t)
+      if (al[t] > 0) l = fma((double)al[t], (double)sc[t], l);
     inv_l = (float)(1.0 / l);
   }
   __syncthreads();
   if (i >= d.hd) return;
   float acc = 0.f;
   for (int t = 0; t < d.T; ++t) {
-    const size_t ix = (size_t)t * nmh + mh;
-    if (!(w.AL[ix] > 0)) continue;
-    acc = fmaf(w.AO[ix * d.hd + i], sc[t], acc);
+    if (!(al[t] > 0)) continue;
+    acc = fmaf(w.AO[((size_t)t * nmh + mh) * d.hd + i], sc[t], acc);
   }
   const float v = r16(__fmul_rn(acc, inv_l));
   out[(size_t)mh * d.hd + i] = v;
@@ -318,17 +322,25 @@ __global__ void __launch_bounds__(512) k_attn_merge(AttnDesc d0, const float* __
   }
 }
 
-// ---- one-kernel split-KV: block = (chunk t, (row, head) pair).  The block computes its chunk's
-// scores (half-warp per key, as k_attn_scores) into shared memory, the chunk max, the exp8 weights
-// and their in-order sum (as k_attn_stats), and O for every dim over the chunk's keys in order (as
-// k_attn_accum); the last of the T blocks of a pair to finish (a counter per pair, zeroed before
-// the launch) merges the chunks (as k_attn_merge) and quantises the row when asked.  Same values
-// as the four-kernel path.
+// ---- one-kernel split-KV for short chunks (sliding-window layers): block = (chunk t, (row, head)
+// pair).  The chunk's K and V rows arrive in shared memory by bulk copies (one per row, rows
+// kAttnRowPad bytes apart so that the two half-warps of a warp read different banks); the block
+// then computes the chunk's scores (half-warp per key, as k_attn_scores), the chunk max, the exp8
+// weights and their in-order sum (as k_attn_stats), and O for every dim over the chunk's keys in
+// order (as k_attn_accum); the last of the T blocks of a pair to finish (a counter per pair, zeroed
+// before the launch) merges the chunks (as k_attn_merge) and quantises the row when asked.  Same
+// values as the four-kernel path.
+constexpr int kAttnShortKeys = 96;  // longest chunk served by k_attn_short
+constexpr int kAttnRowPad = 32;
+__host__ __device__ inline size_t attn_short_smem(int hd) {
+  return 128 + 2 * (size_t)kAttnShortKeys * (hd * 2 + kAttnRowPad) + sizeof(float) * kAttnShortKeys;
+}
+
 template <int STEPS>
-__global__ void __launch_bounds__(256) k_attn_fused(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
+__global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
                                                     const float* __restrict__ q, AttnDesc d0, float* __restrict__ ws,
                                                     int* __restrict__ counters, float* __restrict__ out) {
-  extern __shared__ __align__(16) float sc[];  // chunk scores, then weights
+  extern __shared__ __align__(128) uint8_t sm_raw[];
   __shared__ float red_f[8];
   __shared__ float msc[64];
   __shared__ float s_l8, s_inv;
@@ -339,25 +351,43 @@ __global__ void __launch_bounds__(256) k_attn_fused(const uint16_t* __restrict__
   const int m = mh / d.nh, h = mh % d.nh;
   const int c0 = max(chunk_lo(d, t), d.lo[m]), c1 = min(chunk_lo(d, t + 1), d.pos[m] + 1);
   const int n = max(0, c1 - c0);
+  const int rs = d.hd * 2 + kAttnRowPad;  // shared-memory row stride (bytes)
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm_raw);
+  uint8_t* ks = sm_raw + 128;
+  uint8_t* vs = ks + (size_t)kAttnShortKeys * rs;
+  float* sc = reinterpret_cast<float*>(vs + (size_t)kAttnShortKeys * rs);
   const int hw = threadIdx.x >> 4, c = threadIdx.x & 15, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  // scores
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (n > 0 && wid == 0) {
+    const uint32_t rowb = (uint32_t)d.hd * 2;
+    if (lane == 0) mbar_expect_tx(bar, 2u * rowb * (uint32_t)n);
+    __syncwarp();
+    for (int k = lane; k < n; k += 32) {
+      bulk_g2s(ks + (size_t)k * rs, Kc + (size_t)(c0 + k) * d.hd, rowb, bar);
+      bulk_g2s(vs + (size_t)k * rs, Vc + (size_t)(c0 + k) * d.hd, rowb, bar);
+    }
+  }
+  float qr[STEPS];
   {
-    float qr[STEPS];
     const float* qh = q + ((size_t)m * d.nh + h) * d.hd;
 #pragma unroll
     for (int i = 0; i < STEPS; ++i) qr[i] = qh[c + 16 * i];
-    const int nk2 = (n + 15) / 16 * 16;  // keep half-warp pairs together for the shuffles
-    for (int k = hw; k < nk2; k += 16) {
-      const int kk = min(k, n - 1);
-      float acc = 0.f;
-      if (n > 0) {
-        const uint16_t* kr = Kc + (size_t)(c0 + kk) * d.hd;
+  }
+  if (n > 0 && !cta_wait(bar, 0)) return;
+  // scores
+  const int nk2 = (n + 15) / 16 * 16;  // both half-warps of a warp run the same iterations
+  for (int k = hw; k < nk2; k += 16) {
+    const int kk = min(k, n - 1);
+    const uint16_t* kr = reinterpret_cast<const uint16_t*>(ks + (size_t)kk * rs);
+    float acc = 0.f;
 #pragma unroll
-        for (int i = 0; i < STEPS; ++i) acc = fmaf(qr[i], bf2f(__ldg(kr + c + 16 * i)), acc);
-      }
-      const float sv = hsum8_octet(__fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8)));
-      if (c == 0 && k < n) sc[k] = sv;
-    }
+    for (int i = 0; i < STEPS; ++i) acc = fmaf(qr[i], bf2f(kr[c + 16 * i]), acc);
+    const float sv = hsum8_octet(__fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8)));
+    if (c == 0 && k < n) sc[k] = sv;
   }
   __syncthreads();
   // chunk max (order-free), then the weights
@@ -371,7 +401,7 @@ __global__ void __launch_bounds__(256) k_attn_fused(const uint16_t* __restrict__
   for (int i = 1; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, red_f[i]);
   for (int k = threadIdx.x; k < n; k += blockDim.x) sc[k] = exp8(__fsub_rn(sc[k], mx));
   __syncthreads();
-  // in-order sum of the weights (warp 0: 32 keys per step, handed over by shuffles)
+  // in-order sum of the weights (warp 0)
   if (wid == 0) {
     float l8 = 0.f;
     for (int kb = 0; kb < n; kb += 32) {
@@ -393,16 +423,9 @@ __global__ void __launch_bounds__(256) k_attn_fused(const uint16_t* __restrict__
   const size_t ix = (size_t)t * nmh + mh;
   for (int i = threadIdx.x; i < d.hd; i += blockDim.x) {
     float o = 0.f;
-    const uint16_t* vp = Vc + (size_t)c0 * d.hd + i;
-    int k = 0;
-    for (; k + 8 <= n; k += 8) {
-      uint16_t v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __ldg(vp + (size_t)(k + u) * d.hd);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) o = fmaf(sc[k + u], bf2f(v[u]), o);
-    }
-    for (; k < n; ++k) o = fmaf(sc[k], bf2f(__ldg(vp + (size_t)k * d.hd)), o);
+    const uint8_t* vp = vs + (size_t)i * 2;
+#pragma unroll 8
+    for (int k = 0; k < n; ++k) o = fmaf(sc[k], bf2f(*reinterpret_cast<const uint16_t*>(vp + (size_t)k * rs)), o);
     w.AO[ix * d.hd + i] = o;
   }
   __syncthreads();
@@ -416,22 +439,30 @@ __global__ void __launch_bounds__(256) k_attn_fused(const uint16_t* __restrict__
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // merge (k_attn_merge) by the last block of the pair
+  // merge (k_attn_merge) by the last block of the pair: chunk factors in parallel, l in order
+  if (threadIdx.x < d.T) {
+    const size_t jx = (size_t)threadIdx.x * nmh + mh;
+    const float al = __ldcg(&w.AL[jx]);
+    msc[threadIdx.x] = al > 0 ? __ldcg(&w.AM[jx]) : -1e30f;
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
     float M0 = -1e30f;
-    for (int tt = 0; tt < d.T; ++tt) {
-      const size_t jx = (size_t)tt * nmh + mh;
-      if (__ldcg(&w.AL[jx]) > 0) M0 = fmaxf(M0, __ldcg(&w.AM[jx]));
-    }
+    for (int tt = 0; tt < d.T; ++tt) M0 = fmaxf(M0, msc[tt]);
+    red_f[0] = M0;
+  }
+  __syncthreads();
+  if (threadIdx.x < d.T) {
+    const size_t jx = (size_t)threadIdx.x * nmh + mh;
+    const float al = __ldcg(&w.AL[jx]);
+    msc[32 + threadIdx.x] = al;
+    msc[threadIdx.x] = al > 0 ? exp_cr(__fsub_rn(__ldcg(&w.AM[jx]), red_f[0])) : 0.f;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
     double l = 0;
-    for (int tt = 0; tt < d.T; ++tt) {
-      const size_t jx = (size_t)tt * nmh + mh;
-      msc[tt] = 0.f;
-      const float al = __ldcg(&w.AL[jx]);
-      if (!(al > 0)) continue;
-      msc[tt] = exp_cr(__fsub_rn(__ldcg(&w.AM[jx]), M0));
-      l = fma((double)al, (double)msc[tt], l);
-    }
+    for (int tt = 0; tt < d.T; ++tt)
+      if (msc[32 + tt] > 0) l = fma((double)msc[32 + tt], (double)msc[tt], l);
     s_inv = (float)(1.0 / l);
     counters[mh] = 0;  // ready for the next launch
   }
@@ -439,9 +470,8 @@ __global__ void __launch_bounds__(256) k_attn_fused(const uint16_t* __restrict__
   for (int i = threadIdx.x; i < d.hd; i += blockDim.x) {
     float acc = 0.f;
     for (int tt = 0; tt < d.T; ++tt) {
-      const size_t jx = (size_t)tt * nmh + mh;
-      if (!(__ldcg(&w.AL[jx]) > 0)) continue;
-      acc = fmaf(__ldcg(&w.AO[jx * d.hd + i]), msc[tt], acc);
+      if (!(msc[32 + tt] > 0)) continue;
+      acc = fmaf(__ldcg(&w.AO[((size_t)tt * nmh + mh) * d.hd + i]), msc[tt], acc);
     }
     const float v = r16(__fmul_rn(acc, s_inv));
     out[(size_t)mh * d.hd + i] = v;
@@ -495,7 +525,7 @@ static int launch_attn(const uint16_t* Kc, const uint16_t* Vc, const float* q, c
   if (int rc = check_launch("k_attn_stats")) return rc;
   k_attn_accum<<<dim3(d.T, d.hd / 16, (nmh + 7) / 8), 64, 0, st>>>(Vc, d, w);
   if (int rc = check_launch("k_attn_accum")) return rc;
-  k_attn_merge<<<nmh, d.hd, 0, st>>>(d, w, out);
+  k_attn_merge<<<nmh, d.hd > 64 ? d.hd : 64, 0, st>>>(d, w, out);
   return check_launch("k_attn_merge");
 }
 
@@ -508,29 +538,30 @@ extern "C" size_t g4_attn_splitkv_ws_bytes(int M, int nh, int hd, int kmin, int 
   return attn_counter_offset(M, nh, hd, kmax - kmin + 1, T) + sizeof(int) * (size_t)M * nh;
 }
 
-// One-kernel path (k_attn_fused) when a chunk's scores fit in shared memory; max_len bounds the
-// key range (the device may pick a shorter one) and sizes the workspace.
-static int launch_attn_fused(const uint16_t* Kc, const uint16_t* Vc, const float* q, const AttnDesc& d, void* ws,
+// One-kernel path (k_attn_short) when every chunk has at most kAttnShortKeys keys; max_len bounds
+// the key range (the device may pick a shorter one) and sizes the workspace.
+static int launch_attn_short(const uint16_t* Kc, const uint16_t* Vc, const float* q, const AttnDesc& d, void* ws,
                              float* out, cudaStream_t st, int max_len) {
   const int nmh = d.M * d.nh;
-  const int max_chunk = (max_len + d.T - 1) / d.T + 1;
-  const size_t smem = sizeof(float) * (size_t)max_chunk;
+  const size_t smem = attn_short_smem(d.hd);
   int* counters = reinterpret_cast<int*>(static_cast<char*>(ws) + attn_counter_offset(d.M, d.nh, d.hd, max_len, d.T));
   cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int) * (size_t)nmh, st);
   if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "attention: counter reset: %s", cudaGetErrorString(e));
   float* w = static_cast<float*>(ws);
   const dim3 grid(d.T, nmh);
   auto launch = [&](auto kern) {
-    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kern<<<grid, 256, smem, st>>>(Kc, Vc, q, d, w, counters, out);
   };
-  if (d.hd == 256) launch(k_attn_fused<16>);
-  else if (d.hd == 512) launch(k_attn_fused<32>);
-  else if (d.hd == 128) launch(k_attn_fused<8>);
-  else return set_error(G4_ERR_UNSUPPORTED, "attention: hd=%d (supported: 128, 256, 512)", d.hd);
-  return check_launch("k_attn_fused");
+  if (d.hd == 256) launch(k_attn_short<16>);
+  else if (d.hd == 128) launch(k_attn_short<8>);
+  else return set_error(G4_ERR_UNSUPPORTED, "attention: hd=%d", d.hd);
+  return check_launch("k_attn_short");
 }
-static bool fused_fits(int max_len, int T) { return (size_t)sizeof(float) * ((max_len + T - 1) / T + 1) <= 200 * 1024; }
+static bool short_fits(int max_len, int T, int hd) {
+  // chunk_lo(t+1) - chunk_lo(t) <= ceil(len / T); T <= 64 for the merge factors
+  return (max_len + T - 1) / T <= kAttnShortKeys && T <= 32 && (hd == 256 || hd == 128);
+}
 
 extern "C" int g4_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, const float* q, const int* pos, const int* lo,
                                int M, int nh, int hd, int kmin, int kmax, int T, float* out, void* ws, size_t ws_bytes,
@@ -543,7 +574,7 @@ extern "C" int g4_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, const flo
   G4_REQUIRE(aligned(ws, 16), "g4_attn_splitkv: workspace must be 16-byte aligned");
   cudaStream_t st = as_stream(stream);
   const int len = kmax - kmin + 1;
-  if (fused_fits(len, T)) return launch_attn_fused(Kc, Vc, q, d, ws, out, st, len);
+  if (short_fits(len, T, hd)) return launch_attn_short(Kc, Vc, q, d, ws, out, st, len);
   return launch_attn(Kc, Vc, q, d, static_cast<float*>(ws), out, st);
 }
 
@@ -562,7 +593,7 @@ int g4::attn_splitkv_dev(const uint16_t* Kc, const uint16_t* Vc, const float* q,
   d.qo = qo;
   const size_t need = g4_attn_splitkv_ws_bytes(M, nh, hd, 0, max_len - 1, T);
   if (ws_bytes < need) return set_error(G4_ERR_NOMEM, "attn_splitkv_dev: workspace %zu < %zu bytes", ws_bytes, need);
-  if (fused_fits(max_len, T)) return launch_attn_fused(Kc, Vc, q, d, ws, out, st, max_len);
+  if (short_fits(max_len, T, hd)) return launch_attn_short(Kc, Vc, q, d, ws, out, st, max_len);
   return launch_attn(Kc, Vc, q, d, static_cast<float*>(ws), out, st, max_len);
 }
 

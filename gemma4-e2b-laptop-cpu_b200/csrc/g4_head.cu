@@ -15,6 +15,7 @@
 #include "g4_async.cuh"
 #include "g4_common.cuh"
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -333,6 +334,97 @@ __global__ void __launch_bounds__(256) k_bf16p_gemv_staged(HeadPacked P, const f
       fence_proxy_async_smem();  // this stage's reads happen before the next bulk copies rewrite it
       issue(blk + 2 * gridDim.x, s);
     }
+  }
+}
+
+// Row-per-thread variant: one thread runs all eight octet-lane chains of its row (the lanes of the
+// reference's 8-wide vectors), so each group's exponent codes are decoded once for every
+// activation row.  The thread reads its row straight from global memory, four groups (176 bytes)
+// at a time as 11 aligned 16-byte loads through L1 (the 32 rows of a warp share no cache lines,
+// each 128-byte line serves 8 consecutive loads of its thread), so occupancy is set by registers,
+// not shared memory.  A persistent grid takes 256-row tiles in turn; the activations sit in shared
+// memory as [k][pair] float2 (one 16-byte broadcast load per element for four rows).  Values are
+// those of k_bf16p_gemv.
+constexpr int kBrThreads = 256;
+__host__ __device__ inline size_t head_rows_smem(int M, int K) { return (size_t)K * ((M + 1) / 2) * 8; }
+
+template <int M>
+__global__ void __launch_bounds__(kBrThreads) k_bf16p_rows(HeadPacked P, const float* __restrict__ X,
+                                                           float* __restrict__ Y, int ldy, const int* __restrict__ gate) {
+  constexpr int NP = (M + 1) / 2;
+  if (gate != nullptr && *gate == 0) return;
+  extern __shared__ __align__(16) float2 xs[];  // [K][NP]
+  const int K = P.K, G = K >> 5, rowb = G * 44;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    float v[2 * NP];
+#pragma unroll
+    for (int m = 0; m < 2 * NP; ++m) v[m] = m < M ? X[(size_t)m * K + i] : 0.f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) xs[(size_t)i * NP + p] = make_float2(v[2 * p], v[2 * p + 1]);
+  }
+  __syncthreads();
+  const uint32_t cb_lo = P.cb_lo, cb_hi = P.cb_hi;
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n - (int)threadIdx.x < P.N; n += gridDim.x * blockDim.x) {
+    if (n >= P.N) continue;
+    const uint4* rowp = reinterpret_cast<const uint4*>(P.data + (size_t)n * rowb);
+    float2 acc[8][NP];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int p = 0; p < NP; ++p) acc[j][p] = make_float2(0.f, 0.f);
+#pragma unroll 1
+    for (int u = 0; u < G / 4; ++u) {
+      uint32_t wv[44];
+#pragma unroll
+      for (int k = 0; k < 11; ++k) {
+        const uint4 t4 = __ldg(rowp + u * 11 + k);
+        wv[4 * k] = t4.x; wv[4 * k + 1] = t4.y; wv[4 * k + 2] = t4.z; wv[4 * k + 3] = t4.w;
+      }
+#pragma unroll
+      for (int gg = 0; gg < 4; ++gg) {
+        const int g = u * 4 + gg;
+        const uint32_t* gw = wv + gg * 11;
+        const uint32_t p0 = gw[8], p1 = gw[9], p2 = gw[10];
+        const float2* xg = xs + (size_t)g * 32 * NP;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t cc = ((p0 >> j) & 0x01010101u) | (((p1 >> j) & 0x01010101u) << 1) | (((p2 >> j) & 0x01010101u) << 2);
+          const uint32_t sel = (cc & 7u) | ((cc >> 4) & 0x70u) | ((cc >> 8) & 0x700u) | ((cc >> 12) & 0x7000u);
+          const uint32_t ex4 = __byte_perm(cb_lo, cb_hi, sel);  // exponent of element j + 8i in byte i
+#pragma unroll
+          for (int ii = 0; ii < 4; ++ii) {
+            const int i8 = (ii == 1) ? 2 : (ii == 2 ? 1 : ii);  // chain order: elements j, 16+j, 8+j, 24+j
+            const int e = j + 8 * i8;
+            const uint32_t smb = (gw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+            const uint32_t ex = (ex4 >> (8 * i8)) & 0xFFu;
+            const float wgt = __uint_as_float((((smb & 0x80u) << 8) | (ex << 7) | (smb & 0x7Fu)) << 16);
+#pragma unroll
+            for (int p = 0; p < NP; ++p) acc[j][p] = __ffma2_rn(make_float2(wgt, wgt), xg[e * NP + p], acc[j][p]);
+          }
+        }
+      }
+    }
+    float y[2 * NP];
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      // hsum8: ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7))
+      y[2 * p] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].x, acc[4][p].x), __fadd_rn(acc[1][p].x, acc[5][p].x)),
+                           __fadd_rn(__fadd_rn(acc[2][p].x, acc[6][p].x), __fadd_rn(acc[3][p].x, acc[7][p].x)));
+      y[2 * p + 1] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].y, acc[4][p].y), __fadd_rn(acc[1][p].y, acc[5][p].y)),
+                               __fadd_rn(__fadd_rn(acc[2][p].y, acc[6][p].y), __fadd_rn(acc[3][p].y, acc[7][p].y)));
+    }
+    for (long long e = P.exc_ptr[n]; e < P.exc_ptr[n + 1]; ++e) {  // CSR order, unfused (bf16_exp3_head.h:103)
+      const float dl = P.exc_delta[e];
+      const int col = P.exc_col[e];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        const float2 xv = xs[(size_t)col * NP + p];
+        y[2 * p] = __fadd_rn(y[2 * p], __fmul_rn(dl, xv.x));
+        y[2 * p + 1] = __fadd_rn(y[2 * p + 1], __fmul_rn(dl, xv.y));
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) Y[(size_t)m * ldy + n] = y[m];
   }
 }
 
@@ -673,6 +765,17 @@ static int num_sms() {
 
 template <int M>
 static void launch_head_gemv(const HeadPacked& P, const float* X, float* Y, int ldy, const int* gate, cudaStream_t st) {
+  const size_t rsmem = head_rows_smem(M, P.K);
+  const char* hv = getenv("G4_HEAD_GEMV");  // "octet" selects the octet-per-row variant (experiments)
+  if (P.K % 128 == 0 && rsmem <= 100 * 1024 && aligned(P.data, 16) && !(hv && hv[0] == 'o')) {
+    if (rsmem > 48 * 1024) cudaFuncSetAttribute(k_bf16p_rows<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem);
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_bf16p_rows<M>, kBrThreads, rsmem) != cudaSuccess || occ < 1)
+      occ = 1;
+    const int nblk = (P.N + kBrThreads - 1) / kBrThreads;
+    k_bf16p_rows<M><<<std::min(nblk, num_sms() * occ), kBrThreads, rsmem, st>>>(P, X, Y, ldy, gate);
+    return;
+  }
   const size_t smem = head_smem_bytes(M, P.K);
   if (P.K % 256 == 0 && smem <= 227 * 1024 && aligned(P.data, 16)) {
     cudaFuncSetAttribute(k_bf16p_gemv_staged<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

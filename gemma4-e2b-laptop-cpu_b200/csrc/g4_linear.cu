@@ -12,6 +12,7 @@
 #include "g4_api.h"
 #include "g4_common.cuh"
 #include "g4_async.cuh"
+#include <algorithm>
 #include <cstdlib>
 #include <cstdio>
 
@@ -202,6 +203,101 @@ k_w4g32(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const fl
   }
 }
 
+// W4G32 float GEMV, row-per-thread variant for tall matrices (the head screen: 262,144 rows).
+// One thread runs the eight lane chains of its row, so each 16-byte group of weights is decoded
+// once for all M activation rows.  The thread reads its row's weights and scales straight from
+// global memory through L1 (16-byte loads; a row's 128-byte lines serve 8 consecutive loads of its
+// thread), so occupancy is set by registers; a persistent grid takes 256-row tiles in turn.  The
+// activations sit in shared memory as [k][4] (one 16-byte broadcast load per element), the group
+// sums as [g][4].  Values are those of k_w4g32: per lane j and group, a = t(2j)x(2j);
+// a = fma(t(16+2j), x(16+2j), a); a = fma(t(2j+1), ...); a = fma(t(17+2j), ...);
+// row_j = fma(a, s, row_j); off = fma(s, gsum, off); y = hsum8(row) - 8 off.
+constexpr int kWrThreads = 256;
+__host__ __device__ inline size_t w4g32_rows_smem(int K) { return (size_t)K * 16 + (size_t)(K / 32) * 16; }
+
+template <int M>
+__global__ void __launch_bounds__(kWrThreads) k_w4g32_rows(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S,
+                                                            const float* __restrict__ X, int N, int K,
+                                                            float* __restrict__ Y, int ldy) {
+  extern __shared__ __align__(16) float4 xs[];  // [K], then group sums [G]
+  const int G = K >> 5;
+  float4* gs = xs + K;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    float v[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) v[m] = m < M ? X[(size_t)m * K + i] : 0.f;
+    xs[i] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {  // ((x0 + x1) + ...) + x31 from 0 (w4g32_avx2.h:22)
+    float v[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      float sm = 0.f;
+      if (m < M)
+        for (int k = 0; k < 32; ++k) sm = __fadd_rn(sm, X[(size_t)m * K + g * 32 + k]);
+      v[m] = sm;
+    }
+    gs[g] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+  __syncthreads();
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n - (int)threadIdx.x < N; n += gridDim.x * blockDim.x) {
+    if (n >= N) continue;
+    const uint4* wrow = reinterpret_cast<const uint4*>(Wp + (size_t)n * (K >> 1));
+    const uint4* srow = reinterpret_cast<const uint4*>(S + (size_t)n * G);
+    float2 row[8][2], off[2];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) row[j][0] = row[j][1] = make_float2(0.f, 0.f);
+    off[0] = off[1] = make_float2(0.f, 0.f);
+#pragma unroll 1
+    for (int g8 = 0; g8 < G; g8 += 8) {
+      const uint4 s8 = __ldg(srow + (g8 >> 3));
+      const uint32_t s8w[4] = {s8.x, s8.y, s8.z, s8.w};
+      uint4 wq[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) wq[u] = __ldg(wrow + g8 + u);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int g = g8 + u;
+        const uint32_t w4[4] = {wq[u].x, wq[u].y, wq[u].z, wq[u].w};
+        const float scl = bf2f((u & 1) ? (s8w[u >> 1] >> 16) : (s8w[u >> 1] & 0xFFFFu));
+        const float2 sc2 = make_float2(scl, scl);
+        const float4* xg = xs + g * 32;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t v = (w4[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;  // bytes 2j, 2j+1
+          float t0, t1, t2, t3;
+          nib4_to_f(v, t0, t1, t2, t3);
+          const float4 x0 = xg[2 * j], x1 = xg[16 + 2 * j], x2 = xg[2 * j + 1], x3 = xg[17 + 2 * j];
+          float2 a0 = __fmul2_rn(make_float2(t0, t0), make_float2(x0.x, x0.y));
+          float2 a1 = __fmul2_rn(make_float2(t0, t0), make_float2(x0.z, x0.w));
+          a0 = __ffma2_rn(make_float2(t1, t1), make_float2(x1.x, x1.y), a0);
+          a1 = __ffma2_rn(make_float2(t1, t1), make_float2(x1.z, x1.w), a1);
+          a0 = __ffma2_rn(make_float2(t2, t2), make_float2(x2.x, x2.y), a0);
+          a1 = __ffma2_rn(make_float2(t2, t2), make_float2(x2.z, x2.w), a1);
+          a0 = __ffma2_rn(make_float2(t3, t3), make_float2(x3.x, x3.y), a0);
+          a1 = __ffma2_rn(make_float2(t3, t3), make_float2(x3.z, x3.w), a1);
+          row[j][0] = __ffma2_rn(a0, sc2, row[j][0]);
+          row[j][1] = __ffma2_rn(a1, sc2, row[j][1]);
+        }
+        const float4 gv = gs[g];
+        off[0] = __ffma2_rn(sc2, make_float2(gv.x, gv.y), off[0]);
+        off[1] = __ffma2_rn(sc2, make_float2(gv.z, gv.w), off[1]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int p = m >> 1;
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = (m & 1) ? row[j][p].y : row[j][p].x;
+      const float h = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[4]), __fadd_rn(v[1], v[5])),
+                                __fadd_rn(__fadd_rn(v[2], v[6]), __fadd_rn(v[3], v[7])));
+      const float o = (m & 1) ? off[p].y : off[p].x;
+      Y[(size_t)m * ldy + n] = __fsub_rn(h, __fmul_rn(8.f, o));
+    }
+  }
+}
+
 // ------------------------------------------------------------------------ W4A8 quantisation
 // One warp per (row, 32-group), lane i owning element i: amax, sx = amax/127, inv = sx>0 ? 1/sx
 // : 0, r = RNE(x*inv) (x86 cvtps_epi32 semantics: out of range or NaN -> INT32_MIN), sum of the
@@ -371,23 +467,32 @@ k_w4a8_all(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const
                  &bars[c]);
     if (lane == 0) bulk_g2s(sc, S + (size_t)n0 * G, (uint32_t)nvalid * G * 2, &bars[0]);
   }
+  // phase 1: item (group gl of a chunk, row subset rs); with T > CH the rows of a group are split
+  // over T / CH threads.  Each thread's activations for its first item are loaded before the
+  // wait, so their latency overlaps the weights' arrival.
+  const int RS = T > CH ? min(T / CH, ROWS) : 1;
+  int4 qa[M], qb[M];
+  int bias[M];
+  float sxm[M];
+  auto load_act = [&](int g) {
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int4* qp = reinterpret_cast<const int4*>(q + (size_t)m * K + (size_t)g * 32);
+      qa[m] = __ldg(qp);
+      qb[m] = __ldg(qp + 1);
+      bias[m] = -8 * __ldg(sum + (size_t)m * G + g);
+      sxm[m] = __ldg(sx + (size_t)m * G + g);
+    }
+  };
+  if ((int)threadIdx.x < CH * RS) load_act(threadIdx.x % CH);
   for (int c = 0; c < nchunk; ++c) {
     if (!cta_wait(&bars[c], 0)) return;
-    for (int gl = threadIdx.x; gl < CH; gl += T) {
+    for (int idx = threadIdx.x; idx < CH * RS; idx += T) {
+      const int gl = idx % CH, rs = idx / CH;
       const int g = c * CH + gl;
-      int4 qa[M], qb[M];
-      int bias[M];
-      float sxm[M];
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        const int4* qp = reinterpret_cast<const int4*>(q + (size_t)m * K + (size_t)g * 32);
-        qa[m] = __ldg(qp);
-        qb[m] = __ldg(qp + 1);
-        bias[m] = -8 * __ldg(sum + (size_t)m * G + g);
-        sxm[m] = __ldg(sx + (size_t)m * G + g);
-      }
+      if (c > 0 || idx >= T) load_act(g);
 #pragma unroll 2
-      for (int r = 0; r < ROWS; ++r) {
+      for (int r = rs; r < ROWS; r += RS) {
         const uint4 wv = *reinterpret_cast<const uint4*>(wbuf + (size_t)r * wrs + (size_t)g * 16);
         const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
         uint32_t lo[4], hi[4];
@@ -425,11 +530,134 @@ k_w4a8_all(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const
   }
 }
 
+// W4A8 GEMV, persistent ring variant: a grid of at most a few CTAs per SM, each taking blocks of
+// ROWS weight rows in turn.  The activations (int8 rows, scales, sums) are staged in shared memory
+// once per CTA; each block's rows and scales arrive by bulk copies into one of NS stages, issued
+// NS blocks ahead, so the weight stream never waits for the arithmetic.  Per block, phase 1 gives
+// every (group, row subset) to a thread (integer dots for all M activation rows) and phase 2 runs
+// the ROWS*M fp32 chains in group order: the values of k_w4a8.
+template <int M, int ROWS, int WARPS, int NS>
+__global__ void __launch_bounds__(WARPS * 32)
+k_w4a8_ring(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const int8_t* __restrict__ q,
+            const float* __restrict__ sx, const int32_t* __restrict__ sum, int N, int K, float* __restrict__ Y, int ldy) {
+  constexpr int T = WARPS * 32;
+  const int G = K >> 5;
+  const int wrs = (K >> 1) + 16;
+  const size_t wbytes = (size_t)ROWS * wrs, sbytes = ((size_t)ROWS * G * 2 + 15) / 16 * 16;
+  const size_t stage_bytes = wbytes + sbytes;
+  const int acs = G + 1;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint8_t* stages = smem + 128;
+  int8_t* qs = reinterpret_cast<int8_t*>(stages + NS * stage_bytes);           // [M][K]
+  float* sxs = reinterpret_cast<float*>(qs + (size_t)M * K);                     // [M][G]
+  int32_t* sums = reinterpret_cast<int32_t*>(sxs + (size_t)M * G);               // [M][G]
+  float2* ac = reinterpret_cast<float2*>(sums + (size_t)M * G);                  // [ROWS*M][G+1]
+  const int nblk = (N + ROWS - 1) / ROWS;
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < NS; ++b) mbar_init(&bars[b], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int blk, int st) {  // warp 0
+    const int lane = threadIdx.x & 31;
+    const int n0 = blk * ROWS, nvalid = min(ROWS, N - n0);
+    uint8_t* wb = stages + (size_t)st * stage_bytes;
+    if (lane == 0) mbar_expect_tx(&bars[st], (uint32_t)nvalid * (uint32_t)(K >> 1) + (uint32_t)nvalid * G * 2);
+    __syncwarp();
+    for (int r = lane; r < nvalid; r += 32)
+      bulk_g2s(wb + (size_t)r * wrs, Wp + (size_t)(n0 + r) * (K >> 1), (uint32_t)(K >> 1), &bars[st]);
+    if (lane == 0) bulk_g2s(wb + wbytes, S + (size_t)n0 * G, (uint32_t)nvalid * G * 2, &bars[st]);
+  };
+  if (threadIdx.x < 32)
+    for (int b = 0; b < NS; ++b)
+      if ((int)(blockIdx.x + b * gridDim.x) < nblk) issue(blockIdx.x + b * gridDim.x, b);
+  // activations into shared memory (16-byte pieces; K % 256 == 0)
+  for (int i = threadIdx.x; i < M * K / 16; i += T) reinterpret_cast<int4*>(qs)[i] = __ldg(reinterpret_cast<const int4*>(q) + i);
+  for (int i = threadIdx.x; i < M * G; i += T) { sxs[i] = __ldg(sx + i); sums[i] = __ldg(sum + i); }
+  __syncthreads();
+  constexpr int RS_MAX = T;  // row subsets when T > G
+  const int RS = T > G ? min(T / G, ROWS) : 1;
+  (void)RS_MAX;
+  int it = 0;
+  for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x, ++it) {
+    const int st = it % NS;
+    if (!cta_wait(&bars[st], (uint32_t)(it / NS) & 1u)) return;
+    const uint8_t* wb = stages + (size_t)st * stage_bytes;
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(wb + wbytes);
+    const int n0 = blk * ROWS, nvalid = min(ROWS, N - n0);
+    for (int idx = threadIdx.x; idx < G * RS; idx += T) {
+      const int g = idx % G, rs = idx / G;
+      int4 qa[M], qb[M];
+      int bias[M];
+      float sxm[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const int4* qp = reinterpret_cast<const int4*>(qs + (size_t)m * K + (size_t)g * 32);
+        qa[m] = qp[0];
+        qb[m] = qp[1];
+        bias[m] = -8 * sums[m * G + g];
+        sxm[m] = sxs[m * G + g];
+      }
+      for (int r = rs; r < ROWS; r += RS) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(wb + (size_t)r * wrs + (size_t)g * 16);
+        const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { lo[k] = w4[k] & 0x0F0F0F0Fu; hi[k] = (w4[k] >> 4) & 0x0F0F0F0Fu; }
+        const float sw = bf2f(sc[(size_t)r * G + g]);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          int acc = bias[m];
+          acc = __dp4a((int)lo[0], qa[m].x, acc);
+          acc = __dp4a((int)lo[1], qa[m].y, acc);
+          acc = __dp4a((int)lo[2], qa[m].z, acc);
+          acc = __dp4a((int)lo[3], qa[m].w, acc);
+          acc = __dp4a((int)hi[0], qb[m].x, acc);
+          acc = __dp4a((int)hi[1], qb[m].y, acc);
+          acc = __dp4a((int)hi[2], qb[m].z, acc);
+          acc = __dp4a((int)hi[3], qb[m].w, acc);
+          ac[(size_t)(r * M + m) * acs + g] = make_float2((float)acc, __fmul_rn(sw, sxm[m]));
+        }
+      }
+    }
+    __syncthreads();
+    const int ci = threadIdx.x;
+    if (ci < ROWS * M) {
+      const int cr = ci / M, cm = ci % M;
+      const float2* a = ac + (size_t)ci * acs;
+      float row = 0.f;
+#pragma unroll 8
+      for (int g = 0; g < G; ++g) {
+        const float2 v = a[g];
+        row = fmaf(v.x, v.y, row);
+      }
+      if (cr < nvalid) Y[(size_t)cm * ldy + n0 + cr] = row;
+    }
+    __syncthreads();  // stage st and ac are free again
+    if (threadIdx.x < 32 && blk + NS * (int)gridDim.x < nblk) {
+      fence_proxy_async_smem();
+      issue(blk + NS * gridDim.x, st);
+    }
+  }
+}
+
 }  // namespace g4
 
 G4_STATUS_READER(linear)
 
 using namespace g4;
+
+static int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
 
 extern "C" int g4_w4_pack(const uint8_t* W, int N, int K, uint8_t* Wp, void* stream) {
   G4_REQUIRE(W && Wp && N > 0 && K > 0 && K % 32 == 0, "g4_w4_pack: bad arguments N=%d K=%d", N, K);
@@ -492,6 +720,25 @@ extern "C" int g4_w4g32_gemm(const uint8_t* Wp, const uint16_t* S, const float* 
   G4_REQUIRE(aligned(Wp, 16) && aligned(S, 16) && aligned(X, 16) && (gsum == nullptr || aligned(gsum, 4)),
              "g4_w4g32_gemm: Wp, S and X must be 16-byte aligned");
   cudaStream_t st = as_stream(stream);
+  // tall matrices (the head screen): row-per-thread variant
+  const char* rv = getenv("G4_W4G32_ROWS");  // "0" turns it off (experiments)
+  if (M <= 4 && gsum == nullptr && N >= 16384 && w4g32_rows_smem(K) <= 100 * 1024 && !(rv && rv[0] == '0')) {
+    const size_t smem = w4g32_rows_smem(K);
+    auto go = [&](auto kern) {
+      if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      int occ = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kWrThreads, smem) != cudaSuccess || occ < 1) occ = 1;
+      const int grid = std::min((N + kWrThreads - 1) / kWrThreads, sm_count() * occ);
+      kern<<<grid, kWrThreads, smem, st>>>(Wp, S, X, N, K, Y, ldy);
+      return check_launch("k_w4g32_rows");
+    };
+    switch (M) {
+      case 1: return go(k_w4g32_rows<1>);
+      case 2: return go(k_w4g32_rows<2>);
+      case 3: return go(k_w4g32_rows<3>);
+      default: return go(k_w4g32_rows<4>);
+    }
+  }
   switch (M) {
     case 1: return launch_w4g32<1>(Wp, S, X, gsum, N, K, Y, ldy, st);
     case 2: return launch_w4g32<2>(Wp, S, X, gsum, N, K, Y, ldy, st);
@@ -541,24 +788,72 @@ static int launch_w4a8_all_t(const uint8_t* Wp, const uint16_t* S, const int8_t*
   return check_launch("k_w4a8_all");
 }
 
+static size_t w4a8_ring_smem(int M, int rows, int K, int ns) {
+  const int G = K / 32;
+  const size_t stage = (size_t)rows * (K / 2 + 16) + ((size_t)rows * G * 2 + 15) / 16 * 16;
+  return 128 + ns * stage + (size_t)M * K + (size_t)M * G * 8 + (size_t)rows * M * (G + 1) * 8;
+}
+
+template <int M, int ROWS, int WARPS, int NS>
+static int launch_w4a8_ring_t(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
+                              int N, int K, float* Y, int ldy, int per_sm, cudaStream_t st) {
+  const size_t smem = w4a8_ring_smem(M, ROWS, K, NS);
+  auto kern = k_w4a8_ring<M, ROWS, WARPS, NS>;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, WARPS * 32, smem) != cudaSuccess || occ < 1) occ = 1;
+  const int nblk = (N + ROWS - 1) / ROWS;
+  const int grid = std::min(nblk, sm_count() * std::min(occ, per_sm));
+  kern<<<grid, WARPS * 32, smem, st>>>(Wp, S, q, sx, sum, N, K, Y, ldy);
+  return check_launch("k_w4a8_ring");
+}
+
+// G4_W4A8_RING="rows,warps,stages,per_sm" selects the ring variant (rows 4/8/16, warps 2/4, stages
+// 2/3/4) for experiments; unset, the whole-block variant runs.
+template <int M>
+static int launch_w4a8_ring(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
+                            int N, int K, float* Y, int ldy, cudaStream_t st, bool* done) {
+  int R = 0, W = 4, NS = 3, per_sm = 4;  // off unless G4_W4A8_RING asks for it
+  if (const char* e = getenv("G4_W4A8_RING")) sscanf(e, "%d,%d,%d,%d", &R, &W, &NS, &per_sm);
+  *done = false;
+  if (R <= 0) return G4_OK;
+  if (R != 4 && R != 8 && R != 16) R = 8;
+  if (W != 2 && W != 4) W = 4;
+  if (NS < 2 || NS > 4) NS = 3;
+  if (W * 32 < R * M) return G4_OK;
+  if (w4a8_ring_smem(M, R, K, NS) > 220 * 1024) return G4_OK;
+  *done = true;
+#define G4_RING(RR, WW, SS) \
+  if (R == RR && W == WW && NS == SS) return launch_w4a8_ring_t<M, RR, WW, SS>(Wp, S, q, sx, sum, N, K, Y, ldy, per_sm, st);
+  G4_RING(4, 2, 2) G4_RING(4, 2, 3) G4_RING(4, 2, 4) G4_RING(4, 4, 2) G4_RING(4, 4, 3) G4_RING(4, 4, 4)
+  G4_RING(8, 2, 2) G4_RING(8, 2, 3) G4_RING(8, 2, 4) G4_RING(8, 4, 2) G4_RING(8, 4, 3) G4_RING(8, 4, 4)
+  G4_RING(16, 2, 2) G4_RING(16, 2, 3) G4_RING(16, 2, 4) G4_RING(16, 4, 2) G4_RING(16, 4, 3) G4_RING(16, 4, 4)
+#undef G4_RING
+  *done = false;
+  return G4_OK;
+}
+
 template <int M>
 static int launch_w4a8(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
                        int N, int K, float* Y, int ldy, cudaStream_t st) {
+  {
+    bool done = false;
+    const int rc = launch_w4a8_ring<M>(Wp, S, q, sx, sum, N, K, Y, ldy, st, &done);
+    if (done || rc) return rc;
+  }
   // whole-block variant (all rows of a CTA in flight at once) when its shared memory fits;
-  // 16 rows per CTA for the widest matrices, threads >= chains
-  int AR = (N >= 8192 && M <= 4) ? 16 : 8, AW = 2;
+  // G4_W4A8_ALL="rows,warps" (rows 8/16, warps 2/4/8) overrides the choice for experiments
+  int AR = (N >= 8192 && M <= 4) ? 16 : 8, AW = 4;
   if (const char* e = getenv("G4_W4A8_ALL")) sscanf(e, "%d,%d", &AR, &AW);
   if (AR != 16) AR = AR > 0 ? 8 : 0;
-  if (AW != 4) AW = 2;
-  if (AW * 32 < AR * M) AW = 4;
+  if (AW != 2 && AW != 8) AW = 4;
+  while (AW < 8 && AW * 32 < AR * M) AW *= 2;
   const int G = K / 32, ACH = pick_ch(G);
   if (AR > 0 && AW * 32 >= AR * M && G / ACH <= 16 && w4a8_all_smem(M, AR, K) <= 200 * 1024) {
-    if (AR == 16) {
-      if (AW == 4) return launch_w4a8_all_t<M, 16, 4>(Wp, S, q, sx, sum, N, K, Y, ldy, ACH, st);
-      return launch_w4a8_all_t<M, 16, 2>(Wp, S, q, sx, sum, N, K, Y, ldy, ACH, st);
-    }
-    if (AW == 4) return launch_w4a8_all_t<M, 8, 4>(Wp, S, q, sx, sum, N, K, Y, ldy, ACH, st);
-    return launch_w4a8_all_t<M, 8, 2>(Wp, S, q, sx, sum, N, K, Y, ldy, ACH, st);
+#define G4_ALL(RR, WW) \
+    if (AR == RR && AW == WW) return launch_w4a8_all_t<M, RR, WW>(Wp, S, q, sx, sum, N, K, Y, ldy, ACH, st);
+    G4_ALL(8, 2) G4_ALL(8, 4) G4_ALL(8, 8) G4_ALL(16, 2) G4_ALL(16, 4) G4_ALL(16, 8)
+#undef G4_ALL
   }
   int WARPS = 2, CH = pick_ch(K / 32), NB = 3;
   if (const char* e = getenv("G4_W4A8_CFG")) sscanf(e, "%d,%d,%d", &WARPS, &CH, &NB);
