@@ -13,6 +13,16 @@ int set_error(int code, const char* fmt, ...) {
   return code;
 }
 
+long long& launch_count() {
+  static thread_local long long n = 0;
+  return n;
+}
+
+bool& pdl_enabled() {
+  static thread_local bool on = false;
+  return on;
+}
+
 int check_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
@@ -21,7 +31,7 @@ int check_launch(const char* what) {
 }  // namespace g4
 
 extern "C" const char* g4_last_error(void) { return g4::g_msg; }
-extern "C" int g4_abi_version(void) { return 3; }
+extern "C" int g4_abi_version(void) { return 4; }
 
 namespace g4 {
 unsigned status_read_linear(bool reset);

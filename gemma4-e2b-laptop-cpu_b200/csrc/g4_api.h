@@ -5,6 +5,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include "g4.h"
+#include <utility>
 
 namespace g4 {
 int set_error(int code, const char* fmt, ...);
@@ -13,11 +14,48 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 int check_launch(const char* what);
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 struct QuantOut;
+// Programmatic dependent launch.  While pdl_enabled() is set on this host thread (the engine sets
+// it while it records a decode round into a CUDA graph), launch() gives kernels the programmatic
+// stream serialisation attribute: such a kernel may start while its predecessor on the stream is
+// still running, and its pdl_wait() (g4_common.cuh) blocks until that predecessor has finished and
+// its writes are visible.  Every kernel launched this way calls pdl_wait() before it touches
+// anything an earlier kernel writes, so only read-only prologues (weight prefetches, barrier set-up)
+// overlap the previous kernel.  Otherwise launch() is an ordinary <<<>>> launch.
+bool& pdl_enabled();
+// Kernels started through launch() on this host thread (the engine counts its launches with it).
+long long& launch_count();
+template <typename... KArgs, typename... Args>
+inline int launch(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                  Args&&... args) {
+  cudaError_t e;
+  if (pdl_enabled()) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  } else {
+    kern<<<grid, block, smem, st>>>(std::forward<Args>(args)...);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  ++launch_count();
+  return G4_OK;
+}
+
 // Split-KV attention whose key ranges are computed on the device from a position (g4_attn.cu); the
-// output rows are also quantised for a W4A8 linear when qo.q is set.
+// output rows are also quantised for a W4A8 linear when qo.q is set.  zeroed_counters (may be NULL):
+// M*nh ints that are 0 on entry, reserved for such calls (they are 0 again when the call
+// completes); with them no counter reset is enqueued.
 int attn_splitkv_dev(const uint16_t* Kc, const uint16_t* Vc, const float* q, int M, int nh, int hd, const int* dP,
                      int base_add, int q_add, int window, int max_len, int T, float* out, void* ws, size_t ws_bytes,
-                     cudaStream_t st, QuantOut qo);
+                     cudaStream_t st, QuantOut qo, int* zeroed_counters = nullptr);
 }  // namespace g4
 
 #define G4_REQUIRE(cond, ...) \

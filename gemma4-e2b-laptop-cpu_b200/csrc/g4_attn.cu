@@ -17,6 +17,7 @@
 #include "g4_api.h"
 #include "g4_async.cuh"
 #include "g4_common.cuh"
+#include <cstdlib>
 
 namespace g4 {
 
@@ -83,6 +84,8 @@ constexpr int kScoreKeys = 32;
 template <int STEPS>  // hd / 16
 __global__ void __launch_bounds__(512) k_attn_scores(const uint16_t* __restrict__ Kc, const float* __restrict__ q,
                                                      AttnDesc d0, float* __restrict__ ws) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t sm_raw[];
   const AttnDesc d = resolve(d0);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm_raw);
@@ -144,6 +147,8 @@ __global__ void __launch_bounds__(512) k_attn_scores(const uint16_t* __restrict_
 // 32*kStatSlots keys.
 constexpr int kStatSlots = 32;
 __global__ void __launch_bounds__(256) k_attn_stats(AttnDesc d0, float* __restrict__ ws) {
+  pdl_wait();
+  pdl_trigger();
   const AttnDesc d = resolve(d0);
   const AttnWs w = attn_ws(ws, d);
   const int mh = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31, t = blockIdx.x;
@@ -219,6 +224,8 @@ __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_
 // asynchronous copies, double-buffered so that the next tile loads while this one is consumed.
 constexpr int kAccKeys = 128;
 __global__ void __launch_bounds__(64) k_attn_accum(const uint16_t* __restrict__ Vc, AttnDesc d0, float* __restrict__ ws) {
+  pdl_wait();
+  pdl_trigger();
   const AttnDesc d = resolve(d0);
   __shared__ __align__(16) uint32_t vs[2][kAccKeys][8];    // 16 bf16 dims per key
   __shared__ __align__(16) float wsm[2][8][kAccKeys + 1];  // weights [pair][key], padded against bank conflicts
@@ -273,6 +280,8 @@ __global__ void __launch_bounds__(64) k_attn_accum(const uint16_t* __restrict__ 
 // product exact); out = r16((sum_t fma(O_t, sc_t)) * (float)(1/l)).  The per-chunk factors are
 // computed once per block.
 __global__ void __launch_bounds__(512) k_attn_merge(AttnDesc d0, const float* __restrict__ ws, float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sc[64], al[64];
   __shared__ float inv_l, s_m0;
   const AttnDesc d = resolve(d0);
@@ -322,6 +331,156 @@ __global__ void __launch_bounds__(512) k_attn_merge(AttnDesc d0, const float* __
   }
 }
 
+// ---- chunk kernel for long chunks (global layers): statistics, accumulation and merge in one
+// launch after k_attn_scores.  Block = (chunk t, 32-dim slice, group of 8 (row, head) pairs),
+// 256 threads.  Warp p loads pair p's allowed scores of the chunk into shared memory, takes their
+// max and turns them into exp8 weights in place (as k_attn_stats).  Then, concurrently, lanes of
+// warp 0 run each pair's weight sum in key order, and warps 4-7 (thread = pair x dim pair) run
+// the O chains over the chunk's keys in order with V staged by double-buffered cp.async (as
+// k_attn_accum).  The last of the T blocks of a (slice, group) merges the chunks for its 32 dims
+// (as k_attn_merge) and quantises them when asked.  Same values as the four-kernel path.
+constexpr int kChunkMaxKeys = 1536, kChunkTile = 128;
+__host__ __device__ inline size_t attn_chunk_smem() {
+  return sizeof(float) * 8 * (kChunkMaxKeys + 1) + 2 * (size_t)kChunkTile * 64;
+}
+__device__ __forceinline__ void cp_async16_g(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void named_sync_128() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__global__ void __launch_bounds__(256) k_attn_chunk(const uint16_t* __restrict__ Vc, AttnDesc d0, float* __restrict__ ws,
+                                                    int* __restrict__ counters, float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(16) uint8_t csm[];
+  float* wsm = reinterpret_cast<float*>(csm);                                     // [8][kChunkMaxKeys + 1]
+  uint32_t* vt = reinterpret_cast<uint32_t*>(csm + sizeof(float) * 8 * (kChunkMaxKeys + 1));  // [2][tile][16]
+  __shared__ float smx[8], sl8[8];
+  __shared__ int s_last;
+  const AttnDesc d = resolve(d0);
+  const AttnWs w = attn_ws(ws, d);
+  const int t = blockIdx.x, y = blockIdx.y, grp = blockIdx.z, i0 = y * 32;
+  const int nmh = d.M * d.nh, len = d.kmax - d.kmin + 1, G8 = (nmh + 7) / 8;
+  const int mhb = grp * 8, ng = min(8, nmh - mhb);
+  const int cl = chunk_lo(d, t), ch = chunk_lo(d, t + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int WS = kChunkMaxKeys + 1;
+  // scores of pair `warp` -> shared memory, max, weights
+  if (warp < ng) {
+    const int mh = mhb + warp, m = mh / d.nh;
+    const int a = max(cl, d.lo[m]), b = min(ch - 1, d.pos[m]);
+    const float* srow = w.S + (size_t)mh * len - d.kmin;
+    float* wp = wsm + warp * WS - cl;
+    float mx = -1e30f;
+    for (int k = a + lane; k <= b; k += 32) {
+      const float v = srow[k];
+      wp[k] = v;
+      mx = fmaxf(mx, v);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    for (int k = a + lane; k <= b; k += 32) wp[k] = exp8(__fsub_rn(wp[k], mx));
+    if (lane == 0) smx[warp] = mx;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // in-order weight sums, one lane per pair
+    if (lane < ng) {
+      const int mh = mhb + lane, m = mh / d.nh;
+      const int a = max(cl, d.lo[m]), b = min(ch - 1, d.pos[m]);
+      const float* wp = wsm + lane * WS - cl;
+      float l8 = 0.f;
+      for (int k = a; k <= b; ++k) l8 = __fadd_rn(l8, wp[k]);
+      sl8[lane] = (d.lo[m] > d.pos[m]) ? 0.0f : l8;
+    }
+  } else if (warp >= 4) {
+    // O chains: thread = (pair p, dim pair dp) over this block's 32 dims
+    const int at = threadIdx.x - 128, p = at >> 4, dp = at & 15;
+    const bool live = p < ng;
+    const int mh = mhb + (live ? p : 0), m = mh / d.nh;
+    const int a = max(cl, d.lo[m]), b = min(ch - 1, d.pos[m]);
+    const float* wp = wsm + (live ? p : 0) * WS - cl;
+    float2 o = make_float2(0.f, 0.f);
+    auto stage = [&](int buf, int pb) {
+      const int nk = min(kChunkTile, ch - pb);
+      for (int e = at; e < nk * 4; e += 128)  // 4 x 16 B per key (32 bf16 dims)
+        cp_async16_g(vt + ((size_t)buf * kChunkTile + (e >> 2)) * 16 + (e & 3) * 4,
+                     Vc + (size_t)(pb + (e >> 2)) * d.hd + i0 + (e & 3) * 8);
+    };
+    if (cl < ch) stage(0, cl);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int pb = cl, it = 0; pb < ch; pb += kChunkTile, ++it) {
+      if (pb + kChunkTile < ch) stage((it + 1) & 1, pb + kChunkTile);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+      named_sync_128();
+      if (live) {
+        const int ka = max(a, pb), kb = min(b, pb + kChunkTile - 1);
+        const uint32_t* vb = vt + (size_t)(it & 1) * kChunkTile * 16 + dp - (size_t)pb * 16;
+#pragma unroll 4
+        for (int k = ka; k <= kb; ++k) {
+          const uint32_t vv = vb[(size_t)k * 16];
+          const float wt = wp[k];
+          o = __ffma2_rn(make_float2(wt, wt), make_float2(__uint_as_float(vv << 16), __uint_as_float(vv & 0xFFFF0000u)), o);
+        }
+      }
+      named_sync_128();
+    }
+    if (live) {
+      float* ao = w.AO + ((size_t)t * nmh + mh) * d.hd + i0 + 2 * dp;
+      ao[0] = o.x;
+      ao[1] = o.y;
+    }
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < ng) {  // every slice writes the same statistics
+    w.AM[(size_t)t * nmh + mhb + threadIdx.x] = smx[threadIdx.x];
+    w.AL[(size_t)t * nmh + mhb + threadIdx.x] = sl8[threadIdx.x];
+  }
+  __threadfence();
+  __syncthreads();
+  int* cnt = counters + (size_t)y * G8 + grp;
+  if (threadIdx.x == 0) s_last = atomicAdd(cnt, 1) == d.T - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (warp < ng) {
+    // merge (k_attn_merge) for pair `warp`, dim i0 + lane
+    const int mh = mhb + warp;
+    float M0 = -1e30f;
+    for (int tt = 0; tt < d.T; ++tt) {
+      const size_t jx = (size_t)tt * nmh + mh;
+      if (__ldcg(&w.AL[jx]) > 0) M0 = fmaxf(M0, __ldcg(&w.AM[jx]));
+    }
+    double l = 0;
+    float acc = 0.f;
+    for (int tt = 0; tt < d.T; ++tt) {
+      const size_t jx = (size_t)tt * nmh + mh;
+      const float al = __ldcg(&w.AL[jx]);
+      if (!(al > 0)) continue;
+      const float sc = exp_cr(__fsub_rn(__ldcg(&w.AM[jx]), M0));
+      l = fma((double)al, (double)sc, l);
+      acc = fmaf(__ldcg(&w.AO[jx * d.hd + i0 + lane]), sc, acc);
+    }
+    const float inv = (float)(1.0 / l);
+    const float v = r16(__fmul_rn(acc, inv));
+    const size_t flat = (size_t)mh * d.hd + i0 + lane;
+    out[flat] = v;
+    if (d.qo.q) {
+      int8_t qv;
+      float sxv;
+      int32_t tot;
+      quant_group32(v, qv, sxv, tot);
+      d.qo.q[flat] = qv;
+      if (lane == 0) {
+        d.qo.sx[flat >> 5] = sxv;
+        d.qo.sum[flat >> 5] = tot;
+      }
+    }
+  }
+  if (threadIdx.x == 0) *cnt = 0;  // ready for the next launch
+}
+
 // ---- one-kernel split-KV for short chunks (sliding-window layers): block = (chunk t, (row, head)
 // pair).  The chunk's K and V rows arrive in shared memory by bulk copies (one per row, rows
 // kAttnRowPad bytes apart so that the two half-warps of a warp read different banks); the block
@@ -340,6 +499,8 @@ template <int STEPS>
 __global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
                                                     const float* __restrict__ q, AttnDesc d0, float* __restrict__ ws,
                                                     int* __restrict__ counters, float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t sm_raw[];
   __shared__ float red_f[8];
   __shared__ float msc[64];
@@ -512,50 +673,86 @@ static int fill_desc(AttnDesc& d, const uint16_t* Kc, const uint16_t* Vc, int M,
   return G4_OK;
 }
 
+static size_t attn_counter_offset(int M, int nh, int hd, int len, int T);
+static int attn_counter_count(int M, int nh, int hd) {
+  const int a = M * nh, b = (hd / 32) * ((M * nh + 7) / 8);
+  return a > b ? a : b;
+}
+
+// Scores, then either the chunk kernel (chunks of at most kChunkMaxKeys keys) or statistics,
+// accumulation and merge as three kernels.  zeroed_counters as for launch_attn_short; NULL = the
+// workspace's, reset first.  four = true forces the three-kernel tail (the allocation-free entry
+// point, whose fixed scratch has no counters).
 static int launch_attn(const uint16_t* Kc, const uint16_t* Vc, const float* q, const AttnDesc& d, float* w, float* out,
-                       cudaStream_t st, int max_len = 0) {
+                       cudaStream_t st, int max_len = 0, int* zeroed_counters = nullptr, bool four = false) {
   const int len = max_len > 0 ? max_len : d.kmax - d.kmin + 1, nmh = d.M * d.nh;
   const size_t ssm = 128 + (size_t)kScoreKeys * d.hd * 2;
-  if (d.hd == 256) k_attn_scores<16><<<(len + kScoreKeys - 1) / kScoreKeys, nmh * 16, ssm, st>>>(Kc, q, d, w);
-  else if (d.hd == 512) k_attn_scores<32><<<(len + kScoreKeys - 1) / kScoreKeys, nmh * 16, ssm, st>>>(Kc, q, d, w);
-  else if (d.hd == 128) k_attn_scores<8><<<(len + kScoreKeys - 1) / kScoreKeys, nmh * 16, ssm, st>>>(Kc, q, d, w);
+  int rc = G4_OK;
+  const dim3 sgrid((len + kScoreKeys - 1) / kScoreKeys), sblk(nmh * 16);
+  if (d.hd == 256) rc = launch("k_attn_scores", k_attn_scores<16>, sgrid, sblk, ssm, st, Kc, q, d, w);
+  else if (d.hd == 512) rc = launch("k_attn_scores", k_attn_scores<32>, sgrid, sblk, ssm, st, Kc, q, d, w);
+  else if (d.hd == 128) rc = launch("k_attn_scores", k_attn_scores<8>, sgrid, sblk, ssm, st, Kc, q, d, w);
   else return set_error(G4_ERR_UNSUPPORTED, "attention: hd=%d (supported: 128, 256, 512)", d.hd);
-  if (int rc = check_launch("k_attn_scores")) return rc;
-  k_attn_stats<<<dim3(d.T, (nmh + 7) / 8), 256, 0, st>>>(d, w);
-  if (int rc = check_launch("k_attn_stats")) return rc;
-  k_attn_accum<<<dim3(d.T, d.hd / 16, (nmh + 7) / 8), 64, 0, st>>>(Vc, d, w);
-  if (int rc = check_launch("k_attn_accum")) return rc;
-  k_attn_merge<<<nmh, d.hd > 64 ? d.hd : 64, 0, st>>>(d, w, out);
+  if (rc) return rc;
+  static const bool chunk_on = [] {  // G4_ATTN_CHUNK=0/1 overrides the default (experiments)
+    const char* e = getenv("G4_ATTN_CHUNK");
+    return e ? e[0] == '1' : false;
+  }();
+  if (chunk_on && !four && (len + d.T - 1) / d.T + 1 <= kChunkMaxKeys && d.hd % 32 == 0) {
+    int* counters = zeroed_counters;
+    if (counters == nullptr) {
+      counters = reinterpret_cast<int*>(reinterpret_cast<char*>(w) + attn_counter_offset(d.M, d.nh, d.hd, len, d.T));
+      cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int) * (size_t)attn_counter_count(d.M, d.nh, d.hd), st);
+      if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "attention: counter reset: %s", cudaGetErrorString(e));
+    }
+    const size_t csm = attn_chunk_smem();
+    cudaFuncSetAttribute(k_attn_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm);
+    return launch("k_attn_chunk", k_attn_chunk, dim3(d.T, d.hd / 32, (nmh + 7) / 8), dim3(256), csm, st, Vc, d, w,
+                  counters, out);
+  }
+  if (int rc_ = launch("k_attn_stats", k_attn_stats, dim3(d.T, (nmh + 7) / 8), dim3(256), 0, st, d, w)) return rc_;
+  if (int rc_ = launch("k_attn_accum", k_attn_accum, dim3(d.T, d.hd / 16, (nmh + 7) / 8), dim3(64), 0, st, Vc, d, w))
+    return rc_;
+  if (int rc_ = launch("k_attn_merge", k_attn_merge, dim3(nmh), dim3(d.hd > 64 ? d.hd : 64), 0, st, d, w, out)) return rc_;
   return check_launch("k_attn_merge");
 }
 
-// Workspace of g4_attn_splitkv: the partial results (attn_ws_floats), then one int counter per
-// (row, head) pair for the one-kernel path.
+// Workspace of g4_attn_splitkv: the partial results (attn_ws_floats), then the int counters of the
+// one-kernel and chunk paths (one per (row, head) pair, or per (32-dim slice, group of 8 pairs)).
 static size_t attn_counter_offset(int M, int nh, int hd, int len, int T) {
   return (sizeof(float) * attn_ws_floats(M, nh, hd, len, T) + 15) / 16 * 16;
 }
 extern "C" size_t g4_attn_splitkv_ws_bytes(int M, int nh, int hd, int kmin, int kmax, int T) {
-  return attn_counter_offset(M, nh, hd, kmax - kmin + 1, T) + sizeof(int) * (size_t)M * nh;
+  return attn_counter_offset(M, nh, hd, kmax - kmin + 1, T) + sizeof(int) * (size_t)attn_counter_count(M, nh, hd);
 }
 
 // One-kernel path (k_attn_short) when every chunk has at most kAttnShortKeys keys; max_len bounds
 // the key range (the device may pick a shorter one) and sizes the workspace.
+// zeroed_counters: caller-owned per-pair counters known to be 0 (the merging block of every pair
+// leaves its counter at 0 again); NULL = use the workspace's and reset them first.
 static int launch_attn_short(const uint16_t* Kc, const uint16_t* Vc, const float* q, const AttnDesc& d, void* ws,
-                             float* out, cudaStream_t st, int max_len) {
+                             float* out, cudaStream_t st, int max_len, int* zeroed_counters = nullptr) {
   const int nmh = d.M * d.nh;
   const size_t smem = attn_short_smem(d.hd);
-  int* counters = reinterpret_cast<int*>(static_cast<char*>(ws) + attn_counter_offset(d.M, d.nh, d.hd, max_len, d.T));
-  cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int) * (size_t)nmh, st);
-  if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "attention: counter reset: %s", cudaGetErrorString(e));
+  int* counters = zeroed_counters;
+  if (counters == nullptr) {
+    counters = reinterpret_cast<int*>(static_cast<char*>(ws) + attn_counter_offset(d.M, d.nh, d.hd, max_len, d.T));
+    cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int) * (size_t)nmh, st);
+    if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "attention: counter reset: %s", cudaGetErrorString(e));
+  }
   float* w = static_cast<float*>(ws);
   const dim3 grid(d.T, nmh);
-  auto launch = [&](auto kern) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<grid, 256, smem, st>>>(Kc, Vc, q, d, w, counters, out);
-  };
-  if (d.hd == 256) launch(k_attn_short<16>);
-  else if (d.hd == 128) launch(k_attn_short<8>);
-  else return set_error(G4_ERR_UNSUPPORTED, "attention: hd=%d", d.hd);
+  if (d.hd == 256) {
+    cudaFuncSetAttribute(k_attn_short<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (int rc = launch("k_attn_short", k_attn_short<16>, grid, dim3(256), smem, st, Kc, Vc, q, d, w, counters, out))
+      return rc;
+  } else if (d.hd == 128) {
+    cudaFuncSetAttribute(k_attn_short<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (int rc = launch("k_attn_short", k_attn_short<8>, grid, dim3(256), smem, st, Kc, Vc, q, d, w, counters, out))
+      return rc;
+  } else {
+    return set_error(G4_ERR_UNSUPPORTED, "attention: hd=%d", d.hd);
+  }
   return check_launch("k_attn_short");
 }
 static bool short_fits(int max_len, int T, int hd) {
@@ -583,7 +780,7 @@ extern "C" int g4_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, const flo
 // see and sizes the score grid (blocks past kmax return at once).  ws must hold max_len keys.
 int g4::attn_splitkv_dev(const uint16_t* Kc, const uint16_t* Vc, const float* q, int M, int nh, int hd, const int* dP,
                          int base_add, int q_add, int window, int max_len, int T, float* out, void* ws, size_t ws_bytes,
-                         cudaStream_t st, QuantOut qo) {
+                         cudaStream_t st, QuantOut qo, int* zeroed_counters) {
   G4_REQUIRE(Kc && Vc && q && out && ws && dP && max_len >= 1, "attn_splitkv_dev: bad arguments");
   int pos[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
   for (int m = 0; m < M && m < 4; ++m) pos[m] = m;
@@ -593,8 +790,8 @@ int g4::attn_splitkv_dev(const uint16_t* Kc, const uint16_t* Vc, const float* q,
   d.qo = qo;
   const size_t need = g4_attn_splitkv_ws_bytes(M, nh, hd, 0, max_len - 1, T);
   if (ws_bytes < need) return set_error(G4_ERR_NOMEM, "attn_splitkv_dev: workspace %zu < %zu bytes", ws_bytes, need);
-  if (short_fits(max_len, T, hd)) return launch_attn_short(Kc, Vc, q, d, ws, out, st, max_len);
-  return launch_attn(Kc, Vc, q, d, static_cast<float*>(ws), out, st, max_len);
+  if (short_fits(max_len, T, hd)) return launch_attn_short(Kc, Vc, q, d, ws, out, st, max_len, zeroed_counters);
+  return launch_attn(Kc, Vc, q, d, static_cast<float*>(ws), out, st, max_len, zeroed_counters);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -653,5 +850,5 @@ extern "C" int g4_attn_splitkv_noalloc(const uint16_t* Kc, const uint16_t* Vc, c
   float* w = nullptr;
   if (int rc = attn_scratch_for_current_device(&w)) return rc;
   cudaStream_t st = as_stream(stream);
-  return launch_attn(Kc, Vc, q, d, w, out, st);
+  return launch_attn(Kc, Vc, q, d, w, out, st, 0, nullptr, /*four=*/true);
 }

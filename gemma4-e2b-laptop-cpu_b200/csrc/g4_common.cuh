@@ -22,6 +22,12 @@ __device__ __forceinline__ uint32_t f2bf(float f) {
 }
 __device__ __forceinline__ float r16(float f) { return bf2f(f2bf(f)); }
 
+// Programmatic dependent launch (see launch() in g4_api.h): pdl_wait() returns once the grid this
+// kernel depends on has completed and its writes are visible (at once for an ordinary launch);
+// pdl_trigger() allows the next dependent grid to begin launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Exact small-integer to float: 0x4B000000 | t is the float 2^23 + t for 0 <= t < 2^23.
 __device__ __forceinline__ float u4f(uint32_t t) { return __fsub_rn(__uint_as_float(0x4B000000u | t), 8388608.0f); }
 

@@ -105,6 +105,8 @@ struct g4_engine {
   int* G;
   int* hio = nullptr;  // pinned host mirror: ctl [8 + MMAX], then G [MMAX], then drafts [8]
   void* attn_ws = nullptr;
+  int* attn_cnt = nullptr;  // per-(row, head) counters of the captured rounds' attention, 0 between calls
+  bool pdl_ok = true;       // captures use programmatic dependent launch unless that failed once
   size_t attn_ws_bytes = 0;
   void* head_ws = nullptr;
   size_t head_ws_bytes = 0;
@@ -119,6 +121,7 @@ struct g4_engine {
   // positions are read from ctl[0] on the device, so one capture serves every round
   cudaGraphExec_t gverify[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   cudaGraphExec_t gdraft = nullptr;
+  int gk_verify[5] = {0, 0, 0, 0, 0}, gk_draft = 0;  // kernel nodes of each graph
   cudaEvent_t tev[4] = {nullptr, nullptr, nullptr, nullptr};  // draft start/end, verify start/end
   int fake_n = 0;
   // decode state between g4_engine_decode calls
@@ -304,6 +307,9 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
   if (!rc) rc = ealloc_t(e, &e->G, (size_t)MM);
   e->attn_ws_bytes = g4_attn_splitkv_ws_bytes(4, d.NQ, d.HD, 0, c.ctx_max - 1, c.attn_chunks);
   if (!rc) rc = ealloc(e, &e->attn_ws, e->attn_ws_bytes);
+  if (!rc) rc = ealloc_t(e, &e->attn_cnt, 64);
+  if (!rc && cudaMemsetAsync(e->attn_cnt, 0, 64 * sizeof(int), e->st) != cudaSuccess)  // captured attention's counters
+    rc = set_error(G4_ERR_CUDA, "g4_engine_create: counter reset");
   e->head_ws_bytes = g4_head_screen_ws_bytes(4, d.V, c.screen_lim);
   if (!rc) rc = ealloc(e, &e->head_ws, e->head_ws_bytes);
   if (!rc) rc = ealloc_t(e, &e->head_ns, 4);
@@ -384,8 +390,8 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
   PhaseTimer& pf = e->prof;
   const QuantOut qo = quant_out(e, M, false);
   pf.mark(e->st, PH_EMBED_NORM);
-  k_embed<<<M, 256, 0, e->st>>>(e->E, e->toks, H, sqrtH, e->x);
-  k_norm_q<<<M, 256, 0, e->st>>>(e->x, e->L[0].in_ln, H, e->a, 0, qo);
+  RCK(launch("k_embed", k_embed, dim3(M), dim3(256), 0, e->st, e->E, e->toks, H, sqrtH, e->x));
+  RCK(launch("k_norm_q", k_norm_q, dim3(M), dim3(256), 0, e->st, e->x, e->L[0].in_ln, H, e->a, 0, qo));
   RCK(check_launch("k_norm_q"));
   for (int l = 0; l < d.NL; ++l) {
     const TLayer& t = e->L[l];
@@ -397,16 +403,16 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
     pf.mark(e->st, PH_EMBED_NORM);
     const bool split = dyn || (M <= 4 && pos0 + M > e->cfg.att_par);
     // split-KV reads the rotated queries from qs ([M][QD]); the per-row paths read them in place
-    k_qkv_post<<<dim3(M, d.NQ + 2), 256, 0, e->st>>>(e->qkv, ld, d.NQ, d.HD, dyn ? 1 : pos0, dyn ? e->ctl : nullptr,
+    RCK(launch("k_qkv_post", k_qkv_post, dim3(dim3(M, d.NQ + 2)), dim3(256), 0, e->st, e->qkv, ld, d.NQ, d.HD, dyn ? 1 : pos0, dyn ? e->ctl : nullptr,
                                                      t.qn, t.kn, e->rope[ty][0], e->rope[ty][1], Kc, Vc,
-                                                     split ? e->qs : e->qkv, split ? QD : ld);
+                                                     split ? e->qs : e->qkv, split ? QD : ld));
     RCK(check_launch("k_qkv_post"));
     pf.mark(e->st, PH_ATTN);
     bool att_q = false;
     if (dyn) {
       const int max_len = t.global ? e->cfg.ctx_max : std::min(e->cfg.ctx_max, d.WINDOW + 4);
       RCK(attn_splitkv_dev(Kc, Vc, e->qs, M, d.NQ, d.HD, e->ctl, 1, 1, t.global ? 0 : d.WINDOW, max_len,
-                           e->cfg.attn_chunks, e->att, e->attn_ws, e->attn_ws_bytes, e->st, qo));
+                           e->cfg.attn_chunks, e->att, e->attn_ws, e->attn_ws_bytes, e->st, qo, e->attn_cnt));
       att_q = true;
     } else if (split) {
       // split-KV (:1305-1327)
@@ -428,19 +434,19 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
     pf.mark(e->st, PH_LINEAR);
     RCK(lin(e, t.o, e->att, M, e->o, false, att_q));
     pf.mark(e->st, PH_EMBED_NORM);
-    k_post_attn_q<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_attn, t.pre_ff, e->mlp_in, H, qo);
+    RCK(launch("k_post_attn_q", k_post_attn_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, t.post_attn, t.pre_ff, e->mlp_in, H, qo));
     pf.mark(e->st, PH_LINEAR);
     RCK(lin(e, t.gu, e->mlp_in, M, e->gu, false, true));
     pf.mark(e->st, PH_EMBED_NORM);
-    k_act_q<<<(unsigned)((long long)M * d.I / 256), 256, 0, e->st>>>(e->gu, d.I, M, e->act, qo);
+    RCK(launch("k_act_q", k_act_q, dim3((unsigned)((long long)M * d.I / 256)), dim3(256), 0, e->st, e->gu, d.I, M, e->act, qo));
     pf.mark(e->st, PH_LINEAR);
     RCK(lin(e, t.down, e->act, M, e->o, false, true));
     pf.mark(e->st, PH_EMBED_NORM);
     if (l + 1 < d.NL)  // residual (layer scalar 1) and the next layer's input norm
-      k_resid_norm_q<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_ff, 1.0f, H, e->L[l + 1].in_ln, e->a, 0, qo);
+      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, t.post_ff, 1.0f, H, e->L[l + 1].in_ln, e->a, 0, qo));
     else  // residual and the final norm (rounded) of every row into hbuf
-      k_resid_norm_q<<<M, 256, 0, e->st>>>(e->o, e->x, t.post_ff, 1.0f, H, e->fnorm, e->hbuf, 1,
-                                           QuantOut{nullptr, nullptr, nullptr});
+      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, t.post_ff, 1.0f, H, e->fnorm, e->hbuf, 1,
+                                           QuantOut{nullptr, nullptr, nullptr}));
     RCK(check_launch("layer"));
   }
   pf.mark(e->st, PH_HEAD);
@@ -474,10 +480,10 @@ static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos,
   const int H = d.H;
   const QuantOut qo{e->xq, e->xsx, e->xsum};
   e->prof.mark(e->st, PH_DRAFT);
-  k_draft_in<<<8, 256, 0, e->st>>>(e->E, dtok_in, h, H, sqrtf((float)H), e->dcomb);
+  RCK(launch("k_draft_in", k_draft_in, dim3(8), dim3(256), 0, e->st, e->E, dtok_in, h, H, sqrtf((float)H), e->dcomb));
   RCK(lin(e, e->dpre, e->dcomb, 1, e->dx, true));
-  k_round<<<gridfor(H), 256, 0, e->st>>>(e->dx, H);
-  k_norm_q<<<1, 256, 0, e->st>>>(e->dx, e->DL[0].in_ln, H, e->da, 0, qo);
+  RCK(launch("k_round", k_round, dim3(gridfor(H)), dim3(256), 0, e->st, e->dx, H));
+  RCK(launch("k_norm_q", k_norm_q, dim3(1), dim3(256), 0, e->st, e->dx, e->DL[0].in_ln, H, e->da, 0, qo));
   for (int l = 0; l < d.DL; ++l) {
     const DLayerW& t = e->DL[l];
     const int ty = t.global ? 1 : 0;
@@ -487,15 +493,15 @@ static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos,
       if (d.global_layer(l2) == t.global) { tl = l2; break; }
     if (tl < 0) return set_error(G4_ERR_UNSUPPORTED, "draft_step: the target has no %s layer", t.global ? "global" : "sliding");
     RCK(lin(e, t.q, e->da, 1, e->dq, true, true));
-    k_q_post<<<d.NQ, 256, 0, e->st>>>(e->dq, d.HD, dyn ? 1 + j : pos, dyn ? e->ctl : nullptr, t.qn, e->rope[ty][0],
-                                      e->rope[ty][1]);
+    RCK(launch("k_q_post", k_q_post, dim3(d.NQ), dim3(256), 0, e->st, e->dq, d.HD, dyn ? 1 + j : pos, dyn ? e->ctl : nullptr, t.qn, e->rope[ty][0],
+                                      e->rope[ty][1]));
     const uint16_t* Kt = e->Kc + (size_t)tl * e->cfg.ctx_max * d.HD;
     const uint16_t* Vt = e->Vc + (size_t)tl * e->cfg.ctx_max * d.HD;
     bool att_q = false;
     if (dyn) {
       const int max_len = t.global ? e->cfg.ctx_max : std::min(e->cfg.ctx_max, d.WINDOW);
       RCK(attn_splitkv_dev(Kt, Vt, e->dq, 1, d.NQ, d.HD, e->ctl, 0, 1 + j, t.global ? 0 : d.WINDOW, max_len,
-                           e->cfg.attn_chunks, e->dopt, e->attn_ws, e->attn_ws_bytes, e->st, qo));
+                           e->cfg.attn_chunks, e->dopt, e->attn_ws, e->attn_ws_bytes, e->st, qo, e->attn_cnt));
       att_q = true;
     } else {
       const int lo = t.global ? 0 : std::max(0, pos - (d.WINDOW - 1));
@@ -505,24 +511,24 @@ static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos,
     }
     RCK(lin(e, t.o, e->dopt, 1, e->da, true, att_q));
     // o residual (no layer scalar), then the pre-MLP norm (rounded)
-    k_resid_norm_q<<<1, 256, 0, e->st>>>(e->da, e->dx, t.post_attn, 0.0f, H, t.pre_ff, e->da, 1, qo);
+    RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(1), dim3(256), 0, e->st, e->da, e->dx, t.post_attn, 0.0f, H, t.pre_ff, e->da, 1, qo));
     RCK(lin(e, t.gu, e->da, 1, e->dgu, true, true));
-    k_act_q<<<(unsigned)(d.I / 256), 256, 0, e->st>>>(e->dgu, d.I, 1, e->dact, qo);
+    RCK(launch("k_act_q", k_act_q, dim3((unsigned)(d.I / 256)), dim3(256), 0, e->st, e->dgu, d.I, 1, e->dact, qo));
     RCK(lin(e, t.down, e->dact, 1, e->da, true, true));
     // MLP residual with the layer scalar 1, then the next layer's input norm or the final norm
     if (l + 1 < d.DL)
-      k_resid_norm_q<<<1, 256, 0, e->st>>>(e->da, e->dx, t.post_ff, 1.0f, H, e->DL[l + 1].in_ln, e->da, 0, qo);
+      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(1), dim3(256), 0, e->st, e->da, e->dx, t.post_ff, 1.0f, H, e->DL[l + 1].in_ln, e->da, 0, qo));
     else
-      k_resid_norm_q<<<1, 256, 0, e->st>>>(e->da, e->dx, t.post_ff, 1.0f, H, e->dnorm, e->dh, 1, qo);
+      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(1), dim3(256), 0, e->st, e->da, e->dx, t.post_ff, 1.0f, H, e->dnorm, e->dh, 1, qo));
     RCK(check_launch("draft layer"));
   }
   RCK(lin(e, e->dpost, e->dh, 1, e->bcur, true, true));
   RCK(lin(e, e->dcent, e->dh, 1, e->dscore, true, true));
-  k_round<<<gridfor(H), 256, 0, e->st>>>(e->bcur, H);
+  RCK(launch("k_round", k_round, dim3(gridfor(H)), dim3(256), 0, e->st, e->bcur, H));
   const int nc = d.DTOP * d.DPER;
-  k_topk_cand<<<(d.DCENT + 31) / 32, 256, sizeof(float) * d.DCENT, e->st>>>(e->dscore, d.DCENT, d.DTOP, d.DPER, d.V, e->cand);
-  k_cand_scores<<<(nc * 16 + 255) / 256, 256, 0, e->st>>>(e->E, e->cand, nc, e->dh, H, e->cscore);
-  k_cand_best<<<1, 1024, 0, e->st>>>(e->cscore, e->cand, nc, dtok_out);
+  RCK(launch("k_topk_cand", k_topk_cand, dim3((d.DCENT + 31) / 32), dim3(256), sizeof(float) * d.DCENT, e->st, e->dscore, d.DCENT, d.DTOP, d.DPER, d.V, e->cand));
+  RCK(launch("k_cand_scores", k_cand_scores, dim3((nc * 16 + 255) / 256), dim3(256), 0, e->st, e->E, e->cand, nc, e->dh, H, e->cscore));
+  RCK(launch("k_cand_best", k_cand_best, dim3(1), dim3(1024), 0, e->st, e->cscore, e->cand, nc, dtok_out));
   e->prof.mark(e->st, PH_COPY);
   return check_launch("draft_step");
 }
@@ -619,11 +625,14 @@ extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int
   return G4_OK;
 }
 
-// Record the launches of body() on the engine stream into an executable graph.
+// Record the launches of body() on the engine stream into an executable graph, its kernels launched
+// for programmatic dependent launch; if that capture fails, record it again with ordinary launches.
 template <class F>
-static int capture(g4_engine* e, cudaGraphExec_t* out, F body) {
+static int capture_once(g4_engine* e, cudaGraphExec_t* out, F body, bool pdl, int* kernels) {
   ECK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+  pdl_enabled() = pdl;
   const int rc = body();
+  pdl_enabled() = false;
   cudaGraph_t g = nullptr;
   const cudaError_t ce = cudaStreamEndCapture(e->st, &g);
   if (rc != G4_OK) {
@@ -631,10 +640,29 @@ static int capture(g4_engine* e, cudaGraphExec_t* out, F body) {
     return rc;
   }
   if (ce != cudaSuccess) return set_error(G4_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+  size_t nn = 0;
+  if (kernels && cudaGraphGetNodes(g, nullptr, &nn) == cudaSuccess && nn > 0) {
+    std::vector<cudaGraphNode_t> nodes(nn);
+    *kernels = 0;
+    if (cudaGraphGetNodes(g, nodes.data(), &nn) == cudaSuccess)
+      for (size_t i = 0; i < nn; ++i) {
+        cudaGraphNodeType ty;
+        if (cudaGraphNodeGetType(nodes[i], &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++*kernels;
+      }
+  }
   const cudaError_t ie = cudaGraphInstantiate(out, g, 0);
   cudaGraphDestroy(g);
   if (ie != cudaSuccess) return set_error(G4_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ie));
   return G4_OK;
+}
+template <class F>
+static int capture(g4_engine* e, cudaGraphExec_t* out, F body, int* kernels) {
+  if (e->cfg.graphs == 1 && e->pdl_ok) {
+    if (capture_once(e, out, body, true, kernels) == G4_OK) return G4_OK;
+    cudaGetLastError();
+    e->pdl_ok = false;
+  }
+  return capture_once(e, out, body, false, kernels);
 }
 
 // The k MTP drafts of a round from ctl (tokens[0] = the confirmed token, ctl[0] = P) and hprev:
@@ -699,10 +727,13 @@ extern "C" int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, in
     if (drafting) {
       ECK(cudaEventRecord(e->tev[0], e->st));
       if (use_g) {
-        if (!e->gdraft) RCK(capture(e, &e->gdraft, [&] { return draft_chain(e, true); }));
+        if (!e->gdraft) RCK(capture(e, &e->gdraft, [&] { return draft_chain(e, true); }, &e->gk_draft));
         ECK(cudaGraphLaunch(e->gdraft, e->st));
+        e->stats.kernel_launches += e->gk_draft;
       } else {
+        const long long l0 = launch_count();
         RCK(draft_chain(e, false));
+        e->stats.kernel_launches += launch_count() - l0;
       }
       ECK(cudaEventRecord(e->tev[1], e->st));
       e->stats.drafted += e->cfg.k_draft;
@@ -711,10 +742,13 @@ extern "C" int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, in
     }
     ECK(cudaEventRecord(e->tev[2], e->st));
     if (use_g) {
-      if (!e->gverify[M]) RCK(capture(e, &e->gverify[M], [&] { return forward(e, M, 0, true, 0, true); }));
+      if (!e->gverify[M]) RCK(capture(e, &e->gverify[M], [&] { return forward(e, M, 0, true, 0, true); }, &e->gk_verify[M]));
       ECK(cudaGraphLaunch(e->gverify[M], e->st));
+      e->stats.kernel_launches += e->gk_verify[M];
     } else {
+      const long long l0 = launch_count();
       RCK(forward(e, M, e->P + 1, true, 0));
+      e->stats.kernel_launches += launch_count() - l0;
     }
     ECK(cudaEventRecord(e->tev[3], e->st));
     ECK(cudaMemcpyAsync(hG, e->G, sizeof(int) * M, cudaMemcpyDeviceToHost, e->st));

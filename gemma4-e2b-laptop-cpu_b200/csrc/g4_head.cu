@@ -200,6 +200,8 @@ __device__ __forceinline__ float bf16p_patch(const HeadPacked& P, int n, const f
 template <int M>
 __global__ void __launch_bounds__(256) k_bf16p_gemv(HeadPacked P, const float* __restrict__ X, float* __restrict__ Y,
                                                     int ldy, const int* __restrict__ gate) {
+  pdl_wait();
+  pdl_trigger();
   if (gate != nullptr && *gate == 0) return;
   const int j = threadIdx.x & 7;
   const int n_raw = blockIdx.x * 32 + (threadIdx.x >> 3);
@@ -236,6 +238,8 @@ template <int M>
 __global__ void __launch_bounds__(256) k_bf16p_gemv_staged(HeadPacked P, const float* __restrict__ X,
                                                            float* __restrict__ Y, int ldy,
                                                            const int* __restrict__ gate) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int NP = (M + 1) / 2;
   if (gate != nullptr && *gate == 0) return;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -339,23 +343,54 @@ __global__ void __launch_bounds__(256) k_bf16p_gemv_staged(HeadPacked P, const f
 
 // Row-per-thread variant: one thread runs all eight octet-lane chains of its row (the lanes of the
 // reference's 8-wide vectors), so each group's exponent codes are decoded once for every
-// activation row.  The thread reads its row straight from global memory, four groups (176 bytes)
-// at a time as 11 aligned 16-byte loads through L1 (the 32 rows of a warp share no cache lines,
-// each 128-byte line serves 8 consecutive loads of its thread), so occupancy is set by registers,
-// not shared memory.  A persistent grid takes 256-row tiles in turn; the activations sit in shared
-// memory as [k][pair] float2 (one 16-byte broadcast load per element for four rows).  Values are
-// those of k_bf16p_gemv.
-constexpr int kBrThreads = 256;
-__host__ __device__ inline size_t head_rows_smem(int M, int K) { return (size_t)K * ((M + 1) / 2) * 8; }
+// activation row.  A persistent CTA takes blocks of kBrRows rows; per pipeline item every row
+// brings 4 groups (176 bytes) by its own bulk copy into one of kBrNS shared-memory stages, issued
+// kBrNS items ahead; rows sit kBrStride = 208 bytes apart (an odd multiple of 16), so the 8 threads
+// of a 16-byte load phase read 8 different bank quads.  Four weights at a time are decoded with
+// byte permutes: the exponent codes of 4 consecutive elements are spread to bytes by one multiply
+// per bit plane and turned into a permute selector over the 8-entry codebook; the sign/mantissa
+// word and the 4 exponents give the 4 bf16 high and low bytes, which 2 permutes interleave into
+// 2 x 2 floats.  Lane j's chain order (elements j, 16+j, 8+j, 24+j) is kept by visiting the
+// element octets 0, 2, 1, 3 of each group.  The activations sit in shared memory as [k][pair]
+// float2 (one 16-byte broadcast load per element for four rows).  Values are those of
+// k_bf16p_gemv.
+constexpr int kBrRows = 256, kBrStride = 208, kBrNS = 3;
+__host__ __device__ inline size_t head_rows_smem(int M, int K) {
+  return 128 + (size_t)kBrNS * kBrRows * kBrStride + (size_t)K * ((M + 1) / 2) * 8;
+}
 
 template <int M>
-__global__ void __launch_bounds__(kBrThreads) k_bf16p_rows(HeadPacked P, const float* __restrict__ X,
-                                                           float* __restrict__ Y, int ldy, const int* __restrict__ gate) {
+__global__ void __launch_bounds__(kBrRows) k_bf16p_rows(HeadPacked P, const float* __restrict__ X,
+                                                        float* __restrict__ Y, int ldy, const int* __restrict__ gate) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int NP = (M + 1) / 2;
   if (gate != nullptr && *gate == 0) return;
-  extern __shared__ __align__(16) float2 xs[];  // [K][NP]
-  const int K = P.K, G = K >> 5, rowb = G * 44;
-  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint8_t* stages = smem + 128;
+  float2* xs = reinterpret_cast<float2*>(stages + (size_t)kBrNS * kBrRows * kBrStride);  // [K][NP]
+  const int K = P.K, G = K >> 5, nch = G / 4, rowb = G * 44;
+  const int nblk = (P.N + kBrRows - 1) / kBrRows;
+  const int myblk = nblk > (int)blockIdx.x ? (nblk - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int nitems = myblk * nch;
+  const int r = threadIdx.x;
+  if (r == 0) {
+    for (int b = 0; b < kBrNS; ++b) mbar_init(&bars[b], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // item i: row block blockIdx.x + (i / nch) * gridDim.x, groups [4c, 4c + 4) with c = i % nch
+  auto issue = [&](int i, int st) {
+    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
+    const int r0 = blk * kBrRows, nr = min(kBrRows, P.N - r0);
+    if (r == 0) mbar_expect_tx(&bars[st], 176u * (uint32_t)nr);
+    if (r < nr)
+      bulk_g2s(stages + ((size_t)st * kBrRows + r) * kBrStride, P.data + (size_t)(r0 + r) * rowb + (size_t)c * 176, 176u,
+               &bars[st]);
+  };
+  for (int b = 0; b < kBrNS && b < nitems; ++b) issue(b, b);
+  for (int i = r; i < K; i += blockDim.x) {
     float v[2 * NP];
 #pragma unroll
     for (int m = 0; m < 2 * NP; ++m) v[m] = m < M ? X[(size_t)m * K + i] : 0.f;
@@ -364,77 +399,100 @@ __global__ void __launch_bounds__(kBrThreads) k_bf16p_rows(HeadPacked P, const f
   }
   __syncthreads();
   const uint32_t cb_lo = P.cb_lo, cb_hi = P.cb_hi;
-  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n - (int)threadIdx.x < P.N; n += gridDim.x * blockDim.x) {
-    if (n >= P.N) continue;
-    const uint4* rowp = reinterpret_cast<const uint4*>(P.data + (size_t)n * rowb);
-    float2 acc[8][NP];
+  float2 acc[8][NP];
+  for (int i = 0; i < nitems; ++i) {
+    const int st = i % kBrNS;
+    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
+    const int n = blk * kBrRows + r;
+    if (!cta_wait(&bars[st], (uint32_t)(i / kBrNS) & 1u)) return;
+    if (c == 0) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < 8; ++j)
 #pragma unroll
-      for (int p = 0; p < NP; ++p) acc[j][p] = make_float2(0.f, 0.f);
-#pragma unroll 1
-    for (int u = 0; u < G / 4; ++u) {
-      uint32_t wv[44];
+        for (int p = 0; p < NP; ++p) acc[j][p] = make_float2(0.f, 0.f);
+    }
+    const uint4* rowp = reinterpret_cast<const uint4*>(stages + ((size_t)st * kBrRows + r) * kBrStride);
+    uint32_t wv[44];
 #pragma unroll
-      for (int k = 0; k < 11; ++k) {
-        const uint4 t4 = __ldg(rowp + u * 11 + k);
-        wv[4 * k] = t4.x; wv[4 * k + 1] = t4.y; wv[4 * k + 2] = t4.z; wv[4 * k + 3] = t4.w;
-      }
+    for (int k = 0; k < 11; ++k) {
+      const uint4 t4 = rowp[k];
+      wv[4 * k] = t4.x; wv[4 * k + 1] = t4.y; wv[4 * k + 2] = t4.z; wv[4 * k + 3] = t4.w;
+    }
 #pragma unroll
-      for (int gg = 0; gg < 4; ++gg) {
-        const int g = u * 4 + gg;
-        const uint32_t* gw = wv + gg * 11;
-        const uint32_t p0 = gw[8], p1 = gw[9], p2 = gw[10];
-        const float2* xg = xs + (size_t)g * 32 * NP;
+    for (int gg = 0; gg < 4; ++gg) {
+      const int g = c * 4 + gg;
+      const uint32_t* gw = wv + gg * 11;
+      const uint32_t p0 = gw[8], p1 = gw[9], p2 = gw[10];
+      const float2* xg = xs + (size_t)g * 32 * NP;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t cc = ((p0 >> j) & 0x01010101u) | (((p1 >> j) & 0x01010101u) << 1) | (((p2 >> j) & 0x01010101u) << 2);
-          const uint32_t sel = (cc & 7u) | ((cc >> 4) & 0x70u) | ((cc >> 8) & 0x700u) | ((cc >> 12) & 0x7000u);
-          const uint32_t ex4 = __byte_perm(cb_lo, cb_hi, sel);  // exponent of element j + 8i in byte i
+      for (int oi = 0; oi < 4; ++oi) {
+        const int o8 = (oi == 1) ? 2 : (oi == 2 ? 1 : oi);  // element octets in chain order 0, 2, 1, 3
 #pragma unroll
-          for (int ii = 0; ii < 4; ++ii) {
-            const int i8 = (ii == 1) ? 2 : (ii == 2 ? 1 : ii);  // chain order: elements j, 16+j, 8+j, 24+j
-            const int e = j + 8 * i8;
-            const uint32_t smb = (gw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
-            const uint32_t ex = (ex4 >> (8 * i8)) & 0xFFu;
-            const float wgt = __uint_as_float((((smb & 0x80u) << 8) | (ex << 7) | (smb & 0x7Fu)) << 16);
+        for (int h = 0; h < 2; ++h) {
+          const int sh = 8 * o8 + 4 * h;  // elements sh .. sh+3 = lanes 4h .. 4h+3
+          const uint32_t s0 = (((p0 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
+          const uint32_t s1 = (((p1 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
+          const uint32_t s2 = (((p2 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
+          const uint32_t cc = s0 | (s1 << 1) | (s2 << 2);  // code of element sh + k in byte k
+          const uint32_t sel = __byte_perm(cc | (cc >> 4), 0u, 0x0020u);
+          const uint32_t ex4 = __byte_perm(cb_lo, cb_hi, sel);
+          const uint32_t smw = gw[sh >> 2];
+          const uint32_t hb4 = (smw & 0x80808080u) | ((ex4 >> 1) & 0x7F7F7F7Fu);
+          const uint32_t lb4 = ((ex4 << 7) & 0x80808080u) | (smw & 0x7F7F7F7Fu);
+          const uint32_t t01 = __byte_perm(lb4, hb4, 0x5140u), t23 = __byte_perm(lb4, hb4, 0x7362u);
+          const float wk[4] = {__uint_as_float(t01 << 16), __uint_as_float(t01 & 0xFFFF0000u),
+                               __uint_as_float(t23 << 16), __uint_as_float(t23 & 0xFFFF0000u)};
 #pragma unroll
-            for (int p = 0; p < NP; ++p) acc[j][p] = __ffma2_rn(make_float2(wgt, wgt), xg[e * NP + p], acc[j][p]);
+          for (int k = 0; k < 4; ++k) {
+            const int e = sh + k, j = 4 * h + k;
+#pragma unroll
+            for (int p = 0; p < NP; ++p) acc[j][p] = __ffma2_rn(make_float2(wk[k], wk[k]), xg[e * NP + p], acc[j][p]);
           }
         }
       }
     }
-    float y[2 * NP];
-#pragma unroll
-    for (int p = 0; p < NP; ++p) {
-      // hsum8: ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7))
-      y[2 * p] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].x, acc[4][p].x), __fadd_rn(acc[1][p].x, acc[5][p].x)),
-                           __fadd_rn(__fadd_rn(acc[2][p].x, acc[6][p].x), __fadd_rn(acc[3][p].x, acc[7][p].x)));
-      y[2 * p + 1] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].y, acc[4][p].y), __fadd_rn(acc[1][p].y, acc[5][p].y)),
-                               __fadd_rn(__fadd_rn(acc[2][p].y, acc[6][p].y), __fadd_rn(acc[3][p].y, acc[7][p].y)));
-    }
-    for (long long e = P.exc_ptr[n]; e < P.exc_ptr[n + 1]; ++e) {  // CSR order, unfused (bf16_exp3_head.h:103)
-      const float dl = P.exc_delta[e];
-      const int col = P.exc_col[e];
+    if (c == nch - 1 && n < P.N) {
+      float y[2 * NP];
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
-        const float2 xv = xs[(size_t)col * NP + p];
-        y[2 * p] = __fadd_rn(y[2 * p], __fmul_rn(dl, xv.x));
-        y[2 * p + 1] = __fadd_rn(y[2 * p + 1], __fmul_rn(dl, xv.y));
+        // hsum8: ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7))
+        y[2 * p] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].x, acc[4][p].x), __fadd_rn(acc[1][p].x, acc[5][p].x)),
+                             __fadd_rn(__fadd_rn(acc[2][p].x, acc[6][p].x), __fadd_rn(acc[3][p].x, acc[7][p].x)));
+        y[2 * p + 1] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].y, acc[4][p].y), __fadd_rn(acc[1][p].y, acc[5][p].y)),
+                                 __fadd_rn(__fadd_rn(acc[2][p].y, acc[6][p].y), __fadd_rn(acc[3][p].y, acc[7][p].y)));
       }
-    }
+      for (long long e = P.exc_ptr[n]; e < P.exc_ptr[n + 1]; ++e) {  // CSR order, unfused (bf16_exp3_head.h:103)
+        const float dl = P.exc_delta[e];
+        const int col = P.exc_col[e];
 #pragma unroll
-    for (int m = 0; m < M; ++m) Y[(size_t)m * ldy + n] = y[m];
+        for (int p = 0; p < NP; ++p) {
+          const float2 xv = xs[(size_t)col * NP + p];
+          y[2 * p] = __fadd_rn(y[2 * p], __fmul_rn(dl, xv.x));
+          y[2 * p + 1] = __fadd_rn(y[2 * p + 1], __fmul_rn(dl, xv.y));
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) Y[(size_t)m * ldy + n] = y[m];
+    }
+    __syncthreads();  // stage st is consumed by every row
+    if (i + kBrNS < nitems) {
+      fence_proxy_async_smem();
+      issue(i + kBrNS, st);
+    }
   }
 }
 
 // ------------------------------------------------------------------------------ greedy pick
 // Slots per row m: [0] ordered-int max of r16 logits, [1] winner index.
 __global__ void k_pick_init(int* __restrict__ slots, int M) {
+  pdl_wait();
+  pdl_trigger();
   const int m = threadIdx.x;
   if (m < M) { slots[2 * m] = f2ord(-1e30f); slots[2 * m + 1] = 0x7FFFFFFF; }
 }
 __global__ void k_pick_max(const float* __restrict__ Y, int N, int ldy, int* __restrict__ slots, const int* __restrict__ gate) {
+  pdl_wait();
+  pdl_trigger();
   if (gate != nullptr && *gate == 0) return;
   const int m = blockIdx.y;
   float mx = -1e30f;
@@ -445,6 +503,8 @@ __global__ void k_pick_max(const float* __restrict__ Y, int N, int ldy, int* __r
 }
 // lowest index with v >= mx - 2 and cap(v) == cap(mx) (gemma4_engine.cpp:1496)
 __global__ void k_pick_idx(const float* __restrict__ Y, int N, int ldy, int* __restrict__ slots, const int* __restrict__ gate) {
+  pdl_wait();
+  pdl_trigger();
   if (gate != nullptr && *gate == 0) return;
   const int m = blockIdx.y;
   const float mx = ord2f(slots[2 * m]);
@@ -459,6 +519,8 @@ __global__ void k_pick_idx(const float* __restrict__ Y, int N, int ldy, int* __r
   if ((threadIdx.x & 31) == 0 && best != 0x7FFFFFFF) atomicMin(&slots[2 * m + 1], best);
 }
 __global__ void k_pick_out(const int* __restrict__ slots, int M, int* __restrict__ out, const int* __restrict__ gate) {
+  pdl_wait();
+  pdl_trigger();
   if (gate != nullptr && *gate == 0) return;
   const int m = threadIdx.x;
   if (m < M) out[m] = slots[2 * m + 1] == 0x7FFFFFFF ? -1 : slots[2 * m + 1];
@@ -540,6 +602,8 @@ static size_t screen_ws_layout(int M, int N, int lim, ScreenWs* w, char* base) {
 
 // |h| per row in double, in the order of ss_avx2 (gemma4_engine.cpp:326-343); one warp per row.
 __global__ void k_screen_init(const float* __restrict__ H, int K, int M, ScreenWs w) {
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x, lane = threadIdx.x;
   double s = 0;
   if (lane < 16) {
@@ -560,6 +624,8 @@ __global__ void k_screen_init(const float* __restrict__ H, int K, int M, ScreenW
 }
 // L = max over rows of fma(-c, hn, s) (screen_task :484, vmx)
 __global__ void k_screen_L(const float* __restrict__ coef, int N, ScreenWs w) {
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.y;
   const float hn = w.hn[m];
   float mx = -1e30f;
@@ -570,12 +636,16 @@ __global__ void k_screen_L(const float* __restrict__ coef, int N, ScreenWs w) {
   if ((threadIdx.x & 31) == 0) atomicMax(&w.Lord[m], f2ord(mx));
 }
 __global__ void k_screen_thr(int M, ScreenWs w) {
+  pdl_wait();
+  pdl_trigger();
   const int m = threadIdx.x;
   if (m < M) w.thr[m] = calc_thr(ord2f(w.Lord[m]));
 }
 // survivors: upper = fma(c, hn, s) >= thr (eval_row :1461); more than lim -> fallback flag.
 // Warp-uniform iteration with one atomic per warp; the order of the list is irrelevant.
 __global__ void k_screen_collect(const float* __restrict__ coef, int N, int lim, ScreenWs w) {
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.y, lane = threadIdx.x & 31;
   const float hn = w.hn[m], thr = w.thr[m];
   const int wstride = gridDim.x * blockDim.x;
@@ -596,6 +666,8 @@ __global__ void k_screen_collect(const float* __restrict__ coef, int N, int lim,
 }
 // rescore survivors with the exact head (octet per survivor, resc_task :540-571): fval = r16(y)
 __global__ void __launch_bounds__(256) k_screen_rescore(HeadPacked P, const float* __restrict__ H, int lim, ScreenWs w) {
+  pdl_wait();
+  pdl_trigger();
   if (*w.fb) return;
   const int m = blockIdx.y;
   const int count = min(w.cnt[m], lim);
@@ -614,6 +686,8 @@ __global__ void __launch_bounds__(256) k_screen_rescore(HeadPacked P, const floa
 // pick among survivors: max value, then lowest index with the tie rule (eval_row :1469-1471 with
 // ties to the lowest index).  One block per row.
 __global__ void k_screen_pick(int lim, ScreenWs w, int* __restrict__ out, int* __restrict__ nsurv) {
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   const int count = min(w.cnt[m], lim);
   if (threadIdx.x == 0) nsurv[m] = *w.fb ? -1 : count;
@@ -645,6 +719,8 @@ __global__ void k_screen_pick(int lim, ScreenWs w, int* __restrict__ out, int* _
 }
 // fallback pick writes the winners (only when the flag is set)
 __global__ void k_screen_fb_out(const int* __restrict__ slots, int M, const ScreenWs w, int* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   if (!*w.fb) return;
   const int m = threadIdx.x;
   if (m < M) out[m] = slots[2 * m + 1] == 0x7FFFFFFF ? -1 : slots[2 * m + 1];
@@ -764,35 +840,31 @@ static int num_sms() {
 }
 
 template <int M>
-static void launch_head_gemv(const HeadPacked& P, const float* X, float* Y, int ldy, const int* gate, cudaStream_t st) {
+static int launch_head_gemv(const HeadPacked& P, const float* X, float* Y, int ldy, const int* gate, cudaStream_t st) {
   const size_t rsmem = head_rows_smem(M, P.K);
   const char* hv = getenv("G4_HEAD_GEMV");  // "octet" selects the octet-per-row variant (experiments)
-  if (P.K % 128 == 0 && rsmem <= 100 * 1024 && aligned(P.data, 16) && !(hv && hv[0] == 'o')) {
-    if (rsmem > 48 * 1024) cudaFuncSetAttribute(k_bf16p_rows<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem);
-    int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_bf16p_rows<M>, kBrThreads, rsmem) != cudaSuccess || occ < 1)
-      occ = 1;
-    const int nblk = (P.N + kBrThreads - 1) / kBrThreads;
-    k_bf16p_rows<M><<<std::min(nblk, num_sms() * occ), kBrThreads, rsmem, st>>>(P, X, Y, ldy, gate);
-    return;
+  if (P.K % 128 == 0 && rsmem <= 227 * 1024 && aligned(P.data, 16) && !(hv && hv[0] == 'o')) {
+    cudaFuncSetAttribute(k_bf16p_rows<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem);
+    const int nblk = (P.N + kBrRows - 1) / kBrRows;
+    return launch("k_bf16p_rows", k_bf16p_rows<M>, dim3(std::min(nblk, num_sms())), dim3(kBrRows), rsmem, st, P, X, Y,
+                  ldy, gate);
   }
   const size_t smem = head_smem_bytes(M, P.K);
   if (P.K % 256 == 0 && smem <= 227 * 1024 && aligned(P.data, 16)) {
     cudaFuncSetAttribute(k_bf16p_gemv_staged<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int nblk = (P.N + kHeadBlkRows - 1) / kHeadBlkRows;
-    k_bf16p_gemv_staged<M><<<std::min(nblk, num_sms()), 256, smem, st>>>(P, X, Y, ldy, gate);
-  } else {
-    k_bf16p_gemv<M><<<(P.N + 31) / 32, 256, 0, st>>>(P, X, Y, ldy, gate);
+    return launch("k_bf16p_gemv_staged", k_bf16p_gemv_staged<M>, dim3(std::min(nblk, num_sms())), dim3(256), smem, st, P,
+                  X, Y, ldy, gate);
   }
+  return launch("k_bf16p_gemv", k_bf16p_gemv<M>, dim3((P.N + 31) / 32), dim3(256), 0, st, P, X, Y, ldy, gate);
 }
 static int head_gemv(const HeadPacked& P, const float* X, int M, float* Y, int ldy, const int* gate, cudaStream_t st) {
   switch (M) {
-    case 1: launch_head_gemv<1>(P, X, Y, ldy, gate, st); break;
-    case 2: launch_head_gemv<2>(P, X, Y, ldy, gate, st); break;
-    case 3: launch_head_gemv<3>(P, X, Y, ldy, gate, st); break;
-    default: launch_head_gemv<4>(P, X, Y, ldy, gate, st); break;
+    case 1: return launch_head_gemv<1>(P, X, Y, ldy, gate, st);
+    case 2: return launch_head_gemv<2>(P, X, Y, ldy, gate, st);
+    case 3: return launch_head_gemv<3>(P, X, Y, ldy, gate, st);
+    default: return launch_head_gemv<4>(P, X, Y, ldy, gate, st);
   }
-  return check_launch("k_bf16p_gemv");
 }
 
 extern "C" int g4_bf16p_gemm(const uint8_t* data, const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col,
@@ -804,10 +876,10 @@ extern "C" int g4_bf16p_gemm(const uint8_t* data, const uint8_t* cb8, const long
 }
 
 static int pick(const float* Y, int M, int N, int ldy, int* slots, int* out, const int* gate, cudaStream_t st) {
-  k_pick_init<<<1, 32, 0, st>>>(slots, M);
-  k_pick_max<<<dim3(296, M), 256, 0, st>>>(Y, N, ldy, slots, gate);
-  k_pick_idx<<<dim3(296, M), 256, 0, st>>>(Y, N, ldy, slots, gate);
-  if (out) k_pick_out<<<1, 32, 0, st>>>(slots, M, out, gate);
+  if (int rc_ = launch("k_pick_init", k_pick_init, dim3(1), dim3(32), 0, st, slots, M)) return rc_;
+  if (int rc_ = launch("k_pick_max", k_pick_max, dim3(dim3(296, M)), dim3(256), 0, st, Y, N, ldy, slots, gate)) return rc_;
+  if (int rc_ = launch("k_pick_idx", k_pick_idx, dim3(dim3(296, M)), dim3(256), 0, st, Y, N, ldy, slots, gate)) return rc_;
+  if (out) if (int rc_ = launch("k_pick_out", k_pick_out, dim3(1), dim3(32), 0, st, slots, M, out, gate)) return rc_;
   return check_launch("head pick");
 }
 
@@ -844,18 +916,18 @@ extern "C" int g4_head_screen(const uint8_t* W4p, const uint16_t* S4, const floa
   ScreenWs w;
   screen_ws_layout(M, N, lim, &w, static_cast<char*>(ws));
   const HeadPacked P = make_head(data, cb8, exc_ptr, exc_col, exc_delta, N, K);
-  k_screen_init<<<M, 32, 0, st>>>(H, K, M, w);
+  if (int rc_ = launch("k_screen_init", k_screen_init, dim3(M), dim3(32), 0, st, H, K, M, w)) return rc_;
   if (int rc = check_launch("k_screen_init")) return rc;
   if (int rc = g4_w4g32_gemm(W4p, S4, H, nullptr, M, N, K, w.s, N, stream)) return rc;
-  k_screen_L<<<dim3(296, M), 256, 0, st>>>(coef, N, w);
-  k_screen_thr<<<1, 32, 0, st>>>(M, w);
-  k_screen_collect<<<dim3(296, M), 256, 0, st>>>(coef, N, lim, w);
-  k_screen_rescore<<<dim3((lim + 31) / 32, M), 256, 0, st>>>(P, H, lim, w);
-  k_screen_pick<<<M, 256, 0, st>>>(lim, w, out_idx, out_nsurv);
+  if (int rc_ = launch("k_screen_L", k_screen_L, dim3(dim3(296, M)), dim3(256), 0, st, coef, N, w)) return rc_;
+  if (int rc_ = launch("k_screen_thr", k_screen_thr, dim3(1), dim3(32), 0, st, M, w)) return rc_;
+  if (int rc_ = launch("k_screen_collect", k_screen_collect, dim3(dim3(296, M)), dim3(256), 0, st, coef, N, lim, w)) return rc_;
+  if (int rc_ = launch("k_screen_rescore", k_screen_rescore, dim3(dim3((lim + 31) / 32, M)), dim3(256), 0, st, P, H, lim, w)) return rc_;
+  if (int rc_ = launch("k_screen_pick", k_screen_pick, dim3(M), dim3(256), 0, st, lim, w, out_idx, out_nsurv)) return rc_;
   if (int rc = check_launch("screen")) return rc;
   // fallback: full exact head for all rows, gated on the device flag
   if (int rc = head_gemv(P, H, M, w.s, N, w.fb, st)) return rc;
   if (int rc = pick(w.s, M, N, N, w.slots, nullptr, w.fb, st)) return rc;
-  k_screen_fb_out<<<1, 32, 0, st>>>(w.slots, M, w, out_idx);
+  if (int rc_ = launch("k_screen_fb_out", k_screen_fb_out, dim3(1), dim3(32), 0, st, w.slots, M, w, out_idx)) return rc_;
   return check_launch("k_screen_fb_out");
 }

@@ -50,6 +50,8 @@ __device__ __forceinline__ void stage_row(float* dst, const float* __restrict__ 
 
 // y[m] = (x[m]*r)*w, optionally rounded to bf16 (rms / rms_prep_x, :344-352, :365-381).
 __global__ void k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w, int n, float* __restrict__ y, int round) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ double red[17];
   const float* xm = x + (size_t)blockIdx.x * n;
   float* ym = y + (size_t)blockIdx.x * n;
@@ -62,6 +64,8 @@ __global__ void k_rmsnorm(const float* __restrict__ x, const float* __restrict__
 
 // x[m] = r16(E[tok[m]] * sqrt(H))   (embed, :1264)
 __global__ void k_embed(const uint16_t* __restrict__ E, const int* __restrict__ toks, int H, float sqrtH, float* __restrict__ x) {
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   const uint16_t* er = E + (size_t)toks[m] * H;
   for (int i = threadIdx.x; i < H; i += blockDim.x) x[(size_t)m * H + i] = r16(__fmul_rn(bf2f(er[i]), sqrtH));
@@ -75,6 +79,8 @@ __global__ void k_qkv_post(const float* __restrict__ qkv, int ldqkv, int nq, int
                            const int* __restrict__ dpos, const float* __restrict__ qn, const float* __restrict__ kn,
                            const float* __restrict__ cosT, const float* __restrict__ sinT, uint16_t* __restrict__ Kc,
                            uint16_t* __restrict__ Vc, float* __restrict__ qdst, int ldq) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ double red[17];
   __shared__ __align__(16) float hbuf[512];
   if (dpos) pos0 += *dpos;  // position read on the device (captured decode steps)
@@ -114,6 +120,8 @@ __global__ void k_qkv_post(const float* __restrict__ qkv, int ldqkv, int nq, int
 // place, rms_r16 with q_norm then RoPE at position pos.
 __global__ void k_q_post(float* __restrict__ q, int hd, int pos, const int* __restrict__ dpos, const float* __restrict__ qn,
                          const float* __restrict__ cosT, const float* __restrict__ sinT) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ double red[17];
   __shared__ __align__(16) float hbuf[512];
   if (dpos) pos += *dpos;
@@ -137,6 +145,8 @@ __global__ void k_q_post(float* __restrict__ q, int hd, int pos, const int* __re
 // input mlp_in = r16((x*r')*w_pre_ff) (rms_prep_x with rounding, :1360).
 __global__ void k_post_attn(float* __restrict__ o, float* __restrict__ x, const float* __restrict__ w_post,
                             const float* __restrict__ w_pre, float* __restrict__ mlp_in, int n) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ double red[17];
   float* om = o + (size_t)blockIdx.x * n;
   float* xm = x + (size_t)blockIdx.x * n;
@@ -153,6 +163,8 @@ __global__ void k_post_attn(float* __restrict__ o, float* __restrict__ x, const 
 // After down_proj (:1375-1378) and the layer scalar (:1395): o = r16(o);
 // x = r16(x + r16((o*r)*w_post_ff)); x = r16(x * scalar).
 __global__ void k_post_ff(float* __restrict__ o, float* __restrict__ x, const float* __restrict__ w_post, float scalar, int n) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ double red[17];
   float* om = o + (size_t)blockIdx.x * n;
   float* xm = x + (size_t)blockIdx.x * n;
@@ -167,6 +179,8 @@ __global__ void k_post_ff(float* __restrict__ o, float* __restrict__ x, const fl
 
 // GeGLU: act = r16(r16(gelu(r16 g)) * r16 u), gate in columns [0, I), up in [I, 2I) (:1370).
 __global__ void k_act(const float* __restrict__ gu, int I, int M, float* __restrict__ act) {
+  pdl_wait();
+  pdl_trigger();
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)M * I) return;
   const int m = (int)(idx / I), i = (int)(idx % I);
@@ -176,6 +190,8 @@ __global__ void k_act(const float* __restrict__ gu, int I, int M, float* __restr
 
 // o_drafter residual (:1548): x = r16(x + r16((o*r)*w)) after o = r16(o); no second norm.
 __global__ void k_resid_norm(float* __restrict__ o, float* __restrict__ x, const float* __restrict__ w, int n) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ double red[17];
   for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = r16(o[i]);
   __syncthreads();
@@ -189,20 +205,51 @@ __global__ void k_resid_norm(float* __restrict__ o, float* __restrict__ x, const
 // next linear consumes (quant_group32 per 32-group, identical to g4_w4a8_quant).  They replace
 // norm -> quantise pairs of launches with one and compute the same values as the unfused kernels.
 constexpr int kRowMax = 2048;
+constexpr int kRowPer = kRowMax / 256;  // elements per thread of a 256-thread row block
 
 // quantise row ys (shared memory, n % 32 == 0) into row m of qo (row length n); needs a barrier
-// between the writes of ys and this call
+// between the writes of ys and this call.  Each warp keeps four groups in flight (the arithmetic
+// of quant_group32 per group).
 __device__ __forceinline__ void quant_row(const float* ys, int n, int m, const QuantOut& qo) {
+  constexpr int U = 4;  // groups per warp in flight
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5, G = n >> 5;
-  for (int g = w; g < G; g += nw) {
-    int8_t qv;
-    float sx;
-    int32_t tot;
-    quant_group32(ys[g * 32 + lane], qv, sx, tot);
-    qo.q[(size_t)m * n + g * 32 + lane] = qv;
-    if (lane == 0) {
-      qo.sx[(size_t)m * G + g] = sx;
-      qo.sum[(size_t)m * G + g] = tot;
+  for (int g0 = w; g0 < G; g0 += nw * U) {
+    float x[U], amax[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int g = g0 + u * nw;
+      x[u] = g < G ? ys[g * 32 + lane] : 0.f;
+      amax[u] = fabsf(x[u]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < U; ++u) amax[u] = fmaxf(amax[u], __shfl_xor_sync(FULL, amax[u], o));
+    float s[U];
+    int32_t r[U], t[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      s[u] = __fdiv_rn(amax[u], 127.0f);
+      const float inv = s[u] > 0.f ? __fdiv_rn(1.0f, s[u]) : 0.0f;
+      const float v = __fmul_rn(x[u], inv);
+      r[u] = (v > -2147483648.f && v < 2147483648.f) ? __float2int_rn(v) : INT32_MIN;
+      t[u] = r[u];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < U; ++u) t[u] += __shfl_xor_sync(FULL, t[u], o);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int g = g0 + u * nw;
+      if (g < G) {
+        const int32_t r16v = r[u] < -32768 ? -32768 : (r[u] > 32767 ? 32767 : r[u]);
+        qo.q[(size_t)m * n + g * 32 + lane] = (int8_t)(r16v < -128 ? -128 : (r16v > 127 ? 127 : r16v));
+        if (lane == 0) {
+          qo.sx[(size_t)m * G + g] = s[u];
+          qo.sum[(size_t)m * G + g] = t[u];
+        }
+      }
     }
   }
 }
@@ -210,6 +257,8 @@ __device__ __forceinline__ void quant_row(const float* ys, int n, int m, const Q
 // y[m] = (x[m]*r)*w, optionally rounded to bf16 (rms / rms_prep_x, :344-352, :365-381).
 __global__ void __launch_bounds__(256) k_norm_q(const float* __restrict__ x, const float* __restrict__ w, int n,
                                                 float* __restrict__ y, int round, QuantOut qo) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ __align__(16) float xs[kRowMax];
   __shared__ double red[17];
   const int m = blockIdx.x;
@@ -233,28 +282,45 @@ __global__ void __launch_bounds__(256) k_norm_q(const float* __restrict__ x, con
 __global__ void __launch_bounds__(256) k_post_attn_q(const float* __restrict__ o, float* __restrict__ x,
                                                      const float* __restrict__ w_post, const float* __restrict__ w_pre,
                                                      float* __restrict__ mlp_in, int n, QuantOut qo) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ __align__(16) float os[kRowMax];
   __shared__ __align__(16) float xs[kRowMax];
   __shared__ double red[17];
   const int m = blockIdx.x;
   float* xm = x + (size_t)m * n;
+  float wa[kRowPer], wb[kRowPer];  // this thread's norm weights, loaded with the rows
+#pragma unroll
+  for (int k = 0; k < kRowPer; ++k) {
+    const int i = threadIdx.x + 256 * k;
+    wa[k] = i < n ? w_post[i] : 0.f;
+    wb[k] = i < n ? w_pre[i] : 0.f;
+  }
   stage_row(os, o + (size_t)m * n, n);
   stage_row(xs, xm, n);
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += blockDim.x) os[i] = r16(os[i]);
   __syncthreads();
   const float r = block_rms_scale(os, n, red);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = r16(__fadd_rn(xs[i], r16(__fmul_rn(__fmul_rn(os[i], r), w_post[i]))));
-    xs[i] = v;
-    xm[i] = v;
+#pragma unroll
+  for (int k = 0; k < kRowPer; ++k) {
+    const int i = threadIdx.x + 256 * k;
+    if (i < n) {
+      const float v = r16(__fadd_rn(xs[i], r16(__fmul_rn(__fmul_rn(os[i], r), wa[k]))));
+      xs[i] = v;
+      xm[i] = v;
+    }
   }
   __syncthreads();
   const float r2 = block_rms_scale(xs, n, red);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = r16(__fmul_rn(__fmul_rn(xs[i], r2), w_pre[i]));
-    mlp_in[(size_t)m * n + i] = v;
-    os[i] = v;
+#pragma unroll
+  for (int k = 0; k < kRowPer; ++k) {
+    const int i = threadIdx.x + 256 * k;
+    if (i < n) {
+      const float v = r16(__fmul_rn(__fmul_rn(xs[i], r2), wb[k]));
+      mlp_in[(size_t)m * n + i] = v;
+      os[i] = v;
+    }
   }
   if (qo.q) {
     __syncthreads();
@@ -270,31 +336,48 @@ __global__ void __launch_bounds__(256) k_resid_norm_q(const float* __restrict__ 
                                                       const float* __restrict__ w_post, float scalar, int n,
                                                       const float* __restrict__ w_next, float* __restrict__ a,
                                                       int round_next, QuantOut qo) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ __align__(16) float os[kRowMax];
   __shared__ __align__(16) float xs[kRowMax];
   __shared__ double red[17];
   const int m = blockIdx.x;
   float* xm = x + (size_t)m * n;
+  float wa[kRowPer], wb[kRowPer];  // this thread's norm weights, loaded with the rows
+#pragma unroll
+  for (int k = 0; k < kRowPer; ++k) {
+    const int i = threadIdx.x + 256 * k;
+    wa[k] = i < n ? w_post[i] : 0.f;
+    wb[k] = (i < n && w_next != nullptr) ? w_next[i] : 0.f;
+  }
   stage_row(os, o + (size_t)m * n, n);
   stage_row(xs, xm, n);
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += blockDim.x) os[i] = r16(os[i]);
   __syncthreads();
   const float r = block_rms_scale(os, n, red);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float v = r16(__fadd_rn(xs[i], r16(__fmul_rn(__fmul_rn(os[i], r), w_post[i]))));
-    if (scalar != 0.f) v = r16(__fmul_rn(v, scalar));
-    xs[i] = v;
-    xm[i] = v;
+#pragma unroll
+  for (int k = 0; k < kRowPer; ++k) {
+    const int i = threadIdx.x + 256 * k;
+    if (i < n) {
+      float v = r16(__fadd_rn(xs[i], r16(__fmul_rn(__fmul_rn(os[i], r), wa[k]))));
+      if (scalar != 0.f) v = r16(__fmul_rn(v, scalar));
+      xs[i] = v;
+      xm[i] = v;
+    }
   }
   if (w_next == nullptr) return;
   __syncthreads();
   const float r2 = block_rms_scale(xs, n, red);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float v = __fmul_rn(__fmul_rn(xs[i], r2), w_next[i]);
-    if (round_next) v = r16(v);
-    a[(size_t)m * n + i] = v;
-    os[i] = v;
+#pragma unroll
+  for (int k = 0; k < kRowPer; ++k) {
+    const int i = threadIdx.x + 256 * k;
+    if (i < n) {
+      float v = __fmul_rn(__fmul_rn(xs[i], r2), wb[k]);
+      if (round_next) v = r16(v);
+      a[(size_t)m * n + i] = v;
+      os[i] = v;
+    }
   }
   if (qo.q) {
     __syncthreads();
@@ -306,6 +389,8 @@ __global__ void __launch_bounds__(256) k_resid_norm_q(const float* __restrict__ 
 // blockDim 256, grid M*I/256).
 __global__ void __launch_bounds__(256) k_act_q(const float* __restrict__ gu, int I, int M, float* __restrict__ act,
                                                QuantOut qo) {
+  pdl_wait();
+  pdl_trigger();
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)M * I) return;  // warp-uniform (M*I is a multiple of 32)
   const int m = (int)(idx / I), i = (int)(idx % I);
@@ -327,16 +412,22 @@ __global__ void __launch_bounds__(256) k_act_q(const float* __restrict__ gu, int
 
 // elementwise helpers
 __global__ void k_round(float* __restrict__ p, long long n) {
+  pdl_wait();
+  pdl_trigger();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] = r16(p[i]);
 }
 __global__ void k_scale_round(float* __restrict__ p, long long n, float s) {
+  pdl_wait();
+  pdl_trigger();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] = r16(__fmul_rn(p[i], s));
 }
 // drafter input [r16(E[tok]*sqrt(H)) | h]
 __global__ void k_draft_in(const uint16_t* __restrict__ E, const int* __restrict__ tok, const float* __restrict__ h, int H,
                            float sqrtH, float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const uint16_t* er = E + (size_t)(*tok) * H;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) {
     out[i] = r16(__fmul_rn(bf2f(er[i]), sqrtH));
@@ -354,6 +445,8 @@ __global__ void k_draft_in(const uint16_t* __restrict__ E, const int* __restrict
 __global__ void __launch_bounds__(256) k_attn_rows(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
                                                    const float* __restrict__ q, int ldq, int nh, int hd, int pos0,
                                                    int window, int variant, float* __restrict__ out, int ldo) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float sc[];
   __shared__ float s_red[32];
   const int m = blockIdx.x, h = blockIdx.y;
@@ -427,6 +520,8 @@ __global__ void __launch_bounds__(256) k_attn_rows(const uint16_t* __restrict__ 
 // first maximum in candidate order (:1557-1558).  One half-warp per candidate.
 __global__ void k_cand_scores(const uint16_t* __restrict__ E, const int* __restrict__ cand, int nc, const float* __restrict__ dh,
                               int H, float* __restrict__ score) {
+  pdl_wait();
+  pdl_trigger();
   const int hw = (blockIdx.x * blockDim.x + threadIdx.x) >> 4, c = threadIdx.x & 15;
   const int base = hw & ~1;  // warp-uniform
   if (base >= nc) return;
@@ -442,6 +537,8 @@ __global__ void k_cand_scores(const uint16_t* __restrict__ E, const int* __restr
 // :1554-1555 does) and the candidate list cand[t*per + j] = perm((top t)*per + j).
 __global__ void __launch_bounds__(256) k_topk_cand(const float* __restrict__ score, int n, int T, int per, int vocab,
                                                    int* __restrict__ cand) {
+  pdl_wait();
+  pdl_trigger();
   // block of 32 scores (one per lane); the 8 warps each count the higher-ranked scores in one
   // eighth of the list, and the partial ranks are summed (rank = #(s_j > v) + #(s_j == v, j < i))
   extern __shared__ float s[];
@@ -472,6 +569,8 @@ __global__ void __launch_bounds__(256) k_topk_cand(const float* __restrict__ sco
 }
 // first argmax in candidate order -> *best (one block)
 __global__ void k_cand_best(const float* __restrict__ score, const int* __restrict__ cand, int nc, int* __restrict__ best) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sv[32];
   __shared__ int si[32];
   float bv = -1e30f;

@@ -22,6 +22,8 @@ namespace g4 {
 // Reference layout byte b = element 2b | element 2b+1 << 4  ->  device layout byte b =
 // element b | element 16+b << 4.  One thread per 32-group.
 __global__ void k_w4_pack(const uint8_t* __restrict__ W, long long groups, uint8_t* __restrict__ Wp) {
+  pdl_wait();
+  pdl_trigger();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= groups) return;
   const uint4 v = reinterpret_cast<const uint4*>(W)[i];
@@ -43,6 +45,8 @@ __global__ void k_w4_pack(const uint8_t* __restrict__ W, long long groups, uint8
 // gsum[m][g] = ((x0 + x1) + x2) + ... + x31 starting from 0 (w4g32_avx2.h:22; XP::prep
 // gemma4_engine.cpp:191).  One thread per (m, g).
 __global__ void k_gsum(const float* __restrict__ X, int MG, int G, float* __restrict__ gs) {
+  pdl_wait();
+  pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= MG) return;
   const float* x = X + (size_t)(i / G) * G * 32 + (size_t)(i % G) * 32;
@@ -118,6 +122,9 @@ k_w4g32(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const fl
   };
   if (threadIdx.x == 0)
     for (int c = 0; c < geo.NB; ++c) issue(c);
+
+  pdl_wait();  // the weights above are read-only; activations come from the previous kernel
+  pdl_trigger();
 
   // group sums (given, or ((x0 + x1) + ...) + x31 from 0, w4g32_avx2.h:22) while the copies fly
   if (gsum_in != nullptr) {
@@ -205,30 +212,59 @@ k_w4g32(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const fl
 
 // W4G32 float GEMV, row-per-thread variant for tall matrices (the head screen: 262,144 rows).
 // One thread runs the eight lane chains of its row, so each 16-byte group of weights is decoded
-// once for all M activation rows.  The thread reads its row's weights and scales straight from
-// global memory through L1 (16-byte loads; a row's 128-byte lines serve 8 consecutive loads of its
-// thread), so occupancy is set by registers; a persistent grid takes 256-row tiles in turn.  The
-// activations sit in shared memory as [k][4] (one 16-byte broadcast load per element), the group
-// sums as [g][4].  Values are those of k_w4g32: per lane j and group, a = t(2j)x(2j);
-// a = fma(t(16+2j), x(16+2j), a); a = fma(t(2j+1), ...); a = fma(t(17+2j), ...);
+// once for all M activation rows.  A persistent CTA takes blocks of kWrRows rows; per pipeline item
+// every row brings 8 groups of weights (128 B) and their 8 scales (16 B) by bulk copies into one of
+// kWrNS shared-memory stages, issued kWrNS items ahead; rows sit kWrStride = 144 bytes apart (an
+// odd multiple of 16) so the 8 threads of a 16-byte load phase read 8 different bank quads.  The
+// activations sit in shared memory as [k][4] (one 16-byte broadcast load per element for four
+// rows), the group sums as [g][4].  Values are those of k_w4g32: per lane j and group,
+// a = t(2j)x(2j); a = fma(t(16+2j), x(16+2j), a); a = fma(t(2j+1), ...); a = fma(t(17+2j), ...);
 // row_j = fma(a, s, row_j); off = fma(s, gsum, off); y = hsum8(row) - 8 off.
-constexpr int kWrThreads = 256;
-__host__ __device__ inline size_t w4g32_rows_smem(int K) { return (size_t)K * 16 + (size_t)(K / 32) * 16; }
+constexpr int kWrRows = 256, kWrStride = 144, kWrNS = 2;
+__host__ __device__ inline size_t w4g32_rows_smem(int K) {
+  return 128 + (size_t)kWrNS * kWrRows * kWrStride + (size_t)K * 16 + (size_t)(K / 32) * 16;
+}
 
 template <int M>
-__global__ void __launch_bounds__(kWrThreads) k_w4g32_rows(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S,
-                                                            const float* __restrict__ X, int N, int K,
-                                                            float* __restrict__ Y, int ldy) {
-  extern __shared__ __align__(16) float4 xs[];  // [K], then group sums [G]
-  const int G = K >> 5;
-  float4* gs = xs + K;
-  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+__global__ void __launch_bounds__(kWrRows) k_w4g32_rows(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S,
+                                                         const float* __restrict__ X, int N, int K,
+                                                         float* __restrict__ Y, int ldy) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint8_t* stages = smem + 128;
+  float4* xs = reinterpret_cast<float4*>(stages + (size_t)kWrNS * kWrRows * kWrStride);  // [K]
+  float4* gs = xs + K;                                                                    // [G]
+  const int G = K >> 5, nch = G / 8;
+  const int nblk = (N + kWrRows - 1) / kWrRows;
+  const int myblk = nblk > (int)blockIdx.x ? (nblk - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int nitems = myblk * nch;
+  const int r = threadIdx.x;
+  if (r == 0) {
+    for (int b = 0; b < kWrNS; ++b) mbar_init(&bars[b], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // item i: row block blockIdx.x + (i / nch) * gridDim.x, groups [8c, 8c + 8) with c = i % nch
+  auto issue = [&](int i, int st) {
+    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
+    const int r0 = blk * kWrRows, nr = min(kWrRows, N - r0);
+    if (r == 0) mbar_expect_tx(&bars[st], 144u * (uint32_t)nr);
+    if (r < nr) {
+      uint8_t* dst = stages + ((size_t)st * kWrRows + r) * kWrStride;
+      bulk_g2s(dst, Wp + (size_t)(r0 + r) * (K >> 1) + (size_t)c * 128, 128u, &bars[st]);
+      bulk_g2s(dst + 128, S + (size_t)(r0 + r) * G + (size_t)c * 8, 16u, &bars[st]);
+    }
+  };
+  for (int b = 0; b < kWrNS && b < nitems; ++b) issue(b, b);  // weights only: read-only
+  pdl_wait();
+  pdl_trigger();
+  for (int i = r; i < K; i += blockDim.x) {
     float v[4];
 #pragma unroll
     for (int m = 0; m < 4; ++m) v[m] = m < M ? X[(size_t)m * K + i] : 0.f;
     xs[i] = make_float4(v[0], v[1], v[2], v[3]);
   }
-  for (int g = threadIdx.x; g < G; g += blockDim.x) {  // ((x0 + x1) + ...) + x31 from 0 (w4g32_avx2.h:22)
+  for (int g = r; g < G; g += blockDim.x) {  // ((x0 + x1) + ...) + x31 from 0 (w4g32_avx2.h:22)
     float v[4];
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
@@ -240,60 +276,66 @@ __global__ void __launch_bounds__(kWrThreads) k_w4g32_rows(const uint8_t* __rest
     gs[g] = make_float4(v[0], v[1], v[2], v[3]);
   }
   __syncthreads();
-  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n - (int)threadIdx.x < N; n += gridDim.x * blockDim.x) {
-    if (n >= N) continue;
-    const uint4* wrow = reinterpret_cast<const uint4*>(Wp + (size_t)n * (K >> 1));
-    const uint4* srow = reinterpret_cast<const uint4*>(S + (size_t)n * G);
-    float2 row[8][2], off[2];
+  float2 row[8][2], off[2];
+  for (int i = 0; i < nitems; ++i) {
+    const int st = i % kWrNS;
+    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
+    const int n = blk * kWrRows + r;
+    if (!cta_wait(&bars[st], (uint32_t)(i / kWrNS) & 1u)) return;
+    if (c == 0) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) row[j][0] = row[j][1] = make_float2(0.f, 0.f);
-    off[0] = off[1] = make_float2(0.f, 0.f);
-#pragma unroll 1
-    for (int g8 = 0; g8 < G; g8 += 8) {
-      const uint4 s8 = __ldg(srow + (g8 >> 3));
-      const uint32_t s8w[4] = {s8.x, s8.y, s8.z, s8.w};
-      uint4 wq[8];
+      for (int j = 0; j < 8; ++j) row[j][0] = row[j][1] = make_float2(0.f, 0.f);
+      off[0] = off[1] = make_float2(0.f, 0.f);
+    }
+    const uint4* rowp = reinterpret_cast<const uint4*>(stages + ((size_t)st * kWrRows + r) * kWrStride);
+    const uint4 s8 = rowp[8];
+    const uint32_t s8w[4] = {s8.x, s8.y, s8.z, s8.w};
 #pragma unroll
-      for (int u = 0; u < 8; ++u) wq[u] = __ldg(wrow + g8 + u);
+    for (int u = 0; u < 8; ++u) {
+      const int g = c * 8 + u;
+      const uint4 wq = rowp[u];
+      const uint32_t w4[4] = {wq.x, wq.y, wq.z, wq.w};
+      const float scl = bf2f((u & 1) ? (s8w[u >> 1] >> 16) : (s8w[u >> 1] & 0xFFFFu));
+      const float2 sc2 = make_float2(scl, scl);
+      const float4* xg = xs + g * 32;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int g = g8 + u;
-        const uint32_t w4[4] = {wq[u].x, wq[u].y, wq[u].z, wq[u].w};
-        const float scl = bf2f((u & 1) ? (s8w[u >> 1] >> 16) : (s8w[u >> 1] & 0xFFFFu));
-        const float2 sc2 = make_float2(scl, scl);
-        const float4* xg = xs + g * 32;
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t v = (w4[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;  // bytes 2j, 2j+1
+        float t0, t1, t2, t3;
+        nib4_to_f(v, t0, t1, t2, t3);
+        const float4 x0 = xg[2 * j], x1 = xg[16 + 2 * j], x2 = xg[2 * j + 1], x3 = xg[17 + 2 * j];
+        float2 a0 = __fmul2_rn(make_float2(t0, t0), make_float2(x0.x, x0.y));
+        float2 a1 = __fmul2_rn(make_float2(t0, t0), make_float2(x0.z, x0.w));
+        a0 = __ffma2_rn(make_float2(t1, t1), make_float2(x1.x, x1.y), a0);
+        a1 = __ffma2_rn(make_float2(t1, t1), make_float2(x1.z, x1.w), a1);
+        a0 = __ffma2_rn(make_float2(t2, t2), make_float2(x2.x, x2.y), a0);
+        a1 = __ffma2_rn(make_float2(t2, t2), make_float2(x2.z, x2.w), a1);
+        a0 = __ffma2_rn(make_float2(t3, t3), make_float2(x3.x, x3.y), a0);
+        a1 = __ffma2_rn(make_float2(t3, t3), make_float2(x3.z, x3.w), a1);
+        row[j][0] = __ffma2_rn(a0, sc2, row[j][0]);
+        row[j][1] = __ffma2_rn(a1, sc2, row[j][1]);
+      }
+      const float4 gv = gs[g];
+      off[0] = __ffma2_rn(sc2, make_float2(gv.x, gv.y), off[0]);
+      off[1] = __ffma2_rn(sc2, make_float2(gv.z, gv.w), off[1]);
+    }
+    if (c == nch - 1 && n < N) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t v = (w4[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;  // bytes 2j, 2j+1
-          float t0, t1, t2, t3;
-          nib4_to_f(v, t0, t1, t2, t3);
-          const float4 x0 = xg[2 * j], x1 = xg[16 + 2 * j], x2 = xg[2 * j + 1], x3 = xg[17 + 2 * j];
-          float2 a0 = __fmul2_rn(make_float2(t0, t0), make_float2(x0.x, x0.y));
-          float2 a1 = __fmul2_rn(make_float2(t0, t0), make_float2(x0.z, x0.w));
-          a0 = __ffma2_rn(make_float2(t1, t1), make_float2(x1.x, x1.y), a0);
-          a1 = __ffma2_rn(make_float2(t1, t1), make_float2(x1.z, x1.w), a1);
-          a0 = __ffma2_rn(make_float2(t2, t2), make_float2(x2.x, x2.y), a0);
-          a1 = __ffma2_rn(make_float2(t2, t2), make_float2(x2.z, x2.w), a1);
-          a0 = __ffma2_rn(make_float2(t3, t3), make_float2(x3.x, x3.y), a0);
-          a1 = __ffma2_rn(make_float2(t3, t3), make_float2(x3.z, x3.w), a1);
-          row[j][0] = __ffma2_rn(a0, sc2, row[j][0]);
-          row[j][1] = __ffma2_rn(a1, sc2, row[j][1]);
-        }
-        const float4 gv = gs[g];
-        off[0] = __ffma2_rn(sc2, make_float2(gv.x, gv.y), off[0]);
-        off[1] = __ffma2_rn(sc2, make_float2(gv.z, gv.w), off[1]);
+      for (int m = 0; m < M; ++m) {
+        const int p = m >> 1;
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = (m & 1) ? row[j][p].y : row[j][p].x;
+        const float h = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[4]), __fadd_rn(v[1], v[5])),
+                                  __fadd_rn(__fadd_rn(v[2], v[6]), __fadd_rn(v[3], v[7])));
+        const float o = (m & 1) ? off[p].y : off[p].x;
+        Y[(size_t)m * ldy + n] = __fsub_rn(h, __fmul_rn(8.f, o));
       }
     }
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const int p = m >> 1;
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = (m & 1) ? row[j][p].y : row[j][p].x;
-      const float h = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[4]), __fadd_rn(v[1], v[5])),
-                                __fadd_rn(__fadd_rn(v[2], v[6]), __fadd_rn(v[3], v[7])));
-      const float o = (m & 1) ? off[p].y : off[p].x;
-      Y[(size_t)m * ldy + n] = __fsub_rn(h, __fmul_rn(8.f, o));
+    __syncthreads();  // stage st is consumed by every row
+    if (i + kWrNS < nitems) {
+      fence_proxy_async_smem();
+      issue(i + kWrNS, st);
     }
   }
 }
@@ -304,6 +346,8 @@ __global__ void __launch_bounds__(kWrThreads) k_w4g32_rows(const uint8_t* __rest
 // unsaturated r, q = r saturated to int16 then int8 (w4a8_avx2.h:30-42).
 __global__ void k_w4a8_quant(const float* __restrict__ X, int MG, int G, int8_t* __restrict__ q,
                              float* __restrict__ sx, int32_t* __restrict__ sum) {
+  pdl_wait();
+  pdl_trigger();
   const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (wid >= MG) return;
@@ -359,6 +403,9 @@ k_w4a8(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const int
   };
   if (threadIdx.x == 0)
     for (int c = 0; c < geo.NB; ++c) issue(c);
+
+  pdl_wait();  // the weights above are read-only; activations come from the previous kernel
+  pdl_trigger();
 
   // chain slots: thread t owns (row, activation row) pairs t, t+T, ... of the ROWS*M chains
   constexpr int CPT = (ROWS * M + T - 1) / T;
@@ -467,6 +514,8 @@ k_w4a8_all(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const
                  &bars[c]);
     if (lane == 0) bulk_g2s(sc, S + (size_t)n0 * G, (uint32_t)nvalid * G * 2, &bars[0]);
   }
+  pdl_wait();  // the weights above are read-only; activations come from the previous kernel
+  pdl_trigger();
   // phase 1: item (group gl of a chunk, row subset rs); with T > CH the rows of a group are split
   // over T / CH threads.  Each thread's activations for its first item are loaded before the
   // wait, so their latency overlaps the weights' arrival.
@@ -573,6 +622,8 @@ k_w4a8_ring(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, cons
   if (threadIdx.x < 32)
     for (int b = 0; b < NS; ++b)
       if ((int)(blockIdx.x + b * gridDim.x) < nblk) issue(blockIdx.x + b * gridDim.x, b);
+  pdl_wait();  // the weights above are read-only; activations come from the previous kernel
+  pdl_trigger();
   // activations into shared memory (16-byte pieces; K % 256 == 0)
   for (int i = threadIdx.x; i < M * K / 16; i += T) reinterpret_cast<int4*>(qs)[i] = __ldg(reinterpret_cast<const int4*>(q) + i);
   for (int i = threadIdx.x; i < M * G; i += T) { sxs[i] = __ldg(sx + i); sums[i] = __ldg(sum + i); }
@@ -698,7 +749,7 @@ static int launch_w4g32_t(const uint8_t* Wp, const uint16_t* S, const float* X, 
   const size_t smem = w4g32_smem(M, ROWS, g);
   if (smem > 227 * 1024) return set_error(G4_ERR_UNSUPPORTED, "g4_w4g32_gemm: %zu B of shared memory", smem);
   if (smem > 48 * 1024) cudaFuncSetAttribute(k_w4g32<M, R, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k_w4g32<M, R, WARPS><<<(N + ROWS - 1) / ROWS, WARPS * 32, smem, st>>>(Wp, S, X, gsum, N, K, Y, ldy, CH, NB);
+  if (int rc_ = launch("k_w4g32", k_w4g32<M, R, WARPS>, dim3((N + ROWS - 1) / ROWS), dim3(WARPS * 32), smem, st, Wp, S, X, gsum, N, K, Y, ldy, CH, NB)) return rc_;
   return check_launch("k_w4g32");
 }
 
@@ -722,14 +773,14 @@ extern "C" int g4_w4g32_gemm(const uint8_t* Wp, const uint16_t* S, const float* 
   cudaStream_t st = as_stream(stream);
   // tall matrices (the head screen): row-per-thread variant
   const char* rv = getenv("G4_W4G32_ROWS");  // "0" turns it off (experiments)
-  if (M <= 4 && gsum == nullptr && N >= 16384 && w4g32_rows_smem(K) <= 100 * 1024 && !(rv && rv[0] == '0')) {
+  if (M <= 4 && gsum == nullptr && N >= 16384 && w4g32_rows_smem(K) <= 227 * 1024 && !(rv && rv[0] == '0')) {
     const size_t smem = w4g32_rows_smem(K);
     auto go = [&](auto kern) {
-      if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       int occ = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kWrThreads, smem) != cudaSuccess || occ < 1) occ = 1;
-      const int grid = std::min((N + kWrThreads - 1) / kWrThreads, sm_count() * occ);
-      kern<<<grid, kWrThreads, smem, st>>>(Wp, S, X, N, K, Y, ldy);
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kWrRows, smem) != cudaSuccess || occ < 1) occ = 1;
+      const int grid = std::min((N + kWrRows - 1) / kWrRows, sm_count() * occ);
+      if (int rc_ = launch("k_w4g32_rows", kern, dim3(grid), dim3(kWrRows), smem, st, Wp, S, X, N, K, Y, ldy)) return rc_;
       return check_launch("k_w4g32_rows");
     };
     switch (M) {
@@ -755,7 +806,7 @@ extern "C" int g4_w4a8_quant(const float* X, int M, int K, int8_t* q, float* sx,
   G4_REQUIRE(X && q && sx && sum && M > 0 && K > 0 && K % 32 == 0, "g4_w4a8_quant: bad arguments M=%d K=%d", M, K);
   const int MG = M * (K / 32);
   const int threads = 256, per_block = threads / 32;
-  k_w4a8_quant<<<(MG + per_block - 1) / per_block, threads, 0, as_stream(stream)>>>(X, MG, K / 32, q, sx, sum);
+  if (int rc_ = launch("k_w4a8_quant", k_w4a8_quant, dim3((MG + per_block - 1) / per_block), dim3(threads), 0, as_stream(stream), X, MG, K / 32, q, sx, sum)) return rc_;
   return check_launch("k_w4a8_quant");
 }
 
@@ -770,7 +821,7 @@ static int launch_w4a8_t(const uint8_t* Wp, const uint16_t* S, const int8_t* q, 
   const size_t smem = w4a8_smem(M, g);
   if (smem > 227 * 1024) return set_error(G4_ERR_UNSUPPORTED, "g4_w4a8_gemm: %zu B of shared memory", smem);
   if (smem > 48 * 1024) cudaFuncSetAttribute(k_w4a8<M, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k_w4a8<M, WARPS><<<(N + kW4A8Rows - 1) / kW4A8Rows, WARPS * 32, smem, st>>>(Wp, S, q, sx, sum, N, K, Y, ldy, CH, NB);
+  if (int rc_ = launch("k_w4a8", k_w4a8<M, WARPS>, dim3((N + kW4A8Rows - 1) / kW4A8Rows), dim3(WARPS * 32), smem, st, Wp, S, q, sx, sum, N, K, Y, ldy, CH, NB)) return rc_;
   return check_launch("k_w4a8");
 }
 
@@ -784,7 +835,7 @@ static int launch_w4a8_all_t(const uint8_t* Wp, const uint16_t* S, const int8_t*
                              int N, int K, float* Y, int ldy, int CH, cudaStream_t st) {
   const size_t smem = w4a8_all_smem(M, ROWS, K);
   if (smem > 48 * 1024) cudaFuncSetAttribute(k_w4a8_all<M, ROWS, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k_w4a8_all<M, ROWS, WARPS><<<(N + ROWS - 1) / ROWS, WARPS * 32, smem, st>>>(Wp, S, q, sx, sum, N, K, Y, ldy, CH);
+  if (int rc_ = launch("k_w4a8_all", k_w4a8_all<M, ROWS, WARPS>, dim3((N + ROWS - 1) / ROWS), dim3(WARPS * 32), smem, st, Wp, S, q, sx, sum, N, K, Y, ldy, CH)) return rc_;
   return check_launch("k_w4a8_all");
 }
 
@@ -804,7 +855,8 @@ static int launch_w4a8_ring_t(const uint8_t* Wp, const uint16_t* S, const int8_t
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, WARPS * 32, smem) != cudaSuccess || occ < 1) occ = 1;
   const int nblk = (N + ROWS - 1) / ROWS;
   const int grid = std::min(nblk, sm_count() * std::min(occ, per_sm));
-  kern<<<grid, WARPS * 32, smem, st>>>(Wp, S, q, sx, sum, N, K, Y, ldy);
+  if (int rc_ = launch("k_w4a8_ring", kern, dim3(grid), dim3(WARPS * 32), smem, st, Wp, S, q, sx, sum, N, K, Y, ldy))
+    return rc_;
   return check_launch("k_w4a8_ring");
 }
 

@@ -153,7 +153,8 @@ typedef struct {
   int att_par;                       /* ENGINE_ATT_PAR (192) */
   int drafter;                       /* build the MTP drafter (1) */
   unsigned long long seed;           /* weight seed */
-  int graphs;                        /* replay decode rounds as CUDA graphs (1); 0 = eager launches */
+  int graphs;                        /* decode rounds as CUDA graphs with programmatic dependent
+                                        launch (1), graphs with ordinary launches (2), eager (0) */
 } g4_engine_config;
 typedef struct {
   int rounds, ngram_rounds, drafted, accepted, prefill_tokens, decode_tokens;
@@ -162,6 +163,7 @@ typedef struct {
   int verify_passes, verify_rows, draft_steps;
   double verify_gpu_ms, draft_gpu_ms; /* CUDA events around each verify pass / each round's drafts */
   long long h2d_bytes, d2h_bytes;     /* host<->device copies made by the decode calls */
+  long long kernel_launches;          /* kernels the decode calls ran (graph kernel nodes included) */
 } g4_engine_stats;
 
 int g4_engine_default_config(g4_engine_config* cfg);

@@ -77,10 +77,11 @@ def test_attention_workspace_too_small():
         g4.attn_splitkv(kv, kv, q, [15], [0], ws=torch.zeros(4, device="cuda"))
 
 
-@pytest.mark.parametrize("ctx,M,nh,T", [(9000, 2, 8, 8), (3000, 4, 3, 2), (777, 1, 5, 7)])
+@pytest.mark.parametrize("ctx,M,nh,T", [(9000, 2, 8, 8), (3000, 4, 3, 2), (777, 1, 5, 7), (13000, 1, 8, 8)])
 def test_attention_long_chunks_and_odd_head_counts(ctx, M, nh, T):
     """Chunks longer than the statistics kernel's register tile (9,000 keys in 8 chunks; 3,000 in
-    2), head counts that leave (row, head) groups partly empty, and an odd chunk count."""
+    2), chunks longer than the chunk kernel serves (13,000 keys: the three-kernel tail), head
+    counts that leave (row, head) groups partly empty, and an odd chunk count."""
     rng = np.random.default_rng(ctx + nh)
     hd = 256
     Kc = bf16_bits(rng.standard_normal((ctx, hd), dtype=np.float32))
