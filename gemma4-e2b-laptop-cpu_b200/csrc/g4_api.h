@@ -1,6 +1,7 @@
 // Host-side helpers shared by the C-ABI entry points: thread-local error message and the checks
 // every entry point runs before it launches anything.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdarg>
 #include <cstdio>
@@ -21,6 +22,11 @@ struct QuantOut;
 // its writes are visible.  Every kernel launched this way calls pdl_wait() before it touches
 // anything an earlier kernel writes, so only read-only prologues (weight prefetches, barrier set-up)
 // overlap the previous kernel.  Otherwise launch() is an ordinary <<<>>> launch.
+// A 2D tiled tensor map over a row-major [outer][inner] array (row stride stride_bytes), boxes of
+// [box_outer][box_inner] elements, for cp.async.bulk.tensor loads (cuTensorMapEncodeTiled, reached
+// through the runtime's driver entry point).  False when the driver lacks it or rejects the map.
+bool encode_tmap_2d(CUtensorMap* out, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
+                    uint64_t stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
 bool& pdl_enabled();
 // Kernels started through launch() on this host thread (the engine counts its launches with it).
 long long& launch_count();

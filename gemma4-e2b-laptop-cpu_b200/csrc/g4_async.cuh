@@ -67,6 +67,13 @@ __device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t parity) {
   }
   return !any_fail;
 }
+// 2D tiled tensor load (TMA) global -> this CTA's shared memory, completion on an mbarrier.  The
+// innermost coordinate x (in elements) times the element size must be a multiple of 16 bytes.
+// No cluster multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
+  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+               ::"r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
+}
 // Orders this thread's earlier generic-proxy accesses of shared memory before its later
 // async-proxy (bulk copy) writes into the same buffer.
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }

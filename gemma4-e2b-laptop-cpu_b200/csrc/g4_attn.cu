@@ -390,7 +390,24 @@ __global__ void __launch_bounds__(256) k_attn_chunk(const uint16_t* __restrict__
       const int a = max(cl, d.lo[m]), b = min(ch - 1, d.pos[m]);
       const float* wp = wsm + lane * WS - cl;
       float l8 = 0.f;
-      for (int k = a; k <= b; ++k) l8 = __fadd_rn(l8, wp[k]);
+      int k = a;
+      if (k + 8 <= b + 1) {  // key order; the next 8 weights load while these 8 are added
+        float cur[8], nxt[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) cur[u] = wp[k + u];
+        for (; k + 16 <= b + 1; k += 8) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) nxt[u] = wp[k + 8 + u];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) l8 = __fadd_rn(l8, cur[u]);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) l8 = __fadd_rn(l8, cur[u]);
+        k += 8;
+      }
+      for (; k <= b; ++k) l8 = __fadd_rn(l8, wp[k]);
       sl8[lane] = (d.lo[m] > d.pos[m]) ? 0.0f : l8;
     }
   } else if (warp >= 4) {
@@ -482,17 +499,16 @@ __global__ void __launch_bounds__(256) k_attn_chunk(const uint16_t* __restrict__
 }
 
 // ---- one-kernel split-KV for short chunks (sliding-window layers): block = (chunk t, (row, head)
-// pair).  The chunk's K and V rows arrive in shared memory by bulk copies (one per row, rows
-// kAttnRowPad bytes apart so that the two half-warps of a warp read different banks); the block
+// pair).  The chunk's K and V rows arrive in shared memory by two bulk copies (its rows are
+// contiguous in the cache; one copy per row costs microseconds of issue time); the block
 // then computes the chunk's scores (half-warp per key, as k_attn_scores), the chunk max, the exp8
 // weights and their in-order sum (as k_attn_stats), and O for every dim over the chunk's keys in
 // order (as k_attn_accum); the last of the T blocks of a pair to finish (a counter per pair, zeroed
 // before the launch) merges the chunks (as k_attn_merge) and quantises the row when asked.  Same
 // values as the four-kernel path.
 constexpr int kAttnShortKeys = 96;  // longest chunk served by k_attn_short
-constexpr int kAttnRowPad = 32;
 __host__ __device__ inline size_t attn_short_smem(int hd) {
-  return 128 + 2 * (size_t)kAttnShortKeys * (hd * 2 + kAttnRowPad) + sizeof(float) * kAttnShortKeys;
+  return 128 + 2 * (size_t)kAttnShortKeys * hd * 2 + sizeof(float) * kAttnShortKeys;
 }
 
 template <int STEPS>
@@ -503,7 +519,7 @@ __global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__
   pdl_trigger();
   extern __shared__ __align__(128) uint8_t sm_raw[];
   __shared__ float red_f[8];
-  __shared__ float msc[64];
+  __shared__ float msc[64], red_f_am[32];
   __shared__ float s_l8, s_inv;
   __shared__ int s_last;
   const AttnDesc d = resolve(d0);
@@ -512,7 +528,7 @@ __global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__
   const int m = mh / d.nh, h = mh % d.nh;
   const int c0 = max(chunk_lo(d, t), d.lo[m]), c1 = min(chunk_lo(d, t + 1), d.pos[m] + 1);
   const int n = max(0, c1 - c0);
-  const int rs = d.hd * 2 + kAttnRowPad;  // shared-memory row stride (bytes)
+  const int rs = d.hd * 2;  // shared-memory row stride (bytes)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm_raw);
   uint8_t* ks = sm_raw + 128;
   uint8_t* vs = ks + (size_t)kAttnShortKeys * rs;
@@ -523,14 +539,11 @@ __global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__
     fence_mbar_init();
   }
   __syncthreads();
-  if (n > 0 && wid == 0) {
-    const uint32_t rowb = (uint32_t)d.hd * 2;
-    if (lane == 0) mbar_expect_tx(bar, 2u * rowb * (uint32_t)n);
-    __syncwarp();
-    for (int k = lane; k < n; k += 32) {
-      bulk_g2s(ks + (size_t)k * rs, Kc + (size_t)(c0 + k) * d.hd, rowb, bar);
-      bulk_g2s(vs + (size_t)k * rs, Vc + (size_t)(c0 + k) * d.hd, rowb, bar);
-    }
+  if (n > 0 && threadIdx.x == 0) {  // the chunk's rows are contiguous: one copy for K, one for V
+    const uint32_t bytes = (uint32_t)d.hd * 2 * (uint32_t)n;
+    mbar_expect_tx(bar, 2u * bytes);
+    bulk_g2s(ks, Kc + (size_t)c0 * d.hd, bytes, bar);
+    bulk_g2s(vs, Vc + (size_t)c0 * d.hd, bytes, bar);
   }
   float qr[STEPS];
   {
@@ -539,16 +552,21 @@ __global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__
     for (int i = 0; i < STEPS; ++i) qr[i] = qh[c + 16 * i];
   }
   if (n > 0 && !cta_wait(bar, 0)) return;
-  // scores
-  const int nk2 = (n + 15) / 16 * 16;  // both half-warps of a warp run the same iterations
-  for (int k = hw; k < nk2; k += 16) {
-    const int kk = min(k, n - 1);
-    const uint16_t* kr = reinterpret_cast<const uint16_t*>(ks + (size_t)kk * rs);
-    float acc = 0.f;
+  // scores, two keys per half-warp iteration (independent chains)
+  const int nk32 = (n + 31) / 32 * 32;  // both half-warps of a warp run the same iterations
+  for (int k = hw; k < nk32; k += 32) {
+    const uint16_t* kr0 = reinterpret_cast<const uint16_t*>(ks + (size_t)min(k, n - 1) * rs);
+    const uint16_t* kr1 = reinterpret_cast<const uint16_t*>(ks + (size_t)min(k + 16, n - 1) * rs);
+    float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < STEPS; ++i) acc = fmaf(qr[i], bf2f(kr[c + 16 * i]), acc);
-    const float sv = hsum8_octet(__fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8)));
-    if (c == 0 && k < n) sc[k] = sv;
+    for (int i = 0; i < STEPS; ++i) {
+      a0 = fmaf(qr[i], bf2f(kr0[c + 16 * i]), a0);
+      a1 = fmaf(qr[i], bf2f(kr1[c + 16 * i]), a1);
+    }
+    const float s0 = hsum8_octet(__fadd_rn(a0, __shfl_xor_sync(FULL, a0, 8)));
+    const float s1 = hsum8_octet(__fadd_rn(a1, __shfl_xor_sync(FULL, a1, 8)));
+    if (c == 0 && k < n) sc[k] = s0;
+    if (c == 0 && k + 16 < n) sc[k + 16] = s1;
   }
   __syncthreads();
   // chunk max (order-free), then the weights
@@ -600,24 +618,24 @@ __global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // merge (k_attn_merge) by the last block of the pair: chunk factors in parallel, l in order
+  // merge (k_attn_merge) by the last block of the pair: every load first (the chunks' O values
+  // of this thread's dim, the chunk maxima and sums), then the factors in parallel, l in order
+  float aov[8];
+  if ((int)threadIdx.x < d.hd)
+#pragma unroll
+    for (int tt = 0; tt < 8; ++tt)
+      if (tt < d.T) aov[tt] = __ldcg(&w.AO[((size_t)tt * nmh + mh) * d.hd + threadIdx.x]);
   if (threadIdx.x < d.T) {
     const size_t jx = (size_t)threadIdx.x * nmh + mh;
-    const float al = __ldcg(&w.AL[jx]);
-    msc[threadIdx.x] = al > 0 ? __ldcg(&w.AM[jx]) : -1e30f;
+    msc[32 + threadIdx.x] = __ldcg(&w.AL[jx]);
+    red_f_am[threadIdx.x] = __ldcg(&w.AM[jx]);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < d.T) {
     float M0 = -1e30f;
-    for (int tt = 0; tt < d.T; ++tt) M0 = fmaxf(M0, msc[tt]);
-    red_f[0] = M0;
-  }
-  __syncthreads();
-  if (threadIdx.x < d.T) {
-    const size_t jx = (size_t)threadIdx.x * nmh + mh;
-    const float al = __ldcg(&w.AL[jx]);
-    msc[32 + threadIdx.x] = al;
-    msc[threadIdx.x] = al > 0 ? exp_cr(__fsub_rn(__ldcg(&w.AM[jx]), red_f[0])) : 0.f;
+    for (int tt = 0; tt < d.T; ++tt)
+      if (msc[32 + tt] > 0) M0 = fmaxf(M0, red_f_am[tt]);
+    msc[threadIdx.x] = msc[32 + threadIdx.x] > 0 ? exp_cr(__fsub_rn(red_f_am[threadIdx.x], M0)) : 0.f;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -630,9 +648,13 @@ __global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__
   __syncthreads();
   for (int i = threadIdx.x; i < d.hd; i += blockDim.x) {
     float acc = 0.f;
-    for (int tt = 0; tt < d.T; ++tt) {
-      if (!(msc[32 + tt] > 0)) continue;
-      acc = fmaf(__ldcg(&w.AO[((size_t)tt * nmh + mh) * d.hd + i]), msc[tt], acc);
+    if (i == (int)threadIdx.x && d.T <= 8) {
+#pragma unroll
+      for (int tt = 0; tt < 8; ++tt)
+        if (tt < d.T && msc[32 + tt] > 0) acc = fmaf(aov[tt], msc[tt], acc);
+    } else {
+      for (int tt = 0; tt < d.T; ++tt)
+        if (msc[32 + tt] > 0) acc = fmaf(__ldcg(&w.AO[((size_t)tt * nmh + mh) * d.hd + i]), msc[tt], acc);
     }
     const float v = r16(__fmul_rn(acc, s_inv));
     out[(size_t)mh * d.hd + i] = v;
@@ -696,7 +718,7 @@ static int launch_attn(const uint16_t* Kc, const uint16_t* Vc, const float* q, c
   if (rc) return rc;
   static const bool chunk_on = [] {  // G4_ATTN_CHUNK=0/1 overrides the default (experiments)
     const char* e = getenv("G4_ATTN_CHUNK");
-    return e ? e[0] == '1' : false;
+    return e ? e[0] == '1' : true;
   }();
   if (chunk_on && !four && (len + d.T - 1) / d.T + 1 <= kChunkMaxKeys && d.hd % 32 == 0) {
     int* counters = zeroed_counters;

@@ -39,7 +39,7 @@ __device__ __forceinline__ void quant_group32(float x, int8_t& q, float& sx, int
 #pragma unroll
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, o));
   const float s = __fdiv_rn(amax, 127.0f);
-  const float inv = s > 0.f ? __fdiv_rn(1.0f, s) : 0.0f;
+  const float inv = s > 0.f ? __frcp_rn(s) : 0.0f;  // = __fdiv_rn(1.0f, s): both correctly rounded
   const float v = __fmul_rn(x, inv);
   const int32_t r = (v > -2147483648.f && v < 2147483648.f) ? __float2int_rn(v) : INT32_MIN;
   int32_t t = r;

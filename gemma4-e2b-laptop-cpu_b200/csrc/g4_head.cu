@@ -343,53 +343,151 @@ __global__ void __launch_bounds__(256) k_bf16p_gemv_staged(HeadPacked P, const f
 
 // Row-per-thread variant: one thread runs all eight octet-lane chains of its row (the lanes of the
 // reference's 8-wide vectors), so each group's exponent codes are decoded once for every
-// activation row.  A persistent CTA takes blocks of kBrRows rows; per pipeline item every row
-// brings 4 groups (176 bytes) by its own bulk copy into one of kBrNS shared-memory stages, issued
-// kBrNS items ahead; rows sit kBrStride = 208 bytes apart (an odd multiple of 16), so the 8 threads
-// of a 16-byte load phase read 8 different bank quads.  Four weights at a time are decoded with
-// byte permutes: the exponent codes of 4 consecutive elements are spread to bytes by one multiply
-// per bit plane and turned into a permute selector over the 8-entry codebook; the sign/mantissa
-// word and the 4 exponents give the 4 bf16 high and low bytes, which 2 permutes interleave into
-// 2 x 2 floats.  Lane j's chain order (elements j, 16+j, 8+j, 24+j) is kept by visiting the
-// element octets 0, 2, 1, 3 of each group.  The activations sit in shared memory as [k][pair]
-// float2 (one 16-byte broadcast load per element for four rows).  Values are those of
+// activation row.  The thread reads its row straight from global memory, four groups (176 bytes)
+// at a time as 11 aligned 16-byte loads through L1 (the 32 rows of a warp share no cache lines,
+// each 128-byte line serves 8 consecutive loads of its thread), so occupancy is set by registers,
+// not shared memory.  A persistent grid takes 256-row tiles in turn; the activations sit in shared
+// memory as [k][pair] float2 (one 16-byte broadcast load per element for four rows).  Four weights
+// at a time are decoded with byte permutes: the exponent codes of 4 consecutive elements are spread
+// to bytes by one multiply per bit plane and turned into a permute selector over the 8-entry
+// codebook; the sign/mantissa word and the 4 exponents give the bf16 high and low bytes, which 2
+// permutes interleave into 2 x 2 floats.  Lane j's chain order (elements j, 16+j, 8+j, 24+j) is
+// kept by visiting the element octets 0, 2, 1, 3 of each group.  Values are those of
 // k_bf16p_gemv.
-constexpr int kBrRows = 256, kBrStride = 208, kBrNS = 3;
-__host__ __device__ inline size_t head_rows_smem(int M, int K) {
-  return 128 + (size_t)kBrNS * kBrRows * kBrStride + (size_t)K * ((M + 1) / 2) * 8;
+constexpr int kBrThreads = 256;
+__host__ __device__ inline size_t head_rows_smem(int M, int K) { return (size_t)K * ((M + 1) / 2) * 8; }
+
+template <int M>
+__global__ void __launch_bounds__(kBrThreads) k_bf16p_rows(HeadPacked P, const float* __restrict__ X,
+                                                           float* __restrict__ Y, int ldy, const int* __restrict__ gate) {
+  constexpr int NP = (M + 1) / 2;
+  pdl_wait();
+  pdl_trigger();
+  if (gate != nullptr && *gate == 0) return;
+  extern __shared__ __align__(16) float2 xs[];  // [K][NP]
+  const int K = P.K, G = K >> 5, rowb = G * 44;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    float v[2 * NP];
+#pragma unroll
+    for (int m = 0; m < 2 * NP; ++m) v[m] = m < M ? X[(size_t)m * K + i] : 0.f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) xs[(size_t)i * NP + p] = make_float2(v[2 * p], v[2 * p + 1]);
+  }
+  __syncthreads();
+  const uint32_t cb_lo = P.cb_lo, cb_hi = P.cb_hi;
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n - (int)threadIdx.x < P.N; n += gridDim.x * blockDim.x) {
+    if (n >= P.N) continue;
+    const uint4* rowp = reinterpret_cast<const uint4*>(P.data + (size_t)n * rowb);
+    float2 acc[8][NP];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int p = 0; p < NP; ++p) acc[j][p] = make_float2(0.f, 0.f);
+#pragma unroll 1
+    for (int u = 0; u < G / 4; ++u) {
+      uint32_t wv[44];
+#pragma unroll
+      for (int k = 0; k < 11; ++k) {
+        const uint4 t4 = __ldg(rowp + u * 11 + k);
+        wv[4 * k] = t4.x; wv[4 * k + 1] = t4.y; wv[4 * k + 2] = t4.z; wv[4 * k + 3] = t4.w;
+      }
+#pragma unroll
+      for (int gg = 0; gg < 4; ++gg) {
+        const int g = u * 4 + gg;
+        const uint32_t* gw = wv + gg * 11;
+        const uint32_t p0 = gw[8], p1 = gw[9], p2 = gw[10];
+        const float2* xg = xs + (size_t)g * 32 * NP;
+#pragma unroll
+        for (int oi = 0; oi < 4; ++oi) {
+          const int o8 = (oi == 1) ? 2 : (oi == 2 ? 1 : oi);  // element octets in chain order 0, 2, 1, 3
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int sh = 8 * o8 + 4 * h;  // elements sh .. sh+3 = lanes 4h .. 4h+3
+            const uint32_t s0 = (((p0 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
+            const uint32_t s1 = (((p1 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
+            const uint32_t s2 = (((p2 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
+            const uint32_t cc = s0 | (s1 << 1) | (s2 << 2);  // code of element sh + k in byte k
+            const uint32_t sel = __byte_perm(cc | (cc >> 4), 0u, 0x0020u);
+            const uint32_t ex4 = __byte_perm(cb_lo, cb_hi, sel);
+            const uint32_t smw = gw[sh >> 2];
+            const uint32_t hb4 = (smw & 0x80808080u) | ((ex4 >> 1) & 0x7F7F7F7Fu);
+            const uint32_t lb4 = ((ex4 << 7) & 0x80808080u) | (smw & 0x7F7F7F7Fu);
+            const uint32_t t01 = __byte_perm(lb4, hb4, 0x5140u), t23 = __byte_perm(lb4, hb4, 0x7362u);
+            const float wk[4] = {__uint_as_float(t01 << 16), __uint_as_float(t01 & 0xFFFF0000u),
+                                 __uint_as_float(t23 << 16), __uint_as_float(t23 & 0xFFFF0000u)};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int e = sh + k, j = 4 * h + k;
+#pragma unroll
+              for (int p = 0; p < NP; ++p) acc[j][p] = __ffma2_rn(make_float2(wk[k], wk[k]), xg[e * NP + p], acc[j][p]);
+            }
+          }
+        }
+      }
+    }
+    float y[2 * NP];
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      // hsum8: ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7))
+      y[2 * p] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].x, acc[4][p].x), __fadd_rn(acc[1][p].x, acc[5][p].x)),
+                           __fadd_rn(__fadd_rn(acc[2][p].x, acc[6][p].x), __fadd_rn(acc[3][p].x, acc[7][p].x)));
+      y[2 * p + 1] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].y, acc[4][p].y), __fadd_rn(acc[1][p].y, acc[5][p].y)),
+                               __fadd_rn(__fadd_rn(acc[2][p].y, acc[6][p].y), __fadd_rn(acc[3][p].y, acc[7][p].y)));
+    }
+    for (long long e = P.exc_ptr[n]; e < P.exc_ptr[n + 1]; ++e) {  // CSR order, unfused (bf16_exp3_head.h:103)
+      const float dl = P.exc_delta[e];
+      const int col = P.exc_col[e];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        const float2 xv = xs[(size_t)col * NP + p];
+        y[2 * p] = __fadd_rn(y[2 * p], __fmul_rn(dl, xv.x));
+        y[2 * p + 1] = __fadd_rn(y[2 * p + 1], __fmul_rn(dl, xv.y));
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) Y[(size_t)m * ldy + n] = y[m];
+  }
+}
+
+// Row-per-thread variant fed by the TMA: a persistent CTA takes blocks of 256 rows; per pipeline
+// item one 2D tensor-map load brings 4 groups (176 bytes) of all 256 rows into one of kBtNS
+// shared-memory stages as a dense [256][176] box (176 = 11 x 16 bytes, an odd multiple of 16, so
+// the 8 threads of a 16-byte load phase read 8 different bank quads; rows past N read as zeros).
+// The arithmetic is that of k_bf16p_rows.
+constexpr int kBtRows = 256, kBtNS = 3, kBtBox = 176;
+__host__ __device__ inline size_t head_tma_smem(int M, int K) {
+  return 128 + (size_t)kBtNS * kBtRows * kBtBox + (size_t)K * ((M + 1) / 2) * 8;
 }
 
 template <int M>
-__global__ void __launch_bounds__(kBrRows) k_bf16p_rows(HeadPacked P, const float* __restrict__ X,
-                                                        float* __restrict__ Y, int ldy, const int* __restrict__ gate) {
-  pdl_wait();
-  pdl_trigger();
+__global__ void __launch_bounds__(kBtRows) k_bf16p_rows_tma(const __grid_constant__ CUtensorMap tmap, HeadPacked P,
+                                                            const float* __restrict__ X, float* __restrict__ Y, int ldy,
+                                                            const int* __restrict__ gate) {
   constexpr int NP = (M + 1) / 2;
-  if (gate != nullptr && *gate == 0) return;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   uint8_t* stages = smem + 128;
-  float2* xs = reinterpret_cast<float2*>(stages + (size_t)kBrNS * kBrRows * kBrStride);  // [K][NP]
-  const int K = P.K, G = K >> 5, nch = G / 4, rowb = G * 44;
-  const int nblk = (P.N + kBrRows - 1) / kBrRows;
+  float2* xs = reinterpret_cast<float2*>(stages + (size_t)kBtNS * kBtRows * kBtBox);  // [K][NP]
+  pdl_wait();
+  pdl_trigger();
+  if (gate != nullptr && *gate == 0) return;
+  const int K = P.K, G = K >> 5, nch = G / 4;
+  const int nblk = (P.N + kBtRows - 1) / kBtRows;
   const int myblk = nblk > (int)blockIdx.x ? (nblk - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int nitems = myblk * nch;
   const int r = threadIdx.x;
   if (r == 0) {
-    for (int b = 0; b < kBrNS; ++b) mbar_init(&bars[b], 1);
+    for (int b = 0; b < kBtNS; ++b) mbar_init(&bars[b], 1);
     fence_mbar_init();
   }
   __syncthreads();
-  // item i: row block blockIdx.x + (i / nch) * gridDim.x, groups [4c, 4c + 4) with c = i % nch
-  auto issue = [&](int i, int st) {
+  auto issue = [&](int i, int st) {  // thread 0
     const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
-    const int r0 = blk * kBrRows, nr = min(kBrRows, P.N - r0);
-    if (r == 0) mbar_expect_tx(&bars[st], 176u * (uint32_t)nr);
-    if (r < nr)
-      bulk_g2s(stages + ((size_t)st * kBrRows + r) * kBrStride, P.data + (size_t)(r0 + r) * rowb + (size_t)c * 176, 176u,
-               &bars[st]);
+    mbar_expect_tx(&bars[st], (uint32_t)(kBtRows * kBtBox));
+    tma_load_2d(stages + (size_t)st * kBtRows * kBtBox, &tmap, c * kBtBox, blk * kBtRows, &bars[st]);
   };
-  for (int b = 0; b < kBrNS && b < nitems; ++b) issue(b, b);
+  if (r == 0)
+    for (int b = 0; b < kBtNS && b < nitems; ++b) issue(b, b);
   for (int i = r; i < K; i += blockDim.x) {
     float v[2 * NP];
 #pragma unroll
@@ -401,22 +499,27 @@ __global__ void __launch_bounds__(kBrRows) k_bf16p_rows(HeadPacked P, const floa
   const uint32_t cb_lo = P.cb_lo, cb_hi = P.cb_hi;
   float2 acc[8][NP];
   for (int i = 0; i < nitems; ++i) {
-    const int st = i % kBrNS;
+    const int st = i % kBtNS;
     const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
-    const int n = blk * kBrRows + r;
-    if (!cta_wait(&bars[st], (uint32_t)(i / kBrNS) & 1u)) return;
+    const int n = blk * kBtRows + r;
+    if (!cta_wait(&bars[st], (uint32_t)(i / kBtNS) & 1u)) return;
     if (c == 0) {
 #pragma unroll
       for (int j = 0; j < 8; ++j)
 #pragma unroll
         for (int p = 0; p < NP; ++p) acc[j][p] = make_float2(0.f, 0.f);
     }
-    const uint4* rowp = reinterpret_cast<const uint4*>(stages + ((size_t)st * kBrRows + r) * kBrStride);
+    const uint4* rowp = reinterpret_cast<const uint4*>(stages + ((size_t)st * kBtRows + r) * kBtBox);
     uint32_t wv[44];
 #pragma unroll
     for (int k = 0; k < 11; ++k) {
       const uint4 t4 = rowp[k];
       wv[4 * k] = t4.x; wv[4 * k + 1] = t4.y; wv[4 * k + 2] = t4.z; wv[4 * k + 3] = t4.w;
+    }
+    __syncthreads();  // every row has its words in registers: the stage can be refilled
+    if (r == 0 && i + kBtNS < nitems) {
+      fence_proxy_async_smem();
+      issue(i + kBtNS, st);
     }
 #pragma unroll
     for (int gg = 0; gg < 4; ++gg) {
@@ -429,11 +532,11 @@ __global__ void __launch_bounds__(kBrRows) k_bf16p_rows(HeadPacked P, const floa
         const int o8 = (oi == 1) ? 2 : (oi == 2 ? 1 : oi);  // element octets in chain order 0, 2, 1, 3
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int sh = 8 * o8 + 4 * h;  // elements sh .. sh+3 = lanes 4h .. 4h+3
+          const int sh = 8 * o8 + 4 * h;
           const uint32_t s0 = (((p0 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
           const uint32_t s1 = (((p1 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
           const uint32_t s2 = (((p2 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
-          const uint32_t cc = s0 | (s1 << 1) | (s2 << 2);  // code of element sh + k in byte k
+          const uint32_t cc = s0 | (s1 << 1) | (s2 << 2);
           const uint32_t sel = __byte_perm(cc | (cc >> 4), 0u, 0x0020u);
           const uint32_t ex4 = __byte_perm(cb_lo, cb_hi, sel);
           const uint32_t smw = gw[sh >> 2];
@@ -455,7 +558,6 @@ __global__ void __launch_bounds__(kBrRows) k_bf16p_rows(HeadPacked P, const floa
       float y[2 * NP];
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
-        // hsum8: ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7))
         y[2 * p] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].x, acc[4][p].x), __fadd_rn(acc[1][p].x, acc[5][p].x)),
                              __fadd_rn(__fadd_rn(acc[2][p].x, acc[6][p].x), __fadd_rn(acc[3][p].x, acc[7][p].x)));
         y[2 * p + 1] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].y, acc[4][p].y), __fadd_rn(acc[1][p].y, acc[5][p].y)),
@@ -473,11 +575,6 @@ __global__ void __launch_bounds__(kBrRows) k_bf16p_rows(HeadPacked P, const floa
       }
 #pragma unroll
       for (int m = 0; m < M; ++m) Y[(size_t)m * ldy + n] = y[m];
-    }
-    __syncthreads();  // stage st is consumed by every row
-    if (i + kBrNS < nitems) {
-      fence_proxy_async_smem();
-      issue(i + kBrNS, st);
     }
   }
 }
@@ -829,6 +926,26 @@ static HeadPacked make_head(const uint8_t* data, const uint8_t* cb8, const long 
   return P;
 }
 
+// The packed head as a 2D byte tensor [N][rowb] with boxes of [kBtRows][kBtBox]; cached per
+// (address, N, K).  False when the driver entry point or the encoding is unavailable.
+static bool head_tmap(const HeadPacked& P, CUtensorMap* out) {
+  static std::mutex mu;
+  struct Entry { const void* ptr; int N, K; CUtensorMap map; };
+  static Entry cache[8];
+  static int used = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].ptr == P.data && cache[i].N == P.N && cache[i].K == P.K) { *out = cache[i].map; return true; }
+  const uint64_t rowb = (uint64_t)(P.K / 32) * 44;
+  CUtensorMap m;
+  if (!encode_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, P.data, rowb, (uint64_t)P.N, rowb, kBtBox, kBtRows,
+                      CU_TENSOR_MAP_SWIZZLE_NONE))
+    return false;
+  if (used < 8) cache[used++] = Entry{P.data, P.N, P.K, m};
+  *out = m;
+  return true;
+}
+
 static int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -841,13 +958,24 @@ static int num_sms() {
 
 template <int M>
 static int launch_head_gemv(const HeadPacked& P, const float* X, float* Y, int ldy, const int* gate, cudaStream_t st) {
+  const char* hv = getenv("G4_HEAD_GEMV");  // "direct" / "octet" select other variants (experiments)
+  CUtensorMap tm;
+  const size_t tsmem = head_tma_smem(M, P.K);
+  if (!hv && P.K % 128 == 0 && (P.K / 32) * 44 % 16 == 0 && aligned(P.data, 16) && tsmem <= 227 * 1024 && head_tmap(P, &tm)) {
+    cudaFuncSetAttribute(k_bf16p_rows_tma<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem);
+    const int nblk = (P.N + kBtRows - 1) / kBtRows;
+    return launch("k_bf16p_rows_tma", k_bf16p_rows_tma<M>, dim3(std::min(nblk, num_sms())), dim3(kBtRows), tsmem, st, tm, P,
+                  X, Y, ldy, gate);
+  }
   const size_t rsmem = head_rows_smem(M, P.K);
-  const char* hv = getenv("G4_HEAD_GEMV");  // "octet" selects the octet-per-row variant (experiments)
-  if (P.K % 128 == 0 && rsmem <= 227 * 1024 && aligned(P.data, 16) && !(hv && hv[0] == 'o')) {
-    cudaFuncSetAttribute(k_bf16p_rows<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem);
-    const int nblk = (P.N + kBrRows - 1) / kBrRows;
-    return launch("k_bf16p_rows", k_bf16p_rows<M>, dim3(std::min(nblk, num_sms())), dim3(kBrRows), rsmem, st, P, X, Y,
-                  ldy, gate);
+  if (P.K % 128 == 0 && rsmem <= 100 * 1024 && aligned(P.data, 16) && !(hv && hv[0] == 'o')) {
+    if (rsmem > 48 * 1024) cudaFuncSetAttribute(k_bf16p_rows<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem);
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_bf16p_rows<M>, kBrThreads, rsmem) != cudaSuccess || occ < 1)
+      occ = 1;
+    const int nblk = (P.N + kBrThreads - 1) / kBrThreads;
+    return launch("k_bf16p_rows", k_bf16p_rows<M>, dim3(std::min(nblk, num_sms() * occ)), dim3(kBrThreads), rsmem, st, P,
+                  X, Y, ldy, gate);
   }
   const size_t smem = head_smem_bytes(M, P.K);
   if (P.K % 256 == 0 && smem <= 227 * 1024 && aligned(P.data, 16)) {

@@ -207,11 +207,23 @@ __global__ void k_resid_norm(float* __restrict__ o, float* __restrict__ x, const
 constexpr int kRowMax = 2048;
 constexpr int kRowPer = kRowMax / 256;  // elements per thread of a 256-thread row block
 
+// stage_row with every element rounded to bf16 on the way (o = r16(o) before a residual norm).
+__device__ __forceinline__ void stage_row_r16(float* dst, const float* __restrict__ src, int n) {
+  if ((n & 3) == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+    for (int i = threadIdx.x; i < (n >> 2); i += blockDim.x) {
+      const float4 v = reinterpret_cast<const float4*>(src)[i];
+      reinterpret_cast<float4*>(dst)[i] = make_float4(r16(v.x), r16(v.y), r16(v.z), r16(v.w));
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = r16(src[i]);
+  }
+}
+
 // quantise row ys (shared memory, n % 32 == 0) into row m of qo (row length n); needs a barrier
-// between the writes of ys and this call.  Each warp keeps four groups in flight (the arithmetic
+// between the writes of ys and this call.  Each warp keeps eight groups in flight (the arithmetic
 // of quant_group32 per group).
 __device__ __forceinline__ void quant_row(const float* ys, int n, int m, const QuantOut& qo) {
-  constexpr int U = 4;  // groups per warp in flight
+  constexpr int U = 8;  // groups per warp in flight (a 2048-wide row: all of a warp's groups)
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5, G = n >> 5;
   for (int g0 = w; g0 < G; g0 += nw * U) {
     float x[U], amax[U];
@@ -230,7 +242,7 @@ __device__ __forceinline__ void quant_row(const float* ys, int n, int m, const Q
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       s[u] = __fdiv_rn(amax[u], 127.0f);
-      const float inv = s[u] > 0.f ? __fdiv_rn(1.0f, s[u]) : 0.0f;
+      const float inv = s[u] > 0.f ? __frcp_rn(s[u]) : 0.0f;  // = __fdiv_rn(1.0f, s): both correctly rounded
       const float v = __fmul_rn(x[u], inv);
       r[u] = (v > -2147483648.f && v < 2147483648.f) ? __float2int_rn(v) : INT32_MIN;
       t[u] = r[u];
@@ -282,8 +294,6 @@ __global__ void __launch_bounds__(256) k_norm_q(const float* __restrict__ x, con
 __global__ void __launch_bounds__(256) k_post_attn_q(const float* __restrict__ o, float* __restrict__ x,
                                                      const float* __restrict__ w_post, const float* __restrict__ w_pre,
                                                      float* __restrict__ mlp_in, int n, QuantOut qo) {
-  pdl_wait();
-  pdl_trigger();
   __shared__ __align__(16) float os[kRowMax];
   __shared__ __align__(16) float xs[kRowMax];
   __shared__ double red[17];
@@ -296,10 +306,10 @@ __global__ void __launch_bounds__(256) k_post_attn_q(const float* __restrict__ o
     wa[k] = i < n ? w_post[i] : 0.f;
     wb[k] = i < n ? w_pre[i] : 0.f;
   }
-  stage_row(os, o + (size_t)m * n, n);
+  pdl_wait();  // the norm weights above are read-only; the rows come from the previous kernel
+  pdl_trigger();
+  stage_row_r16(os, o + (size_t)m * n, n);  // o = r16(o)
   stage_row(xs, xm, n);
-  __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) os[i] = r16(os[i]);
   __syncthreads();
   const float r = block_rms_scale(os, n, red);
 #pragma unroll
@@ -336,8 +346,6 @@ __global__ void __launch_bounds__(256) k_resid_norm_q(const float* __restrict__ 
                                                       const float* __restrict__ w_post, float scalar, int n,
                                                       const float* __restrict__ w_next, float* __restrict__ a,
                                                       int round_next, QuantOut qo) {
-  pdl_wait();
-  pdl_trigger();
   __shared__ __align__(16) float os[kRowMax];
   __shared__ __align__(16) float xs[kRowMax];
   __shared__ double red[17];
@@ -350,10 +358,10 @@ __global__ void __launch_bounds__(256) k_resid_norm_q(const float* __restrict__ 
     wa[k] = i < n ? w_post[i] : 0.f;
     wb[k] = (i < n && w_next != nullptr) ? w_next[i] : 0.f;
   }
-  stage_row(os, o + (size_t)m * n, n);
+  pdl_wait();  // the norm weights above are read-only; the rows come from the previous kernel
+  pdl_trigger();
+  stage_row_r16(os, o + (size_t)m * n, n);  // o = r16(o)
   stage_row(xs, xm, n);
-  __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) os[i] = r16(os[i]);
   __syncthreads();
   const float r = block_rms_scale(os, n, red);
 #pragma unroll

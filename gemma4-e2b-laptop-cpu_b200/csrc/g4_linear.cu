@@ -212,59 +212,32 @@ k_w4g32(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const fl
 
 // W4G32 float GEMV, row-per-thread variant for tall matrices (the head screen: 262,144 rows).
 // One thread runs the eight lane chains of its row, so each 16-byte group of weights is decoded
-// once for all M activation rows.  A persistent CTA takes blocks of kWrRows rows; per pipeline item
-// every row brings 8 groups of weights (128 B) and their 8 scales (16 B) by bulk copies into one of
-// kWrNS shared-memory stages, issued kWrNS items ahead; rows sit kWrStride = 144 bytes apart (an
-// odd multiple of 16) so the 8 threads of a 16-byte load phase read 8 different bank quads.  The
-// activations sit in shared memory as [k][4] (one 16-byte broadcast load per element for four
-// rows), the group sums as [g][4].  Values are those of k_w4g32: per lane j and group,
-// a = t(2j)x(2j); a = fma(t(16+2j), x(16+2j), a); a = fma(t(2j+1), ...); a = fma(t(17+2j), ...);
+// once for all M activation rows.  The thread reads its row's weights and scales straight from
+// global memory through L1 (16-byte loads; a row's 128-byte lines serve 8 consecutive loads of its
+// thread), so occupancy is set by registers; a persistent grid takes 256-row tiles in turn.  The
+// activations sit in shared memory as [k][4] (one 16-byte broadcast load per element), the group
+// sums as [g][4].  Values are those of k_w4g32: per lane j and group, a = t(2j)x(2j);
+// a = fma(t(16+2j), x(16+2j), a); a = fma(t(2j+1), ...); a = fma(t(17+2j), ...);
 // row_j = fma(a, s, row_j); off = fma(s, gsum, off); y = hsum8(row) - 8 off.
-constexpr int kWrRows = 256, kWrStride = 144, kWrNS = 2;
-__host__ __device__ inline size_t w4g32_rows_smem(int K) {
-  return 128 + (size_t)kWrNS * kWrRows * kWrStride + (size_t)K * 16 + (size_t)(K / 32) * 16;
-}
+constexpr int kWrThreads = 256;
+__host__ __device__ inline size_t w4g32_rows_smem(int K) { return (size_t)K * 16 + (size_t)(K / 32) * 16; }
 
 template <int M>
-__global__ void __launch_bounds__(kWrRows) k_w4g32_rows(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S,
-                                                         const float* __restrict__ X, int N, int K,
-                                                         float* __restrict__ Y, int ldy) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-  uint8_t* stages = smem + 128;
-  float4* xs = reinterpret_cast<float4*>(stages + (size_t)kWrNS * kWrRows * kWrStride);  // [K]
-  float4* gs = xs + K;                                                                    // [G]
-  const int G = K >> 5, nch = G / 8;
-  const int nblk = (N + kWrRows - 1) / kWrRows;
-  const int myblk = nblk > (int)blockIdx.x ? (nblk - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int nitems = myblk * nch;
-  const int r = threadIdx.x;
-  if (r == 0) {
-    for (int b = 0; b < kWrNS; ++b) mbar_init(&bars[b], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  // item i: row block blockIdx.x + (i / nch) * gridDim.x, groups [8c, 8c + 8) with c = i % nch
-  auto issue = [&](int i, int st) {
-    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
-    const int r0 = blk * kWrRows, nr = min(kWrRows, N - r0);
-    if (r == 0) mbar_expect_tx(&bars[st], 144u * (uint32_t)nr);
-    if (r < nr) {
-      uint8_t* dst = stages + ((size_t)st * kWrRows + r) * kWrStride;
-      bulk_g2s(dst, Wp + (size_t)(r0 + r) * (K >> 1) + (size_t)c * 128, 128u, &bars[st]);
-      bulk_g2s(dst + 128, S + (size_t)(r0 + r) * G + (size_t)c * 8, 16u, &bars[st]);
-    }
-  };
-  for (int b = 0; b < kWrNS && b < nitems; ++b) issue(b, b);  // weights only: read-only
+__global__ void __launch_bounds__(kWrThreads) k_w4g32_rows(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S,
+                                                            const float* __restrict__ X, int N, int K,
+                                                            float* __restrict__ Y, int ldy) {
+  extern __shared__ __align__(16) float4 xs[];  // [K], then group sums [G]
   pdl_wait();
   pdl_trigger();
-  for (int i = r; i < K; i += blockDim.x) {
+  const int G = K >> 5;
+  float4* gs = xs + K;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
     float v[4];
 #pragma unroll
     for (int m = 0; m < 4; ++m) v[m] = m < M ? X[(size_t)m * K + i] : 0.f;
     xs[i] = make_float4(v[0], v[1], v[2], v[3]);
   }
-  for (int g = r; g < G; g += blockDim.x) {  // ((x0 + x1) + ...) + x31 from 0 (w4g32_avx2.h:22)
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {  // ((x0 + x1) + ...) + x31 from 0 (w4g32_avx2.h:22)
     float v[4];
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
@@ -276,66 +249,60 @@ __global__ void __launch_bounds__(kWrRows) k_w4g32_rows(const uint8_t* __restric
     gs[g] = make_float4(v[0], v[1], v[2], v[3]);
   }
   __syncthreads();
-  float2 row[8][2], off[2];
-  for (int i = 0; i < nitems; ++i) {
-    const int st = i % kWrNS;
-    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
-    const int n = blk * kWrRows + r;
-    if (!cta_wait(&bars[st], (uint32_t)(i / kWrNS) & 1u)) return;
-    if (c == 0) {
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n - (int)threadIdx.x < N; n += gridDim.x * blockDim.x) {
+    if (n >= N) continue;
+    const uint4* wrow = reinterpret_cast<const uint4*>(Wp + (size_t)n * (K >> 1));
+    const uint4* srow = reinterpret_cast<const uint4*>(S + (size_t)n * G);
+    float2 row[8][2], off[2];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) row[j][0] = row[j][1] = make_float2(0.f, 0.f);
-      off[0] = off[1] = make_float2(0.f, 0.f);
-    }
-    const uint4* rowp = reinterpret_cast<const uint4*>(stages + ((size_t)st * kWrRows + r) * kWrStride);
-    const uint4 s8 = rowp[8];
-    const uint32_t s8w[4] = {s8.x, s8.y, s8.z, s8.w};
+    for (int j = 0; j < 8; ++j) row[j][0] = row[j][1] = make_float2(0.f, 0.f);
+    off[0] = off[1] = make_float2(0.f, 0.f);
+#pragma unroll 1
+    for (int g8 = 0; g8 < G; g8 += 8) {
+      const uint4 s8 = __ldg(srow + (g8 >> 3));
+      const uint32_t s8w[4] = {s8.x, s8.y, s8.z, s8.w};
+      uint4 wq[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int g = c * 8 + u;
-      const uint4 wq = rowp[u];
-      const uint32_t w4[4] = {wq.x, wq.y, wq.z, wq.w};
-      const float scl = bf2f((u & 1) ? (s8w[u >> 1] >> 16) : (s8w[u >> 1] & 0xFFFFu));
-      const float2 sc2 = make_float2(scl, scl);
-      const float4* xg = xs + g * 32;
+      for (int u = 0; u < 8; ++u) wq[u] = __ldg(wrow + g8 + u);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t v = (w4[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;  // bytes 2j, 2j+1
-        float t0, t1, t2, t3;
-        nib4_to_f(v, t0, t1, t2, t3);
-        const float4 x0 = xg[2 * j], x1 = xg[16 + 2 * j], x2 = xg[2 * j + 1], x3 = xg[17 + 2 * j];
-        float2 a0 = __fmul2_rn(make_float2(t0, t0), make_float2(x0.x, x0.y));
-        float2 a1 = __fmul2_rn(make_float2(t0, t0), make_float2(x0.z, x0.w));
-        a0 = __ffma2_rn(make_float2(t1, t1), make_float2(x1.x, x1.y), a0);
-        a1 = __ffma2_rn(make_float2(t1, t1), make_float2(x1.z, x1.w), a1);
-        a0 = __ffma2_rn(make_float2(t2, t2), make_float2(x2.x, x2.y), a0);
-        a1 = __ffma2_rn(make_float2(t2, t2), make_float2(x2.z, x2.w), a1);
-        a0 = __ffma2_rn(make_float2(t3, t3), make_float2(x3.x, x3.y), a0);
-        a1 = __ffma2_rn(make_float2(t3, t3), make_float2(x3.z, x3.w), a1);
-        row[j][0] = __ffma2_rn(a0, sc2, row[j][0]);
-        row[j][1] = __ffma2_rn(a1, sc2, row[j][1]);
-      }
-      const float4 gv = gs[g];
-      off[0] = __ffma2_rn(sc2, make_float2(gv.x, gv.y), off[0]);
-      off[1] = __ffma2_rn(sc2, make_float2(gv.z, gv.w), off[1]);
-    }
-    if (c == nch - 1 && n < N) {
+      for (int u = 0; u < 8; ++u) {
+        const int g = g8 + u;
+        const uint32_t w4[4] = {wq[u].x, wq[u].y, wq[u].z, wq[u].w};
+        const float scl = bf2f((u & 1) ? (s8w[u >> 1] >> 16) : (s8w[u >> 1] & 0xFFFFu));
+        const float2 sc2 = make_float2(scl, scl);
+        const float4* xg = xs + g * 32;
 #pragma unroll
-      for (int m = 0; m < M; ++m) {
-        const int p = m >> 1;
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = (m & 1) ? row[j][p].y : row[j][p].x;
-        const float h = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[4]), __fadd_rn(v[1], v[5])),
-                                  __fadd_rn(__fadd_rn(v[2], v[6]), __fadd_rn(v[3], v[7])));
-        const float o = (m & 1) ? off[p].y : off[p].x;
-        Y[(size_t)m * ldy + n] = __fsub_rn(h, __fmul_rn(8.f, o));
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t v = (w4[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;  // bytes 2j, 2j+1
+          float t0, t1, t2, t3;
+          nib4_to_f(v, t0, t1, t2, t3);
+          const float4 x0 = xg[2 * j], x1 = xg[16 + 2 * j], x2 = xg[2 * j + 1], x3 = xg[17 + 2 * j];
+          float2 a0 = __fmul2_rn(make_float2(t0, t0), make_float2(x0.x, x0.y));
+          float2 a1 = __fmul2_rn(make_float2(t0, t0), make_float2(x0.z, x0.w));
+          a0 = __ffma2_rn(make_float2(t1, t1), make_float2(x1.x, x1.y), a0);
+          a1 = __ffma2_rn(make_float2(t1, t1), make_float2(x1.z, x1.w), a1);
+          a0 = __ffma2_rn(make_float2(t2, t2), make_float2(x2.x, x2.y), a0);
+          a1 = __ffma2_rn(make_float2(t2, t2), make_float2(x2.z, x2.w), a1);
+          a0 = __ffma2_rn(make_float2(t3, t3), make_float2(x3.x, x3.y), a0);
+          a1 = __ffma2_rn(make_float2(t3, t3), make_float2(x3.z, x3.w), a1);
+          row[j][0] = __ffma2_rn(a0, sc2, row[j][0]);
+          row[j][1] = __ffma2_rn(a1, sc2, row[j][1]);
+        }
+        const float4 gv = gs[g];
+        off[0] = __ffma2_rn(sc2, make_float2(gv.x, gv.y), off[0]);
+        off[1] = __ffma2_rn(sc2, make_float2(gv.z, gv.w), off[1]);
       }
     }
-    __syncthreads();  // stage st is consumed by every row
-    if (i + kWrNS < nitems) {
-      fence_proxy_async_smem();
-      issue(i + kWrNS, st);
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int p = m >> 1;
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = (m & 1) ? row[j][p].y : row[j][p].x;
+      const float h = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[4]), __fadd_rn(v[1], v[5])),
+                                __fadd_rn(__fadd_rn(v[2], v[6]), __fadd_rn(v[3], v[7])));
+      const float o = (m & 1) ? off[p].y : off[p].x;
+      Y[(size_t)m * ldy + n] = __fsub_rn(h, __fmul_rn(8.f, o));
     }
   }
 }
@@ -487,10 +454,10 @@ k_w4a8_all(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const
            int CH) {
   constexpr int T = WARPS * 32;
   const int G = K >> 5, nchunk = G / CH;
-  const int wrs = (K >> 1) + 16;  // shared-memory row stride (16 B of padding against bank conflicts)
+  const int wrs = K >> 1;  // the CTA's rows sit as in memory (phase 1 reads one row at a time)
   const int acs = G + 1;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);  // [nchunk] (<= 16)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   uint8_t* wbuf = smem + 128;
   uint16_t* sc = reinterpret_cast<uint16_t*>(wbuf + (size_t)ROWS * wrs);
   float2* ac = reinterpret_cast<float2*>(sc + (size_t)ROWS * G);  // [ROWS*M][G+1]
@@ -498,22 +465,16 @@ k_w4a8_all(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const
   const int nvalid = min(ROWS, N - n0);
 
   if (threadIdx.x == 0) {
-    for (int c = 0; c < nchunk; ++c) mbar_init(&bars[c], 1);
+    mbar_init(&bars[0], 1);
     fence_mbar_init();
+    // the CTA's rows and their scales are contiguous in memory: two bulk copies (one per row
+    // costs issue time)
+    const uint32_t wbytes = (uint32_t)nvalid * (uint32_t)(K >> 1), sbytes = (uint32_t)nvalid * G * 2;
+    mbar_expect_tx(&bars[0], wbytes + sbytes);
+    bulk_g2s(wbuf, Wp + (size_t)n0 * (K >> 1), wbytes, &bars[0]);
+    bulk_g2s(sc, S + (size_t)n0 * G, sbytes, &bars[0]);
   }
-  __syncthreads();
-  if (threadIdx.x < 32) {  // warp 0: lane r issues row r's copies
-    const int lane = threadIdx.x;
-    const uint32_t wbytes = (uint32_t)CH * 16;
-    if (lane == 0)
-      for (int c = 0; c < nchunk; ++c) mbar_expect_tx(&bars[c], nvalid * wbytes + (c == 0 ? (uint32_t)nvalid * G * 2 : 0u));
-    __syncwarp();
-    for (int r = lane; r < nvalid; r += 32)
-      for (int c = 0; c < nchunk; ++c)
-        bulk_g2s(wbuf + (size_t)r * wrs + (size_t)c * wbytes, Wp + (size_t)(n0 + r) * (K >> 1) + (size_t)c * wbytes, wbytes,
-                 &bars[c]);
-    if (lane == 0) bulk_g2s(sc, S + (size_t)n0 * G, (uint32_t)nvalid * G * 2, &bars[0]);
-  }
+  __syncthreads();  // the barrier is initialised before anyone polls it
   pdl_wait();  // the weights above are read-only; activations come from the previous kernel
   pdl_trigger();
   // phase 1: item (group gl of a chunk, row subset rs); with T > CH the rows of a group are split
@@ -535,7 +496,7 @@ k_w4a8_all(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const
   };
   if ((int)threadIdx.x < CH * RS) load_act(threadIdx.x % CH);
   for (int c = 0; c < nchunk; ++c) {
-    if (!cta_wait(&bars[c], 0)) return;
+    if (c == 0 && !cta_wait(&bars[0], 0)) return;
     for (int idx = threadIdx.x; idx < CH * RS; idx += T) {
       const int gl = idx % CH, rs = idx / CH;
       const int g = c * CH + gl;
@@ -773,14 +734,14 @@ extern "C" int g4_w4g32_gemm(const uint8_t* Wp, const uint16_t* S, const float* 
   cudaStream_t st = as_stream(stream);
   // tall matrices (the head screen): row-per-thread variant
   const char* rv = getenv("G4_W4G32_ROWS");  // "0" turns it off (experiments)
-  if (M <= 4 && gsum == nullptr && N >= 16384 && w4g32_rows_smem(K) <= 227 * 1024 && !(rv && rv[0] == '0')) {
+  if (M <= 4 && gsum == nullptr && N >= 16384 && w4g32_rows_smem(K) <= 100 * 1024 && !(rv && rv[0] == '0')) {
     const size_t smem = w4g32_rows_smem(K);
     auto go = [&](auto kern) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       int occ = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kWrRows, smem) != cudaSuccess || occ < 1) occ = 1;
-      const int grid = std::min((N + kWrRows - 1) / kWrRows, sm_count() * occ);
-      if (int rc_ = launch("k_w4g32_rows", kern, dim3(grid), dim3(kWrRows), smem, st, Wp, S, X, N, K, Y, ldy)) return rc_;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kWrThreads, smem) != cudaSuccess || occ < 1) occ = 1;
+      const int grid = std::min((N + kWrThreads - 1) / kWrThreads, sm_count() * occ);
+      if (int rc_ = launch("k_w4g32_rows", kern, dim3(grid), dim3(kWrThreads), smem, st, Wp, S, X, N, K, Y, ldy)) return rc_;
       return check_launch("k_w4g32_rows");
     };
     switch (M) {
@@ -827,7 +788,7 @@ static int launch_w4a8_t(const uint8_t* Wp, const uint16_t* S, const int8_t* q, 
 
 static size_t w4a8_all_smem(int M, int rows, int K) {
   const int G = K / 32;
-  return 128 + (size_t)rows * (K / 2 + 16) + (size_t)rows * G * 2 + (size_t)rows * M * (G + 1) * 8;
+  return 128 + (size_t)rows * (K / 2) + (size_t)rows * G * 2 + (size_t)rows * M * (G + 1) * 8;
 }
 
 template <int M, int ROWS, int WARPS>

@@ -58,6 +58,31 @@ def test_pack_and_logits_golden():
     assert list(idx) == [or_pick(Y[m]) for m in range(Y.shape[0])]
 
 
+@pytest.mark.parametrize("N", [192, 1000, 4099])
+def test_logits_kernel_variants_agree(N, monkeypatch):
+    """The tensor-map-fed head GEMV (default), the direct-load one and the staged octet one compute
+    the same bits for M = 1..4, including a ragged last block of rows, and match the oracle."""
+    rng = np.random.default_rng(N)
+    K = 2048
+    E = bf16_bits(rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+    head = g4.PackedHead(dev(E.view(np.int16)))
+    packed = (head.data.cpu().numpy(), head.exc_ptr.cpu().numpy(),
+              head.exc_col.cpu().numpy()[:head.n_exc].view(np.uint16), head.exc_delta.cpu().numpy()[:head.n_exc])
+    for M in (1, 2, 3, 4):
+        X = (rng.standard_normal((M, K), dtype=np.float32) / np.float32(45.0)).astype(np.float32)
+        Yo = or_head_logits(packed, np.frombuffer(head.cb_host, np.uint8), N, K, X)
+        outs = []
+        for variant in (None, "direct", "octet"):
+            if variant is None:
+                monkeypatch.delenv("G4_HEAD_GEMV", raising=False)
+            else:
+                monkeypatch.setenv("G4_HEAD_GEMV", variant)
+            outs.append(head.logits(dev(X)).cpu().numpy())
+        monkeypatch.delenv("G4_HEAD_GEMV", raising=False)
+        for Y in outs:
+            assert np.array_equal(bits(Y), bits(Yo)), M
+
+
 def test_pick_tie_rule():
     raw = np.zeros((2, 4096), np.float32)
     raw[0, [70, 900, 3000]] = [5.0, 5.0009766, 5.0]  # equal after bf16 rounding: lowest index wins
