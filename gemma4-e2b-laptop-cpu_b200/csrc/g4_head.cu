@@ -449,20 +449,23 @@ __global__ void __launch_bounds__(kBrThreads) k_bf16p_rows(HeadPacked P, const f
   }
 }
 
-// Row-per-thread variant fed by the TMA: a persistent CTA takes blocks of 256 rows; per pipeline
-// item one 2D tensor-map load brings 4 groups (176 bytes) of all 256 rows into one of kBtNS
-// shared-memory stages as a dense [256][176] box (176 = 11 x 16 bytes, an odd multiple of 16, so
-// the 8 threads of a 16-byte load phase read 8 different bank quads; rows past N read as zeros).
-// The arithmetic is that of k_bf16p_rows.
-constexpr int kBtRows = 256, kBtNS = 3, kBtBox = 176;
+// Variant fed by the TMA, two threads per row: thread half h runs lane chains 4h..4h+3 (elements
+// 4h..4h+3 of each octet) over every group in order, and the halves meet in the final hsum8
+// through one shuffle.  A persistent CTA of 256 threads takes 128-row blocks (2 CTAs per SM; the
+// 2048 blocks of the 262,144-row head balance to within 1%); per pipeline item one 2D tensor-map
+// load brings 4 groups (176 bytes) of all 128 rows into one of kBtNS shared-memory stages as a dense
+// [128][176] box (176 = 11 x 16 bytes, an odd multiple of 16, so 16-byte loads of 8 consecutive
+// rows hit 8 different bank quads; rows past N read as zeros).  The arithmetic is that of
+// k_bf16p_rows; the exception patches of activation row m run on half m & 1.
+constexpr int kBtRows = 128, kBtThreads = 256, kBtNS = 3, kBtBox = 176;
 __host__ __device__ inline size_t head_tma_smem(int M, int K) {
   return 128 + (size_t)kBtNS * kBtRows * kBtBox + (size_t)K * ((M + 1) / 2) * 8;
 }
 
 template <int M>
-__global__ void __launch_bounds__(kBtRows) k_bf16p_rows_tma(const __grid_constant__ CUtensorMap tmap, HeadPacked P,
-                                                            const float* __restrict__ X, float* __restrict__ Y, int ldy,
-                                                            const int* __restrict__ gate) {
+__global__ void __launch_bounds__(kBtThreads, 2) k_bf16p_rows_tma(const __grid_constant__ CUtensorMap tmap, HeadPacked P,
+                                                                  const float* __restrict__ X, float* __restrict__ Y, int ldy,
+                                                                  const int* __restrict__ gate) {
   constexpr int NP = (M + 1) / 2;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
@@ -475,8 +478,8 @@ __global__ void __launch_bounds__(kBtRows) k_bf16p_rows_tma(const __grid_constan
   const int nblk = (P.N + kBtRows - 1) / kBtRows;
   const int myblk = nblk > (int)blockIdx.x ? (nblk - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int nitems = myblk * nch;
-  const int r = threadIdx.x;
-  if (r == 0) {
+  const int t = threadIdx.x, rl = t >> 1, half = t & 1;
+  if (t == 0) {
     for (int b = 0; b < kBtNS; ++b) mbar_init(&bars[b], 1);
     fence_mbar_init();
   }
@@ -486,9 +489,9 @@ __global__ void __launch_bounds__(kBtRows) k_bf16p_rows_tma(const __grid_constan
     mbar_expect_tx(&bars[st], (uint32_t)(kBtRows * kBtBox));
     tma_load_2d(stages + (size_t)st * kBtRows * kBtBox, &tmap, c * kBtBox, blk * kBtRows, &bars[st]);
   };
-  if (r == 0)
+  if (t == 0)
     for (int b = 0; b < kBtNS && b < nitems; ++b) issue(b, b);
-  for (int i = r; i < K; i += blockDim.x) {
+  for (int i = t; i < K; i += kBtThreads) {
     float v[2 * NP];
 #pragma unroll
     for (int m = 0; m < 2 * NP; ++m) v[m] = m < M ? X[(size_t)m * K + i] : 0.f;
@@ -497,19 +500,20 @@ __global__ void __launch_bounds__(kBtRows) k_bf16p_rows_tma(const __grid_constan
   }
   __syncthreads();
   const uint32_t cb_lo = P.cb_lo, cb_hi = P.cb_hi;
-  float2 acc[8][NP];
+  const int hsh = 4 * half;
+  float2 acc[4][NP];
   for (int i = 0; i < nitems; ++i) {
     const int st = i % kBtNS;
     const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
-    const int n = blk * kBtRows + r;
+    const int n = blk * kBtRows + rl;
     if (!cta_wait(&bars[st], (uint32_t)(i / kBtNS) & 1u)) return;
     if (c == 0) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int p = 0; p < NP; ++p) acc[j][p] = make_float2(0.f, 0.f);
     }
-    const uint4* rowp = reinterpret_cast<const uint4*>(stages + ((size_t)st * kBtRows + r) * kBtBox);
+    const uint4* rowp = reinterpret_cast<const uint4*>(stages + ((size_t)st * kBtRows + rl) * kBtBox);
     uint32_t wv[44];
 #pragma unroll
     for (int k = 0; k < 11; ++k) {
@@ -517,7 +521,7 @@ __global__ void __launch_bounds__(kBtRows) k_bf16p_rows_tma(const __grid_constan
       wv[4 * k] = t4.x; wv[4 * k + 1] = t4.y; wv[4 * k + 2] = t4.z; wv[4 * k + 3] = t4.w;
     }
     __syncthreads();  // every row has its words in registers: the stage can be refilled
-    if (r == 0 && i + kBtNS < nitems) {
+    if (t == 0 && i + kBtNS < nitems) {
       fence_proxy_async_smem();
       issue(i + kBtNS, st);
     }
@@ -526,55 +530,64 @@ __global__ void __launch_bounds__(kBtRows) k_bf16p_rows_tma(const __grid_constan
       const int g = c * 4 + gg;
       const uint32_t* gw = wv + gg * 11;
       const uint32_t p0 = gw[8], p1 = gw[9], p2 = gw[10];
-      const float2* xg = xs + (size_t)g * 32 * NP;
+      const float2* xg = xs + ((size_t)g * 32 + hsh) * NP;
 #pragma unroll
       for (int oi = 0; oi < 4; ++oi) {
         const int o8 = (oi == 1) ? 2 : (oi == 2 ? 1 : oi);  // element octets in chain order 0, 2, 1, 3
+        const int sh = 8 * o8 + hsh;
+        const uint32_t s0 = (((p0 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
+        const uint32_t s1 = (((p1 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
+        const uint32_t s2 = (((p2 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
+        const uint32_t cc = s0 | (s1 << 1) | (s2 << 2);
+        const uint32_t sel = __byte_perm(cc | (cc >> 4), 0u, 0x0020u);
+        const uint32_t ex4 = __byte_perm(cb_lo, cb_hi, sel);
+        const uint32_t smw = half ? gw[2 * o8 + 1] : gw[2 * o8];
+        const uint32_t hb4 = (smw & 0x80808080u) | ((ex4 >> 1) & 0x7F7F7F7Fu);
+        const uint32_t lb4 = ((ex4 << 7) & 0x80808080u) | (smw & 0x7F7F7F7Fu);
+        const uint32_t t01 = __byte_perm(lb4, hb4, 0x5140u), t23 = __byte_perm(lb4, hb4, 0x7362u);
+        const float wk[4] = {__uint_as_float(t01 << 16), __uint_as_float(t01 & 0xFFFF0000u),
+                             __uint_as_float(t23 << 16), __uint_as_float(t23 & 0xFFFF0000u)};
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int sh = 8 * o8 + 4 * h;
-          const uint32_t s0 = (((p0 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
-          const uint32_t s1 = (((p1 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
-          const uint32_t s2 = (((p2 >> sh) & 0xFu) * 0x00204081u) & 0x01010101u;
-          const uint32_t cc = s0 | (s1 << 1) | (s2 << 2);
-          const uint32_t sel = __byte_perm(cc | (cc >> 4), 0u, 0x0020u);
-          const uint32_t ex4 = __byte_perm(cb_lo, cb_hi, sel);
-          const uint32_t smw = gw[sh >> 2];
-          const uint32_t hb4 = (smw & 0x80808080u) | ((ex4 >> 1) & 0x7F7F7F7Fu);
-          const uint32_t lb4 = ((ex4 << 7) & 0x80808080u) | (smw & 0x7F7F7F7Fu);
-          const uint32_t t01 = __byte_perm(lb4, hb4, 0x5140u), t23 = __byte_perm(lb4, hb4, 0x7362u);
-          const float wk[4] = {__uint_as_float(t01 << 16), __uint_as_float(t01 & 0xFFFF0000u),
-                               __uint_as_float(t23 << 16), __uint_as_float(t23 & 0xFFFF0000u)};
+        for (int k = 0; k < 4; ++k)
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int e = sh + k, j = 4 * h + k;
-#pragma unroll
-            for (int p = 0; p < NP; ++p) acc[j][p] = __ffma2_rn(make_float2(wk[k], wk[k]), xg[e * NP + p], acc[j][p]);
-          }
-        }
+          for (int p = 0; p < NP; ++p)
+            acc[k][p] = __ffma2_rn(make_float2(wk[k], wk[k]), xg[(8 * o8 + k) * NP + p], acc[k][p]);
       }
     }
-    if (c == nch - 1 && n < P.N) {
+    if (c == nch - 1) {
+      // lanes 4..7 come from the other half; fadd is commutative, so both halves hold
+      // ((v0 + v4) + (v1 + v5)) + ((v2 + v6) + (v3 + v7)) bit for bit
       float y[2 * NP];
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
-        y[2 * p] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].x, acc[4][p].x), __fadd_rn(acc[1][p].x, acc[5][p].x)),
-                             __fadd_rn(__fadd_rn(acc[2][p].x, acc[6][p].x), __fadd_rn(acc[3][p].x, acc[7][p].x)));
-        y[2 * p + 1] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].y, acc[4][p].y), __fadd_rn(acc[1][p].y, acc[5][p].y)),
-                                 __fadd_rn(__fadd_rn(acc[2][p].y, acc[6][p].y), __fadd_rn(acc[3][p].y, acc[7][p].y)));
-      }
-      for (long long e = P.exc_ptr[n]; e < P.exc_ptr[n + 1]; ++e) {  // CSR order, unfused (bf16_exp3_head.h:103)
-        const float dl = P.exc_delta[e];
-        const int col = P.exc_col[e];
+        float2 w[4];
 #pragma unroll
-        for (int p = 0; p < NP; ++p) {
-          const float2 xv = xs[(size_t)col * NP + p];
-          y[2 * p] = __fadd_rn(y[2 * p], __fmul_rn(dl, xv.x));
-          y[2 * p + 1] = __fadd_rn(y[2 * p + 1], __fmul_rn(dl, xv.y));
+        for (int k = 0; k < 4; ++k) {
+          w[k].x = __shfl_xor_sync(0xffffffffu, acc[k][p].x, 1);
+          w[k].y = __shfl_xor_sync(0xffffffffu, acc[k][p].y, 1);
         }
+        y[2 * p] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].x, w[0].x), __fadd_rn(acc[1][p].x, w[1].x)),
+                             __fadd_rn(__fadd_rn(acc[2][p].x, w[2].x), __fadd_rn(acc[3][p].x, w[3].x)));
+        y[2 * p + 1] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].y, w[0].y), __fadd_rn(acc[1][p].y, w[1].y)),
+                                 __fadd_rn(__fadd_rn(acc[2][p].y, w[2].y), __fadd_rn(acc[3][p].y, w[3].y)));
       }
+      if (n < P.N) {
+        float yo[NP];  // this half's activation rows 2p + half
 #pragma unroll
-      for (int m = 0; m < M; ++m) Y[(size_t)m * ldy + n] = y[m];
+        for (int p = 0; p < NP; ++p) yo[p] = half ? y[2 * p + 1] : y[2 * p];
+        for (long long e = P.exc_ptr[n]; e < P.exc_ptr[n + 1]; ++e) {  // CSR order, unfused (bf16_exp3_head.h:103)
+          const float dl = P.exc_delta[e];
+          const int col = P.exc_col[e];
+#pragma unroll
+          for (int p = 0; p < NP; ++p) {
+            const float2 xv = xs[(size_t)col * NP + p];
+            yo[p] = __fadd_rn(yo[p], __fmul_rn(dl, half ? xv.y : xv.x));
+          }
+        }
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+          if (2 * p + half < M) Y[(size_t)(2 * p + half) * ldy + n] = yo[p];
+      }
     }
   }
 }
@@ -963,9 +976,13 @@ static int launch_head_gemv(const HeadPacked& P, const float* X, float* Y, int l
   const size_t tsmem = head_tma_smem(M, P.K);
   if (!hv && P.K % 128 == 0 && (P.K / 32) * 44 % 16 == 0 && aligned(P.data, 16) && tsmem <= 227 * 1024 && head_tmap(P, &tm)) {
     cudaFuncSetAttribute(k_bf16p_rows_tma<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem);
+    cudaFuncSetAttribute(k_bf16p_rows_tma<M>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);  // 2 CTAs per SM
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_bf16p_rows_tma<M>, kBtThreads, tsmem) != cudaSuccess || occ < 1)
+      occ = 1;
     const int nblk = (P.N + kBtRows - 1) / kBtRows;
-    return launch("k_bf16p_rows_tma", k_bf16p_rows_tma<M>, dim3(std::min(nblk, num_sms())), dim3(kBtRows), tsmem, st, tm, P,
-                  X, Y, ldy, gate);
+    return launch("k_bf16p_rows_tma", k_bf16p_rows_tma<M>, dim3(std::min(nblk, num_sms() * occ)), dim3(kBtThreads), tsmem,
+                  st, tm, P, X, Y, ldy, gate);
   }
   const size_t rsmem = head_rows_smem(M, P.K);
   if (P.K % 128 == 0 && rsmem <= 100 * 1024 && aligned(P.data, 16) && !(hv && hv[0] == 'o')) {

@@ -3,6 +3,7 @@
 // candidate scoring, and the seeded weight generator.  Each follows the rounding points of the
 // reference's fwd (gemma4_engine.cpp:1262-1404) operation for operation.
 #include "g4_layers.cuh"
+#include "g4_api.h"
 
 namespace g4 {
 
@@ -199,197 +200,271 @@ __global__ void k_resid_norm(float* __restrict__ o, float* __restrict__ x, const
   for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = r16(__fadd_rn(x[i], r16(__fmul_rn(__fmul_rn(o[i], r), w[i]))));
 }
 
-// ---- fused row kernels: one block (256 threads) per activation row.  The row is first staged in
-// shared memory (one coalesced pass), so the RMS partial sums run from shared memory; each kernel
-// then writes its float outputs and, when qo.q is set, the W4A8 quantisation of the row that the
-// next linear consumes (quant_group32 per 32-group, identical to g4_w4a8_quant).  They replace
-// norm -> quantise pairs of launches with one and compute the same values as the unfused kernels.
+// ---- fused row kernels: one block (256 threads) per activation row, rows up to kRowMax wide and a
+// multiple of 256.  Thread t owns the float4 blocks f = t + 256k (elements 4f..4f+3) and keeps them
+// in registers from load to store; the row also goes to shared memory for the sequential fallback
+// of the RMS sum.  When qo.q is set the kernel writes the W4A8 quantisation of its output row for
+// the next linear (the values of g4_w4a8_quant).  They compute the values of the unfused kernels.
 constexpr int kRowMax = 2048;
-constexpr int kRowPer = kRowMax / 256;  // elements per thread of a 256-thread row block
+constexpr int kF4 = kRowMax / 1024;  // float4 blocks per thread
 
-// stage_row with every element rounded to bf16 on the way (o = r16(o) before a residual norm).
-__device__ __forceinline__ void stage_row_r16(float* dst, const float* __restrict__ src, int n) {
-  if ((n & 3) == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
-    for (int i = threadIdx.x; i < (n >> 2); i += blockDim.x) {
-      const float4 v = reinterpret_cast<const float4*>(src)[i];
-      reinterpret_cast<float4*>(dst)[i] = make_float4(r16(v.x), r16(v.y), r16(v.z), r16(v.w));
-    }
-  } else {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = r16(src[i]);
-  }
+struct RmsScratch {
+  double part[8][16];     // per warp and partial: the warp's share of the partial sum
+  uint32_t keys[8][8];    // per warp: exponent keys of two partials per word (see row_rms_scale)
+  double chain[16];       // the 16 partial sums
+};
+
+// Exponent keys of x for the exactness test of row_rms_scale, packed as the bytes of a max-reduced
+// word: (kmax, 255 - kmin) of the nonzero elements' biased exponents (subnormals as 1; a value that
+// is not bf16-valued or not finite counts as kmax 255, kmin 1, which fails the test).
+__device__ __forceinline__ uint32_t ekeys(float x) {
+  const uint32_t b = __float_as_uint(x) & 0x7FFFFFFFu;
+  if (b == 0u) return 0u;
+  uint32_t e = b >> 23;
+  if ((b & 0xFFFFu) != 0u || e == 255u) return (255u << 8) | 254u;
+  if (e == 0u) e = 1u;
+  return (e << 8) | (255u - e);
 }
 
-// quantise row ys (shared memory, n % 32 == 0) into row m of qo (row length n); needs a barrier
-// between the writes of ys and this call.  Each warp keeps eight groups in flight (the arithmetic
-// of quant_group32 per group).
-__device__ __forceinline__ void quant_row(const float* ys, int n, int m, const QuantOut& qo) {
-  constexpr int U = 8;  // groups per warp in flight (a 2048-wide row: all of a warp's groups)
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5, G = n >> 5;
-  for (int g0 = w; g0 < G; g0 += nw * U) {
-    float x[U], amax[U];
+// RMS scale of a row held as float4 blocks, in the reference's order (gemma4_engine.cpp:326-343):
+// the sum of squares in double over 16 partials (element j to partial j % 16, each partial in
+// element order), combined as ((p_b + p_4+b) + (p_8+b + p_12+b)) for b = 0..3, then
+// (t0 + t2) + (t1 + t3); r = 1 / sqrtf((float)(ss / n) + eps).
+// A partial is summed as a tree when that is exact: if its elements are bf16-valued and the biased
+// exponents of its nonzero elements span at most 15, every squared element is an integer multiple
+// of u = 2^(2 e_min - 268) and any sum of at most 128 of them is below 2^(2 e_max - 245) =
+// 2^(23 + 2 span) u <= 2^53 u, hence exact in double; the sequential sum then equals the exact sum,
+// as does any other order.  Other partials take the sequential chain over xs (the row in shared
+// memory, written before the call).  Needs blockDim 256, n <= 2048; every thread gets r.
+__device__ float row_rms_scale(const float4 (&v)[kF4], const float* xs, int n, RmsScratch& sc) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5, nf = n >> 2;
+  double d[4] = {0.0, 0.0, 0.0, 0.0};  // partials 4 (t % 4) + e
+  uint32_t k01 = 0u, k23 = 0u;         // keys of partials e = 0, 1 and 2, 3 (two bytes each)
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int g = g0 + u * nw;
-      x[u] = g < G ? ys[g * 32 + lane] : 0.f;
-      amax[u] = fabsf(x[u]);
+  for (int k = 0; k < kF4; ++k)
+    if (t + 256 * k < nf) {
+      const float c[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) { const double x = c[e]; d[e] = fma(x, x, d[e]); }
+      k01 = __vmaxu4(k01, ekeys(c[0]) | (ekeys(c[1]) << 16));
+      k23 = __vmaxu4(k23, ekeys(c[2]) | (ekeys(c[3]) << 16));
     }
 #pragma unroll
-    for (int o = 16; o; o >>= 1)
+  for (int o = 4; o < 32; o <<= 1) {  // lanes with equal lane % 4 hold the same partials
 #pragma unroll
-      for (int u = 0; u < U; ++u) amax[u] = fmaxf(amax[u], __shfl_xor_sync(FULL, amax[u], o));
-    float s[U];
-    int32_t r[U], t[U];
+    for (int e = 0; e < 4; ++e) d[e] += __shfl_xor_sync(FULL, d[e], o);
+    k01 = __vmaxu4(k01, __shfl_xor_sync(FULL, k01, o));
+    k23 = __vmaxu4(k23, __shfl_xor_sync(FULL, k23, o));
+  }
+  if (lane < 4) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      s[u] = __fdiv_rn(amax[u], 127.0f);
-      const float inv = s[u] > 0.f ? __frcp_rn(s[u]) : 0.0f;  // = __fdiv_rn(1.0f, s): both correctly rounded
-      const float v = __fmul_rn(x[u], inv);
-      r[u] = (v > -2147483648.f && v < 2147483648.f) ? __float2int_rn(v) : INT32_MIN;
-      t[u] = r[u];
+    for (int e = 0; e < 4; ++e) sc.part[w][4 * lane + e] = d[e];
+    sc.keys[w][2 * lane] = k01;
+    sc.keys[w][2 * lane + 1] = k23;
+  }
+  __syncthreads();
+  if (t < 16) {
+    double s = 0.0;
+    uint32_t kw = 0u;
+#pragma unroll
+    for (int ww = 0; ww < 8; ++ww) {
+      s += sc.part[ww][t];
+      kw = __vmaxu4(kw, sc.keys[ww][t >> 1]);
     }
-#pragma unroll
-    for (int o = 16; o; o >>= 1)
-#pragma unroll
-      for (int u = 0; u < U; ++u) t[u] += __shfl_xor_sync(FULL, t[u], o);
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int g = g0 + u * nw;
-      if (g < G) {
-        const int32_t r16v = r[u] < -32768 ? -32768 : (r[u] > 32767 ? 32767 : r[u]);
-        qo.q[(size_t)m * n + g * 32 + lane] = (int8_t)(r16v < -128 ? -128 : (r16v > 127 ? 127 : r16v));
-        if (lane == 0) {
-          qo.sx[(size_t)m * G + g] = s[u];
-          qo.sum[(size_t)m * G + g] = t[u];
-        }
-      }
+    const uint32_t kk = (kw >> (16 * (t & 1))) & 0xFFFFu;  // this partial's (kmax, 255 - kmin)
+    const int kmax = (int)(kk >> 8), kmin = 255 - (int)(kk & 0xFFu);
+    if (kmax - kmin > 15) {  // the chain may round: the sequential sum in element order
+      s = 0.0;
+      for (int i = t; i < n; i += 16) { const double x = xs[i]; s = fma(x, x, s); }
     }
+    sc.chain[t] = s;
+  }
+  __syncthreads();
+  double tb[4];
+#pragma unroll
+  for (int b = 0; b < 4; ++b) tb[b] = (sc.chain[b] + sc.chain[4 + b]) + (sc.chain[8 + b] + sc.chain[12 + b]);
+  const double ss = (tb[0] + tb[2]) + (tb[1] + tb[3]);
+  const double mean = (n & (n - 1)) == 0 ? ss * (1.0 / (double)n) : ss / (double)n;  // equal for a power of two
+  return __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)mean, 1e-6f)));
+}
+
+__device__ __forceinline__ float4 f4_r16(float4 a) { return make_float4(r16(a.x), r16(a.y), r16(a.z), r16(a.w)); }
+__device__ __forceinline__ float4 f4_load(const float* p, int f) { return reinterpret_cast<const float4*>(p)[f]; }
+__device__ __forceinline__ void f4_store(float* p, int f, float4 a) { reinterpret_cast<float4*>(p)[f] = a; }
+// (a * r) * w per element
+__device__ __forceinline__ float4 f4_scale(float4 a, float r, float4 w) {
+  return make_float4(__fmul_rn(__fmul_rn(a.x, r), w.x), __fmul_rn(__fmul_rn(a.y, r), w.y),
+                     __fmul_rn(__fmul_rn(a.z, r), w.z), __fmul_rn(__fmul_rn(a.w, r), w.w));
+}
+// r16(x + r16((o * r) * w)) per element
+__device__ __forceinline__ float4 f4_resid(float4 x, float4 o, float r, float4 w) {
+  const float4 u = f4_r16(f4_scale(o, r, w));
+  return f4_r16(make_float4(__fadd_rn(x.x, u.x), __fadd_rn(x.y, u.y), __fadd_rn(x.z, u.z), __fadd_rn(x.w, u.w)));
+}
+
+// quant_group32 of one float4 block per thread: a group of 32 is the 8 consecutive lanes holding
+// its blocks; all 32 lanes of the warp call it together.
+__device__ __forceinline__ void quant_f4(float4 y, int f, int m, int n, const QuantOut& qo) {
+  float amax = fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w)));
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, o));
+  const float s = __fdiv_rn(amax, 127.0f);
+  const float inv = s > 0.f ? __frcp_rn(s) : 0.0f;  // = __fdiv_rn(1.0f, s): both correctly rounded
+  const float c[4] = {y.x, y.y, y.z, y.w};
+  int32_t tot = 0;
+  uint32_t packed = 0u;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float v = __fmul_rn(c[e], inv);
+    const int32_t r = (v > -2147483648.f && v < 2147483648.f) ? __float2int_rn(v) : INT32_MIN;
+    tot += r;
+    const int32_t r16v = r < -32768 ? -32768 : (r > 32767 ? 32767 : r);
+    const int32_t q = r16v < -128 ? -128 : (r16v > 127 ? 127 : r16v);
+    packed |= ((uint32_t)q & 0xFFu) << (8 * e);
+  }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) tot += __shfl_xor_sync(FULL, tot, o);
+  reinterpret_cast<uint32_t*>(qo.q + (size_t)m * n)[f] = packed;
+  if ((threadIdx.x & 7) == 0) {
+    const int G = n >> 5;
+    qo.sx[(size_t)m * G + (f >> 3)] = s;
+    qo.sum[(size_t)m * G + (f >> 3)] = tot;
   }
 }
 
 // y[m] = (x[m]*r)*w, optionally rounded to bf16 (rms / rms_prep_x, :344-352, :365-381).
 __global__ void __launch_bounds__(256) k_norm_q(const float* __restrict__ x, const float* __restrict__ w, int n,
                                                 float* __restrict__ y, int round, QuantOut qo) {
-  pdl_wait();
-  pdl_trigger();
   __shared__ __align__(16) float xs[kRowMax];
-  __shared__ double red[17];
-  const int m = blockIdx.x;
-  stage_row(xs, x + (size_t)m * n, n);
-  __syncthreads();
-  const float r = block_rms_scale(xs, n, red);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float v = __fmul_rn(__fmul_rn(xs[i], r), w[i]);
-    if (round) v = r16(v);
-    y[(size_t)m * n + i] = v;
-    xs[i] = v;
+  __shared__ RmsScratch sc;
+  const int m = blockIdx.x, t = threadIdx.x, nf = n >> 2;
+  float4 wv[kF4], v[kF4];
+#pragma unroll
+  for (int k = 0; k < kF4; ++k) wv[k] = t + 256 * k < nf ? f4_load(w, t + 256 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
+  pdl_wait();  // the norm weights above are read-only; the row comes from the previous kernel
+  pdl_trigger();
+#pragma unroll
+  for (int k = 0; k < kF4; ++k) {
+    const int f = t + 256 * k;
+    v[k] = f < nf ? f4_load(x + (size_t)m * n, f) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (f < nf) f4_store(xs, f, v[k]);
   }
-  if (qo.q) {
-    __syncthreads();
-    quant_row(xs, n, m, qo);
+  const float r = row_rms_scale(v, xs, n, sc);
+#pragma unroll
+  for (int k = 0; k < kF4; ++k) {
+    const int f = t + 256 * k;
+    if (f < nf) {  // warp-uniform (nf is a multiple of 64)
+      float4 yv = f4_scale(v[k], r, wv[k]);
+      if (round) yv = f4_r16(yv);
+      f4_store(y + (size_t)m * n, f, yv);
+      if (qo.q) quant_f4(yv, f, m, n, qo);
+    }
   }
 }
 
-// k_post_attn with the pre-MLP input quantised: o = r16(o); x = r16(x + r16((o*r)*w_post));
-// mlp_in = r16((x*r')*w_pre).
+// After o_proj (:1358-1361) with the pre-MLP input quantised: o = r16(o);
+// x = r16(x + r16((o*r)*w_post)); mlp_in = r16((x*r')*w_pre).
 __global__ void __launch_bounds__(256) k_post_attn_q(const float* __restrict__ o, float* __restrict__ x,
                                                      const float* __restrict__ w_post, const float* __restrict__ w_pre,
                                                      float* __restrict__ mlp_in, int n, QuantOut qo) {
   __shared__ __align__(16) float os[kRowMax];
   __shared__ __align__(16) float xs[kRowMax];
-  __shared__ double red[17];
-  const int m = blockIdx.x;
+  __shared__ RmsScratch sc1, sc2;
+  const int m = blockIdx.x, t = threadIdx.x, nf = n >> 2;
   float* xm = x + (size_t)m * n;
-  float wa[kRowPer], wb[kRowPer];  // this thread's norm weights, loaded with the rows
+  float4 wa[kF4], wb[kF4], ov[kF4], xv[kF4];
 #pragma unroll
-  for (int k = 0; k < kRowPer; ++k) {
-    const int i = threadIdx.x + 256 * k;
-    wa[k] = i < n ? w_post[i] : 0.f;
-    wb[k] = i < n ? w_pre[i] : 0.f;
+  for (int k = 0; k < kF4; ++k) {
+    const bool in = t + 256 * k < nf;
+    wa[k] = in ? f4_load(w_post, t + 256 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    wb[k] = in ? f4_load(w_pre, t + 256 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  pdl_wait();  // the norm weights above are read-only; the rows come from the previous kernel
+  pdl_wait();  // the norm weights above are read-only; the rows come from earlier kernels
   pdl_trigger();
-  stage_row_r16(os, o + (size_t)m * n, n);  // o = r16(o)
-  stage_row(xs, xm, n);
-  __syncthreads();
-  const float r = block_rms_scale(os, n, red);
 #pragma unroll
-  for (int k = 0; k < kRowPer; ++k) {
-    const int i = threadIdx.x + 256 * k;
-    if (i < n) {
-      const float v = r16(__fadd_rn(xs[i], r16(__fmul_rn(__fmul_rn(os[i], r), wa[k]))));
-      xs[i] = v;
-      xm[i] = v;
+  for (int k = 0; k < kF4; ++k) {
+    const int f = t + 256 * k;
+    const bool in = f < nf;
+    ov[k] = in ? f4_r16(f4_load(o + (size_t)m * n, f)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    xv[k] = in ? f4_load(xm, f) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (in) f4_store(os, f, ov[k]);
+  }
+  const float r = row_rms_scale(ov, os, n, sc1);
+#pragma unroll
+  for (int k = 0; k < kF4; ++k) {
+    const int f = t + 256 * k;
+    if (f < nf) {
+      xv[k] = f4_resid(xv[k], ov[k], r, wa[k]);
+      f4_store(xm, f, xv[k]);
+      f4_store(xs, f, xv[k]);
     }
   }
-  __syncthreads();
-  const float r2 = block_rms_scale(xs, n, red);
+  const float r2 = row_rms_scale(xv, xs, n, sc2);
 #pragma unroll
-  for (int k = 0; k < kRowPer; ++k) {
-    const int i = threadIdx.x + 256 * k;
-    if (i < n) {
-      const float v = r16(__fmul_rn(__fmul_rn(xs[i], r2), wb[k]));
-      mlp_in[(size_t)m * n + i] = v;
-      os[i] = v;
+  for (int k = 0; k < kF4; ++k) {
+    const int f = t + 256 * k;
+    if (f < nf) {  // warp-uniform
+      const float4 yv = f4_r16(f4_scale(xv[k], r2, wb[k]));
+      f4_store(mlp_in + (size_t)m * n, f, yv);
+      if (qo.q) quant_f4(yv, f, m, n, qo);
     }
-  }
-  if (qo.q) {
-    __syncthreads();
-    quant_row(os, n, m, qo);
   }
 }
 
 // Residual after the MLP (or the drafter's attention / MLP), then the next norm:
 //   o = r16(o); x = r16(x + r16((o*r)*w_post)); if (scalar != 0) x = r16(x*scalar)
 //   (k_post_ff / k_resid_norm + k_scale_round); then, when w_next is set,
-//   a = (x*r')*w_next (rounded when round_next) and its quantisation.
-__global__ void __launch_bounds__(256) k_resid_norm_q(const float* __restrict__ o, float* __restrict__ x,
+//   a = (x*r')*w_next (rounded when round_next) and its quantisation.  a may alias o.
+__global__ void __launch_bounds__(256) k_resid_norm_q(const float* o, float* __restrict__ x,
                                                       const float* __restrict__ w_post, float scalar, int n,
-                                                      const float* __restrict__ w_next, float* __restrict__ a,
+                                                      const float* __restrict__ w_next, float* a,
                                                       int round_next, QuantOut qo) {
   __shared__ __align__(16) float os[kRowMax];
   __shared__ __align__(16) float xs[kRowMax];
-  __shared__ double red[17];
-  const int m = blockIdx.x;
+  __shared__ RmsScratch sc1, sc2;
+  const int m = blockIdx.x, t = threadIdx.x, nf = n >> 2;
   float* xm = x + (size_t)m * n;
-  float wa[kRowPer], wb[kRowPer];  // this thread's norm weights, loaded with the rows
+  float4 wa[kF4], wb[kF4], ov[kF4], xv[kF4];
 #pragma unroll
-  for (int k = 0; k < kRowPer; ++k) {
-    const int i = threadIdx.x + 256 * k;
-    wa[k] = i < n ? w_post[i] : 0.f;
-    wb[k] = (i < n && w_next != nullptr) ? w_next[i] : 0.f;
+  for (int k = 0; k < kF4; ++k) {
+    const bool in = t + 256 * k < nf;
+    wa[k] = in ? f4_load(w_post, t + 256 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    wb[k] = (in && w_next != nullptr) ? f4_load(w_next, t + 256 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  pdl_wait();  // the norm weights above are read-only; the rows come from the previous kernel
+  pdl_wait();  // the norm weights above are read-only; the rows come from earlier kernels
   pdl_trigger();
-  stage_row_r16(os, o + (size_t)m * n, n);  // o = r16(o)
-  stage_row(xs, xm, n);
-  __syncthreads();
-  const float r = block_rms_scale(os, n, red);
 #pragma unroll
-  for (int k = 0; k < kRowPer; ++k) {
-    const int i = threadIdx.x + 256 * k;
-    if (i < n) {
-      float v = r16(__fadd_rn(xs[i], r16(__fmul_rn(__fmul_rn(os[i], r), wa[k]))));
-      if (scalar != 0.f) v = r16(__fmul_rn(v, scalar));
-      xs[i] = v;
-      xm[i] = v;
+  for (int k = 0; k < kF4; ++k) {
+    const int f = t + 256 * k;
+    const bool in = f < nf;
+    ov[k] = in ? f4_r16(f4_load(o + (size_t)m * n, f)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    xv[k] = in ? f4_load(xm, f) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (in) f4_store(os, f, ov[k]);
+  }
+  const float r = row_rms_scale(ov, os, n, sc1);
+#pragma unroll
+  for (int k = 0; k < kF4; ++k) {
+    const int f = t + 256 * k;
+    if (f < nf) {
+      float4 v = f4_resid(xv[k], ov[k], r, wa[k]);
+      if (scalar != 0.f) v = f4_r16(make_float4(__fmul_rn(v.x, scalar), __fmul_rn(v.y, scalar), __fmul_rn(v.z, scalar),
+                                                __fmul_rn(v.w, scalar)));
+      xv[k] = v;
+      f4_store(xm, f, v);
+      f4_store(xs, f, v);
     }
   }
   if (w_next == nullptr) return;
-  __syncthreads();
-  const float r2 = block_rms_scale(xs, n, red);
+  const float r2 = row_rms_scale(xv, xs, n, sc2);
 #pragma unroll
-  for (int k = 0; k < kRowPer; ++k) {
-    const int i = threadIdx.x + 256 * k;
-    if (i < n) {
-      float v = __fmul_rn(__fmul_rn(xs[i], r2), wb[k]);
-      if (round_next) v = r16(v);
-      a[(size_t)m * n + i] = v;
-      os[i] = v;
+  for (int k = 0; k < kF4; ++k) {
+    const int f = t + 256 * k;
+    if (f < nf) {  // warp-uniform
+      float4 yv = f4_scale(xv[k], r2, wb[k]);
+      if (round_next) yv = f4_r16(yv);
+      f4_store(a + (size_t)m * n, f, yv);
+      if (qo.q) quant_f4(yv, f, m, n, qo);
     }
-  }
-  if (qo.q) {
-    __syncthreads();
-    quant_row(os, n, m, qo);
   }
 }
 
@@ -619,3 +694,16 @@ __global__ void k_gen_embed(uint64_t seed, long long n, uint16_t* __restrict__ o
 }
 
 }  // namespace g4
+
+extern "C" int g4_rmsnorm(const float* x, const float* w, int M, int n, float* y, int round, int8_t* q, float* sx,
+                          int32_t* sum, void* stream) {
+  using namespace g4;
+  G4_REQUIRE(x && w && y && (q == nullptr || (sx && sum)), "g4_rmsnorm: null pointer");
+  G4_REQUIRE(M >= 1 && n >= 256 && n <= kRowMax && n % 256 == 0, "g4_rmsnorm: unsupported shape M=%d n=%d", M, n);
+  G4_REQUIRE(aligned(x, 16) && aligned(w, 16) && aligned(y, 16) && (q == nullptr || aligned(q, 4)),
+             "g4_rmsnorm: x, w and y must be 16-byte aligned, q 4-byte aligned");
+  if (int rc = launch("k_norm_q", k_norm_q, dim3(M), dim3(256), 0, as_stream(stream), x, w, n, y, round,
+                      QuantOut{q, sx, sum}))
+    return rc;
+  return check_launch("k_norm_q");
+}

@@ -15,6 +15,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <cstdio>
+#include <mutex>
 
 namespace g4 {
 
@@ -303,6 +304,151 @@ __global__ void __launch_bounds__(kWrThreads) k_w4g32_rows(const uint8_t* __rest
                                 __fadd_rn(__fadd_rn(v[2], v[6]), __fadd_rn(v[3], v[7])));
       const float o = (m & 1) ? off[p].y : off[p].x;
       Y[(size_t)m * ldy + n] = __fsub_rn(h, __fmul_rn(8.f, o));
+    }
+  }
+}
+
+// W4G32 float GEMV fed by the TMA (the head screen's tall matrix), same values as k_w4g32_rows.
+// Two threads share a row: thread half h runs lane chains 4h..4h+3 over every group in order, and
+// the two halves meet in the final hsum8 through one shuffle.  A persistent CTA of 256 threads
+// takes 128-row blocks (2048 blocks for the 262,144-row screen balance over 2 CTAs per SM to
+// within 1%); per pipeline item two 2D tensor-map loads bring 8 groups of all 128 rows into one of
+// kTwNS stages: the weights as a [128][128 B] box under the 128-byte swizzle (chunk u of row r
+// lands at chunk u ^ (r & 7), so a 16-thread phase of 8-byte loads hits 8 distinct bank quads) and
+// the bf16 scales as a [128][16 B] box.  Rows past N read as zeros and are not stored.  The
+// activations sit in shared memory as element pairs [k/2][NP] float4 {x_m(2q), x_m+1(2q),
+// x_m(2q+1), x_m+1(2q+1)}, which serve a lane's elements 2j, 2j+1 and 16+2j, 17+2j in two loads.
+constexpr int kTwRows = 128, kTwThreads = 256, kTwNS = 4;
+constexpr int kTwStage = kTwRows * 128 + kTwRows * 16;  // 18 KB, a multiple of the swizzle span
+__host__ __device__ inline size_t w4g32_tma_smem(int M, int K) {
+  const int NP = (M + 1) / 2;
+  return 1024 + (size_t)kTwNS * kTwStage + (size_t)(K / 2) * NP * 16 + (size_t)(K / 32) * NP * 8;
+}
+
+template <int M>
+__global__ void __launch_bounds__(kTwThreads, 2)
+k_w4g32_rows_tma(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
+                 const float* __restrict__ X, int N, int K, float* __restrict__ Y, int ldy) {
+  constexpr int NP = (M + 1) / 2;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[kTwNS];
+  uint8_t* stages = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // 1024-byte aligned
+  float4* xs = reinterpret_cast<float4*>(stages + (size_t)kTwNS * kTwStage);       // [K/2][NP]
+  float2* gs = reinterpret_cast<float2*>(xs + (size_t)(K / 2) * NP);               // [G][NP]
+  pdl_wait();
+  pdl_trigger();
+  const int G = K >> 5, nch = G >> 3;
+  const int nblk = (N + kTwRows - 1) / kTwRows;
+  const int myblk = nblk > (int)blockIdx.x ? (nblk - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int nitems = myblk * nch;
+  const int t = threadIdx.x, rl = t >> 1, half = t & 1;
+  if (t == 0) {
+    for (int b = 0; b < kTwNS; ++b) mbar_init(&bars[b], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int i, int st) {  // thread 0
+    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
+    uint8_t* sb = stages + (size_t)st * kTwStage;
+    mbar_expect_tx(&bars[st], (uint32_t)kTwStage);
+    tma_load_2d(sb, &tw, c * 128, blk * kTwRows, &bars[st]);
+    tma_load_2d(sb + kTwRows * 128, &ts, c * 8, blk * kTwRows, &bars[st]);
+  };
+  if (t == 0)
+    for (int b = 0; b < kTwNS && b < nitems; ++b) issue(b, b);
+  for (int q = t; q < K / 2; q += kTwThreads) {
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      const int m0 = 2 * p, m1 = 2 * p + 1;
+      const float a0 = X[(size_t)m0 * K + 2 * q], b0 = X[(size_t)m0 * K + 2 * q + 1];
+      const float a1 = m1 < M ? X[(size_t)m1 * K + 2 * q] : 0.f, b1 = m1 < M ? X[(size_t)m1 * K + 2 * q + 1] : 0.f;
+      xs[(size_t)q * NP + p] = make_float4(a0, a1, b0, b1);
+    }
+  }
+  for (int g = t; g < G; g += kTwThreads) {  // ((x0 + x1) + ...) + x31 from 0 (w4g32_avx2.h:22)
+    float v[2 * NP];
+#pragma unroll
+    for (int m = 0; m < 2 * NP; ++m) {
+      float sm = 0.f;
+      if (m < M)
+        for (int k = 0; k < 32; ++k) sm = __fadd_rn(sm, X[(size_t)m * K + g * 32 + k]);
+      v[m] = sm;
+    }
+#pragma unroll
+    for (int p = 0; p < NP; ++p) gs[(size_t)g * NP + p] = make_float2(v[2 * p], v[2 * p + 1]);
+  }
+  __syncthreads();
+  float2 row[4][NP], off[NP];
+  for (int i = 0; i < nitems; ++i) {
+    const int st = i % kTwNS;
+    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
+    const int n = blk * kTwRows + rl;
+    if (!cta_wait(&bars[st], (uint32_t)(i / kTwNS) & 1u)) return;
+    if (c == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int p = 0; p < NP; ++p) row[j][p] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int p = 0; p < NP; ++p) off[p] = make_float2(0.f, 0.f);
+    }
+    const uint8_t* sb = stages + (size_t)st * kTwStage;
+    uint2 wq[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      wq[u] = *reinterpret_cast<const uint2*>(sb + rl * 128 + ((u ^ (rl & 7)) << 4) + half * 8);
+    const uint4 s8 = *reinterpret_cast<const uint4*>(sb + kTwRows * 128 + rl * 16);
+    __syncthreads();  // every thread has its words in registers: the stage can be refilled
+    if (t == 0 && i + kTwNS < nitems) {
+      fence_proxy_async_smem();
+      issue(i + kTwNS, st);
+    }
+    const uint32_t s8w[4] = {s8.x, s8.y, s8.z, s8.w};
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int g = c * 8 + u;
+      const float scl = bf2f((u & 1) ? (s8w[u >> 1] >> 16) : (s8w[u >> 1] & 0xFFFFu));
+      const float2 sc2 = make_float2(scl, scl);
+      const float4* xg = xs + (size_t)g * 16 * NP;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int j = 4 * half + jj;  // lane chain: bytes 2j, 2j+1 of the group
+        const uint32_t v = ((jj < 2 ? wq[u].x : wq[u].y) >> (16 * (jj & 1))) & 0xFFFFu;
+        float t0, t1, t2, t3;
+        nib4_to_f(v, t0, t1, t2, t3);
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+          const float4 A = xg[j * NP + p], B = xg[(8 + j) * NP + p];
+          float2 a = __fmul2_rn(make_float2(t0, t0), make_float2(A.x, A.y));
+          a = __ffma2_rn(make_float2(t1, t1), make_float2(B.x, B.y), a);
+          a = __ffma2_rn(make_float2(t2, t2), make_float2(A.z, A.w), a);
+          a = __ffma2_rn(make_float2(t3, t3), make_float2(B.z, B.w), a);
+          row[jj][p] = __ffma2_rn(a, sc2, row[jj][p]);
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < NP; ++p) off[p] = __ffma2_rn(sc2, gs[(size_t)g * NP + p], off[p]);
+    }
+    if (c == nch - 1) {
+      // lanes 4..7 of the row come from the other half; fadd is commutative, so both halves get
+      // ((v0 + v4) + (v1 + v5)) + ((v2 + v6) + (v3 + v7)) bit for bit
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        float2 w[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          w[jj].x = __shfl_xor_sync(0xffffffffu, row[jj][p].x, 1);
+          w[jj].y = __shfl_xor_sync(0xffffffffu, row[jj][p].y, 1);
+        }
+        const float hx = __fadd_rn(__fadd_rn(__fadd_rn(row[0][p].x, w[0].x), __fadd_rn(row[1][p].x, w[1].x)),
+                                   __fadd_rn(__fadd_rn(row[2][p].x, w[2].x), __fadd_rn(row[3][p].x, w[3].x)));
+        const float hy = __fadd_rn(__fadd_rn(__fadd_rn(row[0][p].y, w[0].y), __fadd_rn(row[1][p].y, w[1].y)),
+                                   __fadd_rn(__fadd_rn(row[2][p].y, w[2].y), __fadd_rn(row[3][p].y, w[3].y)));
+        if (n < N) {
+          if (half == 0) Y[(size_t)(2 * p) * ldy + n] = __fsub_rn(hx, __fmul_rn(8.f, off[p].x));
+          else if (2 * p + 1 < M) Y[(size_t)(2 * p + 1) * ldy + n] = __fsub_rn(hy, __fmul_rn(8.f, off[p].y));
+        }
+      }
     }
   }
 }
@@ -714,6 +860,34 @@ static int launch_w4g32_t(const uint8_t* Wp, const uint16_t* S, const float* X, 
   return check_launch("k_w4g32");
 }
 
+// Tensor maps of a packed W4G32 matrix for k_w4g32_rows_tma: the weights as bytes [N][K/2] in
+// [128][128 B] boxes under the 128-byte swizzle, the bf16 scales as [N][K/32] in [128][8] boxes.
+// Cached per (weights, scales, N, K).
+static bool w4g32_tmaps(const uint8_t* Wp, const uint16_t* S, int N, int K, CUtensorMap* tw, CUtensorMap* ts) {
+  static std::mutex mu;
+  struct Entry { const void* w; const void* s; int N, K; CUtensorMap mw, ms; };
+  static Entry cache[8];
+  static int used = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].w == Wp && cache[i].s == S && cache[i].N == N && cache[i].K == K) {
+      *tw = cache[i].mw;
+      *ts = cache[i].ms;
+      return true;
+    }
+  const uint64_t G = (uint64_t)K / 32;
+  CUtensorMap mw, ms;
+  if (!encode_tmap_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, Wp, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
+                      kTwRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT16, S, G, (uint64_t)N, G * 2, 8, kTwRows,
+                      CU_TENSOR_MAP_SWIZZLE_NONE))
+    return false;
+  if (used < 8) cache[used++] = Entry{Wp, S, N, K, mw, ms};
+  *tw = mw;
+  *ts = ms;
+  return true;
+}
+
 template <int M>
 static int launch_w4g32(const uint8_t* Wp, const uint16_t* S, const float* X, const float* gsum, int N, int K,
                         float* Y, int ldy, cudaStream_t st) {
@@ -732,8 +906,28 @@ extern "C" int g4_w4g32_gemm(const uint8_t* Wp, const uint16_t* S, const float* 
   G4_REQUIRE(aligned(Wp, 16) && aligned(S, 16) && aligned(X, 16) && (gsum == nullptr || aligned(gsum, 4)),
              "g4_w4g32_gemm: Wp, S and X must be 16-byte aligned");
   cudaStream_t st = as_stream(stream);
-  // tall matrices (the head screen): row-per-thread variant
-  const char* rv = getenv("G4_W4G32_ROWS");  // "0" turns it off (experiments)
+  // tall matrices (the head screen): the TMA-fed variant, else the row-per-thread one
+  const char* rv = getenv("G4_W4G32_ROWS");  // "0" / "direct" select other variants (experiments)
+  CUtensorMap tw, ts;
+  const size_t tsmem = w4g32_tma_smem(M, K);
+  if (M <= 4 && gsum == nullptr && N >= 16384 && !rv && tsmem <= 113 * 1024 && w4g32_tmaps(Wp, S, N, K, &tw, &ts)) {
+    auto go = [&](auto kern) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem);
+      cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);  // 2 CTAs per SM
+      int occ = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTwThreads, tsmem) != cudaSuccess || occ < 1) occ = 1;
+      const int grid = std::min((N + kTwRows - 1) / kTwRows, sm_count() * occ);
+      if (int rc_ = launch("k_w4g32_rows_tma", kern, dim3(grid), dim3(kTwThreads), tsmem, st, tw, ts, X, N, K, Y, ldy))
+        return rc_;
+      return check_launch("k_w4g32_rows_tma");
+    };
+    switch (M) {
+      case 1: return go(k_w4g32_rows_tma<1>);
+      case 2: return go(k_w4g32_rows_tma<2>);
+      case 3: return go(k_w4g32_rows_tma<3>);
+      default: return go(k_w4g32_rows_tma<4>);
+    }
+  }
   if (M <= 4 && gsum == nullptr && N >= 16384 && w4g32_rows_smem(K) <= 100 * 1024 && !(rv && rv[0] == '0')) {
     const size_t smem = w4g32_rows_smem(K);
     auto go = [&](auto kern) {

@@ -33,6 +33,7 @@ SIGNATURES = {
     "g4_bf16p_pack": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _P]),
     "g4_bf16p_gemm": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _I, _P, _I, _P]),
     "g4_head_argmax": (_I, [_P, _I, _I, _I, _P, _P, _SZ, _P]),
+    "g4_rmsnorm": (_I, [_P, _P, _I, _I, _P, _I, _P, _P, _P, _P]),
     "g4_screen_build": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "g4_head_screen_ws_bytes": (_SZ, [_I, _I, _I]),
     "g4_head_screen": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _SZ, _P]),
@@ -133,6 +134,25 @@ def w4g32_gemm(Wp, S, X, gsum=None, out=None):
     check(lib().g4_w4g32_gemm(_ptr(Wp), _ptr(S), _ptr(X), _ptr(gsum), M, N, K, _ptr(Y), Y.stride(0), _stream()),
           "g4_w4g32_gemm")
     return Y
+
+
+def rmsnorm(X, w, round_=False, quant=False):
+    """Y = (X * r) * w per row (bf16-rounded when round_), and with quant the W4A8 quantisation of
+    Y as (q, sx, sum); r in the order of the reference's rms."""
+    import torch
+    _dev(X, "X")
+    _dev(w, "w")
+    M, n = X.shape
+    Y = torch.empty((M, n), dtype=torch.float32, device=X.device)
+    if quant:
+        q = torch.empty((M, n), dtype=torch.int8, device=X.device)
+        sx = torch.empty((M, n // 32), dtype=torch.float32, device=X.device)
+        sm = torch.empty((M, n // 32), dtype=torch.int32, device=X.device)
+    else:
+        q = sx = sm = None
+    check(lib().g4_rmsnorm(_ptr(X), _ptr(w), M, n, _ptr(Y), int(round_), _ptr(q), _ptr(sx), _ptr(sm), _stream()),
+          "g4_rmsnorm")
+    return (Y, q, sx, sm) if quant else Y
 
 
 def w4a8_quant(X):

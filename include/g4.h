@@ -71,6 +71,16 @@ int g4_w4a8_quant(const float* X, int M, int K, int8_t* q, float* sx, int32_t* s
 int g4_w4a8_gemm(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
                  int M, int N, int K, float* Y, int ldy, void* stream);
 
+/* ---------------------------------------------------------------- row norms */
+
+/* RMS norm of M rows, y = (x * r) * w with r = 1 / sqrtf((float)(ss / n) + 1e-6f) and ss the sum
+ * of squares in double over the reference's 16 ordered partials (rms / rms_prep_x,
+ * gemma4_engine.cpp:326-352, 365-381); y rounded to bf16 when round != 0.  When q is not NULL the
+ * rows of y are also quantised as g4_w4a8_quant does (q [M][n], sx and sum [M][n/32]).
+ * x, w, y dev; n a multiple of 256, at most 2048. */
+int g4_rmsnorm(const float* x, const float* w, int M, int n, float* y, int round, int8_t* q, float* sx, int32_t* sum,
+               void* stream);
+
 /* ---------------------------------------------------------------- output head */
 
 /* Once per device, before any stream capture: uploads the softcap table (r16(30*tanh(s/30)) of

@@ -207,6 +207,10 @@ static void rmsnorm(const float* x, const float* w, int n, float* y, int round) 
   const float r = rms_scale(x, n);
   for (int i = 0; i < n; ++i) { const float v = (x[i] * r) * w[i]; y[i] = round ? or_r16(v) : v; }
 }
+/* M rows of rmsnorm (the checker of g4_rmsnorm). */
+void or_rmsnorm(const float* x, const float* w, int M, int n, float* y, int round) {
+  for (int m = 0; m < M; ++m) rmsnorm(x + (size_t)m * n, w, n, y + (size_t)m * n, round);
+}
 static void rope(float* h, const float* cs, const float* sn, int hd) {
   const int hh = hd / 2;
   for (int j = 0; j < hh; ++j) {

@@ -53,6 +53,7 @@ _SIGS_ORACLE = {
     "or_e2e_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "or_e2e_gen_bytes": (None, [ctypes.c_ulonglong, ctypes.c_ulonglong, ctypes.c_longlong, _P]),
     "or_e2e_fake_ctx": (None, [_P, _I]),
+    "or_rmsnorm": (None, [_P, _P, _I, _I, _P, _I]),
 }
 
 _SIGS_REF = {
@@ -133,6 +134,15 @@ def or_w4g32(W, S, X):
     N = W.shape[0]
     Y = np.empty((M, N), np.float32)
     oracle().or_w4g32_gemm(ptr(W), ptr(S), ptr(X), M, N, K, ptr(Y))
+    return Y
+
+
+def or_rmsnorm(X, w, round_):
+    X = np.ascontiguousarray(X, np.float32)
+    M, n = X.shape
+    Y = np.empty((M, n), np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    oracle().or_rmsnorm(ptr(X), ptr(w), M, n, ptr(Y), int(round_))
     return Y
 
 

@@ -89,6 +89,30 @@ def test_w4g32_cfg0(M):
     assert np.array_equal(bits(Y), bits(ref))
 
 
+@pytest.mark.parametrize("N,K", [(16384, 2048), (20011, 2048), (16500, 4096)])
+def test_w4g32_tall_variants(N, K, monkeypatch):
+    """Tall matrices (the head screen's shape class, N >= 16384) take the tensor-map-fed kernel by
+    default; the row-per-thread kernel and the generic CTA-per-rows kernel must give the same
+    bits, for M = 1..4, a ragged last row block and an output stride ldy > N."""
+    rng = np.random.default_rng(N + K)
+    W, S = w4g32_weights(rng, N, K)
+    Wp, Sd = g4.w4_pack(dev(W)), dev(S)
+    for M in (1, 2, 3, 4):
+        X = rng.standard_normal((M, K), dtype=np.float32)
+        ref = or_w4g32(W, S, X)
+        for variant in (None, "direct", "0"):
+            if variant is None:
+                monkeypatch.delenv("G4_W4G32_ROWS", raising=False)
+            else:
+                monkeypatch.setenv("G4_W4G32_ROWS", variant)
+            out = torch.full((M, N + 13), -7.0, device="cuda")
+            g4.w4g32_gemm(Wp, Sd, dev(X), out=out[:, :N])
+            Y = out.cpu().numpy()
+            assert np.array_equal(bits(Y[:, :N]), bits(ref)), (M, variant)
+            assert np.all(Y[:, N:] == -7.0), (M, variant)
+        monkeypatch.delenv("G4_W4G32_ROWS", raising=False)
+
+
 def test_w4g32_precomputed_gsum_and_ldy():
     rng = np.random.default_rng(7)
     W, S = w4g32_weights(rng, 1000, 4096)
