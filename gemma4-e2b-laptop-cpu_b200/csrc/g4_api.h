@@ -59,6 +59,11 @@ inline int launch(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 bloc
 // output rows are also quantised for a W4A8 linear when qo.q is set.  zeroed_counters (may be NULL):
 // M*nh ints that are 0 on entry, reserved for such calls (they are 0 again when the call
 // completes); with them no counter reset is enqueued.
+// g4_head_screen with the fallback GEMV over the unpacked copy of the head (unp, may be NULL).
+int head_screen_impl(const uint8_t* W4p, const uint16_t* S4, const float* coef, const uint8_t* data, const uint8_t* unp,
+                     const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col, const float* exc_delta, int N,
+                     int K, const float* H, int M, int lim, int* out_idx, int* out_nsurv, void* ws, size_t ws_bytes,
+                     void* stream);
 int attn_splitkv_dev(const uint16_t* Kc, const uint16_t* Vc, const float* q, int M, int nh, int hd, const int* dP,
                      int base_add, int q_add, int window, int max_len, int T, float* out, void* ws, size_t ws_bytes,
                      cudaStream_t st, QuantOut qo, int* zeroed_counters = nullptr);

@@ -37,6 +37,7 @@ __device__ __forceinline__ AttnDesc resolve(const AttnDesc& d0) {
   if (d.dynP != nullptr) {
     const int P = *d.dynP;
     d.kmin = 1 << 30;
+#pragma unroll
     for (int m = 0; m < 4; ++m) {
       if (m < d.M) {
         d.pos[m] = P + d.base_add + m;
@@ -52,7 +53,18 @@ __device__ __forceinline__ AttnDesc resolve(const AttnDesc& d0) {
   return d;
 }
 
-__device__ __forceinline__ bool allowed(const AttnDesc& d, int m, int p) { return p >= d.lo[m] && p <= d.pos[m]; }
+// Row m's first and last key, selected without indexing the descriptor's arrays (a runtime index
+// would move the descriptor to local memory).
+__device__ __forceinline__ int sel4(const int (&a)[4], int m) {
+  int r = a[0];
+  r = m == 1 ? a[1] : r;
+  r = m == 2 ? a[2] : r;
+  r = m == 3 ? a[3] : r;
+  return r;
+}
+__device__ __forceinline__ int dlo(const AttnDesc& d, int m) { return sel4(d.lo, m); }
+__device__ __forceinline__ int dpos(const AttnDesc& d, int m) { return sel4(d.pos, m); }
+__device__ __forceinline__ bool allowed(const AttnDesc& d, int m, int p) { return p >= dlo(d, m) && p <= dpos(d, m); }
 __device__ __forceinline__ int chunk_lo(const AttnDesc& d, int t) {
   const int len = d.kmax - d.kmin + 1;
   return d.kmin + (int)((long long)t * len / d.T);
@@ -77,19 +89,32 @@ __device__ __forceinline__ AttnWs attn_ws(float* base, const AttnDesc& d) {
 }
 
 // ---- scores.  A block takes kScoreKeys consecutive keys, copies their K rows into shared memory
-// (one bulk copy), and gives each (row, head) pair one half-warp: lane c runs the reference's AVX
-// partial sum c (elements c, c+16, ...; q for the pair stays in registers), then the two 8-lane
-// halves are added and reduced with the 8-lane tree of hsum (:786-797).
+// (one bulk copy) and transposes them so that the elements c, c+16, ... of partial c sit together
+// (lane slots of kLaneStr bytes, an odd multiple of 16, so a half-warp's 16-byte loads are
+// conflict-free); each (row, head) pair gets one half-warp: lane c runs the reference's AVX
+// partial sum c (elements c, c+16, ... in order; q for the pair stays in registers), then the two
+// 8-lane halves are added and reduced with the 8-lane tree of hsum (:786-797).
 constexpr int kScoreKeys = 32;
+template <int STEPS>
+struct ScoreTile {
+  static constexpr int kLaneStr = ((STEPS * 2 / 16) | 1) * 16;  // bytes per lane slot
+  static constexpr int kKeyStr = 16 * kLaneStr;                   // bytes per transposed key
+};
+__host__ __device__ inline size_t attn_scores_smem(int hd) {
+  const int steps = hd / 16, lane_str = ((steps * 2 / 16) | 1) * 16;
+  return 128 + (size_t)kScoreKeys * hd * 2 + (size_t)kScoreKeys * 16 * lane_str;
+}
 template <int STEPS>  // hd / 16
 __global__ void __launch_bounds__(512) k_attn_scores(const uint16_t* __restrict__ Kc, const float* __restrict__ q,
                                                      AttnDesc d0, float* __restrict__ ws) {
   pdl_wait();
   pdl_trigger();
+  constexpr int HD = STEPS * 16, LS = ScoreTile<STEPS>::kLaneStr, KS = ScoreTile<STEPS>::kKeyStr;
   extern __shared__ __align__(128) uint8_t sm_raw[];
   const AttnDesc d = resolve(d0);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm_raw);
-  const uint16_t* kt = reinterpret_cast<const uint16_t*>(sm_raw + 128);
+  const uint4* kraw = reinterpret_cast<const uint4*>(sm_raw + 128);
+  uint8_t* ktt = sm_raw + 128 + (size_t)kScoreKeys * HD * 2;
   const AttnWs w = attn_ws(ws, d);
   const int len = d.kmax - d.kmin + 1;
   const int p0 = d.kmin + blockIdx.x * kScoreKeys;
@@ -101,29 +126,52 @@ __global__ void __launch_bounds__(512) k_attn_scores(const uint16_t* __restrict_
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    const uint32_t bytes = (uint32_t)nk * d.hd * 2;
+    const uint32_t bytes = (uint32_t)nk * HD * 2;
     mbar_expect_tx(bar, bytes);
-    bulk_g2s(sm_raw + 128, Kc + (size_t)p0 * d.hd, bytes, bar);
+    bulk_g2s(sm_raw + 128, Kc + (size_t)p0 * HD, bytes, bar);
   }
   const int hw = threadIdx.x >> 4, c = threadIdx.x & 15;
   const bool live_mh = hw < d.M * d.nh;
   const int m = live_mh ? hw / d.nh : 0, h = live_mh ? hw % d.nh : 0;
   float qr[STEPS];
-  const float* qh = q + ((size_t)m * d.nh + h) * d.hd;
+  const float* qh = q + ((size_t)m * d.nh + h) * HD;
 #pragma unroll
   for (int i = 0; i < STEPS; ++i) qr[i] = qh[c + 16 * i];
   if (!cta_wait(bar, 0)) return;
+  // transpose: element e = c + 16 i of a key goes to lane slot c, position i
+  for (int e8 = threadIdx.x; e8 < nk * (HD / 8); e8 += blockDim.x) {
+    const int key = e8 / (HD / 8), e0 = (e8 % (HD / 8)) * 8;
+    const uint4 v = kraw[e8];
+    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    uint16_t* kd = reinterpret_cast<uint16_t*>(ktt + (size_t)key * KS);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = e0 + j;
+      kd[((e & 15) * LS >> 1) + (e >> 4)] = (uint16_t)(wv[j >> 1] >> (16 * (j & 1)));
+    }
+  }
+  __syncthreads();
   float* srow = w.S + (size_t)hw * len + (p0 - d.kmin);
+  auto score = [&](int k) {  // lane c's partial for key k
+    const uint4* kp = reinterpret_cast<const uint4*>(ktt + (size_t)k * KS + c * LS);
+    float acc = 0.f;
+#pragma unroll
+    for (int v4 = 0; v4 < STEPS / 8; ++v4) {
+      const uint4 t4 = kp[v4];
+      const uint32_t wv[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t u = wv[j >> 1];
+        acc = fmaf(qr[8 * v4 + j], __uint_as_float((j & 1) ? (u & 0xFFFF0000u) : (u << 16)), acc);
+      }
+    }
+    return acc;
+  };
   int k = 0;
   for (; k + 4 <= nk; k += 4) {  // four keys at a time: independent chains for latency hiding
     float acc[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint16_t* kr = kt + (size_t)(k + u) * d.hd;
-      acc[u] = 0.f;
-#pragma unroll
-      for (int i = 0; i < STEPS; ++i) acc[u] = fmaf(qr[i], bf2f(kr[c + 16 * i]), acc[u]);
-    }
+    for (int u = 0; u < 4; ++u) acc[u] = score(k + u);
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const float sc = hsum8_octet(__fadd_rn(acc[u], __shfl_xor_sync(FULL, acc[u], 8)));
@@ -131,10 +179,7 @@ __global__ void __launch_bounds__(512) k_attn_scores(const uint16_t* __restrict_
     }
   }
   for (; k < nk; ++k) {
-    const uint16_t* kr = kt + (size_t)k * d.hd;
-    float acc = 0.f;
-#pragma unroll
-    for (int i = 0; i < STEPS; ++i) acc = fmaf(qr[i], bf2f(kr[c + 16 * i]), acc);
+    const float acc = score(k);
     const float sc = hsum8_octet(__fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8)));
     if (c == 0 && live_mh && allowed(d, m, p0 + k)) srow[k] = sc;
   }
@@ -154,7 +199,7 @@ __global__ void __launch_bounds__(256) k_attn_stats(AttnDesc d0, float* __restri
   const int mh = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31, t = blockIdx.x;
   if (mh >= d.M * d.nh) return;
   const int m = mh / d.nh, len = d.kmax - d.kmin + 1;
-  const int c0 = max(chunk_lo(d, t), d.lo[m]), c1 = min(chunk_lo(d, t + 1), d.pos[m] + 1);  // allowed keys of the chunk
+  const int c0 = max(chunk_lo(d, t), dlo(d, m)), c1 = min(chunk_lo(d, t + 1), dpos(d, m) + 1);  // allowed keys of the chunk
   float* srow = w.S + (size_t)mh * len - d.kmin;
   constexpr int SEG = 32 * kStatSlots;
   const bool one = c1 - c0 <= SEG;  // the whole chunk fits the registers: load it once
@@ -204,7 +249,7 @@ __global__ void __launch_bounds__(256) k_attn_stats(AttnDesc d0, float* __restri
   if (lane == 0) {
     const size_t ix = (size_t)t * d.M * d.nh + mh;
     w.AM[ix] = mx;
-    w.AL[ix] = (d.lo[m] > d.pos[m]) ? 0.0f : l8;
+    w.AL[ix] = (dlo(d, m) > dpos(d, m)) ? 0.0f : l8;
   }
 }
 
@@ -237,7 +282,7 @@ __global__ void __launch_bounds__(64) k_attn_accum(const uint16_t* __restrict__ 
   const bool live = g < ng;
   const int mh = mhb + (live ? g : 0), m = mh / d.nh;
   const int c0 = chunk_lo(d, t), c1 = chunk_lo(d, t + 1);
-  const int a = max(c0, d.lo[m]), b = min(c1 - 1, d.pos[m]);
+  const int a = max(c0, dlo(d, m)), b = min(c1 - 1, dpos(d, m));
   auto stage = [&](int buf, int pb) {
     const int nk = min(kAccKeys, c1 - pb);
     for (int e = threadIdx.x; e < nk * 2; e += 64)  // V: 2 x 16 B per key
@@ -311,9 +356,18 @@ __global__ void __launch_bounds__(512) k_attn_merge(AttnDesc d0, const float* __
   __syncthreads();
   if (i >= d.hd) return;
   float acc = 0.f;
-  for (int t = 0; t < d.T; ++t) {
-    if (!(al[t] > 0)) continue;
-    acc = fmaf(w.AO[((size_t)t * nmh + mh) * d.hd + i], sc[t], acc);
+  if (d.T <= 16) {  // every chunk's O loaded at once, then the chain in chunk order
+    float aov[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) aov[t] = t < d.T ? w.AO[((size_t)t * nmh + mh) * d.hd + i] : 0.f;
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+      if (t < d.T && al[t] > 0) acc = fmaf(aov[t], sc[t], acc);
+  } else {
+    for (int t = 0; t < d.T; ++t) {
+      if (!(al[t] > 0)) continue;
+      acc = fmaf(w.AO[((size_t)t * nmh + mh) * d.hd + i], sc[t], acc);
+    }
   }
   const float v = r16(__fmul_rn(acc, inv_l));
   out[(size_t)mh * d.hd + i] = v;
@@ -333,116 +387,127 @@ __global__ void __launch_bounds__(512) k_attn_merge(AttnDesc d0, const float* __
 
 // ---- chunk kernel for long chunks (global layers): statistics, accumulation and merge in one
 // launch after k_attn_scores.  Block = (chunk t, 32-dim slice, group of 8 (row, head) pairs),
-// 256 threads.  Warp p loads pair p's allowed scores of the chunk into shared memory, takes their
-// max and turns them into exp8 weights in place (as k_attn_stats).  Then, concurrently, lanes of
-// warp 0 run each pair's weight sum in key order, and warps 4-7 (thread = pair x dim pair) run
-// the O chains over the chunk's keys in order with V staged by double-buffered cp.async (as
-// k_attn_accum).  The last of the T blocks of a (slice, group) merges the chunks for its 32 dims
-// (as k_attn_merge) and quantises them when asked.  Same values as the four-kernel path.
-constexpr int kChunkMaxKeys = 1536, kChunkTile = 128;
+// 256 threads.  The chunk's V slice (64 bytes of each key) is requested by cp.async before the
+// wait on the previous kernel (the cache rows were written two launches earlier, by the KV write,
+// which had completed before the scores kernel started).  Warp p loads pair p's allowed scores of
+// the chunk into shared memory, takes their max and turns them into exp8 weights in place (as
+// k_attn_stats).  Then, concurrently, warps 0-3 run the weight sums of pairs w and w+4 in key
+// order (32 weights at a time handed to every lane by shuffles), and warps 4-7 (thread = pair x
+// dim pair) run the O chains over the chunk's keys in order, with the weights and V of the next 8
+// keys loaded while the current 8 are accumulated (as k_attn_accum).  The last of the T blocks of
+// a (slice, group) merges the chunks for its 32 dims (as k_attn_merge) and quantises them when
+// asked.  Same values as the four-kernel path.
+constexpr int kChunkMaxKeys = 1536;
+constexpr int kChunkWs = kChunkMaxKeys + 4;  // a multiple of 4 whose rows start in distinct banks
 __host__ __device__ inline size_t attn_chunk_smem() {
-  return sizeof(float) * 8 * (kChunkMaxKeys + 1) + 2 * (size_t)kChunkTile * 64;
+  return sizeof(float) * 8 * kChunkWs + (size_t)kChunkMaxKeys * 64;
 }
 __device__ __forceinline__ void cp_async16_g(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
-__device__ __forceinline__ void named_sync_128() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 __global__ void __launch_bounds__(256) k_attn_chunk(const uint16_t* __restrict__ Vc, AttnDesc d0, float* __restrict__ ws,
                                                     int* __restrict__ counters, float* __restrict__ out) {
-  pdl_wait();
-  pdl_trigger();
   extern __shared__ __align__(16) uint8_t csm[];
-  float* wsm = reinterpret_cast<float*>(csm);                                     // [8][kChunkMaxKeys + 1]
-  uint32_t* vt = reinterpret_cast<uint32_t*>(csm + sizeof(float) * 8 * (kChunkMaxKeys + 1));  // [2][tile][16]
+  float* wsm = reinterpret_cast<float*>(csm);                                  // [8][kChunkWs]
+  uint32_t* vsl = reinterpret_cast<uint32_t*>(csm + sizeof(float) * 8 * kChunkWs);  // [key - cl][16]
   __shared__ float smx[8], sl8[8];
   __shared__ int s_last;
-  const AttnDesc d = resolve(d0);
-  const AttnWs w = attn_ws(ws, d);
+  const AttnDesc d = resolve(d0);  // positions come from the host-written control word
   const int t = blockIdx.x, y = blockIdx.y, grp = blockIdx.z, i0 = y * 32;
   const int nmh = d.M * d.nh, len = d.kmax - d.kmin + 1, G8 = (nmh + 7) / 8;
   const int mhb = grp * 8, ng = min(8, nmh - mhb);
   const int cl = chunk_lo(d, t), ch = chunk_lo(d, t + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int WS = kChunkMaxKeys + 1;
+  for (int e = threadIdx.x; e < (ch - cl) * 4; e += 256)  // 4 x 16 B per key (32 bf16 dims)
+    cp_async16_g(vsl + (size_t)e * 4, Vc + (size_t)(cl + (e >> 2)) * d.hd + i0 + (e & 3) * 8);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  pdl_wait();  // the scores come from the previous kernel
+  pdl_trigger();
+  const AttnWs w = attn_ws(ws, d);
+  constexpr int WS = kChunkWs;  // weights of pair p at wsm[p * WS + (k - cl)]
   // scores of pair `warp` -> shared memory, max, weights
   if (warp < ng) {
     const int mh = mhb + warp, m = mh / d.nh;
-    const int a = max(cl, d.lo[m]), b = min(ch - 1, d.pos[m]);
+    const int a = max(cl, dlo(d, m)), b = min(ch - 1, dpos(d, m));
     const float* srow = w.S + (size_t)mh * len - d.kmin;
     float* wp = wsm + warp * WS - cl;
     float mx = -1e30f;
-    for (int k = a + lane; k <= b; k += 32) {
-      const float v = srow[k];
-      wp[k] = v;
-      mx = fmaxf(mx, v);
+    constexpr int kPer = kChunkMaxKeys / 32;
+    float v[kPer];  // every score load in flight at once
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int k = a + lane + 32 * j;
+      v[j] = k <= b ? __ldcg(srow + k) : -1e30f;
     }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) mx = fmaxf(mx, v[j]);
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
-    for (int k = a + lane; k <= b; k += 32) wp[k] = exp8(__fsub_rn(wp[k], mx));
+    const int jn = b >= a ? (b - a + 32) / 32 : 0;  // slots holding keys (warp-uniform)
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      if (j >= jn) break;
+      const int k = a + lane + 32 * j;
+      if (k <= b) wp[k] = exp8(__fsub_rn(v[j], mx));
+    }
     if (lane == 0) smx[warp] = mx;
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   if (warp == 0) {
-    // in-order weight sums, one lane per pair
+    // in-order weight sums, one lane per pair, four weights per 16-byte load
     if (lane < ng) {
       const int mh = mhb + lane, m = mh / d.nh;
-      const int a = max(cl, d.lo[m]), b = min(ch - 1, d.pos[m]);
-      const float* wp = wsm + lane * WS - cl;
+      const float* wr = wsm + lane * WS;
+      int k = max(cl, dlo(d, m)) - cl;
+      const int ke = min(ch - 1, dpos(d, m)) - cl;  // inclusive
       float l8 = 0.f;
-      int k = a;
-      if (k + 8 <= b + 1) {  // key order; the next 8 weights load while these 8 are added
-        float cur[8], nxt[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) cur[u] = wp[k + u];
-        for (; k + 16 <= b + 1; k += 8) {
-#pragma unroll
-          for (int u = 0; u < 8; ++u) nxt[u] = wp[k + 8 + u];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) l8 = __fadd_rn(l8, cur[u]);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
+      for (; k <= ke && (k & 3); ++k) l8 = __fadd_rn(l8, wr[k]);
+      if (k + 3 <= ke) {
+        float4 cur = *reinterpret_cast<const float4*>(wr + k);
+        for (; k + 7 <= ke; k += 4) {
+          const float4 nxt = *reinterpret_cast<const float4*>(wr + k + 4);
+          l8 = __fadd_rn(l8, cur.x);
+          l8 = __fadd_rn(l8, cur.y);
+          l8 = __fadd_rn(l8, cur.z);
+          l8 = __fadd_rn(l8, cur.w);
+          cur = nxt;
         }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) l8 = __fadd_rn(l8, cur[u]);
-        k += 8;
+        l8 = __fadd_rn(l8, cur.x);
+        l8 = __fadd_rn(l8, cur.y);
+        l8 = __fadd_rn(l8, cur.z);
+        l8 = __fadd_rn(l8, cur.w);
+        k += 4;
       }
-      for (; k <= b; ++k) l8 = __fadd_rn(l8, wp[k]);
-      sl8[lane] = (d.lo[m] > d.pos[m]) ? 0.0f : l8;
+      for (; k <= ke; ++k) l8 = __fadd_rn(l8, wr[k]);
+      sl8[lane] = (dlo(d, m) > dpos(d, m)) ? 0.0f : l8;
     }
   } else if (warp >= 4) {
-    // O chains: thread = (pair p, dim pair dp) over this block's 32 dims
+    // O chains: thread = (pair p, dim pair dp) over this block's 32 dims; 8 keys per step, their
+    // weights in two 16-byte loads
     const int at = threadIdx.x - 128, p = at >> 4, dp = at & 15;
     const bool live = p < ng;
     const int mh = mhb + (live ? p : 0), m = mh / d.nh;
-    const int a = max(cl, d.lo[m]), b = min(ch - 1, d.pos[m]);
-    const float* wp = wsm + (live ? p : 0) * WS - cl;
+    int k = max(cl, dlo(d, m)) - cl;
+    const int ke = live ? min(ch - 1, dpos(d, m)) - cl : k - 1;  // inclusive
+    const float* wr = wsm + (live ? p : 0) * WS;
+    const uint32_t* vr = vsl + dp;
     float2 o = make_float2(0.f, 0.f);
-    auto stage = [&](int buf, int pb) {
-      const int nk = min(kChunkTile, ch - pb);
-      for (int e = at; e < nk * 4; e += 128)  // 4 x 16 B per key (32 bf16 dims)
-        cp_async16_g(vt + ((size_t)buf * kChunkTile + (e >> 2)) * 16 + (e & 3) * 4,
-                     Vc + (size_t)(pb + (e >> 2)) * d.hd + i0 + (e & 3) * 8);
+    auto step = [&](float wt, uint32_t vv) {
+      o = __ffma2_rn(make_float2(wt, wt), make_float2(__uint_as_float(vv << 16), __uint_as_float(vv & 0xFFFF0000u)), o);
     };
-    if (cl < ch) stage(0, cl);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    for (int pb = cl, it = 0; pb < ch; pb += kChunkTile, ++it) {
-      if (pb + kChunkTile < ch) stage((it + 1) & 1, pb + kChunkTile);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-      named_sync_128();
-      if (live) {
-        const int ka = max(a, pb), kb = min(b, pb + kChunkTile - 1);
-        const uint32_t* vb = vt + (size_t)(it & 1) * kChunkTile * 16 + dp - (size_t)pb * 16;
-#pragma unroll 4
-        for (int k = ka; k <= kb; ++k) {
-          const uint32_t vv = vb[(size_t)k * 16];
-          const float wt = wp[k];
-          o = __ffma2_rn(make_float2(wt, wt), make_float2(__uint_as_float(vv << 16), __uint_as_float(vv & 0xFFFF0000u)), o);
-        }
-      }
-      named_sync_128();
+    for (; k <= ke && (k & 3); ++k) step(wr[k], vr[(size_t)k * 16]);
+#pragma unroll 2
+    for (; k + 7 <= ke; k += 8) {
+      const float4 w0 = *reinterpret_cast<const float4*>(wr + k), w1 = *reinterpret_cast<const float4*>(wr + k + 4);
+      uint32_t vv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) vv[u] = vr[(size_t)(k + u) * 16];
+      step(w0.x, vv[0]); step(w0.y, vv[1]); step(w0.z, vv[2]); step(w0.w, vv[3]);
+      step(w1.x, vv[4]); step(w1.y, vv[5]); step(w1.z, vv[6]); step(w1.w, vv[7]);
     }
+    for (; k <= ke; ++k) step(wr[k], vr[(size_t)k * 16]);
     if (live) {
       float* ao = w.AO + ((size_t)t * nmh + mh) * d.hd + i0 + 2 * dp;
       ao[0] = o.x;
@@ -464,20 +529,28 @@ __global__ void __launch_bounds__(256) k_attn_chunk(const uint16_t* __restrict__
   if (warp < ng) {
     // merge (k_attn_merge) for pair `warp`, dim i0 + lane
     const int mh = mhb + warp;
-    float M0 = -1e30f;
-    for (int tt = 0; tt < d.T; ++tt) {
+    constexpr int kT = 16;  // every load first (T <= 16), then the factors, then l and O in chunk order
+    float alv[kT], amv[kT], aov[kT];
+#pragma unroll
+    for (int tt = 0; tt < kT; ++tt) {
       const size_t jx = (size_t)tt * nmh + mh;
-      if (__ldcg(&w.AL[jx]) > 0) M0 = fmaxf(M0, __ldcg(&w.AM[jx]));
+      const bool in = tt < d.T;
+      alv[tt] = in ? __ldcg(&w.AL[jx]) : 0.f;
+      amv[tt] = in ? __ldcg(&w.AM[jx]) : 0.f;
+      aov[tt] = in ? __ldcg(&w.AO[jx * d.hd + i0 + lane]) : 0.f;
     }
+    float M0 = -1e30f;
+#pragma unroll
+    for (int tt = 0; tt < kT; ++tt)
+      if (alv[tt] > 0) M0 = fmaxf(M0, amv[tt]);
     double l = 0;
     float acc = 0.f;
-    for (int tt = 0; tt < d.T; ++tt) {
-      const size_t jx = (size_t)tt * nmh + mh;
-      const float al = __ldcg(&w.AL[jx]);
-      if (!(al > 0)) continue;
-      const float sc = exp_cr(__fsub_rn(__ldcg(&w.AM[jx]), M0));
-      l = fma((double)al, (double)sc, l);
-      acc = fmaf(__ldcg(&w.AO[jx * d.hd + i0 + lane]), sc, acc);
+#pragma unroll
+    for (int tt = 0; tt < kT; ++tt) {
+      if (!(alv[tt] > 0)) continue;
+      const float sc = exp_cr(__fsub_rn(amv[tt], M0));
+      l = fma((double)alv[tt], (double)sc, l);
+      acc = fmaf(aov[tt], sc, acc);
     }
     const float inv = (float)(1.0 / l);
     const float v = r16(__fmul_rn(acc, inv));
@@ -526,7 +599,7 @@ __global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__
   const AttnWs w = attn_ws(ws, d);
   const int t = blockIdx.x, mh = blockIdx.y, nmh = d.M * d.nh;
   const int m = mh / d.nh, h = mh % d.nh;
-  const int c0 = max(chunk_lo(d, t), d.lo[m]), c1 = min(chunk_lo(d, t + 1), d.pos[m] + 1);
+  const int c0 = max(chunk_lo(d, t), dlo(d, m)), c1 = min(chunk_lo(d, t + 1), dpos(d, m) + 1);
   const int n = max(0, c1 - c0);
   const int rs = d.hd * 2;  // shared-memory row stride (bytes)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm_raw);
@@ -610,7 +683,7 @@ __global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__
   __syncthreads();
   if (threadIdx.x == 0) {
     w.AM[ix] = mx;
-    w.AL[ix] = (d.lo[m] > d.pos[m]) ? 0.0f : s_l8;
+    w.AL[ix] = (dlo(d, m) > dpos(d, m)) ? 0.0f : s_l8;
   }
   __threadfence();  // every thread's partial results are visible device-wide before the count
   __syncthreads();
@@ -708,11 +781,14 @@ static int attn_counter_count(int M, int nh, int hd) {
 static int launch_attn(const uint16_t* Kc, const uint16_t* Vc, const float* q, const AttnDesc& d, float* w, float* out,
                        cudaStream_t st, int max_len = 0, int* zeroed_counters = nullptr, bool four = false) {
   const int len = max_len > 0 ? max_len : d.kmax - d.kmin + 1, nmh = d.M * d.nh;
-  const size_t ssm = 128 + (size_t)kScoreKeys * d.hd * 2;
+  const size_t ssm = attn_scores_smem(d.hd);
   int rc = G4_OK;
   const dim3 sgrid((len + kScoreKeys - 1) / kScoreKeys), sblk(nmh * 16);
   if (d.hd == 256) rc = launch("k_attn_scores", k_attn_scores<16>, sgrid, sblk, ssm, st, Kc, q, d, w);
-  else if (d.hd == 512) rc = launch("k_attn_scores", k_attn_scores<32>, sgrid, sblk, ssm, st, Kc, q, d, w);
+  else if (d.hd == 512) {
+    cudaFuncSetAttribute(k_attn_scores<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm);
+    rc = launch("k_attn_scores", k_attn_scores<32>, sgrid, sblk, ssm, st, Kc, q, d, w);
+  }
   else if (d.hd == 128) rc = launch("k_attn_scores", k_attn_scores<8>, sgrid, sblk, ssm, st, Kc, q, d, w);
   else return set_error(G4_ERR_UNSUPPORTED, "attention: hd=%d (supported: 128, 256, 512)", d.hd);
   if (rc) return rc;
@@ -720,7 +796,7 @@ static int launch_attn(const uint16_t* Kc, const uint16_t* Vc, const float* q, c
     const char* e = getenv("G4_ATTN_CHUNK");
     return e ? e[0] == '1' : true;
   }();
-  if (chunk_on && !four && (len + d.T - 1) / d.T + 1 <= kChunkMaxKeys && d.hd % 32 == 0) {
+  if (chunk_on && !four && d.T <= 16 && (len + d.T - 1) / d.T + 1 <= kChunkMaxKeys && d.hd % 32 == 0) {
     int* counters = zeroed_counters;
     if (counters == nullptr) {
       counters = reinterpret_cast<int*>(reinterpret_cast<char*>(w) + attn_counter_offset(d.M, d.nh, d.hd, len, d.T));

@@ -84,7 +84,7 @@ struct g4_engine {
   float *fnorm = nullptr, *dnorm = nullptr;
   uint16_t* E = nullptr;
   // head
-  uint8_t *hdata = nullptr, *sW4 = nullptr;
+  uint8_t *hdata = nullptr, *hunp = nullptr, *sW4 = nullptr;
   uint16_t* sS4 = nullptr;
   float* scoef = nullptr;
   long long* hexc_ptr = nullptr;
@@ -229,6 +229,10 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
     if (!rc && ealloc_t(e, &e->hexc_col, (size_t)std::max(1LL, total))) rc = G4_ERR_CUDA;
     if (!rc && ealloc_t(e, &e->hexc_delta, (size_t)std::max(1LL, total))) rc = G4_ERR_CUDA;
     if (!rc) rc = g4_bf16p_pack(e->E, d.V, H, e->cb8, e->hdata, e->hexc_ptr, e->hexc_col, e->hexc_delta, e->st);
+    if (!rc && H % 64 == 0) {  // the unpacked copy that the head GEMV reads
+      if (ealloc_t(e, &e->hunp, (size_t)d.V * (H / 32) * 64)) rc = G4_ERR_CUDA;
+      if (!rc) rc = g4_bf16p_unpack(e->hdata, e->cb8, d.V, H, e->hunp, e->st);
+    }
     if (!rc && ealloc_t(e, &e->sW4, (size_t)d.V * H / 2)) rc = G4_ERR_CUDA;
     if (!rc && ealloc_t(e, &e->sS4, (size_t)d.V * H / 32)) rc = G4_ERR_CUDA;
     if (!rc && ealloc_t(e, &e->scoef, (size_t)d.V)) rc = G4_ERR_CUDA;
@@ -455,13 +459,17 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
   for (int r0 = hf; r0 < M; r0 += 4) {
     const int mh = std::min(4, M - r0);
     if (e->cfg.head_screen) {
-      RCK(g4_head_screen(e->sW4, e->sS4, e->scoef, e->hdata, e->cb8, e->hexc_ptr, e->hexc_col, e->hexc_delta, d.V, H,
-                         e->hbuf + (size_t)r0 * H, mh, e->cfg.screen_lim, e->G + r0, e->head_ns, e->head_ws,
-                         e->head_ws_bytes, e->st));
+      RCK(head_screen_impl(e->sW4, e->sS4, e->scoef, e->hdata, e->hunp, e->cb8, e->hexc_ptr, e->hexc_col, e->hexc_delta,
+                           d.V, H, e->hbuf + (size_t)r0 * H, mh, e->cfg.screen_lim, e->G + r0, e->head_ns, e->head_ws,
+                           e->head_ws_bytes, e->st));
     } else {
       float* logits = static_cast<float*>(e->head_ws);
-      RCK(g4_bf16p_gemm(e->hdata, e->cb8, e->hexc_ptr, e->hexc_col, e->hexc_delta, d.V, H, e->hbuf + (size_t)r0 * H, mh,
-                        logits, d.V, e->st));
+      if (e->hunp)
+        RCK(g4_bf16p_unpacked_gemm(e->hunp, e->hexc_ptr, e->hexc_col, e->hexc_delta, d.V, H, e->hbuf + (size_t)r0 * H, mh,
+                                   logits, d.V, e->st));
+      else
+        RCK(g4_bf16p_gemm(e->hdata, e->cb8, e->hexc_ptr, e->hexc_col, e->hexc_delta, d.V, H, e->hbuf + (size_t)r0 * H, mh,
+                          logits, d.V, e->st));
       RCK(g4_head_argmax(logits, mh, d.V, d.V, e->G + r0, static_cast<char*>(e->head_ws) + sizeof(float) * (size_t)4 * d.V,
                          64, e->st));
     }

@@ -155,6 +155,7 @@ __global__ void k_bf16p_fill(const uint16_t* __restrict__ E, int K, Codebook cb,
 // ------------------------------------------------------------------------- exact head dot
 struct HeadPacked {
   const uint8_t* data;
+  const uint8_t* unp;  // the same head in the unpacked layout (g4_bf16p_unpack), or NULL
   const long long* exc_ptr;
   const uint16_t* exc_col;
   const float* exc_delta;
@@ -933,7 +934,7 @@ extern "C" int g4_bf16p_pack(const uint16_t* E, int N, int K, const uint8_t* cb8
 static HeadPacked make_head(const uint8_t* data, const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col,
                             const float* exc_delta, int N, int K) {
   HeadPacked P;
-  P.data = data; P.exc_ptr = exc_ptr; P.exc_col = exc_col; P.exc_delta = exc_delta; P.N = N; P.K = K;
+  P.data = data; P.unp = nullptr; P.exc_ptr = exc_ptr; P.exc_col = exc_col; P.exc_delta = exc_delta; P.N = N; P.K = K;
   std::memcpy(&P.cb_lo, cb8, 4);
   std::memcpy(&P.cb_hi, cb8 + 4, 4);
   return P;
@@ -959,6 +960,188 @@ static bool head_tmap(const HeadPacked& P, CUtensorMap* out) {
   return true;
 }
 
+// ---- unpacked layout of the packed head (64 bytes per group): the 32 weights as bf16p::pack
+// represents them (codebook exponent, before the exception patches) stored as bf16, in the order
+// that the two threads of a row consume them: bytes 32h..32h+31 hold half h's 16 weights, octets
+// in chain order 0, 2, 1, 3, elements 8o+4h..8o+4h+3 within an octet.  The GEMV then turns each
+// 32-bit word into two floats with one shift and one mask, instead of decoding exponent codes.
+__device__ __forceinline__ uint32_t bf16p_bits(const uint32_t* w, int e, uint32_t cb_lo, uint32_t cb_hi) {
+  const uint32_t idx = ((w[8] >> e) & 1u) | (((w[9] >> e) & 1u) << 1) | (((w[10] >> e) & 1u) << 2);
+  const uint32_t ex = __byte_perm(cb_lo, cb_hi, idx) & 0xFFu;
+  const uint32_t sm = (w[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+  return ((sm & 0x80u) << 8) | (ex << 7) | (sm & 0x7Fu);
+}
+__global__ void k_bf16u_pack(const uint8_t* __restrict__ data, long long ngroups, uint32_t cb_lo, uint32_t cb_hi,
+                             uint8_t* __restrict__ out) {
+  const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= ngroups) return;
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(data + g * 44);  // 4-byte aligned (44 = 4 * 11)
+  uint32_t w[11];
+#pragma unroll
+  for (int i = 0; i < 11; ++i) w[i] = src[i];
+  uint32_t* dst = reinterpret_cast<uint32_t*>(out + g * 64);
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int oi = 0; oi < 4; ++oi) {
+      const int o8 = (oi == 1) ? 2 : (oi == 2 ? 1 : oi);
+#pragma unroll
+      for (int pr = 0; pr < 2; ++pr) {
+        const int e = 8 * o8 + 4 * h + 2 * pr;
+        dst[8 * h + 2 * oi + pr] = bf16p_bits(w, e, cb_lo, cb_hi) | (bf16p_bits(w, e + 1, cb_lo, cb_hi) << 16);
+      }
+    }
+}
+
+// Exact-head GEMV over the unpacked layout, fed by the TMA, two threads per row (as
+// k_bf16p_rows_tma, same values): per pipeline item one tensor-map load brings 2 groups (128
+// bytes) of 128 rows under the 128-byte swizzle (16-byte chunk u of row r lands at chunk
+// u ^ (r & 7)), so the half-row loads of a 16-byte phase hit distinct bank quads.
+constexpr int kBuRows = 128, kBuThreads = 256, kBuNS = 4, kBuBox = 128;
+__host__ __device__ inline size_t head_unp_smem(int M, int K) {
+  return 1024 + 128 + (size_t)kBuNS * kBuRows * kBuBox + (size_t)K * ((M + 1) / 2) * 8;
+}
+
+template <int M>
+__global__ void __launch_bounds__(kBuThreads, 2) k_bf16u_rows_tma(const __grid_constant__ CUtensorMap tmap, HeadPacked P,
+                                                                  const float* __restrict__ X, float* __restrict__ Y, int ldy,
+                                                                  const int* __restrict__ gate) {
+  constexpr int NP = (M + 1) / 2;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[kBuNS];
+  uint8_t* stages = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // 1024-byte aligned
+  float2* xs = reinterpret_cast<float2*>(stages + (size_t)kBuNS * kBuRows * kBuBox);  // [K][NP]
+  pdl_wait();
+  pdl_trigger();
+  if (gate != nullptr && *gate == 0) return;
+  const int K = P.K, G = K >> 5, nch = G / 2;
+  const int nblk = (P.N + kBuRows - 1) / kBuRows;
+  const int myblk = nblk > (int)blockIdx.x ? (nblk - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int nitems = myblk * nch;
+  const int t = threadIdx.x, rl = t >> 1, half = t & 1;
+  if (t == 0) {
+    for (int b = 0; b < kBuNS; ++b) mbar_init(&bars[b], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int i, int st) {  // thread 0
+    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
+    mbar_expect_tx(&bars[st], (uint32_t)(kBuRows * kBuBox));
+    tma_load_2d(stages + (size_t)st * kBuRows * kBuBox, &tmap, c * kBuBox, blk * kBuRows, &bars[st]);
+  };
+  if (t == 0)
+    for (int b = 0; b < kBuNS && b < nitems; ++b) issue(b, b);
+  for (int i = t; i < K; i += kBuThreads) {
+    float v[2 * NP];
+#pragma unroll
+    for (int m = 0; m < 2 * NP; ++m) v[m] = m < M ? X[(size_t)m * K + i] : 0.f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) xs[(size_t)i * NP + p] = make_float2(v[2 * p], v[2 * p + 1]);
+  }
+  __syncthreads();
+  const int hsh = 4 * half;
+  float2 acc[4][NP];
+  for (int i = 0; i < nitems; ++i) {
+    const int st = i % kBuNS;
+    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
+    const int n = blk * kBuRows + rl;
+    if (!cta_wait(&bars[st], (uint32_t)(i / kBuNS) & 1u)) return;
+    if (c == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int p = 0; p < NP; ++p) acc[j][p] = make_float2(0.f, 0.f);
+    }
+    const uint8_t* rowp = stages + ((size_t)st * kBuRows + rl) * kBuBox;
+    uint32_t wv[16];  // this half's words of the item's 2 groups
+#pragma unroll
+    for (int gg = 0; gg < 2; ++gg)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int chunk = gg * 4 + half * 2 + u;
+        const uint4 t4 = *reinterpret_cast<const uint4*>(rowp + ((chunk ^ (rl & 7)) << 4));
+        wv[8 * gg + 4 * u] = t4.x; wv[8 * gg + 4 * u + 1] = t4.y; wv[8 * gg + 4 * u + 2] = t4.z; wv[8 * gg + 4 * u + 3] = t4.w;
+      }
+    __syncthreads();  // every row has its words in registers: the stage can be refilled
+    if (t == 0 && i + kBuNS < nitems) {
+      fence_proxy_async_smem();
+      issue(i + kBuNS, st);
+    }
+#pragma unroll
+    for (int gg = 0; gg < 2; ++gg) {
+      const int g = c * 2 + gg;
+      const float2* xg = xs + ((size_t)g * 32 + hsh) * NP;
+#pragma unroll
+      for (int oi = 0; oi < 4; ++oi) {
+        const int o8 = (oi == 1) ? 2 : (oi == 2 ? 1 : oi);  // element octets in chain order 0, 2, 1, 3
+        const uint32_t w0 = wv[8 * gg + 2 * oi], w1 = wv[8 * gg + 2 * oi + 1];
+        const float wk[4] = {__uint_as_float(w0 << 16), __uint_as_float(w0 & 0xFFFF0000u), __uint_as_float(w1 << 16),
+                             __uint_as_float(w1 & 0xFFFF0000u)};
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int p = 0; p < NP; ++p)
+            acc[k][p] = __ffma2_rn(make_float2(wk[k], wk[k]), xg[(8 * o8 + k) * NP + p], acc[k][p]);
+      }
+    }
+    if (c == nch - 1) {
+      // lanes 4..7 come from the other half; fadd is commutative, so both halves hold
+      // ((v0 + v4) + (v1 + v5)) + ((v2 + v6) + (v3 + v7)) bit for bit
+      float y[2 * NP];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        float2 w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          w[k].x = __shfl_xor_sync(0xffffffffu, acc[k][p].x, 1);
+          w[k].y = __shfl_xor_sync(0xffffffffu, acc[k][p].y, 1);
+        }
+        y[2 * p] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].x, w[0].x), __fadd_rn(acc[1][p].x, w[1].x)),
+                             __fadd_rn(__fadd_rn(acc[2][p].x, w[2].x), __fadd_rn(acc[3][p].x, w[3].x)));
+        y[2 * p + 1] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].y, w[0].y), __fadd_rn(acc[1][p].y, w[1].y)),
+                                 __fadd_rn(__fadd_rn(acc[2][p].y, w[2].y), __fadd_rn(acc[3][p].y, w[3].y)));
+      }
+      if (n < P.N) {
+        float yo[NP];  // this half's activation rows 2p + half
+#pragma unroll
+        for (int p = 0; p < NP; ++p) yo[p] = half ? y[2 * p + 1] : y[2 * p];
+        for (long long e = P.exc_ptr[n]; e < P.exc_ptr[n + 1]; ++e) {  // CSR order, unfused (bf16_exp3_head.h:103)
+          const float dl = P.exc_delta[e];
+          const int col = P.exc_col[e];
+#pragma unroll
+          for (int p = 0; p < NP; ++p) {
+            const float2 xv = xs[(size_t)col * NP + p];
+            yo[p] = __fadd_rn(yo[p], __fmul_rn(dl, half ? xv.y : xv.x));
+          }
+        }
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+          if (2 * p + half < M) Y[(size_t)(2 * p + half) * ldy + n] = yo[p];
+      }
+    }
+  }
+}
+
+// The unpacked head as a 2D byte tensor [N][G*64] with boxes of [kBuRows][kBuBox] under the
+// 128-byte swizzle; cached per (address, N, K).
+static bool head_unp_tmap(const HeadPacked& P, CUtensorMap* out) {
+  static std::mutex mu;
+  struct Entry { const void* ptr; int N, K; CUtensorMap map; };
+  static Entry cache[8];
+  static int used = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].ptr == P.unp && cache[i].N == P.N && cache[i].K == P.K) { *out = cache[i].map; return true; }
+  const uint64_t rowb = (uint64_t)(P.K / 32) * 64;
+  CUtensorMap m;
+  if (!encode_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, P.unp, rowb, (uint64_t)P.N, rowb, kBuBox, kBuRows,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+    return false;
+  if (used < 8) cache[used++] = Entry{P.unp, P.N, P.K, m};
+  *out = m;
+  return true;
+}
+
 static int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -973,6 +1156,19 @@ template <int M>
 static int launch_head_gemv(const HeadPacked& P, const float* X, float* Y, int ldy, const int* gate, cudaStream_t st) {
   const char* hv = getenv("G4_HEAD_GEMV");  // "direct" / "octet" select other variants (experiments)
   CUtensorMap tm;
+  const size_t usmem = head_unp_smem(M, P.K);
+  if (P.unp != nullptr && P.K % 64 == 0 && aligned(P.unp, 16) && usmem <= 113 * 1024 && head_unp_tmap(P, &tm)) {
+    cudaFuncSetAttribute(k_bf16u_rows_tma<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)usmem);
+    cudaFuncSetAttribute(k_bf16u_rows_tma<M>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);  // 2 CTAs per SM
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_bf16u_rows_tma<M>, kBuThreads, usmem) != cudaSuccess || occ < 1)
+      occ = 1;
+    const int nblk = (P.N + kBuRows - 1) / kBuRows;
+    return launch("k_bf16u_rows_tma", k_bf16u_rows_tma<M>, dim3(std::min(nblk, num_sms() * occ)), dim3(kBuThreads), usmem,
+                  st, tm, P, X, Y, ldy, gate);
+  }
+  if (P.data == nullptr)
+    return set_error(G4_ERR_UNSUPPORTED, "bf16p unpacked GEMV: K=%d (a multiple of 64 and a 16-byte aligned head needed)", P.K);
   const size_t tsmem = head_tma_smem(M, P.K);
   if (!hv && P.K % 128 == 0 && (P.K / 32) * 44 % 16 == 0 && aligned(P.data, 16) && tsmem <= 227 * 1024 && head_tmap(P, &tm)) {
     cudaFuncSetAttribute(k_bf16p_rows_tma<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem);
@@ -1020,6 +1216,30 @@ extern "C" int g4_bf16p_gemm(const uint8_t* data, const uint8_t* cb8, const long
   return head_gemv(make_head(data, cb8, exc_ptr, exc_col, exc_delta, N, K), X, M, Y, ldy, nullptr, as_stream(stream));
 }
 
+extern "C" int g4_bf16p_unpack(const uint8_t* data, const uint8_t* cb8, int N, int K, uint8_t* unp, void* stream) {
+  G4_REQUIRE(data && cb8 && unp, "g4_bf16p_unpack: null pointer");
+  G4_REQUIRE(N > 0 && K > 0 && K % 32 == 0, "g4_bf16p_unpack: bad shape N=%d K=%d", N, K);
+  G4_REQUIRE(aligned(data, 4) && aligned(unp, 16), "g4_bf16p_unpack: data 4-byte, unp 16-byte aligned");
+  const long long ng = (long long)N * (K / 32);
+  uint32_t cb_lo, cb_hi;
+  std::memcpy(&cb_lo, cb8, 4);
+  std::memcpy(&cb_hi, cb8 + 4, 4);
+  k_bf16u_pack<<<(unsigned)((ng + 255) / 256), 256, 0, as_stream(stream)>>>(data, ng, cb_lo, cb_hi, unp);
+  return check_launch("k_bf16u_pack");
+}
+
+extern "C" int g4_bf16p_unpacked_gemm(const uint8_t* unp, const long long* exc_ptr, const uint16_t* exc_col,
+                                      const float* exc_delta, int N, int K, const float* X, int M, float* Y, int ldy,
+                                      void* stream) {
+  G4_REQUIRE(unp && exc_ptr && X && Y, "g4_bf16p_unpacked_gemm: null pointer");
+  G4_REQUIRE(M >= 1 && M <= 4 && N > 0 && K > 0 && K % 64 == 0 && ldy >= N,
+             "g4_bf16p_unpacked_gemm: bad shape M=%d N=%d K=%d", M, N, K);
+  const uint8_t zero_cb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  HeadPacked P = make_head(nullptr, zero_cb, exc_ptr, exc_col, exc_delta, N, K);
+  P.unp = unp;
+  return head_gemv(P, X, M, Y, ldy, nullptr, as_stream(stream));
+}
+
 static int pick(const float* Y, int M, int N, int ldy, int* slots, int* out, const int* gate, cudaStream_t st) {
   if (int rc_ = launch("k_pick_init", k_pick_init, dim3(1), dim3(32), 0, st, slots, M)) return rc_;
   if (int rc_ = launch("k_pick_max", k_pick_max, dim3(dim3(296, M)), dim3(256), 0, st, Y, N, ldy, slots, gate)) return rc_;
@@ -1049,6 +1269,16 @@ extern "C" int g4_head_screen(const uint8_t* W4p, const uint16_t* S4, const floa
                               const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col,
                               const float* exc_delta, int N, int K, const float* H, int M, int lim, int* out_idx,
                               int* out_nsurv, void* ws, size_t ws_bytes, void* stream) {
+  return head_screen_impl(W4p, S4, coef, data, nullptr, cb8, exc_ptr, exc_col, exc_delta, N, K, H, M, lim, out_idx,
+                          out_nsurv, ws, ws_bytes, stream);
+}
+
+// The screen with the fallback head GEMV over the unpacked copy of the head when unp is set
+// (the rescoring of survivors reads the bf16p rows).
+int g4::head_screen_impl(const uint8_t* W4p, const uint16_t* S4, const float* coef, const uint8_t* data, const uint8_t* unp,
+                         const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col, const float* exc_delta,
+                         int N, int K, const float* H, int M, int lim, int* out_idx, int* out_nsurv, void* ws,
+                         size_t ws_bytes, void* stream) {
   G4_REQUIRE(W4p && S4 && coef && data && cb8 && exc_ptr && H && out_idx && out_nsurv && ws,
              "g4_head_screen: null pointer");
   G4_REQUIRE(M >= 1 && M <= 4 && N > 0 && K > 0 && K % 256 == 0 && lim > 0, "g4_head_screen: bad shape M=%d N=%d K=%d", M,
@@ -1060,7 +1290,8 @@ extern "C" int g4_head_screen(const uint8_t* W4p, const uint16_t* S4, const floa
   cudaStream_t st = as_stream(stream);
   ScreenWs w;
   screen_ws_layout(M, N, lim, &w, static_cast<char*>(ws));
-  const HeadPacked P = make_head(data, cb8, exc_ptr, exc_col, exc_delta, N, K);
+  HeadPacked P = make_head(data, cb8, exc_ptr, exc_col, exc_delta, N, K);
+  P.unp = unp;
   if (int rc_ = launch("k_screen_init", k_screen_init, dim3(M), dim3(32), 0, st, H, K, M, w)) return rc_;
   if (int rc = check_launch("k_screen_init")) return rc;
   if (int rc = g4_w4g32_gemm(W4p, S4, H, nullptr, M, N, K, w.s, N, stream)) return rc;

@@ -34,6 +34,8 @@ SIGNATURES = {
     "g4_bf16p_gemm": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _I, _P, _I, _P]),
     "g4_head_argmax": (_I, [_P, _I, _I, _I, _P, _P, _SZ, _P]),
     "g4_rmsnorm": (_I, [_P, _P, _I, _I, _P, _I, _P, _P, _P, _P]),
+    "g4_bf16p_unpack": (_I, [_P, _P, _I, _I, _P, _P]),
+    "g4_bf16p_unpacked_gemm": (_I, [_P, _P, _P, _P, _I, _I, _P, _I, _P, _I, _P]),
     "g4_screen_build": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "g4_head_screen_ws_bytes": (_SZ, [_I, _I, _I]),
     "g4_head_screen": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _SZ, _P]),
@@ -235,6 +237,25 @@ class PackedHead:
         Y = out if out is not None else torch.empty((M, self.N), dtype=torch.float32, device=X.device)
         check(lib().g4_bf16p_gemm(*self.args(), self.N, self.K, _ptr(X), M, _ptr(Y), Y.stride(0), _stream()),
               "g4_bf16p_gemm")
+        return Y
+
+    def unpacked(self):
+        """The unpacked copy of the head (g4_bf16p_unpack), made on first use."""
+        import torch
+        if getattr(self, "_unp", None) is None:
+            self._unp = torch.empty(self.N * (self.K // 32) * 64, dtype=torch.uint8, device=self.data.device)
+            check(lib().g4_bf16p_unpack(_ptr(self.data), self.cb, self.N, self.K, _ptr(self._unp), _stream()),
+                  "g4_bf16p_unpack")
+        return self._unp
+
+    def logits_unpacked(self, X, out=None):
+        """logits() through the unpacked copy (g4_bf16p_unpacked_gemm): the same values."""
+        import torch
+        M = X.shape[0]
+        Y = out if out is not None else torch.empty((M, self.N), dtype=torch.float32, device=X.device)
+        check(lib().g4_bf16p_unpacked_gemm(_ptr(self.unpacked()), _ptr(self.exc_ptr), _ptr(self.exc_col),
+                                           _ptr(self.exc_delta), self.N, self.K, _ptr(X), M, _ptr(Y), Y.stride(0),
+                                           _stream()), "g4_bf16p_unpacked_gemm")
         return Y
 
 

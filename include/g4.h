@@ -102,6 +102,15 @@ int g4_bf16p_pack(const uint16_t* E, int N, int K, const uint8_t* cb8, uint8_t* 
  * (bf16_exp3_head.h:84-107) / head_task (gemma4_engine.cpp:574-579).  X dev [M][K], M <= 4. */
 int g4_bf16p_gemm(const uint8_t* data, const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col,
                   const float* exc_delta, int N, int K, const float* X, int M, float* Y, int ldy, void* stream);
+/* B200 copy of a packed head in the unpacked layout: per group the 32 weights as bf16p::pack
+ * represents them (codebook exponent, before the exception patches) as bf16, 64 bytes per group,
+ * bytes 32h..32h+31 holding the weights of half h (octets in the order 0, 2, 1, 3, elements
+ * 8o+4h..8o+4h+3 of octet o).  data dev (g4_bf16p_pack), cb8 host -> unp dev [N*K/32*64], 16-byte
+ * aligned. */
+int g4_bf16p_unpack(const uint8_t* data, const uint8_t* cb8, int N, int K, uint8_t* unp, void* stream);
+/* g4_bf16p_gemm over the unpacked copy and the same exceptions: the same values (K a multiple of 64). */
+int g4_bf16p_unpacked_gemm(const uint8_t* unp, const long long* exc_ptr, const uint16_t* exc_col, const float* exc_delta,
+                           int N, int K, const float* X, int M, float* Y, int ldy, void* stream);
 /* Greedy pick over raw logits: r16, max, then the lowest index whose softcapped value equals the
  * max's (gemma4_engine.cpp:1491-1497).  out_idx dev [M]; ws dev >= 8*M B. */
 int g4_head_argmax(const float* Y, int M, int N, int ldy, int* out_idx, void* ws, size_t ws_bytes, void* stream);

@@ -79,8 +79,27 @@ def test_logits_kernel_variants_agree(N, monkeypatch):
                 monkeypatch.setenv("G4_HEAD_GEMV", variant)
             outs.append(head.logits(dev(X)).cpu().numpy())
         monkeypatch.delenv("G4_HEAD_GEMV", raising=False)
+        outs.append(head.logits_unpacked(dev(X)).cpu().numpy())
         for Y in outs:
             assert np.array_equal(bits(Y), bits(Yo)), M
+
+
+def test_unpacked_layout():
+    """The unpacked copy: each weight as bf16p::pack represents it (codebook exponent), as bf16,
+    half h's 16 weights in bytes 32h..32h+31 (octets 0, 2, 1, 3; elements 8o+4h..8o+4h+3)."""
+    d = np.load(GOLD / "bf16p.npz")
+    head = g4.PackedHead(dev(d["E"].view(np.int16)))
+    unp = head.unpacked().cpu().numpy().reshape(-1, 64).view(np.uint16)
+    data = np.asarray(d["data"]).reshape(-1, 44)
+    cb = np.frombuffer(head.cb_host, np.uint8)
+    sm = data[:, :32].astype(np.uint32)
+    planes = data[:, 32:44].copy().view(np.uint32)
+    e = np.arange(32, dtype=np.uint32)
+    codes = ((planes[:, 0:1] >> e) & 1) | (((planes[:, 1:2] >> e) & 1) << 1) | (((planes[:, 2:3] >> e) & 1) << 2)
+    ex = cb[codes].astype(np.uint32)
+    w = ((sm & 0x80) << 8) | (ex << 7) | (sm & 0x7F)
+    order = [8 * o + 4 * h + k for h in range(2) for o in (0, 2, 1, 3) for k in range(4)]
+    assert np.array_equal(unp, w[:, order].astype(np.uint16))
 
 
 def test_pick_tie_rule():
