@@ -1,6 +1,6 @@
 """Benchmark driver (one JSON line on stdout from rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl g4|reference] [--workload NAME]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl g4|reference] [--workload decode|gemv|head]
 
 Workloads:
   decode (default) configs[4]: greedy speculative decode of the synthetic E2B model (30 layers,
@@ -273,6 +273,136 @@ def run_gemv_g4(args, world, rank, local):
     return out, dist_
 
 
+# --------------------------------------------------------------------------- head workload
+N_CFG2, K_CFG2, M_CFG2 = 262144, 2048, 4
+
+
+def run_head_g4(args, world, rank, local):
+    """configs[2]'s exact head: the bf16p logits of M=4 hidden states against the 262,144 x 2048 head
+    (the screen's fallback), through the unpacked copy (g4_bf16p_unpacked_gemm).  Bytes counted:
+    the bf16p rows (44 per group), the exceptions, x and the logits."""
+    import torch
+    import g4
+    torch.cuda.set_device(local)
+    dist_ = init_pg(world, local)
+    g4.device_init()
+    gen = torch.Generator(device="cuda").manual_seed(262144 + rank)
+    E = (torch.randn(N_CFG2, K_CFG2, device="cuda", generator=gen) * 0.02).to(torch.bfloat16).view(torch.int16)
+    head = g4.PackedHead(E)
+    del E
+    torch.cuda.empty_cache()
+    unp = head.unpacked()
+    Xd = torch.randn(M_CFG2, K_CFG2, device="cuda", generator=gen) / float(np.sqrt(K_CFG2))
+    Y = torch.empty((M_CFG2, N_CFG2), device="cuda")
+    nbytes = (N_CFG2 * (K_CFG2 // 32) * 44 + head.n_exc * 6 + (N_CFG2 + 1) * 8 + M_CFG2 * K_CFG2 * 4
+              + M_CFG2 * N_CFG2 * 4)
+    lib = g4.lib()
+    stream = torch.cuda.Stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    cargs = (ctypes.c_void_p(unp.data_ptr()), ctypes.c_void_p(head.exc_ptr.data_ptr()),
+             ctypes.c_void_p(head.exc_col.data_ptr()), ctypes.c_void_p(head.exc_delta.data_ptr()), N_CFG2, K_CFG2,
+             ctypes.c_void_p(Xd.data_ptr()), M_CFG2, ctypes.c_void_p(Y.data_ptr()), N_CFG2, sp)
+
+    def step():
+        if lib.g4_bf16p_unpacked_gemm(*cargs):
+            raise RuntimeError(lib.g4_last_error().decode())
+
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(args.steps):
+            step()
+    with torch.cuda.stream(stream):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(dist_)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_one = time.perf_counter()
+    with torch.cuda.stream(stream):
+        graph.replay()
+    torch.cuda.synchronize()
+    roll = max(1, int(0.6 / max(time.perf_counter() - t_one, 1e-5)))  # the clock record spans ~1.2 s
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            for _ in range(roll):
+                graph.replay()
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            for _ in range(roll):
+                graph.replay()
+        torch.cuda.synchronize()
+    barrier(dist_)
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms, dist_)
+    del graph
+    # e2e: x from pinned host memory, the logits back to it, every step
+    xh = Xd.cpu().pin_memory()
+    yh = torch.empty((M_CFG2, N_CFG2), dtype=torch.float32).pin_memory()
+    with torch.cuda.stream(stream):
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            Xd.copy_(xh, non_blocking=True)
+            step()
+            yh.copy_(Y, non_blocking=True)
+        f1.record(stream)
+        torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), dist_)
+    out = None
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        per_gpu = nbytes * args.steps / (ms / 1e3) / 1e9
+        out = {
+            "metric": METRIC, "value": nbytes * args.steps * world / (ms_max / 1e3) / 1e9, "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded head ~ N(0, 0.02) bf16, x ~ N(0,1)/sqrt(2048))",
+            "config": {"workload": "configs[2] exact head (bf16p) 262144x2048, M=4", "N": N_CFG2, "K": K_CFG2,
+                       "M": M_CFG2, "exceptions": int(head.n_exc), "bytes_per_step": nbytes,
+                       "timing": "K launches replayed as one CUDA graph, CUDA events on its stream",
+                       "l2": "every step reads the 1.07 GB unpacked head (> L2)", "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
+                         "peak_kind": peak_kind, "traffic": profile_traffic("head_unpacked_gemv_cfg2"),
+                         "kernel": "k_bf16u_rows_tma<4>"},
+            "e2e": {"value": nbytes * args.steps * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": M_CFG2 * K_CFG2 * 4, "d2h_bytes_per_step": M_CFG2 * N_CFG2 * 4},
+            "gpu_launches": args.steps,
+            "clocks": clk.summary(),
+        }
+    return out, (dist_, head, Xd)
+
+
+def cpu_head_port(head_and_x, rows=8192, seconds=10.0):
+    """The oracle's bf16p logits (the restatement of bf16p::rows_tile, OpenMP over rows) for the first
+    `rows` rows of the same head and x, on the host's cores."""
+    from oracle_lib import or_head_logits
+    head, Xd = head_and_x
+    K = head.K
+    data = head.data[: rows * (K // 32) * 44].cpu().numpy()
+    ep = head.exc_ptr[: rows + 1].cpu().numpy()
+    ne = int(ep[-1])
+    col = head.exc_col[:max(ne, 1)].cpu().numpy().view(np.uint16)
+    dl = head.exc_delta[:max(ne, 1)].cpu().numpy()
+    X = Xd.cpu().numpy()
+    cb = np.frombuffer(head.cb_host, np.uint8)
+    nbytes = rows * (K // 32) * 44 + ne * 6 + (rows + 1) * 8 + X.size * 4 + X.shape[0] * rows * 4
+    or_head_logits((data, ep, col, dl), cb, rows, K, X)
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < seconds and n < 1000:
+        or_head_logits((data, ep, col, dl), cb, rows, K, X)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": nbytes * n / dt / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} calls of the oracle's bf16p logits over the first {rows} rows, M=4 (OpenMP)"}
+
+
 # --------------------------------------------------------------------------- decode workload
 PROMPT_SEED, N_PROMPT = 4, 6841
 TOKENS_METRIC_UNIT = "tok/s"
@@ -454,14 +584,14 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "head"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--fake-ctx", action="store_true",
                     help="decode: build the 6.8k context with the reference's ENGINE_FAKE_CTX values instead of a "
                          "prefill (short, for profiling)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 64 if args.workload == "decode" else 200
+        args.steps = {"decode": 64, "gemv": 200, "head": 20}[args.workload]
     if args.warmup is None:
         args.warmup = 3 if args.workload == "decode" else 10
     args.warmup = max(args.warmup, 3)
@@ -474,6 +604,9 @@ def main():
             return
         if args.workload == "decode":
             reference_decode(args)
+        elif args.workload == "head":
+            print(json.dumps({"impl": "reference", "unavailable": "the head workload has no reference arm; "
+                              "its cpu_baseline is the oracle's restatement of bf16p::rows_tile"}))
         else:
             reference_gemv(args)
         return
@@ -482,6 +615,10 @@ def main():
         out, dist_ = run_decode_g4(args, world, rank, local)
         if rank == 0 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_decode_port()
+    elif args.workload == "head":
+        out, (dist_, head, Xd) = run_head_g4(args, world, rank, local)
+        if rank == 0 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_head_port((head, Xd))
     else:
         out, dist_ = run_gemv_g4(args, world, rank, local)
         if rank == 0 and not args.no_cpu_baseline:
