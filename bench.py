@@ -403,6 +403,121 @@ def cpu_head_port(head_and_x, rows=8192, seconds=10.0):
             "sample": f"{n} calls of the oracle's bf16p logits over the first {rows} rows, M=4 (OpenMP)"}
 
 
+# --------------------------------------------------------------------------- screen workload
+SCREEN_BYTES = N_CFG2 * (K_CFG2 // 2) + N_CFG2 * (K_CFG2 // 32) * 2 + N_CFG2 * 4  # int4 + scales + coef
+
+
+def run_screen_g4(args, world, rank, local):
+    """configs[2]'s certified head screen, vocab-parallel: rank r holds rows [r N/W, (r+1) N/W) of
+    the 262,144 x 2,048 head (screen copy, packed rows, unpacked copy) and one call is the hidden
+    broadcast, the shard's screen, the all-reduced bound, survivors or the shard's full exact head,
+    the all-reduced candidate max and the all-reduced winner (NCCL between the device phases).
+    Total work is fixed as W grows ("strong").  Bytes counted per call: the int4 screen, plus the
+    bf16p rows and exceptions of every shard that fell back."""
+    import torch
+    import g4
+    torch.cuda.set_device(local)
+    dist_ = init_pg(world, local)
+    g4.device_init()
+    n_loc = N_CFG2 // world
+    gen = torch.Generator(device="cuda").manual_seed(262144 * 16 + rank)
+    E = (torch.randn(n_loc, K_CFG2, device="cuda", generator=gen) * 0.02).to(torch.bfloat16).view(torch.int16)
+    shard = g4.ScreenShard(E, rank * n_loc, lim=30000, M=M_CFG2)
+    del E
+    torch.cuda.empty_cache()
+    hgen = torch.Generator(device="cuda").manual_seed(2048)
+    H = torch.randn(M_CFG2, K_CFG2, device="cuda", generator=hgen) / float(np.sqrt(K_CFG2))
+
+    def step():
+        if dist_ is None:
+            idx, ns = g4.screen_sharded([shard], H)
+        else:
+            idx = g4.screen_shard_dist(shard, H, dist_)
+        return idx
+
+    for _ in range(args.warmup):
+        idx = step()
+    torch.cuda.synchronize()
+    _, ns = shard.select(H, shard.bound(H))  # survivors of this shard (fallback = -1)
+    fell_back = bool((ns < 0).any().item())
+    nb = torch.tensor([shard.head.n_exc], dtype=torch.float64, device="cuda")
+    if dist_ is not None:
+        dist_.all_reduce(nb)
+    n_exc = int(nb.item())
+    nbytes = SCREEN_BYTES + M_CFG2 * K_CFG2 * 4 + (N_CFG2 * (K_CFG2 // 32) * 44 + n_exc * 6 if fell_back else 0)
+    barrier(dist_)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            idx = step()
+        e1.record()
+        torch.cuda.synchronize()
+    barrier(dist_)
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms, dist_)
+    # e2e: the hidden rows from pinned host memory on rank 0, the winners back to host every call
+    hh = H.cpu().pin_memory()
+    ih = torch.empty(M_CFG2, dtype=torch.int32).pin_memory()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        if rank == 0:
+            H.copy_(hh, non_blocking=True)
+        idx = step()
+        ih.copy_(idx, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), dist_)
+    out = None
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        per_gpu = nbytes / world * args.steps / (ms_max / 1e3) / 1e9
+        out = {
+            "metric": METRIC, "value": nbytes * args.steps / (ms_max / 1e3) / 1e9, "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded head ~ N(0, 0.02) bf16 per shard, h ~ N(0,1)/sqrt(2048))",
+            "config": {"workload": f"configs[2] certified head screen 262144x2048, M=4, vocab-parallel x{world}",
+                       "rows_per_gpu": n_loc, "lim": 30000, "fallback": fell_back, "bytes_per_step": nbytes,
+                       "collectives": "NCCL broadcast h, all-reduce max (bound, candidate max), all-reduce min "
+                                      "(winner) between the device phases" if world > 1 else "none",
+                       "timing": "CUDA events around K calls (eager launches), max over ranks",
+                       "parallelism": f"vocab-parallel x{world}"},
+            "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
+                         "peak_kind": peak_kind, "traffic": None,
+                         "kernel": "whole screen call per GPU (screen GEMV + exact-head fallback + collectives)"},
+            "e2e": {"value": nbytes * args.steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": M_CFG2 * K_CFG2 * 4, "d2h_bytes_per_step": M_CFG2 * 4},
+            "gpu_launches": 13 * args.steps,  # per call: bound 4, select 8, pick 1 (per GPU)
+            "clocks": clk.summary(),
+            "winners": [int(i) for i in idx.cpu().numpy()],
+        }
+    return out, dist_
+
+
+def cpu_screen_port(rows=16384, seconds=10.0):
+    """The oracle's screen row (screen_task's bound and survivor list, restated) over the first
+    `rows` rows of a configs[2]-distributed head, for M=4 hidden rows, on the host's cores."""
+    from oracle_lib import bf16_bits, or_screen_build, or_screen_row
+    rng = np.random.default_rng(2)
+    E = bf16_bits(rng.standard_normal((rows, K_CFG2), dtype=np.float32) * np.float32(0.02))
+    W4, S4, coef = or_screen_build(E)
+    H = (rng.standard_normal((M_CFG2, K_CFG2), dtype=np.float32) / np.float32(np.sqrt(K_CFG2))).astype(np.float32)
+    nbytes = rows * (K_CFG2 // 2) + rows * (K_CFG2 // 32) * 2 + rows * 4
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < seconds and n < 200:
+        for m in range(M_CFG2):
+            or_screen_row(W4, S4, coef, H[m], lim=rows)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": nbytes * n / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{n} screens of {rows} rows x M=4 (oracle restatement of screen_task, scalar; no exact head)"}
+
+
 # --------------------------------------------------------------------------- decode workload
 PROMPT_SEED, N_PROMPT = 4, 6841
 TOKENS_METRIC_UNIT = "tok/s"
@@ -584,14 +699,14 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "head"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "head", "screen"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--fake-ctx", action="store_true",
                     help="decode: build the 6.8k context with the reference's ENGINE_FAKE_CTX values instead of a "
                          "prefill (short, for profiling)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"decode": 64, "gemv": 200, "head": 20}[args.workload]
+        args.steps = {"decode": 64, "gemv": 200, "head": 20, "screen": 20}[args.workload]
     if args.warmup is None:
         args.warmup = 3 if args.workload == "decode" else 10
     args.warmup = max(args.warmup, 3)
@@ -604,9 +719,9 @@ def main():
             return
         if args.workload == "decode":
             reference_decode(args)
-        elif args.workload == "head":
-            print(json.dumps({"impl": "reference", "unavailable": "the head workload has no reference arm; "
-                              "its cpu_baseline is the oracle's restatement of bf16p::rows_tile"}))
+        elif args.workload in ("head", "screen"):
+            print(json.dumps({"impl": "reference", "unavailable": f"the {args.workload} workload has no reference "
+                              "arm; its cpu_baseline is the oracle's restatement"}))
         else:
             reference_gemv(args)
         return
@@ -615,6 +730,10 @@ def main():
         out, dist_ = run_decode_g4(args, world, rank, local)
         if rank == 0 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_decode_port()
+    elif args.workload == "screen":
+        out, dist_ = run_screen_g4(args, world, rank, local)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_screen_port()
     elif args.workload == "head":
         out, (dist_, head, Xd) = run_head_g4(args, world, rank, local)
         if rank == 0 and not args.no_cpu_baseline:

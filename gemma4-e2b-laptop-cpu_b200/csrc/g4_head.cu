@@ -837,6 +837,77 @@ __global__ void k_screen_fb_out(const int* __restrict__ slots, int M, const Scre
   if (m < M) out[m] = slots[2 * m + 1] == 0x7FFFFFFF ? -1 : slots[2 * m + 1];
 }
 
+// ---- vocab-parallel screen: one shard of the head's rows per GPU.  The single-GPU screen is
+// split at its two global reductions, the bound L (a max over all rows) and the pick (the max
+// candidate value, then the lowest index whose capped value equals the cap of that max); the
+// caller reduces between the phases (all-reduce max / min across the shards).
+__global__ void k_shard_L_out(const ScreenWs w, int M, float* __restrict__ L) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = threadIdx.x;
+  if (m < M) L[m] = ord2f(w.Lord[m]);
+}
+__global__ void k_shard_set_L(const float* __restrict__ L, int M, ScreenWs w) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = threadIdx.x;
+  if (m < M) w.Lord[m] = f2ord(L[m]);
+}
+// the shard's largest candidate value per row: the rescored survivors, or (fallback) the r16
+// logits of every row, whose max k_pick_max left in slots
+__global__ void k_shard_vmax(int lim, const ScreenWs w, const int* __restrict__ slots, float* __restrict__ vmax,
+                             int* __restrict__ nsurv) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.x;
+  const int count = min(w.cnt[m], lim);
+  __shared__ float smx[32];
+  float mx = -1e30f;
+  if (!*w.fb)
+    for (int k = threadIdx.x; k < count; k += blockDim.x) mx = fmaxf(mx, w.fval[(size_t)m * lim + k]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+  if ((threadIdx.x & 31) == 0) smx[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, smx[i]);
+    vmax[m] = *w.fb ? ord2f(slots[2 * m]) : mx;
+    nsurv[m] = *w.fb ? -1 : count;
+  }
+}
+// lowest shard index whose candidate v satisfies v >= gmax - 2 and cap(v) == cap(gmax), as a global
+// index (row0 + local), or INT_MAX; survivors, or every row on the fallback
+__global__ void k_shard_pick(const float* __restrict__ gmax, int lim, const ScreenWs w, int N, int row0,
+                             int* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.x;
+  const float mx = gmax[m];
+  const float cm = cap_bf(mx), lo = __fsub_rn(mx, 2.0f);
+  __shared__ int sidx[32];
+  int best = 0x7FFFFFFF;
+  if (*w.fb) {
+    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+      const float v = r16(w.s[(size_t)m * N + i]);
+      if (v >= lo && cap_bf(v) == cm) { best = i; break; }  // strided: later i only larger
+    }
+  } else {
+    const int count = min(w.cnt[m], lim);
+    for (int k = threadIdx.x; k < count; k += blockDim.x) {
+      const float v = w.fval[(size_t)m * lim + k];
+      if (v >= lo && cap_bf(v) == cm) best = min(best, w.surv[(size_t)m * lim + k]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) best = min(best, __shfl_xor_sync(FULL, best, o));
+  if ((threadIdx.x & 31) == 0) sidx[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) best = min(best, sidx[i]);
+    out[m] = best == 0x7FFFFFFF ? 0x7FFFFFFF : row0 + best;
+  }
+}
+
 }  // namespace g4
 
 G4_STATUS_READER(head)
@@ -1306,4 +1377,63 @@ int g4::head_screen_impl(const uint8_t* W4p, const uint16_t* S4, const float* co
   if (int rc = pick(w.s, M, N, N, w.slots, nullptr, w.fb, st)) return rc;
   if (int rc_ = launch("k_screen_fb_out", k_screen_fb_out, dim3(1), dim3(32), 0, st, w.slots, M, w, out_idx)) return rc_;
   return check_launch("k_screen_fb_out");
+}
+
+// ---- vocab-parallel screen phases (one shard of N rows of the head on this device)
+extern "C" int g4_head_screen_shard_bound(const uint8_t* W4p, const uint16_t* S4, const float* coef, int N, int K,
+                                          const float* H, int M, int lim, float* L_out, void* ws, size_t ws_bytes,
+                                          void* stream) {
+  G4_REQUIRE(W4p && S4 && coef && H && L_out && ws, "g4_head_screen_shard_bound: null pointer");
+  G4_REQUIRE(M >= 1 && M <= 4 && N > 0 && K > 0 && K % 256 == 0 && lim > 0, "g4_head_screen_shard_bound: bad shape");
+  G4_NEED_INIT("g4_head_screen_shard_bound");
+  const size_t need = screen_ws_layout(M, N, lim, nullptr, nullptr);
+  if (ws_bytes < need) return set_error(G4_ERR_NOMEM, "g4_head_screen_shard_bound: workspace %zu < %zu bytes", ws_bytes, need);
+  G4_REQUIRE(aligned(ws, 256), "g4_head_screen_shard_bound: workspace must be 256-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  ScreenWs w;
+  screen_ws_layout(M, N, lim, &w, static_cast<char*>(ws));
+  if (int rc_ = launch("k_screen_init", k_screen_init, dim3(M), dim3(32), 0, st, H, K, M, w)) return rc_;
+  if (int rc = g4_w4g32_gemm(W4p, S4, H, nullptr, M, N, K, w.s, N, stream)) return rc;
+  if (int rc_ = launch("k_screen_L", k_screen_L, dim3(dim3(296, M)), dim3(256), 0, st, coef, N, w)) return rc_;
+  if (int rc_ = launch("k_shard_L_out", k_shard_L_out, dim3(1), dim3(32), 0, st, w, M, L_out)) return rc_;
+  return check_launch("g4_head_screen_shard_bound");
+}
+
+extern "C" int g4_head_screen_shard_select(const float* coef, const uint8_t* data, const uint8_t* unp, const uint8_t* cb8,
+                                           const long long* exc_ptr, const uint16_t* exc_col, const float* exc_delta,
+                                           int N, int K, const float* H, int M, int lim, const float* L,
+                                           float* vmax_out, int* out_nsurv, void* ws, size_t ws_bytes, void* stream) {
+  G4_REQUIRE(coef && data && cb8 && exc_ptr && H && L && vmax_out && out_nsurv && ws,
+             "g4_head_screen_shard_select: null pointer");
+  G4_REQUIRE(M >= 1 && M <= 4 && N > 0 && K > 0 && K % 256 == 0 && lim > 0, "g4_head_screen_shard_select: bad shape");
+  const size_t need = screen_ws_layout(M, N, lim, nullptr, nullptr);
+  if (ws_bytes < need) return set_error(G4_ERR_NOMEM, "g4_head_screen_shard_select: workspace %zu < %zu bytes", ws_bytes, need);
+  cudaStream_t st = as_stream(stream);
+  ScreenWs w;
+  screen_ws_layout(M, N, lim, &w, static_cast<char*>(ws));
+  HeadPacked P = make_head(data, cb8, exc_ptr, exc_col, exc_delta, N, K);
+  P.unp = unp;
+  if (int rc_ = launch("k_shard_set_L", k_shard_set_L, dim3(1), dim3(32), 0, st, L, M, w)) return rc_;
+  if (int rc_ = launch("k_screen_thr", k_screen_thr, dim3(1), dim3(32), 0, st, M, w)) return rc_;
+  if (int rc_ = launch("k_screen_collect", k_screen_collect, dim3(dim3(296, M)), dim3(256), 0, st, coef, N, lim, w)) return rc_;
+  if (int rc_ = launch("k_screen_rescore", k_screen_rescore, dim3(dim3((lim + 31) / 32, M)), dim3(256), 0, st, P, H, lim, w)) return rc_;
+  // fallback: the shard's full exact head and its max, gated on the device flag
+  if (int rc = head_gemv(P, H, M, w.s, N, w.fb, st)) return rc;
+  if (int rc_ = launch("k_pick_init", k_pick_init, dim3(1), dim3(32), 0, st, w.slots, M)) return rc_;
+  if (int rc_ = launch("k_pick_max", k_pick_max, dim3(dim3(296, M)), dim3(256), 0, st, w.s, N, N, w.slots, w.fb)) return rc_;
+  if (int rc_ = launch("k_shard_vmax", k_shard_vmax, dim3(M), dim3(256), 0, st, lim, w, w.slots, vmax_out, out_nsurv)) return rc_;
+  return check_launch("g4_head_screen_shard_select");
+}
+
+extern "C" int g4_head_screen_shard_pick(int N, int M, int lim, int row0, const float* gmax, int* idx_out, void* ws,
+                                         size_t ws_bytes, void* stream) {
+  G4_REQUIRE(gmax && idx_out && ws, "g4_head_screen_shard_pick: null pointer");
+  G4_REQUIRE(M >= 1 && M <= 4 && N > 0 && lim > 0 && row0 >= 0, "g4_head_screen_shard_pick: bad shape");
+  const size_t need = screen_ws_layout(M, N, lim, nullptr, nullptr);
+  if (ws_bytes < need) return set_error(G4_ERR_NOMEM, "g4_head_screen_shard_pick: workspace %zu < %zu bytes", ws_bytes, need);
+  ScreenWs w;
+  screen_ws_layout(M, N, lim, &w, static_cast<char*>(ws));
+  if (int rc_ = launch("k_shard_pick", k_shard_pick, dim3(M), dim3(1024), 0, as_stream(stream), gmax, lim, w, N, row0, idx_out))
+    return rc_;
+  return check_launch("k_shard_pick");
 }

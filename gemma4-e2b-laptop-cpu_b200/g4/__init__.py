@@ -35,6 +35,9 @@ SIGNATURES = {
     "g4_head_argmax": (_I, [_P, _I, _I, _I, _P, _P, _SZ, _P]),
     "g4_rmsnorm": (_I, [_P, _P, _I, _I, _P, _I, _P, _P, _P, _P]),
     "g4_bf16p_unpack": (_I, [_P, _P, _I, _I, _P, _P]),
+    "g4_head_screen_shard_bound": (_I, [_P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _SZ, _P]),
+    "g4_head_screen_shard_select": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _SZ, _P]),
+    "g4_head_screen_shard_pick": (_I, [_I, _I, _I, _I, _P, _P, _P, _SZ, _P]),
     "g4_bf16p_unpacked_gemm": (_I, [_P, _P, _P, _P, _I, _I, _P, _I, _P, _I, _P]),
     "g4_screen_build": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "g4_head_screen_ws_bytes": (_SZ, [_I, _I, _I]),
@@ -257,6 +260,105 @@ class PackedHead:
                                            _ptr(self.exc_delta), self.N, self.K, _ptr(X), M, _ptr(Y), Y.stride(0),
                                            _stream()), "g4_bf16p_unpacked_gemm")
         return Y
+
+
+class ScreenShard:
+    """One shard of the head for the vocab-parallel screen: rows row0 .. row0 + N of E (bf16 on the
+    device), its packed rows, its unpacked copy and its int4 screen copy, and the workspace that
+    the three phases share."""
+
+    def __init__(self, E_rows, row0, lim=30000, M=4, unpacked=True):
+        import torch
+        _dev(E_rows, "E_rows")
+        self.N, self.K = E_rows.shape
+        self.row0, self.lim, self.M = int(row0), int(lim), int(M)
+        self.head = PackedHead(E_rows)
+        self.unp = self.head.unpacked() if unpacked and self.K % 64 == 0 else None
+        self.screen = screen_build(E_rows)
+        nb = lib().g4_head_screen_ws_bytes(self.M, self.N, self.lim)
+        self.ws = torch.empty(nb // 4 + 64, dtype=torch.float32, device=E_rows.device)
+        self.ws_bytes = self.ws.numel() * 4
+
+    def bound(self, H):
+        import torch
+        M = H.shape[0]
+        L = torch.empty(M, dtype=torch.float32, device=H.device)
+        W4, S4, coef = self.screen
+        check(lib().g4_head_screen_shard_bound(_ptr(W4), _ptr(S4), _ptr(coef), self.N, self.K, _ptr(H), M, self.lim,
+                                               _ptr(L), _ptr(self.ws), self.ws_bytes, _stream()),
+              "g4_head_screen_shard_bound")
+        return L
+
+    def select(self, H, L):
+        import torch
+        M = H.shape[0]
+        vmax = torch.empty(M, dtype=torch.float32, device=H.device)
+        ns = torch.empty(M, dtype=torch.int32, device=H.device)
+        h = self.head
+        check(lib().g4_head_screen_shard_select(_ptr(self.screen[2]), _ptr(h.data), _ptr(self.unp), h.cb, _ptr(h.exc_ptr),
+                                                _ptr(h.exc_col), _ptr(h.exc_delta), self.N, self.K, _ptr(H), M, self.lim,
+                                                _ptr(L), _ptr(vmax), _ptr(ns), _ptr(self.ws), self.ws_bytes, _stream()),
+              "g4_head_screen_shard_select")
+        return vmax, ns
+
+    def pick(self, gmax):
+        import torch
+        M = gmax.shape[0]
+        idx = torch.empty(M, dtype=torch.int32, device=gmax.device)
+        check(lib().g4_head_screen_shard_pick(self.N, M, self.lim, self.row0, _ptr(gmax), _ptr(idx), _ptr(self.ws),
+                                              self.ws_bytes, _stream()), "g4_head_screen_shard_pick")
+        return idx
+
+
+INT_MAX = 0x7FFFFFFF
+
+
+def screen_sharded(shards, H):
+    """The vocab-parallel screen with every shard on this process (the reductions done here):
+    winners [M] (-1 = none) and survivors per shard [G][M] (-1 = that shard fell back)."""
+    import torch
+    L = torch.stack([s.bound(H) for s in shards]).max(0).values
+    sel = [s.select(H, L) for s in shards]
+    gmax = torch.stack([v for v, _ in sel]).max(0).values
+    idx = torch.stack([s.pick(gmax) for s in shards]).min(0).values
+    idx = torch.where(idx == INT_MAX, torch.full_like(idx, -1), idx)
+    return idx, torch.stack([n for _, n in sel])
+
+
+def screen_shard_dist(shard, H, dist_, group=None, src=0):
+    """The vocab-parallel screen with one shard per rank of a torch.distributed group (NCCL over
+    NVLink on GPUs): H is broadcast from `src`, then the bound, the candidate max and the winner
+    index are all-reduced between the phases.  Returns the winners [M] (-1 = none) on every rank."""
+    phases = _ShardPhases(shard)
+    return screen_dist(phases, H, dist_, group, src)
+
+
+class _ShardPhases:
+    def __init__(self, shard):
+        self.s = shard
+
+    def bound(self, H):
+        return self.s.bound(H)
+
+    def select(self, H, L):
+        return self.s.select(H, L)[0]
+
+    def pick(self, gmax):
+        return self.s.pick(gmax)
+
+
+def screen_dist(phases, H, dist_, group=None, src=0):
+    """The collective skeleton of the vocab-parallel screen over any object with bound / select /
+    pick (the device phases on a GPU; a host restatement in the CPU tests)."""
+    import torch
+    dist_.broadcast(H, src=src, group=group)
+    L = phases.bound(H)
+    dist_.all_reduce(L, op=dist_.ReduceOp.MAX, group=group)
+    vmax = phases.select(H, L)
+    dist_.all_reduce(vmax, op=dist_.ReduceOp.MAX, group=group)
+    idx = phases.pick(vmax)
+    dist_.all_reduce(idx, op=dist_.ReduceOp.MIN, group=group)
+    return torch.where(idx == INT_MAX, torch.full_like(idx, -1), idx)
 
 
 def head_argmax(Y):

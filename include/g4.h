@@ -127,6 +127,27 @@ int g4_head_screen(const uint8_t* W4p, const uint16_t* S4, const float* coef, co
                    const float* H, int M, int lim, int* out_idx, int* out_nsurv, void* ws, size_t ws_bytes,
                    void* stream);
 
+/* Vocab-parallel screen (one shard of N head rows per device, rows row0.. of the full head): the
+ * single-device screen split at its two global reductions.  Per call, with M <= 4 rows of H:
+ *   1. g4_head_screen_shard_bound: screen GEMV and the shard's bound L_out dev [M];
+ *   2. the caller reduces L across the shards (max) into L;
+ *   3. g4_head_screen_shard_select: survivors against the global threshold, exact rescoring or (on
+ *      overflow) the shard's full exact head (unp may be NULL: the bf16p rows are read), and the
+ *      shard's largest candidate value vmax_out dev [M]; out_nsurv dev [M] (-1 = fallback);
+ *   4. the caller reduces vmax across the shards (max) into gmax;
+ *   5. g4_head_screen_shard_pick: the shard's lowest global index whose candidate value v has
+ *      v >= gmax - 2 and the same softcapped value as gmax, or INT_MAX; idx_out dev [M];
+ *   6. the caller reduces the indices (min); INT_MAX means no winner (-1).
+ * ws as for g4_head_screen (g4_head_screen_ws_bytes(M, N, lim)), kept between the phases. */
+int g4_head_screen_shard_bound(const uint8_t* W4p, const uint16_t* S4, const float* coef, int N, int K, const float* H,
+                               int M, int lim, float* L_out, void* ws, size_t ws_bytes, void* stream);
+int g4_head_screen_shard_select(const float* coef, const uint8_t* data, const uint8_t* unp, const uint8_t* cb8,
+                                const long long* exc_ptr, const uint16_t* exc_col, const float* exc_delta, int N, int K,
+                                const float* H, int M, int lim, const float* L, float* vmax_out, int* out_nsurv, void* ws,
+                                size_t ws_bytes, void* stream);
+int g4_head_screen_shard_pick(int N, int M, int lim, int row0, const float* gmax, int* idx_out, void* ws, size_t ws_bytes,
+                              void* stream);
+
 /* ---------------------------------------------------------------- split-KV decode attention */
 
 /* Workspace bytes g4_attn_splitkv needs for these sizes. */
