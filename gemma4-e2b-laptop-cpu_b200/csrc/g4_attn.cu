@@ -107,8 +107,6 @@ __host__ __device__ inline size_t attn_scores_smem(int hd) {
 template <int STEPS>  // hd / 16
 __global__ void __launch_bounds__(512) k_attn_scores(const uint16_t* __restrict__ Kc, const float* __restrict__ q,
                                                      AttnDesc d0, float* __restrict__ ws) {
-  pdl_wait();
-  pdl_trigger();
   constexpr int HD = STEPS * 16, LS = ScoreTile<STEPS>::kLaneStr, KS = ScoreTile<STEPS>::kKeyStr;
   extern __shared__ __align__(128) uint8_t sm_raw[];
   const AttnDesc d = resolve(d0);
@@ -118,18 +116,28 @@ __global__ void __launch_bounds__(512) k_attn_scores(const uint16_t* __restrict_
   const AttnWs w = attn_ws(ws, d);
   const int len = d.kmax - d.kmin + 1;
   const int p0 = d.kmin + blockIdx.x * kScoreKeys;
-  if (p0 > d.kmax) return;  // grid sized for the longest key range (positions read on the device)
+  if (p0 > d.kmax) {  // grid sized for the longest key range (positions read on the device)
+    pdl_wait();
+    pdl_trigger();
+    return;
+  }
   const int nk = min(kScoreKeys, d.kmax + 1 - p0);
   if (threadIdx.x == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
+  // keys before the first query row's position were written by earlier passes: requested before
+  // the wait on the previous kernel (the KV write of the current rows), the current rows after it
+  const int nold = min(nk, max(0, d.pos[0] - p0));
   if (threadIdx.x == 0) {
-    const uint32_t bytes = (uint32_t)nk * HD * 2;
-    mbar_expect_tx(bar, bytes);
-    bulk_g2s(sm_raw + 128, Kc + (size_t)p0 * HD, bytes, bar);
+    mbar_expect_tx(bar, (uint32_t)nk * HD * 2);
+    if (nold > 0) bulk_g2s(sm_raw + 128, Kc + (size_t)p0 * HD, (uint32_t)nold * HD * 2, bar);
   }
+  pdl_wait();
+  pdl_trigger();
+  if (nk > nold && threadIdx.x == 0)
+    bulk_g2s(sm_raw + 128 + (size_t)nold * HD * 2, Kc + (size_t)(p0 + nold) * HD, (uint32_t)(nk - nold) * HD * 2, bar);
   const int hw = threadIdx.x >> 4, c = threadIdx.x & 15;
   const bool live_mh = hw < d.M * d.nh;
   const int m = live_mh ? hw / d.nh : 0, h = live_mh ? hw % d.nh : 0;
@@ -588,8 +596,6 @@ template <int STEPS>
 __global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
                                                     const float* __restrict__ q, AttnDesc d0, float* __restrict__ ws,
                                                     int* __restrict__ counters, float* __restrict__ out) {
-  pdl_wait();
-  pdl_trigger();
   extern __shared__ __align__(128) uint8_t sm_raw[];
   __shared__ float red_f[8];
   __shared__ float msc[64], red_f_am[32];
@@ -612,11 +618,23 @@ __global__ void __launch_bounds__(256) k_attn_short(const uint16_t* __restrict__
     fence_mbar_init();
   }
   __syncthreads();
-  if (n > 0 && threadIdx.x == 0) {  // the chunk's rows are contiguous: one copy for K, one for V
-    const uint32_t bytes = (uint32_t)d.hd * 2 * (uint32_t)n;
-    mbar_expect_tx(bar, 2u * bytes);
-    bulk_g2s(ks, Kc + (size_t)c0 * d.hd, bytes, bar);
-    bulk_g2s(vs, Vc + (size_t)c0 * d.hd, bytes, bar);
+  // The chunk's rows are contiguous: one copy for K, one for V.  Keys before the first query row's
+  // position were written by earlier passes, so their rows are requested before the wait on the
+  // previous kernel (the KV write of the current rows); the current rows follow after it.
+  const int nold = min(n, max(0, d.pos[0] - c0));
+  const uint32_t rb = (uint32_t)d.hd * 2;
+  if (n > 0 && threadIdx.x == 0) {
+    mbar_expect_tx(bar, 2u * rb * (uint32_t)n);
+    if (nold > 0) {
+      bulk_g2s(ks, Kc + (size_t)c0 * d.hd, rb * (uint32_t)nold, bar);
+      bulk_g2s(vs, Vc + (size_t)c0 * d.hd, rb * (uint32_t)nold, bar);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (n > nold && threadIdx.x == 0) {
+    bulk_g2s(ks + (size_t)nold * rs, Kc + (size_t)(c0 + nold) * d.hd, rb * (uint32_t)(n - nold), bar);
+    bulk_g2s(vs + (size_t)nold * rs, Vc + (size_t)(c0 + nold) * d.hd, rb * (uint32_t)(n - nold), bar);
   }
   float qr[STEPS];
   {

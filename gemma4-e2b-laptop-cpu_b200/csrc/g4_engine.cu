@@ -407,9 +407,14 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
     pf.mark(e->st, PH_EMBED_NORM);
     const bool split = dyn || (M <= 4 && pos0 + M > e->cfg.att_par);
     // split-KV reads the rotated queries from qs ([M][QD]); the per-row paths read them in place
-    RCK(launch("k_qkv_post", k_qkv_post, dim3(dim3(M, d.NQ + 2)), dim3(256), 0, e->st, e->qkv, ld, d.NQ, d.HD, dyn ? 1 : pos0, dyn ? e->ctl : nullptr,
-                                                     t.qn, t.kn, e->rope[ty][0], e->rope[ty][1], Kc, Vc,
-                                                     split ? e->qs : e->qkv, split ? QD : ld));
+    if (d.HD % 64 == 0 && d.HD <= 512 && d.NQ + 2 <= 16)  // warp per head
+      RCK(launch("k_qkv_post_w", k_qkv_post_w, dim3(M), dim3(32 * (d.NQ + 2)), 0, e->st, e->qkv, ld, d.NQ, d.HD,
+                 dyn ? 1 : pos0, dyn ? e->ctl : nullptr, t.qn, t.kn, e->rope[ty][0], e->rope[ty][1], Kc, Vc,
+                 split ? e->qs : e->qkv, split ? QD : ld));
+    else
+      RCK(launch("k_qkv_post", k_qkv_post, dim3(dim3(M, d.NQ + 2)), dim3(256), 0, e->st, e->qkv, ld, d.NQ, d.HD, dyn ? 1 : pos0, dyn ? e->ctl : nullptr,
+                                                       t.qn, t.kn, e->rope[ty][0], e->rope[ty][1], Kc, Vc,
+                                                       split ? e->qs : e->qkv, split ? QD : ld));
     RCK(check_launch("k_qkv_post"));
     pf.mark(e->st, PH_ATTN);
     bool att_q = false;

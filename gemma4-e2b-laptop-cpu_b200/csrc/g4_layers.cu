@@ -117,6 +117,77 @@ __global__ void k_qkv_post(const float* __restrict__ qkv, int ldqkv, int nq, int
   }
 }
 
+// Warp-per-head variant of k_qkv_post (same values): block = row m, warp w = part w (q heads, then
+// k, then v), hd a multiple of 64 and at most 512.  Lanes 0..15 run the 16 ordered partial sums of
+// the RMS (lane c: elements c, c+16, ... in order, from global memory); the reference's combine
+// ((p_b + p_4+b) + (p_8+b + p_12+b)), then (t0 + t2) + (t1 + t3), is done by shuffles (fadd is
+// commutative, so each sum pairs the same operands); lane l owns elements j = l + 32k (k < hd/64)
+// and j + hd/2, the RoPE pairs.  The norm weights and the RoPE rows (positions read on the device
+// come from the host-written control word) are loaded before the wait on the previous kernel.
+__global__ void __launch_bounds__(512) k_qkv_post_w(const float* __restrict__ qkv, int ldqkv, int nq, int hd, int pos0,
+                                                    const int* __restrict__ dpos, const float* __restrict__ qn,
+                                                    const float* __restrict__ kn, const float* __restrict__ cosT,
+                                                    const float* __restrict__ sinT, uint16_t* __restrict__ Kc,
+                                                    uint16_t* __restrict__ Vc, float* __restrict__ qdst, int ldq) {
+  constexpr int kMaxPer = 8;  // hd / 64
+  const int m = blockIdx.x, part = threadIdx.x >> 5, lane = threadIdx.x & 31, hh = hd >> 1, per = hd >> 6;
+  if (dpos) pos0 += *dpos;
+  const int pos = pos0 + m;
+  const float* w = part < nq ? qn : (part == nq ? kn : nullptr);
+  float wl[kMaxPer], wh[kMaxPer], cs[kMaxPer], sn[kMaxPer];
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int j = lane + 32 * k;
+    const bool in = k < per;
+    wl[k] = (in && w) ? w[j] : 1.f;
+    wh[k] = (in && w) ? w[j + hh] : 1.f;
+    cs[k] = (in && part <= nq) ? cosT[(size_t)pos * hh + j] : 0.f;
+    sn[k] = (in && part <= nq) ? sinT[(size_t)pos * hh + j] : 0.f;
+  }
+  pdl_wait();  // the weights and tables above are read-only; the row comes from the previous kernel
+  pdl_trigger();
+  const float* src = qkv + (size_t)m * ldqkv + (size_t)part * hd;
+  float xl[kMaxPer], xh[kMaxPer];
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int j = lane + 32 * k;
+    xl[k] = k < per ? src[j] : 0.f;
+    xh[k] = k < per ? src[j + hh] : 0.f;
+  }
+  double s = 0.0;  // partial lane (lanes 0..15): elements lane, lane + 16, ... in order
+  if (lane < 16)
+    for (int i = lane; i < hd; i += 16) { const double d = src[i]; s = fma(d, d, s); }
+  double u = s + __shfl_down_sync(FULL, s, 4);   // lanes 0-3, 8-11: p_b + p_4+b and p_8+b + p_12+b
+  double t = u + __shfl_down_sync(FULL, u, 8);   // lanes 0-3: t_b
+  double v2 = t + __shfl_down_sync(FULL, t, 2);  // lanes 0, 1: t0 + t2, t1 + t3
+  double ss = v2 + __shfl_down_sync(FULL, v2, 1);
+  ss = __shfl_sync(FULL, ss, 0);
+  const double mean = (hd & (hd - 1)) == 0 ? ss * (1.0 / (double)hd) : ss / (double)hd;
+  const float r = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)mean, 1e-6f)));
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    if (k >= per) break;
+    const int j = lane + 32 * k;
+    const float a = w ? r16(__fmul_rn(__fmul_rn(xl[k], r), wl[k])) : r16(__fmul_rn(xl[k], r));
+    const float b = w ? r16(__fmul_rn(__fmul_rn(xh[k], r), wh[k])) : r16(__fmul_rn(xh[k], r));
+    if (part == nq + 1) {
+      Vc[(size_t)pos * hd + j] = (uint16_t)f2bf(a);
+      Vc[(size_t)pos * hd + j + hh] = (uint16_t)f2bf(b);
+      continue;
+    }
+    const float ra = fmaf(a, cs[k], -__fmul_rn(b, sn[k]));
+    const float rb = fmaf(b, cs[k], __fmul_rn(a, sn[k]));
+    if (part == nq) {
+      Kc[(size_t)pos * hd + j] = (uint16_t)f2bf(ra);
+      Kc[(size_t)pos * hd + j + hh] = (uint16_t)f2bf(rb);
+    } else {
+      float* dst = qdst + (size_t)m * ldq + (size_t)part * hd;
+      dst[j] = ra;
+      dst[j + hh] = rb;
+    }
+  }
+}
+
 // Query-only variant for the drafter (and any caller whose k/v are not written): heads of q in
 // place, rms_r16 with q_norm then RoPE at position pos.
 __global__ void k_q_post(float* __restrict__ q, int hd, int pos, const int* __restrict__ dpos, const float* __restrict__ qn,

@@ -11,6 +11,9 @@ __global__ void k_embed(const uint16_t* E, const int* toks, int H, float sqrtH, 
 __global__ void k_qkv_post(const float* qkv, int ldqkv, int nq, int hd, int pos0, const int* dpos, const float* qn,
                            const float* kn, const float* cosT, const float* sinT, uint16_t* Kc, uint16_t* Vc,
                            float* qdst, int ldq);
+__global__ void k_qkv_post_w(const float* qkv, int ldqkv, int nq, int hd, int pos0, const int* dpos, const float* qn,
+                             const float* kn, const float* cosT, const float* sinT, uint16_t* Kc, uint16_t* Vc,
+                             float* qdst, int ldq);
 __global__ void k_q_post(float* q, int hd, int pos, const int* dpos, const float* qn, const float* cosT, const float* sinT);
 __global__ void k_post_attn(float* o, float* x, const float* w_post, const float* w_pre, float* mlp_in, int n);
 __global__ void k_post_ff(float* o, float* x, const float* w_post, float scalar, int n);
