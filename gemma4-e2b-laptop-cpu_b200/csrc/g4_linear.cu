@@ -320,9 +320,12 @@ __global__ void __launch_bounds__(kWrThreads) k_w4g32_rows(const uint8_t* __rest
 // x_m(2q+1), x_m+1(2q+1)}, which serve a lane's elements 2j, 2j+1 and 16+2j, 17+2j in two loads.
 constexpr int kTwRows = 128, kTwThreads = 256, kTwNS = 4;
 constexpr int kTwStage = kTwRows * 128 + kTwRows * 16;  // 18 KB, a multiple of the swizzle span
+// With two activation-row pairs (M > 2) a float4 of padding follows every 4 element pairs, so that
+// the two threads of a row (elements 8h.., 16+8h..) read bank-disjoint 16-byte slots.
+__host__ __device__ constexpr int w4g32_xpad(int NP, int q) { return NP == 2 ? (q >> 2) : 0; }
 __host__ __device__ inline size_t w4g32_tma_smem(int M, int K) {
   const int NP = (M + 1) / 2;
-  return 1024 + (size_t)kTwNS * kTwStage + (size_t)(K / 2) * NP * 16 + (size_t)(K / 32) * NP * 8;
+  return 1024 + (size_t)kTwNS * kTwStage + ((size_t)(K / 2) * NP + w4g32_xpad(NP, K / 2)) * 16 + (size_t)(K / 32) * NP * 8;
 }
 
 template <int M>
@@ -334,7 +337,7 @@ k_w4g32_rows_tma(const __grid_constant__ CUtensorMap tw, const __grid_constant__
   __shared__ __align__(8) uint64_t bars[kTwNS];
   uint8_t* stages = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // 1024-byte aligned
   float4* xs = reinterpret_cast<float4*>(stages + (size_t)kTwNS * kTwStage);       // [K/2][NP]
-  float2* gs = reinterpret_cast<float2*>(xs + (size_t)(K / 2) * NP);               // [G][NP]
+  float2* gs = reinterpret_cast<float2*>(xs + (size_t)(K / 2) * NP + w4g32_xpad(NP, K / 2));  // [G][NP]
   pdl_wait();
   pdl_trigger();
   const int G = K >> 5, nch = G >> 3;
@@ -362,7 +365,7 @@ k_w4g32_rows_tma(const __grid_constant__ CUtensorMap tw, const __grid_constant__
       const int m0 = 2 * p, m1 = 2 * p + 1;
       const float a0 = X[(size_t)m0 * K + 2 * q], b0 = X[(size_t)m0 * K + 2 * q + 1];
       const float a1 = m1 < M ? X[(size_t)m1 * K + 2 * q] : 0.f, b1 = m1 < M ? X[(size_t)m1 * K + 2 * q + 1] : 0.f;
-      xs[(size_t)q * NP + p] = make_float4(a0, a1, b0, b1);
+      xs[(size_t)q * NP + p + w4g32_xpad(NP, q)] = make_float4(a0, a1, b0, b1);
     }
   }
   for (int g = t; g < G; g += kTwThreads) {  // ((x0 + x1) + ...) + x31 from 0 (w4g32_avx2.h:22)
@@ -409,7 +412,7 @@ k_w4g32_rows_tma(const __grid_constant__ CUtensorMap tw, const __grid_constant__
       const int g = c * 8 + u;
       const float scl = bf2f((u & 1) ? (s8w[u >> 1] >> 16) : (s8w[u >> 1] & 0xFFFFu));
       const float2 sc2 = make_float2(scl, scl);
-      const float4* xg = xs + (size_t)g * 16 * NP;
+      const float4* xg = xs + (size_t)g * 16 * NP + w4g32_xpad(NP, g * 16);
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
         const int j = 4 * half + jj;  // lane chain: bytes 2j, 2j+1 of the group
@@ -418,7 +421,7 @@ k_w4g32_rows_tma(const __grid_constant__ CUtensorMap tw, const __grid_constant__
         nib4_to_f(v, t0, t1, t2, t3);
 #pragma unroll
         for (int p = 0; p < NP; ++p) {
-          const float4 A = xg[j * NP + p], B = xg[(8 + j) * NP + p];
+          const float4 A = xg[j * NP + p + w4g32_xpad(NP, j)], B = xg[(8 + j) * NP + p + w4g32_xpad(NP, 8 + j)];
           float2 a = __fmul2_rn(make_float2(t0, t0), make_float2(A.x, A.y));
           a = __ffma2_rn(make_float2(t1, t1), make_float2(B.x, B.y), a);
           a = __ffma2_rn(make_float2(t2, t2), make_float2(A.z, A.w), a);
