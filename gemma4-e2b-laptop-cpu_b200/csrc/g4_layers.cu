@@ -290,11 +290,9 @@ struct RmsScratch {
 // is not bf16-valued or not finite counts as kmax 255, kmin 1, which fails the test).
 __device__ __forceinline__ uint32_t ekeys(float x) {
   const uint32_t b = __float_as_uint(x) & 0x7FFFFFFFu;
-  if (b == 0u) return 0u;
-  uint32_t e = b >> 23;
-  if ((b & 0xFFFFu) != 0u || e == 255u) return (255u << 8) | 254u;
-  if (e == 0u) e = 1u;
-  return (e << 8) | (255u - e);
+  const uint32_t e = max(b >> 23, 1u);
+  const uint32_t key = ((b & 0xFFFFu) != 0u || e == 255u) ? ((255u << 8) | 254u) : ((e << 8) | (255u - e));
+  return b == 0u ? 0u : key;
 }
 
 // RMS scale of a row held as float4 blocks, in the reference's order (gemma4_engine.cpp:326-343):
@@ -335,13 +333,15 @@ __device__ float row_rms_scale(const float4 (&v)[kF4], const float* xs, int n, R
   }
   __syncthreads();
   if (t < 16) {
-    double s = 0.0;
+    double p8[8];
     uint32_t kw = 0u;
 #pragma unroll
     for (int ww = 0; ww < 8; ++ww) {
-      s += sc.part[ww][t];
+      p8[ww] = sc.part[ww][t];
       kw = __vmaxu4(kw, sc.keys[ww][t >> 1]);
     }
+    // exact on the fast path (any order), replaced by the chain otherwise: a tree
+    double s = ((p8[0] + p8[1]) + (p8[2] + p8[3])) + ((p8[4] + p8[5]) + (p8[6] + p8[7]));
     const uint32_t kk = (kw >> (16 * (t & 1))) & 0xFFFFu;  // this partial's (kmax, 255 - kmin)
     const int kmax = (int)(kk >> 8), kmin = 255 - (int)(kk & 0xFFu);
     if (kmax - kmin > 15) {  // the chain may round: the sequential sum in element order
