@@ -560,9 +560,10 @@ def run_decode_g4(args, world, rank, local):
     torch.cuda.synchronize()
     # nvidia-smi samples every 200 ms: untimed rounds (the same work) run for ~0.4 s before and after
     # the timed call so that the clock record covers it
+    pad_s = 0.0 if args.no_clock_window else 0.4  # no padding rounds: profiling runs only
     with Clocks(local) as clk:
         t_pad, n_pad = time.perf_counter(), 0
-        while time.perf_counter() - t_pad < 0.4 and n_pad < 60:  # <= 60 rounds: the context must hold them
+        while time.perf_counter() - t_pad < pad_s and n_pad < 60:  # <= 60 rounds: the context must hold them
             eng.decode(4, 1 << 30)
             n_pad += 4
         _, st_w = eng.decode(0, 1 << 30)
@@ -571,7 +572,7 @@ def run_decode_g4(args, world, rank, local):
         n_tok, st = eng.decode(args.steps, 1 << 30)
         wall_s = time.perf_counter() - t1
         t_pad, n_pad = time.perf_counter(), 0
-        while time.perf_counter() - t_pad < 0.4 and n_pad < 60:
+        while time.perf_counter() - t_pad < pad_s and n_pad < 60:
             eng.decode(4, 1 << 30)
             n_pad += 4
     d = {k: st[k] - st_w[k] for k in ("rounds", "ngram_rounds", "drafted", "accepted", "decode_tokens", "verify_passes",
@@ -701,6 +702,8 @@ def main():
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "head", "screen"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clock-window", action="store_true",
+                    help="decode: no untimed padding rounds around the timed call (for profiling; clocks unsampled)")
     ap.add_argument("--fake-ctx", action="store_true",
                     help="decode: build the 6.8k context with the reference's ENGINE_FAKE_CTX values instead of a "
                          "prefill (short, for profiling)")
