@@ -423,10 +423,18 @@ def run_screen_g4(args, world, rank, local):
     gen = torch.Generator(device="cuda").manual_seed(262144 * 16 + rank)
     E = (torch.randn(n_loc, K_CFG2, device="cuda", generator=gen) * 0.02).to(torch.bfloat16).view(torch.int16)
     shard = g4.ScreenShard(E, rank * n_loc, lim=30000, M=M_CFG2)
+    if args.planted:  # rank 0's rows for the planted hidden states (broadcast to every rank)
+        E0 = E[:M_CFG2 * 9973 + 8].view(torch.bfloat16).float() if rank == 0 else None
+        shard.head_rows_f32 = lambda rows: E0[rows] if E0 is not None else torch.zeros(len(rows), K_CFG2, device="cuda")
     del E
     torch.cuda.empty_cache()
     hgen = torch.Generator(device="cuda").manual_seed(2048)
     H = torch.randn(M_CFG2, K_CFG2, device="cuda", generator=hgen) / float(np.sqrt(K_CFG2))
+    if args.planted:  # h = a w_j / |w_j| + sqrt(1 - a^2) noise for rows j of rank 0's shard
+        rows = [5 + 9973 * m for m in range(M_CFG2)]
+        Wj = shard.head_rows_f32(rows)
+        a = float(args.plant_weight)
+        H = a * Wj / Wj.norm(dim=1, keepdim=True) + float(np.sqrt(max(0.0, 1.0 - a * a))) * H
 
     def step():
         if dist_ is None:
@@ -438,8 +446,11 @@ def run_screen_g4(args, world, rank, local):
     for _ in range(args.warmup):
         idx = step()
     torch.cuda.synchronize()
-    _, ns = shard.select(H, shard.bound(H))  # survivors of this shard (fallback = -1)
+    if dist_ is not None:
+        dist_.broadcast(H, src=0)
+    _, ns = shard.select(H, shard.bound(H))  # survivors of this shard (fallback = -1), local bound
     fell_back = bool((ns < 0).any().item())
+    nsurv = [int(v) for v in ns.cpu().numpy()]
     nb = torch.tensor([shard.head.n_exc], dtype=torch.float64, device="cuda")
     if dist_ is not None:
         dist_.all_reduce(nb)
@@ -480,8 +491,10 @@ def run_screen_g4(args, world, rank, local):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded head ~ N(0, 0.02) bf16 per shard, h ~ N(0,1)/sqrt(2048))",
-            "config": {"workload": f"configs[2] certified head screen 262144x2048, M=4, vocab-parallel x{world}",
+            "config": {"workload": f"configs[2] certified head screen 262144x2048, M=4, vocab-parallel x{world}"
+                                   + (f", planted hidden states (weight {args.plant_weight})" if args.planted else ""),
                        "rows_per_gpu": n_loc, "lim": 30000, "fallback": fell_back, "bytes_per_step": nbytes,
+                       "rank0_survivors_local_bound": nsurv,
                        "collectives": "NCCL broadcast h, all-reduce max (bound, candidate max), all-reduce min "
                                       "(winner) between the device phases" if world > 1 else "none",
                        "timing": "CUDA events around K calls (eager launches), max over ranks",
@@ -702,6 +715,9 @@ def main():
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "head", "screen"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--planted", action="store_true",
+                    help="screen: planted hidden states a * w_j/|w_j| + sqrt(1 - a^2) * noise (a = --plant-weight)")
+    ap.add_argument("--plant-weight", type=float, default=0.3)
     ap.add_argument("--no-clock-window", action="store_true",
                     help="decode: no untimed padding rounds around the timed call (for profiling; clocks unsampled)")
     ap.add_argument("--fake-ctx", action="store_true",
