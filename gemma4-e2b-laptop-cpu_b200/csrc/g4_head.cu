@@ -1065,12 +1065,14 @@ __global__ void k_bf16u_pack(const uint8_t* __restrict__ data, long long ngroups
 }
 
 // Exact-head GEMV over the unpacked layout, fed by the TMA, two threads per row (as
-// k_bf16p_rows_tma, same values): per pipeline item one tensor-map load brings 2 groups (128
-// bytes) of 128 rows under the 128-byte swizzle (16-byte chunk u of row r lands at chunk
-// u ^ (r & 7)), so the half-row loads of a 16-byte phase hit distinct bank quads.
-constexpr int kBuRows = 128, kBuThreads = 256, kBuNS = 4, kBuBox = 128;
+// k_bf16p_rows_tma, same values): per pipeline item two tensor-map loads bring 4 groups (2 boxes
+// of 128 bytes) of 128 rows under the 128-byte swizzle (16-byte chunk u of row r lands at chunk
+// u ^ (r & 7)), so the half-row loads of a 16-byte phase hit distinct bank quads.  Two stages of
+// 32 KB hold as many bytes in flight as four of 16 KB, with half the CTA barriers per byte.
+constexpr int kBuRows = 128, kBuThreads = 256, kBuNS = 2, kBuBox = 128, kBuBoxes = 2;  // 4 groups per item
+constexpr int kBuStage = kBuBoxes * kBuRows * kBuBox;
 __host__ __device__ inline size_t head_unp_smem(int M, int K) {
-  return 1024 + 128 + (size_t)kBuNS * kBuRows * kBuBox + (size_t)K * ((M + 1) / 2) * 8;
+  return 1024 + 128 + (size_t)kBuNS * kBuStage + (size_t)K * ((M + 1) / 2) * 8;
 }
 
 template <int M>
@@ -1081,11 +1083,11 @@ __global__ void __launch_bounds__(kBuThreads, 2) k_bf16u_rows_tma(const __grid_c
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[kBuNS];
   uint8_t* stages = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // 1024-byte aligned
-  float2* xs = reinterpret_cast<float2*>(stages + (size_t)kBuNS * kBuRows * kBuBox);  // [K][NP]
+  float2* xs = reinterpret_cast<float2*>(stages + (size_t)kBuNS * kBuStage);  // [K][NP]
   pdl_wait();
   pdl_trigger();
   if (gate != nullptr && *gate == 0) return;
-  const int K = P.K, G = K >> 5, nch = G / 2;
+  const int K = P.K, G = K >> 5, nch = G / (2 * kBuBoxes);
   const int nblk = (P.N + kBuRows - 1) / kBuRows;
   const int myblk = nblk > (int)blockIdx.x ? (nblk - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int nitems = myblk * nch;
@@ -1097,8 +1099,11 @@ __global__ void __launch_bounds__(kBuThreads, 2) k_bf16u_rows_tma(const __grid_c
   __syncthreads();
   auto issue = [&](int i, int st) {  // thread 0
     const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
-    mbar_expect_tx(&bars[st], (uint32_t)(kBuRows * kBuBox));
-    tma_load_2d(stages + (size_t)st * kBuRows * kBuBox, &tmap, c * kBuBox, blk * kBuRows, &bars[st]);
+    mbar_expect_tx(&bars[st], (uint32_t)kBuStage);
+#pragma unroll
+    for (int b = 0; b < kBuBoxes; ++b)
+      tma_load_2d(stages + (size_t)st * kBuStage + (size_t)b * kBuRows * kBuBox, &tmap, (c * kBuBoxes + b) * kBuBox,
+                  blk * kBuRows, &bars[st]);
   };
   if (t == 0)
     for (int b = 0; b < kBuNS && b < nitems; ++b) issue(b, b);
@@ -1123,14 +1128,14 @@ __global__ void __launch_bounds__(kBuThreads, 2) k_bf16u_rows_tma(const __grid_c
 #pragma unroll
         for (int p = 0; p < NP; ++p) acc[j][p] = make_float2(0.f, 0.f);
     }
-    const uint8_t* rowp = stages + ((size_t)st * kBuRows + rl) * kBuBox;
-    uint32_t wv[16];  // this half's words of the item's 2 groups
+    const uint8_t* rowp = stages + (size_t)st * kBuStage + (size_t)rl * kBuBox;
+    uint32_t wv[16 * kBuBoxes];  // this half's words of the item's groups (2 per box)
 #pragma unroll
-    for (int gg = 0; gg < 2; ++gg)
+    for (int gg = 0; gg < 2 * kBuBoxes; ++gg)
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
-        const int chunk = gg * 4 + half * 2 + u;
-        const uint4 t4 = *reinterpret_cast<const uint4*>(rowp + ((chunk ^ (rl & 7)) << 4));
+        const int chunk = (gg & 1) * 4 + half * 2 + u;
+        const uint4 t4 = *reinterpret_cast<const uint4*>(rowp + (size_t)(gg >> 1) * kBuRows * kBuBox + ((chunk ^ (rl & 7)) << 4));
         wv[8 * gg + 4 * u] = t4.x; wv[8 * gg + 4 * u + 1] = t4.y; wv[8 * gg + 4 * u + 2] = t4.z; wv[8 * gg + 4 * u + 3] = t4.w;
       }
     __syncthreads();  // every row has its words in registers: the stage can be refilled
@@ -1139,8 +1144,8 @@ __global__ void __launch_bounds__(kBuThreads, 2) k_bf16u_rows_tma(const __grid_c
       issue(i + kBuNS, st);
     }
 #pragma unroll
-    for (int gg = 0; gg < 2; ++gg) {
-      const int g = c * 2 + gg;
+    for (int gg = 0; gg < 2 * kBuBoxes; ++gg) {
+      const int g = c * 2 * kBuBoxes + gg;
       const float2* xg = xs + ((size_t)g * 32 + hsh) * NP;
 #pragma unroll
       for (int oi = 0; oi < 4; ++oi) {
@@ -1228,7 +1233,7 @@ static int launch_head_gemv(const HeadPacked& P, const float* X, float* Y, int l
   const char* hv = getenv("G4_HEAD_GEMV");  // "direct" / "octet" select other variants (experiments)
   CUtensorMap tm;
   const size_t usmem = head_unp_smem(M, P.K);
-  if (P.unp != nullptr && P.K % 64 == 0 && aligned(P.unp, 16) && usmem <= 113 * 1024 && head_unp_tmap(P, &tm)) {
+  if (P.unp != nullptr && P.K % (64 * kBuBoxes) == 0 && aligned(P.unp, 16) && usmem <= 113 * 1024 && head_unp_tmap(P, &tm)) {
     cudaFuncSetAttribute(k_bf16u_rows_tma<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)usmem);
     cudaFuncSetAttribute(k_bf16u_rows_tma<M>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);  // 2 CTAs per SM
     int occ = 0;
