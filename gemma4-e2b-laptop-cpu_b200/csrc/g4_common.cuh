@@ -28,6 +28,13 @@ __device__ __forceinline__ float r16(float f) { return bf2f(f2bf(f)); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// %globaltimer: a nanosecond clock shared by every SM of the device.
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Exact small-integer to float: 0x4B000000 | t is the float 2^23 + t for 0 <= t < 2^23.
 __device__ __forceinline__ float u4f(uint32_t t) { return __fsub_rn(__uint_as_float(0x4B000000u | t), 8388608.0f); }
 

@@ -70,6 +70,158 @@ struct PhaseTimer {
   }
 };
 
+// Decode-round state on the device: the spec loop's variables (run_req, gemma4_engine.cpp:1616-1663)
+// live here so that the rounds of a decode call run with no host round trip.  Per-call fields are
+// reset by k_decode_setup; totals accumulate from the prefill.
+struct RoundCtl {
+  int P, conf, seq_len, stopped;                 // last committed position, confirmed token, history length, stop seen
+  int produced, rounds_call, max_rounds, max_tokens;  // this decode call
+  int nd, drafting, M, used_ng;                  // the current round
+  int rounds, ngram_rounds, drafted, accepted;   // totals since the prefill
+  int verify_rows, draft_rounds, trace_n, ctx_full;
+  int head_fallbacks, pad_[3];                   // verify passes whose certified screen fell back to the full head
+  int rounds_m[5];                               // rounds by verify rows M (launch accounting)
+  int ctx_max, trace_cap, out_cap;
+  unsigned long long t_begin, t_verify;          // %globaltimer stamps of the current round
+  unsigned long long draft_ns, verify_ns;        // totals since the prefill
+};
+
+__device__ __forceinline__ bool stop_token(int t) { return t == 106 || t == 1; }
+
+// Reset the per-call fields (budgets come in as arguments: no host copy).
+__global__ void k_decode_setup(RoundCtl* rc, int max_rounds, int max_tokens) {
+  rc->produced = 0;
+  rc->rounds_call = 0;
+  rc->max_rounds = max_rounds;
+  rc->max_tokens = max_tokens;
+  rc->ctx_full = 0;
+}
+
+// Start of a round: prompt lookup over the committed history (:1624-1628: the latest earlier match of
+// the last `ngram` tokens, up to nglen following tokens), else k MTP drafts; writes the round's
+// tokens and P into the control block the captured passes read, and (in a graph) selects the draft
+// and verify bodies.  One block of 256 threads; the history is scanned backwards in 2,048-position
+// chunks staged in shared memory.
+constexpr int kScanChunk = 2048;
+__global__ void __launch_bounds__(256) k_round_begin(RoundCtl* rc, const int* __restrict__ seq, int* ctl, int ngram,
+                                                     int nglen, int kdraft, cudaGraphConditionalHandle hdraft,
+                                                     cudaGraphConditionalHandle hm, int set_handles) {
+  __shared__ int s[kScanChunk + 16];
+  __shared__ int s_best;
+  const int t = threadIdx.x;
+  const int L = rc->seq_len;
+  int best = -1;
+  if (ngram > 0 && ngram <= 8 && L > ngram) {
+    int key[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) key[j] = j < ngram ? seq[L - ngram + j] : 0;
+    for (int hi = L - ngram - 1; hi >= 0; hi -= kScanChunk) {
+      const int lo = hi - (kScanChunk - 1) > 0 ? hi - (kScanChunk - 1) : 0;
+      for (int i = t; i < hi - lo + 1 + ngram; i += blockDim.x) s[i] = seq[lo + i];
+      if (t == 0) s_best = -1;
+      __syncthreads();
+      for (int i = hi - t; i >= lo; i -= blockDim.x) {
+        bool eq = true;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (j < ngram && s[i - lo + j] != key[j]) eq = false;
+        if (eq) { atomicMax(&s_best, i); break; }  // descending: the first hit is this thread's latest
+      }
+      __syncthreads();
+      best = s_best;
+      __syncthreads();
+      if (best >= 0) break;
+    }
+  }
+  if (t == 0) {
+    int nd = 0;
+    int* toks = ctl + 8;
+    toks[0] = rc->conf;
+    if (best >= 0)
+      for (int j = 0; j < nglen && j < 7 && best + ngram + j < L; ++j) toks[1 + nd++] = seq[best + ngram + j];
+    const int used_ng = nd > 0;
+    const int drafting = !used_ng && kdraft > 0;
+    const int M = (drafting ? kdraft : nd) + 1;
+    rc->nd = drafting ? kdraft : nd;
+    rc->used_ng = used_ng;
+    rc->drafting = drafting;
+    rc->M = M;
+    ctl[0] = rc->P;
+    if (set_handles) {
+      cudaGraphSetConditional(hdraft, drafting ? 1u : 0u);
+      cudaGraphSetConditional(hm, (unsigned)(M - 1));
+    }
+    rc->t_begin = globaltimer();
+    rc->t_verify = rc->t_begin;
+  }
+}
+
+// End of a round: nacc = leading drafts equal to the verified tokens, commit G[0..nacc] (history,
+// the call's output, stop tokens 1 / 106), conf = G[nacc], hprev = the final hidden of row nacc,
+// P += nacc + 1 (:1656-1660); the round's trace record; in a graph, whether the loop continues.
+__global__ void __launch_bounds__(256) k_round_end(RoundCtl* rc, int* seq, const int* ctl, const int* G, const float* hbuf,
+                                                   float* hprev, int H, int* out, int* trace, const int* head_ns,
+                                                   cudaGraphConditionalHandle hloop, int set_handle) {
+  __shared__ int s_nacc;
+  const int t = threadIdx.x;
+  if (t == 0) {
+    const unsigned long long now = globaltimer();
+    const int* toks = ctl + 8;
+    const int nd = rc->nd;
+    int nacc = 0;
+    while (nacc < nd && toks[1 + nacc] == G[nacc]) ++nacc;
+    for (int i = 0; i <= nacc; ++i) {
+      const int g = G[i];
+      seq[rc->seq_len++] = g;
+      if (rc->produced < rc->out_cap) out[rc->produced] = g;  // every committed token (the history mirror)
+      rc->produced++;
+      if (stop_token(g)) { rc->stopped = 1; break; }
+    }
+    rc->conf = G[nacc];
+    rc->P += nacc + 1;
+    rc->rounds++;
+    rc->rounds_call++;
+    rc->accepted += nacc;
+    rc->verify_rows += rc->M;
+    rc->rounds_m[rc->M]++;
+    if (rc->used_ng) rc->ngram_rounds++;
+    if (rc->drafting) {
+      rc->drafted += nd;
+      rc->draft_rounds++;
+      rc->draft_ns += rc->t_verify - rc->t_begin;
+    }
+    rc->verify_ns += now - rc->t_verify;
+    if (head_ns != nullptr && head_ns[0] < 0) rc->head_fallbacks++;
+    if (rc->trace_n < rc->trace_cap) {
+      int* tr = trace + 6 * (size_t)rc->trace_n;
+      tr[0] = nd;
+      tr[1] = rc->used_ng;
+      for (int j = 0; j < 3; ++j) tr[2 + j] = (rc->drafting && j < nd) ? toks[1 + j] : -1;
+      tr[5] = nacc;
+    }
+    rc->trace_n++;
+    const bool budget = rc->rounds_call < rc->max_rounds && rc->produced < rc->max_tokens;
+    const bool room = rc->P + 1 + 8 < rc->ctx_max;
+    if (!rc->stopped && budget && !room) rc->ctx_full = 1;
+    if (set_handle) cudaGraphSetConditional(hloop, (!rc->stopped && budget && room) ? 1u : 0u);
+    s_nacc = nacc;
+  }
+  __syncthreads();
+  const float* src = hbuf + (size_t)s_nacc * H;
+  for (int i = t; i < H; i += blockDim.x) hprev[i] = src[i];
+}
+
+// Arms the decode loop: the WHILE handle's default is 0, so a launch in which the device could not
+// set a conditional value runs no round at all (rather than an unbounded loop).
+__global__ void k_loop_arm(cudaGraphConditionalHandle hloop) { cudaGraphSetConditional(hloop, 1u); }
+
+// The first kernel of a captured verify pass stamps its start (after the previous kernel finished).
+__global__ void k_stamp(RoundCtl* rc) {
+  pdl_wait();
+  pdl_trigger();
+  rc->t_verify = globaltimer();
+}
+
 }  // namespace g4
 
 struct g4_engine {
@@ -124,10 +276,20 @@ struct g4_engine {
   int gk_verify[5] = {0, 0, 0, 0, 0}, gk_draft = 0;  // kernel nodes of each graph
   cudaEvent_t tev[4] = {nullptr, nullptr, nullptr, nullptr};  // draft start/end, verify start/end
   int fake_n = 0;
-  // decode state between g4_engine_decode calls
-  std::vector<int> seq;  // prompt + committed tokens (prompt-lookup history)
+  // decode state between g4_engine_decode calls: on the device (RoundCtl, history, outputs, trace),
+  // mirrored on the host after every call
+  g4::RoundCtl* rc = nullptr;      // device
+  g4::RoundCtl* rch = nullptr;     // pinned host mirror
+  int *dseq = nullptr, *dout = nullptr, *dtrace = nullptr;
+  int out_cap = 0, trace_cap = 0;
+  std::vector<int> seq;  // prompt + committed tokens (host mirror of dseq)
   int P = -1, conf = 0;
   bool stopped = false;
+  // the decode loop as one graph: WHILE(round) { begin; IF(drafting) drafts; SWITCH(M) verify; end }
+  cudaGraphExec_t gloop = nullptr;
+  cudaGraph_t graw_verify[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+  cudaGraph_t graw_draft = nullptr;
+  bool loop_failed = false;
 };
 
 using namespace g4;
@@ -332,6 +494,14 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
   if (!rc) rc = ealloc_t(e, &e->cscore, (size_t)d.DTOP * d.DPER);
   if (!rc) rc = ealloc_t(e, &e->cand, (size_t)d.DTOP * d.DPER);
   if (!rc) rc = ealloc_t(e, &e->dtok, 4);
+  e->out_cap = c.ctx_max;
+  e->trace_cap = c.ctx_max;
+  if (!rc) rc = ealloc_t(e, &e->rc, 1);
+  if (!rc) rc = ealloc_t(e, &e->dseq, (size_t)c.ctx_max + 64);
+  if (!rc) rc = ealloc_t(e, &e->dout, (size_t)e->out_cap);
+  if (!rc) rc = ealloc_t(e, &e->dtrace, (size_t)e->trace_cap * 6);
+  if (!rc && cudaHostAlloc(reinterpret_cast<void**>(&e->rch), sizeof(RoundCtl), cudaHostAllocDefault) != cudaSuccess)
+    rc = set_error(G4_ERR_CUDA, "g4_engine_create: pinned host buffer");
   if (rc) return fail(rc);
   if (cudaStreamSynchronize(e->st) != cudaSuccess) return fail(set_error(G4_ERR_CUDA, "g4_engine_create: %s", cudaGetErrorString(cudaGetLastError())));
   *out = e;
@@ -344,6 +514,11 @@ extern "C" void g4_engine_destroy(g4_engine* e) {
   for (auto& g : e->gverify)
     if (g) cudaGraphExecDestroy(g);
   if (e->gdraft) cudaGraphExecDestroy(e->gdraft);
+  if (e->gloop) cudaGraphExecDestroy(e->gloop);
+  for (auto& g : e->graw_verify)
+    if (g) cudaGraphDestroy(g);
+  if (e->graw_draft) cudaGraphDestroy(e->graw_draft);
+  if (e->rch) cudaFreeHost(e->rch);
   for (auto& ev : e->tev)
     if (ev) cudaEventDestroy(ev);
   if (e->hio) cudaFreeHost(e->hio);
@@ -605,6 +780,7 @@ extern "C" int g4_engine_fake_ctx(g4_engine* e, int n) {
 // run_req (:1582-1680), split in two: prefill in blocks (int8 per ENGINE_PREFILL_INT8, :1595), then
 // resumable decode rounds (chain mode): prompt lookup or k MTP drafts -> one verify forward ->
 // greedy acceptance.  The committed sequence stays on the host (it is the prompt-lookup history).
+static int upload_round_state(g4_engine* e);
 extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int32_t* first_token) {
   G4_REQUIRE(e && prompt && n >= 1 && e->fake_n + n + 8 <= e->cfg.ctx_max,
              "g4_engine_prefill: bad arguments (n=%d fake context %d ctx_max=%d)", n, e ? e->fake_n : 0,
@@ -631,6 +807,7 @@ extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int
   e->P = FN + n - 1;
   e->conf = first;
   e->stopped = is_stop(first);
+  RCK(upload_round_state(e));
   e->stats = g4_engine_stats{};
   e->stats.prefill_tokens = n;
   e->stats.prefill_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
@@ -638,10 +815,29 @@ extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int
   return G4_OK;
 }
 
+// The device round state after a prefill (or an imported state): history, P, conf, zero totals.
+static int upload_round_state(g4_engine* e) {
+  if ((int)e->seq.size() + 8 > e->cfg.ctx_max + 64) return set_error(G4_ERR_UNSUPPORTED, "history longer than the context");
+  RoundCtl& h = *e->rch;
+  std::memset(&h, 0, sizeof h);
+  h.P = e->P;
+  h.conf = e->conf;
+  h.seq_len = (int)e->seq.size();
+  h.stopped = e->stopped ? 1 : 0;
+  h.ctx_max = e->cfg.ctx_max;
+  h.trace_cap = e->trace_cap;
+  h.out_cap = e->out_cap;
+  ECK(cudaMemcpyAsync(e->dseq, e->seq.data(), sizeof(int) * e->seq.size(), cudaMemcpyHostToDevice, e->st));
+  ECK(cudaMemcpyAsync(e->rc, &h, sizeof h, cudaMemcpyHostToDevice, e->st));
+  ECK(cudaStreamSynchronize(e->st));
+  return G4_OK;
+}
+
 // Record the launches of body() on the engine stream into an executable graph, its kernels launched
 // for programmatic dependent launch; if that capture fails, record it again with ordinary launches.
+// raw (may be NULL) keeps the recorded graph as well (for the decode loop's conditional bodies).
 template <class F>
-static int capture_once(g4_engine* e, cudaGraphExec_t* out, F body, bool pdl, int* kernels) {
+static int capture_once(g4_engine* e, cudaGraphExec_t* out, cudaGraph_t* raw, F body, bool pdl, int* kernels) {
   ECK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
   pdl_enabled() = pdl;
   const int rc = body();
@@ -664,18 +860,23 @@ static int capture_once(g4_engine* e, cudaGraphExec_t* out, F body, bool pdl, in
       }
   }
   const cudaError_t ie = cudaGraphInstantiate(out, g, 0);
-  cudaGraphDestroy(g);
+  if (raw && ie == cudaSuccess) {
+    if (*raw) cudaGraphDestroy(*raw);
+    *raw = g;
+  } else {
+    cudaGraphDestroy(g);
+  }
   if (ie != cudaSuccess) return set_error(G4_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ie));
   return G4_OK;
 }
 template <class F>
-static int capture(g4_engine* e, cudaGraphExec_t* out, F body, int* kernels) {
+static int capture(g4_engine* e, cudaGraphExec_t* out, cudaGraph_t* raw, F body, int* kernels) {
   if (e->cfg.graphs == 1 && e->pdl_ok) {
-    if (capture_once(e, out, body, true, kernels) == G4_OK) return G4_OK;
+    if (capture_once(e, out, raw, body, true, kernels) == G4_OK) return G4_OK;
     cudaGetLastError();
     e->pdl_ok = false;
   }
-  return capture_once(e, out, body, false, kernels);
+  return capture_once(e, out, raw, body, false, kernels);
 }
 
 // The k MTP drafts of a round from ctl (tokens[0] = the confirmed token, ctl[0] = P) and hprev:
@@ -693,112 +894,209 @@ static int draft_chain(g4_engine* e, bool dyn) {
   return G4_OK;
 }
 
+// A captured verify pass for M rows: the start stamp, then the target forward with positions read
+// from ctl[0] on the device.
+static int verify_body(g4_engine* e, int M) {
+  RCK(launch("k_stamp", k_stamp, dim3(1), dim3(32), 0, e->st, e->rc));
+  return forward(e, M, 0, true, 0, true);
+}
+static int ensure_verify_graph(g4_engine* e, int M) {
+  if (!e->gverify[M]) RCK(capture(e, &e->gverify[M], &e->graw_verify[M], [&] { return verify_body(e, M); }, &e->gk_verify[M]));
+  return G4_OK;
+}
+static int ensure_draft_graph(g4_engine* e) {
+  if (!e->gdraft) RCK(capture(e, &e->gdraft, &e->graw_draft, [&] { return draft_chain(e, true); }, &e->gk_draft));
+  return G4_OK;
+}
+
+static int add_kernel_node(cudaGraph_t g, cudaGraphNode_t* node, const cudaGraphNode_t* deps, size_t ndeps, void* fn,
+                           dim3 grid, dim3 block, void** args) {
+  cudaKernelNodeParams kp = {};
+  kp.func = fn;
+  kp.gridDim = grid;
+  kp.blockDim = block;
+  kp.sharedMemBytes = 0;
+  kp.kernelParams = args;
+  ECK(cudaGraphAddKernelNode(node, g, deps, ndeps, &kp));
+  return G4_OK;
+}
+
+// The decode loop as one executable graph (all rounds past att_par):
+//   WHILE (continue) { k_round_begin; IF (drafting) { the k drafts }; SWITCH (M - 1) { verify pass of
+//   M rows }; k_round_end }
+// with the branch values set on the device by k_round_begin / k_round_end, so a whole decode call is
+// one graph launch followed by one copy of the committed tokens.
+static int build_loop_graph(g4_engine* e) {
+  const bool drafter = e->cfg.drafter && e->cfg.k_draft > 0;
+  for (int M = 1; M <= 4; ++M) RCK(ensure_verify_graph(e, M));
+  if (drafter) RCK(ensure_draft_graph(e));
+  cudaGraph_t g = nullptr;
+  ECK(cudaGraphCreate(&g, 0));
+  auto fail = [&](int rc) { cudaGraphDestroy(g); return rc; };
+  cudaGraphConditionalHandle hloop = 0, hdraft = 0, hm = 0;
+  if (cudaGraphConditionalHandleCreate(&hloop, g, 0, cudaGraphCondAssignDefault) != cudaSuccess ||
+      cudaGraphConditionalHandleCreate(&hdraft, g, 0, cudaGraphCondAssignDefault) != cudaSuccess ||
+      cudaGraphConditionalHandleCreate(&hm, g, 0, cudaGraphCondAssignDefault) != cudaSuccess)
+    return fail(set_error(G4_ERR_CUDA, "conditional handles: %s", cudaGetErrorString(cudaGetLastError())));
+  cudaGraphNodeParams wp = {};
+  wp.type = cudaGraphNodeTypeConditional;
+  wp.conditional.handle = hloop;
+  wp.conditional.type = cudaGraphCondTypeWhile;
+  wp.conditional.size = 1;
+  cudaGraphNode_t arm, wnode;
+  void* aargs[] = {&hloop};
+  if (int rc = add_kernel_node(g, &arm, nullptr, 0, reinterpret_cast<void*>(k_loop_arm), dim3(1), dim3(1), aargs)) return fail(rc);
+  if (cudaGraphAddNode(&wnode, g, &arm, 1, &wp) != cudaSuccess)
+    return fail(set_error(G4_ERR_CUDA, "while node: %s", cudaGetErrorString(cudaGetLastError())));
+  cudaGraph_t body = wp.conditional.phGraph_out[0];
+  // k_round_begin
+  RoundCtl* rcp = e->rc;
+  const int* seqc = e->dseq;
+  int* ctl = e->ctl;
+  int ngram = e->cfg.ngram, nglen = e->cfg.ngram_len, kdraft = drafter ? e->cfg.k_draft : 0, one = 1;
+  void* bargs[] = {&rcp, &seqc, &ctl, &ngram, &nglen, &kdraft, &hdraft, &hm, &one};
+  cudaGraphNode_t nbegin, nif = nullptr, nsw, nend;
+  if (int rc = add_kernel_node(body, &nbegin, nullptr, 0, reinterpret_cast<void*>(k_round_begin), dim3(1), dim3(256), bargs)) return fail(rc);
+  cudaGraphNode_t prev = nbegin;
+  if (drafter) {
+    cudaGraphNodeParams ip = {};
+    ip.type = cudaGraphNodeTypeConditional;
+    ip.conditional.handle = hdraft;
+    ip.conditional.type = cudaGraphCondTypeIf;
+    ip.conditional.size = 1;
+    if (cudaGraphAddNode(&nif, body, &prev, 1, &ip) != cudaSuccess)
+      return fail(set_error(G4_ERR_CUDA, "if node: %s", cudaGetErrorString(cudaGetLastError())));
+    cudaGraphNode_t child;
+    if (cudaGraphAddChildGraphNode(&child, ip.conditional.phGraph_out[0], nullptr, 0, e->graw_draft) != cudaSuccess)
+      return fail(set_error(G4_ERR_CUDA, "draft body: %s", cudaGetErrorString(cudaGetLastError())));
+    prev = nif;
+  }
+  cudaGraphNodeParams sp = {};
+  sp.type = cudaGraphNodeTypeConditional;
+  sp.conditional.handle = hm;
+  sp.conditional.type = cudaGraphCondTypeSwitch;
+  sp.conditional.size = 4;
+  if (cudaGraphAddNode(&nsw, body, &prev, 1, &sp) != cudaSuccess)
+    return fail(set_error(G4_ERR_CUDA, "switch node: %s", cudaGetErrorString(cudaGetLastError())));
+  for (int M = 1; M <= 4; ++M) {
+    cudaGraphNode_t child;
+    if (cudaGraphAddChildGraphNode(&child, sp.conditional.phGraph_out[M - 1], nullptr, 0, e->graw_verify[M]) != cudaSuccess)
+      return fail(set_error(G4_ERR_CUDA, "verify body: %s", cudaGetErrorString(cudaGetLastError())));
+  }
+  int* seqm = e->dseq;
+  const int* ctlc = e->ctl;
+  const int* G = e->G;
+  const float* hbuf = e->hbuf;
+  float* hprev = e->hprev;
+  int H = e->d.H;
+  int* out = e->dout;
+  int* trace = e->dtrace;
+  const int* hns = e->cfg.head_screen ? e->head_ns : nullptr;
+  void* eargs[] = {&rcp, &seqm, &ctlc, &G, &hbuf, &hprev, &H, &out, &trace, &hns, &hloop, &one};
+  if (int rc = add_kernel_node(body, &nend, &nsw, 1, reinterpret_cast<void*>(k_round_end), dim3(1), dim3(256), eargs)) return fail(rc);
+  const cudaError_t ie = cudaGraphInstantiate(&e->gloop, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) {
+    e->gloop = nullptr;
+    return set_error(G4_ERR_CUDA, "decode loop instantiate: %s", cudaGetErrorString(ie));
+  }
+  return G4_OK;
+}
+
+static int read_round_state(g4_engine* e) {
+  ECK(cudaMemcpyAsync(e->rch, e->rc, sizeof(RoundCtl), cudaMemcpyDeviceToHost, e->st));
+  ECK(cudaStreamSynchronize(e->st));
+  e->stats.d2h_bytes += sizeof(RoundCtl);
+  return G4_OK;
+}
+
+// One round launched from the host (eager, or graphs of single passes): the device kernels decide
+// as in the loop graph; the host reads the round's shape back once to pick the launches.
+static int host_round(g4_engine* e, bool graphs) {
+  const bool drafter = e->cfg.drafter && e->cfg.k_draft > 0;
+  RCK(launch("k_round_begin", k_round_begin, dim3(1), dim3(256), 0, e->st, e->rc, (const int*)e->dseq, e->ctl, e->cfg.ngram,
+             e->cfg.ngram_len, drafter ? e->cfg.k_draft : 0, (cudaGraphConditionalHandle)0, (cudaGraphConditionalHandle)0, 0));
+  RCK(read_round_state(e));
+  const RoundCtl& h = *e->rch;
+  const int M = h.M;
+  e->P = h.P;
+  const long long l0 = launch_count();
+  if (h.drafting) {
+    if (graphs) {
+      RCK(ensure_draft_graph(e));
+      ECK(cudaGraphLaunch(e->gdraft, e->st));
+      e->stats.kernel_launches += e->gk_draft;
+    } else {
+      RCK(draft_chain(e, false));
+    }
+  }
+  if (graphs) {
+    RCK(ensure_verify_graph(e, M));
+    ECK(cudaGraphLaunch(e->gverify[M], e->st));
+    e->stats.kernel_launches += e->gk_verify[M];
+  } else {
+    RCK(launch("k_stamp", k_stamp, dim3(1), dim3(32), 0, e->st, e->rc));
+    RCK(forward(e, M, e->P + 1, true, 0));
+  }
+  RCK(launch("k_round_end", k_round_end, dim3(1), dim3(256), 0, e->st, e->rc, e->dseq, (const int*)e->ctl, (const int*)e->G,
+             (const float*)e->hbuf, e->hprev, e->d.H, e->dout, e->dtrace,
+             (const int*)(e->cfg.head_screen ? e->head_ns : nullptr), (cudaGraphConditionalHandle)0, 0));
+  e->stats.kernel_launches += launch_count() - l0;
+  RCK(read_round_state(e));
+  e->prof.flush();
+  return G4_OK;
+}
+
 extern "C" int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, int32_t* out, int* n_out,
                                 g4_engine_stats* stats) {
   G4_REQUIRE(e && n_out && max_rounds >= 0 && max_tokens >= 0 && !e->seq.empty(), "g4_engine_decode: call g4_engine_prefill first");
-  const int H = e->d.H, MM = e->MMAX;
   auto t0 = std::chrono::steady_clock::now();
   cudaEvent_t ev0, ev1;
   ECK(cudaEventCreate(&ev0));
   ECK(cudaEventCreate(&ev1));
   ECK(cudaEventRecord(ev0, e->st));
   e->i8_active = e->cfg.decode_int8 && e->cfg.prefill_int8;  // (:1600)
-  int* hctl = e->hio;                  // [0] = P, [8..] = tokens
-  int* hG = e->hio + 8 + MM;           // verified tokens
-  int* hdr = e->hio + 8 + 2 * MM;      // drafts read back
-  int produced = 0, rounds = 0;
-  int block[8];
-  while (rounds < max_rounds && produced < max_tokens && !e->stopped) {
-    if (e->P + 1 + 8 >= e->cfg.ctx_max) return set_error(G4_ERR_UNSUPPORTED, "g4_engine_decode: context full (%d)", e->cfg.ctx_max);
-    block[0] = e->conf;
-    int nd = 0;
-    bool used_ng = false;
-    const std::vector<int>& seq = e->seq;
-    if (e->cfg.ngram > 0) {  // prompt lookup (:1624-1628)
-      const int Ls = (int)seq.size(), NG = e->cfg.ngram;
-      if (Ls > NG)
-        for (int i = Ls - NG - 1; i >= 0; --i) {
-          bool eq = true;
-          for (int t = 0; t < NG; ++t)
-            if (seq[i + t] != seq[Ls - NG + t]) { eq = false; break; }
-          if (eq) {
-            for (int j = 0; j < e->cfg.ngram_len && j < 7 && i + NG + j < Ls; ++j) block[1 + nd++] = seq[i + NG + j];
-            break;
-          }
-        }
-      if (nd > 0) { used_ng = true; e->stats.ngram_rounds++; }
-    }
-    const bool drafting = !used_ng && e->cfg.drafter && e->cfg.k_draft > 0;
-    const int M = (drafting ? e->cfg.k_draft : nd) + 1;
-    // replay captured graphs once the split-KV path applies to every row (positions > att_par)
-    const bool use_g = e->cfg.graphs && !e->prof.on && M <= 4 && e->P + 1 > e->cfg.att_par;
-    hctl[0] = e->P;
-    for (int i = 0; i <= nd; ++i) hctl[8 + i] = block[i];
-    const int nsend = 8 + (drafting ? 1 : M);
-    ECK(cudaMemcpyAsync(e->ctl, hctl, sizeof(int) * nsend, cudaMemcpyHostToDevice, e->st));
-    e->stats.h2d_bytes += sizeof(int) * nsend;
-    if (drafting) {
-      ECK(cudaEventRecord(e->tev[0], e->st));
-      if (use_g) {
-        if (!e->gdraft) RCK(capture(e, &e->gdraft, [&] { return draft_chain(e, true); }, &e->gk_draft));
-        ECK(cudaGraphLaunch(e->gdraft, e->st));
-        e->stats.kernel_launches += e->gk_draft;
-      } else {
-        const long long l0 = launch_count();
-        RCK(draft_chain(e, false));
-        e->stats.kernel_launches += launch_count() - l0;
+  int rc0 = G4_OK;
+  RCK(launch("k_decode_setup", k_decode_setup, dim3(1), dim3(1), 0, e->st, e->rc, max_rounds, max_tokens));
+  e->stats.kernel_launches += 1;
+  int& produced = e->rch->produced;
+  produced = 0;
+  e->rch->rounds_call = 0;
+  e->rch->stopped = e->stopped;
+  e->rch->P = e->P;
+  while (rc0 == G4_OK && e->rch->rounds_call < max_rounds && produced < max_tokens && !e->rch->stopped) {
+    if (e->rch->P + 1 + 8 >= e->cfg.ctx_max) { rc0 = set_error(G4_ERR_UNSUPPORTED, "g4_engine_decode: context full (%d)", e->cfg.ctx_max); break; }
+    // captured graphs once the split-KV path applies to every row (positions > att_par)
+    const bool use_g = e->cfg.graphs && !e->prof.on && e->rch->P + 1 > e->cfg.att_par;
+    if (use_g && !e->loop_failed && !e->gloop) {
+      if (build_loop_graph(e) != G4_OK) {
+        e->loop_failed = true;  // conditional nodes unavailable: rounds launched from the host
+        cudaGetLastError();
       }
-      ECK(cudaEventRecord(e->tev[1], e->st));
-      e->stats.drafted += e->cfg.k_draft;
-      e->stats.draft_steps += e->cfg.k_draft;
-      nd = e->cfg.k_draft;
     }
-    ECK(cudaEventRecord(e->tev[2], e->st));
-    if (use_g) {
-      if (!e->gverify[M]) RCK(capture(e, &e->gverify[M], [&] { return forward(e, M, 0, true, 0, true); }, &e->gk_verify[M]));
-      ECK(cudaGraphLaunch(e->gverify[M], e->st));
-      e->stats.kernel_launches += e->gk_verify[M];
-    } else {
-      const long long l0 = launch_count();
-      RCK(forward(e, M, e->P + 1, true, 0));
-      e->stats.kernel_launches += launch_count() - l0;
+    if (use_g && e->gloop) {
+      const int r0 = e->rch->rounds;
+      int rm[5];
+      std::memcpy(rm, e->rch->rounds_m, sizeof rm);
+      const int dr0 = e->rch->draft_rounds;
+      ECK(cudaGraphLaunch(e->gloop, e->st));
+      RCK(read_round_state(e));
+      const RoundCtl& h = *e->rch;
+      e->stats.kernel_launches += 1 + 2LL * (h.rounds - r0) + (long long)e->gk_draft * (h.draft_rounds - dr0);
+      if (h.rounds == r0) rc0 = set_error(G4_ERR_CUDA, "g4_engine_decode: the round loop graph ran no round");
+      for (int M = 1; M <= 4; ++M) e->stats.kernel_launches += (long long)e->gk_verify[M] * (h.rounds_m[M] - rm[M]);
+      if (h.ctx_full) rc0 = set_error(G4_ERR_UNSUPPORTED, "g4_engine_decode: context full (%d)", e->cfg.ctx_max);
+      break;
     }
-    ECK(cudaEventRecord(e->tev[3], e->st));
-    ECK(cudaMemcpyAsync(hG, e->G, sizeof(int) * M, cudaMemcpyDeviceToHost, e->st));
-    e->stats.d2h_bytes += sizeof(int) * M;
-    if (drafting) {
-      ECK(cudaMemcpyAsync(hdr, e->toks + 1, sizeof(int) * nd, cudaMemcpyDeviceToHost, e->st));
-      e->stats.d2h_bytes += sizeof(int) * nd;
-    }
-    ECK(cudaStreamSynchronize(e->st));
-    e->prof.flush();
-    if (drafting) {
-      for (int j = 0; j < nd; ++j) block[1 + j] = hdr[j];
-      float ms = 0;
-      cudaEventElapsedTime(&ms, e->tev[0], e->tev[1]);
-      e->stats.draft_gpu_ms += ms;
-    }
-    {
-      float ms = 0;
-      cudaEventElapsedTime(&ms, e->tev[2], e->tev[3]);
-      e->stats.verify_gpu_ms += ms;
-      e->stats.verify_passes++;
-      e->stats.verify_rows += M;
-    }
-    e->stats.rounds++;
-    ++rounds;
-    int nacc = 0;
-    while (nacc < nd && block[nacc + 1] == hG[nacc]) ++nacc;
-    e->stats.accepted += nacc;
-    for (int i = 0; i <= nacc; ++i) {
-      e->seq.push_back(hG[i]);
-      if (out && produced < max_tokens) out[produced] = hG[i];
-      ++produced;
-      if (is_stop(hG[i])) { e->stopped = true; break; }
-    }
-    e->conf = hG[nacc];
-    ECK(cudaMemcpyAsync(e->hprev, e->hbuf + (size_t)nacc * H, sizeof(float) * H, cudaMemcpyDeviceToDevice, e->st));
-    e->P += nacc + 1;
+    RCK(host_round(e, use_g));
+  }
+  const RoundCtl& h = *e->rch;
+  const int n = std::min(h.produced, max_tokens);
+  const int ncopy = std::min(h.produced, e->out_cap);  // every committed token, for the history mirror
+  std::vector<int> got(ncopy);
+  if (ncopy > 0) {
+    ECK(cudaMemcpyAsync(got.data(), e->dout, sizeof(int) * ncopy, cudaMemcpyDeviceToHost, e->st));
+    e->stats.d2h_bytes += sizeof(int) * ncopy;
   }
   ECK(cudaEventRecord(ev1, e->st));
   ECK(cudaEventSynchronize(ev1));
@@ -806,11 +1104,88 @@ extern "C" int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, in
   cudaEventElapsedTime(&gms, ev0, ev1);
   cudaEventDestroy(ev0);
   cudaEventDestroy(ev1);
-  e->stats.decode_gpu_ms += gms;
-  e->stats.decode_tokens += std::min(produced, max_tokens);
-  e->stats.decode_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
-  *n_out = std::min(produced, max_tokens);
+  // the committed history: the call's tokens (all of them while they fit the output buffer)
+  for (int i = 0; i < ncopy; ++i) e->seq.push_back(got[i]);
+  if (out) std::memcpy(out, got.data(), sizeof(int) * std::min(n, ncopy));
+  e->P = h.P;
+  e->conf = h.conf;
+  e->stopped = h.stopped != 0;
+  g4_engine_stats& st = e->stats;
+  st.rounds = h.rounds;
+  st.ngram_rounds = h.ngram_rounds;
+  st.drafted = h.drafted;
+  st.accepted = h.accepted;
+  st.verify_passes = h.rounds;
+  st.verify_rows = h.verify_rows;
+  st.draft_steps = h.draft_rounds * e->cfg.k_draft;
+  st.verify_gpu_ms = h.verify_ns * 1e-6;
+  st.draft_gpu_ms = h.draft_ns * 1e-6;
+  st.head_fallbacks = h.head_fallbacks;
+  st.decode_gpu_ms += gms;
+  st.decode_tokens += n;
+  st.decode_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  *n_out = n;
   if (stats) *stats = e->stats;
+  return rc0;
+}
+
+// Per-round records since the prefill: {nd, prompt lookup used, drafts[3] (-1 padded), nacc}.
+extern "C" int g4_engine_trace(g4_engine* e, int32_t* out, int cap_rounds, int* n_rounds) {
+  G4_REQUIRE(e && n_rounds && cap_rounds >= 0 && (out || cap_rounds == 0), "g4_engine_trace: bad arguments");
+  RCK(read_round_state(e));
+  const int n = std::min(e->rch->trace_n, e->trace_cap);
+  const int k = std::min(n, cap_rounds);
+  if (k > 0) {
+    ECK(cudaMemcpyAsync(out, e->dtrace, sizeof(int) * 6 * (size_t)k, cudaMemcpyDeviceToHost, e->st));
+    ECK(cudaStreamSynchronize(e->st));
+  }
+  *n_rounds = n;
+  return G4_OK;
+}
+
+// Device time of the captured verify pass of M rows at the current position, replayed reps times
+// between two CUDA events on the engine stream (the pass rewrites only the rows that the next round
+// writes again: KV rows P+1.., the greedy tokens and the hidden rows).
+extern "C" int g4_engine_time_verify(g4_engine* e, int M, int reps, double* ms_per_pass) {
+  G4_REQUIRE(e && ms_per_pass && M >= 1 && M <= 4 && reps >= 1 && !e->seq.empty() && e->cfg.graphs &&
+                 e->P + 1 > e->cfg.att_par && e->P + 1 + M < e->cfg.ctx_max,
+             "g4_engine_time_verify: needs a prefilled engine with graphs past att_par");
+  e->i8_active = e->cfg.decode_int8 && e->cfg.prefill_int8;
+  RCK(ensure_verify_graph(e, M));
+  int hctl[8 + 4] = {e->P, 0, 0, 0, 0, 0, 0, 0, e->conf, e->conf, e->conf, e->conf};
+  ECK(cudaMemcpyAsync(e->ctl, hctl, sizeof hctl, cudaMemcpyHostToDevice, e->st));
+  ECK(cudaGraphLaunch(e->gverify[M], e->st));  // warm
+  cudaEvent_t a, b;
+  ECK(cudaEventCreate(&a));
+  ECK(cudaEventCreate(&b));
+  ECK(cudaEventRecord(a, e->st));
+  for (int i = 0; i < reps; ++i) ECK(cudaGraphLaunch(e->gverify[M], e->st));
+  ECK(cudaEventRecord(b, e->st));
+  ECK(cudaEventSynchronize(b));
+  float ms = 0;
+  cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  *ms_per_pass = ms / reps;
+  return G4_OK;
+}
+
+// Decode state for another implementation (or a later restore): K and V of positions [0, npos) of
+// every layer, the committed history, the hidden of the last committed row and its position.
+extern "C" int g4_engine_export_state(g4_engine* e, int npos, uint16_t* Kc, uint16_t* Vc, int32_t* seq, int seq_cap,
+                                      int* seq_len, float* hprev, int* P) {
+  G4_REQUIRE(e && npos >= 0 && npos <= e->cfg.ctx_max && seq_len && P && !e->seq.empty(), "g4_engine_export_state: bad arguments");
+  const ModelDims& d = e->d;
+  ECK(cudaStreamSynchronize(e->st));
+  for (int l = 0; l < d.NL && npos > 0; ++l) {
+    const size_t off = (size_t)l * e->cfg.ctx_max * d.HD, n = (size_t)npos * d.HD;
+    if (Kc) ECK(cudaMemcpy(Kc + (size_t)l * n, e->Kc + off, n * 2, cudaMemcpyDeviceToHost));
+    if (Vc) ECK(cudaMemcpy(Vc + (size_t)l * n, e->Vc + off, n * 2, cudaMemcpyDeviceToHost));
+  }
+  *seq_len = (int)e->seq.size();
+  if (seq) std::memcpy(seq, e->seq.data(), sizeof(int) * std::min<size_t>(seq_cap, e->seq.size()));
+  if (hprev) ECK(cudaMemcpy(hprev, e->hprev, sizeof(float) * d.H, cudaMemcpyDeviceToHost));
+  *P = e->P;
   return G4_OK;
 }
 

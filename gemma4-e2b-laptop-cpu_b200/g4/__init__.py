@@ -52,6 +52,9 @@ SIGNATURES = {
     "g4_engine_prefill": (_I, [_P, _P, _I, _P]),
     "g4_engine_decode": (_I, [_P, _I, _I, _P, _P, _P]),
     "g4_engine_phase_times": (_I, [_P, _I, _P, _P]),
+    "g4_engine_trace": (_I, [_P, _P, _I, _P]),
+    "g4_engine_time_verify": (_I, [_P, _I, _I, _P]),
+    "g4_engine_export_state": (_I, [_P, _I, _P, _P, _P, _I, _P, _P, _P]),
     "g4_attn_splitkv_ws_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "g4_attn_splitkv": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
     "g4_attn_splitkv_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
@@ -411,7 +414,7 @@ class EngineStats(ctypes.Structure):
                                                                  ("decode_gpu_ms", ctypes.c_double)] + [
         (n, ctypes.c_int) for n in ("verify_passes", "verify_rows", "draft_steps")] + [
         ("verify_gpu_ms", ctypes.c_double), ("draft_gpu_ms", ctypes.c_double), ("h2d_bytes", ctypes.c_longlong),
-        ("d2h_bytes", ctypes.c_longlong), ("kernel_launches", ctypes.c_longlong)]
+        ("d2h_bytes", ctypes.c_longlong), ("kernel_launches", ctypes.c_longlong), ("head_fallbacks", ctypes.c_int)]
 
     def as_dict(self):
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -478,6 +481,40 @@ class Engine:
         check(lib().g4_engine_decode(self.h, max_rounds, max_tokens, optr, ctypes.byref(n), ctypes.byref(st)),
               "g4_engine_decode")
         return n.value, st.as_dict()
+
+    def trace(self):
+        """Per-round records since the prefill as an [rounds, 6] int32 array: {nd, prompt lookup used,
+        drafts[3] (-1 padded), nacc}."""
+        import numpy as np
+        n = ctypes.c_int(0)
+        check(lib().g4_engine_trace(self.h, None, 0, ctypes.byref(n)), "g4_engine_trace")
+        buf = np.zeros((max(n.value, 1), 6), np.int32)
+        check(lib().g4_engine_trace(self.h, buf.ctypes.data_as(_P), n.value, ctypes.byref(n)), "g4_engine_trace")
+        return buf[: n.value].copy()
+
+    def time_verify(self, M, reps=20):
+        """Device ms of one verify pass of M rows at the current position (CUDA events)."""
+        ms = ctypes.c_double(0)
+        check(lib().g4_engine_time_verify(self.h, int(M), int(reps), ctypes.byref(ms)), "g4_engine_time_verify")
+        return ms.value
+
+    def export_state(self, npos, kv=True):
+        """(K, V [n_layers, npos, 256] uint16 or None, history int32, hprev float32, P)."""
+        import numpy as np
+        nl = self.cfg.n_layers
+        K = np.zeros((nl, npos, 256), np.uint16) if kv else None
+        V = np.zeros((nl, npos, 256), np.uint16) if kv else None
+        n = ctypes.c_int(0)
+        P = ctypes.c_int(0)
+        check(lib().g4_engine_export_state(self.h, 0, None, None, None, 0, ctypes.byref(n), None, ctypes.byref(P)),
+              "g4_engine_export_state")
+        seq = np.zeros(n.value, np.int32)
+        h = np.zeros(self.cfg.hidden, np.float32)
+        check(lib().g4_engine_export_state(self.h, int(npos) if kv else 0, K.ctypes.data_as(_P) if kv else None,
+                                           V.ctypes.data_as(_P) if kv else None, seq.ctypes.data_as(_P), seq.size,
+                                           ctypes.byref(n), h.ctypes.data_as(_P), ctypes.byref(P)),
+              "g4_engine_export_state")
+        return K, V, seq, h, P.value
 
     PHASES = ("embed_norm_rope", "linear", "attention", "head", "drafter", "copies")
 

@@ -204,6 +204,8 @@ typedef struct {
   double verify_gpu_ms, draft_gpu_ms; /* CUDA events around each verify pass / each round's drafts */
   long long h2d_bytes, d2h_bytes;     /* host<->device copies made by the decode calls */
   long long kernel_launches;          /* kernels the decode calls ran (graph kernel nodes included) */
+  int head_fallbacks;                 /* verify passes whose certified screen kept more than screen_lim
+                                         rows and read the full exact head */
 } g4_engine_stats;
 
 int g4_engine_default_config(g4_engine_config* cfg);
@@ -226,8 +228,28 @@ int g4_engine_fake_ctx(g4_engine* e, int n);
 int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int32_t* first_token);
 /* Continue speculative greedy decode for up to max_rounds rounds or max_tokens committed tokens
  * (whichever comes first) or a stop token; out host [max_tokens] (may be NULL), *n_out = tokens
- * committed by this call; stats (may be NULL) accumulate since the prefill. */
+ * committed by this call; stats (may be NULL) accumulate since the prefill.
+ * Prompt lookup, the choice between it and the MTP drafts, greedy acceptance and the commit run on
+ * the device (the spec loop of run_req, gemma4_engine.cpp:1616-1663).  Once every verify row
+ * takes the split-KV path (position > att_par) and graphs are on, all rounds of the call are one
+ * graph launch (a conditional WHILE over rounds, IF for the drafts, SWITCH over the verify rows)
+ * followed by one copy of the committed tokens; verify_gpu_ms and draft_gpu_ms then come from
+ * %globaltimer stamps taken by the round kernels, decode_gpu_ms from CUDA events around the call. */
 int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, int32_t* out, int* n_out, g4_engine_stats* stats);
+/* Per-round records since the prefill, 6 ints each: {drafts verified nd, prompt lookup used (1) or MTP
+ * (0), the MTP drafts (-1 padded), accepted nacc}; out host [cap_rounds][6]; *n_rounds = rounds
+ * recorded (records past the engine's capacity of ctx_max rounds are not kept). */
+int g4_engine_trace(g4_engine* e, int32_t* out, int cap_rounds, int* n_rounds);
+/* Device time of one verify pass of M rows at the current position: the captured pass replayed reps
+ * times between CUDA events on the engine stream (what a round's verify costs, for roofline
+ * accounting).  Needs graphs on and a position past att_par. */
+int g4_engine_time_verify(g4_engine* e, int M, int reps, double* ms_per_pass);
+/* Decode state after a prefill or decode call: K and V rows of positions [0, npos) of every layer
+ * (host [n_layers][npos][256] bf16 each, may be NULL), the committed history (host seq [seq_cap]
+ * may be NULL, *seq_len its length), the final-normed hidden of the last committed row (host
+ * [hidden], may be NULL) and its position *P. */
+int g4_engine_export_state(g4_engine* e, int npos, uint16_t* Kc, uint16_t* Vc, int32_t* seq, int seq_cap, int* seq_len,
+                           float* hprev, int* P);
 /* Per-phase device time (CUDA events on the engine stream) while profiling is on: out_ms[6] =
  * embed+norms+RoPE+residual, linears, attention, head, drafter, copies; out_marks[6] = intervals.
  * enable = 1 starts (and clears), 0 stops, -1 only reads.  Outputs may be NULL. */

@@ -407,3 +407,9 @@ void or_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, int hd, int nh, int
     }
   free(AM); free(AL); free(AO); free(S);
 }
+
+/* OpenMP threads of the restatement's parallel loops (the process's OMP_NUM_THREADS may be fixed by
+ * a launcher). */
+#include <omp.h>
+void or_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
+int or_get_threads(void) { return omp_get_max_threads(); }

@@ -40,7 +40,18 @@ enum { T_Q = 0, T_K = 1, T_V = 2, T_O = 3, T_GATE = 4, T_UP = 5, T_DOWN = 6, T_I
 static uint64_t layer_id(int l, uint64_t w) { return 16ull * (uint64_t)l + w; }
 static uint64_t dlayer_id(int l, uint64_t w) { return 2100ull + 16ull * (uint64_t)l + w; }
 
-typedef struct { uint8_t* w; uint16_t* s; int N, K; } Lin;
+typedef struct { uint8_t* w; uint16_t* s; int N, K; void* ref; } Lin;
+/* Kernel hooks: when set, the linears, the split-KV attention and the exact head run through these
+ * (bench.py points them at the reference's own AVX2 kernels in oracle/_ref/libg4ref.so, driven by
+ * the reference's thread pool), the rest of the restatement stays as it is. */
+typedef struct {
+  void* (*lin_prepare)(const uint8_t* W, const uint16_t* S, int N, int K);
+  void (*lin_run)(void* h, const float* X, int M, float* Y, int i8);
+  void (*attn)(const uint16_t* Kc, const uint16_t* Vc, int hd, int nh, int M, const float* q, const int* pos,
+               const int* lo, int kmin, int kmax, float* out);
+  void* (*head_prepare)(const uint16_t* E, int N, int K, const uint8_t* cb8);
+  void (*head_run)(void* h, const float* X, int M, float* Y);
+} or_e2e_hooks;
 typedef struct { Lin qkv, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff, *qn, *kn; int global; } TLayer;
 typedef struct { Lin q, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff, *qn; int global; } DLayer;
 
@@ -62,6 +73,14 @@ typedef struct {
   float *rc[2], *rs[2];
   int i8;
   int fake_n; /* ENGINE_FAKE_CTX positions before the prompt */
+  /* decode state between or_e2e_decode calls */
+  int* seq;
+  int seq_len, seq_cap, P, conf, stopped;
+  float* hprev;
+  int st[4];
+  /* optional kernel hooks (or_e2e_set_hooks): the reference's own compiled kernels */
+  or_e2e_hooks hk;
+  void* head_ref;
 } Model;
 
 static void gen_lin(Model* m, Lin* lin, const uint64_t* ids, const int* rows, int parts, int K) {
@@ -187,7 +206,7 @@ void or_e2e_destroy(void* mp) {
     free_lin(&m->dpre); free_lin(&m->dpost); free_lin(&m->dcent); free(m->dnorm);
   }
   free(m->fnorm); free(m->E); free(m->hdata); free(m->exc_ptr); free(m->exc_col); free(m->exc_delta);
-  free(m->Kc); free(m->Vc);
+  free(m->Kc); free(m->Vc); free(m->seq); free(m->hprev);
   for (int t = 0; t < 2; ++t) { free(m->rc[t]); free(m->rs[t]); }
   free(m);
 }
@@ -225,6 +244,10 @@ static void rms_r16_w(float* x, const float* w, int n) {
 }
 
 static void lin(Model* m, const Lin* w, const float* X, int M, float* Y, int force_i8) {
+  if (m->hk.lin_run && w->ref) {
+    m->hk.lin_run(w->ref, X, M, Y, (m->i8 && M >= 2) || force_i8);
+    return;
+  }
   if ((m->i8 && M >= 2) || force_i8) {
     int8_t* q = (int8_t*)malloc((size_t)M * w->K);
     float* sx = (float*)malloc(sizeof(float) * (size_t)M * (w->K / 32));
@@ -325,7 +348,8 @@ static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf
         kmin = lo[r] < kmin ? lo[r] : kmin;
         memcpy(q + (size_t)r * QD, qkv + (size_t)r * ld, sizeof(float) * QD);
       }
-      or_attn_splitkv(Kc, Vc, hd, m->NQ, M, q, pos, lo, kmin, pos0 + M - 1, m->attn_chunks, att);
+      if (m->hk.attn) m->hk.attn(Kc, Vc, hd, m->NQ, M, q, pos, lo, kmin, pos0 + M - 1, att);
+      else or_attn_splitkv(Kc, Vc, hd, m->NQ, M, q, pos, lo, kmin, pos0 + M - 1, m->attn_chunks, att);
       free(q);
     } else {
       const int variant = (M >= 4 && pos0 + M > 64) ? 0 : 1;
@@ -360,11 +384,15 @@ static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf
     }
   }
   if (want) {
-    float* logits = (float*)malloc(sizeof(float) * (size_t)m->V);
-    for (int r = hf; r < M; ++r) {
-      rmsnorm(x + (size_t)r * H, m->fnorm, H, hbuf + (size_t)r * H, 1);
-      or_bf16p_gemm(m->hdata, m->cb, m->exc_ptr, m->exc_col, m->exc_delta, m->V, H, hbuf + (size_t)r * H, 1, logits);
-      G[r] = or_head_pick(logits, m->V);
+    float* logits = (float*)malloc(sizeof(float) * (size_t)m->V * 4);
+    for (int r = hf; r < M; ++r) rmsnorm(x + (size_t)r * H, m->fnorm, H, hbuf + (size_t)r * H, 1);
+    for (int r0 = hf; r0 < M; r0 += 4) { /* rows in groups of 4 (:1500) */
+      const int mh = M - r0 < 4 ? M - r0 : 4;
+      if (m->hk.head_run && m->head_ref)
+        m->hk.head_run(m->head_ref, hbuf + (size_t)r0 * H, mh, logits);
+      else
+        or_bf16p_gemm(m->hdata, m->cb, m->exc_ptr, m->exc_col, m->exc_delta, m->V, H, hbuf + (size_t)r0 * H, mh, logits);
+      for (int r = 0; r < mh; ++r) G[r0 + r] = or_head_pick(logits + (size_t)r * m->V, m->V);
     }
     free(logits);
   }
@@ -400,8 +428,12 @@ static int draft(Model* m, int tok, const float* h, int pos, int P, float* h_nex
     for (int hh = 0; hh < m->NQ; ++hh) { rms_r16_w(dq + (size_t)hh * hd, t->qn, hd); rope(dq + (size_t)hh * hd, cs, sn, hd); }
     const int lo = t->global ? 0 : (pos - 511 > 0 ? pos - 511 : 0);
     int pp = P, ll = lo;
-    or_attn_splitkv(m->Kc + (size_t)tl * m->ctx_max * hd, m->Vc + (size_t)tl * m->ctx_max * hd, hd, m->NQ, 1, dq, &pp, &ll, lo,
-                    P, m->attn_chunks, dopt);
+    if (m->hk.attn)
+      m->hk.attn(m->Kc + (size_t)tl * m->ctx_max * hd, m->Vc + (size_t)tl * m->ctx_max * hd, hd, m->NQ, 1, dq, &pp, &ll, lo, P,
+                 dopt);
+    else
+      or_attn_splitkv(m->Kc + (size_t)tl * m->ctx_max * hd, m->Vc + (size_t)tl * m->ctx_max * hd, hd, m->NQ, 1, dq, &pp, &ll,
+                      lo, P, m->attn_chunks, dopt);
     lin(m, &t->o, dopt, 1, da, 1);
     for (int i = 0; i < H; ++i) da[i] = or_r16(da[i]);
     { const float r = rms_scale(da, H); for (int i = 0; i < H; ++i) dx[i] = or_r16(dx[i] + or_r16((da[i] * r) * t->post_attn[i])); }
@@ -477,12 +509,13 @@ void or_e2e_fake_ctx(void* mp, int n) {
   m->fake_n = n;
 }
 
-/* run_req in chain mode (:1582-1663). stats[0..5] = rounds, ngram_rounds, drafted, accepted. */
-int or_e2e_generate(void* mp, const int32_t* prompt, int n, int n_new, int32_t* out, int* n_out, int* stats) {
+/* run_req (:1582-1663), split like the engine's API into a prefill (blocks of prefill_block, int8 per
+ * ENGINE_PREFILL_INT8, :1595) and resumable chain-mode decode rounds (prompt lookup or k MTP drafts
+ * -> one verify forward -> greedy acceptance).  The decode state lives in the model. */
+int or_e2e_prefill(void* mp, const int32_t* prompt, int n, int32_t* first) {
   Model* m = (Model*)mp;
-  const int FN = m->fake_n;
-  const int H = m->H;
-  int* G = (int*)malloc(sizeof(int) * 64);
+  const int FN = m->fake_n, H = m->H;
+  int G[64];
   float* hbuf = (float*)malloc(sizeof(float) * 64 * H);
   m->i8 = m->prefill_int8;
   int done = 0, lastM = 0;
@@ -492,57 +525,153 @@ int or_e2e_generate(void* mp, const int32_t* prompt, int n, int n_new, int32_t* 
     forward(m, prompt + done, M, FN + done, last, last ? M - 1 : 0, G, hbuf);
     done += M; lastM = M;
   }
-  m->i8 = m->decode_int8 && m->prefill_int8;
-  int* gen = (int*)malloc(sizeof(int) * (n_new + 8));
-  int* seq = (int*)malloc(sizeof(int) * (n + n_new + 8));
-  memcpy(seq, prompt, sizeof(int) * n);
-  int ng = 0, L = n;
-  gen[ng++] = G[lastM - 1];
-  seq[L++] = G[lastM - 1];
-  float* hprev = (float*)malloc(sizeof(float) * H);
+  free(m->seq);
+  m->seq_cap = n + 4096;
+  m->seq = (int*)malloc(sizeof(int) * (size_t)m->seq_cap);
+  memcpy(m->seq, prompt, sizeof(int) * n);
+  m->seq_len = n;
+  m->seq[m->seq_len++] = G[lastM - 1];
+  if (!m->hprev) m->hprev = (float*)malloc(sizeof(float) * H);
+  memcpy(m->hprev, hbuf + (size_t)(lastM - 1) * H, sizeof(float) * H);
+  m->P = FN + n - 1;
+  m->conf = G[lastM - 1];
+  m->stopped = is_stop(m->conf);
+  memset(m->st, 0, sizeof m->st);
+  if (first) *first = G[lastM - 1];
+  free(hbuf);
+  return 0;
+}
+
+/* Decode state from elsewhere (a prefill of the same prompt on another implementation): the K and V
+ * rows of positions [0, npos) of every layer ([NL][npos][HD] bf16), the committed history, the hidden
+ * state of the last committed row and its position P; conf = the last history entry. */
+int or_e2e_set_state(void* mp, const uint16_t* Kc, const uint16_t* Vc, int npos, const int32_t* seq, int seq_len,
+                     const float* hprev, int P) {
+  Model* m = (Model*)mp;
+  if (npos > m->ctx_max || seq_len < 1 || P + 1 > npos) return -1;
+  for (int l = 0; l < m->NL; ++l) {
+    memcpy(m->Kc + (size_t)l * m->ctx_max * m->HD, Kc + (size_t)l * npos * m->HD, sizeof(uint16_t) * (size_t)npos * m->HD);
+    memcpy(m->Vc + (size_t)l * m->ctx_max * m->HD, Vc + (size_t)l * npos * m->HD, sizeof(uint16_t) * (size_t)npos * m->HD);
+  }
+  free(m->seq);
+  m->seq_cap = seq_len + 4096;
+  m->seq = (int*)malloc(sizeof(int) * (size_t)m->seq_cap);
+  memcpy(m->seq, seq, sizeof(int) * seq_len);
+  m->seq_len = seq_len;
+  if (!m->hprev) m->hprev = (float*)malloc(sizeof(float) * m->H);
+  memcpy(m->hprev, hprev, sizeof(float) * m->H);
+  m->P = P;
+  m->conf = seq[seq_len - 1];
+  m->stopped = is_stop(m->conf);
+  memset(m->st, 0, sizeof m->st);
+  return 0;
+}
+
+/* Up to max_rounds rounds or max_tokens committed tokens (or a stop token).  stats (may be NULL)
+ * [0..3] = rounds, ngram_rounds, drafted, accepted since the prefill.  trace (may be NULL): per
+ * round 6 ints {nd, prompt lookup used, drafts[3] (-1 padded), nacc}, at most trace_cap rounds. */
+int or_e2e_decode(void* mp, int max_rounds, int max_tokens, int32_t* out, int* n_out, int* stats, int32_t* trace,
+                  int trace_cap) {
+  Model* m = (Model*)mp;
+  const int H = m->H;
+  int G[8];
+  float* hbuf = (float*)malloc(sizeof(float) * 8 * H);
   float* hcur = (float*)malloc(sizeof(float) * H);
   float* hnext = (float*)malloc(sizeof(float) * H);
-  memcpy(hprev, hbuf + (size_t)(lastM - 1) * H, sizeof(float) * H);
-  int P = FN + n - 1, conf = gen[0], stopped = is_stop(conf);
-  int rounds = 0, ngr = 0, drafted = 0, accepted = 0;
-  while (ng < n_new && !stopped) {
+  m->i8 = m->decode_int8 && m->prefill_int8; /* (:1600) */
+  int produced = 0, rounds = 0;
+  while (rounds < max_rounds && produced < max_tokens && !m->stopped) {
+    if (m->seq_len + 8 > m->seq_cap) {
+      m->seq_cap *= 2;
+      m->seq = (int*)realloc(m->seq, sizeof(int) * (size_t)m->seq_cap);
+    }
+    const int* seq = m->seq;
+    const int L = m->seq_len;
     int block[8], nd = 0, used_ng = 0;
-    block[0] = conf;
-    if (m->ngram > 0 && L > m->ngram) {
+    block[0] = m->conf;
+    if (m->ngram > 0 && L > m->ngram) { /* prompt lookup (:1624-1628) */
       for (int i = L - m->ngram - 1; i >= 0; --i) {
         int eq = 1;
         for (int t = 0; t < m->ngram; ++t) if (seq[i + t] != seq[L - m->ngram + t]) { eq = 0; break; }
         if (eq) { for (int j = 0; j < m->ngram_len && j < 7 && i + m->ngram + j < L; ++j) block[1 + nd++] = seq[i + m->ngram + j]; break; }
       }
-      if (nd > 0) { used_ng = 1; ngr++; }
+      if (nd > 0) { used_ng = 1; m->st[1]++; }
     }
     if (!used_ng && m->drafter && m->k_draft > 0) {
-      int cur = conf;
-      memcpy(hcur, hprev, sizeof(float) * H);
+      int cur = m->conf;
+      memcpy(hcur, m->hprev, sizeof(float) * H);
       for (int j = 0; j < m->k_draft; ++j) {
-        const int dtok = draft(m, cur, hcur, P + 1 + j, P, hnext);
+        const int dtok = draft(m, cur, hcur, m->P + 1 + j, m->P, hnext);
         block[1 + nd++] = dtok;
         cur = dtok;
         memcpy(hcur, hnext, sizeof(float) * H);
       }
-      drafted += nd;
+      m->st[2] += nd;
     }
-    forward(m, block, nd + 1, P + 1, 1, 0, G, hbuf);
+    forward(m, block, nd + 1, m->P + 1, 1, 0, G, hbuf);
+    m->st[0]++;
     rounds++;
     int nacc = 0;
     while (nacc < nd && block[nacc + 1] == G[nacc]) ++nacc;
-    accepted += nacc;
-    for (int i = 0; i <= nacc; ++i) { gen[ng++] = G[i]; seq[L++] = G[i]; if (is_stop(G[i])) { stopped = 1; break; } }
-    conf = G[nacc];
-    memcpy(hprev, hbuf + (size_t)nacc * H, sizeof(float) * H);
-    P += nacc + 1;
+    m->st[3] += nacc;
+    if (trace && m->st[0] <= trace_cap) {
+      int32_t* t = trace + 6 * (size_t)(m->st[0] - 1);
+      t[0] = nd; t[1] = used_ng;
+      for (int j = 0; j < 3; ++j) t[2 + j] = (!used_ng && j < nd) ? block[1 + j] : -1;
+      t[5] = nacc;
+    }
+    for (int i = 0; i <= nacc; ++i) {
+      m->seq[m->seq_len++] = G[i];
+      if (out && produced < max_tokens) out[produced] = G[i];
+      ++produced;
+      if (is_stop(G[i])) { m->stopped = 1; break; }
+    }
+    m->conf = G[nacc];
+    memcpy(m->hprev, hbuf + (size_t)nacc * H, sizeof(float) * H);
+    m->P += nacc + 1;
   }
-  if (ng > n_new) ng = n_new;
-  for (int i = 0; i < ng; ++i) if (is_stop(gen[i])) { ng = i + 1; break; }
-  memcpy(out, gen, sizeof(int) * ng);
-  *n_out = ng;
-  if (stats) { stats[0] = rounds; stats[1] = ngr; stats[2] = drafted; stats[3] = accepted; }
-  free(G); free(hbuf); free(gen); free(seq); free(hprev); free(hcur); free(hnext);
+  *n_out = produced < max_tokens ? produced : max_tokens;
+  if (stats) for (int i = 0; i < 4; ++i) stats[i] = m->st[i];
+  free(hbuf); free(hcur); free(hnext);
+  return 0;
+}
+
+/* run_req: prefill, then decode until n_new tokens (the first from the prefill) or a stop token. */
+int or_e2e_generate_trace(void* mp, const int32_t* prompt, int n, int n_new, int32_t* out, int* n_out, int* stats,
+                          int32_t* trace, int trace_cap) {
+  Model* m = (Model*)mp;
+  int first = 0, got = 0;
+  or_e2e_prefill(mp, prompt, n, &first);
+  out[0] = first;
+  if (n_new > 1 && !m->stopped) or_e2e_decode(mp, 1 << 30, n_new - 1, out + 1, &got, NULL, trace, trace_cap);
+  int total = 1 + got;
+  for (int i = 0; i < total; ++i) if (is_stop(out[i])) { total = i + 1; break; }
+  *n_out = total;
+  if (stats) for (int i = 0; i < 4; ++i) stats[i] = m->st[i];
+  return 0;
+}
+int or_e2e_generate(void* mp, const int32_t* prompt, int n, int n_new, int32_t* out, int* n_out, int* stats) {
+  return or_e2e_generate_trace(mp, prompt, n, n_new, out, n_out, stats, NULL, 0);
+}
+
+/* Route the linears, the split-KV attention and the exact head through h (prepared once per matrix). */
+static void hook_lin(Model* m, Lin* l) { if (l->w) l->ref = m->hk.lin_prepare(l->w, l->s, l->N, l->K); }
+int or_e2e_set_hooks(void* mp, const or_e2e_hooks* h) {
+  Model* m = (Model*)mp;
+  m->hk = *h;
+  if (!h->lin_prepare || !h->head_prepare) return -1;
+  for (int l = 0; l < m->NL; ++l) {
+    TLayer* t = &m->L[l];
+    hook_lin(m, &t->qkv); hook_lin(m, &t->o); hook_lin(m, &t->gu); hook_lin(m, &t->down);
+  }
+  if (m->D) {
+    for (int l = 0; l < m->DL; ++l) {
+      DLayer* t = &m->D[l];
+      hook_lin(m, &t->q); hook_lin(m, &t->o); hook_lin(m, &t->gu); hook_lin(m, &t->down);
+    }
+    hook_lin(m, &m->dpre); hook_lin(m, &m->dpost); hook_lin(m, &m->dcent);
+  }
+  m->head_ref = h->head_prepare(m->E, m->V, m->H, m->cb);
   return 0;
 }
 

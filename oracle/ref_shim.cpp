@@ -133,6 +133,46 @@ void ref_screen_1536(const uint8_t* W4, const uint16_t* S4, const float* coef, c
   }
 }
 
+// One int4 matrix (reference layout) prepared for the engine's dispatch: its Q4 descriptor and the
+// load-time W4A8 repack (w4a8::repack_tiles, as q4() does under ENGINE_DECODE_INT8, :175).
+struct RefLin { Q4 q; w4a8::Packed pk; };
+void* ref_lin_prepare(const uint8_t* W, const uint16_t* S, int N, int K) {
+  RefLin* r = new RefLin;
+  r->q.w = W; r->q.s = S; r->q.N = N; r->q.K = K;
+  w4a8::repack_alloc(N, K, r->pk);
+  w4a8::repack_tiles(W, S, N, K, r->pk, 0, N / 8);
+  r->q.p8 = &r->pk;
+  return r;
+}
+// Y = X W^T through the engine's lin1 (:310-317): W4A8 (i8_task) when i8 and M >= 2, else the float
+// W4G32 path (lin_task); with i8 at M = 1 (the synthetic drafter's int8 linears) i8_task over the
+// pool with one activation row.
+void ref_lin_run(void* h, const float* X, int M, float* Y, int i8) {
+  static XP xp;
+  RefLin* r = static_cast<RefLin*>(h);
+  xp.prep(X, r->q.K, M);
+  if (i8 && M == 1) {
+    w4a8::quant(X, 1, r->q.K, xp.xq);
+    xp.qdone = true;
+    I8Arg a; a.x = &xp; a.nj = 1; a.cum[0] = 0; a.q[0] = &r->q; a.y[0] = Y; a.cum[1] = r->q.N / 8;
+    POOL.run(i8_task, &a);
+    return;
+  }
+  G_I8_ACTIVE = i8 != 0;
+  lin1(xp, r->q, Y);
+  G_I8_ACTIVE = false;
+}
+// The packed exact head (bf16p::pack) and its logits for M <= 4 rows through head_task (:574-579).
+void* ref_head_prepare(const uint16_t* E, int N, int K, const uint8_t* cb8) {
+  bf16p::Packed* P = new bf16p::Packed;
+  bf16p::pack(E, N, K, cb8, *P);
+  return P;
+}
+void ref_head_run(void* h, const float* X, int M, float* Y) {
+  HeadArg ha; ha.P = static_cast<bf16p::Packed*>(h); ha.h = X; ha.logit = Y; ha.M = M;
+  POOL.run(head_task, &ha);
+}
+
 // gelu8 / exp8 on n values (gemma4_engine.cpp:43-60), 8 at a time (n a multiple of 8).
 void ref_gelu8(const float* x, int n, float* y) { for (int i = 0; i < n; i += 8) _mm256_storeu_ps(y + i, gelu8(_mm256_loadu_ps(x + i))); }
 void ref_exp8(const float* x, int n, float* y) { for (int i = 0; i < n; i += 8) _mm256_storeu_ps(y + i, exp8(_mm256_loadu_ps(x + i))); }

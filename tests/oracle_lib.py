@@ -51,9 +51,16 @@ _SIGS_ORACLE = {
     "or_e2e_forward": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "or_e2e_draft": (_I, [_P, _I, _P, _I, _I, _P, _P]),
     "or_e2e_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+    "or_e2e_generate_trace": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _I]),
+    "or_e2e_prefill": (_I, [_P, _P, _I, _P]),
+    "or_e2e_decode": (_I, [_P, _I, _I, _P, _P, _P, _P, _I]),
+    "or_e2e_set_state": (_I, [_P, _P, _P, _I, _P, _I, _P, _I]),
+    "or_e2e_set_hooks": (_I, [_P, _P]),
     "or_e2e_gen_bytes": (None, [ctypes.c_ulonglong, ctypes.c_ulonglong, ctypes.c_longlong, _P]),
     "or_e2e_fake_ctx": (None, [_P, _I]),
     "or_rmsnorm": (None, [_P, _P, _I, _I, _P, _I]),
+    "or_set_threads": (None, [_I]),
+    "or_get_threads": (_I, []),
 }
 
 _SIGS_REF = {
@@ -66,6 +73,10 @@ _SIGS_REF = {
     "ref_attn_splitkv": (None, [_P, _P, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
     "ref_screen_1536": (None, [_P, _P, _P, _P, _I, _P, _P, _P, _P, _I]),
     "ref_gelu8": (None, [_P, _I, _P]),
+    "ref_lin_prepare": (_P, [_P, _P, _I, _I]),
+    "ref_lin_run": (None, [_P, _P, _I, _P, _I]),
+    "ref_head_prepare": (_P, [_P, _I, _I, _P]),
+    "ref_head_run": (None, [_P, _P, _I, _P]),
     "ref_exp8": (None, [_P, _I, _P]),
 }
 
@@ -96,15 +107,18 @@ def oracle():
 REF_THREADS = 8
 
 
-def reference():
-    """The reference's own kernels (pool started with REF_THREADS threads), or None."""
+def reference(threads=None):
+    """The reference's own kernels, or None when oracle/_ref/libg4ref.so was not built.  The
+    reference's thread pool is started on first use with `threads` threads (default: G4_REF_THREADS
+    or REF_THREADS, the T = 8 that the parity fixtures use); it cannot be resized afterwards."""
     global _ref
     if _ref is None:
         path = ORACLE_DIR / "_ref" / "libg4ref.so"
         if not path.exists():
             return None
         _ref = _load(path, _SIGS_REF)
-        _ref.ref_pool_start(int(os.environ.get("G4_REF_THREADS", REF_THREADS)))
+        n = threads if threads else int(os.environ.get("G4_REF_THREADS", REF_THREADS))
+        _ref.pool_threads = _ref.ref_pool_start(int(n))
     return _ref
 
 
@@ -283,14 +297,59 @@ class OracleModel:
     def fake_ctx(self, n):
         oracle().or_e2e_fake_ctx(self.h, n)
 
-    def generate(self, prompt, n_new):
+    def generate(self, prompt, n_new, trace=False):
+        """run_req: prefill + decode.  With trace, also the per-round records
+        {nd, prompt lookup used, drafts[3] (-1 padded), nacc} as an [rounds, 6] array."""
         prompt = np.ascontiguousarray(prompt, np.int32)
         out = np.zeros(n_new + 8, np.int32)
         n_out = np.zeros(1, np.int32)
         st = np.zeros(8, np.int32)
-        oracle().or_e2e_generate(self.h, ptr(prompt), prompt.size, n_new, ptr(out), ptr(n_out), ptr(st))
+        cap = n_new + 8 if trace else 0
+        tr = np.full((max(cap, 1), 6), -1, np.int32)
+        oracle().or_e2e_generate_trace(self.h, ptr(prompt), prompt.size, n_new, ptr(out), ptr(n_out), ptr(st),
+                                       ptr(tr) if trace else None, cap)
+        stats = {"rounds": int(st[0]), "ngram_rounds": int(st[1]), "drafted": int(st[2]), "accepted": int(st[3])}
+        if trace:
+            return out[: n_out[0]].copy(), stats, tr[: stats["rounds"]].copy()
+        return out[: n_out[0]].copy(), stats
+
+    def prefill(self, prompt):
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        first = np.zeros(1, np.int32)
+        oracle().or_e2e_prefill(self.h, ptr(prompt), prompt.size, ptr(first))
+        return int(first[0])
+
+    def decode(self, max_rounds, max_tokens):
+        out = np.zeros(max(max_tokens, 1), np.int32)
+        n_out = np.zeros(1, np.int32)
+        st = np.zeros(8, np.int32)
+        oracle().or_e2e_decode(self.h, max_rounds, max_tokens, ptr(out), ptr(n_out), ptr(st), None, 0)
         return out[: n_out[0]].copy(), {"rounds": int(st[0]), "ngram_rounds": int(st[1]), "drafted": int(st[2]),
                                         "accepted": int(st[3])}
+
+    def set_state(self, Kc, Vc, seq, hprev, P):
+        """Decode state from another implementation's prefill: K/V [NL, npos, HD] bf16 bits, the
+        committed history, the last committed row's hidden and its position."""
+        Kc = np.ascontiguousarray(Kc, np.uint16)
+        Vc = np.ascontiguousarray(Vc, np.uint16)
+        seq = np.ascontiguousarray(seq, np.int32)
+        hprev = np.ascontiguousarray(hprev, np.float32)
+        rc = oracle().or_e2e_set_state(self.h, ptr(Kc), ptr(Vc), Kc.shape[1], ptr(seq), seq.size, ptr(hprev), int(P))
+        if rc:
+            raise RuntimeError("or_e2e_set_state rejected the state")
+
+    def use_reference_kernels(self):
+        """Route the linears, split-KV attention and exact head through the reference's own compiled
+        kernels (oracle/_ref/libg4ref.so, driven by its thread pool).  Returns False when that library
+        was not built."""
+        ref = reference()
+        if ref is None:
+            return False
+        hooks = (ctypes.c_void_p * 5)(*[ctypes.cast(getattr(ref, n), ctypes.c_void_p).value for n in
+                                        ("ref_lin_prepare", "ref_lin_run", "ref_attn_splitkv", "ref_head_prepare",
+                                         "ref_head_run")])
+        self._hooks = hooks
+        return oracle().or_e2e_set_hooks(self.h, ctypes.cast(hooks, ctypes.c_void_p)) == 0
 
 
 def gen_bytes(seed, tid, n):

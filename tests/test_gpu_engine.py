@@ -84,30 +84,68 @@ def test_generate_matches_oracle(pair):
     om, eng = pair
     prompt = make_prompt(5, 320, vocab=4096)
     tg, sg = eng.generate(prompt, 40)
-    to, so = om.generate(prompt, 40)
+    to, so, tro = om.generate(prompt, 40, trace=True)
     assert list(tg) == list(to)
     assert sg["rounds"] == so["rounds"] and sg["accepted"] == so["accepted"]
+    assert np.array_equal(eng.trace(), tro)
 
 
-@pytest.mark.parametrize("ngram,graphs", [(0, 1), (0, 0), (2, 0)])
-def test_generate_graph_replay_and_eager_agree_with_oracle(ngram, graphs):
-    """Decode rounds replayed from captured graphs (positions read on the device) and launched
-    eagerly give the oracle's tokens, with MTP drafts (ngram 0) and with prompt lookup."""
-    om = OracleModel(e2e_config(**SMALL, ngram=ngram))
-    eng = g4.Engine(g4.engine_config(**SMALL, ngram=ngram, graphs=graphs))
+# (ngram, graphs, decode_int8, vocab): MTP drafts (ngram 0) and prompt lookup; rounds replayed as one
+# loop graph with conditional nodes (graphs 1), as graphs of single passes launched from the host
+# (graphs 2) and eagerly (graphs 0); int8 and float (ENGINE_DECODE_INT8=0) verify passes; a vocab of
+# 16,384 gives 128 drafter centroids, so the drafter's top-32 selection is a real choice.
+CASES = [(0, 1, 1, 4096), (0, 0, 1, 4096), (2, 0, 1, 4096), (2, 2, 1, 4096), (2, 1, 0, 4096), (2, 0, 0, 4096),
+         (0, 1, 0, 4096), (0, 1, 1, 16384), (0, 0, 1, 16384), (2, 1, 1, 16384)]
+
+
+@pytest.mark.parametrize("ngram,graphs,decode_int8,vocab", CASES)
+def test_generate_agrees_with_oracle(ngram, graphs, decode_int8, vocab):
+    """Tokens, round counts and the per-round trace (drafts, acceptance) equal the oracle's."""
+    cfg = dict(SMALL, vocab=vocab, ngram=ngram, decode_int8=decode_int8)
+    om = OracleModel(e2e_config(**cfg))
+    eng = g4.Engine(g4.engine_config(**cfg, graphs=graphs))
     try:
-        prompt = make_prompt(6, 300, vocab=4096)
+        prompt = make_prompt(6, 300, vocab=vocab)
         tg, sg = eng.generate(prompt, 32)
-        to, so = om.generate(prompt, 32)
+        to, so, tro = om.generate(prompt, 32, trace=True)
         assert list(tg) == list(to)
         assert sg["rounds"] == so["rounds"] and sg["accepted"] == so["accepted"]
+        assert sg["ngram_rounds"] == so["ngram_rounds"] and sg["drafted"] == so["drafted"]
+        assert np.array_equal(eng.trace(), tro)
         assert sg["verify_passes"] == sg["rounds"] and sg["verify_rows"] >= sg["rounds"]
         if ngram == 0:
             assert sg["draft_steps"] == 3 * sg["rounds"] and sg["draft_gpu_ms"] > 0
-        assert sg["h2d_bytes"] > 0 and sg["d2h_bytes"] > 0
+        assert sg["d2h_bytes"] > 0 and sg["kernel_launches"] > sg["rounds"]
+        assert g4.device_status() == 0
     finally:
         eng.close()
         om.close()
+
+
+def test_decode_calls_resume_and_export_state():
+    """Decode in several calls (each one loop-graph launch) continues the same token stream as one
+    call, and the exported history is the prompt plus every committed token."""
+    cfg = dict(SMALL, ngram=0)
+    a = g4.Engine(g4.engine_config(**cfg))
+    b = g4.Engine(g4.engine_config(**cfg))
+    try:
+        prompt = make_prompt(8, 280, vocab=4096)
+        ta, _ = a.generate(prompt, 25)
+        first = b.prefill(prompt)
+        got = [first]
+        for _ in range(6):
+            out = np.zeros(64, np.int32)
+            n, _ = b.decode(2, 64, out)  # two rounds per call, every committed token returned
+            got += list(out[:n])
+        k = min(len(got), len(ta))
+        assert k >= 13 and got[:k] == list(ta[:k])
+        _, _, seq, h, P = b.export_state(0, kv=False)
+        assert list(seq[:280]) == list(prompt) and seq.size >= 281
+        assert P == seq.size - 2  # the last committed token is verified at the next round's first row
+        assert list(seq[280:280 + len(got)]) == got[: seq.size - 280]
+    finally:
+        a.close()
+        b.close()
 
 
 def test_fake_context_generate_matches_oracle():
@@ -126,17 +164,29 @@ def test_fake_context_generate_matches_oracle():
         om.close()
 
 
-def test_generate_cfg4_golden():
+@pytest.mark.parametrize("name", ["e2e_cfg4", "e2e_cfg4_float", "e2e_cfg4_ngram0"])
+def test_generate_cfg4_golden(name):
     """configs[4] at full size: the seeded 6,841-token prompt, 256 greedy tokens, against the
-    oracle's tokens and round statistics stored by tests/golden/make_golden_e2e.py."""
+    oracle's tokens, round statistics and per-round trace stored by tests/golden/make_golden_e2e.py:
+    the default engine (int8 verify passes, prompt lookup), ENGINE_DECODE_INT8=0 (float verify
+    passes, whose tokens must be bit-exact), and prompt lookup off (every round drafts 3 tokens with
+    the full-size MTP drafter, top 32 of 2,048 centroids, and verifies 4 rows)."""
     import pathlib
-    d = np.load(pathlib.Path(__file__).resolve().parent / "golden" / "e2e_cfg4.npz")
-    eng = g4.Engine(g4.engine_config())
+    path = pathlib.Path(__file__).resolve().parent / "golden" / f"{name}.npz"
+    if not path.exists():
+        pytest.skip(f"{path.name} not generated")
+    d = np.load(path)
+    kw = {}
+    if "decode_int8" in d:
+        kw = dict(decode_int8=int(d["decode_int8"]), ngram=int(d["ngram"]))
+    eng = g4.Engine(g4.engine_config(**kw))
     try:
         assert eng.cfg.seed == int(d["seed"])
         toks, st = eng.generate(d["prompt"], 256)
         assert list(toks) == list(d["tokens"])
         assert (st["rounds"], st["ngram_rounds"], st["accepted"]) == (int(d["rounds"]), int(d["ngram_rounds"]),
                                                                        int(d["accepted"]))
+        if "trace" in d:
+            assert np.array_equal(eng.trace(), d["trace"])
     finally:
         eng.close()

@@ -138,6 +138,14 @@ def test_full_pack_and_screen_build(full_head):
     assert np.array_equal(bits(screen[2].cpu().numpy()), bits(coef))
 
 
+def oracle_logits_full(head, H):
+    """The oracle's exact logits of H over every row of the head (OpenMP over rows)."""
+    N, K = head.N, head.K
+    packed = (head.data.cpu().numpy(), head.exc_ptr.cpu().numpy(),
+              head.exc_col.cpu().numpy()[:head.n_exc].view(np.uint16), head.exc_delta.cpu().numpy()[:head.n_exc])
+    return or_head_logits(packed, np.frombuffer(head.cb_host, np.uint8), N, K, np.ascontiguousarray(H, np.float32))
+
+
 def test_screen_random_rows_fall_back_to_exact_argmax(full_head):
     """configs[2] as specified: h ~ N(0,1)/sqrt(2048), M = 4.  Every row survives the bound, so the
     screen falls back to the full exact head, whose argmax must equal the oracle's."""
@@ -148,13 +156,9 @@ def test_screen_random_rows_fall_back_to_exact_argmax(full_head):
     idx, ns = idx.cpu().numpy(), ns.cpu().numpy()
     assert list(ns) == [-1, -1, -1, -1]
     Y = head.logits(dev(H)).cpu().numpy()
-    packed = (head.data.cpu().numpy(), head.exc_ptr.cpu().numpy(),
-              head.exc_col.cpu().numpy()[:head.n_exc].view(np.uint16), head.exc_delta.cpu().numpy()[:head.n_exc])
-    sub = slice(0, 32768)  # exact logits for a slice (the oracle dot over the full head is slow)
-    Yo = or_head_logits((packed[0][: 32768 * (K // 32) * 44], packed[1][: 32769], packed[2], packed[3]),
-                        np.frombuffer(head.cb_host, np.uint8), 32768, K, H)
-    assert np.array_equal(bits(Y[:, sub]), bits(Yo))
-    assert list(idx) == [or_pick(Y[m]) for m in range(4)]
+    Yo = oracle_logits_full(head, H)  # all 262,144 rows
+    assert np.array_equal(bits(Y), bits(Yo))
+    assert list(idx) == [or_pick(Yo[m]) for m in range(4)]
     assert list(g4.head_argmax(dev(Y)).cpu().numpy()) == list(idx)
 
 
@@ -172,7 +176,7 @@ def test_screen_planted_winners(full_head):
     H = np.stack(H)
     idx, ns = g4.head_screen(screen, head, dev(H))
     idx, ns = idx.cpu().numpy(), ns.cpu().numpy()
-    Y = head.logits(dev(H)).cpu().numpy()
+    Y = oracle_logits_full(head, H)  # the oracle's logits over all 262,144 rows
     survs = [or_screen_row(W4, S4, coef, H[m])[0] for m in range(2)]
     # the batch falls back as a whole when any row has more than lim survivors (as the reference
     # falls back for the whole verify group when any evaluated row overflows)
