@@ -5,6 +5,7 @@
 // synthetic dimensions.  Every kernel launch goes to the engine's stream.
 #include "g4_api.h"
 #include "g4_layers.cuh"
+#include "g4_stream.h"
 #include <algorithm>
 #include <chrono>
 #include <cmath>
@@ -249,6 +250,8 @@ struct g4_engine {
   // activations (M <= MMAX)
   int MMAX = 32;
   float *x, *a, *qkv, *att, *o, *gu, *act, *hbuf, *mlp_in, *qs;
+  float* x2 = nullptr;            // second residual-stream buffer of the segment kernels
+  unsigned* segbar = nullptr;     // grid-barrier counters of a pass's segment launches, then the abort flag
   int8_t* xq;
   float* xsx;
   int32_t* xsum;
@@ -301,6 +304,7 @@ extern "C" int g4_engine_default_config(g4_engine_config* c) {
   c->prefill_block = 32; c->k_draft = 3; c->ngram = 2; c->ngram_len = 3; c->prefill_int8 = 1; c->decode_int8 = 1;
   c->head_screen = 1; c->screen_lim = 30000; c->attn_chunks = 8; c->att_par = 192; c->drafter = 1; c->seed = 20261201ull;
   c->graphs = 1;
+  c->fused_layers = 1;
   return G4_OK;
 }
 
@@ -449,6 +453,8 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
   // activations
   const int MM = e->MMAX;
   int rc = ealloc_t(e, &e->x, (size_t)MM * H);
+  if (!rc) rc = ealloc_t(e, &e->x2, (size_t)MM * H);
+  if (!rc) rc = ealloc_t(e, &e->segbar, (size_t)4 * (c.n_layers + 2) + 1);
   if (!rc) rc = ealloc_t(e, &e->a, (size_t)MM * std::max(H, I));
   if (!rc) rc = ealloc_t(e, &e->qkv, (size_t)MM * (QD + 2 * d.HD));
   if (!rc) rc = ealloc_t(e, &e->att, (size_t)MM * QD);
@@ -562,12 +568,91 @@ static int lin(g4_engine* e, const Lin& w, const float* X, int M, float* Y, bool
 // once and replayed at every position.  Per layer: norm(+quant) -> qkv -> q/k norms, RoPE, KV
 // write -> attention(+quant) -> o -> residual + pre-MLP norm(+quant) -> gate/up -> GeGLU(+quant)
 // -> down -> residual + the next layer's input norm(+quant) (the final norm after the last layer).
+// The layer stack of a verify pass with persistent segment kernels (g4_stream.cu): segment 0 = the
+// embedding, layer 0's input norm, qkv projection and q/k/v post; then per layer its split-KV
+// attention (which quantises its output for the o projection) and segment l+1 = layer l's o, MLP and
+// residuals with the next layer's input norm, qkv and q/k/v post (or the final norm into hbuf).
+static bool fused_ok(const g4_engine* e, int M, int pos0, bool dyn) {
+  const ModelDims& d = e->d;
+  return e->cfg.fused_layers && i8_path(e, M, false) && M >= 2 && M <= 4 && (dyn || pos0 + M > e->cfg.att_par) &&
+         d.H == 2048 && d.I == 8192 && d.HD == 256 && d.NQ == 8 && !e->prof.on;
+}
+static int forward_layers_fused(g4_engine* e, int M, int pos0, bool dyn) {
+  const ModelDims& d = e->d;
+  if (!e->x2 || !e->segbar) return set_error(G4_ERR_INVALID, "segment kernels: buffers missing");
+  const int H = d.H, QD = d.NQ * d.HD;
+  const QuantOut qo = quant_out(e, M, false);
+  ECK(cudaMemsetAsync(e->segbar, 0, sizeof(unsigned) * (4 * (size_t)(d.NL + 2) + 1), e->st));
+  auto lin_of = [](const Lin& l) { return SegLin{l.w, l.s, l.N, l.K}; };
+  SegParams p = {};
+  p.M = M; p.H = H; p.I = d.I; p.QD = QD; p.HD = d.HD; p.NQ = d.NQ;
+  p.x_a = e->x; p.x_b = e->x2;
+  p.att_q = e->xq; p.att_sx = e->xsx; p.att_sum = e->xsum;
+  p.o_out = e->o; p.down_out = e->o;
+  p.act_q = e->xq; p.act_sx = e->xsx; p.act_sum = e->xsum;
+  p.hbuf = e->hbuf; p.qkv_out = e->qkv; p.qs = e->qs; p.ldq = QD;
+  p.dpos = dyn ? e->ctl : nullptr;
+  p.pos0 = dyn ? 1 : pos0;
+  p.E = e->E; p.toks = e->toks; p.sqrtH = sqrtf((float)H);
+  p.abort_flag = e->segbar + 4 * (size_t)(d.NL + 2);
+  auto set_next = [&](int l) {  // the qkv part of a segment: layer l
+    const TLayer& t = e->L[l];
+    const int ty = t.global ? 1 : 0;
+    p.do_qkv = 1;
+    p.qkv = lin_of(t.qkv);
+    p.w_next = t.in_ln;
+    p.qn = t.qn; p.kn = t.kn; p.cosT = e->rope[ty][0]; p.sinT = e->rope[ty][1];
+    p.Kc = e->Kc + (size_t)l * e->cfg.ctx_max * d.HD;
+    p.Vc = e->Vc + (size_t)l * e->cfg.ctx_max * d.HD;
+  };
+  p.do_mlp = 0;
+  set_next(0);
+  p.bar = e->segbar;
+  RCK(seg_launch(p, e->st));
+  for (int l = 0; l < d.NL; ++l) {
+    const TLayer& t = e->L[l];
+    const uint16_t* Kc = e->Kc + (size_t)l * e->cfg.ctx_max * d.HD;
+    const uint16_t* Vc = e->Vc + (size_t)l * e->cfg.ctx_max * d.HD;
+    if (dyn) {
+      const int max_len = t.global ? e->cfg.ctx_max : std::min(e->cfg.ctx_max, d.WINDOW + 4);
+      RCK(attn_splitkv_dev(Kc, Vc, e->qs, M, d.NQ, d.HD, e->ctl, 1, 1, t.global ? 0 : d.WINDOW, max_len,
+                           e->cfg.attn_chunks, e->att, e->attn_ws, e->attn_ws_bytes, e->st, qo, e->attn_cnt));
+    } else {
+      int pos[4], lo[4], kmin = 1 << 30;
+      for (int m = 0; m < M; ++m) {
+        pos[m] = pos0 + m;
+        lo[m] = t.global ? 0 : std::max(0, pos[m] - (d.WINDOW - 1));
+        kmin = std::min(kmin, lo[m]);
+      }
+      RCK(g4_attn_splitkv(Kc, Vc, e->qs, pos, lo, M, d.NQ, d.HD, kmin, pos0 + M - 1, e->cfg.attn_chunks, e->att, e->attn_ws,
+                          e->attn_ws_bytes, e->st));
+      RCK(g4_w4a8_quant(e->att, M, QD, e->xq, e->xsx, e->xsum, e->st));
+    }
+    p.do_mlp = 1;
+    p.o = lin_of(t.o); p.gu = lin_of(t.gu); p.down = lin_of(t.down);
+    p.w_post_attn = t.post_attn; p.w_pre_ff = t.pre_ff; p.w_post_ff = t.post_ff;
+    if (l + 1 < d.NL) {
+      set_next(l + 1);
+    } else {
+      p.do_qkv = 0;
+      p.w_next = e->fnorm;
+    }
+    p.bar = e->segbar + 4 * (size_t)(l + 1);
+    RCK(seg_launch(p, e->st));
+  }
+  return check_launch("segment layers");
+}
+
 static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = false) {
   const ModelDims& d = e->d;
   const int H = d.H, QD = d.NQ * d.HD, ld = QD + 2 * d.HD;
   const float sqrtH = sqrtf((float)H);
   PhaseTimer& pf = e->prof;
   const QuantOut qo = quant_out(e, M, false);
+  if (fused_ok(e, M, pos0, dyn)) {
+    RCK(forward_layers_fused(e, M, pos0, dyn));
+    goto head;
+  }
   pf.mark(e->st, PH_EMBED_NORM);
   RCK(launch("k_embed", k_embed, dim3(M), dim3(256), 0, e->st, e->E, e->toks, H, sqrtH, e->x));
   RCK(launch("k_norm_q", k_norm_q, dim3(M), dim3(256), 0, e->st, e->x, e->L[0].in_ln, H, e->a, 0, qo));
@@ -633,6 +718,7 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
                                            QuantOut{nullptr, nullptr, nullptr}));
     RCK(check_launch("layer"));
   }
+head:
   pf.mark(e->st, PH_HEAD);
   if (!want) return G4_OK;
   // head in groups of 4 rows (:1500)

@@ -195,6 +195,10 @@ typedef struct {
   unsigned long long seed;           /* weight seed */
   int graphs;                        /* decode rounds as CUDA graphs with programmatic dependent
                                         launch (1), graphs with ordinary launches (2), eager (0) */
+  int fused_layers;                  /* verify passes on the int8 path (M = 2..4 rows past att_par)
+                                        run each layer's o, gate/up, down and the next qkv projection
+                                        with their norms in one persistent kernel (1), or as one
+                                        kernel per step (0) */
 } g4_engine_config;
 typedef struct {
   int rounds, ngram_rounds, drafted, accepted, prefill_tokens, decode_tokens;
