@@ -252,6 +252,7 @@ struct g4_engine {
   float *x, *a, *qkv, *att, *o, *gu, *act, *hbuf, *mlp_in, *qs;
   float* x2 = nullptr;            // second residual-stream buffer of the segment kernels
   unsigned* segbar = nullptr;     // grid-barrier counters of a pass's segment launches, then the abort flag
+  unsigned long long* segtrace = nullptr;  // stage timestamps of the last pass's segment launches
   int8_t* xq;
   float* xsx;
   int32_t* xsum;
@@ -304,7 +305,7 @@ extern "C" int g4_engine_default_config(g4_engine_config* c) {
   c->prefill_block = 32; c->k_draft = 3; c->ngram = 2; c->ngram_len = 3; c->prefill_int8 = 1; c->decode_int8 = 1;
   c->head_screen = 1; c->screen_lim = 30000; c->attn_chunks = 8; c->att_par = 192; c->drafter = 1; c->seed = 20261201ull;
   c->graphs = 1;
-  c->fused_layers = 1;
+  c->fused_layers = 0;
   return G4_OK;
 }
 
@@ -455,6 +456,7 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
   int rc = ealloc_t(e, &e->x, (size_t)MM * H);
   if (!rc) rc = ealloc_t(e, &e->x2, (size_t)MM * H);
   if (!rc) rc = ealloc_t(e, &e->segbar, (size_t)4 * (c.n_layers + 2) + 1);
+  if (!rc) rc = ealloc_t(e, &e->segtrace, (size_t)(c.n_layers + 2) * 2 * kSegStamps);
   if (!rc) rc = ealloc_t(e, &e->a, (size_t)MM * std::max(H, I));
   if (!rc) rc = ealloc_t(e, &e->qkv, (size_t)MM * (QD + 2 * d.HD));
   if (!rc) rc = ealloc_t(e, &e->att, (size_t)MM * QD);
@@ -595,6 +597,7 @@ static int forward_layers_fused(g4_engine* e, int M, int pos0, bool dyn) {
   p.pos0 = dyn ? 1 : pos0;
   p.E = e->E; p.toks = e->toks; p.sqrtH = sqrtf((float)H);
   p.abort_flag = e->segbar + 4 * (size_t)(d.NL + 2);
+  p.trace = e->segtrace;
   auto set_next = [&](int l) {  // the qkv part of a segment: layer l
     const TLayer& t = e->L[l];
     const int ty = t.global ? 1 : 0;
@@ -608,6 +611,7 @@ static int forward_layers_fused(g4_engine* e, int M, int pos0, bool dyn) {
   p.do_mlp = 0;
   set_next(0);
   p.bar = e->segbar;
+  p.trace_slot = 0;
   RCK(seg_launch(p, e->st));
   for (int l = 0; l < d.NL; ++l) {
     const TLayer& t = e->L[l];
@@ -638,6 +642,7 @@ static int forward_layers_fused(g4_engine* e, int M, int pos0, bool dyn) {
       p.w_next = e->fnorm;
     }
     p.bar = e->segbar + 4 * (size_t)(l + 1);
+    p.trace_slot = l + 1;
     RCK(seg_launch(p, e->st));
   }
   return check_launch("segment layers");
@@ -1213,6 +1218,18 @@ extern "C" int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, in
   *n_out = n;
   if (stats) *stats = e->stats;
   return rc0;
+}
+
+// Stage timestamps of the last verify pass's segment kernels (see g4.h).
+extern "C" int g4_engine_seg_trace(g4_engine* e, unsigned long long* out, int cap, int* n) {
+  G4_REQUIRE(e && n && cap >= 0 && (out || cap == 0), "g4_engine_seg_trace: bad arguments");
+  const int total = (e->d.NL + 2) * 2 * kSegStamps;
+  *n = total;
+  if (cap > 0) {
+    ECK(cudaStreamSynchronize(e->st));
+    ECK(cudaMemcpy(out, e->segtrace, sizeof(unsigned long long) * std::min(cap, total), cudaMemcpyDeviceToHost));
+  }
+  return G4_OK;
 }
 
 // Per-round records since the prefill: {nd, prompt lookup used, drafts[3] (-1 padded), nacc}.

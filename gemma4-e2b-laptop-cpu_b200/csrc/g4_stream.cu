@@ -36,9 +36,8 @@ constexpr int kSegThreads = kSegConsumers + 32;
 constexpr int kSegRowPad = 16;                                   // bytes after each weight row in a slot
 constexpr int kSegScaleOff = 16 * (1024 + kSegRowPad);          // 16 rows of K = 2048 (4 rows of 8192 fit too)
 constexpr int kSegSlot = kSegScaleOff + 2048;                   // 18,688 bytes
-constexpr int kSegNS = 6;                                       // ring slots
+constexpr int kSegNS = 5;                                       // ring slots
 constexpr int kSegKmax = 8192;
-constexpr int kSegRow = 2048;                                   // hidden width handled by the prologues
 
 // Tile geometry of one matrix: rows per tile R (16 for K = 2048, 4 for K = 8192), tiles grouped in
 // units that stay on one CTA (4 for the gate/up pair: gate rows 32u..32u+31 and the same up rows).
@@ -97,7 +96,6 @@ __device__ bool grid_barrier(unsigned* ctr, unsigned* abort_flag, unsigned G, bo
       if (v >= G) break;
       asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(ab) : "l"(abort_flag) : "memory");
       if (ab != 0u || globaltimer() - t0 > kWaitLimitNs) { ok = false; break; }
-      __nanosleep(64);
     }
     if (!ok) {
       sh.flag = 1;
@@ -110,14 +108,65 @@ __device__ bool grid_barrier(unsigned* ctr, unsigned* abort_flag, unsigned G, bo
   return ok_s != 0;
 }
 
-// ------------------------------------------------------------------------- rows in registers
-// Thread t (< 256) owns float4 blocks t and t + 256 of each of the M rows (elements 4f..4f+3).
-template <int M>
-struct Rows {
-  float4 v[M][2];
-};
+// ---------------------------------------------------------------------------- row prologues
+// The norm prologues work on M <= 4 rows of H = 2048 floats in shared memory; thread t (< 256) owns
+// float4 blocks t and t + 256 of every row.  Each helper is compiled once (not inlined) and loops
+// over the rows, so that the code a launch runs once stays small: a launch runs on every SM once,
+// and each new line of code is an instruction-cache miss.
+constexpr int kH = 2048;
 
-// Exponent keys for the exactness test (see rows_rms): bytes (kmax, 255 - kmin) of the nonzero
+__device__ __forceinline__ float4 r16x4(float4 a) { return make_float4(r16(a.x), r16(a.y), r16(a.z), r16(a.w)); }
+// (a * r) * w per element
+__device__ __forceinline__ float4 scale4(float4 a, float r, float4 w) {
+  return make_float4(__fmul_rn(__fmul_rn(a.x, r), w.x), __fmul_rn(__fmul_rn(a.y, r), w.y),
+                     __fmul_rn(__fmul_rn(a.z, r), w.z), __fmul_rn(__fmul_rn(a.w, r), w.w));
+}
+// r16(x + r16((o * r) * w)) per element
+__device__ __forceinline__ float4 resid4(float4 x, float4 o, float r, float4 w) {
+  const float4 u = r16x4(scale4(o, r, w));
+  return r16x4(make_float4(__fadd_rn(x.x, u.x), __fadd_rn(x.y, u.y), __fadd_rn(x.z, u.z), __fadd_rn(x.w, u.w)));
+}
+
+// rows [M][kH] from global memory (written earlier in this pass: read through L2), optionally
+// rounded to bf16, into shared memory; all 2M loads are in flight before the first store.
+__device__ __noinline__ void seg_load_rows(float* dst, const float* src, int M, int round) {
+  const int t = threadIdx.x;
+  float4 v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < 2 * M) v[i] = ldcg4(src + (size_t)(i >> 1) * kH + 4 * (t + 256 * (i & 1)));
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < 2 * M) reinterpret_cast<float4*>(dst + (size_t)(i >> 1) * kH)[t + 256 * (i & 1)] = round ? r16x4(v[i]) : v[i];
+}
+
+// rows [M][kH] from shared memory to global memory
+__device__ __noinline__ void seg_store_rows(float* dst, const float* src, int M) {
+  const int t = threadIdx.x;
+  for (int i = 0; i < 2 * M; ++i)
+    reinterpret_cast<float4*>(dst + (size_t)(i >> 1) * kH)[t + 256 * (i & 1)] =
+        reinterpret_cast<const float4*>(src + (size_t)(i >> 1) * kH)[t + 256 * (i & 1)];
+}
+
+// x = r16(E[tok] * sqrt(H)) for the M tokens (:1264)
+__device__ __noinline__ void seg_embed(float* dst, const uint16_t* E, const int* toks, int M, float sqrtH) {
+  const int t = threadIdx.x;
+  uint2 b[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < 2 * M) {
+      const uint16_t* er = E + (size_t)__ldcg(toks + (i >> 1)) * kH;
+      b[i] = __ldg(reinterpret_cast<const uint2*>(er) + t + 256 * (i & 1));
+    }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < 2 * M)
+      reinterpret_cast<float4*>(dst + (size_t)(i >> 1) * kH)[t + 256 * (i & 1)] =
+          make_float4(r16(__fmul_rn(bf2f(b[i].x & 0xFFFFu), sqrtH)), r16(__fmul_rn(bf2f(b[i].x >> 16), sqrtH)),
+                      r16(__fmul_rn(bf2f(b[i].y & 0xFFFFu), sqrtH)), r16(__fmul_rn(bf2f(b[i].y >> 16), sqrtH)));
+}
+
+// Exponent keys for the exactness test (see seg_rms): bytes (kmax, 255 - kmin) of the nonzero
 // elements' biased exponents; a value that is not bf16-valued or not finite fails the test.
 __device__ __forceinline__ uint32_t seg_ekeys(float x) {
   const uint32_t b = __float_as_uint(x) & 0x7FFFFFFFu;
@@ -126,29 +175,29 @@ __device__ __forceinline__ uint32_t seg_ekeys(float x) {
   return b == 0u ? 0u : key;
 }
 
-// RMS scales of M rows of n (<= 2048) elements in the reference's order (ss_avx2, :326-343): per
-// row the sum of squares in double over 16 partials (element j to partial j % 16, each in element
-// order), combined ((p_b + p_4+b) + (p_8+b + p_12+b)), then (t0 + t2) + (t1 + t3);
+// RMS scales sh.r[m] of the M rows in shared memory, in the reference's order (ss_avx2,
+// :326-343): per row the sum of squares in double over 16 partials (element j to partial j % 16,
+// each in element order), combined ((p_b + p_4+b) + (p_8+b + p_12+b)), then (t0 + t2) + (t1 + t3);
 // r = 1 / sqrtf((float)(ss / n) + 1e-6).  A partial whose elements are bf16-valued with nonzero
 // exponents spanning at most 15 is an exact sum in double in any order (every square is a multiple
 // of 2^(2 e_min - 268) and 128 of them stay below 2^53 such units), so it is summed as a tree;
-// any other partial runs the sequential chain over xs (the rows in shared memory, stride n).
-template <int M>
-__device__ void rows_rms(const Rows<M>& rw, const float* xs, int n, SegShared& sh, float (&r)[M]) {
-  const int t = threadIdx.x, lane = t & 31, w = t >> 5, nf = n >> 2;
-#pragma unroll
+// any other partial runs the sequential chain.
+__device__ __noinline__ void seg_rms(const float* rows, int M, SegShared& sh) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+#pragma unroll 1
   for (int m = 0; m < M; ++m) {
-    double d[4] = {0.0, 0.0, 0.0, 0.0};
+    const float4 v0 = reinterpret_cast<const float4*>(rows + (size_t)m * kH)[t];
+    const float4 v1 = reinterpret_cast<const float4*>(rows + (size_t)m * kH)[t + 256];
+    const float c[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    double d[4];
     uint32_t k01 = 0u, k23 = 0u;
 #pragma unroll
-    for (int k = 0; k < 2; ++k)
-      if (t + 256 * k < nf) {
-        const float c[4] = {rw.v[m][k].x, rw.v[m][k].y, rw.v[m][k].z, rw.v[m][k].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) { const double x = c[e]; d[e] = fma(x, x, d[e]); }
-        k01 = __vmaxu4(k01, seg_ekeys(c[0]) | (seg_ekeys(c[1]) << 16));
-        k23 = __vmaxu4(k23, seg_ekeys(c[2]) | (seg_ekeys(c[3]) << 16));
-      }
+    for (int e = 0; e < 4; ++e) {
+      const double a = c[e], b = c[4 + e];
+      d[e] = fma(b, b, a * a);  // element order within the thread: block t, then block t + 256
+    }
+    k01 = __vmaxu4(seg_ekeys(c[0]) | (seg_ekeys(c[1]) << 16), seg_ekeys(c[4]) | (seg_ekeys(c[5]) << 16));
+    k23 = __vmaxu4(seg_ekeys(c[2]) | (seg_ekeys(c[3]) << 16), seg_ekeys(c[6]) | (seg_ekeys(c[7]) << 16));
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
 #pragma unroll
@@ -166,45 +215,51 @@ __device__ void rows_rms(const Rows<M>& rw, const float* xs, int n, SegShared& s
   consumer_sync();
   if (t < 16 * M) {
     const int m = t >> 4, p = t & 15;
-    double p8[8];
+    double s = 0.0;
     uint32_t kw = 0u;
 #pragma unroll
     for (int ww = 0; ww < 8; ++ww) {
-      p8[ww] = sh.part[ww][m][p];
+      s += sh.part[ww][m][p];
       kw = __vmaxu4(kw, sh.keys[ww][m][p >> 1]);
     }
-    double s = ((p8[0] + p8[1]) + (p8[2] + p8[3])) + ((p8[4] + p8[5]) + (p8[6] + p8[7]));
     const uint32_t kk = (kw >> (16 * (p & 1))) & 0xFFFFu;
     const int kmax = (int)(kk >> 8), kmin = 255 - (int)(kk & 0xFFu);
-    if (kmax - kmin > 15) {
+    if (kmax - kmin > 15) {  // the chain in element order, 8 loads in flight ahead of it
       s = 0.0;
-      const float* xr = xs + (size_t)m * n;
-      for (int i = p; i < n; i += 16) { const double x = xr[i]; s = fma(x, x, s); }
+      const float* xr = rows + (size_t)m * kH;
+#pragma unroll 1
+      for (int i = p; i < kH; i += 128) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = xr[i + 16 * u];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) { const double x = v[u]; s = fma(x, x, s); }
+      }
     }
     sh.chain[m][p] = s;
   }
   consumer_sync();
-#pragma unroll
-  for (int m = 0; m < M; ++m) {
+  if (t < M) {
     double tb[4];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) tb[b] = (sh.chain[m][b] + sh.chain[m][4 + b]) + (sh.chain[m][8 + b] + sh.chain[m][12 + b]);
+    for (int b = 0; b < 4; ++b) tb[b] = (sh.chain[t][b] + sh.chain[t][4 + b]) + (sh.chain[t][8 + b] + sh.chain[t][12 + b]);
     const double ss = (tb[0] + tb[2]) + (tb[1] + tb[3]);
-    const double mean = (n & (n - 1)) == 0 ? ss * (1.0 / (double)n) : ss / (double)n;
-    r[m] = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)mean, 1e-6f)));
+    sh.r[t] = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)(ss * (1.0 / (double)kH)), 1e-6f)));  // kH a power of two
   }
+  consumer_sync();
 }
 
-__device__ __forceinline__ float4 r16x4(float4 a) { return make_float4(r16(a.x), r16(a.y), r16(a.z), r16(a.w)); }
-// (a * r) * w per element
-__device__ __forceinline__ float4 scale4(float4 a, float r, float4 w) {
-  return make_float4(__fmul_rn(__fmul_rn(a.x, r), w.x), __fmul_rn(__fmul_rn(a.y, r), w.y),
-                     __fmul_rn(__fmul_rn(a.z, r), w.z), __fmul_rn(__fmul_rn(a.w, r), w.w));
-}
-// r16(x + r16((o * r) * w)) per element
-__device__ __forceinline__ float4 resid4(float4 x, float4 o, float r, float4 w) {
-  const float4 u = r16x4(scale4(o, r, w));
-  return r16x4(make_float4(__fadd_rn(x.x, u.x), __fadd_rn(x.y, u.y), __fadd_rn(x.z, u.z), __fadd_rn(x.w, u.w)));
+// x = r16(x + r16((o * r_m) * w)) for the M rows in shared memory (r from seg_rms of o)
+__device__ __noinline__ void seg_resid(float* x, const float* o, float4 w0, float4 w1, int M, const SegShared& sh) {
+  const int t = threadIdx.x;
+#pragma unroll 1
+  for (int m = 0; m < M; ++m) {
+    const float r = sh.r[m];
+    float4* xm = reinterpret_cast<float4*>(x + (size_t)m * kH);
+    const float4* om = reinterpret_cast<const float4*>(o + (size_t)m * kH);
+    xm[t] = resid4(xm[t], om[t], r, w0);
+    xm[t + 256] = resid4(xm[t + 256], om[t + 256], r, w1);
+  }
 }
 
 // w4a8::quant of the float4 block f of row m into shared memory: a 32-group is the 8 consecutive
@@ -236,46 +291,39 @@ __device__ __forceinline__ void quant4_smem(float4 y, int f, int m, int8_t* q, i
   }
 }
 
+// y = (x * r_m) * w (rounded to bf16 when round) for the M rows: to out (global, when not NULL) or
+// quantised into the stage's int8 activations q / sx / sm (stride kH + 16).
+__device__ __noinline__ void seg_scale(const float* x, float4 w0, float4 w1, int M, int round, const SegShared& sh, int8_t* q,
+                                       float* sx, int32_t* sm, float* out) {
+  const int t = threadIdx.x;
+#pragma unroll 1
+  for (int m = 0; m < M; ++m) {
+    const float r = sh.r[m];
+    const float4* xm = reinterpret_cast<const float4*>(x + (size_t)m * kH);
+    float4 y0 = scale4(xm[t], r, w0), y1 = scale4(xm[t + 256], r, w1);
+    if (round) { y0 = r16x4(y0); y1 = r16x4(y1); }
+    if (out) {
+      reinterpret_cast<float4*>(out + (size_t)m * kH)[t] = y0;
+      reinterpret_cast<float4*>(out + (size_t)m * kH)[t + 256] = y1;
+    } else {
+      quant4_smem(y0, t, m, q, kH + 16, sx, sm);
+      quant4_smem(y1, t + 256, m, q, kH + 16, sx, sm);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------ kernel
 struct SegSmem {
   uint8_t* slots;   // kSegNS x kSegSlot
   int8_t* q;        // [M][K + 16] int8 activations
   float* sx;        // [M][256]
   int32_t* sm;      // [M][256]
-  float* rows;      // [M][2048] rows for the RMS chains
-  float* gub;       // [8 teams][M][16] gate/up outputs of a round
+  int* ac;          // phase-1 integer dots of a round (kSegAcBytes)
+  float* ra;        // [M][2048] prologue rows A and B (alias ac: used only between GEMV stages)
+  float* rb;
+  uint16_t* scl;    // the round's tile scales (kSegSclBytes)
+  float* gub;       // [8 tiles][4][16] gate/up outputs of a round
 };
-
-// One team's chain rows: thread j -> (tile row r = j % R, activation row m = j / R).
-template <int M>
-__device__ __forceinline__ float tile_chain(const uint8_t* slot, int K, int R, int r, int m, const SegSmem& S) {
-  const int G = K >> 5;
-  const int rs = (K >> 1) + kSegRowPad;
-  const uint8_t* wrow = slot + (size_t)r * rs;
-  const uint16_t* srow = reinterpret_cast<const uint16_t*>(slot + kSegScaleOff) + (size_t)r * G;
-  const int8_t* xq = S.q + (size_t)m * (K + 16);
-  const float* sxm = S.sx + m * 256;
-  const int32_t* smm = S.sm + m * 256;
-  float row = 0.f;
-#pragma unroll 4
-  for (int g = 0; g < G; ++g) {
-    const uint4 wv = *reinterpret_cast<const uint4*>(wrow + (size_t)g * 16);
-    const int4 qa = *reinterpret_cast<const int4*>(xq + (size_t)g * 32);
-    const int4 qb = *reinterpret_cast<const int4*>(xq + (size_t)g * 32 + 16);
-    int a0 = -8 * smm[g], a1 = 0;
-    a0 = __dp4a((int)(wv.x & 0x0F0F0F0Fu), qa.x, a0);
-    a1 = __dp4a((int)(wv.y & 0x0F0F0F0Fu), qa.y, a1);
-    a0 = __dp4a((int)(wv.z & 0x0F0F0F0Fu), qa.z, a0);
-    a1 = __dp4a((int)(wv.w & 0x0F0F0F0Fu), qa.w, a1);
-    a0 = __dp4a((int)((wv.x >> 4) & 0x0F0F0F0Fu), qb.x, a0);
-    a1 = __dp4a((int)((wv.y >> 4) & 0x0F0F0F0Fu), qb.y, a1);
-    a0 = __dp4a((int)((wv.z >> 4) & 0x0F0F0F0Fu), qb.z, a0);
-    a1 = __dp4a((int)((wv.w >> 4) & 0x0F0F0F0Fu), qb.w, a1);
-    const float s = __fmul_rn(bf2f(srow[g]), sxm[g]);
-    row = fmaf((float)(a0 + a1), s, row);  // the integer dot is exact in any order
-  }
-  return row;
-}
 
 // Load the int8 activations [M][K] (+ scales, sums) of a stage from global memory (written earlier
 // in this pass by other CTAs or kernels) into shared memory.
@@ -295,56 +343,117 @@ __device__ void load_act(const int8_t* q, const float* sx, const int32_t* sm, in
   }
 }
 
-// Wait for a ring slot to fill (team-wide poll, bounded).
-__device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity) {
-  return mbar_wait(bar, parity);
-}
+// A GEMV stage over this CTA's tiles of one matrix, in rounds of up to kSegRoundTiles(M) tiles:
+//   phase 1 (all 256 threads): as each tile lands, thread (group g, row subset) computes the exact
+//     integer dots a32 = sum t*xq - 8*sum of its rows for all M activation rows into ac, and the
+//     tile's bf16 scales are copied out; the ring slot is then freed;
+//   phase 2: one thread per (tile, row, activation row) runs the fp32 chain
+//     row = fma(float(a32), sw*sx, row) over the groups in order.
+// Output rows go to Y (or, for the gate/up pair, to the GeGLU of the round's units, whose int8
+// quantisation is written to aq / asx / asum).
+constexpr int kSegAcBytes = 68 * 1024;   // 4 or 8 tiles x 16 x 4 or 2 rows x 68 ints
+constexpr int kSegSclBytes = 18 * 1024;  // 8 tiles x 16 rows x 72 bf16
+template <int M>
+__device__ __forceinline__ int seg_round_tiles() { return M == 2 ? 8 : 4; }
 
 template <int M>
-__device__ bool gemv_stage(const SegMatDev& mt, int stage_tiles_base, int& ring, float* Y, int ldy, int half_rows,
-                           const SegSmem& S, SegShared& sh, bool geglu, int8_t* aq, float* asx, int32_t* asum) {
+__device__ __noinline__ bool gemv_stage(const SegMatDev mt, int ring, float* Y, int ldy, int half_rows, const SegSmem S,
+                                        SegShared& sh, bool geglu, int8_t* aq, float* asx, int32_t* asum) {
   const int G = gridDim.x, c = blockIdx.x, t = threadIdx.x;
-  constexpr int MT = M == 3 ? 4 : M;  // team slots per tile row (teams stay warp-aligned)
-  const int R = mt.R, tsz = R * MT;
-  const int nteams = kSegConsumers / tsz;
-  const int team = t / tsz, j = t % tsz, r = j % R, m = j / R;
+  constexpr int MT = M == 3 ? 4 : M;
+  const int R = mt.R, K = mt.K, NG = K >> 5;
+  const int acs = NG + 4;                 // ac row stride (ints): 16-byte pad, bank-spread rows
+  const int scs = NG + 8;                 // scale row stride (bf16)
+  const int RS = kSegConsumers / NG;      // row subsets in phase 1 (4 for K = 2048, 1 for 8192)
+  const int ntr = seg_round_tiles<M>();
   const int nunits = seg_units(mt, c, G);
-  const int ntl = nunits * mt.tpu;  // this CTA's tiles of the stage, in ring order
+  const int ntl = nunits * mt.tpu;
+  // phase-1 role: group g, rows rsub, rsub + RS, ...; its activations stay in registers all stage
+  const int g = t % NG, rsub = t / NG;
+  int4 qa[M], qb[M];
+  int bias[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    qa[m] = *reinterpret_cast<const int4*>(S.q + (size_t)m * (K + 16) + (size_t)g * 32);
+    qb[m] = *reinterpret_cast<const int4*>(S.q + (size_t)m * (K + 16) + (size_t)g * 32 + 16);
+    bias[m] = -8 * S.sm[m * 256 + g];
+  }
   bool ok = true;
-  for (int base = 0; base < ntl; base += nteams) {
-    const int i = base + team;  // the team's tile in this round
-    float val = 0.f;
-    int n0 = -1;
-    if (team < nteams && i < ntl) {
+  for (int base = 0; base < ntl; base += ntr) {
+    const int nt = min(ntr, ntl - base);
+    for (int ti = 0; ti < nt; ++ti) {
+      const int i = base + ti;
       const int slot = (ring + i) % kSegNS;
-      const uint32_t par = (uint32_t)(((ring + i) / kSegNS) & 1);
-      if (!slot_wait(&sh.full[slot], par)) ok = false;
-      const int u = seg_unit(mt, c, G, i / mt.tpu), tj = i % mt.tpu;
-      n0 = seg_tile_row(mt, u, tj, half_rows);
-      if (ok && m < M) val = tile_chain<M>(S.slots + (size_t)slot * kSegSlot, mt.K, R, r, m, S);
-      // the team has read its slot: one elected thread frees it
-      if (tsz >= 32) {
-        asm volatile("bar.sync %0, %1;" ::"r"(2 + team), "r"(tsz) : "memory");
-        if (j == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sh.empty[slot])) : "memory");
-      } else {
-        const unsigned mask = ((1u << tsz) - 1u) << (t & 31 & ~(tsz - 1));
-        __syncwarp(mask);
-        if (j == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sh.empty[slot])) : "memory");
+      if (!mbar_wait(&sh.full[slot], (uint32_t)(((ring + i) / kSegNS) & 1))) ok = false;
+      const uint8_t* sb = S.slots + (size_t)slot * kSegSlot;
+      if (ok) {
+        for (int r = rsub; r < R; r += RS) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(sb + (size_t)r * ((K >> 1) + kSegRowPad) + (size_t)g * 16);
+          const uint32_t lo0 = wv.x & 0x0F0F0F0Fu, lo1 = wv.y & 0x0F0F0F0Fu, lo2 = wv.z & 0x0F0F0F0Fu, lo3 = wv.w & 0x0F0F0F0Fu;
+          const uint32_t hi0 = (wv.x >> 4) & 0x0F0F0F0Fu, hi1 = (wv.y >> 4) & 0x0F0F0F0Fu, hi2 = (wv.z >> 4) & 0x0F0F0F0Fu,
+                         hi3 = (wv.w >> 4) & 0x0F0F0F0Fu;
+          int* acr = S.ac + ((size_t)(ti * R + r) * MT) * acs + g;
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            int a0 = bias[m], a1 = 0;  // the integer dot is exact in any order
+            a0 = __dp4a((int)lo0, qa[m].x, a0);
+            a1 = __dp4a((int)lo1, qa[m].y, a1);
+            a0 = __dp4a((int)lo2, qa[m].z, a0);
+            a1 = __dp4a((int)lo3, qa[m].w, a1);
+            a0 = __dp4a((int)hi0, qb[m].x, a0);
+            a1 = __dp4a((int)hi1, qb[m].y, a1);
+            a0 = __dp4a((int)hi2, qb[m].z, a0);
+            a1 = __dp4a((int)hi3, qb[m].w, a1);
+            acr[(size_t)m * acs] = a0 + a1;
+          }
+        }
+        // the tile's scales, to a bank-spread copy
+        const int cpr = NG >> 3;  // 16-byte chunks per scale row
+        if (t < R * cpr) {
+          const int rr = t / cpr, ch = t % cpr;
+          *reinterpret_cast<uint4*>(S.scl + (size_t)(ti * R + rr) * scs + ch * 8) =
+              *reinterpret_cast<const uint4*>(sb + kSegScaleOff + (size_t)rr * NG * 2 + ch * 16);
+        }
       }
-      if (!geglu && ok && m < M) Y[(size_t)m * ldy + n0 + r] = val;
-      if (geglu && m < M) S.gub[((size_t)team * 4 + m) * 16 + r] = val;
+      consumer_sync();  // every thread is done with the slot
+      if (t == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&sh.empty[slot])) : "memory");
     }
-    if (geglu) {
-      // GeGLU of the round's units (teams 4k..4k+3 hold gate rows 0-15, 16-31, up rows 0-15,
-      // 16-31 of one unit): act = r16(r16(gelu(r16 g)) * r16 u), then the 32-group quantisation
-      consumer_sync();
+    // phase 2: chain (tile ti, activation row m, row r), r fastest
+    const int per_tile = R * M;
+    if (ok && t < nt * per_tile) {
+      const int ti = t / per_tile, rem = t % per_tile, r = rem % R, m = rem / R;
+      const int* acr = S.ac + ((size_t)(ti * R + r) * MT + m) * acs;
+      const uint16_t* scr = S.scl + (size_t)(ti * R + r) * scs;
+      const float* sxm = S.sx + m * 256;
+      float row = 0.f;
+#pragma unroll 2
+      for (int g8 = 0; g8 < NG; g8 += 8) {
+        const int4 a_lo = *reinterpret_cast<const int4*>(acr + g8), a_hi = *reinterpret_cast<const int4*>(acr + g8 + 4);
+        const uint4 s8 = *reinterpret_cast<const uint4*>(scr + g8);
+        const float4 x_lo = *reinterpret_cast<const float4*>(sxm + g8), x_hi = *reinterpret_cast<const float4*>(sxm + g8 + 4);
+        const int av[8] = {a_lo.x, a_lo.y, a_lo.z, a_lo.w, a_hi.x, a_hi.y, a_hi.z, a_hi.w};
+        const uint32_t sw[4] = {s8.x, s8.y, s8.z, s8.w};
+        const float xv[8] = {x_lo.x, x_lo.y, x_lo.z, x_lo.w, x_hi.x, x_hi.y, x_hi.z, x_hi.w};
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint32_t b = (u & 1) ? (sw[u >> 1] >> 16) : (sw[u >> 1] & 0xFFFFu);
+          row = fmaf((float)av[u], __fmul_rn(bf2f(b), xv[u]), row);
+        }
+      }
+      const int u = seg_unit(mt, c, G, (base + ti) / mt.tpu), tj = (base + ti) % mt.tpu;
+      const int n0 = seg_tile_row(mt, u, tj, half_rows);
+      if (geglu) S.gub[((size_t)ti * 4 + m) * 16 + r] = row;
+      else Y[(size_t)m * ldy + n0 + r] = row;
+    }
+    consumer_sync();
+    if (geglu && ok) {
+      // GeGLU of the round's units (tiles 4k..4k+3: gate rows 0-15, 16-31, up rows 0-15, 16-31 of
+      // one unit): act = r16(r16(gelu(r16 g)) * r16 u), then the 32-group quantisation
       const int w = t >> 5, lane = t & 31;
-      const int units_round = nteams / 4;
-      for (int pi = w; pi < units_round * M; pi += 8) {
+      const int units = nt / 4;
+      for (int pi = w; pi < units * M; pi += 8) {
         const int ur = pi / M, mm = pi % M;
-        const int i0 = base + 4 * ur;
-        if (i0 >= ntl) continue;
-        const int u = seg_unit(mt, c, G, i0 / 4);
+        const int u = seg_unit(mt, c, G, (base + 4 * ur) / 4);
         const float gv = r16(S.gub[((size_t)(4 * ur + (lane >> 4)) * 4 + mm) * 16 + (lane & 15)]);
         const float uv = r16(S.gub[((size_t)(4 * ur + 2 + (lane >> 4)) * 4 + mm) * 16 + (lane & 15)]);
         const float v = r16(__fmul_rn(r16(gelu(gv)), uv));
@@ -362,8 +471,6 @@ __device__ bool gemv_stage(const SegMatDev& mt, int stage_tiles_base, int& ring,
       consumer_sync();
     }
   }
-  ring += ntl;
-  (void)stage_tiles_base;
   return ok;
 }
 
@@ -425,17 +532,19 @@ __global__ void __launch_bounds__(kSegThreads, 1) k_seg(const __grid_constant__ 
   S.q = reinterpret_cast<int8_t*>(smem + (size_t)kSegNS * kSegSlot);
   S.sx = reinterpret_cast<float*>(S.q + (size_t)M * (kSegKmax + 16));
   S.sm = reinterpret_cast<int32_t*>(S.sx + M * 256);
-  S.rows = reinterpret_cast<float*>(S.sm + M * 256);
-  S.gub = S.rows + (size_t)M * kSegRow;
+  S.ac = reinterpret_cast<int*>(S.sm + M * 256);
+  S.ra = reinterpret_cast<float*>(S.ac);
+  S.rb = S.ra + (size_t)M * kH;
+  S.scl = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(S.ac) + kSegAcBytes);
+  S.gub = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(S.scl) + kSegSclBytes);
   const int t = threadIdx.x;
-  const int H = p.H, nf = H >> 2;
   if (t == 0) {
     for (int i = 0; i < kSegNS; ++i) { mbar_init(&sh.full[i], 1); mbar_init(&sh.empty[i], 1); }
     fence_mbar_init();
     sh.flag = 0;
   }
   __syncthreads();
-  // the matrices of this launch, in stage order
+  // the matrices of this launch, in stage order (the producer streams their tiles in this order)
   SegMatDev mats[4];
   int half[4] = {0, 0, 0, 0};
   int nm = 0, i_o = -1, i_gu = -1, i_dn = -1, i_qkv = -1;
@@ -445,166 +554,116 @@ __global__ void __launch_bounds__(kSegThreads, 1) k_seg(const __grid_constant__ 
     i_dn = nm; mats[nm++] = SegMatDev{p.down.w, p.down.s, p.down.N, p.down.K, 4, p.down.N / 4, 1, 74};
   }
   if (p.do_qkv) { i_qkv = nm; mats[nm++] = SegMatDev{p.qkv.w, p.qkv.s, p.qkv.N, p.qkv.K, 16, p.qkv.N / 16, 1, 111}; }
+  const bool tracer = p.trace != nullptr && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1);
+  unsigned long long* trc = tracer ? p.trace + ((size_t)p.trace_slot * 2 + (blockIdx.x ? 1 : 0)) * kSegStamps : nullptr;
+  auto stamp = [&](int k) {
+    if (trc && (threadIdx.x == 0 || threadIdx.x == kSegConsumers)) trc[k] = globaltimer();
+  };
   if (t >= kSegConsumers) {  // producer warp: weights are read-only, no wait on earlier kernels
+    stamp(20);
     seg_producer(mats, nm, half, S, sh, p.abort_flag);
+    stamp(22);
     return;
   }
+  stamp(0);
+  // the norm weights of this launch (read-only) in registers before the wait on the previous kernel
+  float4 w_pa[2], w_pf[2], w_pff[2], w_nx[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    w_pa[k] = p.do_mlp ? __ldg(reinterpret_cast<const float4*>(p.w_post_attn) + t + 256 * k) : z;
+    w_pf[k] = p.do_mlp ? __ldg(reinterpret_cast<const float4*>(p.w_pre_ff) + t + 256 * k) : z;
+    w_pff[k] = p.do_mlp ? __ldg(reinterpret_cast<const float4*>(p.w_post_ff) + t + 256 * k) : z;
+    w_nx[k] = __ldg(reinterpret_cast<const float4*>(p.w_next) + t + 256 * k);
+  }
   pdl_wait();
-  pdl_trigger();
+  stamp(1);
   const unsigned G = gridDim.x;
   int ring = 0;
   bool ok = true;
   int bar = 0;
-  float r1[M], r2[M];
-  Rows<M> A, B;
-  auto load_rows = [&](Rows<M>& dst, const float* src, bool round) {
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int f = t + 256 * k;
-        float4 v = f < nf ? ldcg4(src + (size_t)m * H + 4 * f) : make_float4(0.f, 0.f, 0.f, 0.f);
-        dst.v[m][k] = round ? r16x4(v) : v;
-      }
-  };
-  auto stash = [&](const Rows<M>& src) {  // the rows for the RMS chains
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int f = t + 256 * k;
-        if (f < nf) reinterpret_cast<float4*>(S.rows + (size_t)m * H)[f] = src.v[m][k];
-      }
-  };
-  auto quant_rows = [&](const Rows<M>& y) {
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int f = t + 256 * k;
-        if (f < nf) quant4_smem(y.v[m][k], f, m, S.q, H + 16, S.sx, S.sm);  // warp-uniform (nf % 64 == 0)
-      }
-  };
-  auto store_rows = [&](float* dst, const Rows<M>& src) {
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int f = t + 256 * k;
-        if (f < nf) reinterpret_cast<float4*>(dst + (size_t)m * H)[f] = src.v[m][k];
-      }
-  };
-  auto weights4 = [&](const float* w, int k) {
-    const int f = t + 256 * k;
-    return f < nf ? __ldg(reinterpret_cast<const float4*>(w) + f) : make_float4(0.f, 0.f, 0.f, 0.f);
-  };
+  auto tiles = [&](int i) { return seg_units(mats[i], blockIdx.x, G) * mats[i].tpu; };
 
   if (p.do_mlp) {
     // ---- S1: o projection of the attention output (quantised by the attention kernel)
     load_act<M>(p.att_q, p.att_sx, p.att_sum, p.o.K, S);
     consumer_sync();
-    ok = gemv_stage<M>(mats[i_o], 0, ring, p.o_out, p.H, 0, S, sh, false, nullptr, nullptr, nullptr) && ok;
+    stamp(2);
+    ok = gemv_stage<M>(mats[i_o], ring, p.o_out, p.H, 0, S, sh, false, nullptr, nullptr, nullptr) && ok;
+    ring += tiles(i_o);
+    stamp(3);
     ok = grid_barrier(p.bar + bar++, p.abort_flag, G, ok, sh);
+    stamp(4);
     // ---- S2: o = r16(o); x = r16(x + r16((o*r)*w_post)); mlp_in = r16((x*r')*w_pre), quantised;
     //          then gate/up with GeGLU and the down projection's quantisation
     if (ok) {
-      load_rows(A, p.o_out, true);
-      load_rows(B, p.x_a, false);
-      stash(A);
+      seg_load_rows(S.ra, p.o_out, M, 1);
+      seg_load_rows(S.rb, p.x_a, M, 0);
       consumer_sync();
-      rows_rms<M>(A, S.rows, H, sh, r1);
-#pragma unroll
-      for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int k = 0; k < 2; ++k) B.v[m][k] = resid4(B.v[m][k], A.v[m][k], r1[m], weights4(p.w_post_attn, k));
+      seg_rms(S.ra, M, sh);
+      stamp(5);
+      seg_resid(S.rb, S.ra, w_pa[0], w_pa[1], M, sh);
       consumer_sync();
-      stash(B);
-      if (blockIdx.x == 0) store_rows(p.x_b, B);
+      if (blockIdx.x == 0) seg_store_rows(p.x_b, S.rb, M);
+      seg_rms(S.rb, M, sh);
+      seg_scale(S.rb, w_pf[0], w_pf[1], M, 1, sh, S.q, S.sx, S.sm, nullptr);
       consumer_sync();
-      rows_rms<M>(B, S.rows, H, sh, r2);
-#pragma unroll
-      for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int k = 0; k < 2; ++k) A.v[m][k] = r16x4(scale4(B.v[m][k], r2[m], weights4(p.w_pre_ff, k)));
-      quant_rows(A);
-      consumer_sync();
-      ok = gemv_stage<M>(mats[i_gu], 0, ring, nullptr, 0, p.I, S, sh, true, p.act_q, p.act_sx, p.act_sum) && ok;
+      stamp(6);
+      ok = gemv_stage<M>(mats[i_gu], ring, nullptr, 0, p.I, S, sh, true, p.act_q, p.act_sx, p.act_sum) && ok;
+      stamp(7);
     }
+    ring += tiles(i_gu);
     ok = grid_barrier(p.bar + bar++, p.abort_flag, G, ok, sh);
+    stamp(8);
     // ---- S3: down projection
     if (ok) {
       load_act<M>(p.act_q, p.act_sx, p.act_sum, p.down.K, S);
       consumer_sync();
-      ok = gemv_stage<M>(mats[i_dn], 0, ring, p.down_out, p.H, 0, S, sh, false, nullptr, nullptr, nullptr) && ok;
+      stamp(9);
+      ok = gemv_stage<M>(mats[i_dn], ring, p.down_out, p.H, 0, S, sh, false, nullptr, nullptr, nullptr) && ok;
+      stamp(10);
     }
+    ring += tiles(i_dn);
     ok = grid_barrier(p.bar + bar++, p.abort_flag, G, ok, sh);
+    stamp(11);
     // ---- S4: o = r16(down); x = r16(x + r16((o*r)*w_post_ff)) (layer scalar 1); then the next
     //          layer's input norm (x*r')*w_in, quantised, or the final norm (rounded) into hbuf
     if (ok) {
-      load_rows(A, p.down_out, true);
-      load_rows(B, p.x_b, false);
-      stash(A);
+      seg_load_rows(S.ra, p.down_out, M, 1);
+      seg_load_rows(S.rb, p.x_b, M, 0);
       consumer_sync();
-      rows_rms<M>(A, S.rows, H, sh, r1);
-#pragma unroll
-      for (int m = 0; m < M; ++m)
-#pragma unroll
-        for (int k = 0; k < 2; ++k) B.v[m][k] = resid4(B.v[m][k], A.v[m][k], r1[m], weights4(p.w_post_ff, k));
+      stamp(16);
+      seg_rms(S.ra, M, sh);
+      stamp(17);
+      seg_resid(S.rb, S.ra, w_pff[0], w_pff[1], M, sh);
       consumer_sync();
-      stash(B);
-      if (blockIdx.x == 0) store_rows(p.x_a, B);
-      consumer_sync();
-      rows_rms<M>(B, S.rows, H, sh, r2);
+      if (blockIdx.x == 0) seg_store_rows(p.x_a, S.rb, M);
+      stamp(18);
+      seg_rms(S.rb, M, sh);
+      stamp(19);
       if (!p.do_qkv) {  // final norm, rounded (:1402)
-        if (blockIdx.x == 0) {
-#pragma unroll
-          for (int m = 0; m < M; ++m)
-#pragma unroll
-            for (int k = 0; k < 2; ++k) A.v[m][k] = r16x4(scale4(B.v[m][k], r2[m], weights4(p.w_next, k)));
-          store_rows(p.hbuf, A);
-        }
+        if (blockIdx.x == 0) seg_scale(S.rb, w_nx[0], w_nx[1], M, 1, sh, nullptr, nullptr, nullptr, p.hbuf);
       } else {
-#pragma unroll
-        for (int m = 0; m < M; ++m)
-#pragma unroll
-          for (int k = 0; k < 2; ++k) A.v[m][k] = scale4(B.v[m][k], r2[m], weights4(p.w_next, k));
-        quant_rows(A);
+        seg_scale(S.rb, w_nx[0], w_nx[1], M, 0, sh, S.q, S.sx, S.sm, nullptr);
       }
       consumer_sync();
     }
   } else if (p.do_qkv) {
     // ---- first launch of a pass: x = r16(E[tok] * sqrt(H)) (:1264), a = (x*r)*w_in, quantised
-    const int* toks = p.toks;
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const uint16_t* er = p.E + (size_t)__ldcg(toks + m) * H;
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int f = t + 256 * k;
-        if (f < nf) {
-          const uint2 b = __ldg(reinterpret_cast<const uint2*>(er) + f);
-          B.v[m][k] = make_float4(r16(__fmul_rn(bf2f(b.x & 0xFFFFu), p.sqrtH)), r16(__fmul_rn(bf2f(b.x >> 16), p.sqrtH)),
-                                  r16(__fmul_rn(bf2f(b.y & 0xFFFFu), p.sqrtH)), r16(__fmul_rn(bf2f(b.y >> 16), p.sqrtH)));
-        } else {
-          B.v[m][k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-    }
-    stash(B);
-    if (blockIdx.x == 0) store_rows(p.x_a, B);
+    seg_embed(S.rb, p.E, p.toks, M, p.sqrtH);
     consumer_sync();
-    rows_rms<M>(B, S.rows, H, sh, r2);
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-      for (int k = 0; k < 2; ++k) A.v[m][k] = scale4(B.v[m][k], r2[m], weights4(p.w_next, k));
-    quant_rows(A);
+    if (blockIdx.x == 0) seg_store_rows(p.x_a, S.rb, M);
+    seg_rms(S.rb, M, sh);
+    seg_scale(S.rb, w_nx[0], w_nx[1], M, 0, sh, S.q, S.sx, S.sm, nullptr);
     consumer_sync();
   }
   if (p.do_qkv) {
     // ---- qkv projection of the next layer
-    if (ok) ok = gemv_stage<M>(mats[i_qkv], 0, ring, p.qkv_out, p.qkv.N, 0, S, sh, false, nullptr, nullptr, nullptr) && ok;
+    stamp(12);
+    if (ok) ok = gemv_stage<M>(mats[i_qkv], ring, p.qkv_out, p.qkv.N, 0, S, sh, false, nullptr, nullptr, nullptr) && ok;
+    stamp(13);
     ok = grid_barrier(p.bar + bar++, p.abort_flag, G, ok, sh);
+    stamp(14);
     // ---- S5: q/k/v norms, RoPE and the KV write (:1290-1303), warp per (row, part)
     if (ok) {
       const int HD = p.HD, hh = HD >> 1, per = HD >> 6, nparts = p.NQ + 2;
@@ -621,9 +680,14 @@ __global__ void __launch_bounds__(kSegThreads, 1) k_seg(const __grid_constant__ 
           xl[k] = k < per ? __ldcg(src + j) : 0.f;
           xh[k] = k < per ? __ldcg(src + j + hh) : 0.f;
         }
-        double s = 0.0;  // lanes 0..15: partial `lane` (elements lane, lane + 16, ... in order)
-        if (lane < 16)
-          for (int i = lane; i < HD; i += 16) { const double d = __ldcg(src + i); s = fma(d, d, s); }
+        double s = 0.0;  // lanes 0..15: partial `lane` (elements lane, lane + 16, ... in order; HD = 256)
+        if (lane < 16) {
+          float v[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) v[k] = __ldcg(src + lane + 16 * k);
+#pragma unroll
+          for (int k = 0; k < 16; ++k) { const double d = v[k]; s = fma(d, d, s); }
+        }
         double u = s + __shfl_down_sync(FULL, s, 4);
         double tt = u + __shfl_down_sync(FULL, u, 8);
         double v2 = tt + __shfl_down_sync(FULL, tt, 2);
@@ -657,6 +721,7 @@ __global__ void __launch_bounds__(kSegThreads, 1) k_seg(const __grid_constant__ 
       }
     }
   }
+  stamp(15);
   (void)ok;
 }
 
@@ -666,7 +731,7 @@ using namespace g4;
 
 namespace g4 {
 size_t seg_smem_bytes(int M) {
-  return (size_t)kSegNS * kSegSlot + (size_t)M * (kSegKmax + 16) + (size_t)M * 256 * 8 + (size_t)M * kSegRow * 4 +
+  return (size_t)kSegNS * kSegSlot + (size_t)M * (kSegKmax + 16) + (size_t)M * 256 * 8 + kSegAcBytes + kSegSclBytes +
          (size_t)8 * 4 * 16 * 4;
 }
 
@@ -678,10 +743,13 @@ int seg_check(const SegParams& p) {
   return G4_OK;
 }
 
-// Launch with one CTA per SM; the grid barriers need every CTA resident at once, which the
-// cooperative attribute makes the driver guarantee (a launch it cannot place fails instead of
-// hanging).  Programmatic dependent launch lets the producer's weight stream start under the
-// previous kernel when the engine records a pass.
+// Launch with one CTA per SM (the shared memory allows no second one): the grid barriers need every
+// CTA resident at once, which holds because the grid is no larger than the SM count and the only
+// other kernels in flight are the one before it in the stream, which does not wait for this one,
+// and the one after it, which (programmatic launch) starts only once every CTA here has issued
+// launch_dependents, i.e. is resident.  Every barrier wait is bounded in any case.  Programmatic
+// dependent launch lets the producer's weight stream start under the previous kernel when the
+// engine records a pass.
 int seg_launch(const SegParams& p, cudaStream_t st) {
   if (int rc = seg_check(p)) return rc;
   static int nsm = 0;
@@ -702,12 +770,12 @@ int seg_launch(const SegParams& p, cudaStream_t st) {
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     if (occ * nsm < nsm) return set_error(G4_ERR_UNSUPPORTED, "segment kernel: grid does not fit");
-    // attribute sets tried in order: cooperative + programmatic, cooperative, ordinary
+    // attribute sets tried in order: programmatic (when recording a pass), ordinary, cooperative
     cudaError_t e = cudaErrorUnknown;
     for (int variant = pdl_enabled() ? 0 : 1; variant < 3; ++variant) {
       cudaLaunchAttribute at[2];
       int na = 0;
-      if (variant <= 1) {
+      if (variant == 2) {
         at[na].id = cudaLaunchAttributeCooperative;
         at[na].val.cooperative = 1;
         ++na;

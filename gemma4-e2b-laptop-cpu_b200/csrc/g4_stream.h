@@ -49,7 +49,11 @@ struct SegParams {
   // grid barriers of this launch (4 counters, zero at launch) and the pass's abort flag
   unsigned* bar;
   unsigned* abort_flag;
+  // stage timestamps (%globaltimer, may be NULL): [slot][first CTA, last CTA][kSegStamps]
+  unsigned long long* trace;
+  int trace_slot;
 };
+constexpr int kSegStamps = 24;
 
 size_t seg_smem_bytes(int M);
 int seg_check(const SegParams& p);

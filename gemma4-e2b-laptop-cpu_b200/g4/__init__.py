@@ -54,6 +54,7 @@ SIGNATURES = {
     "g4_engine_phase_times": (_I, [_P, _I, _P, _P]),
     "g4_engine_trace": (_I, [_P, _P, _I, _P]),
     "g4_engine_time_verify": (_I, [_P, _I, _I, _P]),
+    "g4_engine_seg_trace": (_I, [_P, _P, _I, _P]),
     "g4_engine_export_state": (_I, [_P, _I, _P, _P, _P, _I, _P, _P, _P]),
     "g4_attn_splitkv_ws_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "g4_attn_splitkv": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
@@ -491,6 +492,16 @@ class Engine:
         buf = np.zeros((max(n.value, 1), 6), np.int32)
         check(lib().g4_engine_trace(self.h, buf.ctypes.data_as(_P), n.value, ctypes.byref(n)), "g4_engine_trace")
         return buf[: n.value].copy()
+
+    def seg_trace(self):
+        """Stage timestamps (ns) of the last fused verify pass: [launch, CTA (first, last), 24]."""
+        import numpy as np
+        n = ctypes.c_int(0)
+        check(lib().g4_engine_seg_trace(self.h, None, 0, ctypes.byref(n)), "g4_engine_seg_trace")
+        buf = np.zeros(n.value, np.uint64)
+        check(lib().g4_engine_seg_trace(self.h, buf.ctypes.data_as(_P), n.value, ctypes.byref(n)),
+              "g4_engine_seg_trace")
+        return buf.reshape(-1, 2, 24)
 
     def time_verify(self, M, reps=20):
         """Device ms of one verify pass of M rows at the current position (CUDA events)."""

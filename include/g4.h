@@ -198,7 +198,7 @@ typedef struct {
   int fused_layers;                  /* verify passes on the int8 path (M = 2..4 rows past att_par)
                                         run each layer's o, gate/up, down and the next qkv projection
                                         with their norms in one persistent kernel (1), or as one
-                                        kernel per step (0) */
+                                        kernel per step (0, the default: measured faster) */
 } g4_engine_config;
 typedef struct {
   int rounds, ngram_rounds, drafted, accepted, prefill_tokens, decode_tokens;
@@ -248,6 +248,11 @@ int g4_engine_trace(g4_engine* e, int32_t* out, int cap_rounds, int* n_rounds);
  * times between CUDA events on the engine stream (what a round's verify costs, for roofline
  * accounting).  Needs graphs on and a position past att_par. */
 int g4_engine_time_verify(g4_engine* e, int M, int reps, double* ms_per_pass);
+/* Profiling aid: %globaltimer stamps (ns) of the stage boundaries inside the persistent segment
+ * kernels of the most recent fused verify pass, [n_layers + 2 launches][first CTA, last CTA][24]
+ * (0 = start, 1 = after the wait on the previous kernel, 2-15 = after each stage and barrier,
+ * 20/22 = weight streamer start/end); *n = the element count. */
+int g4_engine_seg_trace(g4_engine* e, unsigned long long* out, int cap, int* n);
 /* Decode state after a prefill or decode call: K and V rows of positions [0, npos) of every layer
  * (host [n_layers][npos][256] bf16 each, may be NULL), the committed history (host seq [seq_cap]
  * may be NULL, *seq_len its length), the final-normed hidden of the last committed row (host
