@@ -27,6 +27,8 @@ SIGNATURES = {
     "g4_w4g32_gemm": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _I, _P]),
     "g4_w4a8_quant": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "g4_w4a8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _P]),
+    "g4_w4a8_gemm_tc_ws_bytes": (_SZ, [_I, _I, _I]),
+    "g4_w4a8_gemm_tc": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _I, _P, _SZ, _P]),
     "g4_device_init": (_I, []),
     "g4_bf16p_codebook": (_I, [_P, ctypes.c_longlong, _P, _P, _SZ, _P]),
     "g4_bf16p_count": (_I, [_P, _I, _I, _P, _P, _P, _SZ, ctypes.POINTER(ctypes.c_longlong), _P]),
@@ -142,6 +144,22 @@ def w4g32_gemm(Wp, S, X, gsum=None, out=None):
     Y = out if out is not None else torch.empty((M, N), dtype=torch.float32, device=X.device)
     check(lib().g4_w4g32_gemm(_ptr(Wp), _ptr(S), _ptr(X), _ptr(gsum), M, N, K, _ptr(Y), Y.stride(0), _stream()),
           "g4_w4g32_gemm")
+    return Y
+
+
+def w4a8_gemm_tc(Wp, S, q, sx, out=None):
+    """The W4A8 GEMM on the tensor cores (tcgen05 kind::i8) for any M: the same values as
+    w4a8_gemm."""
+    import torch
+    M, K = q.shape
+    N = Wp.shape[0]
+    Y = out if out is not None else torch.empty((M, N), dtype=torch.float32, device=q.device)
+    nb = lib().g4_w4a8_gemm_tc_ws_bytes(M, N, K)
+    ws = torch.empty(nb, dtype=torch.uint8, device=q.device)
+    for t, n in ((Wp, "Wp"), (S, "S"), (q, "q"), (sx, "sx"), (Y, "Y")):
+        _dev(t, n)
+    check(lib().g4_w4a8_gemm_tc(_ptr(Wp), _ptr(S), _ptr(q), _ptr(sx), M, N, K, _ptr(Y), N, _ptr(ws), nb, _stream()),
+          "g4_w4a8_gemm_tc")
     return Y
 
 

@@ -71,6 +71,18 @@ int g4_w4a8_quant(const float* X, int M, int K, int8_t* q, float* sx, int32_t* s
 int g4_w4a8_gemm(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
                  int M, int N, int K, float* Y, int ldy, void* stream);
 
+/* Workspace bytes of g4_w4a8_gemm_tc. */
+size_t g4_w4a8_gemm_tc_ws_bytes(int M, int N, int K);
+/* g4_w4a8_gemm for any M on the tensor cores (tcgen05.mma kind::i8, the prefill path of the
+ * reference's fwd blocks, gemma4_engine.cpp:1595-1599 -> w4a8::tile<MT>, w4a8_avx2.h:46-60): the
+ * same integer group dots (s8 weights q = t - 8 against the int8 activations) and the same fp32
+ * chain per (row, activation row), so the same bits.  Wp dev (device layout), S dev, q dev [M][K],
+ * sx dev [M][K/32] (the group sums are not needed), Y dev [M][ldy]; ws dev of
+ * g4_w4a8_gemm_tc_ws_bytes() (256-byte aligned: the s8 weights and transposed scales are built in
+ * it on every call).  N and K multiples of 128. */
+int g4_w4a8_gemm_tc(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, int M, int N, int K, float* Y,
+                    int ldy, void* ws, size_t ws_bytes, void* stream);
+
 /* ---------------------------------------------------------------- row norms */
 
 /* RMS norm of M rows, y = (x * r) * w with r = 1 / sqrtf((float)(ss / n) + 1e-6f) and ss the sum
