@@ -6,6 +6,7 @@
 #include "g4_api.h"
 #include "g4_layers.cuh"
 #include "g4_stream.h"
+#include "g4_tc.h"
 #include <algorithm>
 #include <chrono>
 #include <cmath>
@@ -30,8 +31,13 @@ struct Lin {  // one int4 W4G32 matrix in device layout
   uint16_t* s = nullptr;
   int N = 0, K = 0;
 };
+struct TcLin {  // the tensor-core operands of a Lin: s8 weights [N][K] and scales transposed [K/32][N]
+  int8_t* w8 = nullptr;
+  uint16_t* swT = nullptr;
+};
 struct TLayer {
   Lin qkv, o, gu, down;
+  TcLin tqkv, to, tgu, tdown;
   float *in_ln, *post_attn, *pre_ff, *post_ff, *qn, *kn;
   bool global;
 };
@@ -280,6 +286,15 @@ struct g4_engine {
   int gk_verify[5] = {0, 0, 0, 0, 0}, gk_draft = 0;  // kernel nodes of each graph
   cudaEvent_t tev[4] = {nullptr, nullptr, nullptr, nullptr};  // draft start/end, verify start/end
   int fake_n = 0;
+  // tensor-core prefill: chunks of up to pmc rows of full prompt blocks
+  bool tc_ready = false;
+  int pmc = 0;
+  int* ptoks = nullptr;
+  float *px = nullptr, *pa = nullptr, *pqkv = nullptr, *patt = nullptr, *po = nullptr, *pgu = nullptr, *pact = nullptr,
+        *pmlp = nullptr, *psxT = nullptr;
+  int8_t* pq = nullptr;
+  float* psx = nullptr;
+  int32_t* psum = nullptr;
   // decode state between g4_engine_decode calls: on the device (RoundCtl, history, outputs, trace),
   // mirrored on the host after every call
   g4::RoundCtl* rc = nullptr;      // device
@@ -306,6 +321,7 @@ extern "C" int g4_engine_default_config(g4_engine_config* c) {
   c->head_screen = 1; c->screen_lim = 30000; c->attn_chunks = 8; c->att_par = 192; c->drafter = 1; c->seed = 20261201ull;
   c->graphs = 1;
   c->fused_layers = 0;
+  c->prefill_tc = 1;
   return G4_OK;
 }
 
@@ -427,6 +443,37 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
       if (!rc) rc = gen_norm(e, &t.qn, dlayer_id(l, T_QN), d.HD, 0.0625f);
     }
     if (rc) return fail(rc);
+  }
+  // tensor-core prefill operands and chunk buffers
+  if (c.prefill_tc && c.prefill_int8 && H % 128 == 0 && QD % 128 == 0 && I % 128 == 0 && (QD + 2 * d.HD) % 128 == 0) {
+    int rc = G4_OK;
+    auto tc_lin = [&](const Lin& l, TcLin& t) {
+      if (rc) return;
+      if (ealloc_t(e, &t.w8, (size_t)l.N * l.K) || ealloc_t(e, &t.swT, (size_t)l.N * (l.K / 32))) { rc = G4_ERR_CUDA; return; }
+      rc = tc_expand_weights(l.w, l.s, l.N, l.K, t.w8, t.swT, e->st);
+    };
+    for (int l = 0; l < d.NL; ++l) {
+      TLayer& t = e->L[l];
+      tc_lin(t.qkv, t.tqkv); tc_lin(t.o, t.to); tc_lin(t.gu, t.tgu); tc_lin(t.down, t.tdown);
+    }
+    const int MC = std::min(2048, c.ctx_max / 32 * 32);
+    e->pmc = MC;
+    const size_t kmax = (size_t)std::max({H, I, QD});
+    if (!rc) rc = ealloc_t(e, &e->ptoks, (size_t)MC);
+    if (!rc) rc = ealloc_t(e, &e->px, (size_t)MC * H);
+    if (!rc) rc = ealloc_t(e, &e->pa, (size_t)MC * H);
+    if (!rc) rc = ealloc_t(e, &e->pqkv, (size_t)MC * (QD + 2 * d.HD));
+    if (!rc) rc = ealloc_t(e, &e->patt, (size_t)MC * QD);
+    if (!rc) rc = ealloc_t(e, &e->po, (size_t)MC * H);
+    if (!rc) rc = ealloc_t(e, &e->pgu, (size_t)MC * 2 * I);
+    if (!rc) rc = ealloc_t(e, &e->pact, (size_t)MC * I);
+    if (!rc) rc = ealloc_t(e, &e->pmlp, (size_t)MC * H);
+    if (!rc) rc = ealloc_t(e, &e->pq, (size_t)MC * kmax);
+    if (!rc) rc = ealloc_t(e, &e->psx, (size_t)MC * kmax / 32);
+    if (!rc) rc = ealloc_t(e, &e->psum, (size_t)MC * kmax / 32);
+    if (!rc) rc = ealloc_t(e, &e->psxT, (size_t)MC * kmax / 32);
+    if (rc) return fail(rc);
+    e->tc_ready = true;
   }
   // KV cache and RoPE tables (host, double -> float, as gemma4_engine.cpp:1246-1247)
   const size_t kvn = (size_t)d.NL * c.ctx_max * d.HD;
@@ -871,6 +918,53 @@ extern "C" int g4_engine_fake_ctx(g4_engine* e, int n) {
 // run_req (:1582-1680), split in two: prefill in blocks (int8 per ENGINE_PREFILL_INT8, :1595), then
 // resumable decode rounds (chain mode): prompt lookup or k MTP drafts -> one verify forward ->
 // greedy acceptance.  The committed sequence stays on the host (it is the prompt-lookup history).
+// Prefill of Mc (a multiple of prefill_block, at most pmc) prompt rows at positions pos0.. that form
+// full prefill blocks, through all layers at once: the row kernels of forward() over Mc rows and the
+// tensor-core W4A8 GEMM (the same values as the blocks' GEMVs: prefill blocks of >= 2 rows take the
+// int8 path, :311); attention per row with its block's variant (k_attn_rows, variant < 0).
+static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0) {
+  const ModelDims& d = e->d;
+  const int H = d.H, QD = d.NQ * d.HD, ld = QD + 2 * d.HD, I = d.I;
+  const int Mpad = (Mc + 127) / 128 * 128;
+  const QuantOut qo{e->pq, e->psx, e->psum};
+  ECK(cudaMemcpyAsync(e->ptoks, toks, sizeof(int) * Mc, cudaMemcpyHostToDevice, e->st));
+  auto gemm = [&](const TcLin& t, const Lin& l, float* Y) {
+    RCK(tc_transpose_sx(e->psx, Mc, l.K / 32, e->psxT, Mpad, e->st));
+    return tc_gemm(e->pq, Mc, l.K, e->psxT, Mpad, t.w8, t.swT, l.N, Y, l.N, e->st);
+  };
+  RCK(launch("k_embed", k_embed, dim3(Mc), dim3(256), 0, e->st, (const uint16_t*)e->E, (const int*)e->ptoks, H,
+             sqrtf((float)H), e->px));
+  RCK(launch("k_norm_q", k_norm_q, dim3(Mc), dim3(256), 0, e->st, (const float*)e->px, (const float*)e->L[0].in_ln, H, e->pa, 0, qo));
+  for (int l = 0; l < d.NL; ++l) {
+    const TLayer& t = e->L[l];
+    const int ty = t.global ? 1 : 0;
+    uint16_t* Kc = e->Kc + (size_t)l * e->cfg.ctx_max * d.HD;
+    uint16_t* Vc = e->Vc + (size_t)l * e->cfg.ctx_max * d.HD;
+    RCK(gemm(t.tqkv, t.qkv, e->pqkv));
+    RCK(launch("k_qkv_post_w", k_qkv_post_w, dim3(Mc), dim3(32 * (d.NQ + 2)), 0, e->st, (const float*)e->pqkv, ld, d.NQ, d.HD,
+               pos0, (const int*)nullptr, (const float*)t.qn, (const float*)t.kn, (const float*)e->rope[ty][0],
+               (const float*)e->rope[ty][1], Kc, Vc, e->pqkv, ld));
+    const int len_max = t.global ? pos0 + Mc : std::min(pos0 + Mc, d.WINDOW);
+    RCK(launch("k_attn_rows", k_attn_rows, dim3(Mc, d.NQ), dim3(256), sizeof(float) * len_max, e->st, (const uint16_t*)Kc,
+               (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.NQ, d.HD, pos0, t.global ? 0 : d.WINDOW, -1, e->patt, QD,
+               e->fake_n, e->cfg.prefill_block));
+    RCK(g4_w4a8_quant(e->patt, Mc, QD, e->pq, e->psx, e->psum, e->st));
+    RCK(gemm(t.to, t.o, e->po));
+    RCK(launch("k_post_attn_q", k_post_attn_q, dim3(Mc), dim3(256), 0, e->st, (const float*)e->po, e->px, (const float*)t.post_attn,
+               (const float*)t.pre_ff, e->pmlp, H, qo));
+    RCK(gemm(t.tgu, t.gu, e->pgu));
+    RCK(launch("k_act_q", k_act_q, dim3((unsigned)((long long)Mc * I / 256)), dim3(256), 0, e->st, (const float*)e->pgu, I, Mc,
+               e->pact, qo));
+    RCK(gemm(t.tdown, t.down, e->po));
+    // residual, then the next layer's input norm and its quantisation (none after the last layer:
+    // these rows need no final norm)
+    RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(Mc), dim3(256), 0, e->st, (const float*)e->po, e->px,
+               (const float*)t.post_ff, 1.0f, H, l + 1 < d.NL ? (const float*)e->L[l + 1].in_ln : (const float*)nullptr,
+               e->pa, 0, qo));
+  }
+  return check_launch("prefill_chunk");
+}
+
 static int upload_round_state(g4_engine* e);
 extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int32_t* first_token) {
   G4_REQUIRE(e && prompt && n >= 1 && e->fake_n + n + 8 <= e->cfg.ctx_max,
@@ -880,6 +974,17 @@ extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int
   auto t0 = std::chrono::steady_clock::now();
   e->i8_active = e->cfg.prefill_int8 != 0;
   int done = 0, last_M = 0;
+  if (e->tc_ready && e->cfg.prefill_tc && e->i8_active && e->cfg.prefill_block >= 2) {
+    // every full block but the last through the tensor-core path, in chunks
+    const int PB = e->cfg.prefill_block;
+    const int nfast = ((n - 1) / PB) * PB;
+    const int chunk = std::max(PB, e->pmc / PB * PB);
+    while (done < nfast) {
+      const int Mc = std::min(chunk, nfast - done);
+      RCK(prefill_chunk(e, prompt + done, Mc, FN + done));
+      done += Mc;
+    }
+  }
   while (done < n) {
     const int M = std::min(e->cfg.prefill_block, n - done);
     const bool last = done + M == n;

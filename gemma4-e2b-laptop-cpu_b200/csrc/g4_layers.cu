@@ -598,13 +598,18 @@ __global__ void k_draft_in(const uint16_t* __restrict__ E, const int* __restrict
 //     out = r16(O).
 __global__ void __launch_bounds__(256) k_attn_rows(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
                                                    const float* __restrict__ q, int ldq, int nh, int hd, int pos0,
-                                                   int window, int variant, float* __restrict__ out, int ldo) {
+                                                   int window, int variant, float* __restrict__ out, int ldo,
+                                                   int blk_fn, int blk) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ float sc[];
   __shared__ float s_red[32];
   const int m = blockIdx.x, h = blockIdx.y;
   const int pos = pos0 + m, lo = window > 0 ? max(0, pos - (window - 1)) : 0, len = pos - lo + 1;
+  if (variant < 0) {  // rows of full prefill blocks of blk rows starting at position blk_fn: the block's choice
+    const int b0 = pos - (pos - blk_fn) % blk;
+    variant = (blk >= 4 && b0 + blk > 64) ? 0 : 1;
+  }
   const float* qh = q + (size_t)m * ldq + (size_t)h * hd;
   const int hw = threadIdx.x >> 4, c = threadIdx.x & 15;
   // scores: one half-warp per key; the two half-warps of a warp take keys pb and pb+1

@@ -30,8 +30,10 @@ __global__ void k_act_q(const float* gu, int I, int M, float* act, QuantOut qo);
 __global__ void k_round(float* p, long long n);
 __global__ void k_scale_round(float* p, long long n, float s);
 __global__ void k_draft_in(const uint16_t* E, const int* tok, const float* h, int H, float sqrtH, float* out);
+// variant < 0: each row takes the variant of its prefill block (full blocks of blk rows from position
+// blk_fn), as fwd chooses per block (:1328-1355).
 __global__ void k_attn_rows(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0,
-                            int window, int variant, float* out, int ldo);
+                            int window, int variant, float* out, int ldo, int blk_fn = 0, int blk = 32);
 __global__ void k_cand_scores(const uint16_t* E, const int* cand, int nc, const float* dh, int H, float* score);
 __global__ void k_topk_cand(const float* score, int n, int T, int per, int vocab, int* cand);
 __global__ void k_cand_best(const float* score, const int* cand, int nc, int* best);

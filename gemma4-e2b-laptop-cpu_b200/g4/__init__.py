@@ -423,7 +423,8 @@ class EngineConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in ("hidden", "n_layers", "mlp", "vocab", "ctx_max", "prefill_block", "k_draft",
                                             "ngram", "ngram_len", "prefill_int8", "decode_int8", "head_screen",
                                             "screen_lim", "attn_chunks", "att_par", "drafter")] + [
-        ("seed", ctypes.c_ulonglong), ("graphs", ctypes.c_int), ("fused_layers", ctypes.c_int)]
+        ("seed", ctypes.c_ulonglong), ("graphs", ctypes.c_int), ("fused_layers", ctypes.c_int),
+        ("prefill_tc", ctypes.c_int)]
 
 
 class EngineStats(ctypes.Structure):

@@ -258,7 +258,7 @@ class E2EConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in ("hidden", "n_layers", "mlp", "vocab", "ctx_max", "prefill_block", "k_draft",
                                             "ngram", "ngram_len", "prefill_int8", "decode_int8", "head_screen",
                                             "screen_lim", "attn_chunks", "att_par", "drafter")] + [
-        ("seed", ctypes.c_ulonglong)]
+        ("seed", ctypes.c_ulonglong)]  # a prefix of g4_engine_config: the oracle reads these fields only
 
 
 def e2e_config(**kw):

@@ -228,3 +228,25 @@ def test_fused_segments_match_per_kernel_path():
         a.close()
         b.close()
         om.close()
+
+
+@pytest.mark.parametrize("cfg", [dict(SMALL), dict(ctx_max=2048)])
+def test_tensor_core_prefill_matches_block_prefill(cfg):
+    """The prompt's full blocks prefilled at once with the tensor-core W4A8 GEMM write the same KV
+    cache, hidden state and first token, bit for bit, as prefill block by block through the GEMV
+    path; at the full width and at reduced dimensions."""
+    vocab = cfg.get("vocab", 262144)
+    prompt = make_prompt(11, 777, vocab=vocab)
+    outs = []
+    for tc in (1, 0):
+        eng = g4.Engine(g4.engine_config(**cfg, prefill_tc=tc))
+        try:
+            first = eng.prefill(prompt)
+            K, V, seq, h, P = eng.export_state(777)
+            outs.append((first, K, V, h, P))
+        finally:
+            eng.close()
+    (f1, K1, V1, h1, P1), (f0, K0, V0, h0, P0) = outs
+    assert f1 == f0 and P1 == P0
+    assert np.array_equal(K1, K0) and np.array_equal(V1, V0)
+    assert np.array_equal(h1.view(np.uint32), h0.view(np.uint32))
