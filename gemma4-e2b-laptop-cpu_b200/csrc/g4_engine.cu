@@ -945,9 +945,18 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0) {
                pos0, (const int*)nullptr, (const float*)t.qn, (const float*)t.kn, (const float*)e->rope[ty][0],
                (const float*)e->rope[ty][1], Kc, Vc, e->pqkv, ld));
     const int len_max = t.global ? pos0 + Mc : std::min(pos0 + Mc, d.WINDOW);
-    RCK(launch("k_attn_rows", k_attn_rows, dim3(Mc, d.NQ), dim3(256), sizeof(float) * len_max, e->st, (const uint16_t*)Kc,
-               (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.NQ, d.HD, pos0, t.global ? 0 : d.WINDOW, -1, e->patt, QD,
-               e->fake_n, e->cfg.prefill_block));
+    if (e->cfg.prefill_tc == 2 && d.NQ % 4 == 0 && d.HD <= 256) {  // four heads per block share each K and V row
+      const size_t smem = sizeof(float) * 4 * (size_t)len_max;
+      if (smem > 200 * 1024) return set_error(G4_ERR_UNSUPPORTED, "prefill attention: %zu B of shared memory", smem);
+      if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      RCK(launch("k_attn_prefill", k_attn_prefill, dim3(Mc, d.NQ / 4), dim3(288), smem, e->st, (const uint16_t*)Kc,
+                 (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.HD, pos0, t.global ? 0 : d.WINDOW, e->fake_n,
+                 e->cfg.prefill_block, e->patt, QD));
+    } else {
+      RCK(launch("k_attn_rows", k_attn_rows, dim3(Mc, d.NQ), dim3(256), sizeof(float) * len_max, e->st, (const uint16_t*)Kc,
+                 (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.NQ, d.HD, pos0, t.global ? 0 : d.WINDOW, -1, e->patt, QD,
+                 e->fake_n, e->cfg.prefill_block));
+    }
     RCK(g4_w4a8_quant(e->patt, Mc, QD, e->pq, e->psx, e->psum, e->st));
     RCK(gemm(t.to, t.o, e->po));
     RCK(launch("k_post_attn_q", k_post_attn_q, dim3(Mc), dim3(256), 0, e->st, (const float*)e->po, e->px, (const float*)t.post_attn,

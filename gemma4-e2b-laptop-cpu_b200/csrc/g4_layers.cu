@@ -655,9 +655,17 @@ __global__ void __launch_bounds__(256) k_attn_rows(const uint16_t* __restrict__ 
     sc[i] = variant == 0 ? exp8(d) : exp_cr(d);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0) {  // the in-order sum, 8 loads in flight ahead of the chain
     float den = 0.f;
-    for (int i = 0; i < len; ++i) den = __fadd_rn(den, sc[i]);
+    int i = 0;
+    for (; i + 8 <= len; i += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = sc[i + u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) den = __fadd_rn(den, v[u]);
+    }
+    for (; i < len; ++i) den = __fadd_rn(den, sc[i]);
     s_red[0] = den;
   }
   __syncthreads();
@@ -669,8 +677,143 @@ __global__ void __launch_bounds__(256) k_attn_rows(const uint16_t* __restrict__ 
   const float inv = __fdiv_rn(1.0f, den);
   for (int i = threadIdx.x; i < hd; i += blockDim.x) {
     float o = 0.f;
-    for (int p = 0; p < len; ++p) o = fmaf(sc[p], bf2f(Vc[(size_t)(lo + p) * hd + i]), o);
+    const uint16_t* vp = Vc + (size_t)lo * hd + i;
+    int p = 0;
+    for (; p + 8 <= len; p += 8) {  // 8 V loads in flight ahead of the in-order chain
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = bf2f(vp[(size_t)(p + u) * hd]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o = fmaf(sc[p + u], v[u], o);
+    }
+    for (; p < len; ++p) o = fmaf(sc[p], bf2f(vp[(size_t)p * hd]), o);
     out[(size_t)m * ldo + (size_t)h * hd + i] = variant == 0 ? r16(__fmul_rn(o, inv)) : r16(o);
+  }
+}
+
+// ---- prefill attention, four query heads of one row per block (they share the KV head: one read of
+// each K and V row serves four heads).  The values are k_attn_rows's, per (row, head): scores in the
+// variant's lane order (variant 0, attn_tile :1061-1083: two 8-lane chains of stride 16; variant 1,
+// :1337-1355: one 8-lane chain of stride 8), the row max, exp8 (0) or the correctly rounded exp (1),
+// the in-order sum of the weights, and O per dim over the keys in order (variant 1 first divides
+// each weight by the sum, variant 0 scales O by its inverse), rounded to bf16.  The variant of a row
+// is its prefill block's (full blocks of blk rows from position blk_fn).  Block (row, head quad),
+// 256 threads; dynamic shared memory 4 x len_max floats.
+constexpr int kApHeads = 4;
+__global__ void __launch_bounds__(288) k_attn_prefill(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
+                                                      const float* __restrict__ q, int ldq, int hd, int pos0, int window,
+                                                      int blk_fn, int blk, float* __restrict__ out, int ldo) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float sc[];  // [kApHeads][len]
+  __shared__ float s_mx[kApHeads], s_den[kApHeads];
+  const int m = blockIdx.x, h0 = blockIdx.y * kApHeads;
+  const int pos = pos0 + m, lo = window > 0 ? max(0, pos - (window - 1)) : 0, len = pos - lo + 1;
+  const int b0 = pos - (pos - blk_fn) % blk;
+  const int variant = (blk >= 4 && b0 + blk > 64) ? 0 : 1;
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  // scores (threads 0-255): half-warp hw runs (head hw % 4, key slot hw / 4) dots in the variant's order
+  if (t < 256) {
+    const int hw = t >> 4, c = t & 15, hh = hw & 3, slot = hw >> 2;
+    const float* qh = q + (size_t)m * ldq + (size_t)(h0 + hh) * hd;
+    float qr[32];
+    if (variant == 0) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) qr[i] = (i < (hd >> 4)) ? qh[c + 16 * i] : 0.f;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) qr[i] = (c < 8 && i < (hd >> 3)) ? qh[c + 8 * i] : 0.f;
+    }
+    float* sh = sc + (size_t)hh * len;
+    for (int pb = 0; pb < len; pb += 4) {
+      const int pi = min(pb + slot, len - 1);
+      const uint16_t* kr = Kc + (size_t)(lo + pi) * hd;
+      float acc = 0.f, s;
+      if (variant == 0) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < (hd >> 4)) acc = fmaf(qr[i], bf2f(kr[c + 16 * i]), acc);
+        s = hsum8_octet(__fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8)));
+      } else {
+        if (c < 8) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < (hd >> 3)) acc = fmaf(qr[i], bf2f(kr[c + 8 * i]), acc);
+        }
+        s = hsum8_octet(acc);
+      }
+      if (c == 0 && pb + slot < len) sh[pb + slot] = s;
+    }
+  }
+  __syncthreads();
+  if (wid < kApHeads) {  // per-head max (order-free)
+    const float* sh = sc + (size_t)wid * len;
+    float mx = -1e30f;
+    for (int i = lane; i < len; i += 32) mx = fmaxf(mx, sh[i]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    if (lane == 0) s_mx[wid] = mx;
+  }
+  __syncthreads();
+  for (int i = t; i < kApHeads * len; i += blockDim.x) {
+    const int hq = i / len;
+    const float d = __fsub_rn(sc[i], s_mx[hq]);
+    sc[i] = variant == 0 ? exp8(d) : exp_cr(d);
+  }
+  __syncthreads();
+  // the in-order sums of the weights: lanes 0-3 of warp 8, one head each (variant 0: while warps
+  // 0-7 run the O chains; variant 1 divides by them first)
+  auto sums = [&]() {
+    if (wid == 8 && lane < kApHeads) {
+      const float* sh = sc + (size_t)lane * len;
+      float den = 0.f;
+      int i = 0;
+      for (; i + 8 <= len; i += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = sh[i + u];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) den = __fadd_rn(den, v[u]);
+      }
+      for (; i < len; ++i) den = __fadd_rn(den, sh[i]);
+      s_den[lane] = den;
+    }
+  };
+  if (variant == 1) {
+    sums();
+    __syncthreads();
+    for (int i = t; i < kApHeads * len; i += blockDim.x) sc[i] = __fdiv_rn(sc[i], s_den[i / len]);
+    __syncthreads();
+  }
+  // O (threads 0-255): thread per dim, the four heads' chains together (one V load, four FMAs)
+  float o[kApHeads] = {0.f, 0.f, 0.f, 0.f};
+  if (t < 256 && t < hd) {
+    const uint16_t* vp = Vc + (size_t)lo * hd + t;
+    int p = 0;
+    for (; p + 8 <= len; p += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = bf2f(vp[(size_t)(p + u) * hd]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int hq = 0; hq < kApHeads; ++hq) o[hq] = fmaf(sc[(size_t)hq * len + p + u], v[u], o[hq]);
+    }
+    for (; p < len; ++p) {
+      const float v = bf2f(vp[(size_t)p * hd]);
+#pragma unroll
+      for (int hq = 0; hq < kApHeads; ++hq) o[hq] = fmaf(sc[(size_t)hq * len + p], v, o[hq]);
+    }
+  } else if (variant == 0) {
+    sums();
+  }
+  __syncthreads();  // the sums are ready
+  if (t < 256 && t < hd) {
+#pragma unroll
+    for (int hq = 0; hq < kApHeads; ++hq) {
+      const float r = variant == 0 ? r16(__fmul_rn(o[hq], __fdiv_rn(1.0f, s_den[hq]))) : r16(o[hq]);
+      out[(size_t)m * ldo + (size_t)(h0 + hq) * hd + t] = r;
+    }
   }
 }
 

@@ -34,6 +34,10 @@ __global__ void k_draft_in(const uint16_t* E, const int* tok, const float* h, in
 // blk_fn), as fwd chooses per block (:1328-1355).
 __global__ void k_attn_rows(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0,
                             int window, int variant, float* out, int ldo, int blk_fn = 0, int blk = 32);
+// Prefill attention for rows of full prefill blocks, four query heads per block (grid (M, nh / 4),
+// 288 threads, hd <= 256, dynamic shared memory 4 * len_max floats): the values of k_attn_rows with variant < 0.
+__global__ void k_attn_prefill(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int hd, int pos0, int window,
+                               int blk_fn, int blk, float* out, int ldo);
 __global__ void k_cand_scores(const uint16_t* E, const int* cand, int nc, const float* dh, int H, float* score);
 __global__ void k_topk_cand(const float* score, int n, int T, int per, int vocab, int* cand);
 __global__ void k_cand_best(const float* score, const int* cand, int nc, int* best);
