@@ -653,6 +653,9 @@ def run_decode_g4(args, world, rank, local):
     P_mid = N_PROMPT + 60  # mid-run context (the warm-up, padding and timed rounds commit ~100-250 tokens)
     peak, peak_kind = measured_peaks()
     roof = decode_roofline(eng, d, M_pass, P_mid, peak, peak_kind)
+    streams = None
+    if not args.no_subrecords:
+        streams = run_streams_subrecord(eng, args, world, rank, local, dist_)
     eng.close()
     del eng
     torch.cuda.empty_cache()
@@ -693,9 +696,71 @@ def run_decode_g4(args, world, rank, local):
             "gpu_launches": d["kernel_launches"],
             "clocks": clocks,
             "mtp": mtp,
+            "streams": streams,
             "gemv_cfg0": gemv,
         }
     return out, (dist_, state)
+
+
+def run_streams_subrecord(eng, args, world, rank, local, dist_, totals=(8, 64)):
+    """configs[4] as independent request streams: S streams in total split over the N GPUs (S/N per
+    GPU), each an engine of its own (KV cache, round state, CUDA stream, round-loop graph) over the
+    weights of the GPU's first engine (g4_engine_create_shared), all decoding at once
+    (g4_engine_decode_async).  Up to 8 distinct prompts are prefilled per GPU; further streams continue
+    copies of those contexts (g4_engine_copy_state).  A step is one round of every stream; value =
+    tokens committed by all streams / the device time from a common start event to the last
+    stream's end (max over ranks)."""
+    import torch
+    import g4
+    from oracle_lib import make_prompt
+    n_ctx = max(1, min(8, max(totals) // world))
+    ctxs = [eng]
+    for i in range(1, n_ctx):
+        e2 = g4.Engine(g4.engine_config(), share=eng)
+        e2.prefill(make_prompt(PROMPT_SEED + 100 * rank + i, N_PROMPT))
+        ctxs.append(e2)
+    pool = list(ctxs)
+    out = {}
+    try:
+        for S in totals:
+            s_loc = max(1, S // world)
+            while len(pool) < s_loc:
+                e2 = g4.Engine(g4.engine_config(), share=eng)
+                e2.copy_state_from(ctxs[len(pool) % n_ctx])
+                pool.append(e2)
+            active = pool[:s_loc]
+            for e in active:  # warm-up (and graph capture of new engines)
+                e.decode_async(args.warmup, 1 << 30)
+            for e in active:
+                e.decode_wait()
+            barrier(dist_)
+            torch.cuda.synchronize()
+            start = torch.cuda.Event(enable_timing=True)
+            with Clocks(local) as clk:
+                start.record()
+                t0 = time.perf_counter()
+                for e in active:
+                    e.decode_async(args.steps, 1 << 30, start)
+                res = [e.decode_wait(start) for e in active]
+                wall = time.perf_counter() - t0
+            ms = max(r[2] for r in res)
+            ntok = sum(len(r[0]) for r in res)
+            ms_max = max_over_ranks(ms, dist_)
+            tok_all = float(ntok)
+            if dist_ is not None:
+                t = torch.tensor([tok_all], dtype=torch.float64, device="cuda")
+                dist_.all_reduce(t)
+                tok_all = float(t.item())
+            out[f"s{S}"] = {"value": tok_all / (ms_max / 1e3), "unit": TOKENS_METRIC_UNIT, "streams_total": S,
+                            "streams_per_gpu": s_loc, "distinct_prompts_per_gpu": min(n_ctx, s_loc),
+                            "rounds_per_stream": args.steps, "tokens": tok_all, "ms": ms_max,
+                            "wall_ms": wall * 1e3, "clocks": clk.summary()}
+    finally:
+        for e in pool[1:]:
+            e.close()
+    out["timing"] = ("CUDA events: a start event that every stream waits on, to each stream's end; max over streams "
+                     "and ranks")
+    return out
 
 
 def run_mtp_subrecord(args, world, rank, local, dist_, peak, peak_kind):

@@ -309,6 +309,12 @@ struct g4_engine {
   cudaGraph_t graw_verify[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   cudaGraph_t graw_draft = nullptr;
   bool loop_failed = false;
+  bool shared = false;  // weights belong to another engine
+  // an asynchronous decode call in flight (g4_engine_decode_async / _wait)
+  bool async_pending = false;
+  int async_max_tokens = 0, async_r0 = 0, async_dr0 = 0, async_rm[5] = {0, 0, 0, 0, 0};
+  cudaEvent_t aev0 = nullptr, aev1 = nullptr;
+  std::chrono::steady_clock::time_point async_t0;
 };
 
 using namespace g4;
@@ -359,7 +365,9 @@ static int gen_norm(g4_engine* e, float** p, uint64_t id, int n, float mul) {
   return check_launch("gen_norm");
 }
 
-extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
+// Engine creation; with share, the weights (target, drafter, head copies, screen, tensor-core
+// operands, RoPE tables) are the other engine's and only the per-stream state is allocated.
+static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_engine** out) {
   if (!cfg || !out) return set_error(G4_ERR_INVALID, "g4_engine_create: null pointer");
   const g4_engine_config c = *cfg;
   G4_REQUIRE(c.hidden % 256 == 0 && c.hidden >= 256 && c.hidden <= 2048 && c.mlp % 256 == 0 && c.n_layers >= 1 && c.vocab % 128 == 0 &&
@@ -376,6 +384,21 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
   auto fail = [&](int rc) { g4_engine_destroy(e); return rc; };
   if (cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking) != cudaSuccess) return fail(set_error(G4_ERR_CUDA, "stream"));
   const int H = d.H, QD = d.NQ * d.HD, I = d.I;
+  if (share) {
+    const g4_engine_config& sc = share->cfg;
+    if (sc.hidden != c.hidden || sc.n_layers != c.n_layers || sc.mlp != c.mlp || sc.vocab != c.vocab || sc.seed != c.seed ||
+        (c.drafter && !sc.drafter) || c.ctx_max > sc.ctx_max || (c.prefill_tc && !share->tc_ready && sc.prefill_tc))
+      return fail(set_error(G4_ERR_INVALID, "g4_engine_create_shared: configuration differs from the weights' engine"));
+    e->L = share->L;
+    e->DL = share->DL;
+    e->dpre = share->dpre; e->dpost = share->dpost; e->dcent = share->dcent;
+    e->fnorm = share->fnorm; e->dnorm = share->dnorm; e->E = share->E;
+    e->hdata = share->hdata; e->hunp = share->hunp; e->sW4 = share->sW4; e->sS4 = share->sS4; e->scoef = share->scoef;
+    e->hexc_ptr = share->hexc_ptr; e->hexc_col = share->hexc_col; e->hexc_delta = share->hexc_delta;
+    std::memcpy(e->cb8, share->cb8, 8);
+    for (int ty = 0; ty < 2; ++ty) { e->rope[ty][0] = share->rope[ty][0]; e->rope[ty][1] = share->rope[ty][1]; }
+    e->shared = true;
+  } else {
   uint8_t* tmp = nullptr;
   const size_t tmp_bytes = (size_t)std::max({(size_t)(QD + 2 * d.HD) * H / 2, (size_t)2 * I * H / 2, (size_t)I * H / 2,
                                               (size_t)QD * H / 2, (size_t)d.DCENT * H / 2, (size_t)H * 2 * H / 2});
@@ -444,6 +467,7 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
     }
     if (rc) return fail(rc);
   }
+  }  // weights generated (not shared)
   // tensor-core prefill operands and chunk buffers
   if (c.prefill_tc && c.prefill_int8 && H % 128 == 0 && QD % 128 == 0 && I % 128 == 0 && (QD + 2 * d.HD) % 128 == 0) {
     int rc = G4_OK;
@@ -452,35 +476,20 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
       if (ealloc_t(e, &t.w8, (size_t)l.N * l.K) || ealloc_t(e, &t.swT, (size_t)l.N * (l.K / 32))) { rc = G4_ERR_CUDA; return; }
       rc = tc_expand_weights(l.w, l.s, l.N, l.K, t.w8, t.swT, e->st);
     };
-    for (int l = 0; l < d.NL; ++l) {
+    for (int l = 0; l < d.NL && !share; ++l) {
       TLayer& t = e->L[l];
       tc_lin(t.qkv, t.tqkv); tc_lin(t.o, t.to); tc_lin(t.gu, t.tgu); tc_lin(t.down, t.tdown);
     }
-    const int MC = std::min(2048, c.ctx_max / 32 * 32);
-    e->pmc = MC;
-    const size_t kmax = (size_t)std::max({H, I, QD});
-    if (!rc) rc = ealloc_t(e, &e->ptoks, (size_t)MC);
-    if (!rc) rc = ealloc_t(e, &e->px, (size_t)MC * H);
-    if (!rc) rc = ealloc_t(e, &e->pa, (size_t)MC * H);
-    if (!rc) rc = ealloc_t(e, &e->pqkv, (size_t)MC * (QD + 2 * d.HD));
-    if (!rc) rc = ealloc_t(e, &e->patt, (size_t)MC * QD);
-    if (!rc) rc = ealloc_t(e, &e->po, (size_t)MC * H);
-    if (!rc) rc = ealloc_t(e, &e->pgu, (size_t)MC * 2 * I);
-    if (!rc) rc = ealloc_t(e, &e->pact, (size_t)MC * I);
-    if (!rc) rc = ealloc_t(e, &e->pmlp, (size_t)MC * H);
-    if (!rc) rc = ealloc_t(e, &e->pq, (size_t)MC * kmax);
-    if (!rc) rc = ealloc_t(e, &e->psx, (size_t)MC * kmax / 32);
-    if (!rc) rc = ealloc_t(e, &e->psum, (size_t)MC * kmax / 32);
-    if (!rc) rc = ealloc_t(e, &e->psxT, (size_t)MC * kmax / 32);
+    e->pmc = std::min(2048, c.ctx_max / 32 * 32);
     if (rc) return fail(rc);
-    e->tc_ready = true;
+    e->tc_ready = true;  // the chunk buffers are allocated by the first prefill that uses them
   }
   // KV cache and RoPE tables (host, double -> float, as gemma4_engine.cpp:1246-1247)
   const size_t kvn = (size_t)d.NL * c.ctx_max * d.HD;
   if (ealloc_t(e, &e->Kc, kvn) || ealloc_t(e, &e->Vc, kvn)) return fail(G4_ERR_CUDA);
   cudaMemsetAsync(e->Kc, 0, kvn * 2, e->st);
   cudaMemsetAsync(e->Vc, 0, kvn * 2, e->st);
-  {
+  if (!share) {
     const int hh = d.HD / 2;
     std::vector<float> cs((size_t)c.ctx_max * hh), sn((size_t)c.ctx_max * hh);
     for (int ty = 0; ty < 2; ++ty) {
@@ -563,6 +572,13 @@ extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) {
   return G4_OK;
 }
 
+extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) { return create_impl(cfg, nullptr, out); }
+
+extern "C" int g4_engine_create_shared(const g4_engine_config* cfg, const g4_engine* weights, g4_engine** out) {
+  G4_REQUIRE(weights, "g4_engine_create_shared: null weights engine");
+  return create_impl(cfg, weights, out);
+}
+
 extern "C" void g4_engine_destroy(g4_engine* e) {
   if (!e) return;
   if (e->st) cudaStreamSynchronize(e->st);
@@ -574,6 +590,8 @@ extern "C" void g4_engine_destroy(g4_engine* e) {
     if (g) cudaGraphDestroy(g);
   if (e->graw_draft) cudaGraphDestroy(e->graw_draft);
   if (e->rch) cudaFreeHost(e->rch);
+  if (e->aev0) cudaEventDestroy(e->aev0);
+  if (e->aev1) cudaEventDestroy(e->aev1);
   for (auto& ev : e->tev)
     if (ev) cudaEventDestroy(ev);
   if (e->hio) cudaFreeHost(e->hio);
@@ -918,6 +936,28 @@ extern "C" int g4_engine_fake_ctx(g4_engine* e, int n) {
 // run_req (:1582-1680), split in two: prefill in blocks (int8 per ENGINE_PREFILL_INT8, :1595), then
 // resumable decode rounds (chain mode): prompt lookup or k MTP drafts -> one verify forward ->
 // greedy acceptance.  The committed sequence stays on the host (it is the prompt-lookup history).
+// The tensor-core prefill's chunk buffers (pmc rows), allocated on first use.
+static int ensure_chunk_buffers(g4_engine* e) {
+  if (e->ptoks) return G4_OK;
+  const ModelDims& d = e->d;
+  const int H = d.H, QD = d.NQ * d.HD, I = d.I, MC = e->pmc;
+  const size_t kmax = (size_t)std::max({H, I, QD});
+  int rc = ealloc_t(e, &e->ptoks, (size_t)MC);
+  if (!rc) rc = ealloc_t(e, &e->px, (size_t)MC * H);
+  if (!rc) rc = ealloc_t(e, &e->pa, (size_t)MC * H);
+  if (!rc) rc = ealloc_t(e, &e->pqkv, (size_t)MC * (QD + 2 * d.HD));
+  if (!rc) rc = ealloc_t(e, &e->patt, (size_t)MC * QD);
+  if (!rc) rc = ealloc_t(e, &e->po, (size_t)MC * H);
+  if (!rc) rc = ealloc_t(e, &e->pgu, (size_t)MC * 2 * I);
+  if (!rc) rc = ealloc_t(e, &e->pact, (size_t)MC * I);
+  if (!rc) rc = ealloc_t(e, &e->pmlp, (size_t)MC * H);
+  if (!rc) rc = ealloc_t(e, &e->pq, (size_t)MC * kmax);
+  if (!rc) rc = ealloc_t(e, &e->psx, (size_t)MC * kmax / 32);
+  if (!rc) rc = ealloc_t(e, &e->psum, (size_t)MC * kmax / 32);
+  if (!rc) rc = ealloc_t(e, &e->psxT, (size_t)MC * kmax / 32);
+  return rc;
+}
+
 // Prefill of Mc (a multiple of prefill_block, at most pmc) prompt rows at positions pos0.. that form
 // full prefill blocks, through all layers at once: the row kernels of forward() over Mc rows and the
 // tensor-core W4A8 GEMM (the same values as the blocks' GEMVs: prefill blocks of >= 2 rows take the
@@ -988,6 +1028,7 @@ extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int
     const int PB = e->cfg.prefill_block;
     const int nfast = ((n - 1) / PB) * PB;
     const int chunk = std::max(PB, e->pmc / PB * PB);
+    if (nfast > 0) RCK(ensure_chunk_buffers(e));
     while (done < nfast) {
       const int Mc = std::min(chunk, nfast - done);
       RCK(prefill_chunk(e, prompt + done, Mc, FN + done));
@@ -1252,6 +1293,7 @@ static int host_round(g4_engine* e, bool graphs) {
   return G4_OK;
 }
 
+static void finish_stats(g4_engine* e, int n, float gms, std::chrono::steady_clock::time_point t0);
 extern "C" int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, int32_t* out, int* n_out,
                                 g4_engine_stats* stats) {
   G4_REQUIRE(e && n_out && max_rounds >= 0 && max_tokens >= 0 && !e->seq.empty(), "g4_engine_decode: call g4_engine_prefill first");
@@ -1312,6 +1354,15 @@ extern "C" int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, in
   // the committed history: the call's tokens (all of them while they fit the output buffer)
   for (int i = 0; i < ncopy; ++i) e->seq.push_back(got[i]);
   if (out) std::memcpy(out, got.data(), sizeof(int) * std::min(n, ncopy));
+  finish_stats(e, n, gms, t0);
+  *n_out = n;
+  if (stats) *stats = e->stats;
+  return rc0;
+}
+
+// The host mirror and statistics after a decode call (the round state is already read back).
+static void finish_stats(g4_engine* e, int n, float gms, std::chrono::steady_clock::time_point t0) {
+  const RoundCtl& h = *e->rch;
   e->P = h.P;
   e->conf = h.conf;
   e->stopped = h.stopped != 0;
@@ -1329,6 +1380,71 @@ extern "C" int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, in
   st.decode_gpu_ms += gms;
   st.decode_tokens += n;
   st.decode_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
+
+// Asynchronous decode: the rounds of the call are enqueued as one launch of the round-loop graph on
+// the engine's stream (after start_event, when given) and the call returns at once; several engines
+// (g4_engine_create_shared) then decode concurrently.  g4_engine_decode_wait completes the call.
+extern "C" int g4_engine_decode_async(g4_engine* e, int max_rounds, int max_tokens, void* start_event) {
+  G4_REQUIRE(e && max_rounds >= 1 && max_tokens >= 1 && !e->seq.empty() && !e->async_pending,
+             "g4_engine_decode_async: bad arguments or a call already pending");
+  if (!e->cfg.graphs || e->prof.on || e->P + 1 <= e->cfg.att_par || e->stopped || e->P + 1 + 8 >= e->cfg.ctx_max)
+    return set_error(G4_ERR_UNSUPPORTED, "g4_engine_decode_async: needs graphs on, a position past att_par and room in the context");
+  if (!e->gloop && !e->loop_failed && build_loop_graph(e) != G4_OK) {
+    e->loop_failed = true;
+    cudaGetLastError();
+  }
+  if (!e->gloop) return set_error(G4_ERR_UNSUPPORTED, "g4_engine_decode_async: the round-loop graph is unavailable");
+  if (!e->aev0) {
+    ECK(cudaEventCreate(&e->aev0));
+    ECK(cudaEventCreate(&e->aev1));
+  }
+  e->async_t0 = std::chrono::steady_clock::now();
+  e->i8_active = e->cfg.decode_int8 && e->cfg.prefill_int8;
+  if (start_event) ECK(cudaStreamWaitEvent(e->st, reinterpret_cast<cudaEvent_t>(start_event), 0));
+  ECK(cudaEventRecord(e->aev0, e->st));
+  RCK(launch("k_decode_setup", k_decode_setup, dim3(1), dim3(1), 0, e->st, e->rc, max_rounds, max_tokens));
+  e->async_r0 = e->rch->rounds;
+  e->async_dr0 = e->rch->draft_rounds;
+  std::memcpy(e->async_rm, e->rch->rounds_m, sizeof e->async_rm);
+  ECK(cudaGraphLaunch(e->gloop, e->st));
+  ECK(cudaEventRecord(e->aev1, e->st));
+  e->async_max_tokens = max_tokens;
+  e->async_pending = true;
+  return G4_OK;
+}
+
+// Waits for the pending asynchronous call; out / n_out / stats as g4_engine_decode.  ms_since_start
+// (may be NULL): device time from start_event (as passed to g4_engine_decode_async) to the end of
+// this engine's rounds.
+extern "C" int g4_engine_decode_wait(g4_engine* e, int32_t* out, int* n_out, g4_engine_stats* stats, void* start_event,
+                                     float* ms_since_start) {
+  G4_REQUIRE(e && n_out && e->async_pending, "g4_engine_decode_wait: no call pending");
+  e->async_pending = false;
+  ECK(cudaEventSynchronize(e->aev1));
+  RCK(read_round_state(e));
+  const RoundCtl& h = *e->rch;
+  int rc0 = G4_OK;
+  e->stats.kernel_launches += 2 + 2LL * (h.rounds - e->async_r0) + (long long)e->gk_draft * (h.draft_rounds - e->async_dr0);
+  for (int M = 1; M <= 4; ++M) e->stats.kernel_launches += (long long)e->gk_verify[M] * (h.rounds_m[M] - e->async_rm[M]);
+  if (h.rounds == e->async_r0) rc0 = set_error(G4_ERR_CUDA, "g4_engine_decode_wait: the round loop graph ran no round");
+  if (h.ctx_full) rc0 = set_error(G4_ERR_UNSUPPORTED, "g4_engine_decode_wait: context full (%d)", e->cfg.ctx_max);
+  const int n = std::min(h.produced, e->async_max_tokens);
+  const int ncopy = std::min(h.produced, e->out_cap);
+  std::vector<int> got(ncopy);
+  if (ncopy > 0) {
+    ECK(cudaMemcpy(got.data(), e->dout, sizeof(int) * ncopy, cudaMemcpyDeviceToHost));
+    e->stats.d2h_bytes += sizeof(int) * ncopy;
+  }
+  for (int i = 0; i < ncopy; ++i) e->seq.push_back(got[i]);
+  if (out) std::memcpy(out, got.data(), sizeof(int) * std::min(n, ncopy));
+  float gms = 0;
+  cudaEventElapsedTime(&gms, e->aev0, e->aev1);
+  if (ms_since_start) {
+    *ms_since_start = 0.f;
+    if (start_event) cudaEventElapsedTime(ms_since_start, reinterpret_cast<cudaEvent_t>(start_event), e->aev1);
+  }
+  finish_stats(e, n, gms, e->async_t0);
   *n_out = n;
   if (stats) *stats = e->stats;
   return rc0;
@@ -1384,6 +1500,31 @@ extern "C" int g4_engine_time_verify(g4_engine* e, int M, int reps, double* ms_p
   cudaEventDestroy(a);
   cudaEventDestroy(b);
   *ms_per_pass = ms / reps;
+  return G4_OK;
+}
+
+// The decode state of src (KV rows of every layer up to its position, history, hidden, round state)
+// copied into dst, an engine of the same model dimensions: dst continues src's stream.
+extern "C" int g4_engine_copy_state(g4_engine* dst, const g4_engine* src) {
+  G4_REQUIRE(dst && src && !src->seq.empty() && dst->d.H == src->d.H && dst->d.NL == src->d.NL && dst->d.HD == src->d.HD &&
+                 src->P + 1 <= dst->cfg.ctx_max && !dst->async_pending,
+             "g4_engine_copy_state: incompatible engines");
+  ECK(cudaStreamSynchronize(src->st));
+  const size_t n = (size_t)(src->P + 2) * dst->d.HD;  // positions 0..P+1 (the next row is rewritten anyway)
+  for (int l = 0; l < dst->d.NL; ++l) {
+    ECK(cudaMemcpyAsync(dst->Kc + (size_t)l * dst->cfg.ctx_max * dst->d.HD, src->Kc + (size_t)l * src->cfg.ctx_max * src->d.HD,
+                        n * 2, cudaMemcpyDeviceToDevice, dst->st));
+    ECK(cudaMemcpyAsync(dst->Vc + (size_t)l * dst->cfg.ctx_max * dst->d.HD, src->Vc + (size_t)l * src->cfg.ctx_max * src->d.HD,
+                        n * 2, cudaMemcpyDeviceToDevice, dst->st));
+  }
+  ECK(cudaMemcpyAsync(dst->hprev, src->hprev, sizeof(float) * dst->d.H, cudaMemcpyDeviceToDevice, dst->st));
+  dst->seq = src->seq;
+  dst->P = src->P;
+  dst->conf = src->conf;
+  dst->stopped = src->stopped;
+  dst->fake_n = src->fake_n;
+  RCK(upload_round_state(dst));
+  dst->stats = g4_engine_stats{};
   return G4_OK;
 }
 

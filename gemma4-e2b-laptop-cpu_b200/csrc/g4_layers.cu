@@ -155,8 +155,17 @@ __global__ void __launch_bounds__(512) k_qkv_post_w(const float* __restrict__ qk
     xh[k] = k < per ? src[j + hh] : 0.f;
   }
   double s = 0.0;  // partial lane (lanes 0..15): elements lane, lane + 16, ... in order
-  if (lane < 16)
-    for (int i = lane; i < hd; i += 16) { const double d = src[i]; s = fma(d, d, s); }
+  if (lane < 16) {
+    int i = lane;
+    for (; i + 112 < hd; i += 128) {  // 8 loads ahead of the chain
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = src[i + 16 * u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) { const double d = v[u]; s = fma(d, d, s); }
+    }
+    for (; i < hd; i += 16) { const double d = src[i]; s = fma(d, d, s); }
+  }
   double u = s + __shfl_down_sync(FULL, s, 4);   // lanes 0-3, 8-11: p_b + p_4+b and p_8+b + p_12+b
   double t = u + __shfl_down_sync(FULL, u, 8);   // lanes 0-3: t_b
   double v2 = t + __shfl_down_sync(FULL, t, 2);  // lanes 0, 1: t0 + t2, t1 + t3
@@ -344,9 +353,17 @@ __device__ float row_rms_scale(const float4 (&v)[kF4], const float* xs, int n, R
     double s = ((p8[0] + p8[1]) + (p8[2] + p8[3])) + ((p8[4] + p8[5]) + (p8[6] + p8[7]));
     const uint32_t kk = (kw >> (16 * (t & 1))) & 0xFFFFu;  // this partial's (kmax, 255 - kmin)
     const int kmax = (int)(kk >> 8), kmin = 255 - (int)(kk & 0xFFu);
-    if (kmax - kmin > 15) {  // the chain may round: the sequential sum in element order
+    if (kmax - kmin > 15) {  // the chain may round: the sequential sum in element order, 8 loads ahead
       s = 0.0;
-      for (int i = t; i < n; i += 16) { const double x = xs[i]; s = fma(x, x, s); }
+      int i = t;
+      for (; i + 112 < n; i += 128) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = xs[i + 16 * u];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) { const double x = v[u]; s = fma(x, x, s); }
+      }
+      for (; i < n; i += 16) { const double x = xs[i]; s = fma(x, x, s); }
     }
     sc.chain[t] = s;
   }

@@ -55,6 +55,10 @@ SIGNATURES = {
     "g4_engine_decode": (_I, [_P, _I, _I, _P, _P, _P]),
     "g4_engine_phase_times": (_I, [_P, _I, _P, _P]),
     "g4_engine_trace": (_I, [_P, _P, _I, _P]),
+    "g4_engine_create_shared": (_I, [_P, _P, _P]),
+    "g4_engine_copy_state": (_I, [_P, _P]),
+    "g4_engine_decode_async": (_I, [_P, _I, _I, _P]),
+    "g4_engine_decode_wait": (_I, [_P, _P, _P, _P, _P, _P]),
     "g4_engine_time_verify": (_I, [_P, _I, _I, _P]),
     "g4_engine_seg_trace": (_I, [_P, _P, _I, _P]),
     "g4_engine_export_state": (_I, [_P, _I, _P, _P, _P, _I, _P, _P, _P]),
@@ -451,10 +455,15 @@ def engine_config(**kw):
 class Engine:
     """The speculative greedy-decode engine (g4_engine_* in include/g4.h)."""
 
-    def __init__(self, cfg=None, **kw):
+    def __init__(self, cfg=None, share=None, **kw):
+        """share: another Engine whose weights this one uses (an independent request stream)."""
         self.cfg = cfg if cfg is not None else engine_config(**kw)
         self.h = ctypes.c_void_p()
-        check(lib().g4_engine_create(ctypes.byref(self.cfg), ctypes.byref(self.h)), "g4_engine_create")
+        if share is not None:
+            check(lib().g4_engine_create_shared(ctypes.byref(self.cfg), share.h, ctypes.byref(self.h)),
+                  "g4_engine_create_shared")
+        else:
+            check(lib().g4_engine_create(ctypes.byref(self.cfg), ctypes.byref(self.h)), "g4_engine_create")
 
     def close(self):
         if self.h:
@@ -545,6 +554,27 @@ class Engine:
                                            ctypes.byref(n), h.ctypes.data_as(_P), ctypes.byref(P)),
               "g4_engine_export_state")
         return K, V, seq, h, P.value
+
+    def copy_state_from(self, other):
+        """Continue other's stream here (KV cache, history, hidden and round state copied)."""
+        check(lib().g4_engine_copy_state(self.h, other.h), "g4_engine_copy_state")
+
+    def decode_async(self, max_rounds, max_tokens, start_event=None):
+        """Enqueue the rounds of a decode call and return (start_event: a torch.cuda.Event or None)."""
+        ev = ctypes.c_void_p(start_event.cuda_event) if start_event is not None else None
+        check(lib().g4_engine_decode_async(self.h, max_rounds, max_tokens, ev), "g4_engine_decode_async")
+
+    def decode_wait(self, start_event=None):
+        """Complete decode_async: (tokens, stats, device ms since start_event or None)."""
+        import numpy as np
+        out = np.zeros(self.cfg.ctx_max, np.int32)  # a call commits fewer tokens than the context holds
+        n = ctypes.c_int(0)
+        st = EngineStats()
+        ms = ctypes.c_float(0)
+        ev = ctypes.c_void_p(start_event.cuda_event) if start_event is not None else None
+        check(lib().g4_engine_decode_wait(self.h, out.ctypes.data_as(_P), ctypes.byref(n), ctypes.byref(st), ev,
+                                          ctypes.byref(ms)), "g4_engine_decode_wait")
+        return out[: n.value].copy(), st.as_dict(), (ms.value if start_event is not None else None)
 
     PHASES = ("embed_norm_rope", "linear", "attention", "head", "drafter", "copies")
 

@@ -231,6 +231,12 @@ int g4_engine_default_config(g4_engine_config* cfg);
 /* Allocates the weights (generated on the device from cfg->seed), KV cache and buffers. */
 int g4_engine_create(const g4_engine_config* cfg, g4_engine** out);
 void g4_engine_destroy(g4_engine* e);
+/* An engine for another independent request stream over the weights of `weights` (same model
+ * dimensions and seed; ctx_max at most the weights engine's): its own KV cache, activations, round
+ * state, CUDA stream and graphs, no copy of the weights.  `weights` must outlive it.  Independent
+ * streams (the reference serves one request at a time) run concurrently through
+ * g4_engine_decode_async. */
+int g4_engine_create_shared(const g4_engine_config* cfg, const g4_engine* weights, g4_engine** out);
 /* One target forward (fwd) over M <= 32 host tokens at positions pos0..; int8 selects the W4A8
  * path for M >= 2.  When want, rows hf.. get the greedy next token G (host [M]) and, if hbuf is
  * non-null, the final-normed hidden (host [M][hidden]). */
@@ -255,6 +261,14 @@ int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int32_t* first
  * followed by one copy of the committed tokens; verify_gpu_ms and draft_gpu_ms then come from
  * %globaltimer stamps taken by the round kernels, decode_gpu_ms from CUDA events around the call. */
 int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, int32_t* out, int* n_out, g4_engine_stats* stats);
+/* g4_engine_decode in two halves, so that several engines decode at the same time: _async enqueues
+ * the call's rounds (one launch of the round-loop graph; needs graphs on and a position past
+ * att_par) on the engine's stream, after start_event (a cudaEvent_t, may be NULL) when given, and
+ * returns; _wait completes it (out, n_out, stats as for g4_engine_decode; ms_since_start, may be
+ * NULL, = device time from start_event to the end of the rounds). */
+int g4_engine_decode_async(g4_engine* e, int max_rounds, int max_tokens, void* start_event);
+int g4_engine_decode_wait(g4_engine* e, int32_t* out, int* n_out, g4_engine_stats* stats, void* start_event,
+                          float* ms_since_start);
 /* Per-round records since the prefill, 6 ints each: {drafts verified nd, prompt lookup used (1) or MTP
  * (0), the MTP drafts (-1 padded), accepted nacc}; out host [cap_rounds][6]; *n_rounds = rounds
  * recorded (records past the engine's capacity of ctx_max rounds are not kept). */
@@ -268,6 +282,9 @@ int g4_engine_time_verify(g4_engine* e, int M, int reps, double* ms_per_pass);
  * (0 = start, 1 = after the wait on the previous kernel, 2-15 = after each stage and barrier,
  * 20/22 = weight streamer start/end); *n = the element count. */
 int g4_engine_seg_trace(g4_engine* e, unsigned long long* out, int cap, int* n);
+/* Continue src's stream in dst (same model dimensions): the KV rows of every layer up to src's
+ * position, the history, the last hidden state and the round state are copied (device to device). */
+int g4_engine_copy_state(g4_engine* dst, const g4_engine* src);
 /* Decode state after a prefill or decode call: K and V rows of positions [0, npos) of every layer
  * (host [n_layers][npos][256] bf16 each, may be NULL), the committed history (host seq [seq_cap]
  * may be NULL, *seq_len its length), the final-normed hidden of the last committed row (host

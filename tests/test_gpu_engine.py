@@ -250,3 +250,31 @@ def test_tensor_core_prefill_matches_block_prefill(cfg):
     assert f1 == f0 and P1 == P0
     assert np.array_equal(K1, K0) and np.array_equal(V1, V0)
     assert np.array_equal(h1.view(np.uint32), h0.view(np.uint32))
+
+
+def test_shared_weight_streams_decode_concurrently():
+    """Independent request streams: engines over one engine's weights, each with its own prompt, KV
+    cache and stream, decoding at the same time (asynchronous calls), commit the same tokens as the
+    oracle's run of each prompt alone."""
+    cfg = dict(SMALL, ngram=0)
+    base = g4.Engine(g4.engine_config(**cfg))
+    streams = [base] + [g4.Engine(g4.engine_config(**cfg), share=base) for _ in range(3)]
+    om = OracleModel(e2e_config(**cfg))
+    try:
+        prompts = [make_prompt(20 + i, 250 + 7 * i, vocab=4096) for i in range(4)]
+        firsts = [eng.prefill(p) for eng, p in zip(streams, prompts)]
+        start = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for eng in streams:
+            eng.decode_async(6, 1 << 20, start)
+        got = [eng.decode_wait(start) for eng in streams]
+        for p, f, (toks, st, ms) in zip(prompts, firsts, got):
+            ref, _ = om.generate(p, 1 + len(toks))
+            assert [f] + list(toks) == list(ref[: 1 + len(toks)])
+            assert st["rounds"] == 6 and ms is not None and ms > 0
+        assert g4.device_status() == 0
+    finally:
+        for eng in streams[1:]:
+            eng.close()
+        base.close()
+        om.close()
