@@ -410,211 +410,128 @@ def cpu_head_port(head_and_x, rows=8192, seconds=10.0):
 SCREEN_BYTES = N_CFG2 * (K_CFG2 // 2) + N_CFG2 * (K_CFG2 // 32) * 2 + N_CFG2 * 4  # int4 + scales + coef
 
 
-def run_screen_g4(args, world, rank, local):
+def run_screen_g4(args, world, rank, local, dist_=None, steps=None, warmup=None, planted=None, min_seconds=1.0):
     """configs[2]'s certified head screen, vocab-parallel: rank r holds rows [r N/W, (r+1) N/W) of
-    the 262,144 x 2,048 head (screen copy, packed rows, unpacked copy) and one call is the hidden
-    broadcast, the shard's screen, the all-reduced bound, survivors or the shard's full exact head,
-    the all-reduced candidate max and the all-reduced winner (NCCL between the device phases).
-    Total work is fixed as W grows ("strong").  Bytes counted per call: the int4 screen, plus the
-    bf16p rows and exceptions of every shard that fell back."""
+    the 262,144 x 2,048 head (screen copy, packed rows, unpacked copy) and one call is the library's
+    g4_head_screen_dist over its own NCCL communicator: the hidden broadcast, the shard's screen, the
+    all-reduced bound, survivors or the shard's full exact head, the all-reduced candidate max and the
+    all-reduced winner, all on the stream.  The timed calls are replays of a CUDA graph that records
+    16 calls (collectives included), repeated until the timed region lasts >= min_seconds.  Total
+    work is fixed as W grows ("strong").  Bytes counted per call: the int4 screen and the hidden rows,
+    plus the bf16p rows and exceptions of every shard when a shard fell back."""
     import torch
     import g4
+    steps = steps or args.steps
+    warmup = warmup or args.warmup
+    planted = args.planted if planted is None else planted
     torch.cuda.set_device(local)
-    dist_ = init_pg(world, local)
+    if dist_ is None:
+        dist_ = init_pg(world, local)
     g4.device_init()
     n_loc = N_CFG2 // world
     gen = torch.Generator(device="cuda").manual_seed(262144 * 16 + rank)
     E = (torch.randn(n_loc, K_CFG2, device="cuda", generator=gen) * 0.02).to(torch.bfloat16).view(torch.int16)
     shard = g4.ScreenShard(E, rank * n_loc, lim=30000, M=M_CFG2)
-    if args.planted:  # rank 0's rows for the planted hidden states (broadcast to every rank)
-        E0 = E[:M_CFG2 * 9973 + 8].view(torch.bfloat16).float() if rank == 0 else None
-        shard.head_rows_f32 = lambda rows: E0[rows] if E0 is not None else torch.zeros(len(rows), K_CFG2, device="cuda")
-    del E
-    torch.cuda.empty_cache()
     hgen = torch.Generator(device="cuda").manual_seed(2048)
     H = torch.randn(M_CFG2, K_CFG2, device="cuda", generator=hgen) / float(np.sqrt(K_CFG2))
-    if args.planted:  # h = a w_j / |w_j| + sqrt(1 - a^2) noise for rows j of rank 0's shard
+    if planted:  # h = a w_j / |w_j| + sqrt(1 - a^2) noise for rows j of rank 0's shard (broadcast by the call)
         rows = [5 + 9973 * m for m in range(M_CFG2)]
-        Wj = shard.head_rows_f32(rows)
+        Wj = E[rows].view(torch.bfloat16).float()
         a = float(args.plant_weight)
         H = a * Wj / Wj.norm(dim=1, keepdim=True) + float(np.sqrt(max(0.0, 1.0 - a * a))) * H
+    del E
+    torch.cuda.empty_cache()
+    comm = g4.NcclComm(dist_) if dist_ is not None else g4.NcclComm()
+    idx = torch.empty(M_CFG2, dtype=torch.int32, device="cuda")
 
     def step():
-        if dist_ is None:
-            idx, ns = g4.screen_sharded([shard], H)
-        else:
-            idx = g4.screen_shard_dist(shard, H, dist_)
-        return idx
+        return g4.screen_dist_native(shard, H, comm, root=0, out=idx)
 
-    for _ in range(args.warmup):
-        idx = step()
+    for _ in range(warmup):
+        step()
     torch.cuda.synchronize()
-    if dist_ is not None:
-        dist_.broadcast(H, src=0)
     _, ns = shard.select(H, shard.bound(H))  # survivors of this shard (fallback = -1), local bound
     fell_back = bool((ns < 0).any().item())
     nsurv = [int(v) for v in ns.cpu().numpy()]
-    nb = torch.tensor([shard.head.n_exc], dtype=torch.float64, device="cuda")
+    nb = torch.tensor([shard.head.n_exc, float(fell_back)], dtype=torch.float64, device="cuda")
     if dist_ is not None:
         dist_.all_reduce(nb)
-    n_exc = int(nb.item())
-    nbytes = SCREEN_BYTES + M_CFG2 * K_CFG2 * 4 + (N_CFG2 * (K_CFG2 // 32) * 44 + n_exc * 6 if fell_back else 0)
+    n_exc, any_fallback = int(nb[0].item()), bool(nb[1].item() > 0)
+    nbytes = SCREEN_BYTES + M_CFG2 * K_CFG2 * 4 + (N_CFG2 * (K_CFG2 // 32) * 44 + n_exc * 6 if any_fallback else 0)
+    inner = 16
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(inner):
+            step()
+    graph.replay()  # calibration replay (also the graph's warm-up)
+    torch.cuda.synchronize()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record()
+    graph.replay()
+    c1.record()
+    torch.cuda.synchronize()
+    per_replay = max_over_ranks(c0.elapsed_time(c1), dist_)
+    reps = int(max(-(-steps // inner), np.ceil(min_seconds * 1e3 / max(per_replay, 1e-3))))
     barrier(dist_)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         e0.record()
-        for _ in range(args.steps):
-            idx = step()
+        for _ in range(reps):
+            graph.replay()
         e1.record()
         torch.cuda.synchronize()
     barrier(dist_)
-    ms = e0.elapsed_time(e1)
-    ms_max = max_over_ranks(ms, dist_)
-    # e2e: the hidden rows from pinned host memory on rank 0, the winners back to host every call
+    calls = reps * inner
+    ms_max = max_over_ranks(e0.elapsed_time(e1), dist_)
+    del graph  # graphs holding NCCL calls go before the communicator
+    # e2e: the hidden rows from pinned host memory on rank 0 (the call broadcasts them), the winners
+    # back to host every call; eager calls
     hh = H.cpu().pin_memory()
     ih = torch.empty(M_CFG2, dtype=torch.int32).pin_memory()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         if rank == 0:
             H.copy_(hh, non_blocking=True)
-        idx = step()
+        step()
         ih.copy_(idx, non_blocking=True)
         torch.cuda.current_stream().synchronize()
     f1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(f0.elapsed_time(f1), dist_)
+    winners = [int(i) for i in idx.cpu().numpy()]
+    barrier(dist_)
+    comm.close()
     out = None
     if rank == 0:
         peak, peak_kind = measured_peaks()
-        per_gpu = nbytes / world * args.steps / (ms_max / 1e3) / 1e9
+        per_gpu = nbytes / world * calls / (ms_max / 1e3) / 1e9
         out = {
-            "metric": METRIC, "value": nbytes * args.steps / (ms_max / 1e3) / 1e9, "unit": "GB/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "metric": METRIC, "value": nbytes * calls / (ms_max / 1e3) / 1e9, "unit": "GB/s",
+            "n_gpus": world, "steps": calls, "warmup": warmup, "ms_per_step": ms_max / calls,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded head ~ N(0, 0.02) bf16 per shard, h ~ N(0,1)/sqrt(2048))",
             "config": {"workload": f"configs[2] certified head screen 262144x2048, M=4, vocab-parallel x{world}"
-                                   + (f", planted hidden states (weight {args.plant_weight})" if args.planted else ""),
-                       "rows_per_gpu": n_loc, "lim": 30000, "fallback": fell_back, "bytes_per_step": nbytes,
+                                   + (f", planted hidden states (weight {args.plant_weight})" if planted else ""),
+                       "rows_per_gpu": n_loc, "lim": 30000, "fallback": any_fallback, "bytes_per_step": nbytes,
                        "rank0_survivors_local_bound": nsurv,
-                       "collectives": "NCCL broadcast h, all-reduce max (bound, candidate max), all-reduce min "
-                                      "(winner) between the device phases" if world > 1 else "none",
-                       "timing": "CUDA events around K calls (eager launches), max over ranks",
+                       "collectives": ("NCCL (the library's own communicator) broadcast h, all-reduce max (bound, "
+                                       "candidate max), all-reduce min (winner) between the device phases"),
+                       "timing": f"CUDA events around {reps} replays of a graph of {inner} calls (collectives "
+                                 "captured), max over ranks",
                        "parallelism": f"vocab-parallel x{world}"},
             "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
                          "peak_kind": peak_kind, "traffic": None,
                          "kernel": "whole screen call per GPU (screen GEMV + exact-head fallback + collectives)"},
-            "e2e": {"value": nbytes * args.steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
-                    "h2d_bytes_per_step": M_CFG2 * K_CFG2 * 4, "d2h_bytes_per_step": M_CFG2 * 4},
-            "gpu_launches": 13 * args.steps,  # per call: bound 4, select 8, pick 1 (per GPU)
+            "e2e": {"value": nbytes * steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": M_CFG2 * K_CFG2 * 4, "d2h_bytes_per_step": M_CFG2 * 4,
+                    "api": "g4_head_screen_dist per call, eager"},
+            "gpu_launches": 14 * calls,  # per call: bound 4, select 8, pick 1, sentinel 1 (per GPU; NCCL's not counted)
             "clocks": clk.summary(),
-            "winners": [int(i) for i in idx.cpu().numpy()],
+            "winners": winners,
         }
     return out, dist_
-
-
-def cpu_screen_port(rows=16384, seconds=10.0):
-    """The oracle's screen row (screen_task's bound and survivor list, restated) over the first
-    `rows` rows of a configs[2]-distributed head, for M=4 hidden rows, on the host's cores."""
-    from oracle_lib import bf16_bits, or_screen_build, or_screen_row
-    rng = np.random.default_rng(2)
-    E = bf16_bits(rng.standard_normal((rows, K_CFG2), dtype=np.float32) * np.float32(0.02))
-    W4, S4, coef = or_screen_build(E)
-    H = (rng.standard_normal((M_CFG2, K_CFG2), dtype=np.float32) / np.float32(np.sqrt(K_CFG2))).astype(np.float32)
-    nbytes = rows * (K_CFG2 // 2) + rows * (K_CFG2 // 32) * 2 + rows * 4
-    t0 = time.perf_counter()
-    n = 0
-    while time.perf_counter() - t0 < seconds and n < 200:
-        for m in range(M_CFG2):
-            or_screen_row(W4, S4, coef, H[m], lim=rows)
-        n += 1
-    dt = time.perf_counter() - t0
-    return {"value": nbytes * n / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"{n} screens of {rows} rows x M=4 (oracle restatement of screen_task, scalar; no exact head)"}
-
-
-# --------------------------------------------------------------------------- decode workload
-PROMPT_SEED, N_PROMPT = 4, 6841
-TOKENS_METRIC_UNIT = "tok/s"
-
-
-def pass_bytes(P, M, H=2048, NL=30, I=8192, NQ=8, HD=256, V=262144, WINDOW=512):
-    """Algorithmic HBM bytes of one verify pass of M rows after position P: every int4 weight and
-    bf16 group scale of the 30 layers, the K and V rows the attention reads (global layers: all
-    P+M positions; sliding: the last 511+M), the K/V rows written, and the int4 head screen
-    (weights, scales, row coefficients).  Exact rescoring of the few survivors is not counted."""
-    QD = NQ * HD
-
-    def lin(N, K):
-        return N * K // 2 + N * (K // 32) * 2
-
-    per_layer = lin(QD + 2 * HD, H) + lin(H, QD) + lin(2 * I, H) + lin(H, I) + 4 * H * 4 + 2 * HD * 4
-    n_glob = sum(1 for l in range(NL) if l % 5 == 4)
-    keys = n_glob * (P + M) + (NL - n_glob) * min(P + M, WINDOW - 1 + M)
-    kv = keys * HD * 2 * 2 + NL * M * HD * 2 * 2
-    head = V * H // 2 + V * (H // 32) * 2 + V * 4
-    return NL * per_layer + kv + head
-
-
-def host_threads():
-    try:
-        return len(os.sched_getaffinity(0))
-    except (AttributeError, OSError):
-        return os.cpu_count() or 1
-
-
-def timed_decode(eng, args, dist_, local, pad=True):
-    """W warm-up rounds, then K timed rounds in one g4_engine_decode call (one graph launch of the
-    device-side round loop), with untimed padding rounds around it so that the clock record covers
-    the timed call.  Returns (tokens, stats delta, wall ms, clock summary)."""
-    import torch
-    _, st_w = eng.decode(args.warmup, 1 << 30)
-    barrier(dist_)
-    torch.cuda.synchronize()
-    pad_s = 0.4 if pad else 0.0
-    with Clocks(local) as clk:
-        t_pad, n_pad = time.perf_counter(), 0
-        while time.perf_counter() - t_pad < pad_s and n_pad < 60:  # <= 60 rounds: the context must hold them
-            eng.decode(4, 1 << 30)
-            n_pad += 4
-        _, st_w = eng.decode(0, 1 << 30)
-        barrier(dist_)
-        t1 = time.perf_counter()
-        n_tok, st = eng.decode(args.steps, 1 << 30)
-        wall_s = time.perf_counter() - t1
-        t_pad, n_pad = time.perf_counter(), 0
-        while time.perf_counter() - t_pad < pad_s and n_pad < 60:
-            eng.decode(4, 1 << 30)
-            n_pad += 4
-    keys = ("rounds", "ngram_rounds", "drafted", "accepted", "decode_tokens", "verify_passes", "verify_rows",
-            "draft_steps", "verify_gpu_ms", "draft_gpu_ms", "decode_gpu_ms", "h2d_bytes", "d2h_bytes",
-            "kernel_launches", "head_fallbacks")
-    d = {k: st[k] - st_w[k] for k in keys}
-    d["P_end"] = st["decode_tokens"]
-    return n_tok, d, wall_s * 1e3, clk.summary()
-
-
-def decode_roofline(eng, d, M_pass, P_mid, peak, peak_kind):
-    """Roofline of the verify pass: its algorithmic bytes over its device time, the pass replayed
-    with CUDA events around it on the engine stream (g4_engine_time_verify) right after the timed
-    call.  algorithmic_bytes: every weight, the K/V rows read and written and the int4 head screen;
-    with_head_fallback adds the bf16p exact head that every pass read (the screen kept more than its
-    30,000-row limit on this random head)."""
-    ms_pass = eng.time_verify(M_pass, reps=20)
-    alg = pass_bytes(P_mid, M_pass)
-    fb = d["head_fallbacks"] >= d["verify_passes"] > 0
-    alg_fb = alg + (HEAD_BF16P_BYTES if fb else 0)
-    achieved = alg / (ms_pass / 1e3) / 1e9
-    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            "peak_kind": peak_kind, "M": M_pass, "ms_per_pass": ms_pass, "algorithmic_bytes": alg,
-            "frac_uses": "algorithmic_bytes",
-            "with_head_fallback": {"bytes": alg_fb, "achieved": alg_fb / (ms_pass / 1e3) / 1e9,
-                                   "frac": alg_fb / (ms_pass / 1e3) / 1e9 / peak, "every_pass_fell_back": bool(fb)},
-            "traffic": profile_traffic(f"verify_pass_cfg4_m{M_pass}") or profile_traffic("verify_pass_cfg4"),
-            "traffic_kind": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one pass (cold, serialised)",
-            "kernel": f"target verify pass of M={M_pass} rows (30 layers + int4 head screen + exact-head fallback), "
-                      "CUDA events around 20 replays of its graph"}
 
 
 HEAD_BF16P_BYTES = 262144 * (2048 // 32) * 44  # the exact head rows the fallback reads
@@ -668,6 +585,13 @@ def run_decode_g4(args, world, rank, local):
         gemv, _ = run_gemv_g4(args, world, rank, local, dist_=dist_, steps=200, warmup=10)
         if gemv is not None:
             gemv = {k: gemv[k] for k in ("value", "unit", "ms_per_step", "config", "roofline", "e2e", "clocks")}
+    screen = None
+    if not args.no_subrecords:  # configs[2]'s head screen split over the N GPUs (one library call per screen)
+        screen, _ = run_screen_g4(args, world, rank, local, dist_=dist_, steps=64, warmup=5, planted=False)
+        if screen is not None:
+            screen = {k: screen[k] for k in ("value", "unit", "n_gpus", "scaling", "ms_per_step", "config", "roofline",
+                                             "e2e", "clocks", "winners")}
+        torch.cuda.empty_cache()
     out = None
     if rank == 0:
         out = {
@@ -698,6 +622,7 @@ def run_decode_g4(args, world, rank, local):
             "mtp": mtp,
             "streams": streams,
             "gemv_cfg0": gemv,
+            "screen_sharded": screen,
         }
     return out, (dist_, state)
 

@@ -40,6 +40,11 @@ SIGNATURES = {
     "g4_head_screen_shard_bound": (_I, [_P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _SZ, _P]),
     "g4_head_screen_shard_select": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _SZ, _P]),
     "g4_head_screen_shard_pick": (_I, [_I, _I, _I, _I, _P, _P, _P, _SZ, _P]),
+    "g4_head_screen_dist_ws_bytes": (_SZ, [_I, _I, _I]),
+    "g4_head_screen_dist": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _I, _P, _P, _SZ, _P]),
+    "g4_nccl_get_unique_id": (_I, [_P]),
+    "g4_nccl_comm_init": (_I, [_P, _I, _I, _P]),
+    "g4_nccl_comm_destroy": (_I, [_P]),
     "g4_bf16p_unpacked_gemm": (_I, [_P, _P, _P, _P, _I, _I, _P, _I, _P, _I, _P]),
     "g4_screen_build": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "g4_head_screen_ws_bytes": (_SZ, [_I, _I, _I]),
@@ -337,6 +342,56 @@ class ScreenShard:
 
 
 INT_MAX = 0x7FFFFFFF
+
+
+class NcclComm:
+    """A communicator of the library (g4_nccl_comm_init) over the ranks of a torch.distributed group:
+    rank 0's unique id is broadcast through the group."""
+
+    def __init__(self, dist_=None, group=None):
+        """dist_ None: a communicator of this process alone (one rank)."""
+        import torch
+        if dist_ is None:
+            uid = torch.zeros(128, dtype=torch.uint8)
+            check(lib().g4_nccl_get_unique_id(ctypes.c_void_p(uid.data_ptr())), "g4_nccl_get_unique_id")
+            self.h = ctypes.c_void_p()
+            check(lib().g4_nccl_comm_init(ctypes.c_void_p(uid.data_ptr()), 1, 0, ctypes.byref(self.h)), "g4_nccl_comm_init")
+            self.rank, self.world = 0, 1
+            return
+        rank, world = dist_.get_rank(group), dist_.get_world_size(group)
+        uid = torch.zeros(128, dtype=torch.uint8)
+        if rank == 0:
+            check(lib().g4_nccl_get_unique_id(ctypes.c_void_p(uid.data_ptr())), "g4_nccl_get_unique_id")
+        uid_d = uid.cuda()
+        dist_.broadcast(uid_d, src=0, group=group)
+        uid = uid_d.cpu()
+        self.h = ctypes.c_void_p()
+        check(lib().g4_nccl_comm_init(ctypes.c_void_p(uid.data_ptr()), world, rank, ctypes.byref(self.h)),
+              "g4_nccl_comm_init")
+        self.rank, self.world = rank, world
+
+    def close(self):
+        if self.h:
+            lib().g4_nccl_comm_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+
+def screen_dist_native(shard, H, comm, root=0, out=None):
+    """The vocab-parallel screen in one library call (g4_head_screen_dist) over a NcclComm."""
+    import torch
+    M = H.shape[0]
+    idx = out if out is not None else torch.empty(M, dtype=torch.int32, device=H.device)
+    nb = lib().g4_head_screen_dist_ws_bytes(M, shard.N, shard.lim)
+    if getattr(shard, "_dist_ws", None) is None or shard._dist_ws.numel() < nb:
+        shard._dist_ws = torch.empty(nb + 256, dtype=torch.uint8, device=H.device)
+    ws = shard._dist_ws
+    W4, S4, coef = shard.screen
+    h = shard.head
+    check(lib().g4_head_screen_dist(comm.h, root, _ptr(W4), _ptr(S4), _ptr(coef), _ptr(h.data), _ptr(shard.unp), h.cb,
+                                    _ptr(h.exc_ptr), _ptr(h.exc_col), _ptr(h.exc_delta), shard.N, shard.K, shard.row0,
+                                    _ptr(H), M, shard.lim, _ptr(idx), _ptr(ws), ws.numel(), _stream()),
+          "g4_head_screen_dist")
+    return idx
 
 
 def screen_sharded(shards, H):

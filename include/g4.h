@@ -160,6 +160,26 @@ int g4_head_screen_shard_select(const float* coef, const uint8_t* data, const ui
 int g4_head_screen_shard_pick(int N, int M, int lim, int row0, const float* gmax, int* idx_out, void* ws, size_t ws_bytes,
                               void* stream);
 
+/* The vocab-parallel screen in one call over an NCCL communicator (one process per GPU, rank r
+ * holding rows row0.. of the head), on `stream`: broadcast of H (dev [M][K]) from root, the
+ * shard's bound, all-reduce max, survivors / rescoring or the shard's exact head, all-reduce max of
+ * the candidate value, the shard's pick, all-reduce min -> out_idx dev [M] (the same winners on every
+ * rank, -1 = none).  Shard arguments as for g4_head_screen_shard_*; ws dev of
+ * g4_head_screen_dist_ws_bytes (256-byte aligned).  Every step is a stream operation: the call can
+ * be recorded in a CUDA graph.  The reference screens on one host (screen_task :460-538, eval_row
+ * :1453-1474); this is its vocab-parallel form. */
+size_t g4_head_screen_dist_ws_bytes(int M, int N, int lim);
+int g4_head_screen_dist(void* nccl_comm, int root, const uint8_t* W4p, const uint16_t* S4, const float* coef,
+                        const uint8_t* data, const uint8_t* unp, const uint8_t* cb8, const long long* exc_ptr,
+                        const uint16_t* exc_col, const float* exc_delta, int N, int K, int row0, float* H, int M, int lim,
+                        int* out_idx, void* ws, size_t ws_bytes, void* stream);
+/* NCCL communicators for g4_head_screen_dist (NCCL is loaded on first use: libnccl.so.2, the copy
+ * already in the process when there is one): a 128-byte unique id made on one rank and shared by
+ * the caller, a communicator per rank on the current device, and its destruction. */
+int g4_nccl_get_unique_id(void* id128);
+int g4_nccl_comm_init(const void* id128, int nranks, int rank, void** comm);
+int g4_nccl_comm_destroy(void* comm);
+
 /* ---------------------------------------------------------------- split-KV decode attention */
 
 /* Workspace bytes g4_attn_splitkv needs for these sizes. */

@@ -70,3 +70,31 @@ def test_sharded_planted_winners(head_and_shards, key):
     idx, ns = g4.screen_sharded(shards[key], H)
     assert list(idx.cpu().numpy()) == list(idx_ref.cpu().numpy()) == rows
     assert (ns.cpu().numpy() >= 0).all()
+
+
+def test_native_dist_screen_one_rank_matches_single_device():
+    """g4_head_screen_dist (broadcast, three phases, three all-reduces on the stream) over a
+    one-rank NCCL communicator gives the single-device screen's winners, eagerly and replayed from a
+    CUDA graph that records the whole call."""
+    rng = np.random.default_rng(77)
+    N, K = 32768, 2048
+    E = bf16_bits(rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+    Ed = torch.from_numpy(E.view(np.int16)).cuda()
+    shard = g4.ScreenShard(Ed, 0, lim=30000, M=4)
+    H = torch.from_numpy((rng.standard_normal((4, K), dtype=np.float32) / np.float32(45.0)).astype(np.float32)).cuda()
+    ref, _ = g4.head_screen(shard.screen, shard.head, H.clone())
+    comm = g4.NcclComm()
+    try:
+        idx = g4.screen_dist_native(shard, H, comm)
+        assert list(idx.cpu().numpy()) == list(ref.cpu().numpy())
+        out = torch.empty(4, dtype=torch.int32, device="cuda")
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            g4.screen_dist_native(shard, H, comm, out=out)
+        g.replay()
+        torch.cuda.synchronize()
+        assert list(out.cpu().numpy()) == list(ref.cpu().numpy())
+        del g
+    finally:
+        comm.close()
+    assert g4.device_status() == 0
