@@ -534,6 +534,109 @@ def run_screen_g4(args, world, rank, local, dist_=None, steps=None, warmup=None,
     return out, dist_
 
 
+def cpu_screen_port(rows=16384, seconds=10.0):
+    """The oracle's screen row (screen_task's bound and survivor list, restated) over the first
+    `rows` rows of a configs[2]-distributed head, for M=4 hidden rows, on the host's cores."""
+    from oracle_lib import bf16_bits, or_screen_build, or_screen_row
+    rng = np.random.default_rng(2)
+    E = bf16_bits(rng.standard_normal((rows, K_CFG2), dtype=np.float32) * np.float32(0.02))
+    W4, S4, coef = or_screen_build(E)
+    H = (rng.standard_normal((M_CFG2, K_CFG2), dtype=np.float32) / np.float32(np.sqrt(K_CFG2))).astype(np.float32)
+    nbytes = rows * (K_CFG2 // 2) + rows * (K_CFG2 // 32) * 2 + rows * 4
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < seconds and n < 200:
+        for m in range(M_CFG2):
+            or_screen_row(W4, S4, coef, H[m], lim=rows)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": nbytes * n / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{n} screens of {rows} rows x M=4 (oracle restatement of screen_task, scalar; no exact head)"}
+
+
+# --------------------------------------------------------------------------- decode workload
+PROMPT_SEED, N_PROMPT = 4, 6841
+TOKENS_METRIC_UNIT = "tok/s"
+
+
+def pass_bytes(P, M, H=2048, NL=30, I=8192, NQ=8, HD=256, V=262144, WINDOW=512):
+    """Algorithmic HBM bytes of one verify pass of M rows after position P: every int4 weight and
+    bf16 group scale of the 30 layers, the K and V rows the attention reads (global layers: all
+    P+M positions; sliding: the last 511+M), the K/V rows written, and the int4 head screen
+    (weights, scales, row coefficients).  Exact rescoring of the few survivors is not counted."""
+    QD = NQ * HD
+
+    def lin(N, K):
+        return N * K // 2 + N * (K // 32) * 2
+
+    per_layer = lin(QD + 2 * HD, H) + lin(H, QD) + lin(2 * I, H) + lin(H, I) + 4 * H * 4 + 2 * HD * 4
+    n_glob = sum(1 for l in range(NL) if l % 5 == 4)
+    keys = n_glob * (P + M) + (NL - n_glob) * min(P + M, WINDOW - 1 + M)
+    kv = keys * HD * 2 * 2 + NL * M * HD * 2 * 2
+    head = V * H // 2 + V * (H // 32) * 2 + V * 4
+    return NL * per_layer + kv + head
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def timed_decode(eng, args, dist_, local, pad=True):
+    """W warm-up rounds, then K timed rounds in one g4_engine_decode call (one graph launch of the
+    device-side round loop), with untimed padding rounds around it so that the clock record covers
+    the timed call.  Returns (tokens, stats delta, wall ms, clock summary)."""
+    import torch
+    _, st_w = eng.decode(args.warmup, 1 << 30)
+    barrier(dist_)
+    torch.cuda.synchronize()
+    pad_s = 0.4 if pad else 0.0
+    with Clocks(local) as clk:
+        t_pad, n_pad = time.perf_counter(), 0
+        while time.perf_counter() - t_pad < pad_s and n_pad < 60:  # <= 60 rounds: the context must hold them
+            eng.decode(4, 1 << 30)
+            n_pad += 4
+        _, st_w = eng.decode(0, 1 << 30)
+        barrier(dist_)
+        t1 = time.perf_counter()
+        n_tok, st = eng.decode(args.steps, 1 << 30)
+        wall_s = time.perf_counter() - t1
+        t_pad, n_pad = time.perf_counter(), 0
+        while time.perf_counter() - t_pad < pad_s and n_pad < 60:
+            eng.decode(4, 1 << 30)
+            n_pad += 4
+    keys = ("rounds", "ngram_rounds", "drafted", "accepted", "decode_tokens", "verify_passes", "verify_rows",
+            "draft_steps", "verify_gpu_ms", "draft_gpu_ms", "decode_gpu_ms", "h2d_bytes", "d2h_bytes",
+            "kernel_launches", "head_fallbacks")
+    d = {k: st[k] - st_w[k] for k in keys}
+    d["P_end"] = st["decode_tokens"]
+    return n_tok, d, wall_s * 1e3, clk.summary()
+
+
+def decode_roofline(eng, d, M_pass, P_mid, peak, peak_kind):
+    """Roofline of the verify pass: its algorithmic bytes over its device time, the pass replayed
+    with CUDA events around it on the engine stream (g4_engine_time_verify) right after the timed
+    call.  algorithmic_bytes: every weight, the K/V rows read and written and the int4 head screen;
+    with_head_fallback adds the bf16p exact head that every pass read (the screen kept more than its
+    30,000-row limit on this random head)."""
+    ms_pass = eng.time_verify(M_pass, reps=20)
+    alg = pass_bytes(P_mid, M_pass)
+    fb = d["head_fallbacks"] >= d["verify_passes"] > 0
+    alg_fb = alg + (HEAD_BF16P_BYTES if fb else 0)
+    achieved = alg / (ms_pass / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "peak_kind": peak_kind, "M": M_pass, "ms_per_pass": ms_pass, "algorithmic_bytes": alg,
+            "frac_uses": "algorithmic_bytes",
+            "with_head_fallback": {"bytes": alg_fb, "achieved": alg_fb / (ms_pass / 1e3) / 1e9,
+                                   "frac": alg_fb / (ms_pass / 1e3) / 1e9 / peak, "every_pass_fell_back": bool(fb)},
+            "traffic": profile_traffic(f"verify_pass_cfg4_m{M_pass}") or profile_traffic("verify_pass_cfg4"),
+            "traffic_kind": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one pass (cold, serialised)",
+            "kernel": f"target verify pass of M={M_pass} rows (30 layers + int4 head screen + exact-head fallback), "
+                      "CUDA events around 20 replays of its graph"}
+
+
 HEAD_BF16P_BYTES = 262144 * (2048 // 32) * 44  # the exact head rows the fallback reads
 
 

@@ -60,6 +60,12 @@ namespace g4 {
 unsigned status_read_linear(bool reset);
 unsigned status_read_attn(bool reset);
 unsigned status_read_head(bool reset);
+unsigned status_read_tc(bool reset);
+unsigned status_read_stream(bool reset);
+std::atomic<bool>& inflight_fault() {
+  static std::atomic<bool> f{false};
+  return f;
+}
 }
 
 // OR of the device status words of all kernel files on the current device; reset clears them.
@@ -69,8 +75,14 @@ extern "C" int g4_device_status(unsigned* out, int reset) {
   v |= g4::status_read_linear(reset != 0);
   v |= g4::status_read_attn(reset != 0);
   v |= g4::status_read_head(reset != 0);
+  v |= g4::status_read_tc(reset != 0);
+  v |= g4::status_read_stream(reset != 0);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return g4::set_error(G4_ERR_CUDA, "g4_device_status: %s", cudaGetErrorString(e));
+  // bit 1: memory of a CTA that ended may have been written after it ended; nothing is launched
+  // through this library until the status is reset
+  if (reset) g4::inflight_fault().store(false);
+  else if (v & 2u) g4::inflight_fault().store(true);
   *out = v;
   return G4_OK;
 }

@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include "g4.h"
+#include <atomic>
 #include <utility>
 
 namespace g4 {
@@ -28,11 +29,18 @@ struct QuantOut;
 bool encode_tmap_2d(CUtensorMap* out, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
                     uint64_t stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
 bool& pdl_enabled();
+// Set when g4_device_status() has seen the in-flight bit (bit 1) and cleared by its reset: while
+// set, launch() refuses every kernel, since a CTA's shared or tensor memory may have been written
+// after that CTA ended.
+std::atomic<bool>& inflight_fault();
 // Kernels started through launch() on this host thread (the engine counts its launches with it).
 long long& launch_count();
 template <typename... KArgs, typename... Args>
 inline int launch(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                   Args&&... args) {
+  if (inflight_fault().load(std::memory_order_relaxed))
+    return set_error(G4_ERR_TIMEOUT, "%s: refused: a kernel ended with copies in flight (device status bit 1); "
+                                     "reset the device status first", what);
   cudaError_t e;
   if (pdl_enabled()) {
     cudaLaunchConfig_t cfg = {};

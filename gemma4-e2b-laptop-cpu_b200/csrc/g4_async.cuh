@@ -8,11 +8,14 @@
 
 namespace g4 {
 
-// Device status word of this translation unit: bit 0 = a bounded wait gave up.  Each .cu file
+// Device status word of this translation unit: bit 0 = a bounded wait gave up; bit 1 = a CTA
+// returned after a wait gave up while its own copies (or tensor-core operations) could still be in
+// flight, so shared or tensor memory that a later CTA owns may have been written.  Each .cu file
 // gets its own copy (no relocatable device code); G4_STATUS_READER(name) defines the host
 // reader that g4_device_status() calls for it.
 static __device__ unsigned int g_dev_status = 0;
 constexpr unsigned kStatusTimeout = 1u;
+constexpr unsigned kStatusInflight = 2u;
 // Every device-side wait gives up after this long (ns on %globaltimer).
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
@@ -57,7 +60,7 @@ __device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t parity) {
   if (any_fail) {
     if (threadIdx.x == 0) {
       atomicOr(&g_dev_status, kStatusTimeout);
-      mbar_wait(bar, parity);
+      if (!mbar_wait(bar, parity)) atomicOr(&g_dev_status, kStatusInflight);
     }
     __syncthreads();
   }

@@ -922,8 +922,10 @@ int g4::attn_splitkv_dev(const uint16_t* Kc, const uint16_t* Vc, const float* q,
 // hd <= 256, T <= 8 chunks and up to 8,192 keys (kmax - kmin + 1); larger calls are rejected.
 //
 // In host code the name g_attn_scratch only stands for the array; the device address comes from
-// cudaGetSymbolAddress, looked up once per device (with that device current) by the first call on
-// it, so make that first call before any stream capture.  All calls on a device share the array
+// cudaGetSymbolAddress, looked up again by every call made outside stream capture (so an address
+// from before a cudaDeviceReset, after which the module is loaded anew, is never reused) and taken
+// from the last such lookup on that device by calls made while the stream is being captured; make
+// one call on the device before capturing.  All calls on a device share the array
 // and it keeps the previous call's contents; every word a call reads is written earlier in the
 // same call, so nothing needs clearing, but two calls whose kernels overlap on the GPU (two
 // streams, or two host threads) race on it and must be serialised by the caller.
@@ -934,13 +936,16 @@ static __device__ __align__(256) float g_attn_scratch[kAttnNoAllocFloats];
 static std::mutex g_attn_scratch_mu;
 static float* g_attn_scratch_dev[128];
 
-static int attn_scratch_for_current_device(float** out) {
+static int attn_scratch_for_current_device(cudaStream_t st, float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "g4_attn_splitkv_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 128) return set_error(G4_ERR_UNSUPPORTED, "g4_attn_splitkv_noalloc: device %d", dev);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(st, &cs);
+  if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "g4_attn_splitkv_noalloc: cudaStreamIsCapturing: %s", cudaGetErrorString(e));
   std::lock_guard<std::mutex> lk(g_attn_scratch_mu);
-  if (g_attn_scratch_dev[dev] == nullptr) {
+  if (cs == cudaStreamCaptureStatusNone || g_attn_scratch_dev[dev] == nullptr) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_attn_scratch);
     if (e != cudaSuccess || p == nullptr)
@@ -963,8 +968,8 @@ extern "C" int g4_attn_splitkv_noalloc(const uint16_t* Kc, const uint16_t* Vc, c
                      "g4_attn_splitkv_noalloc: M=%d nh=%d hd=%d T=%d keys=%d exceed the fixed scratch "
                      "(hd <= 256, T <= 8, keys <= 8192); use g4_attn_splitkv with a workspace",
                      M, nh, hd, T, len);
-  float* w = nullptr;
-  if (int rc = attn_scratch_for_current_device(&w)) return rc;
   cudaStream_t st = as_stream(stream);
+  float* w = nullptr;
+  if (int rc = attn_scratch_for_current_device(st, &w)) return rc;
   return launch_attn(Kc, Vc, q, d, w, out, st, 0, nullptr, /*four=*/true);
 }

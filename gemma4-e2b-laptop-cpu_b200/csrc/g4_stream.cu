@@ -520,7 +520,8 @@ __device__ void seg_producer(const SegMatDev* mats, int nmats, const int* half_r
     }
   }
   // no copy may still be landing when the CTA exits: wait (bounded) for the last fill of every slot
-  for (int k = ring - 1; k >= 0 && k >= ring - kSegNS; --k) mbar_wait(&sh.full[k % kSegNS], (uint32_t)((k / kSegNS) & 1));
+  for (int k = ring - 1; k >= 0 && k >= ring - kSegNS; --k)
+    if (!mbar_wait(&sh.full[k % kSegNS], (uint32_t)((k / kSegNS) & 1))) atomicOr(&g_dev_status, kStatusInflight);
 }
 
 template <int M>
@@ -727,6 +728,8 @@ __global__ void __launch_bounds__(kSegThreads, 1) k_seg(const __grid_constant__ 
 
 }  // namespace g4
 
+G4_STATUS_READER(stream)
+
 using namespace g4;
 
 namespace g4 {
@@ -760,6 +763,8 @@ int seg_launch(const SegParams& p, cudaStream_t st) {
   }
   const size_t smem = seg_smem_bytes(p.M);
   auto go = [&](auto kern) -> int {
+    if (inflight_fault().load(std::memory_order_relaxed))
+      return set_error(G4_ERR_TIMEOUT, "k_seg: refused: a kernel ended with copies in flight (device status bit 1)");
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int occ = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kSegThreads, smem) != cudaSuccess || occ < 1)

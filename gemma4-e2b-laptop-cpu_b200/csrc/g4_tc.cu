@@ -35,9 +35,10 @@ constexpr int kTcStage = 36 * 1024;            // A + B + sx + sw, rounded to 1 
 constexpr int kTcSmem = kTcNS * kTcStage + 1024;
 
 struct TcShared {
-  uint64_t full[kTcNS], empty[kTcNS], accf[4], acce[4];
+  uint64_t full[kTcNS], empty[kTcNS], accf[4], acce[4], drain;
   uint32_t tmem;
   int abort;
+  int issued;  // stages the producer issued
 };
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -99,8 +100,10 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
   if (threadIdx.x == 0) {
     for (int i = 0; i < kTcNS; ++i) { mbar_init(&sh.full[i], 1); mbar_init(&sh.empty[i], 1 + 8); }
     for (int i = 0; i < 4; ++i) { mbar_init(&sh.accf[i], 1); mbar_init(&sh.acce[i], 8); }
+    mbar_init(&sh.drain, 1);
     fence_mbar_init();
     sh.abort = 0;
+    sh.issued = 0;
   }
   if (warp == 9) {  // tensor memory: 512 columns = 4 buffers x 128
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem)), "r"(512)
@@ -116,7 +119,8 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
 
   if (warp == 8) {
     if (lane == 0) {  // producer
-      for (int s = 0; s < nst && !sh.abort; ++s) {
+      int s = 0;
+      for (; s < nst && !sh.abort; ++s) {
         const int st = s % kTcNS;
         if (s >= kTcNS && !tc_wait(&sh.empty[st], (uint32_t)(((s / kTcNS) - 1) & 1), sh)) break;
         uint8_t* sb = stages + (size_t)st * kTcStage;
@@ -127,6 +131,7 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
           bulk_g2s(sb + kTcTileA + kTcTileB + j * 512, sxT + (size_t)(4 * s + j) * Mpad + m0, 512, &sh.full[st]);
           bulk_g2s(sb + kTcTileA + kTcTileB + kTcSx + j * 256, swT + (size_t)(4 * s + j) * N + n0, 256, &sh.full[st]);
         }
+        sh.issued = s + 1;
       }
     }
   } else if (warp == 9) {
@@ -197,6 +202,17 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
   }
   tc_fence_before();
   __syncthreads();
+  if (sh.abort) {  // a wait gave up: before the CTA frees anything, let its own copies and MMAs finish
+    if (warp == 8 && lane == 0) {
+      for (int k = sh.issued > kTcNS ? sh.issued - kTcNS : 0; k < sh.issued; ++k)
+        if (!mbar_wait(&sh.full[k % kTcNS], (uint32_t)((k / kTcNS) & 1))) atomicOr(&g_dev_status, kStatusInflight);
+    } else if (warp == 9 && lane == 0) {
+      tc_commit(&sh.drain);
+      if (!mbar_wait(&sh.drain, 0)) atomicOr(&g_dev_status, kStatusInflight);
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
   if (warp == 9) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
@@ -240,6 +256,8 @@ __global__ void k_transpose_f32(const float* __restrict__ in, int R, int C, floa
 }
 
 }  // namespace g4
+
+G4_STATUS_READER(tc)
 
 using namespace g4;
 

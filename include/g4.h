@@ -41,7 +41,11 @@ const char* g4_last_error(void);
 /* ABI version of this library (bumped on any signature change). */
 int g4_abi_version(void);
 /* Device status word (OR over the library's kernels on the current device): bit 0 set when a
- * device-side bounded wait gave up.  Synchronous; reset != 0 clears it. */
+ * device-side bounded wait gave up; bit 1 set when a CTA then returned while its own bulk copies
+ * or tensor-core operations could still be in flight (a second bounded wait for them gave up too),
+ * so memory a later CTA owns may have been written.  Once a call has returned bit 1, every
+ * launching entry point fails with G4_ERR_TIMEOUT until a call with reset != 0.  Synchronous;
+ * reset != 0 clears the word. */
 int g4_device_status(unsigned* out, int reset);
 
 /* ---------------------------------------------------------------- W4G32 / W4A8 linears */

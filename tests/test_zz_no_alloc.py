@@ -19,8 +19,7 @@ pytestmark = pytest.mark.gpu
 from g4pkg import g4  # noqa: E402
 
 
-def _inputs(rng, ctx, M, sliding):
-    hd, nh = 256, 8
+def _inputs(rng, ctx, M, sliding, hd=256, nh=8):
     Kc = bf16_bits(rng.standard_normal((ctx, hd), dtype=np.float32))
     Vc = bf16_bits(rng.standard_normal((ctx, hd), dtype=np.float32))
     q = (rng.standard_normal((M, nh, hd), dtype=np.float32) * np.float32(0.0625)).astype(np.float32)
@@ -68,5 +67,31 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     rng = np.random.default_rng(1)
     Kc, Vc, q, pos, lo = _inputs(rng, 8200, 1, False)  # 8,200 keys > 8,192
     rc, _ = _noalloc(Kc, Vc, q, pos, lo)
+    assert rc == -5
+    assert b"exceed the fixed scratch" in g4.lib().g4_last_error()
+
+
+@pytest.mark.parametrize("hd", [128, 256])
+def test_noalloc_at_the_bound_of_its_scratch(hd):
+    """The largest call the fixed scratch serves: 8,192 keys (kmax - kmin + 1), M=4, nh=8, T=8,
+    for both head widths; identical to the workspace entry point."""
+    rng = np.random.default_rng(8192 + hd)
+    Kc, Vc, q, pos, lo = _inputs(rng, 8192, 4, False, hd=hd)
+    assert int(max(pos)) - int(min(lo)) + 1 == 8192
+    rc, out = _noalloc(Kc, Vc, q, pos, lo, T=8)
+    assert rc == 0, g4.lib().g4_last_error().decode()
+    ref = g4.attn_splitkv(Kc, Vc, q, pos, lo, T=8)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    assert g4.device_status() == 0
+
+
+@pytest.mark.parametrize("hd,T", [(256, 9), (512, 8)])
+def test_noalloc_rejects_more_chunks_or_wider_heads(hd, T):
+    """T = 9 chunks and hd = 512 are valid for the workspace entry point but beyond the fixed
+    scratch: G4_ERR_UNSUPPORTED, nothing launched."""
+    rng = np.random.default_rng(hd + T)
+    Kc, Vc, q, pos, lo = _inputs(rng, 600, 2, False, hd=hd)
+    rc, _ = _noalloc(Kc, Vc, q, pos, lo, T=T)
     assert rc == -5
     assert b"exceed the fixed scratch" in g4.lib().g4_last_error()
