@@ -559,11 +559,12 @@ PROMPT_SEED, N_PROMPT = 4, 6841
 TOKENS_METRIC_UNIT = "tok/s"
 
 
-def pass_bytes(P, M, H=2048, NL=30, I=8192, NQ=8, HD=256, V=262144, WINDOW=512):
+def pass_bytes(P, M, H=2048, NL=30, I=8192, NQ=8, HD=256, V=262144, WINDOW=512, head=True):
     """Algorithmic HBM bytes of one verify pass of M rows after position P: every int4 weight and
     bf16 group scale of the 30 layers, the K and V rows the attention reads (global layers: all
-    P+M positions; sliding: the last 511+M), the K/V rows written, and the int4 head screen
-    (weights, scales, row coefficients).  Exact rescoring of the few survivors is not counted."""
+    P+M positions; sliding: the last 511+M), the K/V rows written, and (head=True) the int4 head
+    screen (weights, scales, row coefficients).  Exact rescoring of the few survivors is not
+    counted."""
     QD = NQ * HD
 
     def lin(N, K):
@@ -573,8 +574,8 @@ def pass_bytes(P, M, H=2048, NL=30, I=8192, NQ=8, HD=256, V=262144, WINDOW=512):
     n_glob = sum(1 for l in range(NL) if l % 5 == 4)
     keys = n_glob * (P + M) + (NL - n_glob) * min(P + M, WINDOW - 1 + M)
     kv = keys * HD * 2 * 2 + NL * M * HD * 2 * 2
-    head = V * H // 2 + V * (H // 32) * 2 + V * 4
-    return NL * per_layer + kv + head
+    screen = V * H // 2 + V * (H // 32) * 2 + V * 4
+    return NL * per_layer + kv + (screen if head else 0)
 
 
 def host_threads():
@@ -609,7 +610,7 @@ def timed_decode(eng, args, dist_, local, pad=True):
             n_pad += 4
     keys = ("rounds", "ngram_rounds", "drafted", "accepted", "decode_tokens", "verify_passes", "verify_rows",
             "draft_steps", "verify_gpu_ms", "draft_gpu_ms", "decode_gpu_ms", "h2d_bytes", "d2h_bytes",
-            "kernel_launches", "head_fallbacks")
+            "kernel_launches", "head_fallbacks", "screen_skipped")
     d = {k: st[k] - st_w[k] for k in keys}
     d["P_end"] = st["decode_tokens"]
     return n_tok, d, wall_s * 1e3, clk.summary()
@@ -618,19 +619,27 @@ def timed_decode(eng, args, dist_, local, pad=True):
 def decode_roofline(eng, d, M_pass, P_mid, peak, peak_kind):
     """Roofline of the verify pass: its algorithmic bytes over its device time, the pass replayed
     with CUDA events around it on the engine stream (g4_engine_time_verify) right after the timed
-    call.  algorithmic_bytes: every weight, the K/V rows read and written and the int4 head screen;
-    with_head_fallback adds the bf16p exact head that every pass read (the screen kept more than its
-    30,000-row limit on this random head)."""
+    call.  algorithmic_bytes, per pass: every weight, the K/V rows read and written, plus the head
+    as the timed rounds ran it: the int4 screen on the passes that screened, the bf16p exact head
+    on the passes that read the full head (the screen fell back, or its back-off skipped it), as
+    fractions of the timed passes.  screen_every_pass gives the figure of a pass that screens and
+    whose screen certifies (no exact head): the definition used before the back-off existed."""
     ms_pass = eng.time_verify(M_pass, reps=20)
-    alg = pass_bytes(P_mid, M_pass)
-    fb = d["head_fallbacks"] >= d["verify_passes"] > 0
-    alg_fb = alg + (HEAD_BF16P_BYTES if fb else 0)
+    n = max(1, d["verify_passes"])
+    f_screen = 1.0 - d["screen_skipped"] / n
+    f_full = d["head_fallbacks"] / n
+    base = pass_bytes(P_mid, M_pass, head=False)
+    screen = pass_bytes(P_mid, M_pass) - base
+    alg = int(base + f_screen * screen + f_full * HEAD_BF16P_BYTES)
     achieved = alg / (ms_pass / 1e3) / 1e9
+    alg_s = base + screen
     return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "peak_kind": peak_kind, "M": M_pass, "ms_per_pass": ms_pass, "algorithmic_bytes": alg,
             "frac_uses": "algorithmic_bytes",
-            "with_head_fallback": {"bytes": alg_fb, "achieved": alg_fb / (ms_pass / 1e3) / 1e9,
-                                   "frac": alg_fb / (ms_pass / 1e3) / 1e9 / peak, "every_pass_fell_back": bool(fb)},
+            "head_path": {"screened_frac": f_screen, "full_head_frac": f_full, "layers_kv_bytes": base,
+                          "screen_bytes": screen, "exact_head_bf16p_bytes": HEAD_BF16P_BYTES},
+            "screen_every_pass": {"bytes": alg_s, "achieved": alg_s / (ms_pass / 1e3) / 1e9,
+                                  "frac": alg_s / (ms_pass / 1e3) / 1e9 / peak},
             "traffic": profile_traffic(f"verify_pass_cfg4_m{M_pass}") or profile_traffic("verify_pass_cfg4"),
             "traffic_kind": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one pass (cold, serialised)",
             "kernel": f"target verify pass of M={M_pass} rows (30 layers + int4 head screen + exact-head fallback), "
@@ -712,6 +721,8 @@ def run_decode_g4(args, world, rank, local):
                        "accepted_drafts": d["accepted"], "tokens_per_round": n_tok / rounds,
                        "verify_ms_per_pass_in_decode": d["verify_gpu_ms"] / max(1, d["verify_passes"]),
                        "draft_ms_per_round": d["draft_gpu_ms"] / rounds, "head_fallbacks": d["head_fallbacks"],
+                       "screen_skipped": d["screen_skipped"],
+                       "head_screen": "2: certified screen with back-off after fallbacks (same tokens as screening every pass)",
                        "prefill_s": prefill_s, "l2": "every verify pass streams ~1.37 GB of weights, KV and head "
                        "screen (> 10x the 126 MB L2)", "parallelism": f"replicas x{world}",
                        "timing": "CUDA events on the engine stream around the timed decode call (max over ranks)"},

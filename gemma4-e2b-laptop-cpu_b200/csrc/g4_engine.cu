@@ -86,7 +86,9 @@ struct RoundCtl {
   int nd, drafting, M, used_ng;                  // the current round
   int rounds, ngram_rounds, drafted, accepted;   // totals since the prefill
   int verify_rows, draft_rounds, trace_n, ctx_full;
-  int head_fallbacks, pad_[3];                   // verify passes whose certified screen fell back to the full head
+  int head_fallbacks, pad_[3];                   // verify passes that read the full exact head (screen fell back or skipped)
+  int spol[4];                                   // screen back-off state (ScreenWs::pol): skip count, skipped now,
+                                                 // back-off, passes skipped in total
   int rounds_m[5];                               // rounds by verify rows M (launch accounting)
   int ctx_max, trace_cap, out_cap;
   unsigned long long t_begin, t_verify;          // %globaltimer stamps of the current round
@@ -324,7 +326,7 @@ extern "C" int g4_engine_default_config(g4_engine_config* c) {
   std::memset(c, 0, sizeof *c);
   c->hidden = 2048; c->n_layers = 30; c->mlp = 8192; c->vocab = 262144; c->ctx_max = 8192;
   c->prefill_block = 32; c->k_draft = 3; c->ngram = 2; c->ngram_len = 3; c->prefill_int8 = 1; c->decode_int8 = 1;
-  c->head_screen = 1; c->screen_lim = 30000; c->attn_chunks = 8; c->att_par = 192; c->drafter = 1; c->seed = 20261201ull;
+  c->head_screen = 2; c->screen_lim = 30000; c->attn_chunks = 8; c->att_par = 192; c->drafter = 1; c->seed = 20261201ull;
   c->graphs = 1;
   c->fused_layers = 0;
   c->prefill_tc = 1;
@@ -339,6 +341,11 @@ static int ealloc(g4_engine* e, void** p, size_t bytes) {
 }
 template <class T>
 static int ealloc_t(g4_engine* e, T** p, size_t count) { return ealloc(e, reinterpret_cast<void**>(p), count * sizeof(T)); }
+
+// The screen back-off state inside the device round state.
+static int* screen_policy(g4_engine* e) {
+  return reinterpret_cast<int*>(reinterpret_cast<char*>(e->rc) + offsetof(RoundCtl, spol));
+}
 
 static unsigned gridfor(long long n, int block = 256) { return (unsigned)std::min<long long>((n + block - 1) / block, 1 << 20); }
 
@@ -561,6 +568,8 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
   e->out_cap = c.ctx_max;
   e->trace_cap = c.ctx_max;
   if (!rc) rc = ealloc_t(e, &e->rc, 1);
+  if (!rc && cudaMemsetAsync(e->rc, 0, sizeof(RoundCtl), e->st) != cudaSuccess)  // the screen back-off starts off
+    rc = set_error(G4_ERR_CUDA, "g4_engine_create: %s", cudaGetErrorString(cudaGetLastError()));
   if (!rc) rc = ealloc_t(e, &e->dseq, (size_t)c.ctx_max + 64);
   if (!rc) rc = ealloc_t(e, &e->dout, (size_t)e->out_cap);
   if (!rc) rc = ealloc_t(e, &e->dtrace, (size_t)e->trace_cap * 6);
@@ -797,7 +806,7 @@ head:
     if (e->cfg.head_screen) {
       RCK(head_screen_impl(e->sW4, e->sS4, e->scoef, e->hdata, e->hunp, e->cb8, e->hexc_ptr, e->hexc_col, e->hexc_delta,
                            d.V, H, e->hbuf + (size_t)r0 * H, mh, e->cfg.screen_lim, e->G + r0, e->head_ns, e->head_ws,
-                           e->head_ws_bytes, e->st));
+                           e->head_ws_bytes, e->st, e->cfg.head_screen == 2 ? screen_policy(e) : nullptr));
     } else {
       float* logits = static_cast<float*>(e->head_ws);
       if (e->hunp)
@@ -1377,6 +1386,7 @@ static void finish_stats(g4_engine* e, int n, float gms, std::chrono::steady_clo
   st.verify_gpu_ms = h.verify_ns * 1e-6;
   st.draft_gpu_ms = h.draft_ns * 1e-6;
   st.head_fallbacks = h.head_fallbacks;
+  st.screen_skipped = h.spol[3];
   st.decode_gpu_ms += gms;
   st.decode_tokens += n;
   st.decode_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();

@@ -691,7 +691,15 @@ struct ScreenWs {
   int* surv;     // [M][lim]
   float* fval;   // [M][lim]
   int* slots;    // [2M] pick slots
+  // Screen back-off (nullable, caller-owned int[4]): {passes still to skip, this pass skipped,
+  // current back-off, passes skipped in total}.  While the count is positive a pass skips the
+  // screen and runs the full exact head at once (the winners are the same: the screen only
+  // certifies a shortcut to the exact argmax).  A screen that falls back doubles the back-off
+  // (1, 2, 4, .. kScreenBackoffMax passes); a screen that does not resets it.
+  int* pol;
 };
+constexpr int kScreenBackoffMax = 64;
+__device__ __forceinline__ bool screen_skipped(const ScreenWs& w) { return w.pol != nullptr && w.pol[1] != 0; }
 static size_t screen_ws_layout(int M, int N, int lim, ScreenWs* w, char* base) {
   size_t off = 0;
   auto take = [&](size_t bytes) { char* p = base ? base + off : nullptr; off += (bytes + 255) & ~(size_t)255; return p; };
@@ -707,6 +715,7 @@ static size_t screen_ws_layout(int M, int N, int lim, ScreenWs* w, char* base) {
   if (w) {
     w->s = (float*)s; w->hn = (float*)hn; w->Lord = (int*)L; w->thr = (float*)thr; w->cnt = (int*)cnt; w->fb = (int*)fb;
     w->surv = (int*)surv; w->fval = (float*)fval; w->slots = (int*)slots;
+    w->pol = nullptr;
   }
   return off;
 }
@@ -716,6 +725,14 @@ __global__ void k_screen_init(const float* __restrict__ H, int K, int M, ScreenW
   pdl_wait();
   pdl_trigger();
   const int m = blockIdx.x, lane = threadIdx.x;
+  if (w.pol != nullptr) {  // back-off: this pass goes straight to the exact head
+    const bool skip = w.pol[0] > 0;
+    if (m == 0 && lane == 0) {
+      w.pol[1] = skip ? 1 : 0;
+      if (skip) *w.fb = 1;
+    }
+    if (skip) return;
+  }
   double s = 0;
   if (lane < 16) {
     for (int i = 0; i < K; i += 16) { const double d = H[(size_t)m * K + i + lane]; s = fma(d, d, s); }
@@ -737,6 +754,7 @@ __global__ void k_screen_init(const float* __restrict__ H, int K, int M, ScreenW
 __global__ void k_screen_L(const float* __restrict__ coef, int N, ScreenWs w) {
   pdl_wait();
   pdl_trigger();
+  if (screen_skipped(w)) return;
   const int m = blockIdx.y;
   const float hn = w.hn[m];
   float mx = -1e30f;
@@ -749,6 +767,7 @@ __global__ void k_screen_L(const float* __restrict__ coef, int N, ScreenWs w) {
 __global__ void k_screen_thr(int M, ScreenWs w) {
   pdl_wait();
   pdl_trigger();
+  if (screen_skipped(w)) return;
   const int m = threadIdx.x;
   if (m < M) w.thr[m] = calc_thr(ord2f(w.Lord[m]));
 }
@@ -757,6 +776,7 @@ __global__ void k_screen_thr(int M, ScreenWs w) {
 __global__ void k_screen_collect(const float* __restrict__ coef, int N, int lim, ScreenWs w) {
   pdl_wait();
   pdl_trigger();
+  if (screen_skipped(w)) return;
   const int m = blockIdx.y, lane = threadIdx.x & 31;
   const float hn = w.hn[m], thr = w.thr[m];
   const int wstride = gridDim.x * blockDim.x;
@@ -832,9 +852,21 @@ __global__ void k_screen_pick(int lim, ScreenWs w, int* __restrict__ out, int* _
 __global__ void k_screen_fb_out(const int* __restrict__ slots, int M, const ScreenWs w, int* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
-  if (!*w.fb) return;
   const int m = threadIdx.x;
-  if (m < M) out[m] = slots[2 * m + 1] == 0x7FFFFFFF ? -1 : slots[2 * m + 1];
+  const bool fb = *w.fb != 0;
+  if (fb && m < M) out[m] = slots[2 * m + 1] == 0x7FFFFFFF ? -1 : slots[2 * m + 1];
+  if (w.pol != nullptr && m == 0) {  // back-off for the next passes
+    if (w.pol[1] != 0) {
+      w.pol[0] -= 1;
+      w.pol[3] += 1;
+    } else if (fb) {
+      const int r = w.pol[2] > 0 ? min(2 * w.pol[2], kScreenBackoffMax) : 1;
+      w.pol[2] = r;
+      w.pol[0] = r;
+    } else {
+      w.pol[2] = 0;
+    }
+  }
 }
 
 // ---- vocab-parallel screen: one shard of the head's rows per GPU.  The single-GPU screen is
@@ -1354,7 +1386,7 @@ extern "C" int g4_head_screen(const uint8_t* W4p, const uint16_t* S4, const floa
 int g4::head_screen_impl(const uint8_t* W4p, const uint16_t* S4, const float* coef, const uint8_t* data, const uint8_t* unp,
                          const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col, const float* exc_delta,
                          int N, int K, const float* H, int M, int lim, int* out_idx, int* out_nsurv, void* ws,
-                         size_t ws_bytes, void* stream) {
+                         size_t ws_bytes, void* stream, int* policy) {
   G4_REQUIRE(W4p && S4 && coef && data && cb8 && exc_ptr && H && out_idx && out_nsurv && ws,
              "g4_head_screen: null pointer");
   G4_REQUIRE(M >= 1 && M <= 4 && N > 0 && K > 0 && K % 256 == 0 && lim > 0, "g4_head_screen: bad shape M=%d N=%d K=%d", M,
@@ -1366,11 +1398,12 @@ int g4::head_screen_impl(const uint8_t* W4p, const uint16_t* S4, const float* co
   cudaStream_t st = as_stream(stream);
   ScreenWs w;
   screen_ws_layout(M, N, lim, &w, static_cast<char*>(ws));
+  w.pol = policy;
   HeadPacked P = make_head(data, cb8, exc_ptr, exc_col, exc_delta, N, K);
   P.unp = unp;
   if (int rc_ = launch("k_screen_init", k_screen_init, dim3(M), dim3(32), 0, st, H, K, M, w)) return rc_;
   if (int rc = check_launch("k_screen_init")) return rc;
-  if (int rc = g4_w4g32_gemm(W4p, S4, H, nullptr, M, N, K, w.s, N, stream)) return rc;
+  if (int rc = w4g32_gemm_gated(W4p, S4, H, M, N, K, w.s, N, policy ? policy + 1 : nullptr, st)) return rc;
   if (int rc_ = launch("k_screen_L", k_screen_L, dim3(dim3(296, M)), dim3(256), 0, st, coef, N, w)) return rc_;
   if (int rc_ = launch("k_screen_thr", k_screen_thr, dim3(1), dim3(32), 0, st, M, w)) return rc_;
   if (int rc_ = launch("k_screen_collect", k_screen_collect, dim3(dim3(296, M)), dim3(256), 0, st, coef, N, lim, w)) return rc_;

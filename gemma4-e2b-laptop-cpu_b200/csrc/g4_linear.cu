@@ -331,7 +331,7 @@ __host__ __device__ inline size_t w4g32_tma_smem(int M, int K) {
 template <int M>
 __global__ void __launch_bounds__(kTwThreads, 2)
 k_w4g32_rows_tma(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
-                 const float* __restrict__ X, int N, int K, float* __restrict__ Y, int ldy) {
+                 const float* __restrict__ X, int N, int K, float* __restrict__ Y, int ldy, const int* __restrict__ skip) {
   constexpr int NP = (M + 1) / 2;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[kTwNS];
@@ -340,6 +340,7 @@ k_w4g32_rows_tma(const __grid_constant__ CUtensorMap tw, const __grid_constant__
   float2* gs = reinterpret_cast<float2*>(xs + (size_t)(K / 2) * NP + w4g32_xpad(NP, K / 2));  // [G][NP]
   pdl_wait();
   pdl_trigger();
+  if (skip != nullptr && *skip != 0) return;  // before any copy is issued
   const int G = K >> 5, nch = G >> 3;
   const int nblk = (N + kTwRows - 1) / kTwRows;
   const int myblk = nblk > (int)blockIdx.x ? (nblk - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
@@ -901,8 +902,8 @@ static int launch_w4g32(const uint8_t* Wp, const uint16_t* S, const float* X, co
   return launch_w4g32_t<M, 1, 2>(Wp, S, X, gsum, N, K, Y, ldy, c.CH, c.NB, st);
 }
 
-extern "C" int g4_w4g32_gemm(const uint8_t* Wp, const uint16_t* S, const float* X, const float* gsum, int M, int N,
-                             int K, float* Y, int ldy, void* stream) {
+static int w4g32_gemm_impl(const uint8_t* Wp, const uint16_t* S, const float* X, const float* gsum, int M, int N,
+                           int K, float* Y, int ldy, void* stream, const int* skip) {
   G4_REQUIRE(Wp && S && X && Y, "g4_w4g32_gemm: null pointer");
   G4_REQUIRE(M >= 1 && M <= 8 && N > 0 && K > 0 && K % 256 == 0 && ldy >= N,
              "g4_w4g32_gemm: unsupported shape M=%d N=%d K=%d ldy=%d (K must be a multiple of 256)", M, N, K, ldy);
@@ -920,7 +921,7 @@ extern "C" int g4_w4g32_gemm(const uint8_t* Wp, const uint16_t* S, const float* 
       int occ = 0;
       if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTwThreads, tsmem) != cudaSuccess || occ < 1) occ = 1;
       const int grid = std::min((N + kTwRows - 1) / kTwRows, sm_count() * occ);
-      if (int rc_ = launch("k_w4g32_rows_tma", kern, dim3(grid), dim3(kTwThreads), tsmem, st, tw, ts, X, N, K, Y, ldy))
+      if (int rc_ = launch("k_w4g32_rows_tma", kern, dim3(grid), dim3(kTwThreads), tsmem, st, tw, ts, X, N, K, Y, ldy, skip))
         return rc_;
       return check_launch("k_w4g32_rows_tma");
     };
@@ -958,6 +959,16 @@ extern "C" int g4_w4g32_gemm(const uint8_t* Wp, const uint16_t* S, const float* 
     case 7: return launch_w4g32<7>(Wp, S, X, gsum, N, K, Y, ldy, st);
     default: return launch_w4g32<8>(Wp, S, X, gsum, N, K, Y, ldy, st);
   }
+}
+
+extern "C" int g4_w4g32_gemm(const uint8_t* Wp, const uint16_t* S, const float* X, const float* gsum, int M, int N,
+                             int K, float* Y, int ldy, void* stream) {
+  return w4g32_gemm_impl(Wp, S, X, gsum, M, N, K, Y, ldy, stream, nullptr);
+}
+
+int g4::w4g32_gemm_gated(const uint8_t* Wp, const uint16_t* S, const float* X, int M, int N, int K, float* Y, int ldy,
+                         const int* skip, cudaStream_t st) {
+  return w4g32_gemm_impl(Wp, S, X, nullptr, M, N, K, Y, ldy, st, skip);
 }
 
 extern "C" int g4_w4a8_quant(const float* X, int M, int K, int8_t* q, float* sx, int32_t* sum, void* stream) {

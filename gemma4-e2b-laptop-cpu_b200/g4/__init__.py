@@ -493,7 +493,8 @@ class EngineStats(ctypes.Structure):
                                                                  ("decode_gpu_ms", ctypes.c_double)] + [
         (n, ctypes.c_int) for n in ("verify_passes", "verify_rows", "draft_steps")] + [
         ("verify_gpu_ms", ctypes.c_double), ("draft_gpu_ms", ctypes.c_double), ("h2d_bytes", ctypes.c_longlong),
-        ("d2h_bytes", ctypes.c_longlong), ("kernel_launches", ctypes.c_longlong), ("head_fallbacks", ctypes.c_int)]
+        ("d2h_bytes", ctypes.c_longlong), ("kernel_launches", ctypes.c_longlong), ("head_fallbacks", ctypes.c_int),
+        ("screen_skipped", ctypes.c_int)]
 
     def as_dict(self):
         return {n: getattr(self, n) for n, _ in self._fields_}

@@ -224,7 +224,11 @@ typedef struct {
   int k_draft;                       /* ENGINE_K (3) */
   int ngram, ngram_len;              /* ENGINE_NGRAM (2), ENGINE_NGLEN (3) */
   int prefill_int8, decode_int8;     /* ENGINE_PREFILL_INT8 (1), ENGINE_DECODE_INT8 (1) */
-  int head_screen, screen_lim;       /* ENGINE_HEAD_SCREEN (1), survivor limit (30000) */
+  int head_screen, screen_lim;       /* ENGINE_HEAD_SCREEN: 0 = the full exact head every pass, 1 = the
+                                        certified screen every pass (the reference), 2 = the screen
+                                        with back-off (the default): after a pass whose screen fell
+                                        back, the next 1, 2, 4 .. 64 passes go straight to the full
+                                        exact head; same tokens in all three.  Survivor limit (30000) */
   int attn_chunks;                   /* split-KV key chunks = the reference's pool threads (8) */
   int att_par;                       /* ENGINE_ATT_PAR (192) */
   int drafter;                       /* build the MTP drafter (1) */
@@ -247,8 +251,9 @@ typedef struct {
   double verify_gpu_ms, draft_gpu_ms; /* CUDA events around each verify pass / each round's drafts */
   long long h2d_bytes, d2h_bytes;     /* host<->device copies made by the decode calls */
   long long kernel_launches;          /* kernels the decode calls ran (graph kernel nodes included) */
-  int head_fallbacks;                 /* verify passes whose certified screen kept more than screen_lim
-                                         rows and read the full exact head */
+  int head_fallbacks;                 /* verify passes that read the full exact head: the certified
+                                         screen kept more than screen_lim rows, or was skipped */
+  int screen_skipped;                 /* verify passes that skipped the screen (head_screen = 2) */
 } g4_engine_stats;
 
 int g4_engine_default_config(g4_engine_config* cfg);

@@ -122,6 +122,37 @@ def test_generate_agrees_with_oracle(ngram, graphs, decode_int8, vocab):
         om.close()
 
 
+@pytest.mark.parametrize("graphs,lim", [(1, 8), (0, 8), (1, 200)])
+def test_screen_backoff_gives_the_same_tokens(graphs, lim):
+    """head_screen 2 (the default) skips the certified screen for 1, 2, 4 .. 64 passes after a pass
+    whose screen fell back, and runs the full exact head at once.  With a survivor limit of 8 the
+    screen falls back on every pass it runs; the tokens, statistics and per-round trace equal the
+    oracle's (its pick is over the full exact head) for head_screen 2, 1 (the screen every pass)
+    and 0 (the full exact head every pass)."""
+    cfg = dict(SMALL, ngram=0, screen_lim=lim)
+    om = OracleModel(e2e_config(**cfg))
+    engines = {hs: g4.Engine(g4.engine_config(**cfg, head_screen=hs, graphs=graphs)) for hs in (2, 1, 0)}
+    try:
+        prompt = make_prompt(9, 300, vocab=4096)
+        to, so, tro = om.generate(prompt, 40, trace=True)
+        for hs, eng in engines.items():
+            tg, sg = eng.generate(prompt, 40)
+            assert list(tg) == list(to), hs
+            assert sg["rounds"] == so["rounds"] and sg["accepted"] == so["accepted"], hs
+            assert np.array_equal(eng.trace(), tro), hs
+            if hs == 1:
+                assert sg["screen_skipped"] == 0
+            if hs == 2 and lim == 8:
+                assert sg["head_fallbacks"] == sg["verify_passes"]  # every pass read the full head
+                # screened passes: 1 + the probes after back-offs of 1, 2, 4, ... passes
+                assert sg["screen_skipped"] >= sg["verify_passes"] - 8 and sg["screen_skipped"] > 0
+        assert g4.device_status() == 0
+    finally:
+        for eng in engines.values():
+            eng.close()
+        om.close()
+
+
 def test_decode_calls_resume_and_export_state():
     """Decode in several calls (each one loop-graph launch) continues the same token stream as one
     call, and the exported history is the prompt plus every committed token."""
