@@ -971,6 +971,7 @@ static int ensure_chunk_buffers(g4_engine* e) {
 // full prefill blocks, through all layers at once: the row kernels of forward() over Mc rows and the
 // tensor-core W4A8 GEMM (the same values as the blocks' GEMVs: prefill blocks of >= 2 rows take the
 // int8 path, :311); attention per row with its block's variant (k_attn_rows, variant < 0).
+constexpr int kPrefillRows = 4;  // query rows per block of the prefill attention
 static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0) {
   const ModelDims& d = e->d;
   const int H = d.H, QD = d.NQ * d.HD, ld = QD + 2 * d.HD, I = d.I;
@@ -1001,6 +1002,11 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0) {
       RCK(launch("k_attn_prefill", k_attn_prefill, dim3(Mc, d.NQ / 4), dim3(288), smem, e->st, (const uint16_t*)Kc,
                  (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.HD, pos0, t.global ? 0 : d.WINDOW, e->fake_n,
                  e->cfg.prefill_block, e->patt, QD));
+    } else if (e->cfg.prefill_tc != 3 && d.HD <= 256 && d.HD % 16 == 0 &&
+               sizeof(float) * kPrefillRows * (size_t)(len_max + kPrefillRows - 1) <= 200 * 1024) {
+      // kPrefillRows rows of one head per block share each K and V load
+      RCK(attn_rows_multi(kPrefillRows, Kc, Vc, e->pqkv, ld, d.NQ, d.HD, pos0, Mc, t.global ? 0 : d.WINDOW, len_max,
+                          e->patt, QD, e->fake_n, e->cfg.prefill_block, e->st));
     } else {
       RCK(launch("k_attn_rows", k_attn_rows, dim3(Mc, d.NQ), dim3(256), sizeof(float) * len_max, e->st, (const uint16_t*)Kc,
                  (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.NQ, d.HD, pos0, t.global ? 0 : d.WINDOW, -1, e->patt, QD,

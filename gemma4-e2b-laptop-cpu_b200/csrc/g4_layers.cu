@@ -708,6 +708,193 @@ __global__ void __launch_bounds__(256) k_attn_rows(const uint16_t* __restrict__ 
   }
 }
 
+// ---- prefill attention, R consecutive query rows of one head per block.  The rows of a prefill
+// chunk share their keys (global layers: 0..pos; sliding: a window that moves by one per row), so a
+// block takes rows m0..m0+R-1 (positions pos0+m0..) of head h over the union of their key ranges
+// [lo_0, pos_{R-1}]: every K row it loads feeds R score chains, every V element R O chains, and the
+// R in-order weight sums run side by side.  Per (row, head) the values are k_attn_rows's with
+// variant < 0: scores in the variant's lane order, the row max, exp8 / the correctly rounded exp,
+// the in-order sum, O per dim over the row's keys in order, rounded to bf16.  Keys outside a row's
+// range get weight +0 in its O chain, which leaves the chain bit-exact: it starts at +0, an FMA of
+// a zero weight adds a signed zero to it (x + (-0) = x, and +0 + -0 = +0 under round-to-nearest),
+// and the chain can never hold -0 (it starts at +0 and an exact zero sum rounds to +0).  A group
+// whose rows take different variants runs its rows one at a time.  blockDim 256, hd <= 256, hd % 16
+// == 0; dynamic shared memory R * span floats, span = len_max + R - 1.
+template <int R>
+__global__ void __launch_bounds__(256) k_attn_rows_multi(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
+                                                         const float* __restrict__ q, int ldq, int nh, int hd, int pos0,
+                                                         int Mrows, int window, float* __restrict__ out, int ldo,
+                                                         int blk_fn, int blk, int span) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float sc[];  // [R][span]
+  __shared__ float s_red[8][R];
+  __shared__ float s_mx[R], s_den[R];
+  const int m_first = blockIdx.x * R, h = blockIdx.y, tid = threadIdx.x;
+  const int nr_all = min(R, Mrows - m_first);
+  auto variant_of = [&](int m) {
+    const int pos = pos0 + m;
+    const int b0 = pos - (pos - blk_fn) % blk;
+    return (blk >= 4 && b0 + blk > 64) ? 0 : 1;
+  };
+  bool uniform = true;
+  for (int r = 1; r < nr_all; ++r) uniform = uniform && variant_of(m_first + r) == variant_of(m_first);
+  const int groups = uniform ? 1 : nr_all;
+  for (int gi = 0; gi < groups; ++gi) {
+    const int m0 = m_first + (uniform ? 0 : gi), nr = uniform ? nr_all : 1;
+    const int variant = variant_of(m0);
+    const int pos_lo = pos0 + m0, pos_hi = pos_lo + nr - 1;
+    const int lo_min = window > 0 ? max(0, pos_lo - (window - 1)) : 0;
+    const int sp = pos_hi - lo_min + 1;  // keys of the union (<= span)
+    int lo_r[R], hi_r[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int pr = pos_lo + min(r, nr - 1);
+      lo_r[r] = (window > 0 ? max(0, pr - (window - 1)) : 0) - lo_min;
+      hi_r[r] = r < nr ? pr - lo_min : -1;  // rows past nr own no keys
+    }
+    // scores: one half-warp per key, the two half-warps of a warp take keys pb and pb+1
+    const int hw = tid >> 4, c = tid & 15;
+    if (variant == 0) {
+      float qr[R][16];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float* qh = q + (size_t)(m0 + min(r, nr - 1)) * ldq + (size_t)h * hd;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) qr[r][i] = (i < (hd >> 4)) ? qh[c + 16 * i] : 0.f;
+      }
+      for (int pb = (hw & ~1); pb < sp; pb += 16) {
+        const int j = min(pb + (hw & 1), sp - 1);
+        const uint16_t* kr = Kc + (size_t)(lo_min + j) * hd;
+        float kv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) kv[i] = (i < (hd >> 4)) ? bf2f(kr[c + 16 * i]) : 0.f;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float acc = 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (i < (hd >> 4)) acc = fmaf(qr[r][i], kv[i], acc);
+          const float s = hsum8_octet(__fadd_rn(acc, __shfl_xor_sync(FULL, acc, 8)));
+          if (c == 0 && pb + (hw & 1) < sp && j >= lo_r[r] && j <= hi_r[r]) sc[r * span + j] = s;
+        }
+      }
+    } else {
+      float qr[32];  // variant 1 groups are single rows or rows of one block below position 64
+      for (int r = 0; r < nr; ++r) {
+        const float* qh = q + (size_t)(m0 + r) * ldq + (size_t)h * hd;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) qr[i] = (c < 8 && i < (hd >> 3)) ? qh[c + 8 * i] : 0.f;
+        for (int pb = (hw & ~1); pb < sp; pb += 16) {
+          const int j = min(pb + (hw & 1), sp - 1);
+          const uint16_t* kr = Kc + (size_t)(lo_min + j) * hd;
+          float acc = 0.f;
+          if (c < 8) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < (hd >> 3)) acc = fmaf(qr[i], bf2f(kr[c + 8 * i]), acc);
+          }
+          const float s = hsum8_octet(acc);
+          if (c == 0 && pb + (hw & 1) < sp && j >= lo_r[r] && j <= hi_r[r]) sc[r * span + j] = s;
+        }
+      }
+    }
+    __syncthreads();
+    // row maxima over each row's keys
+    float mx[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      mx[r] = -1e30f;
+      if (r < nr)
+        for (int j = lo_r[r] + tid; j <= hi_r[r]; j += blockDim.x) mx[r] = fmaxf(mx[r], sc[r * span + j]);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx[r] = fmaxf(mx[r], __shfl_xor_sync(FULL, mx[r], o));
+      if ((tid & 31) == 0) s_red[tid >> 5][r] = mx[r];
+    }
+    __syncthreads();
+    if (tid < R) {
+      float v = -1e30f;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v = fmaxf(v, s_red[w][tid]);
+      s_mx[tid] = v;
+    }
+    __syncthreads();
+    // weights; +0 outside each row's keys (and for rows past nr)
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float m_r = s_mx[r];
+      for (int j = tid; j < sp; j += blockDim.x) {
+        const bool in = j >= lo_r[r] && j <= hi_r[r];
+        const float d = in ? __fsub_rn(sc[r * span + j], m_r) : 0.f;
+        sc[r * span + j] = in ? (variant == 0 ? exp8(d) : exp_cr(d)) : 0.f;
+      }
+    }
+    __syncthreads();
+    if (tid < nr) {  // the in-order sums, one thread per row, 8 loads in flight ahead of each chain
+      const float* w = sc + tid * span;
+      float den = 0.f;
+      int j = lo_r[tid];
+      for (; j + 8 <= hi_r[tid] + 1; j += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = w[j + u];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) den = __fadd_rn(den, v[u]);
+      }
+      for (; j <= hi_r[tid]; ++j) den = __fadd_rn(den, w[j]);
+      s_den[tid] = den;
+    }
+    __syncthreads();
+    if (variant == 1) {
+      for (int r = 0; r < nr; ++r)
+        for (int j = lo_r[r] + tid; j <= hi_r[r]; j += blockDim.x) sc[r * span + j] = __fdiv_rn(sc[r * span + j], s_den[r]);
+      __syncthreads();
+    }
+    // O: thread i runs dim i of the R rows over the union's keys in order, 8 V loads in flight
+    for (int i = tid; i < hd; i += blockDim.x) {
+      float o[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) o[r] = 0.f;
+      const uint16_t* vp = Vc + (size_t)lo_min * hd + i;
+      int p = 0;
+      for (; p + 8 <= sp; p += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = bf2f(vp[(size_t)(p + u) * hd]);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+          for (int r = 0; r < R; ++r) o[r] = fmaf(sc[r * span + p + u], v[u], o[r]);
+      }
+      for (; p < sp; ++p) {
+        const float v = bf2f(vp[(size_t)p * hd]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) o[r] = fmaf(sc[r * span + p], v, o[r]);
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        if (r < nr) {
+          const float den = s_den[r];
+          out[(size_t)(m0 + r) * ldo + (size_t)h * hd + i] = variant == 0 ? r16(__fmul_rn(o[r], __fdiv_rn(1.0f, den))) : r16(o[r]);
+        }
+    }
+    __syncthreads();  // the next single-row pass reuses the shared arrays
+  }
+}
+
+int attn_rows_multi(int R, const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0,
+                    int Mrows, int window, int len_max, float* out, int ldo, int blk_fn, int blk, cudaStream_t st) {
+  const int span = len_max + R - 1;
+  const size_t smem = sizeof(float) * (size_t)R * span;
+  if (hd > 256 || hd % 16 != 0 || smem > 200 * 1024 || (R != 4 && R != 8))
+    return set_error(G4_ERR_UNSUPPORTED, "prefill attention: R=%d hd=%d span=%d", R, hd, span);
+  auto go = [&](auto kern) -> int {
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return launch("k_attn_rows_multi", kern, dim3((Mrows + R - 1) / R, nh), dim3(256), smem, st, Kc, Vc, q, ldq, nh, hd,
+                  pos0, Mrows, window, out, ldo, blk_fn, blk, span);
+  };
+  return R == 4 ? go(k_attn_rows_multi<4>) : go(k_attn_rows_multi<8>);
+}
+
 // ---- prefill attention, four query heads of one row per block (they share the KV head: one read of
 // each K and V row serves four heads).  The values are k_attn_rows's, per (row, head): scores in the
 // variant's lane order (variant 0, attn_tile :1061-1083: two 8-lane chains of stride 16; variant 1,

@@ -34,6 +34,12 @@ __global__ void k_draft_in(const uint16_t* E, const int* tok, const float* h, in
 // blk_fn), as fwd chooses per block (:1328-1355).
 __global__ void k_attn_rows(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0,
                             int window, int variant, float* out, int ldo, int blk_fn = 0, int blk = 32);
+// Prefill attention for rows of full prefill blocks, R consecutive rows of one head per block (grid
+// (ceil(Mrows / R), nh), 256 threads, hd <= 256, dynamic shared memory R * span floats with span =
+// len_max + R - 1): the values of k_attn_rows with variant < 0.
+// Returns G4_ERR_UNSUPPORTED (nothing launched) when the shape does not fit.
+int attn_rows_multi(int R, const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0,
+                    int Mrows, int window, int len_max, float* out, int ldo, int blk_fn, int blk, cudaStream_t st);
 // Prefill attention for rows of full prefill blocks, four query heads per block (grid (M, nh / 4),
 // 288 threads, hd <= 256, dynamic shared memory 4 * len_max floats): the values of k_attn_rows with variant < 0.
 __global__ void k_attn_prefill(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int hd, int pos0, int window,

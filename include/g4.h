@@ -240,8 +240,10 @@ typedef struct {
                                         with their norms in one persistent kernel (1), or as one
                                         kernel per step (0, the default: measured faster) */
   int prefill_tc;                    /* prefill the prompt's full blocks with the tensor-core W4A8
-                                        GEMM (tcgen05) over up to 2,048 rows at a time (1), or block
-                                        by block through the GEMV path (0); same values either way */
+                                        GEMM (tcgen05) over up to 2,048 rows at a time (1: attention
+                                        with 4 query rows of a head per block; 3: one row per block;
+                                        2: 4 heads of a row per block), or block by block through the
+                                        GEMV path (0); same values in all four */
 } g4_engine_config;
 typedef struct {
   int rounds, ngram_rounds, drafted, accepted, prefill_tokens, decode_tokens;

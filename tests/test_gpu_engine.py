@@ -261,15 +261,18 @@ def test_fused_segments_match_per_kernel_path():
         om.close()
 
 
-@pytest.mark.parametrize("cfg", [dict(SMALL), dict(ctx_max=2048)])
+@pytest.mark.parametrize("cfg", [dict(SMALL), dict(ctx_max=2048), dict(SMALL, prefill_block=7)])
 def test_tensor_core_prefill_matches_block_prefill(cfg):
     """The prompt's full blocks prefilled at once with the tensor-core W4A8 GEMM write the same KV
     cache, hidden state and first token, bit for bit, as prefill block by block through the GEMV
-    path; at the full width and at reduced dimensions."""
+    path; at the full width and at reduced dimensions; with the attention taking four rows of a head
+    per block (prefill_tc 1) or one (3).  Prefill blocks of 7 rows put the switch from the per-row
+    to the tiled attention variant (the first block ending past position 64) inside a group of four
+    rows, which then runs row by row."""
     vocab = cfg.get("vocab", 262144)
     prompt = make_prompt(11, 777, vocab=vocab)
     outs = []
-    for tc in (1, 0):
+    for tc in (1, 3, 0):
         eng = g4.Engine(g4.engine_config(**cfg, prefill_tc=tc))
         try:
             first = eng.prefill(prompt)
@@ -277,10 +280,11 @@ def test_tensor_core_prefill_matches_block_prefill(cfg):
             outs.append((first, K, V, h, P))
         finally:
             eng.close()
-    (f1, K1, V1, h1, P1), (f0, K0, V0, h0, P0) = outs
-    assert f1 == f0 and P1 == P0
-    assert np.array_equal(K1, K0) and np.array_equal(V1, V0)
-    assert np.array_equal(h1.view(np.uint32), h0.view(np.uint32))
+    f0, K0, V0, h0, P0 = outs[-1]
+    for f1, K1, V1, h1, P1 in outs[:-1]:
+        assert f1 == f0 and P1 == P0
+        assert np.array_equal(K1, K0) and np.array_equal(V1, V0)
+        assert np.array_equal(h1.view(np.uint32), h0.view(np.uint32))
 
 
 def test_shared_weight_streams_decode_concurrently():
