@@ -87,6 +87,7 @@ struct RoundCtl {
   int rounds, ngram_rounds, drafted, accepted;   // totals since the prefill
   int verify_rows, draft_rounds, trace_n, ctx_full;
   int head_fallbacks, pad_[3];                   // verify passes that read the full exact head (screen fell back or skipped)
+  int ngram_accepted, pad2_[3];                  // drafts accepted in prompt-lookup rounds
   int spol[4];                                   // screen back-off state (ScreenWs::pol): skip count, skipped now,
                                                  // back-off, passes skipped in total
   int rounds_m[5];                               // rounds by verify rows M (launch accounting)
@@ -193,7 +194,10 @@ __global__ void __launch_bounds__(256) k_round_end(RoundCtl* rc, int* seq, const
     rc->accepted += nacc;
     rc->verify_rows += rc->M;
     rc->rounds_m[rc->M]++;
-    if (rc->used_ng) rc->ngram_rounds++;
+    if (rc->used_ng) {
+      rc->ngram_rounds++;
+      rc->ngram_accepted += nacc;
+    }
     if (rc->drafting) {
       rc->drafted += nd;
       rc->draft_rounds++;
@@ -317,6 +321,22 @@ struct g4_engine {
   int async_max_tokens = 0, async_r0 = 0, async_dr0 = 0, async_rm[5] = {0, 0, 0, 0, 0};
   cudaEvent_t aev0 = nullptr, aev1 = nullptr;
   std::chrono::steady_clock::time_point async_t0;
+  // prefix cache (run_req, gemma4_engine.cpp:1569-1580): the active conversation's tokens whose K/V
+  // (positions [0, kv_len)) is in the engine's cache, and the stored conversations, each with its
+  // own device K/V buffers ([n_layers][ctx_max][head_dim], like the engine's)
+  struct KvSlot {
+    uint16_t* K = nullptr;
+    uint16_t* V = nullptr;
+    std::vector<int> keys;
+    int kv_len = 0;
+    unsigned long long stamp = 0;
+  };
+  std::vector<int> ctx_keys;
+  int kv_len = 0;
+  unsigned long long clock_tick = 0, active_stamp = 0;
+  std::vector<KvSlot> stored;
+  uint16_t *spareK = nullptr, *spareV = nullptr;
+  int slot_switches = 0, slot_evictions = 0;
 };
 
 using namespace g4;
@@ -330,6 +350,8 @@ extern "C" int g4_engine_default_config(g4_engine_config* c) {
   c->graphs = 1;
   c->fused_layers = 0;
   c->prefill_tc = 1;
+  c->slots = 1;
+  c->slot_min_reuse = 32;
   return G4_OK;
 }
 
@@ -380,7 +402,7 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
   G4_REQUIRE(c.hidden % 256 == 0 && c.hidden >= 256 && c.hidden <= 2048 && c.mlp % 256 == 0 && c.n_layers >= 1 && c.vocab % 128 == 0 &&
                  c.vocab <= (1 << 18) && (c.vocab & (c.vocab - 1)) == 0 && c.ctx_max >= 64 && c.ctx_max <= 32768 &&
                  c.prefill_block >= 1 && c.prefill_block <= 32 && c.k_draft >= 0 && c.k_draft <= 3 && c.attn_chunks >= 1 &&
-                 c.attn_chunks <= 16,
+                 c.attn_chunks <= 16 && c.slots >= 0 && c.slots <= 64 && c.slot_min_reuse >= 0,
              "g4_engine_create: unsupported configuration");
   RCK(g4_device_init());
   g4_engine* e = new g4_engine();
@@ -968,11 +990,11 @@ static int ensure_chunk_buffers(g4_engine* e) {
 }
 
 // Prefill of Mc (a multiple of prefill_block, at most pmc) prompt rows at positions pos0.. that form
-// full prefill blocks, through all layers at once: the row kernels of forward() over Mc rows and the
+// full prefill blocks (the blocks start at position blk_fn), through all layers at once: the row kernels of forward() over Mc rows and the
 // tensor-core W4A8 GEMM (the same values as the blocks' GEMVs: prefill blocks of >= 2 rows take the
 // int8 path, :311); attention per row with its block's variant (k_attn_rows, variant < 0).
 constexpr int kPrefillRows = 4;  // query rows per block of the prefill attention
-static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0) {
+static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0, int blk_fn) {
   const ModelDims& d = e->d;
   const int H = d.H, QD = d.NQ * d.HD, ld = QD + 2 * d.HD, I = d.I;
   const int Mpad = (Mc + 127) / 128 * 128;
@@ -1000,17 +1022,17 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0) {
       if (smem > 200 * 1024) return set_error(G4_ERR_UNSUPPORTED, "prefill attention: %zu B of shared memory", smem);
       if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       RCK(launch("k_attn_prefill", k_attn_prefill, dim3(Mc, d.NQ / 4), dim3(288), smem, e->st, (const uint16_t*)Kc,
-                 (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.HD, pos0, t.global ? 0 : d.WINDOW, e->fake_n,
+                 (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.HD, pos0, t.global ? 0 : d.WINDOW, blk_fn,
                  e->cfg.prefill_block, e->patt, QD));
-    } else if (e->cfg.prefill_tc != 3 && d.HD <= 256 && d.HD % 16 == 0 &&
+    } else if (e->cfg.prefill_tc == 3 && d.HD <= 256 && d.HD % 16 == 0 &&
                sizeof(float) * kPrefillRows * (size_t)(len_max + kPrefillRows - 1) <= 200 * 1024) {
       // kPrefillRows rows of one head per block share each K and V load
       RCK(attn_rows_multi(kPrefillRows, Kc, Vc, e->pqkv, ld, d.NQ, d.HD, pos0, Mc, t.global ? 0 : d.WINDOW, len_max,
-                          e->patt, QD, e->fake_n, e->cfg.prefill_block, e->st));
+                          e->patt, QD, blk_fn, e->cfg.prefill_block, e->st));
     } else {
       RCK(launch("k_attn_rows", k_attn_rows, dim3(Mc, d.NQ), dim3(256), sizeof(float) * len_max, e->st, (const uint16_t*)Kc,
                  (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.NQ, d.HD, pos0, t.global ? 0 : d.WINDOW, -1, e->patt, QD,
-                 e->fake_n, e->cfg.prefill_block));
+                 blk_fn, e->cfg.prefill_block));
     }
     RCK(g4_w4a8_quant(e->patt, Mc, QD, e->pq, e->psx, e->psum, e->st));
     RCK(gemm(t.to, t.o, e->po));
@@ -1031,22 +1053,29 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0) {
 
 static int upload_round_state(g4_engine* e);
 extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int32_t* first_token) {
-  G4_REQUIRE(e && prompt && n >= 1 && e->fake_n + n + 8 <= e->cfg.ctx_max,
-             "g4_engine_prefill: bad arguments (n=%d fake context %d ctx_max=%d)", n, e ? e->fake_n : 0,
+  return g4_engine_prefill_from(e, prompt, n, 0, first_token);
+}
+
+extern "C" int g4_engine_prefill_from(g4_engine* e, const int32_t* prompt, int n, int start, int32_t* first_token) {
+  G4_REQUIRE(e && prompt && n >= 1 && start >= 0 && start < n && e->fake_n + n + 8 <= e->cfg.ctx_max,
+             "g4_engine_prefill: bad arguments (n=%d start=%d fake context %d ctx_max=%d)", n, start, e ? e->fake_n : 0,
              e ? e->cfg.ctx_max : 0);
+  G4_REQUIRE(!e->async_pending, "g4_engine_prefill: a decode call is pending");
   const int H = e->d.H, FN = e->fake_n;
+  e->kv_len = 0;  // the prefix cache's record is rewritten by the request that called this (if any)
+  e->ctx_keys.clear();
   auto t0 = std::chrono::steady_clock::now();
   e->i8_active = e->cfg.prefill_int8 != 0;
-  int done = 0, last_M = 0;
+  int done = start, last_M = 0;
   if (e->tc_ready && e->cfg.prefill_tc && e->i8_active && e->cfg.prefill_block >= 2) {
-    // every full block but the last through the tensor-core path, in chunks
+    // every full block but the last through the tensor-core path, in chunks (blocks from start)
     const int PB = e->cfg.prefill_block;
-    const int nfast = ((n - 1) / PB) * PB;
+    const int nfast = start + ((n - start - 1) / PB) * PB;
     const int chunk = std::max(PB, e->pmc / PB * PB);
-    if (nfast > 0) RCK(ensure_chunk_buffers(e));
+    if (nfast > start) RCK(ensure_chunk_buffers(e));
     while (done < nfast) {
       const int Mc = std::min(chunk, nfast - done);
-      RCK(prefill_chunk(e, prompt + done, Mc, FN + done));
+      RCK(prefill_chunk(e, prompt + done, Mc, FN + done, FN + start));
       done += Mc;
     }
   }
@@ -1070,7 +1099,7 @@ extern "C" int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int
   e->stopped = is_stop(first);
   RCK(upload_round_state(e));
   e->stats = g4_engine_stats{};
-  e->stats.prefill_tokens = n;
+  e->stats.prefill_tokens = n - start;
   e->stats.prefill_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   if (first_token) *first_token = first;
   return G4_OK;
@@ -1393,10 +1422,127 @@ static void finish_stats(g4_engine* e, int n, float gms, std::chrono::steady_clo
   st.draft_gpu_ms = h.draft_ns * 1e-6;
   st.head_fallbacks = h.head_fallbacks;
   st.screen_skipped = h.spol[3];
+  st.ngram_accepted = h.ngram_accepted;
   st.decode_gpu_ms += gms;
   st.decode_tokens += n;
   st.decode_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
 }
+
+// ---- requests with the prefix cache (run_req, gemma4_engine.cpp:1569-1680)
+
+// K/V rows [0, len) of every layer from (sK, sV) to (dK, dV), all laid out as the engine's cache.
+static int kv_copy(g4_engine* e, uint16_t* dK, uint16_t* dV, const uint16_t* sK, const uint16_t* sV, int len) {
+  if (len <= 0) return G4_OK;
+  const size_t pitch = sizeof(uint16_t) * (size_t)e->cfg.ctx_max * e->d.HD;
+  const size_t width = sizeof(uint16_t) * (size_t)len * e->d.HD;
+  ECK(cudaMemcpy2DAsync(dK, pitch, sK, pitch, width, e->d.NL, cudaMemcpyDeviceToDevice, e->st));
+  ECK(cudaMemcpy2DAsync(dV, pitch, sV, pitch, width, e->d.NL, cudaMemcpyDeviceToDevice, e->st));
+  return G4_OK;
+}
+
+// The stored slots' K/V buffers and one spare, allocated by the first request (slots > 1).
+static int ensure_slots(g4_engine* e) {
+  const int ns = std::max(1, e->cfg.slots);
+  if (ns <= 1 || !e->stored.empty()) return G4_OK;
+  const size_t elems = (size_t)e->d.NL * e->cfg.ctx_max * e->d.HD;
+  std::vector<g4_engine::KvSlot> st(ns - 1);
+  for (auto& sl : st) {
+    RCK(ealloc_t(e, &sl.K, elems));
+    RCK(ealloc_t(e, &sl.V, elems));
+  }
+  RCK(ealloc_t(e, &e->spareK, elems));
+  RCK(ealloc_t(e, &e->spareV, elems));
+  e->stored = std::move(st);
+  return G4_OK;
+}
+
+// swap_with (:1576): the active conversation and a stored one change places.  The engine's own cache
+// stays where the captured graphs expect it: the active K/V goes to the spare buffer, the slot's K/V
+// is copied in, and the spare buffer becomes the slot's (device-to-device copies of the valid rows).
+static int swap_with(g4_engine* e, g4_engine::KvSlot& sl) {
+  RCK(kv_copy(e, e->spareK, e->spareV, e->Kc, e->Vc, e->kv_len));
+  RCK(kv_copy(e, e->Kc, e->Vc, sl.K, sl.V, sl.kv_len));
+  std::swap(sl.K, e->spareK);
+  std::swap(sl.V, e->spareV);
+  std::swap(e->ctx_keys, sl.keys);
+  std::swap(e->kv_len, sl.kv_len);
+  std::swap(e->active_stamp, sl.stamp);
+  return G4_OK;
+}
+
+static int lcp_len(const std::vector<int>& k, int klen, const int32_t* p, int n) {
+  int c = 0;
+  while (c < klen && c < n && c < (int)k.size() && k[c] == p[c]) ++c;
+  return c;
+}
+
+extern "C" int g4_engine_request(g4_engine* e, const int32_t* prompt, int n, int max_new, int32_t* out, int* n_out,
+                                 g4_request_info* info) {
+  G4_REQUIRE(e && prompt && n >= 1 && max_new >= 1 && out && n_out, "g4_engine_request: bad arguments");
+  G4_REQUIRE(!e->async_pending, "g4_engine_request: a decode call is pending");
+  RCK(ensure_slots(e));
+  int common = lcp_len(e->ctx_keys, e->kv_len, prompt, n);
+  ++e->clock_tick;
+  int slot_used = 0;
+  if (!e->stored.empty()) {
+    int best = -1, bc = common;
+    for (int i = 0; i < (int)e->stored.size(); ++i) {
+      const int c = lcp_len(e->stored[i].keys, e->stored[i].kv_len, prompt, n);
+      if (c > bc) { bc = c; best = i; }
+    }
+    if (best >= 0) {  // a stored conversation shares more of this prompt: switch to it
+      e->active_stamp = e->clock_tick;
+      RCK(swap_with(e, e->stored[best]));
+      ++e->slot_switches;
+      slot_used = best + 1;
+      common = bc;
+    } else if (bc < e->cfg.slot_min_reuse) {  // nothing worth reusing: the LRU slot takes the active one
+      int v = 0;
+      for (int i = 1; i < (int)e->stored.size(); ++i)
+        if (e->stored[i].stamp < e->stored[v].stamp) v = i;
+      e->active_stamp = e->clock_tick;
+      RCK(swap_with(e, e->stored[v]));
+      e->kv_len = 0;
+      e->ctx_keys.clear();
+      common = 0;
+      ++e->slot_evictions;
+      slot_used = v + 1;
+    }
+    e->active_stamp = e->clock_tick;
+  }
+  const int start = std::min(common, n - 1);  // the last prompt token always runs (its logits and hidden)
+  auto t0 = std::chrono::steady_clock::now();
+  int first = 0;
+  RCK(g4_engine_prefill_from(e, prompt, n, start, &first));
+  const double prefill_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  out[0] = first;
+  int got = 0;
+  auto t1 = std::chrono::steady_clock::now();
+  if (max_new > 1 && !e->stopped) RCK(g4_engine_decode(e, 1 << 30, max_new - 1, out + 1, &got, nullptr));
+  const double decode_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t1).count();
+  int total = 1 + got;
+  for (int i = 0; i < total; ++i)
+    if (is_stop(out[i])) { total = i + 1; break; }
+  *n_out = total;
+  // the conversation's tokens whose K/V is written: positions 0..P (:1601)
+  const size_t nk = std::min(e->seq.size(), (size_t)std::max(0, e->P - e->fake_n + 1));
+  e->ctx_keys.assign(e->seq.begin(), e->seq.begin() + nk);
+  e->kv_len = e->fake_n ? 0 : std::min(e->P + 1, (int)e->ctx_keys.size());
+  if (info) {
+    info->prompt_tokens = n;
+    info->reused = start;
+    info->slot = slot_used;
+    info->tokens = total;
+    info->prefill_ms = prefill_ms;
+    info->decode_ms = decode_ms;
+    info->slot_switches = e->slot_switches;
+    info->slot_evictions = e->slot_evictions;
+    info->kv_len = e->kv_len;
+  }
+  return G4_OK;
+}
+
+
 
 // Asynchronous decode: the rounds of the call are enqueued as one launch of the round-loop graph on
 // the engine's stream (after start_event, when given) and the call returns at once; several engines

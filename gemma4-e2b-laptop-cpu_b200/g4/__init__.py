@@ -57,6 +57,8 @@ SIGNATURES = {
     "g4_engine_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "g4_engine_fake_ctx": (_I, [_P, _I]),
     "g4_engine_prefill": (_I, [_P, _P, _I, _P]),
+    "g4_engine_prefill_from": (_I, [_P, _P, _I, _I, _P]),
+    "g4_engine_request": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "g4_engine_decode": (_I, [_P, _I, _I, _P, _P, _P]),
     "g4_engine_phase_times": (_I, [_P, _I, _P, _P]),
     "g4_engine_trace": (_I, [_P, _P, _I, _P]),
@@ -483,7 +485,7 @@ class EngineConfig(ctypes.Structure):
                                             "ngram", "ngram_len", "prefill_int8", "decode_int8", "head_screen",
                                             "screen_lim", "attn_chunks", "att_par", "drafter")] + [
         ("seed", ctypes.c_ulonglong), ("graphs", ctypes.c_int), ("fused_layers", ctypes.c_int),
-        ("prefill_tc", ctypes.c_int)]
+        ("prefill_tc", ctypes.c_int), ("slots", ctypes.c_int), ("slot_min_reuse", ctypes.c_int)]
 
 
 class EngineStats(ctypes.Structure):
@@ -494,7 +496,17 @@ class EngineStats(ctypes.Structure):
         (n, ctypes.c_int) for n in ("verify_passes", "verify_rows", "draft_steps")] + [
         ("verify_gpu_ms", ctypes.c_double), ("draft_gpu_ms", ctypes.c_double), ("h2d_bytes", ctypes.c_longlong),
         ("d2h_bytes", ctypes.c_longlong), ("kernel_launches", ctypes.c_longlong), ("head_fallbacks", ctypes.c_int),
-        ("screen_skipped", ctypes.c_int)]
+        ("screen_skipped", ctypes.c_int), ("ngram_accepted", ctypes.c_int)]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+class RequestInfo(ctypes.Structure):
+    """g4_request_info (include/g4.h)."""
+    _fields_ = [(n, ctypes.c_int) for n in ("prompt_tokens", "reused", "slot", "tokens")] + [
+        ("prefill_ms", ctypes.c_double), ("decode_ms", ctypes.c_double)] + [
+        (n, ctypes.c_int) for n in ("slot_switches", "slot_evictions", "kv_len")]
 
     def as_dict(self):
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -550,13 +562,25 @@ class Engine:
         starts at position n."""
         check(lib().g4_engine_fake_ctx(self.h, int(n)), "g4_engine_fake_ctx")
 
-    def prefill(self, prompt):
+    def prefill(self, prompt, start=0):
+        """start > 0: keep the K/V of positions < start (g4_engine_prefill_from)."""
         import numpy as np
         prompt = np.ascontiguousarray(prompt, np.int32)
         first = ctypes.c_int(0)
-        check(lib().g4_engine_prefill(self.h, prompt.ctypes.data_as(_P), prompt.size, ctypes.byref(first)),
-              "g4_engine_prefill")
+        check(lib().g4_engine_prefill_from(self.h, prompt.ctypes.data_as(_P), prompt.size, int(start),
+                                           ctypes.byref(first)), "g4_engine_prefill_from")
         return first.value
+
+    def request(self, prompt, max_new):
+        """One request through the prefix cache (g4_engine_request): (tokens, info dict)."""
+        import numpy as np
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(max(1, int(max_new)), np.int32)
+        n = ctypes.c_int(0)
+        info = RequestInfo()
+        check(lib().g4_engine_request(self.h, prompt.ctypes.data_as(_P), prompt.size, int(max_new),
+                                      out.ctypes.data_as(_P), ctypes.byref(n), ctypes.byref(info)), "g4_engine_request")
+        return out[: n.value].copy(), info.as_dict()
 
     def decode(self, max_rounds, max_tokens, out=None):
         import numpy as np

@@ -241,9 +241,13 @@ typedef struct {
                                         kernel per step (0, the default: measured faster) */
   int prefill_tc;                    /* prefill the prompt's full blocks with the tensor-core W4A8
                                         GEMM (tcgen05) over up to 2,048 rows at a time (1: attention
-                                        with 4 query rows of a head per block; 3: one row per block;
-                                        2: 4 heads of a row per block), or block by block through the
-                                        GEMV path (0); same values in all four */
+                                        with one query row of a head per block, measured fastest; 3:
+                                        4 rows of a head per block; 2: 4 heads of a row per block), or
+                                        block by block through the GEMV path (0); same values in all
+                                        four */
+  int slots;                         /* ENGINE_SLOTS (1): conversations kept for the prefix cache (the
+                                        active one and slots - 1 stored, each with its own K/V) */
+  int slot_min_reuse;                /* ENGINE_SLOT_MIN_REUSE (32) */
 } g4_engine_config;
 typedef struct {
   int rounds, ngram_rounds, drafted, accepted, prefill_tokens, decode_tokens;
@@ -256,6 +260,7 @@ typedef struct {
   int head_fallbacks;                 /* verify passes that read the full exact head: the certified
                                          screen kept more than screen_lim rows, or was skipped */
   int screen_skipped;                 /* verify passes that skipped the screen (head_screen = 2) */
+  int ngram_accepted;                 /* drafts accepted in prompt-lookup rounds */
 } g4_engine_stats;
 
 int g4_engine_default_config(g4_engine_config* cfg);
@@ -282,6 +287,12 @@ int g4_engine_fake_ctx(g4_engine* e, int n);
 /* Prefill a prompt (host [n]) in blocks of prefill_block and reset the decode state; *first_token =
  * the greedy token after the prompt. */
 int g4_engine_prefill(g4_engine* e, const int32_t* prompt, int n, int32_t* first_token);
+/* Prefill from prompt position start (0 <= start < n), keeping the K/V of positions < start: the
+ * caller guarantees that they hold prompt[0, start) (an earlier request's prefix; the request API
+ * below tracks it).  The prefill blocks start at start, as run_req's do after a prefix-cache hit
+ * (gemma4_engine.cpp:1597-1600), so the values are those of the reference's reuse, not of a full
+ * prefill.  start = 0 is g4_engine_prefill. */
+int g4_engine_prefill_from(g4_engine* e, const int32_t* prompt, int n, int start, int32_t* first_token);
 /* Continue speculative greedy decode for up to max_rounds rounds or max_tokens committed tokens
  * (whichever comes first) or a stop token; out host [max_tokens] (may be NULL), *n_out = tokens
  * committed by this call; stats (may be NULL) accumulate since the prefill.
@@ -300,6 +311,26 @@ int g4_engine_decode(g4_engine* e, int max_rounds, int max_tokens, int32_t* out,
 int g4_engine_decode_async(g4_engine* e, int max_rounds, int max_tokens, void* start_event);
 int g4_engine_decode_wait(g4_engine* e, int32_t* out, int* n_out, g4_engine_stats* stats, void* start_event,
                           float* ms_since_start);
+/* One request of run_req (gemma4_engine.cpp:1581-1613) with its prefix cache (:1569-1594): the
+ * conversation (the active one or a stored slot) whose committed tokens share the longest prefix
+ * with the prompt becomes active (a stored one is swapped in); if no stored conversation shares
+ * more than the active one and the best shares fewer than slot_min_reuse tokens, the least recently
+ * used slot takes the active conversation and the request starts from an empty cache.  Then prefill
+ * from min(shared, n - 1) (g4_engine_prefill_from) and decode until max_new tokens (the first from
+ * the prefill) or a stop token.  out host [max_new]; *n_out = tokens, cut after the first stop
+ * token.  With slots = 1 only the active conversation is reused. */
+typedef struct {
+  int prompt_tokens;                 /* n */
+  int reused;                        /* prompt positions whose K/V came from the cache */
+  int slot;                          /* 0: the active conversation; i: stored slot i - 1 was switched in
+                                        or, on an eviction, took the active conversation */
+  int tokens;                        /* *n_out */
+  double prefill_ms, decode_ms;      /* host wall clock */
+  int slot_switches, slot_evictions; /* totals since the engine was created */
+  int kv_len;                        /* positions of the active conversation now in the cache */
+} g4_request_info;
+int g4_engine_request(g4_engine* e, const int32_t* prompt, int n, int max_new, int32_t* out, int* n_out,
+                      g4_request_info* info);
 /* Per-round records since the prefill, 6 ints each: {drafts verified nd, prompt lookup used (1) or MTP
  * (0), the MTP drafts (-1 padded), accepted nacc}; out host [cap_rounds][6]; *n_rounds = rounds
  * recorded (records past the engine's capacity of ctx_max rounds are not kept). */

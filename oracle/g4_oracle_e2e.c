@@ -512,13 +512,17 @@ void or_e2e_fake_ctx(void* mp, int n) {
 /* run_req (:1582-1663), split like the engine's API into a prefill (blocks of prefill_block, int8 per
  * ENGINE_PREFILL_INT8, :1595) and resumable chain-mode decode rounds (prompt lookup or k MTP drafts
  * -> one verify forward -> greedy acceptance).  The decode state lives in the model. */
-int or_e2e_prefill(void* mp, const int32_t* prompt, int n, int32_t* first) {
+/* run_req's prefill (:1598-1600) from prompt position start: the K/V rows of positions < start are
+ * kept (they hold an earlier request's prefix of this prompt, the prefix cache), the blocks of
+ * prefill_block rows start at start. */
+int or_e2e_prefill_from(void* mp, const int32_t* prompt, int n, int start, int32_t* first) {
   Model* m = (Model*)mp;
   const int FN = m->fake_n, H = m->H;
+  if (start < 0 || start >= n) return -1;
   int G[64];
   float* hbuf = (float*)malloc(sizeof(float) * 64 * H);
   m->i8 = m->prefill_int8;
-  int done = 0, lastM = 0;
+  int done = start, lastM = 0;
   while (done < n) {
     const int M = m->prefill_block < n - done ? m->prefill_block : n - done;
     const int last = done + M == n;
@@ -539,6 +543,17 @@ int or_e2e_prefill(void* mp, const int32_t* prompt, int n, int32_t* first) {
   memset(m->st, 0, sizeof m->st);
   if (first) *first = G[lastM - 1];
   free(hbuf);
+  return 0;
+}
+int or_e2e_prefill(void* mp, const int32_t* prompt, int n, int32_t* first) { return or_e2e_prefill_from(mp, prompt, n, 0, first); }
+
+/* The committed history (prompt and every committed token) and the last committed position P. */
+int or_e2e_history(void* mp, int32_t* out, int cap, int* len, int* P) {
+  Model* m = (Model*)mp;
+  const int k = m->seq_len < cap ? m->seq_len : cap;
+  if (out && m->seq) memcpy(out, m->seq, sizeof(int32_t) * (size_t)k);
+  *len = m->seq_len;
+  *P = m->P;
   return 0;
 }
 

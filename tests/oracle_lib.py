@@ -53,6 +53,8 @@ _SIGS_ORACLE = {
     "or_e2e_generate": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "or_e2e_generate_trace": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _I]),
     "or_e2e_prefill": (_I, [_P, _P, _I, _P]),
+    "or_e2e_prefill_from": (_I, [_P, _P, _I, _I, _P]),
+    "or_e2e_history": (_I, [_P, _P, _I, _P, _P]),
     "or_e2e_decode": (_I, [_P, _I, _I, _P, _P, _P, _P, _I]),
     "or_e2e_set_state": (_I, [_P, _P, _P, _I, _P, _I, _P, _I]),
     "or_e2e_set_hooks": (_I, [_P, _P]),
@@ -313,11 +315,20 @@ class OracleModel:
             return out[: n_out[0]].copy(), stats, tr[: stats["rounds"]].copy()
         return out[: n_out[0]].copy(), stats
 
-    def prefill(self, prompt):
+    def prefill(self, prompt, start=0):
+        """start > 0: keep the K/V of positions < start (a prefix of this prompt prefilled earlier)."""
         prompt = np.ascontiguousarray(prompt, np.int32)
         first = np.zeros(1, np.int32)
-        oracle().or_e2e_prefill(self.h, ptr(prompt), prompt.size, ptr(first))
+        assert oracle().or_e2e_prefill_from(self.h, ptr(prompt), prompt.size, int(start), ptr(first)) == 0
         return int(first[0])
+
+    def history(self):
+        """(committed history: prompt + every committed token, last committed position P)."""
+        n, P = np.zeros(1, np.int32), np.zeros(1, np.int32)
+        oracle().or_e2e_history(self.h, None, 0, ptr(n), ptr(P))
+        out = np.zeros(max(1, int(n[0])), np.int32)
+        oracle().or_e2e_history(self.h, ptr(out), out.size, ptr(n), ptr(P))
+        return out[: n[0]].copy(), int(P[0])
 
     def decode(self, max_rounds, max_tokens):
         out = np.zeros(max(max_tokens, 1), np.int32)

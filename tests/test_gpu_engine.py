@@ -265,8 +265,8 @@ def test_fused_segments_match_per_kernel_path():
 def test_tensor_core_prefill_matches_block_prefill(cfg):
     """The prompt's full blocks prefilled at once with the tensor-core W4A8 GEMM write the same KV
     cache, hidden state and first token, bit for bit, as prefill block by block through the GEMV
-    path; at the full width and at reduced dimensions; with the attention taking four rows of a head
-    per block (prefill_tc 1) or one (3).  Prefill blocks of 7 rows put the switch from the per-row
+    path; at the full width and at reduced dimensions; with the attention taking one row of a head
+    per block (prefill_tc 1) or four (3).  Prefill blocks of 7 rows put the switch from the per-row
     to the tiled attention variant (the first block ending past position 64) inside a group of four
     rows, which then runs row by row."""
     vocab = cfg.get("vocab", 262144)
