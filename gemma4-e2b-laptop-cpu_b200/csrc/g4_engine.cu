@@ -1428,6 +1428,25 @@ static void finish_stats(g4_engine* e, int n, float gms, std::chrono::steady_clo
   st.decode_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
 }
 
+// BENCH_MODE's k (gemma4_engine.cpp:1682): the draft chain and the round loop are recorded for one
+// k, so they are dropped here and recorded again by the next decode call.
+extern "C" int g4_engine_set_k_draft(g4_engine* e, int k) {
+  G4_REQUIRE(e && k >= 0 && k <= 3 && !e->async_pending, "g4_engine_set_k_draft: bad arguments");
+  G4_REQUIRE(k == 0 || e->cfg.drafter, "g4_engine_set_k_draft: the engine has no drafter");
+  if (k == e->cfg.k_draft) return G4_OK;
+  ECK(cudaStreamSynchronize(e->st));
+  if (e->gloop) cudaGraphExecDestroy(e->gloop);
+  if (e->gdraft) cudaGraphExecDestroy(e->gdraft);
+  if (e->graw_draft) cudaGraphDestroy(e->graw_draft);
+  e->gloop = nullptr;
+  e->gdraft = nullptr;
+  e->graw_draft = nullptr;
+  e->gk_draft = 0;
+  e->loop_failed = false;
+  e->cfg.k_draft = k;
+  return G4_OK;
+}
+
 // ---- requests with the prefix cache (run_req, gemma4_engine.cpp:1569-1680)
 
 // K/V rows [0, len) of every layer from (sK, sV) to (dK, dV), all laid out as the engine's cache.
@@ -1477,8 +1496,8 @@ static int lcp_len(const std::vector<int>& k, int klen, const int32_t* p, int n)
 }
 
 extern "C" int g4_engine_request(g4_engine* e, const int32_t* prompt, int n, int max_new, int32_t* out, int* n_out,
-                                 g4_request_info* info) {
-  G4_REQUIRE(e && prompt && n >= 1 && max_new >= 1 && out && n_out, "g4_engine_request: bad arguments");
+                                 g4_request_info* info, g4_token_cb on_tokens, void* user) {
+  G4_REQUIRE(e && prompt && n >= 1 && max_new >= 0 && (out || max_new == 0) && n_out, "g4_engine_request: bad arguments");
   G4_REQUIRE(!e->async_pending, "g4_engine_request: a decode call is pending");
   RCK(ensure_slots(e));
   int common = lcp_len(e->ctx_keys, e->kv_len, prompt, n);
@@ -1515,19 +1534,39 @@ extern "C" int g4_engine_request(g4_engine* e, const int32_t* prompt, int n, int
   int first = 0;
   RCK(g4_engine_prefill_from(e, prompt, n, start, &first));
   const double prefill_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
-  out[0] = first;
-  int got = 0;
-  auto t1 = std::chrono::steady_clock::now();
-  if (max_new > 1 && !e->stopped) RCK(g4_engine_decode(e, 1 << 30, max_new - 1, out + 1, &got, nullptr));
-  const double decode_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t1).count();
-  int total = 1 + got;
-  for (int i = 0; i < total; ++i)
-    if (is_stop(out[i])) { total = i + 1; break; }
+  int total = 0;
+  double decode_ms = 0.0;
+  if (max_new == 0) {  // prefill only (:1607): the prompt's K/V is the conversation
+    e->ctx_keys.assign(prompt, prompt + n);
+    e->kv_len = n;
+  } else {
+    out[0] = first;
+    if (on_tokens) on_tokens(out, 1, user);
+    int got = 0;
+    auto t1 = std::chrono::steady_clock::now();
+    if (max_new > 1 && !e->stopped) {
+      if (on_tokens) {  // one round per call, each round's tokens reported as they commit
+        while (got < max_new - 1 && !e->stopped) {
+          int k = 0;
+          RCK(g4_engine_decode(e, 1, max_new - 1 - got, out + 1 + got, &k, nullptr));
+          if (k > 0) on_tokens(out + 1 + got, k, user);
+          got += k;
+          if (k == 0) break;
+        }
+      } else {
+        RCK(g4_engine_decode(e, 1 << 30, max_new - 1, out + 1, &got, nullptr));
+      }
+    }
+    decode_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t1).count();
+    total = 1 + got;
+    for (int i = 0; i < total; ++i)
+      if (is_stop(out[i])) { total = i + 1; break; }
+    // the conversation's tokens whose K/V is written: positions 0..P (:1601)
+    const size_t nk = std::min(e->seq.size(), (size_t)std::max(0, e->P - e->fake_n + 1));
+    e->ctx_keys.assign(e->seq.begin(), e->seq.begin() + nk);
+    e->kv_len = e->fake_n ? 0 : std::min(e->P + 1, (int)e->ctx_keys.size());
+  }
   *n_out = total;
-  // the conversation's tokens whose K/V is written: positions 0..P (:1601)
-  const size_t nk = std::min(e->seq.size(), (size_t)std::max(0, e->P - e->fake_n + 1));
-  e->ctx_keys.assign(e->seq.begin(), e->seq.begin() + nk);
-  e->kv_len = e->fake_n ? 0 : std::min(e->P + 1, (int)e->ctx_keys.size());
   if (info) {
     info->prompt_tokens = n;
     info->reused = start;
@@ -1538,6 +1577,9 @@ extern "C" int g4_engine_request(g4_engine* e, const int32_t* prompt, int n, int
     info->slot_switches = e->slot_switches;
     info->slot_evictions = e->slot_evictions;
     info->kv_len = e->kv_len;
+    info->rounds = e->stats.rounds;
+    info->ngram_rounds = e->stats.ngram_rounds;
+    info->ngram_accepted = e->stats.ngram_accepted;
   }
   return G4_OK;
 }

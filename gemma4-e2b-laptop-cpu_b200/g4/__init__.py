@@ -58,7 +58,8 @@ SIGNATURES = {
     "g4_engine_fake_ctx": (_I, [_P, _I]),
     "g4_engine_prefill": (_I, [_P, _P, _I, _P]),
     "g4_engine_prefill_from": (_I, [_P, _P, _I, _I, _P]),
-    "g4_engine_request": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+    "g4_engine_set_k_draft": (_I, [_P, _I]),
+    "g4_engine_request": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
     "g4_engine_decode": (_I, [_P, _I, _I, _P, _P, _P]),
     "g4_engine_phase_times": (_I, [_P, _I, _P, _P]),
     "g4_engine_trace": (_I, [_P, _P, _I, _P]),
@@ -502,11 +503,15 @@ class EngineStats(ctypes.Structure):
         return {n: getattr(self, n) for n, _ in self._fields_}
 
 
+TOKEN_CB = ctypes.CFUNCTYPE(None, ctypes.POINTER(ctypes.c_int32), ctypes.c_int, ctypes.c_void_p)
+
+
 class RequestInfo(ctypes.Structure):
     """g4_request_info (include/g4.h)."""
     _fields_ = [(n, ctypes.c_int) for n in ("prompt_tokens", "reused", "slot", "tokens")] + [
         ("prefill_ms", ctypes.c_double), ("decode_ms", ctypes.c_double)] + [
-        (n, ctypes.c_int) for n in ("slot_switches", "slot_evictions", "kv_len")]
+        (n, ctypes.c_int) for n in ("slot_switches", "slot_evictions", "kv_len", "rounds", "ngram_rounds",
+                                    "ngram_accepted")]
 
     def as_dict(self):
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -571,15 +576,20 @@ class Engine:
                                            ctypes.byref(first)), "g4_engine_prefill_from")
         return first.value
 
-    def request(self, prompt, max_new):
-        """One request through the prefix cache (g4_engine_request): (tokens, info dict)."""
+    def request(self, prompt, max_new, on_tokens=None):
+        """One request through the prefix cache (g4_engine_request): (tokens, info dict).
+        on_tokens(list of ints) is called with the tokens as they commit."""
         import numpy as np
         prompt = np.ascontiguousarray(prompt, np.int32)
         out = np.zeros(max(1, int(max_new)), np.int32)
         n = ctypes.c_int(0)
         info = RequestInfo()
+        cb = None
+        if on_tokens is not None:
+            cb = TOKEN_CB(lambda p, k, _u: on_tokens([p[i] for i in range(k)]))
         check(lib().g4_engine_request(self.h, prompt.ctypes.data_as(_P), prompt.size, int(max_new),
-                                      out.ctypes.data_as(_P), ctypes.byref(n), ctypes.byref(info)), "g4_engine_request")
+                                      out.ctypes.data_as(_P), ctypes.byref(n), ctypes.byref(info),
+                                      ctypes.cast(cb, _P) if cb is not None else None, None), "g4_engine_request")
         return out[: n.value].copy(), info.as_dict()
 
     def decode(self, max_rounds, max_tokens, out=None):

@@ -318,7 +318,8 @@ int g4_engine_decode_wait(g4_engine* e, int32_t* out, int* n_out, g4_engine_stat
  * used slot takes the active conversation and the request starts from an empty cache.  Then prefill
  * from min(shared, n - 1) (g4_engine_prefill_from) and decode until max_new tokens (the first from
  * the prefill) or a stop token.  out host [max_new]; *n_out = tokens, cut after the first stop
- * token.  With slots = 1 only the active conversation is reused. */
+ * token.  max_new = 0 prefills only (the prompt becomes the conversation; out may be NULL).  With
+ * slots = 1 only the active conversation is reused.  on_tokens may be NULL. */
 typedef struct {
   int prompt_tokens;                 /* n */
   int reused;                        /* prompt positions whose K/V came from the cache */
@@ -328,9 +329,17 @@ typedef struct {
   double prefill_ms, decode_ms;      /* host wall clock */
   int slot_switches, slot_evictions; /* totals since the engine was created */
   int kv_len;                        /* positions of the active conversation now in the cache */
+  int rounds, ngram_rounds, ngram_accepted; /* decode rounds of this request, those that used prompt
+                                               lookup, drafts they accepted */
 } g4_request_info;
+/* Drafts per round k (0..3; the reference's BENCH_MODE, gemma4_engine.cpp:1682): takes effect at the
+ * next decode call. */
+int g4_engine_set_k_draft(g4_engine* e, int k);
+/* Called by g4_engine_request with tokens as they commit: the first token after the prefill, then
+ * each decode round's tokens (the request then decodes one round per g4_engine_decode call). */
+typedef void (*g4_token_cb)(const int32_t* tokens, int n, void* user);
 int g4_engine_request(g4_engine* e, const int32_t* prompt, int n, int max_new, int32_t* out, int* n_out,
-                      g4_request_info* info);
+                      g4_request_info* info, g4_token_cb on_tokens, void* user);
 /* Per-round records since the prefill, 6 ints each: {drafts verified nd, prompt lookup used (1) or MTP
  * (0), the MTP drafts (-1 padded), accepted nacc}; out host [cap_rounds][6]; *n_rounds = rounds
  * recorded (records past the engine's capacity of ctx_max rounds are not kept). */

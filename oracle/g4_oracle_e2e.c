@@ -547,6 +547,9 @@ int or_e2e_prefill_from(void* mp, const int32_t* prompt, int n, int start, int32
 }
 int or_e2e_prefill(void* mp, const int32_t* prompt, int n, int32_t* first) { return or_e2e_prefill_from(mp, prompt, n, 0, first); }
 
+/* Drafts per round (BENCH_MODE's k). */
+void or_e2e_set_k(void* mp, int k) { ((Model*)mp)->k_draft = k; }
+
 /* The committed history (prompt and every committed token) and the last committed position P. */
 int or_e2e_history(void* mp, int32_t* out, int cap, int* len, int* P) {
   Model* m = (Model*)mp;

@@ -55,6 +55,7 @@ _SIGS_ORACLE = {
     "or_e2e_prefill": (_I, [_P, _P, _I, _P]),
     "or_e2e_prefill_from": (_I, [_P, _P, _I, _I, _P]),
     "or_e2e_history": (_I, [_P, _P, _I, _P, _P]),
+    "or_e2e_set_k": (None, [_P, _I]),
     "or_e2e_decode": (_I, [_P, _I, _I, _P, _P, _P, _P, _I]),
     "or_e2e_set_state": (_I, [_P, _P, _P, _I, _P, _I, _P, _I]),
     "or_e2e_set_hooks": (_I, [_P, _P]),
@@ -321,6 +322,9 @@ class OracleModel:
         first = np.zeros(1, np.int32)
         assert oracle().or_e2e_prefill_from(self.h, ptr(prompt), prompt.size, int(start), ptr(first)) == 0
         return int(first[0])
+
+    def set_k(self, k):
+        oracle().or_e2e_set_k(self.h, int(k))
 
     def history(self):
         """(committed history: prompt + every committed token, last committed position P)."""

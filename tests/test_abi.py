@@ -37,3 +37,12 @@ def test_abi_version_and_error_string():
     rc = lib.g4_w4g32_gemm(None, None, None, None, 1, 8, 32, None, 8, None)
     assert rc == -1
     assert b"null" in lib.g4_last_error()
+
+
+def test_serve_binary_is_built_and_answers_help():
+    """g4_serve (the reference engine's process interface) is built beside libg4.so; --help needs no GPU."""
+    import subprocess
+    b = PKG_DIR / "g4_serve"
+    assert b.exists()
+    r = subprocess.run([str(b), "--help"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and "ENGINE_SERVE" in r.stderr

@@ -32,6 +32,10 @@ class OracleConversations:
         for c in [self.active] + self.stored:
             c[0].close()
 
+    def set_k(self, k):
+        for c in [self.active] + self.stored:
+            c[0].set_k(k)
+
     @staticmethod
     def _lcp(keys, kv_len, prompt):
         c = 0
@@ -67,7 +71,11 @@ class OracleConversations:
             self.active[3] = self.tick
         start = min(common, n - 1)
         m = self.active[0]
-        out = [m.prefill(prompt, start)]
+        first = m.prefill(prompt, start)
+        if max_new <= 0:  # prefill only: the prompt is the conversation
+            self.active[1], self.active[2] = prompt, n
+            return [], start, slot
+        out = [first]
         if max_new > 1 and out[0] not in STOP:
             toks, _ = m.decode(1 << 30, max_new - 1)
             out += [int(t) for t in toks]
