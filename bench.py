@@ -282,8 +282,8 @@ N_CFG2, K_CFG2, M_CFG2 = 262144, 2048, 4
 
 def run_head_g4(args, world, rank, local):
     """configs[2]'s exact head: the bf16p logits of M=4 hidden states against the 262,144 x 2048 head
-    (the screen's fallback), through the unpacked copy (g4_bf16p_unpacked_gemm).  Bytes counted:
-    the bf16p rows (44 per group), the exceptions, x and the logits."""
+    (the screen's fallback), through the split-nibble copy the engine reads (g4_bf16p_nib_gemm, 48 B
+    per group).  Bytes counted: the bf16p rows (44 per group), the exceptions, x and the logits."""
     import torch
     import g4
     torch.cuda.set_device(local)
@@ -294,7 +294,7 @@ def run_head_g4(args, world, rank, local):
     head = g4.PackedHead(E)
     del E
     torch.cuda.empty_cache()
-    unp = head.unpacked()
+    nib = head.nibbled()
     Xd = torch.randn(M_CFG2, K_CFG2, device="cuda", generator=gen) / float(np.sqrt(K_CFG2))
     Y = torch.empty((M_CFG2, N_CFG2), device="cuda")
     nbytes = (N_CFG2 * (K_CFG2 // 32) * 44 + head.n_exc * 6 + (N_CFG2 + 1) * 8 + M_CFG2 * K_CFG2 * 4
@@ -302,12 +302,12 @@ def run_head_g4(args, world, rank, local):
     lib = g4.lib()
     stream = torch.cuda.Stream()
     sp = ctypes.c_void_p(stream.cuda_stream)
-    cargs = (ctypes.c_void_p(unp.data_ptr()), ctypes.c_void_p(head.exc_ptr.data_ptr()),
+    cargs = (ctypes.c_void_p(nib.data_ptr()), head.cb, ctypes.c_void_p(head.exc_ptr.data_ptr()),
              ctypes.c_void_p(head.exc_col.data_ptr()), ctypes.c_void_p(head.exc_delta.data_ptr()), N_CFG2, K_CFG2,
              ctypes.c_void_p(Xd.data_ptr()), M_CFG2, ctypes.c_void_p(Y.data_ptr()), N_CFG2, sp)
 
     def step():
-        if lib.g4_bf16p_unpacked_gemm(*cargs):
+        if lib.g4_bf16p_nib_gemm(*cargs):
             raise RuntimeError(lib.g4_last_error().decode())
 
     torch.cuda.synchronize()
@@ -369,10 +369,10 @@ def run_head_g4(args, world, rank, local):
             "config": {"workload": "configs[2] exact head (bf16p) 262144x2048, M=4", "N": N_CFG2, "K": K_CFG2,
                        "M": M_CFG2, "exceptions": int(head.n_exc), "bytes_per_step": nbytes,
                        "timing": "K launches replayed as one CUDA graph, CUDA events on its stream",
-                       "l2": "every step reads the 1.07 GB unpacked head (> L2)", "parallelism": f"replicas x{world}"},
+                       "l2": "every step reads the 805 MB split-nibble head (> L2)", "parallelism": f"replicas x{world}"},
             "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
-                         "peak_kind": peak_kind, "traffic": profile_traffic("head_unpacked_gemv_cfg2"),
-                         "kernel": "k_bf16u_rows_tma<4>"},
+                         "peak_kind": peak_kind, "traffic": profile_traffic("head_nib_gemv_cfg2"),
+                         "kernel": "k_bf16n_rows_tma<4>"},
             "e2e": {"value": nbytes * args.steps * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
                     "h2d_bytes_per_step": M_CFG2 * K_CFG2 * 4, "d2h_bytes_per_step": M_CFG2 * N_CFG2 * 4},
             "gpu_launches": args.steps,

@@ -71,7 +71,7 @@ inline int launch(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 bloc
 int head_screen_impl(const uint8_t* W4p, const uint16_t* S4, const float* coef, const uint8_t* data, const uint8_t* unp,
                      const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col, const float* exc_delta, int N,
                      int K, const float* H, int M, int lim, int* out_idx, int* out_nsurv, void* ws, size_t ws_bytes,
-                     void* stream, int* policy = nullptr);
+                     void* stream, int* policy = nullptr, const uint8_t* nib = nullptr);
 // The W4G32 GEMV of the head screen, skipped on the device while *skip != 0 (skip may be NULL).
 // Only the TMA-fed variant reads the flag; shapes it does not serve run ungated.
 int w4g32_gemm_gated(const uint8_t* Wp, const uint16_t* S, const float* X, int M, int N, int K, float* Y, int ldy,

@@ -249,7 +249,7 @@ struct g4_engine {
   float *fnorm = nullptr, *dnorm = nullptr;
   uint16_t* E = nullptr;
   // head
-  uint8_t *hdata = nullptr, *hunp = nullptr, *sW4 = nullptr;
+  uint8_t *hdata = nullptr, *hnib = nullptr, *sW4 = nullptr;
   uint16_t* sS4 = nullptr;
   float* scoef = nullptr;
   long long* hexc_ptr = nullptr;
@@ -422,7 +422,7 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
     e->DL = share->DL;
     e->dpre = share->dpre; e->dpost = share->dpost; e->dcent = share->dcent;
     e->fnorm = share->fnorm; e->dnorm = share->dnorm; e->E = share->E;
-    e->hdata = share->hdata; e->hunp = share->hunp; e->sW4 = share->sW4; e->sS4 = share->sS4; e->scoef = share->scoef;
+    e->hdata = share->hdata; e->hnib = share->hnib; e->sW4 = share->sW4; e->sS4 = share->sS4; e->scoef = share->scoef;
     e->hexc_ptr = share->hexc_ptr; e->hexc_col = share->hexc_col; e->hexc_delta = share->hexc_delta;
     std::memcpy(e->cb8, share->cb8, 8);
     for (int ty = 0; ty < 2; ++ty) { e->rope[ty][0] = share->rope[ty][0]; e->rope[ty][1] = share->rope[ty][1]; }
@@ -464,9 +464,9 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
     if (!rc && ealloc_t(e, &e->hexc_col, (size_t)std::max(1LL, total))) rc = G4_ERR_CUDA;
     if (!rc && ealloc_t(e, &e->hexc_delta, (size_t)std::max(1LL, total))) rc = G4_ERR_CUDA;
     if (!rc) rc = g4_bf16p_pack(e->E, d.V, H, e->cb8, e->hdata, e->hexc_ptr, e->hexc_col, e->hexc_delta, e->st);
-    if (!rc && H % 64 == 0) {  // the unpacked copy that the head GEMV reads
-      if (ealloc_t(e, &e->hunp, (size_t)d.V * (H / 32) * 64)) rc = G4_ERR_CUDA;
-      if (!rc) rc = g4_bf16p_unpack(e->hdata, e->cb8, d.V, H, e->hunp, e->st);
+    if (!rc && H % 128 == 0) {  // the split-nibble copy that the full-head GEMV reads
+      if (ealloc_t(e, &e->hnib, g4_bf16p_nib_bytes(d.V, H))) rc = G4_ERR_CUDA;
+      if (!rc) rc = g4_bf16p_nib_pack(e->hdata, d.V, H, e->hnib, e->st);
     }
     if (!rc && ealloc_t(e, &e->sW4, (size_t)d.V * H / 2)) rc = G4_ERR_CUDA;
     if (!rc && ealloc_t(e, &e->sS4, (size_t)d.V * H / 32)) rc = G4_ERR_CUDA;
@@ -826,14 +826,14 @@ head:
   for (int r0 = hf; r0 < M; r0 += 4) {
     const int mh = std::min(4, M - r0);
     if (e->cfg.head_screen) {
-      RCK(head_screen_impl(e->sW4, e->sS4, e->scoef, e->hdata, e->hunp, e->cb8, e->hexc_ptr, e->hexc_col, e->hexc_delta,
+      RCK(head_screen_impl(e->sW4, e->sS4, e->scoef, e->hdata, nullptr, e->cb8, e->hexc_ptr, e->hexc_col, e->hexc_delta,
                            d.V, H, e->hbuf + (size_t)r0 * H, mh, e->cfg.screen_lim, e->G + r0, e->head_ns, e->head_ws,
-                           e->head_ws_bytes, e->st, e->cfg.head_screen == 2 ? screen_policy(e) : nullptr));
+                           e->head_ws_bytes, e->st, e->cfg.head_screen == 2 ? screen_policy(e) : nullptr, e->hnib));
     } else {
       float* logits = static_cast<float*>(e->head_ws);
-      if (e->hunp)
-        RCK(g4_bf16p_unpacked_gemm(e->hunp, e->hexc_ptr, e->hexc_col, e->hexc_delta, d.V, H, e->hbuf + (size_t)r0 * H, mh,
-                                   logits, d.V, e->st));
+      if (e->hnib)
+        RCK(g4_bf16p_nib_gemm(e->hnib, e->cb8, e->hexc_ptr, e->hexc_col, e->hexc_delta, d.V, H, e->hbuf + (size_t)r0 * H, mh,
+                              logits, d.V, e->st));
       else
         RCK(g4_bf16p_gemm(e->hdata, e->cb8, e->hexc_ptr, e->hexc_col, e->hexc_delta, d.V, H, e->hbuf + (size_t)r0 * H, mh,
                           logits, d.V, e->st));

@@ -156,6 +156,7 @@ __global__ void k_bf16p_fill(const uint16_t* __restrict__ E, int K, Codebook cb,
 struct HeadPacked {
   const uint8_t* data;
   const uint8_t* unp;  // the same head in the unpacked layout (g4_bf16p_unpack), or NULL
+  const uint8_t* nib;  // the same head in the split-nibble layout (g4_bf16p_nib_pack), or NULL
   const long long* exc_ptr;
   const uint16_t* exc_col;
   const float* exc_delta;
@@ -1037,7 +1038,7 @@ extern "C" int g4_bf16p_pack(const uint16_t* E, int N, int K, const uint8_t* cb8
 static HeadPacked make_head(const uint8_t* data, const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col,
                             const float* exc_delta, int N, int K) {
   HeadPacked P;
-  P.data = data; P.unp = nullptr; P.exc_ptr = exc_ptr; P.exc_col = exc_col; P.exc_delta = exc_delta; P.N = N; P.K = K;
+  P.data = data; P.unp = nullptr; P.nib = nullptr; P.exc_ptr = exc_ptr; P.exc_col = exc_col; P.exc_delta = exc_delta; P.N = N; P.K = K;
   std::memcpy(&P.cb_lo, cb8, 4);
   std::memcpy(&P.cb_hi, cb8 + 4, 4);
   return P;
@@ -1094,6 +1095,68 @@ __global__ void k_bf16u_pack(const uint8_t* __restrict__ data, long long ngroups
         dst[8 * h + 2 * oi + pr] = bf16p_bits(w, e, cb_lo, cb_hi) | (bf16p_bits(w, e + 1, cb_lo, cb_hi) << 16);
       }
     }
+}
+
+// ---- split-nibble layout of the packed head (48 bytes per group, two arrays): sm [N][G][32] holds
+// the 32 sign/mantissa bytes of bf16p::pack, half h's 16 at byte 16h in the order that half consumes
+// them (octets in chain order 0, 2, 1, 3; elements 8o+4h..8o+4h+3 within an octet: one 32-bit word
+// per octet quad), and codes [N][G][16] the same weights' 3-bit exponent codes as nibbles, half h's
+// 16 at byte 8h (word w of a half: quads 2w and 2w+1, nibble k of a quad = its weight k).  A quad's
+// four codes are one byte-permute selector over the 8-entry codebook: two permutes give the four
+// weights' bf16 high-byte exponent bits (e >> 1) and low-byte bit ((e & 1) << 7), two masked merges
+// add the sign and mantissa, and two permutes interleave the bytes into the two bf16 pairs that the
+// unpacked layout stores, so the values are those of k_bf16u_rows_tma.  11% more bytes than bf16p
+// (44 per group), 25% fewer than the unpacked copy (64).
+__global__ void k_bf16n_pack(const uint8_t* __restrict__ data, long long ngroups, uint8_t* __restrict__ sm_out,
+                             uint8_t* __restrict__ code_out) {
+  const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= ngroups) return;
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(data + g * 44);  // 4-byte aligned (44 = 4 * 11)
+  uint32_t w[11];
+#pragma unroll
+  for (int i = 0; i < 11; ++i) w[i] = src[i];
+  uint32_t* sm = reinterpret_cast<uint32_t*>(sm_out + g * 32);
+  uint32_t* cd = reinterpret_cast<uint32_t*>(code_out + g * 16);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t cw[2] = {0u, 0u};
+#pragma unroll
+    for (int oi = 0; oi < 4; ++oi) {
+      const int o8 = (oi == 1) ? 2 : (oi == 2 ? 1 : oi);
+      uint32_t smw = 0u, code = 0u;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int e = 8 * o8 + 4 * h + k;
+        const uint32_t idx = ((w[8] >> e) & 1u) | (((w[9] >> e) & 1u) << 1) | (((w[10] >> e) & 1u) << 2);
+        smw |= ((w[e >> 2] >> (8 * (e & 3))) & 0xFFu) << (8 * k);
+        code |= idx << (4 * k);
+      }
+      sm[4 * h + oi] = smw;
+      cw[oi >> 1] |= code << (16 * (oi & 1));
+    }
+    cd[2 * h] = cw[0];
+    cd[2 * h + 1] = cw[1];
+  }
+}
+
+// Two bf16 pairs (weights 0, 1 and 2, 3 of a quad) from its sign/mantissa word and code selector.
+__device__ __forceinline__ void bf16n_quad(uint32_t smw, uint32_t sel, uint32_t cbh_lo, uint32_t cbh_hi, uint32_t cbl_lo,
+                                           uint32_t cbl_hi, uint32_t& w0, uint32_t& w1) {
+  const uint32_t hi4 = (smw & 0x80808080u) | __byte_perm(cbh_lo, cbh_hi, sel);
+  const uint32_t lo4 = (smw & 0x7F7F7F7Fu) | __byte_perm(cbl_lo, cbl_hi, sel);
+  w0 = __byte_perm(lo4, hi4, 0x5140);
+  w1 = __byte_perm(lo4, hi4, 0x7362);
+}
+
+// Exact-head GEMV over the split-nibble layout, fed by the TMA, two threads per row (the arithmetic
+// of k_bf16u_rows_tma): per pipeline item two tensor-map loads bring 4 groups of 128 rows, the
+// sign/mantissa bytes as a [128][128 B] box under the 128-byte swizzle and the codes as a [128][64 B]
+// box under the 64-byte swizzle (16-byte chunk c of row r lands at c ^ ((r >> 1) & 3)), into one of
+// kBnNS stages of 24 KB.
+constexpr int kBnRows = 128, kBnThreads = 256, kBnNS = 3;
+constexpr int kBnSm = kBnRows * 128, kBnStage = kBnSm + kBnRows * 64;  // 4 groups per item
+__host__ __device__ inline size_t head_nib_smem(int M, int K) {
+  return 1024 + 128 + (size_t)kBnNS * kBnStage + (size_t)K * ((M + 1) / 2) * 8;
 }
 
 // Exact-head GEMV over the unpacked layout, fed by the TMA, two threads per row (as
@@ -1230,6 +1293,161 @@ __global__ void __launch_bounds__(kBuThreads, 2) k_bf16u_rows_tma(const __grid_c
   }
 }
 
+template <int M>
+__global__ void __launch_bounds__(kBnThreads, 2) k_bf16n_rows_tma(const __grid_constant__ CUtensorMap tsm,
+                                                                  const __grid_constant__ CUtensorMap tcode, HeadPacked P,
+                                                                  const float* __restrict__ X, float* __restrict__ Y, int ldy,
+                                                                  const int* __restrict__ gate) {
+  constexpr int NP = (M + 1) / 2;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[kBnNS];
+  uint8_t* stages = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // 1024-byte aligned
+  float2* xs = reinterpret_cast<float2*>(stages + (size_t)kBnNS * kBnStage);  // [K][NP]
+  pdl_wait();
+  pdl_trigger();
+  if (gate != nullptr && *gate == 0) return;
+  const int K = P.K, G = K >> 5, nch = G / 4;
+  const int nblk = (P.N + kBnRows - 1) / kBnRows;
+  const int myblk = nblk > (int)blockIdx.x ? (nblk - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int nitems = myblk * nch;
+  const int t = threadIdx.x, rl = t >> 1, half = t & 1;
+  // codebook bytes split into the bf16 high-byte bits (e >> 1) and low-byte bit ((e & 1) << 7)
+  const uint32_t cbh_lo = (P.cb_lo >> 1) & 0x7F7F7F7Fu, cbh_hi = (P.cb_hi >> 1) & 0x7F7F7F7Fu;
+  const uint32_t cbl_lo = (P.cb_lo << 7) & 0x80808080u, cbl_hi = (P.cb_hi << 7) & 0x80808080u;
+  if (t == 0) {
+    for (int b = 0; b < kBnNS; ++b) mbar_init(&bars[b], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int i, int st) {  // thread 0
+    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
+    uint8_t* sb = stages + (size_t)st * kBnStage;
+    mbar_expect_tx(&bars[st], (uint32_t)kBnStage);
+    tma_load_2d(sb, &tsm, c * 128, blk * kBnRows, &bars[st]);
+    tma_load_2d(sb + kBnSm, &tcode, c * 64, blk * kBnRows, &bars[st]);
+  };
+  if (t == 0)
+    for (int b = 0; b < kBnNS && b < nitems; ++b) issue(b, b);
+  for (int i = t; i < K; i += kBnThreads) {
+    float v[2 * NP];
+#pragma unroll
+    for (int m = 0; m < 2 * NP; ++m) v[m] = m < M ? X[(size_t)m * K + i] : 0.f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) xs[(size_t)i * NP + p] = make_float2(v[2 * p], v[2 * p + 1]);
+  }
+  __syncthreads();
+  const int hsh = 4 * half;
+  float2 acc[4][NP];
+  for (int i = 0; i < nitems; ++i) {
+    const int st = i % kBnNS;
+    const int blk = blockIdx.x + (i / nch) * gridDim.x, c = i % nch;
+    const int n = blk * kBnRows + rl;
+    if (!cta_wait(&bars[st], (uint32_t)(i / kBnNS) & 1u)) return;
+    if (c == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int p = 0; p < NP; ++p) acc[j][p] = make_float2(0.f, 0.f);
+    }
+    const uint8_t* smrow = stages + (size_t)st * kBnStage + (size_t)rl * 128;
+    const uint8_t* cdrow = stages + (size_t)st * kBnStage + kBnSm + (size_t)rl * 64;
+    uint32_t smv[16], cdv[8];  // this half's sign/mantissa words and code words of the item's 4 groups
+#pragma unroll
+    for (int gg = 0; gg < 4; ++gg) {
+      const uint4 s4 = *reinterpret_cast<const uint4*>(smrow + (((2 * gg + half) ^ (rl & 7)) << 4));
+      smv[4 * gg] = s4.x; smv[4 * gg + 1] = s4.y; smv[4 * gg + 2] = s4.z; smv[4 * gg + 3] = s4.w;
+      const uint2 c2 = *reinterpret_cast<const uint2*>(cdrow + ((gg ^ ((rl >> 1) & 3)) << 4) + 8 * half);
+      cdv[2 * gg] = c2.x; cdv[2 * gg + 1] = c2.y;
+    }
+    __syncthreads();  // every row has its words in registers: the stage can be refilled
+    if (t == 0 && i + kBnNS < nitems) {
+      fence_proxy_async_smem();
+      issue(i + kBnNS, st);
+    }
+#pragma unroll
+    for (int gg = 0; gg < 4; ++gg) {
+      const int g = c * 4 + gg;
+      const float2* xg = xs + ((size_t)g * 32 + hsh) * NP;
+#pragma unroll
+      for (int oi = 0; oi < 4; ++oi) {
+        const int o8 = (oi == 1) ? 2 : (oi == 2 ? 1 : oi);  // element octets in chain order 0, 2, 1, 3
+        const uint32_t cw = cdv[2 * gg + (oi >> 1)];
+        uint32_t w0, w1;
+        bf16n_quad(smv[4 * gg + oi], (oi & 1) ? (cw >> 16) : (cw & 0xFFFFu), cbh_lo, cbh_hi, cbl_lo, cbl_hi, w0, w1);
+        const float wk[4] = {__uint_as_float(w0 << 16), __uint_as_float(w0 & 0xFFFF0000u), __uint_as_float(w1 << 16),
+                             __uint_as_float(w1 & 0xFFFF0000u)};
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int p = 0; p < NP; ++p)
+            acc[k][p] = __ffma2_rn(make_float2(wk[k], wk[k]), xg[(8 * o8 + k) * NP + p], acc[k][p]);
+      }
+    }
+    if (c == nch - 1) {
+      // lanes 4..7 come from the other half; both halves hold the same hsum8 (as k_bf16u_rows_tma)
+      float y[2 * NP];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        float2 w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          w[k].x = __shfl_xor_sync(0xffffffffu, acc[k][p].x, 1);
+          w[k].y = __shfl_xor_sync(0xffffffffu, acc[k][p].y, 1);
+        }
+        y[2 * p] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].x, w[0].x), __fadd_rn(acc[1][p].x, w[1].x)),
+                             __fadd_rn(__fadd_rn(acc[2][p].x, w[2].x), __fadd_rn(acc[3][p].x, w[3].x)));
+        y[2 * p + 1] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0][p].y, w[0].y), __fadd_rn(acc[1][p].y, w[1].y)),
+                                 __fadd_rn(__fadd_rn(acc[2][p].y, w[2].y), __fadd_rn(acc[3][p].y, w[3].y)));
+      }
+      if (n < P.N) {
+        float yo[NP];  // this half's activation rows 2p + half
+#pragma unroll
+        for (int p = 0; p < NP; ++p) yo[p] = half ? y[2 * p + 1] : y[2 * p];
+        for (long long e = P.exc_ptr[n]; e < P.exc_ptr[n + 1]; ++e) {  // CSR order, unfused (bf16_exp3_head.h:103)
+          const float dl = P.exc_delta[e];
+          const int col = P.exc_col[e];
+#pragma unroll
+          for (int p = 0; p < NP; ++p) {
+            const float2 xv = xs[(size_t)col * NP + p];
+            yo[p] = __fadd_rn(yo[p], __fmul_rn(dl, half ? xv.y : xv.x));
+          }
+        }
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+          if (2 * p + half < M) Y[(size_t)(2 * p + half) * ldy + n] = yo[p];
+      }
+    }
+  }
+}
+
+// The split-nibble head as two 2D byte tensors, [N][G*32] in [128][128 B] boxes under the 128-byte
+// swizzle and [N][G*16] in [128][64 B] boxes under the 64-byte swizzle; cached per (address, N, K).
+static bool head_nib_tmaps(const HeadPacked& P, CUtensorMap* tsm, CUtensorMap* tcode) {
+  static std::mutex mu;
+  struct Entry { const void* ptr; int N, K; CUtensorMap ms, mc; };
+  static Entry cache[8];
+  static int used = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].ptr == P.nib && cache[i].N == P.N && cache[i].K == P.K) {
+      *tsm = cache[i].ms;
+      *tcode = cache[i].mc;
+      return true;
+    }
+  const uint64_t G = (uint64_t)P.K / 32;
+  const uint8_t* codes = P.nib + (size_t)P.N * G * 32;
+  CUtensorMap ms, mc;
+  if (!encode_tmap_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT8, P.nib, G * 32, (uint64_t)P.N, G * 32, 128, kBnRows,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, G * 16, (uint64_t)P.N, G * 16, 64, kBnRows,
+                      CU_TENSOR_MAP_SWIZZLE_64B))
+    return false;
+  if (used < 8) cache[used++] = Entry{P.nib, P.N, P.K, ms, mc};
+  *tsm = ms;
+  *tcode = mc;
+  return true;
+}
+
 // The unpacked head as a 2D byte tensor [N][G*64] with boxes of [kBuRows][kBuBox] under the
 // 128-byte swizzle; cached per (address, N, K).
 static bool head_unp_tmap(const HeadPacked& P, CUtensorMap* out) {
@@ -1263,7 +1481,20 @@ static int num_sms() {
 template <int M>
 static int launch_head_gemv(const HeadPacked& P, const float* X, float* Y, int ldy, const int* gate, cudaStream_t st) {
   const char* hv = getenv("G4_HEAD_GEMV");  // "direct" / "octet" select other variants (experiments)
-  CUtensorMap tm;
+  CUtensorMap tm, tm2;
+  const size_t nsmem = head_nib_smem(M, P.K);
+  if (P.nib != nullptr && P.K % 128 == 0 && aligned(P.nib, 16) && nsmem <= 113 * 1024 && head_nib_tmaps(P, &tm, &tm2)) {
+    cudaFuncSetAttribute(k_bf16n_rows_tma<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nsmem);
+    cudaFuncSetAttribute(k_bf16n_rows_tma<M>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);  // 2 CTAs per SM
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_bf16n_rows_tma<M>, kBnThreads, nsmem) != cudaSuccess || occ < 1)
+      occ = 1;
+    const int nblk = (P.N + kBnRows - 1) / kBnRows;
+    return launch("k_bf16n_rows_tma", k_bf16n_rows_tma<M>, dim3(std::min(nblk, num_sms() * occ)), dim3(kBnThreads), nsmem,
+                  st, tm, tm2, P, X, Y, ldy, gate);
+  }
+  if (P.nib != nullptr && P.data == nullptr && P.unp == nullptr)
+    return set_error(G4_ERR_UNSUPPORTED, "bf16p split-nibble GEMV: K=%d (a multiple of 128 and a 16-byte aligned head needed)", P.K);
   const size_t usmem = head_unp_smem(M, P.K);
   if (P.unp != nullptr && P.K % (64 * kBuBoxes) == 0 && aligned(P.unp, 16) && usmem <= 113 * 1024 && head_unp_tmap(P, &tm)) {
     cudaFuncSetAttribute(k_bf16u_rows_tma<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)usmem);
@@ -1336,6 +1567,28 @@ extern "C" int g4_bf16p_unpack(const uint8_t* data, const uint8_t* cb8, int N, i
   return check_launch("k_bf16u_pack");
 }
 
+extern "C" size_t g4_bf16p_nib_bytes(int N, int K) { return (size_t)N * (size_t)(K / 32) * 48; }
+
+extern "C" int g4_bf16p_nib_pack(const uint8_t* data, int N, int K, uint8_t* nib, void* stream) {
+  G4_REQUIRE(data && nib, "g4_bf16p_nib_pack: null pointer");
+  G4_REQUIRE(N > 0 && K > 0 && K % 32 == 0, "g4_bf16p_nib_pack: bad shape N=%d K=%d", N, K);
+  G4_REQUIRE(aligned(data, 4) && aligned(nib, 16), "g4_bf16p_nib_pack: data 4-byte, nib 16-byte aligned");
+  const long long ng = (long long)N * (K / 32);
+  k_bf16n_pack<<<(unsigned)((ng + 255) / 256), 256, 0, as_stream(stream)>>>(data, ng, nib, nib + (size_t)ng * 32);
+  return check_launch("k_bf16n_pack");
+}
+
+extern "C" int g4_bf16p_nib_gemm(const uint8_t* nib, const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col,
+                                 const float* exc_delta, int N, int K, const float* X, int M, float* Y, int ldy,
+                                 void* stream) {
+  G4_REQUIRE(nib && cb8 && exc_ptr && X && Y, "g4_bf16p_nib_gemm: null pointer");
+  G4_REQUIRE(M >= 1 && M <= 4 && N > 0 && K > 0 && K % 128 == 0 && ldy >= N, "g4_bf16p_nib_gemm: bad shape M=%d N=%d K=%d",
+             M, N, K);
+  HeadPacked P = make_head(nullptr, cb8, exc_ptr, exc_col, exc_delta, N, K);
+  P.nib = nib;
+  return head_gemv(P, X, M, Y, ldy, nullptr, as_stream(stream));
+}
+
 extern "C" int g4_bf16p_unpacked_gemm(const uint8_t* unp, const long long* exc_ptr, const uint16_t* exc_col,
                                       const float* exc_delta, int N, int K, const float* X, int M, float* Y, int ldy,
                                       void* stream) {
@@ -1386,7 +1639,7 @@ extern "C" int g4_head_screen(const uint8_t* W4p, const uint16_t* S4, const floa
 int g4::head_screen_impl(const uint8_t* W4p, const uint16_t* S4, const float* coef, const uint8_t* data, const uint8_t* unp,
                          const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col, const float* exc_delta,
                          int N, int K, const float* H, int M, int lim, int* out_idx, int* out_nsurv, void* ws,
-                         size_t ws_bytes, void* stream, int* policy) {
+                         size_t ws_bytes, void* stream, int* policy, const uint8_t* nib) {
   G4_REQUIRE(W4p && S4 && coef && data && cb8 && exc_ptr && H && out_idx && out_nsurv && ws,
              "g4_head_screen: null pointer");
   G4_REQUIRE(M >= 1 && M <= 4 && N > 0 && K > 0 && K % 256 == 0 && lim > 0, "g4_head_screen: bad shape M=%d N=%d K=%d", M,
@@ -1401,6 +1654,7 @@ int g4::head_screen_impl(const uint8_t* W4p, const uint16_t* S4, const float* co
   w.pol = policy;
   HeadPacked P = make_head(data, cb8, exc_ptr, exc_col, exc_delta, N, K);
   P.unp = unp;
+  P.nib = nib;
   if (int rc_ = launch("k_screen_init", k_screen_init, dim3(M), dim3(32), 0, st, H, K, M, w)) return rc_;
   if (int rc = check_launch("k_screen_init")) return rc;
   if (int rc = w4g32_gemm_gated(W4p, S4, H, M, N, K, w.s, N, policy ? policy + 1 : nullptr, st)) return rc;

@@ -41,6 +41,9 @@ SIGNATURES = {
     "g4_head_screen_shard_select": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _SZ, _P]),
     "g4_head_screen_shard_pick": (_I, [_I, _I, _I, _I, _P, _P, _P, _SZ, _P]),
     "g4_head_screen_dist_ws_bytes": (_SZ, [_I, _I, _I]),
+    "g4_bf16p_nib_bytes": (_SZ, [_I, _I]),
+    "g4_bf16p_nib_pack": (_I, [_P, _I, _I, _P, _P]),
+    "g4_bf16p_nib_gemm": (_I, [_P, _P, _P, _P, _P, _I, _I, _P, _I, _P, _I, _P]),
     "g4_head_screen_dist": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _I, _P, _P, _SZ, _P]),
     "g4_nccl_get_unique_id": (_I, [_P]),
     "g4_nccl_comm_init": (_I, [_P, _I, _I, _P]),
@@ -294,6 +297,33 @@ class PackedHead:
                                            _ptr(self.exc_delta), self.N, self.K, _ptr(X), M, _ptr(Y), Y.stride(0),
                                            _stream()), "g4_bf16p_unpacked_gemm")
         return Y
+
+
+def _nib_methods():
+    def nibbled(self):
+        """The split-nibble copy of the head (g4_bf16p_nib_pack), made on first use."""
+        import torch
+        if getattr(self, "_nib", None) is None:
+            nb = lib().g4_bf16p_nib_bytes(self.N, self.K)
+            self._nib = torch.empty(nb, dtype=torch.uint8, device=self.data.device)
+            check(lib().g4_bf16p_nib_pack(_ptr(self.data), self.N, self.K, _ptr(self._nib), _stream()),
+                  "g4_bf16p_nib_pack")
+        return self._nib
+
+    def logits_nib(self, X, out=None):
+        """logits() through the split-nibble copy (g4_bf16p_nib_gemm): the same values."""
+        import torch
+        M = X.shape[0]
+        Y = out if out is not None else torch.empty((M, self.N), dtype=torch.float32, device=X.device)
+        check(lib().g4_bf16p_nib_gemm(_ptr(self.nibbled()), self.cb, _ptr(self.exc_ptr), _ptr(self.exc_col),
+                                      _ptr(self.exc_delta), self.N, self.K, _ptr(X), M, _ptr(Y), Y.stride(0), _stream()),
+              "g4_bf16p_nib_gemm")
+        return Y
+    PackedHead.nibbled = nibbled
+    PackedHead.logits_nib = logits_nib
+
+
+_nib_methods()
 
 
 class ScreenShard:

@@ -125,6 +125,16 @@ int g4_bf16p_gemm(const uint8_t* data, const uint8_t* cb8, const long long* exc_
  * aligned. */
 int g4_bf16p_unpack(const uint8_t* data, const uint8_t* cb8, int N, int K, uint8_t* unp, void* stream);
 /* g4_bf16p_gemm over the unpacked copy and the same exceptions: the same values (K a multiple of 64). */
+/* Split-nibble copy of a packed head (48 B per group: the sign/mantissa bytes [N][G][32], then the
+ * 3-bit exponent codes as nibbles [N][G][16]), in the order the full-head GEMV consumes them:
+ * 25% fewer bytes than the unpacked copy, decoded with byte permutes over the codebook.  nib dev
+ * [g4_bf16p_nib_bytes(N, K)], 16-byte aligned. */
+size_t g4_bf16p_nib_bytes(int N, int K);
+int g4_bf16p_nib_pack(const uint8_t* data, int N, int K, uint8_t* nib, void* stream);
+/* The exact-head GEMV over the split-nibble copy (K % 128 == 0, M <= 4): the values of
+ * g4_bf16p_gemm. */
+int g4_bf16p_nib_gemm(const uint8_t* nib, const uint8_t* cb8, const long long* exc_ptr, const uint16_t* exc_col,
+                      const float* exc_delta, int N, int K, const float* X, int M, float* Y, int ldy, void* stream);
 int g4_bf16p_unpacked_gemm(const uint8_t* unp, const long long* exc_ptr, const uint16_t* exc_col, const float* exc_delta,
                            int N, int K, const float* X, int M, float* Y, int ldy, void* stream);
 /* Greedy pick over raw logits: r16, max, then the lowest index whose softcapped value equals the

@@ -80,6 +80,7 @@ def test_logits_kernel_variants_agree(N, monkeypatch):
             outs.append(head.logits(dev(X)).cpu().numpy())
         monkeypatch.delenv("G4_HEAD_GEMV", raising=False)
         outs.append(head.logits_unpacked(dev(X)).cpu().numpy())
+        outs.append(head.logits_nib(dev(X)).cpu().numpy())
         for Y in outs:
             assert np.array_equal(bits(Y), bits(Yo)), M
 
@@ -100,6 +101,25 @@ def test_unpacked_layout():
     w = ((sm & 0x80) << 8) | (ex << 7) | (sm & 0x7F)
     order = [8 * o + 4 * h + k for h in range(2) for o in (0, 2, 1, 3) for k in range(4)]
     assert np.array_equal(unp, w[:, order].astype(np.uint16))
+
+
+def test_nibble_layout():
+    """The split-nibble copy: sign/mantissa bytes [N][G][32] (half h's 16 at 16h, octets 0, 2, 1, 3,
+    elements 8o+4h..8o+4h+3), then the exponent codes [N][G][16] as nibbles in the same order."""
+    d = np.load(GOLD / "bf16p.npz")
+    head = g4.PackedHead(dev(d["E"].view(np.int16)))
+    nib = head.nibbled().cpu().numpy()
+    data = np.asarray(d["data"]).reshape(-1, 44)
+    ng = data.shape[0]
+    sm_n = nib[: ng * 32].reshape(ng, 32)
+    cd_n = nib[ng * 32:].reshape(ng, 16)
+    planes = data[:, 32:44].copy().view(np.uint32)
+    e = np.arange(32, dtype=np.uint32)
+    codes = ((planes[:, 0:1] >> e) & 1) | (((planes[:, 1:2] >> e) & 1) << 1) | (((planes[:, 2:3] >> e) & 1) << 2)
+    order = [8 * o + 4 * h + k for h in range(2) for o in (0, 2, 1, 3) for k in range(4)]
+    assert np.array_equal(sm_n, data[:, :32][:, order])
+    c = codes[:, order].astype(np.uint8)
+    assert np.array_equal(cd_n, (c[:, 0::2] | (c[:, 1::2] << 4)).astype(np.uint8))
 
 
 def test_pick_tie_rule():
