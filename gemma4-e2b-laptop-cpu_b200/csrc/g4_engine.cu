@@ -1029,6 +1029,10 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0, in
       // kPrefillRows rows of one head per block share each K and V load
       RCK(attn_rows_multi(kPrefillRows, Kc, Vc, e->pqkv, ld, d.NQ, d.HD, pos0, Mc, t.global ? 0 : d.WINDOW, len_max,
                           e->patt, QD, blk_fn, e->cfg.prefill_block, e->st));
+    } else if (e->cfg.prefill_tc == 1 && d.HD <= 256 && d.HD % 16 == 0) {
+      RCK(launch("k_attn_rows2", k_attn_rows2, dim3(Mc, d.NQ), dim3(256), sizeof(float) * len_max, e->st, (const uint16_t*)Kc,
+                 (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.NQ, d.HD, pos0, t.global ? 0 : d.WINDOW, e->patt, QD,
+                 blk_fn, e->cfg.prefill_block));
     } else {
       RCK(launch("k_attn_rows", k_attn_rows, dim3(Mc, d.NQ), dim3(256), sizeof(float) * len_max, e->st, (const uint16_t*)Kc,
                  (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.NQ, d.HD, pos0, t.global ? 0 : d.WINDOW, -1, e->patt, QD,

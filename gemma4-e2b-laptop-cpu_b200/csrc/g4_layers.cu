@@ -708,6 +708,132 @@ __global__ void __launch_bounds__(256) k_attn_rows(const uint16_t* __restrict__ 
   }
 }
 
+// ---- prefill attention with fewer instructions per key (the values of k_attn_rows, variant < 0).
+// Scores (attn_tile rows): eight lanes per key, lane l running chains 2l and 2l+1 (elements 2l+16i
+// and 2l+1+16i, one 32-bit load per i), then v_j = chain j + chain j+8 (xor 4) and the hsum
+// ((v0+v4)+(v1+v5))+((v2+v6)+(v3+v7)) by xor 2 and xor 1: the chains and the order of k_attn_rows.
+// O: thread t runs dims 2t and 2t+1 (one 32-bit V load per key, the weights of 4 keys per 16-byte
+// shared load), each over the keys in order.  Rows of per-row blocks (variant 1) run as in
+// k_attn_rows.  blockDim 256, hd <= 256, hd % 16 == 0; dynamic shared memory len_max floats.
+__global__ void __launch_bounds__(256) k_attn_rows2(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
+                                                    const float* __restrict__ q, int ldq, int nh, int hd, int pos0,
+                                                    int window, float* __restrict__ out, int ldo, int blk_fn, int blk) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(16) float sc[];
+  __shared__ float s_red[32];
+  const int m = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int pos = pos0 + m, lo = window > 0 ? max(0, pos - (window - 1)) : 0, len = pos - lo + 1;
+  const int b0 = pos - (pos - blk_fn) % blk;
+  const int variant = (blk >= 4 && b0 + blk > 64) ? 0 : 1;
+  const float* qh = q + (size_t)m * ldq + (size_t)h * hd;
+  if (variant == 0) {
+    const int l = tid & 7, kq = tid >> 3;  // 32 keys per pass of the block
+    float qa[16], qb[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      qa[i] = i < (hd >> 4) ? qh[2 * l + 16 * i] : 0.f;
+      qb[i] = i < (hd >> 4) ? qh[2 * l + 1 + 16 * i] : 0.f;
+    }
+    for (int pb = lo; pb <= pos; pb += 32) {
+      const int p = min(pb + kq, pos);
+      const uint32_t* kr = reinterpret_cast<const uint32_t*>(Kc + (size_t)p * hd) + l;
+      float aa = 0.f, ab = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < (hd >> 4)) {
+          const uint32_t w = kr[8 * i];
+          aa = fmaf(qa[i], __uint_as_float(w << 16), aa);
+          ab = fmaf(qb[i], __uint_as_float(w & 0xFFFF0000u), ab);
+        }
+      const float va = __fadd_rn(aa, __shfl_xor_sync(FULL, aa, 4)), vb = __fadd_rn(ab, __shfl_xor_sync(FULL, ab, 4));
+      const float pa = __fadd_rn(va, __shfl_xor_sync(FULL, va, 2)), pbv = __fadd_rn(vb, __shfl_xor_sync(FULL, vb, 2));
+      const float s1 = __fadd_rn(pa, pbv);
+      const float s = __fadd_rn(s1, __shfl_xor_sync(FULL, s1, 1));
+      if (l == 0 && pb + kq <= pos) sc[p - lo] = s;
+    }
+  } else {
+    const int hw = tid >> 4, c = tid & 15;
+    float qr[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) qr[i] = (c < 8 && i < (hd >> 3)) ? qh[c + 8 * i] : 0.f;
+    for (int pb = lo + (hw & ~1); pb <= pos; pb += 16) {
+      const int p = min(pb + (hw & 1), pos);
+      const uint16_t* kr = Kc + (size_t)p * hd;
+      float acc = 0.f;
+      if (c < 8) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < (hd >> 3)) acc = fmaf(qr[i], bf2f(kr[c + 8 * i]), acc);
+      }
+      const float s = hsum8_octet(acc);
+      if (c == 0 && pb + (hw & 1) <= pos) sc[p - lo] = s;
+    }
+  }
+  __syncthreads();
+  float mx = -1e30f;
+  for (int i = tid; i < len; i += blockDim.x) mx = fmaxf(mx, sc[i]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+  if ((tid & 31) == 0) s_red[tid >> 5] = mx;
+  __syncthreads();
+  mx = -1e30f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, s_red[i]);
+  __syncthreads();
+  for (int i = tid; i < len; i += blockDim.x) {
+    const float d = __fsub_rn(sc[i], mx);
+    sc[i] = variant == 0 ? exp8(d) : exp_cr(d);
+  }
+  __syncthreads();
+  if (tid == 0) {  // the in-order sum, 8 loads in flight ahead of the chain
+    float den = 0.f;
+    int i = 0;
+    for (; i + 8 <= len; i += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = sc[i + u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) den = __fadd_rn(den, v[u]);
+    }
+    for (; i < len; ++i) den = __fadd_rn(den, sc[i]);
+    s_red[0] = den;
+  }
+  __syncthreads();
+  const float den = s_red[0];
+  if (variant == 1) {
+    for (int i = tid; i < len; i += blockDim.x) sc[i] = __fdiv_rn(sc[i], den);
+    __syncthreads();
+  }
+  const float inv = __fdiv_rn(1.0f, den);
+  for (int t2 = tid; 2 * t2 < hd; t2 += blockDim.x) {
+    float o0 = 0.f, o1 = 0.f;
+    const uint32_t* vp = reinterpret_cast<const uint32_t*>(Vc + (size_t)lo * hd) + t2;
+    const int hw2 = hd >> 1;  // 32-bit words per V row
+    int p = 0;
+    for (; p + 8 <= len; p += 8) {  // 8 V loads in flight ahead of the in-order chains
+      uint32_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = vp[(size_t)(p + u) * hw2];
+      const float4 wa = *reinterpret_cast<const float4*>(sc + p);
+      const float4 wb = *reinterpret_cast<const float4*>(sc + p + 4);
+      const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        o0 = fmaf(w[u], __uint_as_float(v[u] << 16), o0);
+        o1 = fmaf(w[u], __uint_as_float(v[u] & 0xFFFF0000u), o1);
+      }
+    }
+    for (; p < len; ++p) {
+      const uint32_t v = vp[(size_t)p * hw2];
+      o0 = fmaf(sc[p], __uint_as_float(v << 16), o0);
+      o1 = fmaf(sc[p], __uint_as_float(v & 0xFFFF0000u), o1);
+    }
+    float* op = out + (size_t)m * ldo + (size_t)h * hd + 2 * t2;
+    op[0] = variant == 0 ? r16(__fmul_rn(o0, inv)) : r16(o0);
+    op[1] = variant == 0 ? r16(__fmul_rn(o1, inv)) : r16(o1);
+  }
+}
+
 // ---- prefill attention, R consecutive query rows of one head per block.  The rows of a prefill
 // chunk share their keys (global layers: 0..pos; sliding: a window that moves by one per row), so a
 // block takes rows m0..m0+R-1 (positions pos0+m0..) of head h over the union of their key ranges

@@ -34,6 +34,11 @@ __global__ void k_draft_in(const uint16_t* E, const int* tok, const float* h, in
 // blk_fn), as fwd chooses per block (:1328-1355).
 __global__ void k_attn_rows(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0,
                             int window, int variant, float* out, int ldo, int blk_fn = 0, int blk = 32);
+// Prefill attention for rows of full prefill blocks with fewer instructions per key (grid (M, nh),
+// 256 threads, hd <= 256, hd % 16 == 0, dynamic shared memory len_max floats): the values of
+// k_attn_rows with variant < 0.
+__global__ void k_attn_rows2(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0,
+                             int window, float* out, int ldo, int blk_fn, int blk);
 // Prefill attention for rows of full prefill blocks, R consecutive rows of one head per block (grid
 // (ceil(Mrows / R), nh), 256 threads, hd <= 256, dynamic shared memory R * span floats with span =
 // len_max + R - 1): the values of k_attn_rows with variant < 0.
