@@ -35,6 +35,10 @@ import time
 
 import numpy as np
 
+# independent request streams run one CUDA stream each: give the device enough hardware queues that
+# up to 32 of them do not alias onto the default 8 (read when CUDA initialises)
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+
 ROOT = pathlib.Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "gemma4-e2b-laptop-cpu_b200"))
 sys.path.insert(0, str(ROOT / "tests"))
@@ -655,7 +659,7 @@ def run_decode_g4(args, world, rank, local):
     from oracle_lib import make_prompt
     torch.cuda.set_device(local)
     dist_ = init_pg(world, local)
-    eng = g4.Engine(g4.engine_config())
+    eng = g4.Engine(g4.engine_config(graphs=args.graphs))
     prompt = make_prompt(PROMPT_SEED + rank, N_PROMPT)
     if args.fake_ctx:  # the reference's ENGINE_FAKE_CTX mode: LCG K/V for 6,837 positions, then 4 prompt tokens
         eng.fake_ctx(N_PROMPT - 4)
@@ -907,6 +911,9 @@ def main():
                     help="decode: no untimed padding rounds around the timed call (for profiling; clocks unsampled)")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="decode: skip the M=4 MTP and configs[0] GEMV sub-records")
+    ap.add_argument("--graphs", type=int, default=1, choices=[0, 1, 2],
+                    help="decode: 1 = a decode call is one launch of the round-loop graph (default), 2 = one graph "
+                         "launch per verify pass and draft chain, 0 = eager launches")
     ap.add_argument("--fake-ctx", action="store_true",
                     help="decode: build the 6.8k context with the reference's ENGINE_FAKE_CTX values instead of a "
                          "prefill (short, for profiling)")
