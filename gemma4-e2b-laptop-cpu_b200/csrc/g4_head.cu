@@ -1097,11 +1097,14 @@ __global__ void k_bf16u_pack(const uint8_t* __restrict__ data, long long ngroups
     }
 }
 
-// ---- split-nibble layout of the packed head (48 bytes per group, two arrays): sm [N][G][32] holds
-// the 32 sign/mantissa bytes of bf16p::pack, half h's 16 at byte 16h in the order that half consumes
-// them (octets in chain order 0, 2, 1, 3; elements 8o+4h..8o+4h+3 within an octet: one 32-bit word
-// per octet quad), and codes [N][G][16] the same weights' 3-bit exponent codes as nibbles, half h's
-// 16 at byte 8h (word w of a half: quads 2w and 2w+1, nibble k of a quad = its weight k).  A quad's
+// ---- split-nibble layout of the packed head (48 bytes per group, two arrays): sm [N][G/4][2][4][16]
+// holds the 32 sign/mantissa bytes of bf16p::pack, per block of 4 groups first the half-0 parts of
+// the 4 groups, then the half-1 parts (so that the 16-byte loads of 4 rows x 2 halves land on 8
+// distinct bank quads under the 128-byte swizzle), half h's 16 bytes of a group in the order that
+// half consumes them (octets in chain order 0, 2, 1, 3; elements 8o+4h..8o+4h+3 within an octet: one
+// 32-bit word per octet quad); codes [N][G][16] holds the same weights' 3-bit exponent codes as
+// nibbles, half h's 16 at byte 8h (word w of a half: quads 2w and 2w+1, nibble k of a quad = its
+// weight k).  A quad's
 // four codes are one byte-permute selector over the 8-entry codebook: two permutes give the four
 // weights' bf16 high-byte exponent bits (e >> 1) and low-byte bit ((e & 1) << 7), two masked merges
 // add the sign and mantissa, and two permutes interleave the bytes into the two bf16 pairs that the
@@ -1115,7 +1118,7 @@ __global__ void k_bf16n_pack(const uint8_t* __restrict__ data, long long ngroups
   uint32_t w[11];
 #pragma unroll
   for (int i = 0; i < 11; ++i) w[i] = src[i];
-  uint32_t* sm = reinterpret_cast<uint32_t*>(sm_out + g * 32);
+  uint8_t* smb = sm_out + (g >> 2) * 128 + (g & 3) * 16;  // + 64 h: half h's part
   uint32_t* cd = reinterpret_cast<uint32_t*>(code_out + g * 16);
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -1131,7 +1134,7 @@ __global__ void k_bf16n_pack(const uint8_t* __restrict__ data, long long ngroups
         smw |= ((w[e >> 2] >> (8 * (e & 3))) & 0xFFu) << (8 * k);
         code |= idx << (4 * k);
       }
-      sm[4 * h + oi] = smw;
+      reinterpret_cast<uint32_t*>(smb + 64 * h)[oi] = smw;
       cw[oi >> 1] |= code << (16 * (oi & 1));
     }
     cd[2 * h] = cw[0];
@@ -1354,7 +1357,7 @@ __global__ void __launch_bounds__(kBnThreads, 2) k_bf16n_rows_tma(const __grid_c
     uint32_t smv[16], cdv[8];  // this half's sign/mantissa words and code words of the item's 4 groups
 #pragma unroll
     for (int gg = 0; gg < 4; ++gg) {
-      const uint4 s4 = *reinterpret_cast<const uint4*>(smrow + (((2 * gg + half) ^ (rl & 7)) << 4));
+      const uint4 s4 = *reinterpret_cast<const uint4*>(smrow + (((gg + 4 * half) ^ (rl & 7)) << 4));
       smv[4 * gg] = s4.x; smv[4 * gg + 1] = s4.y; smv[4 * gg + 2] = s4.z; smv[4 * gg + 3] = s4.w;
       const uint2 c2 = *reinterpret_cast<const uint2*>(cdrow + ((gg ^ ((rl >> 1) & 3)) << 4) + 8 * half);
       cdv[2 * gg] = c2.x; cdv[2 * gg + 1] = c2.y;
@@ -1376,11 +1379,19 @@ __global__ void __launch_bounds__(kBnThreads, 2) k_bf16n_rows_tma(const __grid_c
         bf16n_quad(smv[4 * gg + oi], (oi & 1) ? (cw >> 16) : (cw & 0xFFFFu), cbh_lo, cbh_hi, cbl_lo, cbl_hi, w0, w1);
         const float wk[4] = {__uint_as_float(w0 << 16), __uint_as_float(w0 & 0xFFFF0000u), __uint_as_float(w1 << 16),
                              __uint_as_float(w1 & 0xFFFF0000u)};
+        // the quad's activations: 4 x NP consecutive pairs, 2 x NP 16-byte loads
+        const float4* x4 = reinterpret_cast<const float4*>(xg + 8 * o8 * NP);
+        float4 xv[2 * NP];
+#pragma unroll
+        for (int j = 0; j < 2 * NP; ++j) xv[j] = x4[j];
 #pragma unroll
         for (int k = 0; k < 4; ++k)
 #pragma unroll
-          for (int p = 0; p < NP; ++p)
-            acc[k][p] = __ffma2_rn(make_float2(wk[k], wk[k]), xg[(8 * o8 + k) * NP + p], acc[k][p]);
+          for (int p = 0; p < NP; ++p) {
+            const int f = k * NP + p;
+            const float2 xp = (f & 1) ? make_float2(xv[f >> 1].z, xv[f >> 1].w) : make_float2(xv[f >> 1].x, xv[f >> 1].y);
+            acc[k][p] = __ffma2_rn(make_float2(wk[k], wk[k]), xp, acc[k][p]);
+          }
       }
     }
     if (c == nch - 1) {
@@ -1571,7 +1582,7 @@ extern "C" size_t g4_bf16p_nib_bytes(int N, int K) { return (size_t)N * (size_t)
 
 extern "C" int g4_bf16p_nib_pack(const uint8_t* data, int N, int K, uint8_t* nib, void* stream) {
   G4_REQUIRE(data && nib, "g4_bf16p_nib_pack: null pointer");
-  G4_REQUIRE(N > 0 && K > 0 && K % 32 == 0, "g4_bf16p_nib_pack: bad shape N=%d K=%d", N, K);
+  G4_REQUIRE(N > 0 && K > 0 && K % 128 == 0, "g4_bf16p_nib_pack: bad shape N=%d K=%d (K % 128 == 0)", N, K);
   G4_REQUIRE(aligned(data, 4) && aligned(nib, 16), "g4_bf16p_nib_pack: data 4-byte, nib 16-byte aligned");
   const long long ng = (long long)N * (K / 32);
   k_bf16n_pack<<<(unsigned)((ng + 255) / 256), 256, 0, as_stream(stream)>>>(data, ng, nib, nib + (size_t)ng * 32);

@@ -125,8 +125,9 @@ int g4_bf16p_gemm(const uint8_t* data, const uint8_t* cb8, const long long* exc_
  * aligned. */
 int g4_bf16p_unpack(const uint8_t* data, const uint8_t* cb8, int N, int K, uint8_t* unp, void* stream);
 /* g4_bf16p_gemm over the unpacked copy and the same exceptions: the same values (K a multiple of 64). */
-/* Split-nibble copy of a packed head (48 B per group: the sign/mantissa bytes [N][G][32], then the
- * 3-bit exponent codes as nibbles [N][G][16]), in the order the full-head GEMV consumes them:
+/* Split-nibble copy of a packed head (48 B per group: the sign/mantissa bytes [N][G/4][2][4][16] —
+ * per 4 groups the half-0 parts, then the half-1 parts — then the 3-bit exponent codes as nibbles
+ * [N][G][16]), in the order the full-head GEMV consumes them (K % 128 == 0):
  * 25% fewer bytes than the unpacked copy, decoded with byte permutes over the codebook.  nib dev
  * [g4_bf16p_nib_bytes(N, K)], 16-byte aligned. */
 size_t g4_bf16p_nib_bytes(int N, int K);

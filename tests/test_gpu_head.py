@@ -104,14 +104,15 @@ def test_unpacked_layout():
 
 
 def test_nibble_layout():
-    """The split-nibble copy: sign/mantissa bytes [N][G][32] (half h's 16 at 16h, octets 0, 2, 1, 3,
-    elements 8o+4h..8o+4h+3), then the exponent codes [N][G][16] as nibbles in the same order."""
+    """The split-nibble copy: sign/mantissa bytes [N][G/4][2][4][16] (per 4 groups the half-0 parts,
+    then the half-1 parts; octets 0, 2, 1, 3, elements 8o+4h..8o+4h+3), then the exponent codes
+    [N][G][16] as nibbles (half h's 16 at byte 8h) in the same order."""
     d = np.load(GOLD / "bf16p.npz")
     head = g4.PackedHead(dev(d["E"].view(np.int16)))
     nib = head.nibbled().cpu().numpy()
     data = np.asarray(d["data"]).reshape(-1, 44)
     ng = data.shape[0]
-    sm_n = nib[: ng * 32].reshape(ng, 32)
+    sm_n = nib[: ng * 32].reshape(ng // 4, 2, 4, 16).transpose(0, 2, 1, 3).reshape(ng, 32)
     cd_n = nib[ng * 32:].reshape(ng, 16)
     planes = data[:, 32:44].copy().view(np.uint32)
     e = np.arange(32, dtype=np.uint32)
