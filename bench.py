@@ -650,6 +650,48 @@ def decode_roofline(eng, d, M_pass, P_mid, peak, peak_kind):
                       "CUDA events around 20 replays of its graph"}
 
 
+def run_prefill_g4(args, world, rank, local):
+    """configs[4]'s prompt prefill: the 6,841-token prompt through the tensor-core path (full blocks
+    in chunks of 2,048 rows, the last block through the GEMV path), W untimed prefills first (the
+    first builds the int8 weight copies), then K timed prefills on the engine stream.  A step is
+    one prefill of the whole prompt; value = prompt tokens / second, summed over replicas."""
+    import torch
+    import g4
+    from oracle_lib import make_prompt
+    torch.cuda.set_device(local)
+    dist_ = init_pg(world, local)
+    n_prompt = args.prompt_tokens or N_PROMPT
+    eng = g4.Engine(g4.engine_config(prefill_tc=args.prefill_tc, ctx_max=max(8192, n_prompt + 64)))
+    prompt = make_prompt(PROMPT_SEED + rank, n_prompt)
+    for _ in range(args.warmup):
+        eng.prefill(prompt)
+    torch.cuda.synchronize()
+    barrier(dist_)
+    times = []
+    with Clocks(local) as clk:
+        for _ in range(args.steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            eng.prefill(prompt)  # host token ids in; the first token back (one H2D and one D2H copy)
+            times.append(time.perf_counter() - t0)
+    s_max = max_over_ranks(sum(times), dist_)
+    eng.close()
+    out = None
+    if rank == 0:
+        out = {
+            "metric": "prompt prefill tok/s (configs[4] prompt)", "value": n_prompt * args.steps * world / s_max,
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": s_max / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32+int8", "data": "synthetic (seeded random-init E2B weights; Zipf(1.1) prompt with copied spans)",
+            "config": {"workload": f"configs[4] prefill of a {n_prompt}-token prompt", "prefill_tc": args.prefill_tc,
+                       "timing": "host wall clock around each g4_engine_prefill call (it synchronises), max over "
+                                 "ranks", "parallelism": f"replicas x{world}"},
+            "e2e": {"value": n_prompt * args.steps * world / s_max, "unit": "tok/s",
+                    "h2d_bytes_per_step": 4 * n_prompt, "d2h_bytes_per_step": 4},
+            "clocks": clk.summary(),
+        }
+    return out, dist_
+
 HEAD_BF16P_BYTES = 262144 * (2048 // 32) * 44  # the exact head rows the fallback reads
 
 
@@ -902,7 +944,10 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "head", "screen"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "head", "screen", "prefill"])
+    ap.add_argument("--prefill-tc", type=int, default=1, choices=[0, 1, 2, 3],
+                    help="prefill: the engine's prefill_tc (1 tensor-core GEMMs + eight-lanes-per-key attention)")
+    ap.add_argument("--prompt-tokens", type=int, default=0, help="prefill: prompt length (default 6,841)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--planted", action="store_true",
                     help="screen: planted hidden states a * w_j/|w_j| + sqrt(1 - a^2) * noise (a = --plant-weight)")
@@ -919,9 +964,9 @@ def main():
                          "prefill (short, for profiling)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"decode": 64, "gemv": 200, "head": 20, "screen": 20}[args.workload]
+        args.steps = {"decode": 64, "gemv": 200, "head": 20, "screen": 20, "prefill": 5}[args.workload]
     if args.warmup is None:
-        args.warmup = 3 if args.workload == "decode" else 10
+        args.warmup = 3 if args.workload in ("decode", "prefill") else 10
     args.warmup = max(args.warmup, 3)
     if args.workload == "decode":
         args.steps = min(args.steps, 120)  # 6,841 + 4 x (W + K + ~2 x 0.4 s of padding rounds) tokens fit 8,192
@@ -932,7 +977,7 @@ def main():
             return
         if args.workload == "decode":
             reference_decode(args)
-        elif args.workload in ("head", "screen"):
+        elif args.workload in ("head", "screen", "prefill"):
             print(json.dumps({"impl": "reference", "unavailable": f"the {args.workload} workload has no reference "
                               "arm; its cpu_baseline is the oracle's restatement"}))
         else:
@@ -947,6 +992,8 @@ def main():
         out, dist_ = run_screen_g4(args, world, rank, local)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_screen_port()
+    elif args.workload == "prefill":
+        out, dist_ = run_prefill_g4(args, world, rank, local)
     elif args.workload == "head":
         out, (dist_, head, Xd) = run_head_g4(args, world, rank, local)
         if rank == 0 and not args.no_cpu_baseline:
