@@ -89,6 +89,13 @@ class Clocks:
                                          stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        t0 = time.perf_counter()  # the sampler's start-up can take a while: wait for its first sample
+        while time.perf_counter() - t0 < 5.0 and self.proc.poll() is None:
+            self.out.flush()
+            if os.fstat(self.out.fileno()).st_size > 0:
+                break
+            time.sleep(0.05)
         return self
 
     def __exit__(self, *a):

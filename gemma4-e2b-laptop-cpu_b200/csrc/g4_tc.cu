@@ -181,8 +181,11 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const int c = 32 * half + 8 * c8 + u;
-              const uint32_t b = (u & 1) ? (wv[u >> 1] >> 16) : (wv[u >> 1] & 0xFFFFu);
-              acc[c] = fmaf((float)(int)r[8 * c8 + u], __fmul_rn(bf2f(b), sx), acc[c]);
+              // the group's integer dot as a float without the conversion pipe: |a32| <= 32 x 8 x 128
+              // < 2^22, so 1.5 x 2^23 + a32 is exact in the mantissa and the subtraction is exact
+              const float a = __fsub_rn(__int_as_float((int)r[8 * c8 + u] + 0x4B400000), 12582912.0f);
+              const float wsc = __uint_as_float((u & 1) ? (wv[u >> 1] & 0xFFFF0000u) : (wv[u >> 1] << 16));
+              acc[c] = fmaf(a, __fmul_rn(wsc, sx), acc[c]);
             }
           }
         }
