@@ -41,11 +41,6 @@ long long& launch_count() {
   return n;
 }
 
-L2Prefetch& next_prefetch() {
-  static thread_local L2Prefetch p;
-  return p;
-}
-
 bool& pdl_enabled() {
   static thread_local bool on = false;
   return on;

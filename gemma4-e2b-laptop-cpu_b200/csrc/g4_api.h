@@ -29,17 +29,6 @@ struct QuantOut;
 bool encode_tmap_2d(CUtensorMap* out, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
                     uint64_t stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
 bool& pdl_enabled();
-// L2 prefetch of the next linear's weights and scales, set by the engine on this host thread for the
-// next W4A8 GEMV launch (which consumes and clears it): each CTA of that GEMV asks L2 for its slice
-// of both ranges in its prologue, so the next GEMV's weights stream from HBM while the kernels in
-// between (norms, attention) leave it idle.  Prefetches only: no data dependency, no values change.
-struct L2Prefetch {
-  const void* w = nullptr;
-  size_t wb = 0;
-  const void* s = nullptr;
-  size_t sb = 0;
-};
-L2Prefetch& next_prefetch();
 // Set when g4_device_status() has seen the in-flight bit (bit 1) and cleared by its reset: while
 // set, launch() refuses every kernel, since a CTA's shared or tensor memory may have been written
 // after that CTA ended.

@@ -659,15 +659,6 @@ static int lin(g4_engine* e, const Lin& w, const float* X, int M, float* Y, bool
   return G4_OK;
 }
 
-// lin() with the next linear's weights and scales requested into L2 by the GEMV's CTAs.
-static int lin_pf(g4_engine* e, const Lin& w, const float* X, int M, float* Y, bool force_i8, bool prequant, const Lin* next) {
-  if (next != nullptr)
-    next_prefetch() = L2Prefetch{next->w, (size_t)next->N * next->K / 2, next->s, (size_t)next->N * (next->K / 32) * 2};
-  const int rc = lin(e, w, X, M, Y, force_i8, prequant);
-  next_prefetch() = L2Prefetch{};
-  return rc;
-}
-
 // One target forward over M tokens at positions pos0.. (fwd, :1256-1502).  toks are device ints;
 // when want, rows hf.. get the final-normed hidden in hbuf and the greedy next token in G.  With
 // dyn the positions are ctl[0] + 1.. read on the device (pos0 unused; M <= 4 and the split-KV path,
@@ -771,7 +762,7 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
     const TLayer& t = e->L[l];
     const int ty = t.global ? 1 : 0;
     pf.mark(e->st, PH_LINEAR);
-    RCK(lin_pf(e, t.qkv, e->a, M, e->qkv, false, true, &t.o));
+    RCK(lin(e, t.qkv, e->a, M, e->qkv, false, true));
     uint16_t* Kc = e->Kc + (size_t)l * e->cfg.ctx_max * d.HD;
     uint16_t* Vc = e->Vc + (size_t)l * e->cfg.ctx_max * d.HD;
     pf.mark(e->st, PH_EMBED_NORM);
@@ -811,15 +802,15 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
       RCK(check_launch("k_attn_rows"));
     }
     pf.mark(e->st, PH_LINEAR);
-    RCK(lin_pf(e, t.o, e->att, M, e->o, false, att_q, &t.gu));
+    RCK(lin(e, t.o, e->att, M, e->o, false, att_q));
     pf.mark(e->st, PH_EMBED_NORM);
     RCK(launch("k_post_attn_q", k_post_attn_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, t.post_attn, t.pre_ff, e->mlp_in, H, qo));
     pf.mark(e->st, PH_LINEAR);
-    RCK(lin_pf(e, t.gu, e->mlp_in, M, e->gu, false, true, &t.down));
+    RCK(lin(e, t.gu, e->mlp_in, M, e->gu, false, true));
     pf.mark(e->st, PH_EMBED_NORM);
     RCK(launch("k_act_q", k_act_q, dim3((unsigned)((long long)M * d.I / 256)), dim3(256), 0, e->st, e->gu, d.I, M, e->act, qo));
     pf.mark(e->st, PH_LINEAR);
-    RCK(lin_pf(e, t.down, e->act, M, e->o, false, true, l + 1 < d.NL ? &e->L[l + 1].qkv : nullptr));
+    RCK(lin(e, t.down, e->act, M, e->o, false, true));
     pf.mark(e->st, PH_EMBED_NORM);
     if (l + 1 < d.NL)  // residual (layer scalar 1) and the next layer's input norm
       RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, t.post_ff, 1.0f, H, e->L[l + 1].in_ln, e->a, 0, qo));

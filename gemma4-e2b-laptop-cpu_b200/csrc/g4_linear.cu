@@ -601,8 +601,7 @@ template <int M, int ROWS, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32)
 k_w4a8_all(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const int8_t* __restrict__ q,
            const float* __restrict__ sx, const int32_t* __restrict__ sum, int N, int K, float* __restrict__ Y, int ldy,
-           int CH, const uint8_t* __restrict__ pfw, unsigned long long pfw_bytes, const uint8_t* __restrict__ pfs,
-           unsigned long long pfs_bytes) {
+           int CH) {
   constexpr int T = WARPS * 32;
   const int G = K >> 5, nchunk = G / CH;
   const int wrs = K >> 1;  // the CTA's rows sit as in memory (phase 1 reads one row at a time)
@@ -624,20 +623,6 @@ k_w4a8_all(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const
     mbar_expect_tx(&bars[0], wbytes + sbytes);
     bulk_g2s(wbuf, Wp + (size_t)n0 * (K >> 1), wbytes, &bars[0]);
     bulk_g2s(sc, S + (size_t)n0 * G, sbytes, &bars[0]);
-    // this CTA's slice of the next linear's weights and scales, into L2 (both multiples of 16 bytes)
-    if (pfw != nullptr) {
-      const unsigned long long tot[2] = {pfw_bytes, pfs_bytes};
-      const uint8_t* base[2] = {pfw, pfs};
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        const unsigned long long per = ((tot[a] + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
-        const unsigned long long off = per * blockIdx.x;
-        if (off < tot[a]) {
-          const unsigned long long nb = min(per, tot[a] - off);
-          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base[a] + off), "r"((uint32_t)nb) : "memory");
-        }
-      }
-    }
   }
   __syncthreads();  // the barrier is initialised before anyone polls it
   pdl_wait();  // the weights above are read-only; activations come from the previous kernel
@@ -1019,13 +1004,7 @@ static int launch_w4a8_all_t(const uint8_t* Wp, const uint16_t* S, const int8_t*
                              int N, int K, float* Y, int ldy, int CH, cudaStream_t st) {
   const size_t smem = w4a8_all_smem(M, ROWS, K);
   if (smem > 48 * 1024) cudaFuncSetAttribute(k_w4a8_all<M, ROWS, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  L2Prefetch pf = next_prefetch();
-  next_prefetch() = L2Prefetch{};
-  if (pf.w == nullptr || pf.s == nullptr || (pf.wb | pf.sb) % 16 != 0 || !aligned(pf.w, 16) || !aligned(pf.s, 16)) pf = L2Prefetch{};
-  if (int rc_ = launch("k_w4a8_all", k_w4a8_all<M, ROWS, WARPS>, dim3((N + ROWS - 1) / ROWS), dim3(WARPS * 32), smem, st, Wp, S, q,
-                       sx, sum, N, K, Y, ldy, CH, static_cast<const uint8_t*>(pf.w), (unsigned long long)pf.wb,
-                       static_cast<const uint8_t*>(pf.s), (unsigned long long)pf.sb))
-    return rc_;
+  if (int rc_ = launch("k_w4a8_all", k_w4a8_all<M, ROWS, WARPS>, dim3((N + ROWS - 1) / ROWS), dim3(WARPS * 32), smem, st, Wp, S, q, sx, sum, N, K, Y, ldy, CH)) return rc_;
   return check_launch("k_w4a8_all");
 }
 
