@@ -156,9 +156,9 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
     // epilogue: warp w -> tensor-memory lanes 32 (w % 4).. (tile rows), columns 64 (w / 4)..
     const int q = warp & 3, h = warp >> 2;
     const int row = 32 * q + lane;
-    float acc[64];
+    float2 acc[32];  // columns 2c, 2c+1: the chains advance in pairs through packed fp32 operations
 #pragma unroll
-    for (int c = 0; c < 64; ++c) acc[c] = 0.f;
+    for (int c = 0; c < 32; ++c) acc[c] = make_float2(0.f, 0.f);
     bool ok = true;
     for (int s = 0; s < nst && ok; ++s) {
       const int st = s % kTcNS;
@@ -179,13 +179,15 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
             const uint4 w8 = *reinterpret_cast<const uint4*>(sw + 32 * half + 8 * c8);
             const uint32_t wv[4] = {w8.x, w8.y, w8.z, w8.w};
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int c = 32 * half + 8 * c8 + u;
-              // the group's integer dot as a float without the conversion pipe: |a32| <= 32 x 8 x 128
+            for (int v = 0; v < 4; ++v) {
+              const int c2 = 16 * half + 4 * c8 + v;  // columns 2 c2, 2 c2 + 1
+              // the group's integer dots as floats without the conversion pipe: |a32| <= 32 x 8 x 128
               // < 2^22, so 1.5 x 2^23 + a32 is exact in the mantissa and the subtraction is exact
-              const float a = __fsub_rn(__int_as_float((int)r[8 * c8 + u] + 0x4B400000), 12582912.0f);
-              const float wsc = __uint_as_float((u & 1) ? (wv[u >> 1] & 0xFFFF0000u) : (wv[u >> 1] << 16));
-              acc[c] = fmaf(a, __fmul_rn(wsc, sx), acc[c]);
+              const float2 a = __fadd2_rn(make_float2(__int_as_float((int)r[8 * c8 + 2 * v] + 0x4B400000),
+                                                      __int_as_float((int)r[8 * c8 + 2 * v + 1] + 0x4B400000)),
+                                          make_float2(-12582912.0f, -12582912.0f));
+              const float2 wsc = make_float2(__uint_as_float(wv[v] << 16), __uint_as_float(wv[v] & 0xFFFF0000u));
+              acc[c2] = __ffma2_rn(a, __fmul2_rn(wsc, make_float2(sx, sx)), acc[c2]);
             }
           }
         }
@@ -200,7 +202,8 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
     if (ok && m < M) {
       float* yr = Y + (size_t)m * ldy + n0 + 64 * h;
 #pragma unroll
-      for (int c = 0; c < 64; c += 4) *reinterpret_cast<float4*>(yr + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+      for (int c = 0; c < 32; c += 2)
+        *reinterpret_cast<float4*>(yr + 2 * c) = make_float4(acc[c].x, acc[c].y, acc[c + 1].x, acc[c + 1].y);
     }
   }
   tc_fence_before();
