@@ -478,6 +478,10 @@ __global__ void k_w4a8_quant(const float* __restrict__ X, int MG, int G, int8_t*
   (void)G;
 }
 
+// An exact group dot |a| < 2^22 as a float without the conversion pipe: 1.5 x 2^23 + a is exact in
+// the mantissa and so is the subtraction (here |a| <= 32 x 8 x 128).
+__device__ __forceinline__ float i32_to_f32(int a) { return __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f); }
+
 // ------------------------------------------------------------------------------ W4A8 GEMV
 // Each CTA owns 8 weight rows streamed into shared memory as in k_w4g32.  Per chunk, phase 1
 // has each thread take one group for all 8 rows (its int8 activations, scale and sum are loaded
@@ -565,7 +569,7 @@ k_w4a8(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const int
           acc = __dp4a((int)hi[1], qb[m].y, acc);
           acc = __dp4a((int)hi[2], qb[m].z, acc);
           acc = __dp4a((int)hi[3], qb[m].w, acc);
-          ac[(size_t)(r * M + m) * acs + gl] = make_float2((float)acc, __fmul_rn(sw, sxm[m]));
+          ac[(size_t)(r * M + m) * acs + gl] = make_float2(i32_to_f32(acc), __fmul_rn(sw, sxm[m]));
         }
       }
     }
@@ -670,7 +674,7 @@ k_w4a8_all(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const
           acc = __dp4a((int)hi[1], qb[m].y, acc);
           acc = __dp4a((int)hi[2], qb[m].z, acc);
           acc = __dp4a((int)hi[3], qb[m].w, acc);
-          ac[(size_t)(r * M + m) * acs + g] = make_float2((float)acc, __fmul_rn(sw, sxm[m]));
+          ac[(size_t)(r * M + m) * acs + g] = make_float2(i32_to_f32(acc), __fmul_rn(sw, sxm[m]));
         }
       }
     }
@@ -780,7 +784,7 @@ k_w4a8_ring(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, cons
           acc = __dp4a((int)hi[1], qb[m].y, acc);
           acc = __dp4a((int)hi[2], qb[m].z, acc);
           acc = __dp4a((int)hi[3], qb[m].w, acc);
-          ac[(size_t)(r * M + m) * acs + g] = make_float2((float)acc, __fmul_rn(sw, sxm[m]));
+          ac[(size_t)(r * M + m) * acs + g] = make_float2(i32_to_f32(acc), __fmul_rn(sw, sxm[m]));
         }
       }
     }
