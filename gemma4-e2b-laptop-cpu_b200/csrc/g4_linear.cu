@@ -478,9 +478,14 @@ __global__ void k_w4a8_quant(const float* __restrict__ X, int MG, int G, int8_t*
   (void)G;
 }
 
-// An exact group dot |a| < 2^22 as a float without the conversion pipe: 1.5 x 2^23 + a is exact in
-// the mantissa and so is the subtraction (here |a| <= 32 x 8 x 128).
-__device__ __forceinline__ float i32_to_f32(int a) { return __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f); }
+// A group dot as a float without the conversion pipe when |a| < 2^22 (always, for finite
+// activations: |a| <= 32 x 8 x 128): 1.5 x 2^23 + a is exact in the mantissa and so is the
+// subtraction.  A group sum of the quantisation of a non-finite row can push a out of range; that
+// case takes the ordinary conversion.
+__device__ __forceinline__ float i32_to_f32(int a) {
+  if ((unsigned)(a + (1 << 22)) < (1u << 23)) return __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f);
+  return (float)a;
+}
 
 // ------------------------------------------------------------------------------ W4A8 GEMV
 // Each CTA owns 8 weight rows streamed into shared memory as in k_w4g32.  Per chunk, phase 1
