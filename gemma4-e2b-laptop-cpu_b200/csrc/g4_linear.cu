@@ -483,7 +483,7 @@ __global__ void k_w4a8_quant(const float* __restrict__ X, int MG, int G, int8_t*
 // subtraction.  A group sum of the quantisation of a non-finite row can push a out of range; that
 // case takes the ordinary conversion.
 __device__ __forceinline__ float i32_to_f32(int a) {
-  if ((unsigned)(a + (1 << 22)) < (1u << 23)) return __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f);
+  if ((unsigned)a + (1u << 22) < (1u << 23)) return __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f);
   return (float)a;
 }
 
