@@ -1031,12 +1031,8 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0, in
                           e->patt, QD, blk_fn, e->cfg.prefill_block, e->st));
     } else if (e->cfg.prefill_tc == 4 && d.HD <= 256 && d.HD % 16 == 0 && d.NQ % 2 == 0 &&
                sizeof(float) * 2 * (size_t)((len_max + 3) & ~3) <= 200 * 1024) {
-      const int ls = (len_max + 3) & ~3;
-      const size_t smem = sizeof(float) * 2 * (size_t)ls;
-      if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_rows2h, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      RCK(launch("k_attn_rows2h", k_attn_rows2h, dim3(Mc, d.NQ / 2), dim3(256), smem, e->st, (const uint16_t*)Kc,
-                 (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.NQ, d.HD, pos0, t.global ? 0 : d.WINDOW, e->patt, QD,
-                 blk_fn, e->cfg.prefill_block, ls));
+      RCK(attn_rows2h(Kc, Vc, e->pqkv, ld, d.NQ, d.HD, pos0, Mc, t.global ? 0 : d.WINDOW, len_max, e->patt, QD, blk_fn,
+                      e->cfg.prefill_block, e->st));
     } else if (e->cfg.prefill_tc == 1 && d.HD <= 256 && d.HD % 16 == 0) {
       RCK(launch("k_attn_rows2", k_attn_rows2, dim3(Mc, d.NQ), dim3(256), sizeof(float) * len_max, e->st, (const uint16_t*)Kc,
                  (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.NQ, d.HD, pos0, t.global ? 0 : d.WINDOW, e->patt, QD,

@@ -997,6 +997,20 @@ __global__ void __launch_bounds__(256) k_attn_rows2h(const uint16_t* __restrict_
   }
 }
 
+int attn_rows2h(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0, int Mrows,
+                int window, int len_max, float* out, int ldo, int blk_fn, int blk, cudaStream_t st) {
+  const int ls = (len_max + 3) & ~3;
+  const size_t smem = sizeof(float) * 2 * (size_t)ls;
+  if (hd > 256 || hd % 16 != 0 || nh % 2 != 0 || smem > 200 * 1024)
+    return set_error(G4_ERR_UNSUPPORTED, "prefill attention (two heads per block): hd=%d nh=%d keys=%d", hd, nh, len_max);
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(k_attn_rows2h, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "k_attn_rows2h: %s", cudaGetErrorString(e));
+  }
+  return launch("k_attn_rows2h", k_attn_rows2h, dim3(Mrows, nh / 2), dim3(256), smem, st, Kc, Vc, q, ldq, nh, hd, pos0,
+                window, out, ldo, blk_fn, blk, ls);
+}
+
 // ---- prefill attention, R consecutive query rows of one head per block.  The rows of a prefill
 // chunk share their keys (global layers: 0..pos; sliding: a window that moves by one per row), so a
 // block takes rows m0..m0+R-1 (positions pos0+m0..) of head h over the union of their key ranges
