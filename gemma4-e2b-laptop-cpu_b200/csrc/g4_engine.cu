@@ -797,6 +797,8 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
     } else {
       const int variant = (M >= 4 && pos0 + M > 64) ? 0 : 1;  // attn_tile, else per-(row, head) (:1328-1355)
       const int len_max = (t.global ? pos0 + M : std::min(pos0 + M, d.WINDOW));
+      if (sizeof(float) * len_max > 40 * 1024)
+        cudaFuncSetAttribute(k_attn_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sizeof(float) * len_max));
       k_attn_rows<<<dim3(M, d.NQ), 256, sizeof(float) * len_max, e->st>>>(Kc, Vc, e->qkv, ld, d.NQ, d.HD, pos0,
                                                                            t.global ? 0 : d.WINDOW, variant, e->att, QD);
       RCK(check_launch("k_attn_rows"));
@@ -1020,7 +1022,7 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0, in
     if (e->cfg.prefill_tc == 2 && d.NQ % 4 == 0 && d.HD <= 256) {  // four heads per block share each K and V row
       const size_t smem = sizeof(float) * 4 * (size_t)len_max;
       if (smem > 200 * 1024) return set_error(G4_ERR_UNSUPPORTED, "prefill attention: %zu B of shared memory", smem);
-      if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (smem > 40 * 1024) cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       RCK(launch("k_attn_prefill", k_attn_prefill, dim3(Mc, d.NQ / 4), dim3(288), smem, e->st, (const uint16_t*)Kc,
                  (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.HD, pos0, t.global ? 0 : d.WINDOW, blk_fn,
                  e->cfg.prefill_block, e->patt, QD));
@@ -1034,10 +1036,14 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0, in
       RCK(attn_rows2h(Kc, Vc, e->pqkv, ld, d.NQ, d.HD, pos0, Mc, t.global ? 0 : d.WINDOW, len_max, e->patt, QD, blk_fn,
                       e->cfg.prefill_block, e->st));
     } else if (e->cfg.prefill_tc == 1 && d.HD <= 256 && d.HD % 16 == 0) {
+      if (sizeof(float) * len_max > 40 * 1024)
+        cudaFuncSetAttribute(k_attn_rows2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sizeof(float) * len_max));
       RCK(launch("k_attn_rows2", k_attn_rows2, dim3(Mc, d.NQ), dim3(256), sizeof(float) * len_max, e->st, (const uint16_t*)Kc,
                  (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.NQ, d.HD, pos0, t.global ? 0 : d.WINDOW, e->patt, QD,
                  blk_fn, e->cfg.prefill_block));
     } else {
+      if (sizeof(float) * len_max > 40 * 1024)
+        cudaFuncSetAttribute(k_attn_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sizeof(float) * len_max));
       RCK(launch("k_attn_rows", k_attn_rows, dim3(Mc, d.NQ), dim3(256), sizeof(float) * len_max, e->st, (const uint16_t*)Kc,
                  (const uint16_t*)Vc, (const float*)e->pqkv, ld, d.NQ, d.HD, pos0, t.global ? 0 : d.WINDOW, -1, e->patt, QD,
                  blk_fn, e->cfg.prefill_block));

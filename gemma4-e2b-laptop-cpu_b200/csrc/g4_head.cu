@@ -1532,7 +1532,7 @@ static int launch_head_gemv(const HeadPacked& P, const float* X, float* Y, int l
   }
   const size_t rsmem = head_rows_smem(M, P.K);
   if (P.K % 128 == 0 && rsmem <= 100 * 1024 && aligned(P.data, 16) && !(hv && hv[0] == 'o')) {
-    if (rsmem > 48 * 1024) cudaFuncSetAttribute(k_bf16p_rows<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem);
+    if (rsmem > 40 * 1024) cudaFuncSetAttribute(k_bf16p_rows<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem);
     int occ = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_bf16p_rows<M>, kBrThreads, rsmem) != cudaSuccess || occ < 1)
       occ = 1;

@@ -1003,7 +1003,7 @@ int attn_rows2h(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq,
   const size_t smem = sizeof(float) * 2 * (size_t)ls;
   if (hd > 256 || hd % 16 != 0 || nh % 2 != 0 || smem > 200 * 1024)
     return set_error(G4_ERR_UNSUPPORTED, "prefill attention (two heads per block): hd=%d nh=%d keys=%d", hd, nh, len_max);
-  if (smem > 48 * 1024) {
+  if (smem > 40 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(k_attn_rows2h, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "k_attn_rows2h: %s", cudaGetErrorString(e));
   }
@@ -1191,7 +1191,7 @@ int attn_rows_multi(int R, const uint16_t* Kc, const uint16_t* Vc, const float* 
   if (hd > 256 || hd % 16 != 0 || smem > 200 * 1024 || (R != 4 && R != 8))
     return set_error(G4_ERR_UNSUPPORTED, "prefill attention: R=%d hd=%d span=%d", R, hd, span);
   auto go = [&](auto kern) -> int {
-    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem > 40 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     return launch("k_attn_rows_multi", kern, dim3((Mrows + R - 1) / R, nh), dim3(256), smem, st, Kc, Vc, q, ldq, nh, hd,
                   pos0, Mrows, window, out, ldo, blk_fn, blk, span);
   };

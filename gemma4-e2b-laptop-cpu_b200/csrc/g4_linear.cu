@@ -868,7 +868,7 @@ static int launch_w4g32_t(const uint8_t* Wp, const uint16_t* S, const float* X, 
   const GemvGeom g = gemv_geom(K, CH, NB);
   const size_t smem = w4g32_smem(M, ROWS, g);
   if (smem > 227 * 1024) return set_error(G4_ERR_UNSUPPORTED, "g4_w4g32_gemm: %zu B of shared memory", smem);
-  if (smem > 48 * 1024) cudaFuncSetAttribute(k_w4g32<M, R, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > 40 * 1024) cudaFuncSetAttribute(k_w4g32<M, R, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (int rc_ = launch("k_w4g32", k_w4g32<M, R, WARPS>, dim3((N + ROWS - 1) / ROWS), dim3(WARPS * 32), smem, st, Wp, S, X, gsum, N, K, Y, ldy, CH, NB)) return rc_;
   return check_launch("k_w4g32");
 }
@@ -944,7 +944,7 @@ static int w4g32_gemm_impl(const uint8_t* Wp, const uint16_t* S, const float* X,
   if (M <= 4 && gsum == nullptr && N >= 16384 && w4g32_rows_smem(K) <= 100 * 1024 && !(rv && rv[0] == '0')) {
     const size_t smem = w4g32_rows_smem(K);
     auto go = [&](auto kern) {
-      if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (smem > 40 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       int occ = 0;
       if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kWrThreads, smem) != cudaSuccess || occ < 1) occ = 1;
       const int grid = std::min((N + kWrThreads - 1) / kWrThreads, sm_count() * occ);
@@ -998,7 +998,7 @@ static int launch_w4a8_t(const uint8_t* Wp, const uint16_t* S, const int8_t* q, 
   const GemvGeom g = gemv_geom(K, CH, NB);
   const size_t smem = w4a8_smem(M, g);
   if (smem > 227 * 1024) return set_error(G4_ERR_UNSUPPORTED, "g4_w4a8_gemm: %zu B of shared memory", smem);
-  if (smem > 48 * 1024) cudaFuncSetAttribute(k_w4a8<M, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > 40 * 1024) cudaFuncSetAttribute(k_w4a8<M, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (int rc_ = launch("k_w4a8", k_w4a8<M, WARPS>, dim3((N + kW4A8Rows - 1) / kW4A8Rows), dim3(WARPS * 32), smem, st, Wp, S, q, sx, sum, N, K, Y, ldy, CH, NB)) return rc_;
   return check_launch("k_w4a8");
 }
@@ -1012,7 +1012,7 @@ template <int M, int ROWS, int WARPS>
 static int launch_w4a8_all_t(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, const int32_t* sum,
                              int N, int K, float* Y, int ldy, int CH, cudaStream_t st) {
   const size_t smem = w4a8_all_smem(M, ROWS, K);
-  if (smem > 48 * 1024) cudaFuncSetAttribute(k_w4a8_all<M, ROWS, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > 40 * 1024) cudaFuncSetAttribute(k_w4a8_all<M, ROWS, WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (int rc_ = launch("k_w4a8_all", k_w4a8_all<M, ROWS, WARPS>, dim3((N + ROWS - 1) / ROWS), dim3(WARPS * 32), smem, st, Wp, S, q, sx, sum, N, K, Y, ldy, CH)) return rc_;
   return check_launch("k_w4a8_all");
 }
@@ -1028,7 +1028,7 @@ static int launch_w4a8_ring_t(const uint8_t* Wp, const uint16_t* S, const int8_t
                               int N, int K, float* Y, int ldy, int per_sm, cudaStream_t st) {
   const size_t smem = w4a8_ring_smem(M, ROWS, K, NS);
   auto kern = k_w4a8_ring<M, ROWS, WARPS, NS>;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > 40 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, WARPS * 32, smem) != cudaSuccess || occ < 1) occ = 1;
   const int nblk = (N + ROWS - 1) / ROWS;
