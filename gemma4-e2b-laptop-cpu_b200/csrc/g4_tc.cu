@@ -9,9 +9,10 @@
 // the epilogue warps run the fp32 chain group by group from tensor memory.  The chain keeps the
 // reference's order, so results are bit-identical to the GEMV path (g4_w4a8_gemm).
 //
-// CTA tile: 128 activation rows x 128 weight rows.  Warp roles: warps 0-7 epilogue (warp w reads
-// tensor-memory lanes 32*(w%4).. and columns 64*(w/4)..), warp 8 the TMA producer (one thread),
-// warp 9 the MMA issuer (one thread; the warp also allocates tensor memory).  A pipeline stage is
+// CTA tile: 128 activation rows x 128 weight rows.  Warp roles: warps 0-15 epilogue (warp w reads
+// tensor-memory lanes 32*(w%4).. and columns 32*(w/4)..; the epilogue is CUDA-core work, so it gets
+// as many warps as the register file allows), warp 16 the TMA producer (one thread), warp 17 the
+// MMA issuer (one thread; the warp also allocates tensor memory).  A pipeline stage is
 // 4 groups (128 bytes of K): the A and B tiles [128][128 B] by 2D tensor-map loads under the 128-byte
 // swizzle (the canonical K-major SW128 layout of the MMA's shared-memory descriptors), plus the 4
 // groups' activation scales (transposed [G][Mpad]) and weight scales (transposed [G][N]) by bulk
@@ -25,7 +26,12 @@
 
 namespace g4 {
 
-constexpr int kTcThreads = 320;
+// warps 0 .. kTcEpi-1: epilogue (4 per tensor-memory lane quarter, kTcCols columns each); then the
+// TMA producer warp and the MMA warp
+constexpr int kTcEpi = 16;
+constexpr int kTcCols = 128 * 4 / kTcEpi;            // columns per epilogue warp
+constexpr int kTcProd = kTcEpi, kTcMma = kTcEpi + 1;
+constexpr int kTcThreads = (kTcEpi + 2) * 32;
 constexpr int kTcNS = 4;
 constexpr int kTcTileA = 128 * 128;            // bytes
 constexpr int kTcTileB = 128 * 128;
@@ -98,14 +104,14 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
   const int n0 = blockIdx.x * 128, m0 = blockIdx.y * 128;
   const int G = K >> 5, nst = G >> 2;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kTcNS; ++i) { mbar_init(&sh.full[i], 1); mbar_init(&sh.empty[i], 1 + 8); }
-    for (int i = 0; i < 4; ++i) { mbar_init(&sh.accf[i], 1); mbar_init(&sh.acce[i], 8); }
+    for (int i = 0; i < kTcNS; ++i) { mbar_init(&sh.full[i], 1); mbar_init(&sh.empty[i], 1 + kTcEpi); }
+    for (int i = 0; i < 4; ++i) { mbar_init(&sh.accf[i], 1); mbar_init(&sh.acce[i], kTcEpi); }
     mbar_init(&sh.drain, 1);
     fence_mbar_init();
     sh.abort = 0;
     sh.issued = 0;
   }
-  if (warp == 9) {  // tensor memory: 512 columns = 4 buffers x 128
+  if (warp == kTcMma) {  // tensor memory: 512 columns = 4 buffers x 128
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem)), "r"(512)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -117,7 +123,7 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
   pdl_wait();
   pdl_trigger();
 
-  if (warp == 8) {
+  if (warp == kTcProd) {
     if (lane == 0) {  // producer
       int s = 0;
       for (; s < nst && !sh.abort; ++s) {
@@ -134,7 +140,7 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
         sh.issued = s + 1;
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == kTcMma) {
     if (lane == 0) {  // MMA issuer: per group one K = 32 MMA into buffer j, overwriting it
       for (int s = 0; s < nst; ++s) {
         const int st = s % kTcNS;
@@ -153,12 +159,12 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
       }
     }
   } else {
-    // epilogue: warp w -> tensor-memory lanes 32 (w % 4).. (tile rows), columns 64 (w / 4)..
+    // epilogue: warp w -> tensor-memory lanes 32 (w % 4).. (tile rows), columns kTcCols (w / 4)..
     const int q = warp & 3, h = warp >> 2;
     const int row = 32 * q + lane;
-    float2 acc[32];  // columns 2c, 2c+1: the chains advance in pairs through packed fp32 operations
+    float2 acc[kTcCols / 2];  // columns 2c, 2c+1: the chains advance in pairs through packed fp32 operations
 #pragma unroll
-    for (int c = 0; c < 32; ++c) acc[c] = make_float2(0.f, 0.f);
+    for (int c = 0; c < kTcCols / 2; ++c) acc[c] = make_float2(0.f, 0.f);
     bool ok = true;
     for (int s = 0; s < nst && ok; ++s) {
       const int st = s % kTcNS;
@@ -169,11 +175,11 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
         if (!tc_wait(&sh.accf[j], (uint32_t)(s & 1), sh)) { ok = false; break; }
         tc_fence_after();
         const float sx = sxs[j * 128 + row];
-        const uint16_t* sw = sws + j * 128 + 64 * h;
+        const uint16_t* sw = sws + j * 128 + kTcCols * h;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        for (int half = 0; half < kTcCols / 32; ++half) {
           uint32_t r[32];
-          tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + 128u * j + 64u * h + 32u * half, r);
+          tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + 128u * j + (uint32_t)(kTcCols * h) + 32u * half, r);
 #pragma unroll
           for (int c8 = 0; c8 < 4; ++c8) {
             const uint4 w8 = *reinterpret_cast<const uint4*>(sw + 32 * half + 8 * c8);
@@ -200,26 +206,26 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
     }
     const int m = m0 + row;
     if (ok && m < M) {
-      float* yr = Y + (size_t)m * ldy + n0 + 64 * h;
+      float* yr = Y + (size_t)m * ldy + n0 + kTcCols * h;
 #pragma unroll
-      for (int c = 0; c < 32; c += 2)
+      for (int c = 0; c < kTcCols / 2; c += 2)
         *reinterpret_cast<float4*>(yr + 2 * c) = make_float4(acc[c].x, acc[c].y, acc[c + 1].x, acc[c + 1].y);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (sh.abort) {  // a wait gave up: before the CTA frees anything, let its own copies and MMAs finish
-    if (warp == 8 && lane == 0) {
+    if (warp == kTcProd && lane == 0) {
       for (int k = sh.issued > kTcNS ? sh.issued - kTcNS : 0; k < sh.issued; ++k)
         if (!mbar_wait(&sh.full[k % kTcNS], (uint32_t)((k / kTcNS) & 1))) atomicOr(&g_dev_status, kStatusInflight);
-    } else if (warp == 9 && lane == 0) {
+    } else if (warp == kTcMma && lane == 0) {
       tc_commit(&sh.drain);
       if (!mbar_wait(&sh.drain, 0)) atomicOr(&g_dev_status, kStatusInflight);
     }
     tc_fence_before();
     __syncthreads();
   }
-  if (warp == 9) {
+  if (warp == kTcMma) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
   }
