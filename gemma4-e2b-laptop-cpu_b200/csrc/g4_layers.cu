@@ -735,31 +735,22 @@ __global__ void __launch_bounds__(256) k_attn_rows2(const uint16_t* __restrict__
       qa[i] = i < (hd >> 4) ? qh[2 * l + 16 * i] : 0.f;
       qb[i] = i < (hd >> 4) ? qh[2 * l + 1 + 16 * i] : 0.f;
     }
-    for (int pb = lo; pb <= pos; pb += 64) {  // two keys per lane group: both keys' loads in flight together
-      int p[2];
-      uint32_t w[2][16];
+    for (int pb = lo; pb <= pos; pb += 32) {
+      const int p = min(pb + kq, pos);
+      const uint32_t* kr = reinterpret_cast<const uint32_t*>(Kc + (size_t)p * hd) + l;
+      float aa = 0.f, ab = 0.f;
 #pragma unroll
-      for (int k2 = 0; k2 < 2; ++k2) {
-        p[k2] = min(pb + 32 * k2 + kq, pos);
-        const uint32_t* kr = reinterpret_cast<const uint32_t*>(Kc + (size_t)p[k2] * hd) + l;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) w[k2][i] = i < (hd >> 4) ? kr[8 * i] : 0u;
-      }
-#pragma unroll
-      for (int k2 = 0; k2 < 2; ++k2) {
-        float aa = 0.f, ab = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (i < (hd >> 4)) {
-            aa = fmaf(qa[i], __uint_as_float(w[k2][i] << 16), aa);
-            ab = fmaf(qb[i], __uint_as_float(w[k2][i] & 0xFFFF0000u), ab);
-          }
-        const float va = __fadd_rn(aa, __shfl_xor_sync(FULL, aa, 4)), vb = __fadd_rn(ab, __shfl_xor_sync(FULL, ab, 4));
-        const float pa = __fadd_rn(va, __shfl_xor_sync(FULL, va, 2)), pbv = __fadd_rn(vb, __shfl_xor_sync(FULL, vb, 2));
-        const float s1 = __fadd_rn(pa, pbv);
-        const float s = __fadd_rn(s1, __shfl_xor_sync(FULL, s1, 1));
-        if (l == 0 && pb + 32 * k2 + kq <= pos) sc[p[k2] - lo] = s;
-      }
+      for (int i = 0; i < 16; ++i)
+        if (i < (hd >> 4)) {
+          const uint32_t w = kr[8 * i];
+          aa = fmaf(qa[i], __uint_as_float(w << 16), aa);
+          ab = fmaf(qb[i], __uint_as_float(w & 0xFFFF0000u), ab);
+        }
+      const float va = __fadd_rn(aa, __shfl_xor_sync(FULL, aa, 4)), vb = __fadd_rn(ab, __shfl_xor_sync(FULL, ab, 4));
+      const float pa = __fadd_rn(va, __shfl_xor_sync(FULL, va, 2)), pbv = __fadd_rn(vb, __shfl_xor_sync(FULL, vb, 2));
+      const float s1 = __fadd_rn(pa, pbv);
+      const float s = __fadd_rn(s1, __shfl_xor_sync(FULL, s1, 1));
+      if (l == 0 && pb + kq <= pos) sc[p - lo] = s;
     }
   } else {
     const int hw = tid >> 4, c = tid & 15;
