@@ -952,7 +952,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "head", "screen", "prefill"])
-    ap.add_argument("--prefill-tc", type=int, default=1, choices=[0, 1, 2, 3, 4],
+    ap.add_argument("--prefill-tc", type=int, default=1, choices=[0, 1, 2, 3],
                     help="prefill: the engine's prefill_tc (1 tensor-core GEMMs + eight-lanes-per-key attention)")
     ap.add_argument("--prompt-tokens", type=int, default=0, help="prefill: prompt length (default 6,841)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

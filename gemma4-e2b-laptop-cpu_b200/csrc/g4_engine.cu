@@ -1031,10 +1031,6 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0, in
       // kPrefillRows rows of one head per block share each K and V load
       RCK(attn_rows_multi(kPrefillRows, Kc, Vc, e->pqkv, ld, d.NQ, d.HD, pos0, Mc, t.global ? 0 : d.WINDOW, len_max,
                           e->patt, QD, blk_fn, e->cfg.prefill_block, e->st));
-    } else if (e->cfg.prefill_tc == 4 && d.HD <= 256 && d.HD % 16 == 0 && d.NQ % 2 == 0 &&
-               sizeof(float) * 2 * (size_t)((len_max + 3) & ~3) <= 200 * 1024) {
-      RCK(attn_rows2h(Kc, Vc, e->pqkv, ld, d.NQ, d.HD, pos0, Mc, t.global ? 0 : d.WINDOW, len_max, e->patt, QD, blk_fn,
-                      e->cfg.prefill_block, e->st));
     } else if (e->cfg.prefill_tc == 1 && d.HD <= 256 && d.HD % 16 == 0) {
       if (sizeof(float) * len_max > 40 * 1024)
         cudaFuncSetAttribute(k_attn_rows2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sizeof(float) * len_max));

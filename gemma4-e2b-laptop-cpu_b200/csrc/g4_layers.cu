@@ -834,183 +834,6 @@ __global__ void __launch_bounds__(256) k_attn_rows2(const uint16_t* __restrict__
   }
 }
 
-// ---- k_attn_rows2 over two query heads of a row per block (they share the KV head, so each K and V
-// load serves both, halving the L2 traffic): the same chains, per head, as k_attn_rows2.  Per-row
-// blocks (variant 1) run their two heads one after the other with k_attn_rows2's variant-1 scores.
-// Dynamic shared memory 2 * ls floats, ls = len_max rounded up to a multiple of 4.
-__global__ void __launch_bounds__(256) k_attn_rows2h(const uint16_t* __restrict__ Kc, const uint16_t* __restrict__ Vc,
-                                                     const float* __restrict__ q, int ldq, int nh, int hd, int pos0,
-                                                     int window, float* __restrict__ out, int ldo, int blk_fn, int blk,
-                                                     int ls) {
-  pdl_wait();
-  pdl_trigger();
-  extern __shared__ __align__(16) float sc[];  // [2][ls]
-  __shared__ float s_red[2][8];
-  __shared__ float s_den[2];
-  const int m = blockIdx.x, h0 = 2 * blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
-  const int pos = pos0 + m, lo = window > 0 ? max(0, pos - (window - 1)) : 0, len = pos - lo + 1;
-  const int b0 = pos - (pos - blk_fn) % blk;
-  const int variant = (blk >= 4 && b0 + blk > 64) ? 0 : 1;
-  if (variant == 0) {
-    const int l = tid & 7, kq = tid >> 3;
-    float qa[2][16], qb[2][16];
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const float* qh = q + (size_t)m * ldq + (size_t)(h0 + hh) * hd;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        qa[hh][i] = i < (hd >> 4) ? qh[2 * l + 16 * i] : 0.f;
-        qb[hh][i] = i < (hd >> 4) ? qh[2 * l + 1 + 16 * i] : 0.f;
-      }
-    }
-    for (int pb = lo; pb <= pos; pb += 32) {
-      const int p = min(pb + kq, pos);
-      const uint32_t* kr = reinterpret_cast<const uint32_t*>(Kc + (size_t)p * hd) + l;
-      float aa[2] = {0.f, 0.f}, ab[2] = {0.f, 0.f};
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (i < (hd >> 4)) {
-          const uint32_t w = kr[8 * i];
-          const float klo = __uint_as_float(w << 16), khi = __uint_as_float(w & 0xFFFF0000u);
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            aa[hh] = fmaf(qa[hh][i], klo, aa[hh]);
-            ab[hh] = fmaf(qb[hh][i], khi, ab[hh]);
-          }
-        }
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const float va = __fadd_rn(aa[hh], __shfl_xor_sync(FULL, aa[hh], 4));
-        const float vb = __fadd_rn(ab[hh], __shfl_xor_sync(FULL, ab[hh], 4));
-        const float pa = __fadd_rn(va, __shfl_xor_sync(FULL, va, 2)), pbv = __fadd_rn(vb, __shfl_xor_sync(FULL, vb, 2));
-        const float s1 = __fadd_rn(pa, pbv);
-        const float s = __fadd_rn(s1, __shfl_xor_sync(FULL, s1, 1));
-        if (l == 0 && pb + kq <= pos) sc[hh * ls + p - lo] = s;
-      }
-    }
-  } else {
-    const int hw = tid >> 4, c = tid & 15;
-    for (int hh = 0; hh < 2; ++hh) {
-      const float* qh = q + (size_t)m * ldq + (size_t)(h0 + hh) * hd;
-      float qr[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) qr[i] = (c < 8 && i < (hd >> 3)) ? qh[c + 8 * i] : 0.f;
-      for (int pb = lo + (hw & ~1); pb <= pos; pb += 16) {
-        const int p = min(pb + (hw & 1), pos);
-        const uint16_t* kr = Kc + (size_t)p * hd;
-        float acc = 0.f;
-        if (c < 8) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < (hd >> 3)) acc = fmaf(qr[i], bf2f(kr[c + 8 * i]), acc);
-        }
-        const float s = hsum8_octet(acc);
-        if (c == 0 && pb + (hw & 1) <= pos) sc[hh * ls + p - lo] = s;
-      }
-    }
-  }
-  __syncthreads();
-  float mx[2] = {-1e30f, -1e30f};
-  for (int i = tid; i < len; i += blockDim.x) {
-    mx[0] = fmaxf(mx[0], sc[i]);
-    mx[1] = fmaxf(mx[1], sc[ls + i]);
-  }
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(FULL, mx[hh], o));
-    if ((tid & 31) == 0) s_red[hh][warp] = mx[hh];
-  }
-  __syncthreads();
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    mx[hh] = -1e30f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) mx[hh] = fmaxf(mx[hh], s_red[hh][i]);
-  }
-  for (int i = tid; i < len; i += blockDim.x) {
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const float d = __fsub_rn(sc[hh * ls + i], mx[hh]);
-      sc[hh * ls + i] = variant == 0 ? exp8(d) : exp_cr(d);
-    }
-  }
-  __syncthreads();
-  if (tid == 0 || tid == 32) {  // the in-order sums, one per head, in two warps
-    const float* w = sc + (tid >> 5) * ls;
-    float den = 0.f;
-    int i = 0;
-    for (; i + 8 <= len; i += 8) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = w[i + u];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) den = __fadd_rn(den, v[u]);
-    }
-    for (; i < len; ++i) den = __fadd_rn(den, w[i]);
-    s_den[tid >> 5] = den;
-  }
-  __syncthreads();
-  const float den[2] = {s_den[0], s_den[1]};
-  if (variant == 1) {
-    for (int i = tid; i < len; i += blockDim.x) {
-      sc[i] = __fdiv_rn(sc[i], den[0]);
-      sc[ls + i] = __fdiv_rn(sc[ls + i], den[1]);
-    }
-    __syncthreads();
-  }
-  const float inv[2] = {__fdiv_rn(1.0f, den[0]), __fdiv_rn(1.0f, den[1])};
-  for (int t2 = tid; 2 * t2 < hd; t2 += blockDim.x) {
-    float o[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-    const uint32_t* vp = reinterpret_cast<const uint32_t*>(Vc + (size_t)lo * hd) + t2;
-    const int hw2 = hd >> 1;
-    int p = 0;
-    for (; p + 8 <= len; p += 8) {
-      uint32_t v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = vp[(size_t)(p + u) * hw2];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const float4 wa = *reinterpret_cast<const float4*>(sc + hh * ls + p);
-        const float4 wb = *reinterpret_cast<const float4*>(sc + hh * ls + p + 4);
-        const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          o[hh][0] = fmaf(w[u], __uint_as_float(v[u] << 16), o[hh][0]);
-          o[hh][1] = fmaf(w[u], __uint_as_float(v[u] & 0xFFFF0000u), o[hh][1]);
-        }
-      }
-    }
-    for (; p < len; ++p) {
-      const uint32_t v = vp[(size_t)p * hw2];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        o[hh][0] = fmaf(sc[hh * ls + p], __uint_as_float(v << 16), o[hh][0]);
-        o[hh][1] = fmaf(sc[hh * ls + p], __uint_as_float(v & 0xFFFF0000u), o[hh][1]);
-      }
-    }
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      float* op = out + (size_t)m * ldo + (size_t)(h0 + hh) * hd + 2 * t2;
-      op[0] = variant == 0 ? r16(__fmul_rn(o[hh][0], inv[hh])) : r16(o[hh][0]);
-      op[1] = variant == 0 ? r16(__fmul_rn(o[hh][1], inv[hh])) : r16(o[hh][1]);
-    }
-  }
-}
-
-int attn_rows2h(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0, int Mrows,
-                int window, int len_max, float* out, int ldo, int blk_fn, int blk, cudaStream_t st) {
-  const int ls = (len_max + 3) & ~3;
-  const size_t smem = sizeof(float) * 2 * (size_t)ls;
-  if (hd > 256 || hd % 16 != 0 || nh % 2 != 0 || smem > 200 * 1024)
-    return set_error(G4_ERR_UNSUPPORTED, "prefill attention (two heads per block): hd=%d nh=%d keys=%d", hd, nh, len_max);
-  if (smem > 40 * 1024) {
-    const cudaError_t e = cudaFuncSetAttribute(k_attn_rows2h, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return set_error(G4_ERR_CUDA, "k_attn_rows2h: %s", cudaGetErrorString(e));
-  }
-  return launch("k_attn_rows2h", k_attn_rows2h, dim3(Mrows, nh / 2), dim3(256), smem, st, Kc, Vc, q, ldq, nh, hd, pos0,
-                window, out, ldo, blk_fn, blk, ls);
-}
-
 // ---- prefill attention, R consecutive query rows of one head per block.  The rows of a prefill
 // chunk share their keys (global layers: 0..pos; sliding: a window that moves by one per row), so a
 // block takes rows m0..m0+R-1 (positions pos0+m0..) of head h over the union of their key ranges

@@ -39,12 +39,6 @@ __global__ void k_attn_rows(const uint16_t* Kc, const uint16_t* Vc, const float*
 // k_attn_rows with variant < 0.
 __global__ void k_attn_rows2(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0,
                              int window, float* out, int ldo, int blk_fn, int blk);
-// k_attn_rows2 over two query heads of a row per block (grid (M, nh / 2), dynamic shared memory
-// 2 * ls floats, ls = len_max rounded up to a multiple of 4).
-__global__ void k_attn_rows2h(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0,
-                              int window, float* out, int ldo, int blk_fn, int blk, int ls);
-int attn_rows2h(const uint16_t* Kc, const uint16_t* Vc, const float* q, int ldq, int nh, int hd, int pos0, int Mrows,
-                int window, int len_max, float* out, int ldo, int blk_fn, int blk, cudaStream_t st);
 // Prefill attention for rows of full prefill blocks, R consecutive rows of one head per block (grid
 // (ceil(Mrows / R), nh), 256 threads, hd <= 256, dynamic shared memory R * span floats with span =
 // len_max + R - 1): the values of k_attn_rows with variant < 0.

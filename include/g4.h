@@ -253,8 +253,7 @@ typedef struct {
   int prefill_tc;                    /* prefill the prompt's full blocks with the tensor-core W4A8
                                         GEMM (tcgen05) over up to 2,048 rows at a time (1: attention
                                         with one query row of a head per block, measured fastest; 3:
-                                        4 rows of a head per block; 2: 4 heads of a row per block; 4:
-                                        2 heads of a row per block), or
+                                        4 rows of a head per block; 2: 4 heads of a row per block), or
                                         block by block through the GEMV path (0); same values in all
                                         four */
   int slots;                         /* ENGINE_SLOTS (1): conversations kept for the prefix cache (the

@@ -272,7 +272,7 @@ def test_tensor_core_prefill_matches_block_prefill(cfg):
     vocab = cfg.get("vocab", 262144)
     prompt = make_prompt(11, 777, vocab=vocab)
     outs = []
-    for tc in (1, 3, 4, 0):
+    for tc in (1, 3, 0):
         eng = g4.Engine(g4.engine_config(**cfg, prefill_tc=tc))
         try:
             first = eng.prefill(prompt)
