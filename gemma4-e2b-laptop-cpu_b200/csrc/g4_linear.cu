@@ -478,15 +478,6 @@ __global__ void k_w4a8_quant(const float* __restrict__ X, int MG, int G, int8_t*
   (void)G;
 }
 
-// A group dot as a float without the conversion pipe when |a| < 2^22 (always, for finite
-// activations: |a| <= 32 x 8 x 128): 1.5 x 2^23 + a is exact in the mantissa and so is the
-// subtraction.  A group sum of the quantisation of a non-finite row can push a out of range; that
-// case takes the ordinary conversion.
-__device__ __forceinline__ float i32_to_f32(int a) {
-  if ((unsigned)a + (1u << 22) < (1u << 23)) return __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f);
-  return (float)a;
-}
-
 // ------------------------------------------------------------------------------ W4A8 GEMV
 // Each CTA owns 8 weight rows streamed into shared memory as in k_w4g32.  Per chunk, phase 1
 // has each thread take one group for all 8 rows (its int8 activations, scale and sum are loaded
@@ -574,7 +565,7 @@ k_w4a8(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const int
           acc = __dp4a((int)hi[1], qb[m].y, acc);
           acc = __dp4a((int)hi[2], qb[m].z, acc);
           acc = __dp4a((int)hi[3], qb[m].w, acc);
-          ac[(size_t)(r * M + m) * acs + gl] = make_float2(i32_to_f32(acc), __fmul_rn(sw, sxm[m]));
+          ac[(size_t)(r * M + m) * acs + gl] = make_float2((float)acc, __fmul_rn(sw, sxm[m]));
         }
       }
     }
@@ -679,7 +670,7 @@ k_w4a8_all(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, const
           acc = __dp4a((int)hi[1], qb[m].y, acc);
           acc = __dp4a((int)hi[2], qb[m].z, acc);
           acc = __dp4a((int)hi[3], qb[m].w, acc);
-          ac[(size_t)(r * M + m) * acs + g] = make_float2(i32_to_f32(acc), __fmul_rn(sw, sxm[m]));
+          ac[(size_t)(r * M + m) * acs + g] = make_float2((float)acc, __fmul_rn(sw, sxm[m]));
         }
       }
     }
@@ -789,7 +780,7 @@ k_w4a8_ring(const uint8_t* __restrict__ Wp, const uint16_t* __restrict__ S, cons
           acc = __dp4a((int)hi[1], qb[m].y, acc);
           acc = __dp4a((int)hi[2], qb[m].z, acc);
           acc = __dp4a((int)hi[3], qb[m].w, acc);
-          ac[(size_t)(r * M + m) * acs + g] = make_float2(i32_to_f32(acc), __fmul_rn(sw, sxm[m]));
+          ac[(size_t)(r * M + m) * acs + g] = make_float2((float)acc, __fmul_rn(sw, sxm[m]));
         }
       }
     }
