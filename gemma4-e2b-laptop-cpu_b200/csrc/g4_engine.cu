@@ -33,7 +33,7 @@ struct Lin {  // one int4 W4G32 matrix in device layout
 };
 struct TcLin {  // the tensor-core operands of a Lin: s8 weights [N][K] and scales transposed [K/32][N]
   int8_t* w8 = nullptr;
-  uint16_t* swT = nullptr;
+  float* swT = nullptr;
 };
 struct TLayer {
   Lin qkv, o, gu, down;

@@ -36,7 +36,7 @@ constexpr int kTcNS = 4;
 constexpr int kTcTileA = 128 * 128;            // bytes
 constexpr int kTcTileB = 128 * 128;
 constexpr int kTcSx = 4 * 128 * 4;             // 4 groups x 128 rows fp32
-constexpr int kTcSw = 4 * 128 * 2;             // 4 groups x 128 cols bf16
+constexpr int kTcSw = 4 * 128 * 4;             // 4 groups x 128 cols, the bf16 scales as fp32
 constexpr int kTcStage = 36 * 1024;            // A + B + sx + sw, rounded to 1 KB (swizzle atoms)
 constexpr int kTcSmem = kTcNS * kTcStage + 1024;
 
@@ -96,7 +96,7 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, TcShared
 
 __global__ void __launch_bounds__(kTcThreads, 1)
 k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const float* __restrict__ sxT,
-          int Mpad, const uint16_t* __restrict__ swT, int M, int N, int K, float* __restrict__ Y, int ldy) {
+          int Mpad, const float* __restrict__ swT, int M, int N, int K, float* __restrict__ Y, int ldy) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __shared__ TcShared sh;
   uint8_t* stages = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // 1 KB aligned (swizzle atoms)
@@ -135,7 +135,7 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
         tma_load_2d(sb + kTcTileA, &tb, s * 128, n0, &sh.full[st]);
         for (int j = 0; j < 4; ++j) {
           bulk_g2s(sb + kTcTileA + kTcTileB + j * 512, sxT + (size_t)(4 * s + j) * Mpad + m0, 512, &sh.full[st]);
-          bulk_g2s(sb + kTcTileA + kTcTileB + kTcSx + j * 256, swT + (size_t)(4 * s + j) * N + n0, 256, &sh.full[st]);
+          bulk_g2s(sb + kTcTileA + kTcTileB + kTcSx + j * 512, swT + (size_t)(4 * s + j) * N + n0, 512, &sh.full[st]);
         }
         sh.issued = s + 1;
       }
@@ -170,20 +170,22 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
       const int st = s % kTcNS;
       const uint8_t* sb = stages + (size_t)st * kTcStage;
       const float* sxs = reinterpret_cast<const float*>(sb + kTcTileA + kTcTileB);
-      const uint16_t* sws = reinterpret_cast<const uint16_t*>(sb + kTcTileA + kTcTileB + kTcSx);
+      const float* sws = reinterpret_cast<const float*>(sb + kTcTileA + kTcTileB + kTcSx);
       for (int j = 0; j < 4; ++j) {
         if (!tc_wait(&sh.accf[j], (uint32_t)(s & 1), sh)) { ok = false; break; }
         tc_fence_after();
         const float sx = sxs[j * 128 + row];
-        const uint16_t* sw = sws + j * 128 + kTcCols * h;
+        const float* sw = sws + j * 128 + kTcCols * h;
 #pragma unroll
         for (int half = 0; half < kTcCols / 32; ++half) {
           uint32_t r[32];
           tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + 128u * j + (uint32_t)(kTcCols * h) + 32u * half, r);
 #pragma unroll
           for (int c8 = 0; c8 < 4; ++c8) {
-            const uint4 w8 = *reinterpret_cast<const uint4*>(sw + 32 * half + 8 * c8);
-            const uint32_t wv[4] = {w8.x, w8.y, w8.z, w8.w};
+            const float4 wlo = *reinterpret_cast<const float4*>(sw + 32 * half + 8 * c8);
+            const float4 whi = *reinterpret_cast<const float4*>(sw + 32 * half + 8 * c8 + 4);
+            const float2 wv[4] = {make_float2(wlo.x, wlo.y), make_float2(wlo.z, wlo.w), make_float2(whi.x, whi.y),
+                                  make_float2(whi.z, whi.w)};
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               const int c2 = 16 * half + 4 * c8 + v;  // columns 2 c2, 2 c2 + 1
@@ -192,8 +194,7 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
               const float2 a = __fadd2_rn(make_float2(__int_as_float((int)r[8 * c8 + 2 * v] + 0x4B400000),
                                                       __int_as_float((int)r[8 * c8 + 2 * v + 1] + 0x4B400000)),
                                           make_float2(-12582912.0f, -12582912.0f));
-              const float2 wsc = make_float2(__uint_as_float(wv[v] << 16), __uint_as_float(wv[v] & 0xFFFF0000u));
-              acc[c2] = __ffma2_rn(a, __fmul2_rn(wsc, make_float2(sx, sx)), acc[c2]);
+              acc[c2] = __ffma2_rn(a, __fmul2_rn(wv[v], make_float2(sx, sx)), acc[c2]);
             }
           }
         }
@@ -251,12 +252,13 @@ __global__ void k_w8_expand(const uint8_t* __restrict__ Wp, long long groups, in
   dst[1] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
 }
 
-// [R][C] -> [C][ldo] transposes (rows past R are left as they are: zeroed by the caller).
-__global__ void k_transpose_u16(const uint16_t* __restrict__ in, int R, int C, uint16_t* __restrict__ out, int ldo) {
+// [R][C] -> [C][ldo] transposes (rows past R are left as they are: zeroed by the caller); the bf16
+// weight scales are widened to fp32 on the way (exact), so the epilogue reads them as floats.
+__global__ void k_transpose_bf2f(const uint16_t* __restrict__ in, int R, int C, float* __restrict__ out, int ldo) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)R * C) return;
   const int r = (int)(i / C), c = (int)(i % C);
-  out[(size_t)c * ldo + r] = in[i];
+  out[(size_t)c * ldo + r] = __uint_as_float((uint32_t)in[i] << 16);
 }
 __global__ void k_transpose_f32(const float* __restrict__ in, int R, int C, float* __restrict__ out, int ldo) {
   pdl_wait();
@@ -275,12 +277,12 @@ using namespace g4;
 
 namespace g4 {
 
-int tc_expand_weights(const uint8_t* Wp, const uint16_t* S, int N, int K, int8_t* W8, uint16_t* swT, cudaStream_t st) {
+int tc_expand_weights(const uint8_t* Wp, const uint16_t* S, int N, int K, int8_t* W8, float* swT, cudaStream_t st) {
   if (N % 128 != 0 || K % 128 != 0) return set_error(G4_ERR_UNSUPPORTED, "tensor-core W4A8: N and K must be multiples of 128");
   const long long groups = (long long)N * (K / 32);
   k_w8_expand<<<(unsigned)((groups + 255) / 256), 256, 0, st>>>(Wp, groups, W8);
   const long long ns = (long long)N * (K / 32);
-  k_transpose_u16<<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(S, N, K / 32, swT, N);
+  k_transpose_bf2f<<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(S, N, K / 32, swT, N);
   return check_launch("tc_expand_weights");
 }
 
@@ -310,7 +312,7 @@ static bool tc_tmap(const void* base, uint64_t K, uint64_t rows, CUtensorMap* ou
   return true;
 }
 
-int tc_gemm(const int8_t* A, int M, int K, const float* sxT, int Mpad, const int8_t* W8, const uint16_t* swT, int N, float* Y,
+int tc_gemm(const int8_t* A, int M, int K, const float* sxT, int Mpad, const int8_t* W8, const float* swT, int N, float* Y,
             int ldy, cudaStream_t st) {
   if (M < 1 || N % 128 != 0 || K % 128 != 0 || Mpad < (M + 127) / 128 * 128 || ldy < N)
     return set_error(G4_ERR_UNSUPPORTED, "tensor-core W4A8: unsupported shape M=%d N=%d K=%d", M, N, K);
@@ -334,7 +336,7 @@ int tc_gemm(const int8_t* A, int M, int K, const float* sxT, int Mpad, const int
 
 size_t g4_w4a8_gemm_tc_ws_bytes(int M, int N, int K) {
   const size_t Mpad = (size_t)(M + 127) / 128 * 128;
-  return (size_t)N * K + 256 + (size_t)(K / 32) * N * 2 + 256 + (size_t)(K / 32) * Mpad * 4 + 256;
+  return (size_t)N * K + 256 + (size_t)(K / 32) * N * 4 + 256 + (size_t)(K / 32) * Mpad * 4 + 256;
 }
 
 extern "C" int g4_w4a8_gemm_tc(const uint8_t* Wp, const uint16_t* S, const int8_t* q, const float* sx, int M, int N, int K,
@@ -348,8 +350,8 @@ extern "C" int g4_w4a8_gemm_tc(const uint8_t* Wp, const uint16_t* S, const int8_
   uint8_t* p = static_cast<uint8_t*>(ws);
   int8_t* W8 = reinterpret_cast<int8_t*>(p);
   p += ((size_t)N * K + 255) / 256 * 256;
-  uint16_t* swT = reinterpret_cast<uint16_t*>(p);
-  p += ((size_t)G * N * 2 + 255) / 256 * 256;
+  float* swT = reinterpret_cast<float*>(p);
+  p += ((size_t)G * N * 4 + 255) / 256 * 256;
   float* sxT = reinterpret_cast<float*>(p);
   if (int rc = tc_expand_weights(Wp, S, N, K, W8, swT, st)) return rc;
   if (int rc = tc_transpose_sx(sx, M, G, sxT, Mpad, st)) return rc;
