@@ -888,7 +888,7 @@ def cpu_decode_reference(state=None, seconds=25.0, rounds_min=16, rounds_max=64,
     round, which the screen falls back to on this model anyway."""
     from oracle_lib import OracleModel, e2e_config, make_prompt, oracle, reference
     threads = host_threads()
-    reference(threads)  # the reference's pool, all host threads
+    reference(min(threads, 16))  # the reference's pool: all host threads, at most the 16 it has slots for (:78, :145)
     oracle().or_set_threads(threads)
     om = OracleModel(e2e_config())
     kind = "reference" if om.use_reference_kernels() else "port"
@@ -923,7 +923,7 @@ def cpu_gemv_reference(seconds=10.0, max_calls=2000):
     """The reference's own W4G32 path (lin_task over its thread pool) on the host's cores, over
     rotating weight copies larger than the last-level cache."""
     from oracle_lib import ptr, reference
-    ref = reference(host_threads())
+    ref = reference(min(host_threads(), 16))  # the reference's pool holds at most 16 threads (:78)
     if ref is None:
         return None
     W, S, X = gemv_inputs(0)

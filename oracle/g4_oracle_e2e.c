@@ -51,6 +51,9 @@ typedef struct {
                const int* lo, int kmin, int kmax, float* out);
   void* (*head_prepare)(const uint16_t* E, int N, int K, const uint8_t* cb8);
   void (*head_run)(void* h, const float* X, int M, float* Y);
+  /* the tiled prefill attention (variant 0) of a whole block; may be NULL */
+  void (*attn_tile)(const uint16_t* Kc, const uint16_t* Vc, int hd, int sliding, const float* q, int qstride, int pos0,
+                    int M, float* att);
 } or_e2e_hooks;
 typedef struct { Lin qkv, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff, *qn, *kn; int global; } TLayer;
 typedef struct { Lin q, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff, *qn; int global; } DLayer;
@@ -353,6 +356,9 @@ static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf
       free(q);
     } else {
       const int variant = (M >= 4 && pos0 + M > 64) ? 0 : 1;
+      if (variant == 0 && m->hk.attn_tile) {
+        m->hk.attn_tile(Kc, Vc, hd, t->global ? 0 : 1, qkv, ld, pos0, M, att);
+      } else
 #pragma omp parallel for schedule(dynamic)
       for (int r = 0; r < M; ++r) {
         const int pos = pos0 + r, lo = t->global ? 0 : (pos - 511 > 0 ? pos - 511 : 0);

@@ -97,6 +97,25 @@ void ref_attn_splitkv(const uint16_t* Kc, const uint16_t* Vc, int hd, int nh, in
   attn_merge(aa, POOL.active_count(), outp, nullptr);
 }
 
+// The tiled prefill attention of a block of M rows at positions pos0.. (fwd's TILED branch,
+// :1328-1336): attn_tile (:1061-1083) over tiles of QB rows x 8 heads on the pool's threads.  q rows
+// (already normed and rotated) qstride apart, att rows 8*hd apart, bf16-rounded.
+struct TileArg {
+  const uint16_t *Kc, *Vc;
+  int hd, sliding, qstride, pos0, M, ntiles;
+  const float* q;
+  float* att;
+};
+static void tile_task(void* p, int tid, int T) {
+  const TileArg* a = static_cast<const TileArg*>(p);
+  for (int t = tid; t < a->ntiles; t += T) attn_tile(a->Kc, a->Vc, a->hd, a->sliding != 0, a->q, a->qstride, a->pos0, a->M, a->att, t, tid);
+}
+void ref_attn_tile_run(const uint16_t* Kc, const uint16_t* Vc, int hd, int sliding, const float* q, int qstride, int pos0,
+                       int M, float* att) {
+  TileArg a{Kc, Vc, hd, sliding, qstride, pos0, M, (M + QB - 1) / QB, q, att};
+  POOL.run(tile_task, &a);
+}
+
 // The reference screen_task (:460-538) at its hard-coded K=1536, N=262144, then eval_row's
 // threshold filter (:1453-1467).  Writes the per-row L, the filtered survivors in list order and
 // their count (or -1 when a per-thread list overflowed).

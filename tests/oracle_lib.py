@@ -80,6 +80,7 @@ _SIGS_REF = {
     "ref_lin_run": (None, [_P, _P, _I, _P, _I]),
     "ref_head_prepare": (_P, [_P, _I, _I, _P]),
     "ref_head_run": (None, [_P, _P, _I, _P]),
+    "ref_attn_tile_run": (None, [_P, _P, _I, _I, _P, _I, _I, _I, _P]),
     "ref_exp8": (None, [_P, _I, _P]),
 }
 
@@ -360,9 +361,9 @@ class OracleModel:
         ref = reference()
         if ref is None:
             return False
-        hooks = (ctypes.c_void_p * 5)(*[ctypes.cast(getattr(ref, n), ctypes.c_void_p).value for n in
+        hooks = (ctypes.c_void_p * 6)(*[ctypes.cast(getattr(ref, n), ctypes.c_void_p).value for n in
                                         ("ref_lin_prepare", "ref_lin_run", "ref_attn_splitkv", "ref_head_prepare",
-                                         "ref_head_run")])
+                                         "ref_head_run", "ref_attn_tile_run")])
         self._hooks = hooks
         return oracle().or_e2e_set_hooks(self.h, ctypes.cast(hooks, ctypes.c_void_p)) == 0
 
