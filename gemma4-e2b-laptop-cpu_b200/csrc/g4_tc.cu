@@ -59,14 +59,27 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 // Instruction descriptor: D s32, A and B s8, both K-major, M = 128, N = 128.
 constexpr uint32_t kTcIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
 
-__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db) {
+// D (+)= A x B: accumulate = 1 adds the products to what tensor memory holds.
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
       :
-      : "r"(tmem_d), "l"(da), "l"(db), "r"(kTcIdesc), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+      : "r"(tmem_d), "l"(da), "l"(db), "r"(kTcIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
+// The int32 word 0x4B400000 (the float 1.5 x 2^23) into 32 columns of this warp's tensor-memory lanes,
+// as four 8-column stores (one 8-register source range instead of 32 registers holding the bias).
+constexpr uint32_t kTcBias = 0x4B400000u;
+__device__ __forceinline__ void tc_st_bias32(uint32_t taddr) {
+  const uint32_t b = kTcBias;
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr + 8u * k),
+                 "r"(b)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -141,7 +154,7 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
       }
     }
   } else if (warp == kTcMma) {
-    if (lane == 0) {  // MMA issuer: per group one K = 32 MMA into buffer j, overwriting it
+    if (lane == 0) {  // MMA issuer: per group one K = 32 MMA added into buffer j (which holds the bias)
       for (int s = 0; s < nst; ++s) {
         const int st = s % kTcNS;
         if (!tc_wait(&sh.full[st], (uint32_t)((s / kTcNS) & 1), sh)) break;
@@ -149,9 +162,11 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
         const uint32_t a0 = smem_u32(stages + (size_t)st * kTcStage), b0 = a0 + kTcTileA;
         bool ok = true;
         for (int j = 0; j < 4; ++j) {
-          if (s > 0 && !tc_wait(&sh.acce[j], (uint32_t)((s - 1) & 1), sh)) { ok = false; break; }
+          // phase s of acce[j]: the epilogue has read buffer j's previous dots and stored the bias again
+          // (phase 0: the first bias)
+          if (!tc_wait(&sh.acce[j], (uint32_t)(s & 1), sh)) { ok = false; break; }
           tc_fence_after();
-          tc_mma(tmem + 128u * j, sw128_desc(a0 + 32u * j), sw128_desc(b0 + 32u * j));
+          tc_mma(tmem + 128u * j, sw128_desc(a0 + 32u * j), sw128_desc(b0 + 32u * j), 1u);
           tc_commit(&sh.accf[j]);
         }
         if (!ok) break;
@@ -165,6 +180,19 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
     float2 acc[kTcCols / 2];  // columns 2c, 2c+1: the chains advance in pairs through packed fp32 operations
 #pragma unroll
     for (int c = 0; c < kTcCols / 2; ++c) acc[c] = make_float2(0.f, 0.f);
+    // every buffer starts at the bias 1.5 x 2^23 (as an int32 word), which the MMAs add the group's
+    // dots to, so the read-back word is the float 1.5 x 2^23 + a32 (exact: |a32| <= 32 x 8 x 128)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int half = 0; half < kTcCols / 32; ++half)
+        tc_st_bias32(tmem + ((uint32_t)(32 * q) << 16) + 128u * j + (uint32_t)(kTcCols * h) + 32u * half);
+    }
+    tc_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0)
+      for (int j = 0; j < 4; ++j) arrive(&sh.acce[j]);
     bool ok = true;
     for (int s = 0; s < nst && ok; ++s) {
       const int st = s % kTcNS;
@@ -179,7 +207,8 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
 #pragma unroll
         for (int half = 0; half < kTcCols / 32; ++half) {
           uint32_t r[32];
-          tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + 128u * j + (uint32_t)(kTcCols * h) + 32u * half, r);
+          const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + 128u * j + (uint32_t)(kTcCols * h) + 32u * half;
+          tc_ld32(ta, r);
 #pragma unroll
           for (int c8 = 0; c8 < 4; ++c8) {
             const float4 wlo = *reinterpret_cast<const float4*>(sw + 32 * half + 8 * c8);
@@ -189,15 +218,16 @@ k_w4a8_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               const int c2 = 16 * half + 4 * c8 + v;  // columns 2 c2, 2 c2 + 1
-              // the group's integer dots as floats without the conversion pipe: |a32| <= 32 x 8 x 128
-              // < 2^22, so 1.5 x 2^23 + a32 is exact in the mantissa and the subtraction is exact
-              const float2 a = __fadd2_rn(make_float2(__int_as_float((int)r[8 * c8 + 2 * v] + 0x4B400000),
-                                                      __int_as_float((int)r[8 * c8 + 2 * v + 1] + 0x4B400000)),
+              // the group's integer dots as floats: 1.5 x 2^23 + a32 was formed by the MMA (exact in
+              // the mantissa, |a32| < 2^22), so the subtraction is exact
+              const float2 a = __fadd2_rn(make_float2(__uint_as_float(r[8 * c8 + 2 * v]), __uint_as_float(r[8 * c8 + 2 * v + 1])),
                                           make_float2(-12582912.0f, -12582912.0f));
               acc[c2] = __ffma2_rn(a, __fmul2_rn(wv[v], make_float2(sx, sx)), acc[c2]);
             }
           }
+          tc_st_bias32(ta);  // the bias back for the next stage's MMA (completed before acce[j] below)
         }
+        tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) arrive(&sh.acce[j]);
