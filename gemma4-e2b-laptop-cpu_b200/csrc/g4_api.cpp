@@ -54,7 +54,7 @@ int check_launch(const char* what) {
 }  // namespace g4
 
 extern "C" const char* g4_last_error(void) { return g4::g_msg; }
-extern "C" int g4_abi_version(void) { return 6; }
+extern "C" int g4_abi_version(void) { return 7; }
 
 namespace g4 {
 unsigned status_read_linear(bool reset);

@@ -4,6 +4,7 @@
 // its fwd lambda (:1256-1502) and the draft step its draft_step (:1534-1563), both at the
 // synthetic dimensions.  Every kernel launch goes to the engine's stream.
 #include "g4_api.h"
+#include "g4_ckpt.h"
 #include "g4_layers.cuh"
 #include "g4_stream.h"
 #include "g4_tc.h"
@@ -40,6 +41,7 @@ struct TLayer {
   TcLin tqkv, to, tgu, tdown;
   float *in_ln, *post_attn, *pre_ff, *post_ff, *qn, *kn;
   bool global;
+  float scalar = 1.0f;  // layer_scalar (:1389-1404): 1 for the synthetic model, a checkpoint's value otherwise
 };
 struct DLayerW {
   Lin q, o, gu, down;
@@ -388,6 +390,23 @@ static int gen_lin(g4_engine* e, Lin& lin, const std::vector<std::pair<uint64_t,
   RCK(g4_w4_pack(tmp, N, K, lin.w, e->st));
   return check_launch("gen_lin");
 }
+// The same from a checkpoint: the reference-layout bytes and bf16 scales of each part, then packed.
+static int ck_lin(g4_engine* e, const g4_checkpoint* ck, Lin& lin, const std::vector<std::pair<std::string, int>>& parts,
+                  int K, uint8_t* tmp) {
+  int N = 0;
+  for (auto& p : parts) N += p.second;
+  lin.N = N; lin.K = K;
+  RCK(ealloc_t(e, &lin.w, (size_t)N * K / 2));
+  RCK(ealloc_t(e, &lin.s, (size_t)N * K / 32));
+  if (cudaStreamSynchronize(e->st) != cudaSuccess) return set_error(G4_ERR_CUDA, "checkpoint: stream");  // tmp is free
+  RCK(ck_load_lin(ck, parts, K, tmp, lin.s));
+  RCK(g4_w4_pack(tmp, N, K, lin.w, e->st));
+  return check_launch("ck_lin");
+}
+static int ck_norm(g4_engine* e, const g4_checkpoint* ck, float** p, const std::string& name, int n) {
+  RCK(ealloc_t(e, p, n));
+  return ck_load_vec(ck, name, n, *p);
+}
 static int gen_norm(g4_engine* e, float** p, uint64_t id, int n, float mul) {
   RCK(ealloc_t(e, p, n));
   k_gen_norm<<<gridfor(n), 256, 0, e->st>>>(e->cfg.seed, id, n, mul, *p);
@@ -396,7 +415,8 @@ static int gen_norm(g4_engine* e, float** p, uint64_t id, int n, float mul) {
 
 // Engine creation; with share, the weights (target, drafter, head copies, screen, tensor-core
 // operands, RoPE tables) are the other engine's and only the per-stream state is allocated.
-static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_engine** out) {
+static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_engine** out,
+                       const g4_checkpoint* ck = nullptr) {
   if (!cfg || !out) return set_error(G4_ERR_INVALID, "g4_engine_create: null pointer");
   const g4_engine_config c = *cfg;
   G4_REQUIRE(c.hidden % 256 == 0 && c.hidden >= 256 && c.hidden <= 2048 && c.mlp % 256 == 0 && c.n_layers >= 1 && c.vocab % 128 == 0 &&
@@ -433,7 +453,24 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
                                               (size_t)QD * H / 2, (size_t)d.DCENT * H / 2, (size_t)H * 2 * H / 2});
   if (ealloc_t(e, &tmp, tmp_bytes)) return fail(G4_ERR_CUDA);
   e->L.resize(d.NL);
-  for (int l = 0; l < d.NL; ++l) {
+  for (int l = 0; l < d.NL && ck; ++l) {  // target weights from a checkpoint (q4 / bfvec, :1222-1229)
+    TLayer& t = e->L[l];
+    t.global = d.global_layer(l);
+    int rc = ck_lin(e, ck, t.qkv, {{ck_layer(l, "self_attn.q_proj"), QD}, {ck_layer(l, "self_attn.k_proj"), d.HD},
+                                   {ck_layer(l, "self_attn.v_proj"), d.HD}}, H, tmp);
+    if (!rc) rc = ck_lin(e, ck, t.o, {{ck_layer(l, "self_attn.o_proj"), H}}, QD, tmp);
+    if (!rc) rc = ck_lin(e, ck, t.gu, {{ck_layer(l, "mlp.gate_proj"), I}, {ck_layer(l, "mlp.up_proj"), I}}, H, tmp);
+    if (!rc) rc = ck_lin(e, ck, t.down, {{ck_layer(l, "mlp.down_proj"), H}}, I, tmp);
+    if (!rc) rc = ck_norm(e, ck, &t.in_ln, ck_layer(l, "input_layernorm.weight"), H);
+    if (!rc) rc = ck_norm(e, ck, &t.post_attn, ck_layer(l, "post_attention_layernorm.weight"), H);
+    if (!rc) rc = ck_norm(e, ck, &t.pre_ff, ck_layer(l, "pre_feedforward_layernorm.weight"), H);
+    if (!rc) rc = ck_norm(e, ck, &t.post_ff, ck_layer(l, "post_feedforward_layernorm.weight"), H);
+    if (!rc) rc = ck_norm(e, ck, &t.qn, ck_layer(l, "self_attn.q_norm.weight"), d.HD);
+    if (!rc) rc = ck_norm(e, ck, &t.kn, ck_layer(l, "self_attn.k_norm.weight"), d.HD);
+    if (!rc) rc = ck_load_scalar(ck, ck_layer(l, "layer_scalar"), &t.scalar);
+    if (rc) return fail(rc);
+  }
+  for (int l = 0; l < d.NL && !ck; ++l) {
     TLayer& t = e->L[l];
     t.global = d.global_layer(l);
     int rc = gen_lin(e, t.qkv, {{layer_id(l, T_Q), QD}, {layer_id(l, T_K), d.HD}, {layer_id(l, T_V), d.HD}}, H, tmp);
@@ -448,11 +485,15 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
     if (!rc) rc = gen_norm(e, &t.kn, layer_id(l, T_KN), d.HD, 1.f);
     if (rc) return fail(rc);
   }
-  if (gen_norm(e, &e->fnorm, T_FNORM, H, 1.f)) return fail(G4_ERR_CUDA);
+  if (ck ? ck_norm(e, ck, &e->fnorm, "norm.weight", H) : gen_norm(e, &e->fnorm, T_FNORM, H, 1.f)) return fail(G4_ERR_CUDA);
   // embedding / tied head, packed exact head, screen
   const long long EV = (long long)d.V * H;
   if (ealloc_t(e, &e->E, (size_t)EV)) return fail(G4_ERR_CUDA);
-  k_gen_embed<<<gridfor(EV), 256, 0, e->st>>>(c.seed, EV, e->E);
+  if (ck) {
+    if (int rc = ck_load_bf16(ck, "embed_tokens.weight", d.V, H, e->E)) return fail(rc);
+  } else {
+    k_gen_embed<<<gridfor(EV), 256, 0, e->st>>>(c.seed, EV, e->E);
+  }
   {
     void* ws = nullptr;
     if (ealloc(e, &ws, std::max<size_t>(2048, 8 * (size_t)d.V))) return fail(G4_ERR_CUDA);
@@ -605,6 +646,13 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
 
 extern "C" int g4_engine_create(const g4_engine_config* cfg, g4_engine** out) { return create_impl(cfg, nullptr, out); }
 
+extern "C" int g4_engine_create_from_checkpoint(const g4_engine_config* cfg, const g4_checkpoint* ck, g4_engine** out) {
+  if (!cfg || !ck || !out) return set_error(G4_ERR_INVALID, "g4_engine_create_from_checkpoint: null pointer");
+  g4_engine_config c = *cfg;
+  RCK(g4_checkpoint_config(ck, &c));
+  return create_impl(&c, nullptr, out, ck);
+}
+
 extern "C" int g4_engine_create_shared(const g4_engine_config* cfg, const g4_engine* weights, g4_engine** out) {
   G4_REQUIRE(weights, "g4_engine_create_shared: null weights engine");
   return create_impl(cfg, weights, out);
@@ -673,7 +721,8 @@ static int lin(g4_engine* e, const Lin& w, const float* X, int M, float* Y, bool
 static bool fused_ok(const g4_engine* e, int M, int pos0, bool dyn) {
   const ModelDims& d = e->d;
   return e->cfg.fused_layers && i8_path(e, M, false) && M >= 2 && M <= 4 && (dyn || pos0 + M > e->cfg.att_par) &&
-         d.H == 2048 && d.I == 8192 && d.HD == 256 && d.NQ == 8 && !e->prof.on;
+         d.H == 2048 && d.I == 8192 && d.HD == 256 && d.NQ == 8 && !e->prof.on &&
+         std::all_of(e->L.begin(), e->L.end(), [](const TLayer& t) { return t.scalar == 1.0f; });
 }
 static int forward_layers_fused(g4_engine* e, int M, int pos0, bool dyn) {
   const ModelDims& d = e->d;
@@ -815,9 +864,9 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
     RCK(lin(e, t.down, e->act, M, e->o, false, true));
     pf.mark(e->st, PH_EMBED_NORM);
     if (l + 1 < d.NL)  // residual (layer scalar 1) and the next layer's input norm
-      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, t.post_ff, 1.0f, H, e->L[l + 1].in_ln, e->a, 0, qo));
+      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, t.post_ff, t.scalar, H, e->L[l + 1].in_ln, e->a, 0, qo));
     else  // residual and the final norm (rounded) of every row into hbuf
-      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, t.post_ff, 1.0f, H, e->fnorm, e->hbuf, 1,
+      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, t.post_ff, t.scalar, H, e->fnorm, e->hbuf, 1,
                                            QuantOut{nullptr, nullptr, nullptr}));
     RCK(check_launch("layer"));
   }
@@ -1055,7 +1104,7 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0, in
     // residual, then the next layer's input norm and its quantisation (none after the last layer:
     // these rows need no final norm)
     RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(Mc), dim3(256), 0, e->st, (const float*)e->po, e->px,
-               (const float*)t.post_ff, 1.0f, H, l + 1 < d.NL ? (const float*)e->L[l + 1].in_ln : (const float*)nullptr,
+               (const float*)t.post_ff, t.scalar, H, l + 1 < d.NL ? (const float*)e->L[l + 1].in_ln : (const float*)nullptr,
                e->pa, 0, qo));
   }
   return check_launch("prefill_chunk");

@@ -67,6 +67,12 @@ SIGNATURES = {
     "g4_engine_phase_times": (_I, [_P, _I, _P, _P]),
     "g4_engine_trace": (_I, [_P, _P, _I, _P]),
     "g4_engine_create_shared": (_I, [_P, _P, _P]),
+    "g4_checkpoint_open": (_I, [ctypes.c_char_p, ctypes.c_char_p, _P]),
+    "g4_checkpoint_close": (None, [_P]),
+    "g4_checkpoint_count": (_I, [_P]),
+    "g4_checkpoint_tensor": (_I, [_P, ctypes.c_char_p, ctypes.c_char_p, _I, _P, _I, _P, _P]),
+    "g4_checkpoint_config": (_I, [_P, _P]),
+    "g4_engine_create_from_checkpoint": (_I, [_P, _P, _P]),
     "g4_engine_copy_state": (_I, [_P, _P]),
     "g4_engine_decode_async": (_I, [_P, _I, _I, _P]),
     "g4_engine_decode_wait": (_I, [_P, _P, _P, _P, _P, _P]),
@@ -555,14 +561,53 @@ def engine_config(**kw):
     return c
 
 
+class Checkpoint:
+    """A checkpoint in the reference's format (g4_checkpoint_* in include/g4.h): model.safetensors
+    read through the reference's index file (make_index.py's lines) or the safetensors header."""
+
+    def __init__(self, path, index=None):
+        self.h = ctypes.c_void_p()
+        check(lib().g4_checkpoint_open(str(path).encode(), None if index is None else str(index).encode(),
+                                       ctypes.byref(self.h)), "g4_checkpoint_open")
+
+    def close(self):
+        if self.h:
+            lib().g4_checkpoint_close(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __len__(self):
+        return lib().g4_checkpoint_count(self.h)
+
+    def tensor(self, name):
+        """(dtype, shape, nbytes) of one tensor."""
+        dt = ctypes.create_string_buffer(16)
+        shape = (ctypes.c_longlong * 8)()
+        nd, nb = ctypes.c_int(0), ctypes.c_longlong(0)
+        check(lib().g4_checkpoint_tensor(self.h, name.encode(), dt, 16, shape, 8, ctypes.byref(nd), ctypes.byref(nb)),
+              "g4_checkpoint_tensor")
+        return dt.value.decode(), tuple(shape[i] for i in range(nd.value)), nb.value
+
+    def config(self, cfg=None, **kw):
+        """An EngineConfig with the checkpoint's model sizes (g4_checkpoint_config)."""
+        cfg = cfg if cfg is not None else engine_config(**kw)
+        check(lib().g4_checkpoint_config(self.h, ctypes.byref(cfg)), "g4_checkpoint_config")
+        return cfg
+
+
 class Engine:
     """The speculative greedy-decode engine (g4_engine_* in include/g4.h)."""
 
-    def __init__(self, cfg=None, share=None, **kw):
-        """share: another Engine whose weights this one uses (an independent request stream)."""
+    def __init__(self, cfg=None, share=None, checkpoint=None, **kw):
+        """share: another Engine whose weights this one uses (an independent request stream);
+        checkpoint: a Checkpoint whose target weights the engine loads (its model sizes replace
+        the configuration's)."""
         self.cfg = cfg if cfg is not None else engine_config(**kw)
         self.h = ctypes.c_void_p()
-        if share is not None:
+        if checkpoint is not None:
+            check(lib().g4_engine_create_from_checkpoint(ctypes.byref(self.cfg), checkpoint.h, ctypes.byref(self.h)),
+                  "g4_engine_create_from_checkpoint")
+            checkpoint.config(self.cfg)
+        elif share is not None:
             check(lib().g4_engine_create_shared(ctypes.byref(self.cfg), share.h, ctypes.byref(self.h)),
                   "g4_engine_create_shared")
         else:

@@ -4,8 +4,10 @@
 //
 //   g4_serve <ckpt> <index> <prompt file> <n_new>
 //
-// The first two arguments are accepted and ignored (the model is the synthetic one, generated from
-// a seed on the device).  With ENGINE_SERVE set, each stdin line is a request "<n_new> <id> <id> ..."
+// When <ckpt> exists (a checkpoint directory holding model.safetensors, or the file itself), the
+// target weights are loaded from it (g4_engine_create_from_checkpoint), through <index> when that
+// file exists (the reference's make_index.py output) and the safetensors header otherwise; else the
+// model is the synthetic one, generated from a seed on the device.  With ENGINE_SERVE set, each stdin line is a request "<n_new> <id> <id> ..."
 // or "BENCH_MODE <k> <tree>"; otherwise one request runs with the token ids of <prompt file>
 // (whitespace separated) and <n_new>.  Per request the output is, as the reference prints it:
 //   FIRST <id>                       (n_new > 0: the token after the prompt, before decoding)
@@ -20,6 +22,8 @@
 // G4_VOCAB, G4_SEED (defaults: configs[4]).  Not built here: the audio tower (AUDIO_* lines answer
 // "AUDIO_UNSUPPORTED"; "A=" words of a request are skipped) and the tree/sibling mode (BENCH_MODE
 // with tree 1 answers MODE_ERROR).
+#include <sys/stat.h>
+
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -145,7 +149,20 @@ int main(int argc, char** argv) {
   c.slot_min_reuse = env_int("ENGINE_SLOT_MIN_REUSE", c.slot_min_reuse);
   if (c.k_draft == 0) c.ngram = 0;  // the reference's plain greedy loop when no drafts (:1614)
   g4_engine* e = nullptr;
-  if (g4_engine_create(&c, &e) != G4_OK) {
+  struct stat sb;
+  const bool from_ckpt = stat(argv[1], &sb) == 0;
+  if (from_ckpt) {
+    g4_checkpoint* ck = nullptr;
+    const bool has_index = stat(argv[2], &sb) == 0 && S_ISREG(sb.st_mode);
+    if (g4_checkpoint_open(argv[1], has_index ? argv[2] : nullptr, &ck) != G4_OK ||
+        g4_engine_create_from_checkpoint(&c, ck, &e) != G4_OK) {
+      std::fprintf(stderr, "g4_serve: checkpoint %s: %s\n", argv[1], g4_last_error());
+      g4_checkpoint_close(ck);
+      return 1;
+    }
+    g4_checkpoint_config(ck, &c);
+    g4_checkpoint_close(ck);
+  } else if (g4_engine_create(&c, &e) != G4_OK) {
     std::fprintf(stderr, "g4_serve: engine: %s\n", g4_last_error());
     return 1;
   }
@@ -153,8 +170,8 @@ int main(int argc, char** argv) {
     std::fprintf(stderr, "g4_serve: fake context: %s\n", g4_last_error());
     return 1;
   }
-  std::fprintf(stderr, "g4_serve: synthetic model hidden=%d layers=%d vocab=%d ctx=%d k=%d ngram=%d slots=%d\n", c.hidden,
-               c.n_layers, c.vocab, c.ctx_max, c.k_draft, c.ngram, c.slots);
+  std::fprintf(stderr, "g4_serve: %s model hidden=%d layers=%d vocab=%d ctx=%d k=%d ngram=%d slots=%d\n", from_ckpt ? "checkpoint" : "synthetic",
+               c.hidden, c.n_layers, c.vocab, c.ctx_max, c.k_draft, c.ngram, c.slots);
   const bool stream = std::getenv("ENGINE_STREAM") != nullptr;
   int rc = 0;
   if (std::getenv("ENGINE_SERVE")) {

@@ -284,6 +284,36 @@ void g4_engine_destroy(g4_engine* e);
  * streams (the reference serves one request at a time) run concurrently through
  * g4_engine_decode_async. */
 int g4_engine_create_shared(const g4_engine_config* cfg, const g4_engine* weights, g4_engine** out);
+/* ---------------------------------------------------------------- checkpoints
+ * A checkpoint in the reference's format, read on the host (no GPU needed): <ckpt>/model.safetensors
+ * (path may name the file or the directory), found through the reference's index file (one line per
+ * tensor: name, dtype, absolute offset, byte count, comma-separated shape, as tools/make_index.py
+ * writes it and gemma4_engine.cpp:1216-1217 reads it) or, when index is NULL, through the
+ * safetensors header itself.  The file is mapped read-only; every tensor's extent and byte count
+ * (dtype x shape) are checked at open. */
+typedef struct g4_checkpoint g4_checkpoint;
+int g4_checkpoint_open(const char* path, const char* index, g4_checkpoint** out);
+void g4_checkpoint_close(g4_checkpoint* ck);
+/* Number of tensors, and one tensor's dtype ("BF16", "I32", ...), shape (up to shape_cap dims) and
+ * byte count. */
+int g4_checkpoint_count(const g4_checkpoint* ck);
+int g4_checkpoint_tensor(const g4_checkpoint* ck, const char* name, char* dtype, int dtype_cap, long long* shape,
+                         int shape_cap, int* ndim, long long* nbytes);
+/* The target model the checkpoint holds: hidden, n_layers, mlp and vocab are written into cfg (its
+ * other fields are left as they are) after every tensor the engine reads has been checked (the
+ * reference's names, gemma4_engine.cpp:1222-1231: layers.<l>.self_attn.{q,k,v,o}_proj and
+ * mlp.{gate,up,down}_proj as weight_packed I32 [N][K/8] (or U8 [N][K/2]) + weight_scale BF16
+ * [N][K/32], the layer's norms BF16, layer_scalar BF16 (1 when absent), norm.weight,
+ * embed_tokens.weight BF16 [vocab][hidden]).  Parts of the real E2B model this build does not run
+ * (per-layer embeddings, KV-shared layers without k/v projections, head_dim other than 256,
+ * per-layer MLP widths) give G4_ERR_UNSUPPORTED with the part named. */
+int g4_checkpoint_config(const g4_checkpoint* ck, g4_engine_config* cfg);
+/* An engine whose target weights are the checkpoint's (the reference's q4 / bfvec loading,
+ * gemma4_engine.cpp:172-175, 1222-1231): cfg's model sizes are replaced by the checkpoint's
+ * (g4_checkpoint_config); the MTP drafter, when cfg->drafter is set, is generated from cfg->seed
+ * (the reference reads its drafter from a separate checkpoint of another format).  ck may be
+ * closed once this returns. */
+int g4_engine_create_from_checkpoint(const g4_engine_config* cfg, const g4_checkpoint* ck, g4_engine** out);
 /* One target forward (fwd) over M <= 32 host tokens at positions pos0..; int8 selects the W4A8
  * path for M >= 2.  When want, rows hf.. get the greedy next token G (host [M]) and, if hbuf is
  * non-null, the final-normed hidden (host [M][hidden]). */

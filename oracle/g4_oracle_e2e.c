@@ -10,6 +10,7 @@
  */
 #include "g4_oracle.h"
 #include <math.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -55,7 +56,7 @@ typedef struct {
   void (*attn_tile)(const uint16_t* Kc, const uint16_t* Vc, int hd, int sliding, const float* q, int qstride, int pos0,
                     int M, float* att);
 } or_e2e_hooks;
-typedef struct { Lin qkv, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff, *qn, *kn; int global; } TLayer;
+typedef struct { Lin qkv, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff, *qn, *kn; int global; float scalar; } TLayer;
 typedef struct { Lin q, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff, *qn; int global; } DLayer;
 
 typedef struct {
@@ -127,6 +128,7 @@ void* or_e2e_create(const or_e2e_config* c) {
   for (int l = 0; l < m->NL; ++l) {
     TLayer* t = &m->L[l];
     t->global = (l % 5 == 4);
+    t->scalar = 1.0f;
     { uint64_t ids[3] = {layer_id(l, T_Q), layer_id(l, T_K), layer_id(l, T_V)}; int rows[3] = {QD, m->HD, m->HD}; gen_lin(m, &t->qkv, ids, rows, 3, H); }
     { uint64_t ids[1] = {layer_id(l, T_O)}; int rows[1] = {H}; gen_lin(m, &t->o, ids, rows, 1, QD); }
     { uint64_t ids[2] = {layer_id(l, T_GATE), layer_id(l, T_UP)}; int rows[2] = {I, I}; gen_lin(m, &t->gu, ids, rows, 2, H); }
@@ -386,7 +388,7 @@ static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf
       float* xm = x + (size_t)r * H;
       for (int i = 0; i < H; ++i) om[i] = or_r16(om[i]);
       const float rr = rms_scale(om, H);
-      for (int i = 0; i < H; ++i) xm[i] = or_r16(or_r16(xm[i] + or_r16((om[i] * rr) * t->post_ff[i])) * 1.0f);
+      for (int i = 0; i < H; ++i) xm[i] = or_r16(or_r16(xm[i] + or_r16((om[i] * rr) * t->post_ff[i])) * t->scalar);
     }
   }
   if (want) {
@@ -702,4 +704,98 @@ int or_e2e_set_hooks(void* mp, const or_e2e_hooks* h) {
 /* raw weight bytes for cross-checking the generator: tensor `id`, first n bytes (reference layout) */
 void or_e2e_gen_bytes(unsigned long long seed, unsigned long long id, long long n, uint8_t* out) {
   for (long long i = 0; i < n; ++i) out[i] = (uint8_t)(wh(seed, id, (uint64_t)i) & 0xFF);
+}
+
+/* layer_scalar of target layer l (gemma4_engine.cpp:1389-1404; 1 unless set): x = r16(x * s) after
+ * the MLP residual, as the library applies it (s is used as given; pass a bf16 value). */
+void or_e2e_set_layer_scalar(void* mp, int l, float s) {
+  Model* m = (Model*)mp;
+  if (l >= 0 && l < m->NL) m->L[l].scalar = s;
+}
+
+/* The target model written as a checkpoint in the reference's format (test fixture writer): a
+ * safetensors file with the names the reference loads (gemma4_engine.cpp:1222-1231) - per layer
+ * the q/k/v/o and gate/up/down matrices as weight_packed (I32 [N][K/8], or U8 [N][K/2] when
+ * packed_u8) plus weight_scale (BF16 [N][K/32]), the six norms and layer_scalar (BF16), then
+ * norm.weight and embed_tokens.weight.  Returns 0, or -1 when the file cannot be written. */
+typedef struct { char name[96]; const char* dtype; long long shape[2]; int nd; const void* data; size_t nbytes; } CkOut;
+static void ck_add(CkOut* o, int* n, const char* name, const char* dtype, long long a, long long b, int nd, const void* data,
+                   size_t nbytes) {
+  CkOut* t = &o[(*n)++];
+  snprintf(t->name, sizeof t->name, "%s", name);
+  t->dtype = dtype; t->shape[0] = a; t->shape[1] = b; t->nd = nd; t->data = data; t->nbytes = nbytes;
+}
+int or_e2e_write_checkpoint(void* mp, const char* path, int packed_u8) {
+  Model* m = (Model*)mp;
+  const int H = m->H, QD = m->NQ * m->HD, HD = m->HD, I = m->I;
+  const int per = 7 * 2 + 7;
+  CkOut* o = (CkOut*)calloc((size_t)m->NL * per + 2, sizeof(CkOut));
+  uint16_t* bf = (uint16_t*)malloc(sizeof(uint16_t) * ((size_t)m->NL * (4 * H + 2 * HD + 1) + H));
+  size_t bo = 0;
+  int n = 0;
+  char nm[96];
+  for (int l = 0; l < m->NL; ++l) {
+    const TLayer* t = &m->L[l];
+    struct { const char* name; const Lin* lin; int row0, rows; } lins[7] = {
+        {"self_attn.q_proj", &t->qkv, 0, QD}, {"self_attn.k_proj", &t->qkv, QD, HD}, {"self_attn.v_proj", &t->qkv, QD + HD, HD},
+        {"self_attn.o_proj", &t->o, 0, H},    {"mlp.gate_proj", &t->gu, 0, I},       {"mlp.up_proj", &t->gu, I, I},
+        {"mlp.down_proj", &t->down, 0, H}};
+    for (int k = 0; k < 7; ++k) {
+      const Lin* L = lins[k].lin;
+      const int K = L->K, rows = lins[k].rows;
+      snprintf(nm, sizeof nm, "layers.%d.%s.weight_packed", l, lins[k].name);
+      if (packed_u8) ck_add(o, &n, nm, "U8", rows, K / 2, 2, L->w + (size_t)lins[k].row0 * K / 2, (size_t)rows * K / 2);
+      else ck_add(o, &n, nm, "I32", rows, K / 8, 2, L->w + (size_t)lins[k].row0 * K / 2, (size_t)rows * K / 2);
+      snprintf(nm, sizeof nm, "layers.%d.%s.weight_scale", l, lins[k].name);
+      ck_add(o, &n, nm, "BF16", rows, K / 32, 2, L->s + (size_t)lins[k].row0 * K / 32, sizeof(uint16_t) * (size_t)rows * K / 32);
+    }
+    struct { const char* name; const float* v; int len; } vecs[6] = {
+        {"input_layernorm.weight", t->in_ln, H}, {"post_attention_layernorm.weight", t->post_attn, H},
+        {"pre_feedforward_layernorm.weight", t->pre_ff, H}, {"post_feedforward_layernorm.weight", t->post_ff, H},
+        {"self_attn.q_norm.weight", t->qn, HD}, {"self_attn.k_norm.weight", t->kn, HD}};
+    for (int k = 0; k < 6; ++k) {
+      uint16_t* dst = bf + bo;
+      for (int i = 0; i < vecs[k].len; ++i) dst[i] = or_f2bf(vecs[k].v[i]);
+      bo += (size_t)vecs[k].len;
+      snprintf(nm, sizeof nm, "layers.%d.%s", l, vecs[k].name);
+      ck_add(o, &n, nm, "BF16", vecs[k].len, 0, 1, dst, sizeof(uint16_t) * (size_t)vecs[k].len);
+    }
+    bf[bo] = or_f2bf(t->scalar);
+    snprintf(nm, sizeof nm, "layers.%d.layer_scalar", l);
+    ck_add(o, &n, nm, "BF16", 1, 0, 1, bf + bo, 2);
+    bo += 1;
+  }
+  {
+    uint16_t* dst = bf + bo;
+    for (int i = 0; i < H; ++i) dst[i] = or_f2bf(m->fnorm[i]);
+    ck_add(o, &n, "norm.weight", "BF16", H, 0, 1, dst, sizeof(uint16_t) * (size_t)H);
+  }
+  ck_add(o, &n, "embed_tokens.weight", "BF16", m->V, H, 2, m->E, sizeof(uint16_t) * (size_t)m->V * H);
+  /* header: JSON, padded with spaces to a multiple of 8 bytes */
+  size_t cap = 256 + (size_t)n * 192, len = 0, off = 0;
+  char* hdr = (char*)malloc(cap);
+  len += (size_t)snprintf(hdr + len, cap - len, "{\"__metadata__\":{\"format\":\"pt\"}");
+  for (int k = 0; k < n; ++k) {
+    if (o[k].nd == 2)
+      len += (size_t)snprintf(hdr + len, cap - len, ",\"%s\":{\"dtype\":\"%s\",\"shape\":[%lld,%lld],\"data_offsets\":[%zu,%zu]}",
+                              o[k].name, o[k].dtype, o[k].shape[0], o[k].shape[1], off, off + o[k].nbytes);
+    else
+      len += (size_t)snprintf(hdr + len, cap - len, ",\"%s\":{\"dtype\":\"%s\",\"shape\":[%lld],\"data_offsets\":[%zu,%zu]}",
+                              o[k].name, o[k].dtype, o[k].shape[0], off, off + o[k].nbytes);
+    off += o[k].nbytes;
+  }
+  len += (size_t)snprintf(hdr + len, cap - len, "}");
+  while (len % 8) hdr[len++] = ' ';
+  int rc = -1;
+  FILE* f = fopen(path, "wb");
+  if (f) {
+    const uint64_t hl = (uint64_t)len;
+    int ok = fwrite(&hl, 8, 1, f) == 1 && fwrite(hdr, 1, len, f) == len;
+    for (int k = 0; k < n && ok; ++k) ok = fwrite(o[k].data, 1, o[k].nbytes, f) == o[k].nbytes;
+    rc = (fclose(f) == 0 && ok) ? 0 : -1;
+  }
+  free(hdr);
+  free(bf);
+  free(o);
+  return rc;
 }

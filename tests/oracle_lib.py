@@ -56,6 +56,8 @@ _SIGS_ORACLE = {
     "or_e2e_prefill_from": (_I, [_P, _P, _I, _I, _P]),
     "or_e2e_history": (_I, [_P, _P, _I, _P, _P]),
     "or_e2e_set_k": (None, [_P, _I]),
+    "or_e2e_set_layer_scalar": (None, [_P, _I, ctypes.c_float]),
+    "or_e2e_write_checkpoint": (_I, [_P, ctypes.c_char_p, _I]),
     "or_e2e_decode": (_I, [_P, _I, _I, _P, _P, _P, _P, _I]),
     "or_e2e_set_state": (_I, [_P, _P, _P, _I, _P, _I, _P, _I]),
     "or_e2e_set_hooks": (_I, [_P, _P]),
@@ -326,6 +328,13 @@ class OracleModel:
 
     def set_k(self, k):
         oracle().or_e2e_set_k(self.h, int(k))
+
+    def set_layer_scalar(self, layer, value):
+        oracle().or_e2e_set_layer_scalar(self.h, int(layer), float(value))
+
+    def write_checkpoint(self, path, packed_u8=False):
+        """The model's target weights as a checkpoint in the reference's format (safetensors)."""
+        assert oracle().or_e2e_write_checkpoint(self.h, str(path).encode(), int(packed_u8)) == 0
 
     def history(self):
         """(committed history: prompt + every committed token, last committed position P)."""
