@@ -1250,6 +1250,7 @@ static int verify_body(g4_engine* e, int M) {
   return forward(e, M, 0, true, 0, true);
 }
 static int ensure_verify_graph(g4_engine* e, int M) {
+  e->i8_active = e->cfg.decode_int8 && e->cfg.prefill_int8;  // verify passes run in the decode mode (:1600)
   if (!e->gverify[M]) RCK(capture(e, &e->gverify[M], &e->graw_verify[M], [&] { return verify_body(e, M); }, &e->gk_verify[M]));
   return G4_OK;
 }
@@ -1653,6 +1654,8 @@ extern "C" int g4_engine_decode_async(g4_engine* e, int max_rounds, int max_toke
              "g4_engine_decode_async: bad arguments or a call already pending");
   if (!e->cfg.graphs || e->prof.on || e->P + 1 <= e->cfg.att_par || e->stopped || e->P + 1 + 8 >= e->cfg.ctx_max)
     return set_error(G4_ERR_UNSUPPORTED, "g4_engine_decode_async: needs graphs on, a position past att_par and room in the context");
+  // the decode mode first: the round-loop graph records the verify passes of the current mode
+  e->i8_active = e->cfg.decode_int8 && e->cfg.prefill_int8;
   if (!e->gloop && !e->loop_failed && build_loop_graph(e) != G4_OK) {
     e->loop_failed = true;
     cudaGetLastError();
@@ -1663,7 +1666,6 @@ extern "C" int g4_engine_decode_async(g4_engine* e, int max_rounds, int max_toke
     ECK(cudaEventCreate(&e->aev1));
   }
   e->async_t0 = std::chrono::steady_clock::now();
-  e->i8_active = e->cfg.decode_int8 && e->cfg.prefill_int8;
   if (start_event) ECK(cudaStreamWaitEvent(e->st, reinterpret_cast<cudaEvent_t>(start_event), 0));
   ECK(cudaEventRecord(e->aev0, e->st));
   RCK(launch("k_decode_setup", k_decode_setup, dim3(1), dim3(1), 0, e->st, e->rc, max_rounds, max_tokens));

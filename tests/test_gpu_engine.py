@@ -313,3 +313,28 @@ def test_shared_weight_streams_decode_concurrently():
             eng.close()
         base.close()
         om.close()
+
+
+def test_copied_stream_decodes_in_the_engine_mode():
+    """A stream engine whose first call is an asynchronous decode (its state copied from another
+    engine, never prefilled itself) records its round graphs in the engine's decode mode (W4A8 here):
+    the same tokens, history and final hidden state as the source engine decoding the same rounds
+    (the hidden state tells the int8 verify passes from float ones even where the tokens agree)."""
+    cfg = dict(hidden=512, n_layers=5, mlp=1024, vocab=4096, ctx_max=1024)
+    a = g4.Engine(g4.engine_config(**cfg))
+    b = g4.Engine(g4.engine_config(**cfg), share=a)
+    try:
+        a.prefill(make_prompt(9, 300, vocab=4096))  # past att_par: the decode runs as graphs
+        b.copy_state_from(a)
+        out = np.zeros(64, np.int32)
+        n, _ = a.decode(8, 64, out)
+        b.decode_async(8, 64)
+        tb, _, _ = b.decode_wait()
+        assert list(out[:n]) == list(tb)
+        _, _, seq_a, h_a, P_a = a.export_state(0, kv=False)
+        _, _, seq_b, h_b, P_b = b.export_state(0, kv=False)
+        assert P_a == P_b and np.array_equal(seq_a, seq_b)
+        assert np.array_equal(h_a, h_b)
+    finally:
+        b.close()
+        a.close()
