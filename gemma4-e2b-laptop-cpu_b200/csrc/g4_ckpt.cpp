@@ -84,15 +84,17 @@ struct Json {
     v = std::strtoll(std::string(s, p).c_str(), nullptr, 10);
     return true;
   }
-  bool skip() {  // any value
+  int depth = 0;
+  bool skip() {  // any value (nesting bounded: a header is a flat object of small objects)
     ws();
-    if (p >= end) return ok = false;
+    if (p >= end || depth > 64) return ok = false;
     if (*p == '"') { std::string s; return str(s); }
     if (*p == '{' || *p == '[') {
       const char close = *p == '{' ? '}' : ']';
       const bool obj = *p == '{';
       ++p;
       if (eat(close)) return true;
+      ++depth;
       do {
         if (obj) {
           std::string k;
@@ -100,6 +102,7 @@ struct Json {
         }
         if (!skip()) return false;
       } while (eat(','));
+      --depth;
       if (!eat(close)) ok = false;
       return ok;
     }

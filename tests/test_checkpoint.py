@@ -154,6 +154,10 @@ def test_damaged_files_fail_at_open(ckpt, tmp_path):
     trunc.write_bytes((ckpt / "model.safetensors").read_bytes()[:4096])
     expect_error(lambda: g4.Checkpoint(trunc), None, ["trunc.safetensors"])
     expect_error(lambda: g4.Checkpoint(tmp_path / "none.safetensors"), None, ["cannot open"])
+    deep = ('{"__metadata__":' + "[" * 200 + "]" * 200 + "}").encode()  # nesting past the parser's bound
+    deep += b" " * (-len(deep) % 8)
+    (tmp_path / "deep.safetensors").write_bytes(struct.pack("<Q", len(deep)) + deep)
+    expect_error(lambda: g4.Checkpoint(tmp_path / "deep.safetensors"), None, ["malformed"])
 
 
 def test_e2b_parts_are_reported_unsupported(ckpt, tmp_path):
