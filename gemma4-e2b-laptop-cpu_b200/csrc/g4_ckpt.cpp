@@ -16,6 +16,7 @@
 
 #include "g4_api.h"
 #include "g4_ckpt.h"
+#include "g4_model.cuh"
 
 using g4::CkTensor;
 using g4::set_error;
@@ -388,9 +389,24 @@ extern "C" int g4_checkpoint_config(const g4_checkpoint* ck, g4_engine_config* c
   const CkTensor* kn0 = ck->find(g4::ck_layer(0, "self_attn.k_norm.weight"));
   if (!kn0 || kn0->shape.size() != 1) return set_error(G4_ERR_INVALID, "checkpoint: layers.0.self_attn.k_norm.weight missing");
   constexpr long long HD = 256, NQ = 8;
+  // KV sharing (owner_of, gemma4_engine.cpp:1251): the layers from the first one without k/v
+  // projections on read their owner's cache; every one of them must lack them and have an owner
+  int OWN = 0;
+  while (OWN < NL && ck->find(g4::ck_layer(OWN, "self_attn.k_proj.weight_scale"))) ++OWN;
+  if (OWN == NL) OWN = 0;
+  g4::ModelDims dd;
+  dd.NL = NL;
+  dd.OWN = OWN;
   for (int l = 0; l < NL; ++l) {
-    if (!ck->find(g4::ck_layer(l, "self_attn.k_proj.weight_scale")))
-      return set_error(G4_ERR_UNSUPPORTED, "checkpoint: layer %d has no k_proj (KV-shared layers are not supported by this build)", l);
+    if (!dd.owns(l) && (ck->find(g4::ck_layer(l, "self_attn.k_proj.weight_scale")) ||
+                        ck->find(g4::ck_layer(l, "self_attn.v_proj.weight_scale"))))
+      return set_error(G4_ERR_UNSUPPORTED, "checkpoint: layer %d has k/v projections after the KV-shared layer %d (the "
+                       "shared layers must be the last ones)", l, OWN);
+    if (dd.owner_of(l) < 0)
+      return set_error(G4_ERR_UNSUPPORTED, "checkpoint: KV-shared layer %d has no %s layer to read its cache from", l,
+                       dd.global_layer(l) ? "global" : "sliding");
+  }
+  for (int l = 0; l < NL; ++l) {
     const CkTensor* kn = ck->find(g4::ck_layer(l, "self_attn.k_norm.weight"));
     if (kn && kn->shape.size() == 1 && kn->shape[0] != HD)
       return set_error(G4_ERR_UNSUPPORTED, "checkpoint: layer %d has head_dim %lld (this build runs head_dim 256)", l, kn->shape[0]);
@@ -404,6 +420,7 @@ extern "C" int g4_checkpoint_config(const g4_checkpoint* ck, g4_engine_config* c
         {"self_attn.o_proj", {H, NQ * HD}}, {"mlp.gate_proj", {I, H}},      {"mlp.up_proj", {I, H}},
         {"mlp.down_proj", {H, I}}};
     for (auto& li : lins) {
+      if (!dd.owns(l) && (!std::strcmp(li.first, "self_attn.k_proj") || !std::strcmp(li.first, "self_attn.v_proj"))) continue;
       const std::string b = p + li.first;
       if (!need_packed(ck, b, li.second.first, li.second.second, &rc)) return rc;
       if (!need(ck, b + ".weight_scale", "BF16", {li.second.first, li.second.second / 32}, &rc)) return rc;
@@ -411,14 +428,17 @@ extern "C" int g4_checkpoint_config(const g4_checkpoint* ck, g4_engine_config* c
     const std::pair<const char*, long long> vecs[] = {{"input_layernorm.weight", H},  {"post_attention_layernorm.weight", H},
                                                       {"pre_feedforward_layernorm.weight", H}, {"post_feedforward_layernorm.weight", H},
                                                       {"self_attn.q_norm.weight", HD}, {"self_attn.k_norm.weight", HD}};
-    for (auto& v : vecs)
+    for (auto& v : vecs) {
+      if (!dd.owns(l) && !std::strcmp(v.first, "self_attn.k_norm.weight")) continue;
       if (!need(ck, p + v.first, "BF16", {v.second}, &rc)) return rc;
+    }
     float s;
     if ((rc = g4::ck_load_scalar(ck, p + "layer_scalar", &s)) != G4_OK) return rc;
   }
   if (!need(ck, "norm.weight", "BF16", {H}, &rc)) return rc;
   cfg->hidden = (int)H;
   cfg->n_layers = NL;
+  cfg->kv_owners = OWN;
   cfg->mlp = (int)I;
   cfg->vocab = (int)V;
   return G4_OK;

@@ -39,8 +39,8 @@ struct TcLin {  // the tensor-core operands of a Lin: s8 weights [N][K] and scal
 struct TLayer {
   Lin qkv, o, gu, down;
   TcLin tqkv, to, tgu, tdown;
-  float *in_ln, *post_attn, *pre_ff, *post_ff, *qn, *kn;
-  bool global;
+  float *in_ln = nullptr, *post_attn = nullptr, *pre_ff = nullptr, *post_ff = nullptr, *qn = nullptr, *kn = nullptr;
+  bool global = false;
   float scalar = 1.0f;  // layer_scalar (:1389-1404): 1 for the synthetic model, a checkpoint's value otherwise
 };
 struct DLayerW {
@@ -354,6 +354,7 @@ extern "C" int g4_engine_default_config(g4_engine_config* c) {
   c->prefill_tc = 1;
   c->slots = 1;
   c->slot_min_reuse = 32;
+  c->kv_owners = 0;
   return G4_OK;
 }
 
@@ -424,11 +425,22 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
                  c.prefill_block >= 1 && c.prefill_block <= 32 && c.k_draft >= 0 && c.k_draft <= 3 && c.attn_chunks >= 1 &&
                  c.attn_chunks <= 16 && c.slots >= 0 && c.slots <= 64 && c.slot_min_reuse >= 0,
              "g4_engine_create: unsupported configuration");
+  G4_REQUIRE(c.kv_owners >= 0 && c.kv_owners <= c.n_layers, "g4_engine_create: kv_owners %d outside [0, %d]", c.kv_owners,
+             c.n_layers);
+  {
+    ModelDims dd;
+    dd.NL = c.n_layers;
+    dd.OWN = c.kv_owners;
+    for (int l = 0; l < dd.NL; ++l)
+      G4_REQUIRE(dd.owner_of(l) >= 0, "g4_engine_create: KV-shared layer %d has no %s layer among the owners", l,
+                 dd.global_layer(l) ? "global" : "sliding");
+  }
   RCK(g4_device_init());
   g4_engine* e = new g4_engine();
   e->cfg = c;
   ModelDims& d = e->d;
   d.H = c.hidden; d.NL = c.n_layers; d.I = c.mlp; d.V = c.vocab; d.DCENT = c.vocab / d.DPER;
+  d.OWN = c.kv_owners;
   d.DTOP = std::min(32, d.DCENT);
   auto fail = [&](int rc) { g4_engine_destroy(e); return rc; };
   if (cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking) != cudaSuccess) return fail(set_error(G4_ERR_CUDA, "stream"));
@@ -436,6 +448,7 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
   if (share) {
     const g4_engine_config& sc = share->cfg;
     if (sc.hidden != c.hidden || sc.n_layers != c.n_layers || sc.mlp != c.mlp || sc.vocab != c.vocab || sc.seed != c.seed ||
+        sc.kv_owners != c.kv_owners ||
         (c.drafter && !sc.drafter) || c.ctx_max > sc.ctx_max || (c.prefill_tc && !share->tc_ready && sc.prefill_tc))
       return fail(set_error(G4_ERR_INVALID, "g4_engine_create_shared: configuration differs from the weights' engine"));
     e->L = share->L;
@@ -456,8 +469,9 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
   for (int l = 0; l < d.NL && ck; ++l) {  // target weights from a checkpoint (q4 / bfvec, :1222-1229)
     TLayer& t = e->L[l];
     t.global = d.global_layer(l);
-    int rc = ck_lin(e, ck, t.qkv, {{ck_layer(l, "self_attn.q_proj"), QD}, {ck_layer(l, "self_attn.k_proj"), d.HD},
-                                   {ck_layer(l, "self_attn.v_proj"), d.HD}}, H, tmp);
+    int rc = d.owns(l) ? ck_lin(e, ck, t.qkv, {{ck_layer(l, "self_attn.q_proj"), QD}, {ck_layer(l, "self_attn.k_proj"), d.HD},
+                                              {ck_layer(l, "self_attn.v_proj"), d.HD}}, H, tmp)
+                       : ck_lin(e, ck, t.qkv, {{ck_layer(l, "self_attn.q_proj"), QD}}, H, tmp);
     if (!rc) rc = ck_lin(e, ck, t.o, {{ck_layer(l, "self_attn.o_proj"), H}}, QD, tmp);
     if (!rc) rc = ck_lin(e, ck, t.gu, {{ck_layer(l, "mlp.gate_proj"), I}, {ck_layer(l, "mlp.up_proj"), I}}, H, tmp);
     if (!rc) rc = ck_lin(e, ck, t.down, {{ck_layer(l, "mlp.down_proj"), H}}, I, tmp);
@@ -466,14 +480,15 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
     if (!rc) rc = ck_norm(e, ck, &t.pre_ff, ck_layer(l, "pre_feedforward_layernorm.weight"), H);
     if (!rc) rc = ck_norm(e, ck, &t.post_ff, ck_layer(l, "post_feedforward_layernorm.weight"), H);
     if (!rc) rc = ck_norm(e, ck, &t.qn, ck_layer(l, "self_attn.q_norm.weight"), d.HD);
-    if (!rc) rc = ck_norm(e, ck, &t.kn, ck_layer(l, "self_attn.k_norm.weight"), d.HD);
+    if (!rc && d.owns(l)) rc = ck_norm(e, ck, &t.kn, ck_layer(l, "self_attn.k_norm.weight"), d.HD);
     if (!rc) rc = ck_load_scalar(ck, ck_layer(l, "layer_scalar"), &t.scalar);
     if (rc) return fail(rc);
   }
   for (int l = 0; l < d.NL && !ck; ++l) {
     TLayer& t = e->L[l];
     t.global = d.global_layer(l);
-    int rc = gen_lin(e, t.qkv, {{layer_id(l, T_Q), QD}, {layer_id(l, T_K), d.HD}, {layer_id(l, T_V), d.HD}}, H, tmp);
+    int rc = d.owns(l) ? gen_lin(e, t.qkv, {{layer_id(l, T_Q), QD}, {layer_id(l, T_K), d.HD}, {layer_id(l, T_V), d.HD}}, H, tmp)
+                       : gen_lin(e, t.qkv, {{layer_id(l, T_Q), QD}}, H, tmp);  // KV-shared: q only
     if (!rc) rc = gen_lin(e, t.o, {{layer_id(l, T_O), H}}, QD, tmp);
     if (!rc) rc = gen_lin(e, t.gu, {{layer_id(l, T_GATE), I}, {layer_id(l, T_UP), I}}, H, tmp);
     if (!rc) rc = gen_lin(e, t.down, {{layer_id(l, T_DOWN), H}}, I, tmp);
@@ -482,7 +497,7 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
     if (!rc) rc = gen_norm(e, &t.pre_ff, layer_id(l, T_PRE_FF), H, 1.f);
     if (!rc) rc = gen_norm(e, &t.post_ff, layer_id(l, T_POST_FF), H, 1.f);
     if (!rc) rc = gen_norm(e, &t.qn, layer_id(l, T_QN), d.HD, 0.0625f);
-    if (!rc) rc = gen_norm(e, &t.kn, layer_id(l, T_KN), d.HD, 1.f);
+    if (!rc && d.owns(l)) rc = gen_norm(e, &t.kn, layer_id(l, T_KN), d.HD, 1.f);
     if (rc) return fail(rc);
   }
   if (ck ? ck_norm(e, ck, &e->fnorm, "norm.weight", H) : gen_norm(e, &e->fnorm, T_FNORM, H, 1.f)) return fail(G4_ERR_CUDA);
@@ -721,7 +736,7 @@ static int lin(g4_engine* e, const Lin& w, const float* X, int M, float* Y, bool
 static bool fused_ok(const g4_engine* e, int M, int pos0, bool dyn) {
   const ModelDims& d = e->d;
   return e->cfg.fused_layers && i8_path(e, M, false) && M >= 2 && M <= 4 && (dyn || pos0 + M > e->cfg.att_par) &&
-         d.H == 2048 && d.I == 8192 && d.HD == 256 && d.NQ == 8 && !e->prof.on &&
+         d.H == 2048 && d.I == 8192 && d.HD == 256 && d.NQ == 8 && !e->prof.on && d.OWN == 0 &&
          std::all_of(e->L.begin(), e->L.end(), [](const TLayer& t) { return t.scalar == 1.0f; });
 }
 static int forward_layers_fused(g4_engine* e, int M, int pos0, bool dyn) {
@@ -795,7 +810,7 @@ static int forward_layers_fused(g4_engine* e, int M, int pos0, bool dyn) {
 
 static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = false) {
   const ModelDims& d = e->d;
-  const int H = d.H, QD = d.NQ * d.HD, ld = QD + 2 * d.HD;
+  const int H = d.H, QD = d.NQ * d.HD;
   const float sqrtH = sqrtf((float)H);
   PhaseTimer& pf = e->prof;
   const QuantOut qo = quant_out(e, M, false);
@@ -812,17 +827,20 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
     const int ty = t.global ? 1 : 0;
     pf.mark(e->st, PH_LINEAR);
     RCK(lin(e, t.qkv, e->a, M, e->qkv, false, true));
-    uint16_t* Kc = e->Kc + (size_t)l * e->cfg.ctx_max * d.HD;
-    uint16_t* Vc = e->Vc + (size_t)l * e->cfg.ctx_max * d.HD;
+    // a KV-shared layer (:1251) has the q projection only and reads its owner's cache
+    const bool own = d.owns(l);
+    const int ld = t.qkv.N, parts = d.NQ + (own ? 2 : 0);
+    uint16_t* Kc = e->Kc + (size_t)d.owner_of(l) * e->cfg.ctx_max * d.HD;
+    uint16_t* Vc = e->Vc + (size_t)d.owner_of(l) * e->cfg.ctx_max * d.HD;
     pf.mark(e->st, PH_EMBED_NORM);
     const bool split = dyn || (M <= 4 && pos0 + M > e->cfg.att_par);
     // split-KV reads the rotated queries from qs ([M][QD]); the per-row paths read them in place
     if (d.HD % 64 == 0 && d.HD <= 512 && d.NQ + 2 <= 16)  // warp per head
-      RCK(launch("k_qkv_post_w", k_qkv_post_w, dim3(M), dim3(32 * (d.NQ + 2)), 0, e->st, e->qkv, ld, d.NQ, d.HD,
+      RCK(launch("k_qkv_post_w", k_qkv_post_w, dim3(M), dim3(32 * parts), 0, e->st, e->qkv, ld, d.NQ, d.HD,
                  dyn ? 1 : pos0, dyn ? e->ctl : nullptr, t.qn, t.kn, e->rope[ty][0], e->rope[ty][1], Kc, Vc,
                  split ? e->qs : e->qkv, split ? QD : ld));
     else
-      RCK(launch("k_qkv_post", k_qkv_post, dim3(dim3(M, d.NQ + 2)), dim3(256), 0, e->st, e->qkv, ld, d.NQ, d.HD, dyn ? 1 : pos0, dyn ? e->ctl : nullptr,
+      RCK(launch("k_qkv_post", k_qkv_post, dim3(dim3(M, parts)), dim3(256), 0, e->st, e->qkv, ld, d.NQ, d.HD, dyn ? 1 : pos0, dyn ? e->ctl : nullptr,
                                                        t.qn, t.kn, e->rope[ty][0], e->rope[ty][1], Kc, Vc,
                                                        split ? e->qs : e->qkv, split ? QD : ld));
     RCK(check_launch("k_qkv_post"));
@@ -916,7 +934,7 @@ static int draft_step(g4_engine* e, const int* dtok_in, const float* h, int pos,
     // target layer whose KV the drafter reads: the last global layer, or the last sliding layer
     int tl = -1;
     for (int l2 = d.NL - 1; l2 >= 0; --l2)
-      if (d.global_layer(l2) == t.global) { tl = l2; break; }
+      if (d.global_layer(l2) == t.global) { tl = d.owner_of(l2); break; }
     if (tl < 0) return set_error(G4_ERR_UNSUPPORTED, "draft_step: the target has no %s layer", t.global ? "global" : "sliding");
     RCK(lin(e, t.q, e->da, 1, e->dq, true, true));
     RCK(launch("k_q_post", k_q_post, dim3(d.NQ), dim3(256), 0, e->st, e->dq, d.HD, dyn ? 1 + j : pos, dyn ? e->ctl : nullptr, t.qn, e->rope[ty][0],
@@ -1002,7 +1020,7 @@ extern "C" int g4_engine_fake_ctx(g4_engine* e, int n) {
     return (uint16_t)(u >> 16);
   };
   ECK(cudaStreamSynchronize(e->st));
-  for (int l = 0; l < e->d.NL; ++l) {
+  for (int l = 0; l < e->d.NL && e->d.owns(l); ++l) {  // the owners' caches, one stream (:1249-1250)
     for (size_t i = 0; i < (size_t)n * HD; ++i) {
       kb[i] = rnd();
       vb[i] = rnd();
@@ -1047,7 +1065,7 @@ static int ensure_chunk_buffers(g4_engine* e) {
 constexpr int kPrefillRows = 4;  // query rows per block of the prefill attention
 static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0, int blk_fn) {
   const ModelDims& d = e->d;
-  const int H = d.H, QD = d.NQ * d.HD, ld = QD + 2 * d.HD, I = d.I;
+  const int H = d.H, QD = d.NQ * d.HD, I = d.I;
   const int Mpad = (Mc + 127) / 128 * 128;
   const QuantOut qo{e->pq, e->psx, e->psum};
   ECK(cudaMemcpyAsync(e->ptoks, toks, sizeof(int) * Mc, cudaMemcpyHostToDevice, e->st));
@@ -1061,10 +1079,11 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0, in
   for (int l = 0; l < d.NL; ++l) {
     const TLayer& t = e->L[l];
     const int ty = t.global ? 1 : 0;
-    uint16_t* Kc = e->Kc + (size_t)l * e->cfg.ctx_max * d.HD;
-    uint16_t* Vc = e->Vc + (size_t)l * e->cfg.ctx_max * d.HD;
+    const int ld = t.qkv.N;  // QD for a KV-shared layer, whose K and V are its owner's
+    uint16_t* Kc = e->Kc + (size_t)d.owner_of(l) * e->cfg.ctx_max * d.HD;
+    uint16_t* Vc = e->Vc + (size_t)d.owner_of(l) * e->cfg.ctx_max * d.HD;
     RCK(gemm(t.tqkv, t.qkv, e->pqkv));
-    RCK(launch("k_qkv_post_w", k_qkv_post_w, dim3(Mc), dim3(32 * (d.NQ + 2)), 0, e->st, (const float*)e->pqkv, ld, d.NQ, d.HD,
+    RCK(launch("k_qkv_post_w", k_qkv_post_w, dim3(Mc), dim3(32 * (d.NQ + (d.owns(l) ? 2 : 0))), 0, e->st, (const float*)e->pqkv, ld, d.NQ, d.HD,
                pos0, (const int*)nullptr, (const float*)t.qn, (const float*)t.kn, (const float*)e->rope[ty][0],
                (const float*)e->rope[ty][1], Kc, Vc, e->pqkv, ld));
     const int len_max = t.global ? pos0 + Mc : std::min(pos0 + Mc, d.WINDOW);

@@ -28,7 +28,17 @@ namespace g4 {
 struct ModelDims {
   int H = 2048, NL = 30, NQ = 8, HD = 256, I = 8192, V = 262144, WINDOW = 512;
   int DL = 4, DCENT = 2048, DTOP = 32, DPER = 128;  // drafter layers, centroids, top centroids, tokens per centroid
+  int OWN = 0;  // KV owners: layers [0, OWN) own a KV cache (0 = all)
   bool global_layer(int l) const { return l % 5 == 4; }
+  bool owns(int l) const { return OWN <= 0 || l < OWN; }
+  // the layer whose KV cache layer l reads (owner_of, gemma4_engine.cpp:1251): itself, or the last
+  // owner of its type; -1 when there is none
+  int owner_of(int l) const {
+    if (owns(l)) return l;
+    for (int j = OWN - 1; j >= 0; --j)
+      if (global_layer(j) == global_layer(l)) return j;
+    return -1;
+  }
 };
 
 // tensor ids

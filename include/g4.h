@@ -259,6 +259,11 @@ typedef struct {
   int slots;                         /* ENGINE_SLOTS (1): conversations kept for the prefix cache (the
                                         active one and slots - 1 stored, each with its own K/V) */
   int slot_min_reuse;                /* ENGINE_SLOT_MIN_REUSE (32) */
+  int kv_owners;                     /* KV sharing (owner_of, gemma4_engine.cpp:1251; the E2B model: 15):
+                                        layers [0, kv_owners) own a KV cache, every later layer reads
+                                        the cache of the last owner of its type (sliding or global)
+                                        and has no k/v projections; 0 (the default) = every layer
+                                        owns its cache */
 } g4_engine_config;
 typedef struct {
   int rounds, ngram_rounds, drafted, accepted, prefill_tokens, decode_tokens;
@@ -304,9 +309,10 @@ int g4_checkpoint_tensor(const g4_checkpoint* ck, const char* name, char* dtype,
  * reference's names, gemma4_engine.cpp:1222-1231: layers.<l>.self_attn.{q,k,v,o}_proj and
  * mlp.{gate,up,down}_proj as weight_packed I32 [N][K/8] (or U8 [N][K/2]) + weight_scale BF16
  * [N][K/32], the layer's norms BF16, layer_scalar BF16 (1 when absent), norm.weight,
- * embed_tokens.weight BF16 [vocab][hidden]).  Parts of the real E2B model this build does not run
- * (per-layer embeddings, KV-shared layers without k/v projections, head_dim other than 256,
- * per-layer MLP widths) give G4_ERR_UNSUPPORTED with the part named. */
+ * embed_tokens.weight BF16 [vocab][hidden]).  Trailing layers without k/v projections (and k_norm)
+ * are KV-shared: cfg->kv_owners is set to the first of them.  Parts of the real E2B model this build
+ * does not run (per-layer embeddings, head_dim other than 256, per-layer MLP widths) give
+ * G4_ERR_UNSUPPORTED with the part named. */
 int g4_checkpoint_config(const g4_checkpoint* ck, g4_engine_config* cfg);
 /* An engine whose target weights are the checkpoint's (the reference's q4 / bfvec loading,
  * gemma4_engine.cpp:172-175, 1222-1231): cfg's model sizes are replaced by the checkpoint's

@@ -61,6 +61,7 @@ typedef struct { Lin q, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff
 
 typedef struct {
   int H, NL, I, V, NQ, HD, WINDOW, DL, DCENT, DTOP, DPER;
+  int OWN; /* KV owners: layers [0, OWN) own a cache (0 = all) */
   int ctx_max, prefill_block, k_draft, ngram, ngram_len, prefill_int8, decode_int8, attn_chunks, att_par, drafter;
   uint64_t seed;
   TLayer* L;
@@ -86,6 +87,16 @@ typedef struct {
   or_e2e_hooks hk;
   void* head_ref;
 } Model;
+
+/* owner_of (gemma4_engine.cpp:1251): the layer whose KV cache layer l reads - itself when it owns
+ * one, else the last owner of its type (l % 5 == 4: global). */
+static int owns(const Model* m, int l) { return m->OWN <= 0 || l < m->OWN; }
+static int owner_of(const Model* m, int l) {
+  if (owns(m, l)) return l;
+  for (int j = m->OWN - 1; j >= 0; --j)
+    if ((j % 5 == 4) == (l % 5 == 4)) return j;
+  return -1;
+}
 
 static void gen_lin(Model* m, Lin* lin, const uint64_t* ids, const int* rows, int parts, int K) {
   int N = 0;
@@ -114,7 +125,8 @@ typedef struct {
   int hidden, n_layers, mlp, vocab, ctx_max, prefill_block, k_draft, ngram, ngram_len, prefill_int8, decode_int8;
   int head_screen, screen_lim, attn_chunks, att_par, drafter;
   unsigned long long seed;
-} or_e2e_config;  /* field order of g4_engine_config */
+  int kv_owners; /* layers [0, kv_owners) own a KV cache (0 = all), g4_engine_config's field */
+} or_e2e_config;  /* g4_engine_config's first fields, then kv_owners */
 
 void* or_e2e_create(const or_e2e_config* c) {
   Model* m = (Model*)calloc(1, sizeof(Model));
@@ -123,13 +135,15 @@ void* or_e2e_create(const or_e2e_config* c) {
   m->ctx_max = c->ctx_max; m->prefill_block = c->prefill_block; m->k_draft = c->k_draft; m->ngram = c->ngram;
   m->ngram_len = c->ngram_len; m->prefill_int8 = c->prefill_int8; m->decode_int8 = c->decode_int8;
   m->attn_chunks = c->attn_chunks; m->att_par = c->att_par; m->drafter = c->drafter; m->seed = c->seed;
+  m->OWN = c->kv_owners;
   const int H = m->H, QD = m->NQ * m->HD, I = m->I;
   m->L = (TLayer*)calloc(m->NL, sizeof(TLayer));
   for (int l = 0; l < m->NL; ++l) {
     TLayer* t = &m->L[l];
     t->global = (l % 5 == 4);
     t->scalar = 1.0f;
-    { uint64_t ids[3] = {layer_id(l, T_Q), layer_id(l, T_K), layer_id(l, T_V)}; int rows[3] = {QD, m->HD, m->HD}; gen_lin(m, &t->qkv, ids, rows, 3, H); }
+    /* a KV-shared layer has the q projection only (no k/v projections, no k_norm) */
+    { uint64_t ids[3] = {layer_id(l, T_Q), layer_id(l, T_K), layer_id(l, T_V)}; int rows[3] = {QD, m->HD, m->HD}; gen_lin(m, &t->qkv, ids, rows, owns(m, l) ? 3 : 1, H); }
     { uint64_t ids[1] = {layer_id(l, T_O)}; int rows[1] = {H}; gen_lin(m, &t->o, ids, rows, 1, QD); }
     { uint64_t ids[2] = {layer_id(l, T_GATE), layer_id(l, T_UP)}; int rows[2] = {I, I}; gen_lin(m, &t->gu, ids, rows, 2, H); }
     { uint64_t ids[1] = {layer_id(l, T_DOWN)}; int rows[1] = {H}; gen_lin(m, &t->down, ids, rows, 1, I); }
@@ -138,7 +152,7 @@ void* or_e2e_create(const or_e2e_config* c) {
     t->pre_ff = gen_norm(m, layer_id(l, T_PRE_FF), H, 1.f);
     t->post_ff = gen_norm(m, layer_id(l, T_POST_FF), H, 1.f);
     t->qn = gen_norm(m, layer_id(l, T_QN), m->HD, 0.0625f);
-    t->kn = gen_norm(m, layer_id(l, T_KN), m->HD, 1.f);
+    t->kn = owns(m, l) ? gen_norm(m, layer_id(l, T_KN), m->HD, 1.f) : NULL;
   }
   m->fnorm = gen_norm(m, T_FNORM, H, 1.f);
   const long long EV = (long long)m->V * H;
@@ -313,10 +327,10 @@ static void attn_row(const Model* m, const uint16_t* Kc, const uint16_t* Vc, con
 
 /* One target forward over M tokens at pos0 (fwd).  G[hf..] = greedy tokens, hbuf[hf..] = hidden. */
 static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf, int* G, float* hbuf) {
-  const int H = m->H, QD = m->NQ * m->HD, ld = QD + 2 * m->HD, I = m->I, hd = m->HD;
+  const int H = m->H, QD = m->NQ * m->HD, ldmax = QD + 2 * m->HD, I = m->I, hd = m->HD;
   float* x = (float*)malloc(sizeof(float) * (size_t)M * H);
   float* a = (float*)malloc(sizeof(float) * (size_t)M * H);
-  float* qkv = (float*)malloc(sizeof(float) * (size_t)M * ld);
+  float* qkv = (float*)malloc(sizeof(float) * (size_t)M * ldmax);
   float* att = (float*)malloc(sizeof(float) * (size_t)M * QD);
   float* o = (float*)malloc(sizeof(float) * (size_t)M * H);
   float* gu = (float*)malloc(sizeof(float) * (size_t)M * 2 * I);
@@ -328,16 +342,18 @@ static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf
   for (int l = 0; l < m->NL; ++l) {
     TLayer* t = &m->L[l];
     const int ty = t->global ? 1 : 0;
+    const int ld = t->qkv.N; /* QD + 2 hd, or QD for a KV-shared layer */
     for (int r = 0; r < M; ++r) rmsnorm(x + (size_t)r * H, t->in_ln, H, a + (size_t)r * H, 0);
     lin(m, &t->qkv, a, M, qkv, 0);
-    uint16_t* Kc = m->Kc + (size_t)l * m->ctx_max * hd;
-    uint16_t* Vc = m->Vc + (size_t)l * m->ctx_max * hd;
+    uint16_t* Kc = m->Kc + (size_t)owner_of(m, l) * m->ctx_max * hd;
+    uint16_t* Vc = m->Vc + (size_t)owner_of(m, l) * m->ctx_max * hd;
     for (int r = 0; r < M; ++r) {
       const int pos = pos0 + r;
       const float* cs = m->rc[ty] + (size_t)pos * (hd / 2);
       const float* sn = m->rs[ty] + (size_t)pos * (hd / 2);
       float* qr = qkv + (size_t)r * ld;
       for (int h = 0; h < m->NQ; ++h) { rms_r16_w(qr + (size_t)h * hd, t->qn, hd); rope(qr + (size_t)h * hd, cs, sn, hd); }
+      if (!owns(m, l)) continue; /* K and V come from the owner's cache */
       float* kr = qr + QD;
       float* vr = qr + QD + hd;
       rms_r16_w(kr, t->kn, hd); rope(kr, cs, sn, hd);
@@ -428,7 +444,7 @@ static int draft(Model* m, int tok, const float* h, int pos, int P, float* h_nex
     const int ty = t->global ? 1 : 0;
     int tl = -1;
     for (int l2 = m->NL - 1; l2 >= 0; --l2)
-      if ((l2 % 5 == 4) == t->global) { tl = l2; break; }
+      if ((l2 % 5 == 4) == t->global) { tl = owner_of(m, l2); break; }
     rmsnorm(dx, t->in_ln, H, da, 0);
     lin(m, &t->q, da, 1, dq, 1);
     const float* cs = m->rc[ty] + (size_t)pos * (hd / 2);
@@ -507,7 +523,7 @@ static int is_stop(int t) { return t == 106 || t == 1; }
 void or_e2e_fake_ctx(void* mp, int n) {
   Model* m = (Model*)mp;
   uint32_t rs = 12345;
-  for (int l = 0; l < m->NL; ++l)
+  for (int l = 0; l < m->NL && owns(m, l); ++l) /* the owners' caches, one stream (:1249-1250) */
     for (size_t i = 0; i < (size_t)n * m->HD; ++i) {
       rs = rs * 1664525u + 1013904223u;
       m->Kc[(size_t)l * m->ctx_max * m->HD + i] = or_f2bf(((int)(rs >> 9) % 2001 - 1000) / 700.0f);
@@ -741,6 +757,7 @@ int or_e2e_write_checkpoint(void* mp, const char* path, int packed_u8) {
         {"self_attn.o_proj", &t->o, 0, H},    {"mlp.gate_proj", &t->gu, 0, I},       {"mlp.up_proj", &t->gu, I, I},
         {"mlp.down_proj", &t->down, 0, H}};
     for (int k = 0; k < 7; ++k) {
+      if (!owns(m, l) && (k == 1 || k == 2)) continue; /* a KV-shared layer has no k/v projections */
       const Lin* L = lins[k].lin;
       const int K = L->K, rows = lins[k].rows;
       snprintf(nm, sizeof nm, "layers.%d.%s.weight_packed", l, lins[k].name);
@@ -754,6 +771,7 @@ int or_e2e_write_checkpoint(void* mp, const char* path, int packed_u8) {
         {"pre_feedforward_layernorm.weight", t->pre_ff, H}, {"post_feedforward_layernorm.weight", t->post_ff, H},
         {"self_attn.q_norm.weight", t->qn, HD}, {"self_attn.k_norm.weight", t->kn, HD}};
     for (int k = 0; k < 6; ++k) {
+      if (!vecs[k].v) continue; /* k_norm of a KV-shared layer */
       uint16_t* dst = bf + bo;
       for (int i = 0; i < vecs[k].len; ++i) dst[i] = or_f2bf(vecs[k].v[i]);
       bo += (size_t)vecs[k].len;

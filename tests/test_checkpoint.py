@@ -170,11 +170,38 @@ def test_e2b_parts_are_reported_unsupported(ckpt, tmp_path):
         expect_error(lambda: ck.config(), None, ["per-layer embeddings"])
     finally:
         ck.close()
-    # a KV-shared layer: no k/v projections
+    # a KV-shared layer without an owner of its type: layer 4 is the first global layer
     shared = [r for r in rows if not r[0].startswith(("layers.4.self_attn.k_proj", "layers.4.self_attn.v_proj"))]
     write_index(tmp_path / "kv.tsv", shared)
     ck = g4.Checkpoint(ckpt / "model.safetensors", tmp_path / "kv.tsv")
     try:
-        expect_error(lambda: ck.config(), None, ["layer 4", "KV-shared"])
+        expect_error(lambda: ck.config(), None, ["KV-shared layer 4", "no global layer"])
+    finally:
+        ck.close()
+    # k/v projections after a KV-shared layer
+    gap = [r for r in rows if not r[0].startswith(("layers.2.self_attn.k_proj", "layers.2.self_attn.v_proj"))]
+    write_index(tmp_path / "gap.tsv", gap)
+    ck = g4.Checkpoint(ckpt / "model.safetensors", tmp_path / "gap.tsv")
+    try:
+        expect_error(lambda: ck.config(), None, ["layer 3 has k/v projections after the KV-shared layer 2"])
+    finally:
+        ck.close()
+
+
+def test_kv_shared_checkpoint(tmp_path):
+    """Trailing layers without k/v projections (the E2B model's KV sharing, :1251): the config names
+    the first of them as kv_owners, and the shared layers carry no k_proj, v_proj or k_norm."""
+    m = OracleModel(e2e_config(**dict(SMALL, n_layers=10), seed=778, kv_owners=5))
+    try:
+        m.write_checkpoint(tmp_path / "model.safetensors")
+    finally:
+        m.close()
+    ck = g4.Checkpoint(tmp_path)
+    try:
+        cfg = ck.config()
+        assert (cfg.n_layers, cfg.kv_owners) == (10, 5)
+        assert len(ck) == 5 * 21 + 5 * 16 + 2
+        expect_error(lambda: ck.tensor("layers.7.self_attn.k_proj.weight_packed"), None, ["no tensor"])
+        assert ck.tensor("layers.7.self_attn.q_proj.weight_packed")[1] == (2048, 64)
     finally:
         ck.close()
