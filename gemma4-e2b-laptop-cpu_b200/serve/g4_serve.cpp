@@ -19,7 +19,7 @@
 // ENGINE_NGRAM, ENGINE_NGLEN, ENGINE_PREFILL_INT8, ENGINE_DECODE_INT8, ENGINE_HEAD_SCREEN,
 // ENGINE_CTX, ENGINE_FAKE_CTX, ENGINE_ATT_PAR, ENGINE_PREFILL_BLOCK, ENGINE_SLOTS,
 // ENGINE_SLOT_MIN_REUSE, ENGINE_STREAM; the synthetic model's size from G4_HIDDEN, G4_LAYERS, G4_MLP,
-// G4_VOCAB, G4_SEED (defaults: configs[4]).  Not built here: the audio tower (AUDIO_* lines answer
+// G4_VOCAB, G4_SEED, G4_KV_OWNERS (defaults: configs[4], no KV sharing).  Not built here: the audio tower (AUDIO_* lines answer
 // "AUDIO_UNSUPPORTED"; "A=" words of a request are skipped) and the tree/sibling mode (BENCH_MODE
 // with tree 1 answers MODE_ERROR).
 #include <sys/stat.h>
@@ -136,6 +136,7 @@ int main(int argc, char** argv) {
   c.mlp = env_int("G4_MLP", c.mlp);
   c.vocab = env_int("G4_VOCAB", c.vocab);
   if (const char* s = std::getenv("G4_SEED")) c.seed = std::strtoull(s, nullptr, 10);
+  c.kv_owners = env_int("G4_KV_OWNERS", c.kv_owners);
   c.ctx_max = env_int("ENGINE_CTX", c.ctx_max);
   c.k_draft = env_int("ENGINE_K", c.k_draft);
   c.ngram = env_int("ENGINE_NGRAM", c.ngram);
