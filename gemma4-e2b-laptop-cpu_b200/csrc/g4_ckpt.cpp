@@ -406,19 +406,27 @@ extern "C" int g4_checkpoint_config(const g4_checkpoint* ck, g4_engine_config* c
       return set_error(G4_ERR_UNSUPPORTED, "checkpoint: KV-shared layer %d has no %s layer to read its cache from", l,
                        dd.global_layer(l) ? "global" : "sliding");
   }
+  // MLP widths: one for the owners (layer 0's), one for the KV-shared layers (the E2B model
+  // doubles it there)
+  long long IS = I;
+  if (OWN > 0) {
+    const CkTensor* gs = ck->find(g4::ck_layer(OWN, "mlp.gate_proj.weight_scale"));
+    if (gs && gs->shape.size() == 2) IS = gs->shape[0];
+  }
   for (int l = 0; l < NL; ++l) {
     const CkTensor* kn = ck->find(g4::ck_layer(l, "self_attn.k_norm.weight"));
     if (kn && kn->shape.size() == 1 && kn->shape[0] != HD)
       return set_error(G4_ERR_UNSUPPORTED, "checkpoint: layer %d has head_dim %lld (this build runs head_dim 256)", l, kn->shape[0]);
+    const long long Il = dd.owns(l) ? I : IS;
     const CkTensor* gl = ck->find(g4::ck_layer(l, "mlp.gate_proj.weight_scale"));
-    if (gl && gl->shape.size() == 2 && gl->shape[0] != I)
-      return set_error(G4_ERR_UNSUPPORTED, "checkpoint: layer %d has MLP width %lld, layer 0 %lld (one width for all layers "
-                       "in this build)", l, gl->shape[0], I);
+    if (gl && gl->shape.size() == 2 && gl->shape[0] != Il)
+      return set_error(G4_ERR_UNSUPPORTED, "checkpoint: layer %d has MLP width %lld, expected %lld (one width for the owner "
+                       "layers and one for the KV-shared layers in this build)", l, gl->shape[0], Il);
     const std::string p = "layers." + std::to_string(l) + ".";
     const std::pair<const char*, std::pair<long long, long long>> lins[] = {
         {"self_attn.q_proj", {NQ * HD, H}}, {"self_attn.k_proj", {HD, H}}, {"self_attn.v_proj", {HD, H}},
-        {"self_attn.o_proj", {H, NQ * HD}}, {"mlp.gate_proj", {I, H}},      {"mlp.up_proj", {I, H}},
-        {"mlp.down_proj", {H, I}}};
+        {"self_attn.o_proj", {H, NQ * HD}}, {"mlp.gate_proj", {Il, H}},     {"mlp.up_proj", {Il, H}},
+        {"mlp.down_proj", {H, Il}}};
     for (auto& li : lins) {
       if (!dd.owns(l) && (!std::strcmp(li.first, "self_attn.k_proj") || !std::strcmp(li.first, "self_attn.v_proj"))) continue;
       const std::string b = p + li.first;
@@ -439,6 +447,7 @@ extern "C" int g4_checkpoint_config(const g4_checkpoint* ck, g4_engine_config* c
   cfg->hidden = (int)H;
   cfg->n_layers = NL;
   cfg->kv_owners = OWN;
+  cfg->mlp_shared = IS != I ? (int)IS : 0;
   cfg->mlp = (int)I;
   cfg->vocab = (int)V;
   return G4_OK;

@@ -355,6 +355,7 @@ extern "C" int g4_engine_default_config(g4_engine_config* c) {
   c->slots = 1;
   c->slot_min_reuse = 32;
   c->kv_owners = 0;
+  c->mlp_shared = 0;
   return G4_OK;
 }
 
@@ -427,6 +428,8 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
              "g4_engine_create: unsupported configuration");
   G4_REQUIRE(c.kv_owners >= 0 && c.kv_owners <= c.n_layers, "g4_engine_create: kv_owners %d outside [0, %d]", c.kv_owners,
              c.n_layers);
+  G4_REQUIRE(c.mlp_shared >= 0 && c.mlp_shared % 256 == 0, "g4_engine_create: mlp_shared %d is not a multiple of 256",
+             c.mlp_shared);
   {
     ModelDims dd;
     dd.NL = c.n_layers;
@@ -441,14 +444,15 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
   ModelDims& d = e->d;
   d.H = c.hidden; d.NL = c.n_layers; d.I = c.mlp; d.V = c.vocab; d.DCENT = c.vocab / d.DPER;
   d.OWN = c.kv_owners;
+  d.IS = c.mlp_shared;
   d.DTOP = std::min(32, d.DCENT);
   auto fail = [&](int rc) { g4_engine_destroy(e); return rc; };
   if (cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking) != cudaSuccess) return fail(set_error(G4_ERR_CUDA, "stream"));
-  const int H = d.H, QD = d.NQ * d.HD, I = d.I;
+  const int H = d.H, QD = d.NQ * d.HD, I = d.I, IM = d.mlp_max();
   if (share) {
     const g4_engine_config& sc = share->cfg;
     if (sc.hidden != c.hidden || sc.n_layers != c.n_layers || sc.mlp != c.mlp || sc.vocab != c.vocab || sc.seed != c.seed ||
-        sc.kv_owners != c.kv_owners ||
+        sc.kv_owners != c.kv_owners || sc.mlp_shared != c.mlp_shared ||
         (c.drafter && !sc.drafter) || c.ctx_max > sc.ctx_max || (c.prefill_tc && !share->tc_ready && sc.prefill_tc))
       return fail(set_error(G4_ERR_INVALID, "g4_engine_create_shared: configuration differs from the weights' engine"));
     e->L = share->L;
@@ -462,7 +466,7 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
     e->shared = true;
   } else {
   uint8_t* tmp = nullptr;
-  const size_t tmp_bytes = (size_t)std::max({(size_t)(QD + 2 * d.HD) * H / 2, (size_t)2 * I * H / 2, (size_t)I * H / 2,
+  const size_t tmp_bytes = (size_t)std::max({(size_t)(QD + 2 * d.HD) * H / 2, (size_t)2 * IM * H / 2, (size_t)IM * H / 2,
                                               (size_t)QD * H / 2, (size_t)d.DCENT * H / 2, (size_t)H * 2 * H / 2});
   if (ealloc_t(e, &tmp, tmp_bytes)) return fail(G4_ERR_CUDA);
   e->L.resize(d.NL);
@@ -473,8 +477,9 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
                                               {ck_layer(l, "self_attn.v_proj"), d.HD}}, H, tmp)
                        : ck_lin(e, ck, t.qkv, {{ck_layer(l, "self_attn.q_proj"), QD}}, H, tmp);
     if (!rc) rc = ck_lin(e, ck, t.o, {{ck_layer(l, "self_attn.o_proj"), H}}, QD, tmp);
-    if (!rc) rc = ck_lin(e, ck, t.gu, {{ck_layer(l, "mlp.gate_proj"), I}, {ck_layer(l, "mlp.up_proj"), I}}, H, tmp);
-    if (!rc) rc = ck_lin(e, ck, t.down, {{ck_layer(l, "mlp.down_proj"), H}}, I, tmp);
+    const int Il = d.mlp_of(l);
+    if (!rc) rc = ck_lin(e, ck, t.gu, {{ck_layer(l, "mlp.gate_proj"), Il}, {ck_layer(l, "mlp.up_proj"), Il}}, H, tmp);
+    if (!rc) rc = ck_lin(e, ck, t.down, {{ck_layer(l, "mlp.down_proj"), H}}, Il, tmp);
     if (!rc) rc = ck_norm(e, ck, &t.in_ln, ck_layer(l, "input_layernorm.weight"), H);
     if (!rc) rc = ck_norm(e, ck, &t.post_attn, ck_layer(l, "post_attention_layernorm.weight"), H);
     if (!rc) rc = ck_norm(e, ck, &t.pre_ff, ck_layer(l, "pre_feedforward_layernorm.weight"), H);
@@ -490,8 +495,9 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
     int rc = d.owns(l) ? gen_lin(e, t.qkv, {{layer_id(l, T_Q), QD}, {layer_id(l, T_K), d.HD}, {layer_id(l, T_V), d.HD}}, H, tmp)
                        : gen_lin(e, t.qkv, {{layer_id(l, T_Q), QD}}, H, tmp);  // KV-shared: q only
     if (!rc) rc = gen_lin(e, t.o, {{layer_id(l, T_O), H}}, QD, tmp);
-    if (!rc) rc = gen_lin(e, t.gu, {{layer_id(l, T_GATE), I}, {layer_id(l, T_UP), I}}, H, tmp);
-    if (!rc) rc = gen_lin(e, t.down, {{layer_id(l, T_DOWN), H}}, I, tmp);
+    const int Il = d.mlp_of(l);
+    if (!rc) rc = gen_lin(e, t.gu, {{layer_id(l, T_GATE), Il}, {layer_id(l, T_UP), Il}}, H, tmp);
+    if (!rc) rc = gen_lin(e, t.down, {{layer_id(l, T_DOWN), H}}, Il, tmp);
     if (!rc) rc = gen_norm(e, &t.in_ln, layer_id(l, T_IN_LN), H, 1.f);
     if (!rc) rc = gen_norm(e, &t.post_attn, layer_id(l, T_POST_ATTN), H, 1.f);
     if (!rc) rc = gen_norm(e, &t.pre_ff, layer_id(l, T_PRE_FF), H, 1.f);
@@ -554,7 +560,8 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
   }
   }  // weights generated (not shared)
   // tensor-core prefill operands and chunk buffers
-  if (c.prefill_tc && c.prefill_int8 && H % 128 == 0 && QD % 128 == 0 && I % 128 == 0 && (QD + 2 * d.HD) % 128 == 0) {
+  if (c.prefill_tc && c.prefill_int8 && H % 128 == 0 && QD % 128 == 0 && I % 128 == 0 && IM % 128 == 0 &&
+      (QD + 2 * d.HD) % 128 == 0) {
     int rc = G4_OK;
     auto tc_lin = [&](const Lin& l, TcLin& t) {
       if (rc) return;
@@ -598,13 +605,13 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
   if (!rc) rc = ealloc_t(e, &e->x2, (size_t)MM * H);
   if (!rc) rc = ealloc_t(e, &e->segbar, (size_t)4 * (c.n_layers + 2) + 1);
   if (!rc) rc = ealloc_t(e, &e->segtrace, (size_t)(c.n_layers + 2) * 2 * kSegStamps);
-  if (!rc) rc = ealloc_t(e, &e->a, (size_t)MM * std::max(H, I));
+  if (!rc) rc = ealloc_t(e, &e->a, (size_t)MM * std::max(H, IM));
   if (!rc) rc = ealloc_t(e, &e->qkv, (size_t)MM * (QD + 2 * d.HD));
   if (!rc) rc = ealloc_t(e, &e->att, (size_t)MM * QD);
   if (!rc) rc = ealloc_t(e, &e->qs, (size_t)4 * QD);
   if (!rc) rc = ealloc_t(e, &e->o, (size_t)MM * H);
-  if (!rc) rc = ealloc_t(e, &e->gu, (size_t)MM * 2 * I);
-  if (!rc) rc = ealloc_t(e, &e->act, (size_t)MM * I);
+  if (!rc) rc = ealloc_t(e, &e->gu, (size_t)MM * 2 * IM);
+  if (!rc) rc = ealloc_t(e, &e->act, (size_t)MM * IM);
   if (!rc) rc = ealloc_t(e, &e->hbuf, (size_t)MM * H);
   if (!rc) rc = ealloc_t(e, &e->mlp_in, (size_t)MM * H);
   const size_t kmax = (size_t)std::max({2 * H, I, QD});  // widest linear input
@@ -877,7 +884,8 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
     pf.mark(e->st, PH_LINEAR);
     RCK(lin(e, t.gu, e->mlp_in, M, e->gu, false, true));
     pf.mark(e->st, PH_EMBED_NORM);
-    RCK(launch("k_act_q", k_act_q, dim3((unsigned)((long long)M * d.I / 256)), dim3(256), 0, e->st, e->gu, d.I, M, e->act, qo));
+    RCK(launch("k_act_q", k_act_q, dim3((unsigned)((long long)M * t.down.K / 256)), dim3(256), 0, e->st, e->gu, t.down.K, M,
+               e->act, qo));
     pf.mark(e->st, PH_LINEAR);
     RCK(lin(e, t.down, e->act, M, e->o, false, true));
     pf.mark(e->st, PH_EMBED_NORM);
@@ -1040,7 +1048,7 @@ extern "C" int g4_engine_fake_ctx(g4_engine* e, int n) {
 static int ensure_chunk_buffers(g4_engine* e) {
   if (e->ptoks) return G4_OK;
   const ModelDims& d = e->d;
-  const int H = d.H, QD = d.NQ * d.HD, I = d.I, MC = e->pmc;
+  const int H = d.H, QD = d.NQ * d.HD, I = d.mlp_max(), MC = e->pmc;
   const size_t kmax = (size_t)std::max({H, I, QD});
   int rc = ealloc_t(e, &e->ptoks, (size_t)MC);
   if (!rc) rc = ealloc_t(e, &e->px, (size_t)MC * H);
@@ -1065,7 +1073,7 @@ static int ensure_chunk_buffers(g4_engine* e) {
 constexpr int kPrefillRows = 4;  // query rows per block of the prefill attention
 static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0, int blk_fn) {
   const ModelDims& d = e->d;
-  const int H = d.H, QD = d.NQ * d.HD, I = d.I;
+  const int H = d.H, QD = d.NQ * d.HD;
   const int Mpad = (Mc + 127) / 128 * 128;
   const QuantOut qo{e->pq, e->psx, e->psum};
   ECK(cudaMemcpyAsync(e->ptoks, toks, sizeof(int) * Mc, cudaMemcpyHostToDevice, e->st));
@@ -1117,8 +1125,8 @@ static int prefill_chunk(g4_engine* e, const int32_t* toks, int Mc, int pos0, in
     RCK(launch("k_post_attn_q", k_post_attn_q, dim3(Mc), dim3(256), 0, e->st, (const float*)e->po, e->px, (const float*)t.post_attn,
                (const float*)t.pre_ff, e->pmlp, H, qo));
     RCK(gemm(t.tgu, t.gu, e->pgu));
-    RCK(launch("k_act_q", k_act_q, dim3((unsigned)((long long)Mc * I / 256)), dim3(256), 0, e->st, (const float*)e->pgu, I, Mc,
-               e->pact, qo));
+    RCK(launch("k_act_q", k_act_q, dim3((unsigned)((long long)Mc * t.down.K / 256)), dim3(256), 0, e->st, (const float*)e->pgu,
+               t.down.K, Mc, e->pact, qo));
     RCK(gemm(t.tdown, t.down, e->po));
     // residual, then the next layer's input norm and its quantisation (none after the last layer:
     // these rows need no final norm)

@@ -29,6 +29,9 @@ struct ModelDims {
   int H = 2048, NL = 30, NQ = 8, HD = 256, I = 8192, V = 262144, WINDOW = 512;
   int DL = 4, DCENT = 2048, DTOP = 32, DPER = 128;  // drafter layers, centroids, top centroids, tokens per centroid
   int OWN = 0;  // KV owners: layers [0, OWN) own a KV cache (0 = all)
+  int IS = 0;   // MLP width of the KV-shared layers (0 = I)
+  int mlp_of(int l) const { return (!owns(l) && IS > 0) ? IS : I; }
+  int mlp_max() const { return IS > I ? IS : I; }
   bool global_layer(int l) const { return l % 5 == 4; }
   bool owns(int l) const { return OWN <= 0 || l < OWN; }
   // the layer whose KV cache layer l reads (owner_of, gemma4_engine.cpp:1251): itself, or the last

@@ -264,6 +264,8 @@ typedef struct {
                                         the cache of the last owner of its type (sliding or global)
                                         and has no k/v projections; 0 (the default) = every layer
                                         owns its cache */
+  int mlp_shared;                    /* MLP width of the KV-shared layers (the E2B model: 12,288, twice
+                                        the owners' 6,144); 0 = mlp */
 } g4_engine_config;
 typedef struct {
   int rounds, ngram_rounds, drafted, accepted, prefill_tokens, decode_tokens;
@@ -310,8 +312,9 @@ int g4_checkpoint_tensor(const g4_checkpoint* ck, const char* name, char* dtype,
  * mlp.{gate,up,down}_proj as weight_packed I32 [N][K/8] (or U8 [N][K/2]) + weight_scale BF16
  * [N][K/32], the layer's norms BF16, layer_scalar BF16 (1 when absent), norm.weight,
  * embed_tokens.weight BF16 [vocab][hidden]).  Trailing layers without k/v projections (and k_norm)
- * are KV-shared: cfg->kv_owners is set to the first of them.  Parts of the real E2B model this build
- * does not run (per-layer embeddings, head_dim other than 256, per-layer MLP widths) give
+ * are KV-shared: cfg->kv_owners is set to the first of them, and cfg->mlp_shared to their MLP width
+ * when it differs from the owners'.  Parts of the real E2B model this build does not run
+ * (per-layer embeddings, head_dim other than 256, MLP widths that vary otherwise) give
  * G4_ERR_UNSUPPORTED with the part named. */
 int g4_checkpoint_config(const g4_checkpoint* ck, g4_engine_config* cfg);
 /* An engine whose target weights are the checkpoint's (the reference's q4 / bfvec loading,

@@ -62,6 +62,7 @@ typedef struct { Lin q, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff
 typedef struct {
   int H, NL, I, V, NQ, HD, WINDOW, DL, DCENT, DTOP, DPER;
   int OWN; /* KV owners: layers [0, OWN) own a cache (0 = all) */
+  int IS;  /* MLP width of the KV-shared layers (0 = I) */
   int ctx_max, prefill_block, k_draft, ngram, ngram_len, prefill_int8, decode_int8, attn_chunks, att_par, drafter;
   uint64_t seed;
   TLayer* L;
@@ -91,6 +92,7 @@ typedef struct {
 /* owner_of (gemma4_engine.cpp:1251): the layer whose KV cache layer l reads - itself when it owns
  * one, else the last owner of its type (l % 5 == 4: global). */
 static int owns(const Model* m, int l) { return m->OWN <= 0 || l < m->OWN; }
+static int mlp_of(const Model* m, int l) { return (!owns(m, l) && m->IS > 0) ? m->IS : m->I; }
 static int owner_of(const Model* m, int l) {
   if (owns(m, l)) return l;
   for (int j = m->OWN - 1; j >= 0; --j)
@@ -126,7 +128,8 @@ typedef struct {
   int head_screen, screen_lim, attn_chunks, att_par, drafter;
   unsigned long long seed;
   int kv_owners; /* layers [0, kv_owners) own a KV cache (0 = all), g4_engine_config's field */
-} or_e2e_config;  /* g4_engine_config's first fields, then kv_owners */
+  int mlp_shared; /* MLP width of the KV-shared layers (0 = mlp) */
+} or_e2e_config;  /* g4_engine_config's first fields, then kv_owners and mlp_shared */
 
 void* or_e2e_create(const or_e2e_config* c) {
   Model* m = (Model*)calloc(1, sizeof(Model));
@@ -136,6 +139,7 @@ void* or_e2e_create(const or_e2e_config* c) {
   m->ngram_len = c->ngram_len; m->prefill_int8 = c->prefill_int8; m->decode_int8 = c->decode_int8;
   m->attn_chunks = c->attn_chunks; m->att_par = c->att_par; m->drafter = c->drafter; m->seed = c->seed;
   m->OWN = c->kv_owners;
+  m->IS = c->mlp_shared;
   const int H = m->H, QD = m->NQ * m->HD, I = m->I;
   m->L = (TLayer*)calloc(m->NL, sizeof(TLayer));
   for (int l = 0; l < m->NL; ++l) {
@@ -145,8 +149,8 @@ void* or_e2e_create(const or_e2e_config* c) {
     /* a KV-shared layer has the q projection only (no k/v projections, no k_norm) */
     { uint64_t ids[3] = {layer_id(l, T_Q), layer_id(l, T_K), layer_id(l, T_V)}; int rows[3] = {QD, m->HD, m->HD}; gen_lin(m, &t->qkv, ids, rows, owns(m, l) ? 3 : 1, H); }
     { uint64_t ids[1] = {layer_id(l, T_O)}; int rows[1] = {H}; gen_lin(m, &t->o, ids, rows, 1, QD); }
-    { uint64_t ids[2] = {layer_id(l, T_GATE), layer_id(l, T_UP)}; int rows[2] = {I, I}; gen_lin(m, &t->gu, ids, rows, 2, H); }
-    { uint64_t ids[1] = {layer_id(l, T_DOWN)}; int rows[1] = {H}; gen_lin(m, &t->down, ids, rows, 1, I); }
+    { const int Il = mlp_of(m, l); uint64_t ids[2] = {layer_id(l, T_GATE), layer_id(l, T_UP)}; int rows[2] = {Il, Il}; gen_lin(m, &t->gu, ids, rows, 2, H); }
+    { uint64_t ids[1] = {layer_id(l, T_DOWN)}; int rows[1] = {H}; gen_lin(m, &t->down, ids, rows, 1, mlp_of(m, l)); }
     t->in_ln = gen_norm(m, layer_id(l, T_IN_LN), H, 1.f);
     t->post_attn = gen_norm(m, layer_id(l, T_POST_ATTN), H, 1.f);
     t->pre_ff = gen_norm(m, layer_id(l, T_PRE_FF), H, 1.f);
@@ -327,7 +331,8 @@ static void attn_row(const Model* m, const uint16_t* Kc, const uint16_t* Vc, con
 
 /* One target forward over M tokens at pos0 (fwd).  G[hf..] = greedy tokens, hbuf[hf..] = hidden. */
 static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf, int* G, float* hbuf) {
-  const int H = m->H, QD = m->NQ * m->HD, ldmax = QD + 2 * m->HD, I = m->I, hd = m->HD;
+  const int H = m->H, QD = m->NQ * m->HD, ldmax = QD + 2 * m->HD, hd = m->HD;
+  const int I = m->IS > m->I ? m->IS : m->I; /* buffer width: the widest MLP */
   float* x = (float*)malloc(sizeof(float) * (size_t)M * H);
   float* a = (float*)malloc(sizeof(float) * (size_t)M * H);
   float* qkv = (float*)malloc(sizeof(float) * (size_t)M * ldmax);
@@ -393,10 +398,11 @@ static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf
       rmsnorm(xm, t->pre_ff, H, mlp_in + (size_t)r * H, 1);
     }
     lin(m, &t->gu, mlp_in, M, gu, 0);
+    const int Il = t->down.K; /* this layer's MLP width */
     for (int r = 0; r < M; ++r)
-      for (int i = 0; i < I; ++i) {
-        const float g = or_r16(gu[(size_t)r * 2 * I + i]), u = or_r16(gu[(size_t)r * 2 * I + I + i]);
-        act[(size_t)r * I + i] = or_r16(or_r16(or_gelu(g)) * u);
+      for (int i = 0; i < Il; ++i) {
+        const float g = or_r16(gu[(size_t)r * 2 * Il + i]), u = or_r16(gu[(size_t)r * 2 * Il + Il + i]);
+        act[(size_t)r * Il + i] = or_r16(or_r16(or_gelu(g)) * u);
       }
     lin(m, &t->down, act, M, o, 0);
     for (int r = 0; r < M; ++r) {
@@ -743,7 +749,7 @@ static void ck_add(CkOut* o, int* n, const char* name, const char* dtype, long l
 }
 int or_e2e_write_checkpoint(void* mp, const char* path, int packed_u8) {
   Model* m = (Model*)mp;
-  const int H = m->H, QD = m->NQ * m->HD, HD = m->HD, I = m->I;
+  const int H = m->H, QD = m->NQ * m->HD, HD = m->HD;
   const int per = 7 * 2 + 7;
   CkOut* o = (CkOut*)calloc((size_t)m->NL * per + 2, sizeof(CkOut));
   uint16_t* bf = (uint16_t*)malloc(sizeof(uint16_t) * ((size_t)m->NL * (4 * H + 2 * HD + 1) + H));
@@ -752,6 +758,7 @@ int or_e2e_write_checkpoint(void* mp, const char* path, int packed_u8) {
   char nm[96];
   for (int l = 0; l < m->NL; ++l) {
     const TLayer* t = &m->L[l];
+    const int I = t->down.K; /* this layer's MLP width */
     struct { const char* name; const Lin* lin; int row0, rows; } lins[7] = {
         {"self_attn.q_proj", &t->qkv, 0, QD}, {"self_attn.k_proj", &t->qkv, QD, HD}, {"self_attn.v_proj", &t->qkv, QD + HD, HD},
         {"self_attn.o_proj", &t->o, 0, H},    {"mlp.gate_proj", &t->gu, 0, I},       {"mlp.up_proj", &t->gu, I, I},

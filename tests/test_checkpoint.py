@@ -190,8 +190,9 @@ def test_e2b_parts_are_reported_unsupported(ckpt, tmp_path):
 
 def test_kv_shared_checkpoint(tmp_path):
     """Trailing layers without k/v projections (the E2B model's KV sharing, :1251): the config names
-    the first of them as kv_owners, and the shared layers carry no k_proj, v_proj or k_norm."""
-    m = OracleModel(e2e_config(**dict(SMALL, n_layers=10), seed=778, kv_owners=5))
+    the first of them as kv_owners and their (here doubled) MLP width as mlp_shared, and the shared
+    layers carry no k_proj, v_proj or k_norm."""
+    m = OracleModel(e2e_config(**dict(SMALL, n_layers=10), seed=778, kv_owners=5, mlp_shared=2048))
     try:
         m.write_checkpoint(tmp_path / "model.safetensors")
     finally:
@@ -199,7 +200,8 @@ def test_kv_shared_checkpoint(tmp_path):
     ck = g4.Checkpoint(tmp_path)
     try:
         cfg = ck.config()
-        assert (cfg.n_layers, cfg.kv_owners) == (10, 5)
+        assert (cfg.n_layers, cfg.kv_owners, cfg.mlp, cfg.mlp_shared) == (10, 5, 1024, 2048)
+        assert ck.tensor("layers.6.mlp.down_proj.weight_scale")[1] == (512, 64)
         assert len(ck) == 5 * 21 + 5 * 16 + 2
         expect_error(lambda: ck.tensor("layers.7.self_attn.k_proj.weight_packed"), None, ["no tensor"])
         assert ck.tensor("layers.7.self_attn.q_proj.weight_packed")[1] == (2048, 64)

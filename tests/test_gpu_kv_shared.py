@@ -5,7 +5,8 @@ read layer 3's cache, global layer 9 reads layer 4's): hidden states of a prefil
 per-round trace of prompt lookup and MTP rounds (the drafter reads the target's last sliding and
 global caches through the same mapping), int8 and float verify passes, graphs and eager rounds, the
 tensor-core prefill, the fake context (filled over the owners only), and a checkpoint whose shared
-layers carry no k/v projections."""
+layers carry no k/v projections.  With mlp_shared the shared layers' MLP is twice as wide (the E2B
+model's 12,288 against 6,144)."""
 import numpy as np
 import pytest
 
@@ -17,11 +18,13 @@ pytestmark = pytest.mark.gpu
 from g4pkg import g4  # noqa: E402
 
 SHARED = dict(hidden=512, n_layers=10, mlp=1024, vocab=4096, ctx_max=1024, kv_owners=5)
+WIDE = dict(SHARED, mlp_shared=2048)
 
 
-def test_forward_matches_oracle():
-    om = OracleModel(e2e_config(**SHARED))
-    eng = g4.Engine(g4.engine_config(**SHARED))
+@pytest.mark.parametrize("cfg", [SHARED, WIDE], ids=["shared", "wide"])
+def test_forward_matches_oracle(cfg):
+    om = OracleModel(e2e_config(**cfg))
+    eng = g4.Engine(g4.engine_config(**cfg))
     try:
         toks = make_prompt(3, 8, vocab=4096)
         G_g, h_g = eng.forward(toks, 0)
@@ -33,10 +36,11 @@ def test_forward_matches_oracle():
         om.close()
 
 
-@pytest.mark.parametrize("ngram,graphs,decode_int8,prefill_tc", [(2, 1, 1, 1), (0, 1, 1, 1), (0, 0, 1, 0), (2, 1, 0, 1),
-                                                                  (0, 2, 1, 3)])
-def test_generate_matches_oracle(ngram, graphs, decode_int8, prefill_tc):
-    cfg = dict(SHARED, ngram=ngram, decode_int8=decode_int8)
+@pytest.mark.parametrize("ngram,graphs,decode_int8,prefill_tc,wide", [(2, 1, 1, 1, 0), (0, 1, 1, 1, 0), (0, 0, 1, 0, 0),
+                                                                       (2, 1, 0, 1, 0), (0, 2, 1, 3, 0), (2, 1, 1, 1, 1),
+                                                                       (0, 0, 0, 0, 1)])
+def test_generate_matches_oracle(ngram, graphs, decode_int8, prefill_tc, wide):
+    cfg = dict(WIDE if wide else SHARED, ngram=ngram, decode_int8=decode_int8)
     om = OracleModel(e2e_config(**cfg))
     eng = g4.Engine(g4.engine_config(**cfg, graphs=graphs, prefill_tc=prefill_tc))
     try:
@@ -68,14 +72,14 @@ def test_fake_context_over_the_owners():
 
 
 def test_shared_checkpoint_matches_oracle(tmp_path):
-    om = OracleModel(e2e_config(**dict(SHARED, seed=991)))
+    om = OracleModel(e2e_config(**dict(WIDE, seed=991)))
     try:
         om.write_checkpoint(tmp_path / "model.safetensors")
         ck = g4.Checkpoint(tmp_path)
         eng = g4.Engine(g4.engine_config(seed=991, ctx_max=1024), checkpoint=ck)
         ck.close()
         try:
-            assert (eng.cfg.n_layers, eng.cfg.kv_owners) == (10, 5)
+            assert (eng.cfg.n_layers, eng.cfg.kv_owners, eng.cfg.mlp, eng.cfg.mlp_shared) == (10, 5, 1024, 2048)
             prompt = make_prompt(8, 260, vocab=4096)
             tg, _ = eng.generate(prompt, 32)
             to, _, tro = om.generate(prompt, 32, trace=True)
