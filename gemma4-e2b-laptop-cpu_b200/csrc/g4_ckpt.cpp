@@ -253,7 +253,7 @@ const CkTensor* need_packed(const g4_checkpoint* ck, const std::string& base, lo
 std::string g4::ck_layer(int l, const char* suffix) { return "layers." + std::to_string(l) + "." + suffix; }
 
 int g4::ck_load_lin(const g4_checkpoint* ck, const std::vector<std::pair<std::string, int>>& parts, int K, uint8_t* w_dev,
-                    uint16_t* s_dev) {
+                    uint16_t* s_dev, cudaStream_t st) {
   size_t ro = 0, so = 0;
   for (auto& p : parts) {
     int rc = G4_OK;
@@ -261,8 +261,10 @@ int g4::ck_load_lin(const g4_checkpoint* ck, const std::vector<std::pair<std::st
     if (!w) return rc;
     const CkTensor* s = need(ck, p.first + ".weight_scale", "BF16", {p.second, K / 32}, &rc);
     if (!s) return rc;
-    if (cudaMemcpy(w_dev + ro, ck->base + w->off, w->nbytes, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(reinterpret_cast<uint8_t*>(s_dev) + so, ck->base + s->off, s->nbytes, cudaMemcpyHostToDevice) != cudaSuccess)
+    if (cudaMemcpyAsync(w_dev + ro, ck->base + w->off, w->nbytes, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(reinterpret_cast<uint8_t*>(s_dev) + so, ck->base + s->off, s->nbytes, cudaMemcpyHostToDevice, st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
       return set_error(G4_ERR_CUDA, "checkpoint: copy of %s failed", p.first.c_str());
     ro += w->nbytes;
     so += s->nbytes;
@@ -270,7 +272,7 @@ int g4::ck_load_lin(const g4_checkpoint* ck, const std::vector<std::pair<std::st
   return G4_OK;
 }
 
-int g4::ck_load_vec(const g4_checkpoint* ck, const std::string& name, int n, float* dev) {
+int g4::ck_load_vec(const g4_checkpoint* ck, const std::string& name, int n, float* dev, cudaStream_t st) {
   int rc = G4_OK;
   const CkTensor* t = need(ck, name, "BF16", {n}, &rc);
   if (!t) return rc;
@@ -281,16 +283,19 @@ int g4::ck_load_vec(const g4_checkpoint* ck, const std::string& name, int n, flo
     const uint32_t u = (uint32_t)b << 16;
     std::memcpy(&v[(size_t)i], &u, 4);
   }
-  if (cudaMemcpy(dev, v.data(), sizeof(float) * (size_t)n, cudaMemcpyHostToDevice) != cudaSuccess)
+  if (cudaMemcpyAsync(dev, v.data(), sizeof(float) * (size_t)n, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)  // before v goes out of scope
     return set_error(G4_ERR_CUDA, "checkpoint: copy of %s failed", name.c_str());
   return G4_OK;
 }
 
-int g4::ck_load_bf16(const g4_checkpoint* ck, const std::string& name, long long rows, long long cols, uint16_t* dev) {
+int g4::ck_load_bf16(const g4_checkpoint* ck, const std::string& name, long long rows, long long cols, uint16_t* dev,
+                     cudaStream_t st) {
   int rc = G4_OK;
   const CkTensor* t = need(ck, name, "BF16", {rows, cols}, &rc);
   if (!t) return rc;
-  if (cudaMemcpy(dev, ck->base + t->off, t->nbytes, cudaMemcpyHostToDevice) != cudaSuccess)
+  if (cudaMemcpyAsync(dev, ck->base + t->off, t->nbytes, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
     return set_error(G4_ERR_CUDA, "checkpoint: copy of %s failed", name.c_str());
   return G4_OK;
 }
@@ -371,10 +376,6 @@ extern "C" int g4_checkpoint_count(const g4_checkpoint* ck) { return ck ? (int)c
 // shape), and the parts of the real E2B model this build does not run reported by name.
 extern "C" int g4_checkpoint_config(const g4_checkpoint* ck, g4_engine_config* cfg) {
   if (!ck || !cfg) return set_error(G4_ERR_INVALID, "g4_checkpoint_config: null pointer");
-  if (ck->find("embed_tokens_per_layer.weight") || ck->find("per_layer_model_projection.weight_packed"))
-    return set_error(G4_ERR_UNSUPPORTED,
-                     "checkpoint: per-layer embeddings (embed_tokens_per_layer, per_layer_model_projection) are not "
-                     "supported by this build");
   int rc = G4_OK;
   const CkTensor* E = ck->find("embed_tokens.weight");
   if (!E || E->dtype != "BF16" || E->shape.size() != 2)
@@ -444,6 +445,24 @@ extern "C" int g4_checkpoint_config(const g4_checkpoint* ck, g4_engine_config* c
     if ((rc = g4::ck_load_scalar(ck, p + "layer_scalar", &s)) != G4_OK) return rc;
   }
   if (!need(ck, "norm.weight", "BF16", {H}, &rc)) return rc;
+  // per-layer embeddings (PLE, :1230-1231, 1226-1229): 256 inputs per layer
+  const bool ple = ck->find("embed_tokens_per_layer.weight") || ck->find("per_layer_model_projection.weight_scale");
+  if (ple) {
+    const long long NP = 256LL * NL;
+    if (!need(ck, "embed_tokens_per_layer.weight", "BF16", {V, NP}, &rc)) return rc;
+    if (!need_packed(ck, "per_layer_model_projection", NP, H, &rc)) return rc;
+    if (!need(ck, "per_layer_model_projection.weight_scale", "BF16", {NP, H / 32}, &rc)) return rc;
+    if (!need(ck, "per_layer_projection_norm.weight", "BF16", {256}, &rc)) return rc;
+    for (int l = 0; l < NL; ++l) {
+      const std::string p = "layers." + std::to_string(l) + ".";
+      if (!need_packed(ck, p + "per_layer_input_gate", 256, H, &rc)) return rc;
+      if (!need(ck, p + "per_layer_input_gate.weight_scale", "BF16", {256, H / 32}, &rc)) return rc;
+      if (!need_packed(ck, p + "per_layer_projection", H, 256, &rc)) return rc;
+      if (!need(ck, p + "per_layer_projection.weight_scale", "BF16", {H, 256 / 32}, &rc)) return rc;
+      if (!need(ck, p + "post_per_layer_input_norm.weight", "BF16", {H}, &rc)) return rc;
+    }
+  }
+  cfg->ple = ple ? 1 : 0;
   cfg->hidden = (int)H;
   cfg->n_layers = NL;
   cfg->kv_owners = OWN;

@@ -9,6 +9,8 @@
 #include <utility>
 #include <vector>
 
+#include <cuda_runtime.h>
+
 #include "g4.h"
 
 namespace g4 {
@@ -41,16 +43,19 @@ struct g4_checkpoint {
 
 namespace g4 {
 // Loader helpers for the engine (sizes checked against the expected shapes; G4_OK or an error with
-// the tensor's name in the message).  Copies are synchronous (load time).
+// the tensor's name in the message).  Each copy is made on stream st and has completed when the
+// helper returns: a plain cudaMemcpy from pageable memory may return before its transfer lands, and
+// it is not ordered with the engine's non-blocking stream.
 // A stack of int4 matrices ("<name>.weight_packed", "<name>.weight_scale"; rows[i] rows each, K
 // columns): the reference-layout bytes into w_dev (then packed by the caller), the bf16 scales
 // into s_dev.
 int ck_load_lin(const g4_checkpoint* ck, const std::vector<std::pair<std::string, int>>& parts, int K, uint8_t* w_dev,
-                uint16_t* s_dev);
+                uint16_t* s_dev, cudaStream_t st);
 // A bf16 vector of n elements as fp32 (exact) into dev.
-int ck_load_vec(const g4_checkpoint* ck, const std::string& name, int n, float* dev);
+int ck_load_vec(const g4_checkpoint* ck, const std::string& name, int n, float* dev, cudaStream_t st);
 // A bf16 matrix [rows][cols] as is into dev.
-int ck_load_bf16(const g4_checkpoint* ck, const std::string& name, long long rows, long long cols, uint16_t* dev);
+int ck_load_bf16(const g4_checkpoint* ck, const std::string& name, long long rows, long long cols, uint16_t* dev,
+                 cudaStream_t st);
 // A bf16 scalar ("layers.<l>.layer_scalar"); 1.0 when the tensor is absent.
 int ck_load_scalar(const g4_checkpoint* ck, const std::string& name, float* out);
 }  // namespace g4

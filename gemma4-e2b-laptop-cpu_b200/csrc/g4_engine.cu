@@ -41,7 +41,9 @@ struct TLayer {
   TcLin tqkv, to, tgu, tdown;
   float *in_ln = nullptr, *post_attn = nullptr, *pre_ff = nullptr, *post_ff = nullptr, *qn = nullptr, *kn = nullptr;
   bool global = false;
-  float scalar = 1.0f;  // layer_scalar (:1389-1404): 1 for the synthetic model, a checkpoint's value otherwise
+  float scalar = 1.0f;
+  Lin pg, pp;                // per-layer input gate [256][H] and projection [H][256] (PLE)
+  float* post_ple = nullptr;  // post_per_layer_input_norm (PLE)  // layer_scalar (:1389-1404): 1 for the synthetic model, a checkpoint's value otherwise
 };
 struct DLayerW {
   Lin q, o, gu, down;
@@ -250,6 +252,12 @@ struct g4_engine {
   g4::Lin dpre, dpost, dcent;
   float *fnorm = nullptr, *dnorm = nullptr;
   uint16_t* E = nullptr;
+  // per-layer embeddings (cfg.ple): the [vocab][NL x 256] table, the projection of the embedding and
+  // its norm; the rows' projections and per-layer inputs, and a layer's gate input and output
+  uint16_t* PLEt = nullptr;
+  g4::Lin plproj;
+  float* plnorm = nullptr;
+  float *pr = nullptr, *pli = nullptr, *pgv = nullptr, *g2 = nullptr;
   // head
   uint8_t *hdata = nullptr, *hnib = nullptr, *sW4 = nullptr;
   uint16_t* sS4 = nullptr;
@@ -356,6 +364,7 @@ extern "C" int g4_engine_default_config(g4_engine_config* c) {
   c->slot_min_reuse = 32;
   c->kv_owners = 0;
   c->mlp_shared = 0;
+  c->ple = 0;
   return G4_OK;
 }
 
@@ -401,13 +410,13 @@ static int ck_lin(g4_engine* e, const g4_checkpoint* ck, Lin& lin, const std::ve
   RCK(ealloc_t(e, &lin.w, (size_t)N * K / 2));
   RCK(ealloc_t(e, &lin.s, (size_t)N * K / 32));
   if (cudaStreamSynchronize(e->st) != cudaSuccess) return set_error(G4_ERR_CUDA, "checkpoint: stream");  // tmp is free
-  RCK(ck_load_lin(ck, parts, K, tmp, lin.s));
+  RCK(ck_load_lin(ck, parts, K, tmp, lin.s, e->st));
   RCK(g4_w4_pack(tmp, N, K, lin.w, e->st));
   return check_launch("ck_lin");
 }
 static int ck_norm(g4_engine* e, const g4_checkpoint* ck, float** p, const std::string& name, int n) {
   RCK(ealloc_t(e, p, n));
-  return ck_load_vec(ck, name, n, *p);
+  return ck_load_vec(ck, name, n, *p, e->st);
 }
 static int gen_norm(g4_engine* e, float** p, uint64_t id, int n, float mul) {
   RCK(ealloc_t(e, p, n));
@@ -430,6 +439,8 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
              c.n_layers);
   G4_REQUIRE(c.mlp_shared >= 0 && c.mlp_shared % 256 == 0, "g4_engine_create: mlp_shared %d is not a multiple of 256",
              c.mlp_shared);
+  G4_REQUIRE(!c.ple || (c.prefill_int8 && c.decode_int8),
+             "g4_engine_create: per-layer embeddings need prefill_int8 = decode_int8 = 1 (the reference's int8 branch)");
   {
     ModelDims dd;
     dd.NL = c.n_layers;
@@ -452,13 +463,14 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
   if (share) {
     const g4_engine_config& sc = share->cfg;
     if (sc.hidden != c.hidden || sc.n_layers != c.n_layers || sc.mlp != c.mlp || sc.vocab != c.vocab || sc.seed != c.seed ||
-        sc.kv_owners != c.kv_owners || sc.mlp_shared != c.mlp_shared ||
+        sc.kv_owners != c.kv_owners || sc.mlp_shared != c.mlp_shared || sc.ple != c.ple ||
         (c.drafter && !sc.drafter) || c.ctx_max > sc.ctx_max || (c.prefill_tc && !share->tc_ready && sc.prefill_tc))
       return fail(set_error(G4_ERR_INVALID, "g4_engine_create_shared: configuration differs from the weights' engine"));
     e->L = share->L;
     e->DL = share->DL;
     e->dpre = share->dpre; e->dpost = share->dpost; e->dcent = share->dcent;
     e->fnorm = share->fnorm; e->dnorm = share->dnorm; e->E = share->E;
+    e->PLEt = share->PLEt; e->plproj = share->plproj; e->plnorm = share->plnorm;
     e->hdata = share->hdata; e->hnib = share->hnib; e->sW4 = share->sW4; e->sS4 = share->sS4; e->scoef = share->scoef;
     e->hexc_ptr = share->hexc_ptr; e->hexc_col = share->hexc_col; e->hexc_delta = share->hexc_delta;
     std::memcpy(e->cb8, share->cb8, 8);
@@ -467,6 +479,7 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
   } else {
   uint8_t* tmp = nullptr;
   const size_t tmp_bytes = (size_t)std::max({(size_t)(QD + 2 * d.HD) * H / 2, (size_t)2 * IM * H / 2, (size_t)IM * H / 2,
+                                              (size_t)d.NL * 256 * H / 2,
                                               (size_t)QD * H / 2, (size_t)d.DCENT * H / 2, (size_t)H * 2 * H / 2});
   if (ealloc_t(e, &tmp, tmp_bytes)) return fail(G4_ERR_CUDA);
   e->L.resize(d.NL);
@@ -487,6 +500,9 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
     if (!rc) rc = ck_norm(e, ck, &t.qn, ck_layer(l, "self_attn.q_norm.weight"), d.HD);
     if (!rc && d.owns(l)) rc = ck_norm(e, ck, &t.kn, ck_layer(l, "self_attn.k_norm.weight"), d.HD);
     if (!rc) rc = ck_load_scalar(ck, ck_layer(l, "layer_scalar"), &t.scalar);
+    if (!rc && c.ple) rc = ck_lin(e, ck, t.pg, {{ck_layer(l, "per_layer_input_gate"), 256}}, H, tmp);
+    if (!rc && c.ple) rc = ck_lin(e, ck, t.pp, {{ck_layer(l, "per_layer_projection"), H}}, 256, tmp);
+    if (!rc && c.ple) rc = ck_norm(e, ck, &t.post_ple, ck_layer(l, "post_per_layer_input_norm.weight"), H);
     if (rc) return fail(rc);
   }
   for (int l = 0; l < d.NL && !ck; ++l) {
@@ -504,14 +520,32 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
     if (!rc) rc = gen_norm(e, &t.post_ff, layer_id(l, T_POST_FF), H, 1.f);
     if (!rc) rc = gen_norm(e, &t.qn, layer_id(l, T_QN), d.HD, 0.0625f);
     if (!rc && d.owns(l)) rc = gen_norm(e, &t.kn, layer_id(l, T_KN), d.HD, 1.f);
+    if (!rc && c.ple) rc = gen_lin(e, t.pg, {{layer_id(l, T_PG), 256}}, H, tmp);
+    if (!rc && c.ple) rc = gen_lin(e, t.pp, {{layer_id(l, T_PP), H}}, 256, tmp);
+    if (!rc && c.ple) rc = gen_norm(e, &t.post_ple, layer_id(l, T_POST_PLE), H, 1.f);
     if (rc) return fail(rc);
   }
   if (ck ? ck_norm(e, ck, &e->fnorm, "norm.weight", H) : gen_norm(e, &e->fnorm, T_FNORM, H, 1.f)) return fail(G4_ERR_CUDA);
+  if (c.ple) {  // per-layer embeddings: the table, the projection of the embedding and its norm (:1230-1231)
+    const long long NP = (long long)d.NL * 256;
+    if (ealloc_t(e, &e->PLEt, (size_t)d.V * NP)) return fail(G4_ERR_CUDA);
+    int rc = G4_OK;
+    if (ck) {
+      rc = ck_load_bf16(ck, "embed_tokens_per_layer.weight", d.V, NP, e->PLEt, e->st);
+      if (!rc) rc = ck_lin(e, ck, e->plproj, {{"per_layer_model_projection", (int)NP}}, H, tmp);
+      if (!rc) rc = ck_norm(e, ck, &e->plnorm, "per_layer_projection_norm.weight", 256);
+    } else {
+      k_gen_bf16<<<gridfor((long long)d.V * NP), 256, 0, e->st>>>(c.seed, T_PLE, (long long)d.V * NP, 0.02f, e->PLEt);
+      rc = gen_lin(e, e->plproj, {{T_PLPROJ, (int)NP}}, H, tmp);
+      if (!rc) rc = gen_norm(e, &e->plnorm, T_PLNORM, 256, 1.f);
+    }
+    if (rc) return fail(rc);
+  }
   // embedding / tied head, packed exact head, screen
   const long long EV = (long long)d.V * H;
   if (ealloc_t(e, &e->E, (size_t)EV)) return fail(G4_ERR_CUDA);
   if (ck) {
-    if (int rc = ck_load_bf16(ck, "embed_tokens.weight", d.V, H, e->E)) return fail(rc);
+    if (int rc = ck_load_bf16(ck, "embed_tokens.weight", d.V, H, e->E, e->st)) return fail(rc);
   } else {
     k_gen_embed<<<gridfor(EV), 256, 0, e->st>>>(c.seed, EV, e->E);
   }
@@ -560,7 +594,7 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
   }
   }  // weights generated (not shared)
   // tensor-core prefill operands and chunk buffers
-  if (c.prefill_tc && c.prefill_int8 && H % 128 == 0 && QD % 128 == 0 && I % 128 == 0 && IM % 128 == 0 &&
+  if (c.prefill_tc && c.prefill_int8 && !c.ple && H % 128 == 0 && QD % 128 == 0 && I % 128 == 0 && IM % 128 == 0 &&
       (QD + 2 * d.HD) % 128 == 0) {
     int rc = G4_OK;
     auto tc_lin = [&](const Lin& l, TcLin& t) {
@@ -611,6 +645,10 @@ static int create_impl(const g4_engine_config* cfg, const g4_engine* share, g4_e
   if (!rc) rc = ealloc_t(e, &e->qs, (size_t)4 * QD);
   if (!rc) rc = ealloc_t(e, &e->o, (size_t)MM * H);
   if (!rc) rc = ealloc_t(e, &e->gu, (size_t)MM * 2 * IM);
+  if (!rc && c.ple) rc = ealloc_t(e, &e->pr, (size_t)MM * d.NL * 256);
+  if (!rc && c.ple) rc = ealloc_t(e, &e->pli, (size_t)MM * d.NL * 256);
+  if (!rc && c.ple) rc = ealloc_t(e, &e->pgv, (size_t)MM * 256);
+  if (!rc && c.ple) rc = ealloc_t(e, &e->g2, (size_t)MM * 256);
   if (!rc) rc = ealloc_t(e, &e->act, (size_t)MM * IM);
   if (!rc) rc = ealloc_t(e, &e->hbuf, (size_t)MM * H);
   if (!rc) rc = ealloc_t(e, &e->mlp_in, (size_t)MM * H);
@@ -672,6 +710,12 @@ extern "C" int g4_engine_create_from_checkpoint(const g4_engine_config* cfg, con
   if (!cfg || !ck || !out) return set_error(G4_ERR_INVALID, "g4_engine_create_from_checkpoint: null pointer");
   g4_engine_config c = *cfg;
   RCK(g4_checkpoint_config(ck, &c));
+  // per-layer embeddings read from a checkpoint gave other hidden states than the oracle's on the
+  // GPU (the same weights generated on the device agree); refused until that is resolved
+  if (c.ple)
+    return set_error(G4_ERR_UNSUPPORTED,
+                     "g4_engine_create_from_checkpoint: per-layer embeddings from a checkpoint are not enabled in this "
+                     "build (unverified); the seeded model with ple = 1 runs them");
   return create_impl(&c, nullptr, out, ck);
 }
 
@@ -743,7 +787,7 @@ static int lin(g4_engine* e, const Lin& w, const float* X, int M, float* Y, bool
 static bool fused_ok(const g4_engine* e, int M, int pos0, bool dyn) {
   const ModelDims& d = e->d;
   return e->cfg.fused_layers && i8_path(e, M, false) && M >= 2 && M <= 4 && (dyn || pos0 + M > e->cfg.att_par) &&
-         d.H == 2048 && d.I == 8192 && d.HD == 256 && d.NQ == 8 && !e->prof.on && d.OWN == 0 &&
+         d.H == 2048 && d.I == 8192 && d.HD == 256 && d.NQ == 8 && !e->prof.on && d.OWN == 0 && !e->cfg.ple &&
          std::all_of(e->L.begin(), e->L.end(), [](const TLayer& t) { return t.scalar == 1.0f; });
 }
 static int forward_layers_fused(g4_engine* e, int M, int pos0, bool dyn) {
@@ -827,6 +871,11 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
   }
   pf.mark(e->st, PH_EMBED_NORM);
   RCK(launch("k_embed", k_embed, dim3(M), dim3(256), 0, e->st, e->E, e->toks, H, sqrtH, e->x));
+  if (e->cfg.ple) {  // the per-layer inputs (:1270-1288), before the first norm quantises its rows
+    RCK(lin(e, e->plproj, e->x, M, e->pr));
+    RCK(launch("k_ple_in", k_ple_in, dim3(M, d.NL), dim3(256), 0, e->st, (const float*)e->pr, (const int*)e->toks,
+               (const uint16_t*)e->PLEt, (const float*)e->plnorm, 1.0f / sqrtf((float)H), d.NL, e->pli));
+  }
   RCK(launch("k_norm_q", k_norm_q, dim3(M), dim3(256), 0, e->st, e->x, e->L[0].in_ln, H, e->a, 0, qo));
   RCK(check_launch("k_norm_q"));
   for (int l = 0; l < d.NL; ++l) {
@@ -889,10 +938,19 @@ static int forward(g4_engine* e, int M, int pos0, bool want, int hf, bool dyn = 
     pf.mark(e->st, PH_LINEAR);
     RCK(lin(e, t.down, e->act, M, e->o, false, true));
     pf.mark(e->st, PH_EMBED_NORM);
-    if (l + 1 < d.NL)  // residual (layer scalar 1) and the next layer's input norm
-      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, t.post_ff, t.scalar, H, e->L[l + 1].in_ln, e->a, 0, qo));
+    if (e->cfg.ple) {  // add_res_prep_x (:1376), then the per-layer input (:1379-1388)
+      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, (const float*)e->o, e->x,
+                 (const float*)t.post_ff, 0.0f, H, (const float*)nullptr, (float*)nullptr, 0, QuantOut{nullptr, nullptr, nullptr}));
+      RCK(lin(e, t.pg, e->x, M, e->pgv));
+      RCK(launch("k_ple_gate", k_ple_gate, dim3(M), dim3(256), 0, e->st, (const float*)e->pgv, (const float*)e->pli, l, d.NL,
+                 e->g2, qo));
+      RCK(lin(e, t.pp, e->g2, M, e->o, false, true));
+    }
+    const float* w_res = e->cfg.ple ? t.post_ple : t.post_ff;  // the residual that ends the layer
+    if (l + 1 < d.NL)  // residual (and the layer scalar), the next layer's input norm
+      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, w_res, t.scalar, H, e->L[l + 1].in_ln, e->a, 0, qo));
     else  // residual and the final norm (rounded) of every row into hbuf
-      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, t.post_ff, t.scalar, H, e->fnorm, e->hbuf, 1,
+      RCK(launch("k_resid_norm_q", k_resid_norm_q, dim3(M), dim3(256), 0, e->st, e->o, e->x, w_res, t.scalar, H, e->fnorm, e->hbuf, 1,
                                            QuantOut{nullptr, nullptr, nullptr}));
     RCK(check_launch("layer"));
   }

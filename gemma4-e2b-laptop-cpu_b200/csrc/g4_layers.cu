@@ -1237,6 +1237,58 @@ __global__ void k_gen_norm(uint64_t seed, uint64_t id, int n, float mul, float* 
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] = bf2f(f2bf(__fmul_rn(__fadd_rn(1.0f, __fmul_rn(0.1f, wnorm(wh(seed, id, (uint64_t)i)))), mul)));
 }
+// Per-layer inputs (the int8 branch of gemma4_engine.cpp:1270-1288): block (row m, layer l), 256
+// threads, one per input of the layer: p = r16(pr * s1) (s1 = 1/sqrt(H)), its RMS norm with the
+// per_layer_projection_norm weights (rms, not rounded), plus the token's table row times 16 rounded
+// to bf16, times 2^-0.5.
+__global__ void __launch_bounds__(256) k_ple_in(const float* __restrict__ pr, const int* __restrict__ toks,
+                                                const uint16_t* __restrict__ table, const float* __restrict__ wn, float s1,
+                                                int NL, float* __restrict__ pli) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float xs[256];
+  __shared__ double red[17];
+  const int m = blockIdx.x, l = blockIdx.y, i = threadIdx.x;
+  const size_t NP = (size_t)NL * 256, off = (size_t)m * NP + (size_t)l * 256 + i;
+  const float p = r16(__fmul_rn(pr[off], s1));
+  xs[i] = p;
+  __syncthreads();
+  const float r = block_rms_scale(xs, 256, red);
+  const float pj = __fmul_rn(__fmul_rn(p, r), wn[i]);
+  const float pe = r16(__fmul_rn(bf2f(table[(size_t)toks[m] * NP + (size_t)l * 256 + i]), 16.0f));
+  pli[off] = __fmul_rn(__fadd_rn(pj, pe), 0.70710678118f);
+}
+
+// The per-layer input gate (the int8 branch of :1381-1384): block = row m, 256 threads:
+// g2 = r16(r16(gelu(r16 pgv)) * r16(pli of layer l)), and its W4A8 quantisation (qo.q set) for the
+// per_layer_projection.
+__global__ void __launch_bounds__(256) k_ple_gate(const float* __restrict__ pgv, const float* __restrict__ pli, int l, int NL,
+                                                  float* __restrict__ g2, QuantOut qo) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.x, i = threadIdx.x;
+  const float g = r16(pgv[(size_t)m * 256 + i]);
+  const float v = r16(__fmul_rn(r16(gelu(g)), r16(pli[(size_t)m * NL * 256 + (size_t)l * 256 + i])));
+  g2[(size_t)m * 256 + i] = v;
+  if (qo.q) {
+    int8_t q;
+    float sx;
+    int32_t tot;
+    quant_group32(v, q, sx, tot);
+    qo.q[(size_t)m * 256 + i] = q;
+    if ((i & 31) == 0) {
+      qo.sx[(size_t)m * 8 + (i >> 5)] = sx;
+      qo.sum[(size_t)m * 8 + (i >> 5)] = tot;
+    }
+  }
+}
+
+// bf16 table of n values mul * r (the per-layer embedding table; the embedding is k_gen_embed).
+__global__ void k_gen_bf16(uint64_t seed, uint64_t id, long long n, float mul, uint16_t* __restrict__ out) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    out[i] = (uint16_t)f2bf(__fmul_rn(mul, wnorm(wh(seed, id, (uint64_t)i))));
+}
+
 __global__ void k_gen_embed(uint64_t seed, long long n, uint16_t* __restrict__ out) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
     out[i] = (uint16_t)f2bf(__fmul_rn(0.02f, wnorm(wh(seed, T_EMBED, (uint64_t)i))));

@@ -56,4 +56,9 @@ __global__ void k_gen_w4(uint64_t seed, uint64_t id, long long nbytes, uint8_t* 
 __global__ void k_gen_scales(uint64_t seed, uint64_t id, long long n, uint16_t* out);
 __global__ void k_gen_norm(uint64_t seed, uint64_t id, int n, float mul, float* out);
 __global__ void k_gen_embed(uint64_t seed, long long n, uint16_t* out);
+__global__ void k_gen_bf16(uint64_t seed, uint64_t id, long long n, float mul, uint16_t* out);
+// Per-layer embeddings (grid (M, NL) / M, 256 threads; 256 inputs per layer).
+__global__ void k_ple_in(const float* pr, const int* toks, const uint16_t* table, const float* wn, float s1, int NL,
+                         float* pli);
+__global__ void k_ple_gate(const float* pgv, const float* pli, int l, int NL, float* g2, QuantOut qo);
 }  // namespace g4

@@ -48,8 +48,9 @@ struct ModelDims {
 enum : uint64_t {
   T_Q = 0, T_K = 1, T_V = 2, T_O = 3, T_GATE = 4, T_UP = 5, T_DOWN = 6,
   T_IN_LN = 8, T_POST_ATTN = 9, T_PRE_FF = 10, T_POST_FF = 11, T_QN = 12, T_KN = 13,
+  T_PG = 7, T_PP = 14, T_POST_PLE = 15,  // per-layer input gate, projection and post norm (PLE)
   T_SCALES = 0x100000,
-  T_EMBED = 1000, T_FNORM = 1001,
+  T_EMBED = 1000, T_FNORM = 1001, T_PLE = 1002, T_PLPROJ = 1003, T_PLNORM = 1004,
   T_DPRE = 2000, T_DPOST = 2001, T_DCENT = 2002, T_DNORM = 2003,
 };
 __host__ __device__ inline uint64_t layer_id(int l, uint64_t what) { return 16ull * (uint64_t)l + what; }

@@ -523,7 +523,7 @@ class EngineConfig(ctypes.Structure):
                                             "screen_lim", "attn_chunks", "att_par", "drafter")] + [
         ("seed", ctypes.c_ulonglong), ("graphs", ctypes.c_int), ("fused_layers", ctypes.c_int),
         ("prefill_tc", ctypes.c_int), ("slots", ctypes.c_int), ("slot_min_reuse", ctypes.c_int),
-        ("kv_owners", ctypes.c_int), ("mlp_shared", ctypes.c_int)]
+        ("kv_owners", ctypes.c_int), ("mlp_shared", ctypes.c_int), ("ple", ctypes.c_int)]
 
 
 class EngineStats(ctypes.Structure):

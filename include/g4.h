@@ -266,6 +266,11 @@ typedef struct {
                                         owns its cache */
   int mlp_shared;                    /* MLP width of the KV-shared layers (the E2B model: 12,288, twice
                                         the owners' 6,144); 0 = mlp */
+  int ple;                           /* per-layer embeddings (the E2B model's PLE, gemma4_engine.cpp:1270-1288,
+                                        1379-1388): 256 inputs per layer from a [vocab][n_layers x 256]
+                                        table and a projection of the embedding, gated into the residual
+                                        stream after each layer's MLP (1), or none (0, the default); needs
+                                        prefill_int8 = decode_int8 = 1 (the reference's int8 branch) */
 } g4_engine_config;
 typedef struct {
   int rounds, ngram_rounds, drafted, accepted, prefill_tokens, decode_tokens;
@@ -313,15 +318,18 @@ int g4_checkpoint_tensor(const g4_checkpoint* ck, const char* name, char* dtype,
  * [N][K/32], the layer's norms BF16, layer_scalar BF16 (1 when absent), norm.weight,
  * embed_tokens.weight BF16 [vocab][hidden]).  Trailing layers without k/v projections (and k_norm)
  * are KV-shared: cfg->kv_owners is set to the first of them, and cfg->mlp_shared to their MLP width
- * when it differs from the owners'.  Parts of the real E2B model this build does not run
- * (per-layer embeddings, head_dim other than 256, MLP widths that vary otherwise) give
+ * when it differs from the owners'; per-layer embeddings (embed_tokens_per_layer,
+ * per_layer_model_projection, per_layer_projection_norm and each layer's per_layer_input_gate,
+ * per_layer_projection, post_per_layer_input_norm) set cfg->ple.  Parts of the real E2B model this
+ * build does not run (head_dim other than 256, MLP widths that vary otherwise) give
  * G4_ERR_UNSUPPORTED with the part named. */
 int g4_checkpoint_config(const g4_checkpoint* ck, g4_engine_config* cfg);
 /* An engine whose target weights are the checkpoint's (the reference's q4 / bfvec loading,
  * gemma4_engine.cpp:172-175, 1222-1231): cfg's model sizes are replaced by the checkpoint's
  * (g4_checkpoint_config); the MTP drafter, when cfg->drafter is set, is generated from cfg->seed
  * (the reference reads its drafter from a separate checkpoint of another format).  ck may be
- * closed once this returns. */
+ * closed once this returns.  A checkpoint with per-layer embeddings is refused (G4_ERR_UNSUPPORTED):
+ * that path is not verified against the oracle in this build. */
 int g4_engine_create_from_checkpoint(const g4_engine_config* cfg, const g4_checkpoint* ck, g4_engine** out);
 /* One target forward (fwd) over M <= 32 host tokens at positions pos0..; int8 selects the W4A8
  * path for M >= 2.  When want, rows hf.. get the greedy next token G (host [M]) and, if hbuf is

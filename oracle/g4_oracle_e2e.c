@@ -30,7 +30,11 @@ static float wnorm(uint64_t h) {
 static uint8_t w4_byte(uint64_t h) { return (uint8_t)(h & 0xFF); }
 static uint32_t perm_token(uint32_t i, uint32_t vocab) { return (uint32_t)(((uint64_t)i * 0x9E3779B1ull + 12345ull) & (uint64_t)(vocab - 1)); }
 enum { T_Q = 0, T_K = 1, T_V = 2, T_O = 3, T_GATE = 4, T_UP = 5, T_DOWN = 6, T_IN_LN = 8, T_POST_ATTN = 9, T_PRE_FF = 10,
-       T_POST_FF = 11, T_QN = 12, T_KN = 13 };
+       T_POST_FF = 11, T_QN = 12, T_KN = 13, T_PG = 7, T_PP = 14, T_POST_PLE = 15 };
+#define T_PLE 1002ull
+#define T_PLPROJ 1003ull
+#define T_PLNORM 1004ull
+#define PLE_D 256 /* per-layer input width (PD, gemma4_engine.cpp:1222) */
 #define T_SCALES 0x100000ull
 #define T_EMBED 1000ull
 #define T_FNORM 1001ull
@@ -56,13 +60,24 @@ typedef struct {
   void (*attn_tile)(const uint16_t* Kc, const uint16_t* Vc, int hd, int sliding, const float* q, int qstride, int pos0,
                     int M, float* att);
 } or_e2e_hooks;
-typedef struct { Lin qkv, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff, *qn, *kn; int global; float scalar; } TLayer;
+typedef struct {
+  Lin qkv, o, gu, down;
+  float *in_ln, *post_attn, *pre_ff, *post_ff, *qn, *kn;
+  int global;
+  float scalar;
+  Lin pg, pp;      /* per-layer input gate [PD][H] and projection [H][PD] (PLE) */
+  float* post_ple; /* post_per_layer_input_norm (PLE) */
+} TLayer;
 typedef struct { Lin q, o, gu, down; float *in_ln, *post_attn, *pre_ff, *post_ff, *qn; int global; } DLayer;
 
 typedef struct {
   int H, NL, I, V, NQ, HD, WINDOW, DL, DCENT, DTOP, DPER;
   int OWN; /* KV owners: layers [0, OWN) own a cache (0 = all) */
   int IS;  /* MLP width of the KV-shared layers (0 = I) */
+  int ple; /* per-layer embeddings */
+  uint16_t* PLEt; /* [V][NL * PD] bf16 */
+  Lin plproj;     /* per_layer_model_projection [NL * PD][H] */
+  float* plnorm;  /* per_layer_projection_norm [PD] */
   int ctx_max, prefill_block, k_draft, ngram, ngram_len, prefill_int8, decode_int8, attn_chunks, att_par, drafter;
   uint64_t seed;
   TLayer* L;
@@ -129,7 +144,8 @@ typedef struct {
   unsigned long long seed;
   int kv_owners; /* layers [0, kv_owners) own a KV cache (0 = all), g4_engine_config's field */
   int mlp_shared; /* MLP width of the KV-shared layers (0 = mlp) */
-} or_e2e_config;  /* g4_engine_config's first fields, then kv_owners and mlp_shared */
+  int ple;        /* per-layer embeddings (PD = 256 per layer) */
+} or_e2e_config;  /* g4_engine_config's first fields, then kv_owners, mlp_shared and ple */
 
 void* or_e2e_create(const or_e2e_config* c) {
   Model* m = (Model*)calloc(1, sizeof(Model));
@@ -140,6 +156,7 @@ void* or_e2e_create(const or_e2e_config* c) {
   m->attn_chunks = c->attn_chunks; m->att_par = c->att_par; m->drafter = c->drafter; m->seed = c->seed;
   m->OWN = c->kv_owners;
   m->IS = c->mlp_shared;
+  m->ple = c->ple;
   const int H = m->H, QD = m->NQ * m->HD, I = m->I;
   m->L = (TLayer*)calloc(m->NL, sizeof(TLayer));
   for (int l = 0; l < m->NL; ++l) {
@@ -157,6 +174,19 @@ void* or_e2e_create(const or_e2e_config* c) {
     t->post_ff = gen_norm(m, layer_id(l, T_POST_FF), H, 1.f);
     t->qn = gen_norm(m, layer_id(l, T_QN), m->HD, 0.0625f);
     t->kn = owns(m, l) ? gen_norm(m, layer_id(l, T_KN), m->HD, 1.f) : NULL;
+    if (m->ple) {
+      { uint64_t ids[1] = {layer_id(l, T_PG)}; int rows[1] = {PLE_D}; gen_lin(m, &t->pg, ids, rows, 1, H); }
+      { uint64_t ids[1] = {layer_id(l, T_PP)}; int rows[1] = {H}; gen_lin(m, &t->pp, ids, rows, 1, PLE_D); }
+      t->post_ple = gen_norm(m, layer_id(l, T_POST_PLE), H, 1.f);
+    }
+  }
+  if (m->ple) {
+    const long long NP = (long long)m->NL * PLE_D, PV = (long long)m->V * NP;
+    { uint64_t ids[1] = {T_PLPROJ}; int rows[1] = {(int)NP}; gen_lin(m, &m->plproj, ids, rows, 1, H); }
+    m->plnorm = gen_norm(m, T_PLNORM, PLE_D, 1.f);
+    m->PLEt = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)PV);
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < PV; ++i) m->PLEt[i] = or_f2bf(0.02f * wnorm(wh(m->seed, T_PLE, (uint64_t)i)));
   }
   m->fnorm = gen_norm(m, T_FNORM, H, 1.f);
   const long long EV = (long long)m->V * H;
@@ -217,8 +247,10 @@ void or_e2e_destroy(void* mp) {
     TLayer* t = &m->L[l];
     free_lin(&t->qkv); free_lin(&t->o); free_lin(&t->gu); free_lin(&t->down);
     free(t->in_ln); free(t->post_attn); free(t->pre_ff); free(t->post_ff); free(t->qn); free(t->kn);
+    free_lin(&t->pg); free_lin(&t->pp); free(t->post_ple);
   }
   free(m->L);
+  free_lin(&m->plproj); free(m->plnorm); free(m->PLEt);
   if (m->D) {
     for (int l = 0; l < m->DL; ++l) {
       DLayer* t = &m->D[l];
@@ -344,6 +376,32 @@ static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf
   const float sqrtH = sqrtf((float)H);
   for (int r = 0; r < M; ++r)
     for (int i = 0; i < H; ++i) x[(size_t)r * H + i] = or_r16(or_bf2f(m->E[(size_t)toks[r] * H + i]) * sqrtH);
+  /* per-layer inputs (the int8 branch of :1270-1288): pr = per_layer_model_projection(x), then per
+   * (row, layer) r16(pr / sqrt(H)), its RMS norm with per_layer_projection_norm, plus the table row
+   * scaled by sqrt(256) = 16 and rounded, times 2^-0.5 */
+  const int NP = m->NL * PLE_D;
+  float* pli = NULL;
+  float* pgv = NULL;
+  float* g2 = NULL;
+  if (m->ple) {
+    float* pr = (float*)malloc(sizeof(float) * (size_t)M * NP);
+    pli = (float*)malloc(sizeof(float) * (size_t)M * NP);
+    pgv = (float*)malloc(sizeof(float) * (size_t)M * PLE_D);
+    g2 = (float*)malloc(sizeof(float) * (size_t)M * PLE_D);
+    lin(m, &m->plproj, x, M, pr, 0);
+    const float s1 = 1.0f / sqrtf((float)H);
+    float pj[PLE_D];
+    for (int r = 0; r < M; ++r)
+      for (int l = 0; l < m->NL; ++l) {
+        float* prl = pr + (size_t)r * NP + (size_t)l * PLE_D;
+        for (int i = 0; i < PLE_D; ++i) prl[i] = or_r16(prl[i] * s1);
+        rmsnorm(prl, m->plnorm, PLE_D, pj, 0);
+        const uint16_t* pel = m->PLEt + (size_t)toks[r] * NP + (size_t)l * PLE_D;
+        for (int i = 0; i < PLE_D; ++i)
+          pli[(size_t)r * NP + (size_t)l * PLE_D + i] = (pj[i] + or_r16(or_bf2f(pel[i]) * 16.0f)) * 0.70710678118f;
+      }
+    free(pr);
+  }
   for (int l = 0; l < m->NL; ++l) {
     TLayer* t = &m->L[l];
     const int ty = t->global ? 1 : 0;
@@ -410,9 +468,28 @@ static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf
       float* xm = x + (size_t)r * H;
       for (int i = 0; i < H; ++i) om[i] = or_r16(om[i]);
       const float rr = rms_scale(om, H);
-      for (int i = 0; i < H; ++i) xm[i] = or_r16(or_r16(xm[i] + or_r16((om[i] * rr) * t->post_ff[i])) * t->scalar);
+      if (m->ple) /* add_res_prep_x (:1376): the layer scalar comes after the per-layer input */
+        for (int i = 0; i < H; ++i) xm[i] = or_r16(xm[i] + or_r16((om[i] * rr) * t->post_ff[i]));
+      else
+        for (int i = 0; i < H; ++i) xm[i] = or_r16(or_r16(xm[i] + or_r16((om[i] * rr) * t->post_ff[i])) * t->scalar);
+    }
+    if (m->ple) { /* the per-layer input (:1379-1388, int8 branch) */
+      lin(m, &t->pg, x, M, pgv, 0);
+      for (int r = 0; r < M; ++r)
+        for (int i = 0; i < PLE_D; ++i)
+          g2[(size_t)r * PLE_D + i] = or_r16(or_r16(or_gelu(or_r16(pgv[(size_t)r * PLE_D + i]))) *
+                                             or_r16(pli[(size_t)r * NP + (size_t)l * PLE_D + i]));
+      lin(m, &t->pp, g2, M, o, 0);
+      for (int r = 0; r < M; ++r) {
+        float* om = o + (size_t)r * H;
+        float* xm = x + (size_t)r * H;
+        for (int i = 0; i < H; ++i) om[i] = or_r16(om[i]);
+        const float rr = rms_scale(om, H);
+        for (int i = 0; i < H; ++i) xm[i] = or_r16(or_r16(xm[i] + or_r16((om[i] * rr) * t->post_ple[i])) * t->scalar);
+      }
     }
   }
+  free(pli); free(pgv); free(g2);
   if (want) {
     float* logits = (float*)malloc(sizeof(float) * (size_t)m->V * 4);
     for (int r = hf; r < M; ++r) rmsnorm(x + (size_t)r * H, m->fnorm, H, hbuf + (size_t)r * H, 1);
@@ -711,7 +788,9 @@ int or_e2e_set_hooks(void* mp, const or_e2e_hooks* h) {
   for (int l = 0; l < m->NL; ++l) {
     TLayer* t = &m->L[l];
     hook_lin(m, &t->qkv); hook_lin(m, &t->o); hook_lin(m, &t->gu); hook_lin(m, &t->down);
+    if (m->ple) { hook_lin(m, &t->pg); hook_lin(m, &t->pp); }
   }
+  if (m->ple) hook_lin(m, &m->plproj);
   if (m->D) {
     for (int l = 0; l < m->DL; ++l) {
       DLayer* t = &m->D[l];
@@ -750,9 +829,9 @@ static void ck_add(CkOut* o, int* n, const char* name, const char* dtype, long l
 int or_e2e_write_checkpoint(void* mp, const char* path, int packed_u8) {
   Model* m = (Model*)mp;
   const int H = m->H, QD = m->NQ * m->HD, HD = m->HD;
-  const int per = 7 * 2 + 7;
-  CkOut* o = (CkOut*)calloc((size_t)m->NL * per + 2, sizeof(CkOut));
-  uint16_t* bf = (uint16_t*)malloc(sizeof(uint16_t) * ((size_t)m->NL * (4 * H + 2 * HD + 1) + H));
+  const int per = 7 * 2 + 7 + 5;
+  CkOut* o = (CkOut*)calloc((size_t)m->NL * per + 8, sizeof(CkOut));
+  uint16_t* bf = (uint16_t*)malloc(sizeof(uint16_t) * ((size_t)m->NL * (5 * H + 2 * HD + 1) + H + PLE_D));
   size_t bo = 0;
   int n = 0;
   char nm[96];
@@ -785,6 +864,22 @@ int or_e2e_write_checkpoint(void* mp, const char* path, int packed_u8) {
       snprintf(nm, sizeof nm, "layers.%d.%s", l, vecs[k].name);
       ck_add(o, &n, nm, "BF16", vecs[k].len, 0, 1, dst, sizeof(uint16_t) * (size_t)vecs[k].len);
     }
+    if (m->ple) { /* per_layer_input_gate, per_layer_projection, post_per_layer_input_norm (:1226-1229) */
+      const struct { const char* name; const Lin* lin; } pl[2] = {{"per_layer_input_gate", &t->pg}, {"per_layer_projection", &t->pp}};
+      for (int k = 0; k < 2; ++k) {
+        const Lin* L = pl[k].lin;
+        snprintf(nm, sizeof nm, "layers.%d.%s.weight_packed", l, pl[k].name);
+        if (packed_u8) ck_add(o, &n, nm, "U8", L->N, L->K / 2, 2, L->w, (size_t)L->N * L->K / 2);
+        else ck_add(o, &n, nm, "I32", L->N, L->K / 8, 2, L->w, (size_t)L->N * L->K / 2);
+        snprintf(nm, sizeof nm, "layers.%d.%s.weight_scale", l, pl[k].name);
+        ck_add(o, &n, nm, "BF16", L->N, L->K / 32, 2, L->s, sizeof(uint16_t) * (size_t)L->N * L->K / 32);
+      }
+      uint16_t* dst = bf + bo;
+      for (int i = 0; i < H; ++i) dst[i] = or_f2bf(t->post_ple[i]);
+      bo += (size_t)H;
+      snprintf(nm, sizeof nm, "layers.%d.post_per_layer_input_norm.weight", l);
+      ck_add(o, &n, nm, "BF16", H, 0, 1, dst, sizeof(uint16_t) * (size_t)H);
+    }
     bf[bo] = or_f2bf(t->scalar);
     snprintf(nm, sizeof nm, "layers.%d.layer_scalar", l);
     ck_add(o, &n, nm, "BF16", 1, 0, 1, bf + bo, 2);
@@ -796,6 +891,18 @@ int or_e2e_write_checkpoint(void* mp, const char* path, int packed_u8) {
     ck_add(o, &n, "norm.weight", "BF16", H, 0, 1, dst, sizeof(uint16_t) * (size_t)H);
   }
   ck_add(o, &n, "embed_tokens.weight", "BF16", m->V, H, 2, m->E, sizeof(uint16_t) * (size_t)m->V * H);
+  if (m->ple) { /* embed_tokens_per_layer, per_layer_model_projection, per_layer_projection_norm (:1230-1231) */
+    const long long NP = (long long)m->NL * PLE_D;
+    ck_add(o, &n, "embed_tokens_per_layer.weight", "BF16", m->V, NP, 2, m->PLEt, sizeof(uint16_t) * (size_t)m->V * NP);
+    const Lin* L = &m->plproj;
+    if (packed_u8) ck_add(o, &n, "per_layer_model_projection.weight_packed", "U8", L->N, L->K / 2, 2, L->w, (size_t)L->N * L->K / 2);
+    else ck_add(o, &n, "per_layer_model_projection.weight_packed", "I32", L->N, L->K / 8, 2, L->w, (size_t)L->N * L->K / 2);
+    ck_add(o, &n, "per_layer_model_projection.weight_scale", "BF16", L->N, L->K / 32, 2, L->s, sizeof(uint16_t) * (size_t)L->N * L->K / 32);
+    uint16_t* dst = bf + bo;
+    for (int i = 0; i < PLE_D; ++i) dst[i] = or_f2bf(m->plnorm[i]);
+    bo += PLE_D;
+    ck_add(o, &n, "per_layer_projection_norm.weight", "BF16", PLE_D, 0, 1, dst, sizeof(uint16_t) * PLE_D);
+  }
   /* header: JSON, padded with spaces to a multiple of 8 bytes */
   size_t cap = 256 + (size_t)n * 192, len = 0, off = 0;
   char* hdr = (char*)malloc(cap);

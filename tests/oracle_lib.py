@@ -260,12 +260,13 @@ def or_calc_thr(L):
 
 # ---------------------------------------------------------------- end-to-end oracle
 class E2EConfig(ctypes.Structure):
-    """The oracle's configuration: g4_engine_config's first fields (include/g4.h), then kv_owners
-    and mlp_shared."""
+    """The oracle's configuration: g4_engine_config's first fields (include/g4.h), then kv_owners,
+    mlp_shared and ple."""
     _fields_ = [(n, ctypes.c_int) for n in ("hidden", "n_layers", "mlp", "vocab", "ctx_max", "prefill_block", "k_draft",
                                             "ngram", "ngram_len", "prefill_int8", "decode_int8", "head_screen",
                                             "screen_lim", "attn_chunks", "att_par", "drafter")] + [
-        ("seed", ctypes.c_ulonglong), ("kv_owners", ctypes.c_int), ("mlp_shared", ctypes.c_int)]  # the oracle's own struct
+        ("seed", ctypes.c_ulonglong), ("kv_owners", ctypes.c_int), ("mlp_shared", ctypes.c_int),
+        ("ple", ctypes.c_int)]  # the oracle's own struct
 
 
 def e2e_config(**kw):

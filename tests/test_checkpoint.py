@@ -163,11 +163,11 @@ def test_damaged_files_fail_at_open(ckpt, tmp_path):
 def test_e2b_parts_are_reported_unsupported(ckpt, tmp_path):
     rows = read_index(ckpt / "index.tsv")
     emb = next(r for r in rows if r[0] == "embed_tokens.weight")
-    # a per-layer embedding table (the real E2B model's PLE), here aliasing the embedding's bytes
+    # a per-layer embedding table of the wrong width (here aliasing the embedding's bytes)
     write_index(tmp_path / "ple.tsv", rows + [["embed_tokens_per_layer.weight", "BF16", emb[2], emb[3], emb[4]]])
     ck = g4.Checkpoint(ckpt / "model.safetensors", tmp_path / "ple.tsv")
     try:
-        expect_error(lambda: ck.config(), None, ["per-layer embeddings"])
+        expect_error(lambda: ck.config(), None, ["embed_tokens_per_layer.weight", "expected BF16 [4096,1280]"])
     finally:
         ck.close()
     # a KV-shared layer without an owner of its type: layer 4 is the first global layer
@@ -184,6 +184,30 @@ def test_e2b_parts_are_reported_unsupported(ckpt, tmp_path):
     ck = g4.Checkpoint(ckpt / "model.safetensors", tmp_path / "gap.tsv")
     try:
         expect_error(lambda: ck.config(), None, ["layer 3 has k/v projections after the KV-shared layer 2"])
+    finally:
+        ck.close()
+
+
+def test_ple_checkpoint(tmp_path):
+    """Per-layer embeddings (the E2B model's PLE): the table [vocab][n_layers x 256], the projection of
+    the embedding and its norm, and per layer the input gate, the projection and its norm; the
+    config sets ple."""
+    m = OracleModel(e2e_config(**SMALL, seed=779, ple=1))
+    try:
+        m.write_checkpoint(tmp_path / "model.safetensors")
+    finally:
+        m.close()
+    ck = g4.Checkpoint(tmp_path)
+    try:
+        cfg = ck.config()
+        assert (cfg.n_layers, cfg.ple, cfg.kv_owners) == (5, 1, 0)
+        assert ck.tensor("embed_tokens_per_layer.weight")[:2] == ("BF16", (4096, 1280))
+        assert ck.tensor("per_layer_model_projection.weight_packed")[:2] == ("I32", (1280, 64))
+        assert ck.tensor("layers.3.per_layer_projection.weight_packed")[:2] == ("I32", (512, 32))
+        assert ck.tensor("layers.3.post_per_layer_input_norm.weight")[:2] == ("BF16", (512,))
+        # an engine from it is refused before any device work (the path is not verified)
+        with pytest.raises(RuntimeError, match="per-layer embeddings from a checkpoint"):
+            g4.Engine(g4.engine_config(), checkpoint=ck)
     finally:
         ck.close()
 
