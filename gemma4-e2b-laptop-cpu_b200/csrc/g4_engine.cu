@@ -41,9 +41,9 @@ struct TLayer {
   TcLin tqkv, to, tgu, tdown;
   float *in_ln = nullptr, *post_attn = nullptr, *pre_ff = nullptr, *post_ff = nullptr, *qn = nullptr, *kn = nullptr;
   bool global = false;
-  float scalar = 1.0f;
-  Lin pg, pp;                // per-layer input gate [256][H] and projection [H][256] (PLE)
-  float* post_ple = nullptr;  // post_per_layer_input_norm (PLE)  // layer_scalar (:1389-1404): 1 for the synthetic model, a checkpoint's value otherwise
+  float scalar = 1.0f;         // layer_scalar (:1389-1404): 1 for the synthetic model, a checkpoint's value otherwise
+  Lin pg, pp;                  // per-layer input gate [256][H] and projection [H][256] (PLE)
+  float* post_ple = nullptr;   // post_per_layer_input_norm (PLE)
 };
 struct DLayerW {
   Lin q, o, gu, down;
