@@ -75,6 +75,9 @@ typedef struct {
   int OWN; /* KV owners: layers [0, OWN) own a cache (0 = all) */
   int IS;  /* MLP width of the KV-shared layers (0 = I) */
   int ple; /* per-layer embeddings */
+  int HDG;    /* head dim of the global layers (0 = HD; the E2B model: 512) */
+  int HDM;    /* the larger of HD and HDG: the KV cache's slot width */
+  int rope_q; /* global layers rotate the first quarter of their pair indices only (proportional RoPE) */
   uint16_t* PLEt; /* [V][NL * PD] bf16 */
   Lin plproj;     /* per_layer_model_projection [NL * PD][H] */
   float* plnorm;  /* per_layer_projection_norm [PD] */
@@ -108,6 +111,8 @@ typedef struct {
  * one, else the last owner of its type (l % 5 == 4: global). */
 static int owns(const Model* m, int l) { return m->OWN <= 0 || l < m->OWN; }
 static int mlp_of(const Model* m, int l) { return (!owns(m, l) && m->IS > 0) ? m->IS : m->I; }
+/* layer l's head dim (a.hd, gemma4_engine.cpp:1224: 256 sliding, 512 global in the E2B model) */
+static int hd_of(const Model* m, int l) { return (l % 5 == 4 && m->HDG > 0) ? m->HDG : m->HD; }
 static int owner_of(const Model* m, int l) {
   if (owns(m, l)) return l;
   for (int j = m->OWN - 1; j >= 0; --j)
@@ -145,6 +150,8 @@ typedef struct {
   int kv_owners; /* layers [0, kv_owners) own a KV cache (0 = all), g4_engine_config's field */
   int mlp_shared; /* MLP width of the KV-shared layers (0 = mlp) */
   int ple;        /* per-layer embeddings (PD = 256 per layer) */
+  int hd_global;  /* head dim of the global layers (0 = 256) */
+  int rope_global_quarter; /* proportional RoPE in the global layers (partial_rotary_factor 0.25) */
 } or_e2e_config;  /* g4_engine_config's first fields, then kv_owners, mlp_shared and ple */
 
 void* or_e2e_create(const or_e2e_config* c) {
@@ -157,6 +164,10 @@ void* or_e2e_create(const or_e2e_config* c) {
   m->OWN = c->kv_owners;
   m->IS = c->mlp_shared;
   m->ple = c->ple;
+  m->HDG = c->hd_global > 0 ? c->hd_global : m->HD;
+  m->HDM = m->HDG > m->HD ? m->HDG : m->HD;
+  m->rope_q = c->rope_global_quarter;
+  if (m->HDG != m->HD) m->drafter = 0; /* the drafter is built for one head size; off with wider global heads */
   const int H = m->H, QD = m->NQ * m->HD, I = m->I;
   m->L = (TLayer*)calloc(m->NL, sizeof(TLayer));
   for (int l = 0; l < m->NL; ++l) {
@@ -164,16 +175,17 @@ void* or_e2e_create(const or_e2e_config* c) {
     t->global = (l % 5 == 4);
     t->scalar = 1.0f;
     /* a KV-shared layer has the q projection only (no k/v projections, no k_norm) */
-    { uint64_t ids[3] = {layer_id(l, T_Q), layer_id(l, T_K), layer_id(l, T_V)}; int rows[3] = {QD, m->HD, m->HD}; gen_lin(m, &t->qkv, ids, rows, owns(m, l) ? 3 : 1, H); }
-    { uint64_t ids[1] = {layer_id(l, T_O)}; int rows[1] = {H}; gen_lin(m, &t->o, ids, rows, 1, QD); }
+    const int hdl = hd_of(m, l), QDl = m->NQ * hdl;
+    { uint64_t ids[3] = {layer_id(l, T_Q), layer_id(l, T_K), layer_id(l, T_V)}; int rows[3] = {QDl, hdl, hdl}; gen_lin(m, &t->qkv, ids, rows, owns(m, l) ? 3 : 1, H); }
+    { uint64_t ids[1] = {layer_id(l, T_O)}; int rows[1] = {H}; gen_lin(m, &t->o, ids, rows, 1, QDl); }
     { const int Il = mlp_of(m, l); uint64_t ids[2] = {layer_id(l, T_GATE), layer_id(l, T_UP)}; int rows[2] = {Il, Il}; gen_lin(m, &t->gu, ids, rows, 2, H); }
     { uint64_t ids[1] = {layer_id(l, T_DOWN)}; int rows[1] = {H}; gen_lin(m, &t->down, ids, rows, 1, mlp_of(m, l)); }
     t->in_ln = gen_norm(m, layer_id(l, T_IN_LN), H, 1.f);
     t->post_attn = gen_norm(m, layer_id(l, T_POST_ATTN), H, 1.f);
     t->pre_ff = gen_norm(m, layer_id(l, T_PRE_FF), H, 1.f);
     t->post_ff = gen_norm(m, layer_id(l, T_POST_FF), H, 1.f);
-    t->qn = gen_norm(m, layer_id(l, T_QN), m->HD, 0.0625f);
-    t->kn = owns(m, l) ? gen_norm(m, layer_id(l, T_KN), m->HD, 1.f) : NULL;
+    t->qn = gen_norm(m, layer_id(l, T_QN), hdl, 0.0625f);
+    t->kn = owns(m, l) ? gen_norm(m, layer_id(l, T_KN), hdl, 1.f) : NULL;
     if (m->ple) {
       { uint64_t ids[1] = {layer_id(l, T_PG)}; int rows[1] = {PLE_D}; gen_lin(m, &t->pg, ids, rows, 1, H); }
       { uint64_t ids[1] = {layer_id(l, T_PP)}; int rows[1] = {H}; gen_lin(m, &t->pp, ids, rows, 1, PLE_D); }
@@ -220,17 +232,21 @@ void* or_e2e_create(const or_e2e_config* c) {
       t->qn = gen_norm(m, dlayer_id(l, T_QN), m->HD, 0.0625f);
     }
   }
-  const size_t kvn = (size_t)m->NL * m->ctx_max * m->HD;
+  /* KV cache: one slot of ctx_max x HDM per layer, rows of the layer's head dim */
+  const size_t kvn = (size_t)m->NL * m->ctx_max * m->HDM;
   m->Kc = (uint16_t*)calloc(kvn, sizeof(uint16_t));
   m->Vc = (uint16_t*)calloc(kvn, sizeof(uint16_t));
-  const int hh = m->HD / 2;
+  /* RoPE tables per layer type (:1246-1247): pair index j < ra rotates at theta^(-2j/hd), the rest
+   * not at all; ra = hd/2, or hd/8 for proportional RoPE in the global layers */
   for (int ty = 0; ty < 2; ++ty) {
     const double theta = ty ? 1e6 : 1e4;
+    const int hdt = ty ? m->HDG : m->HD, hh = hdt / 2;
+    const int ra = (int)(hdt * ((ty && m->rope_q) ? 0.25 : 1.0)) / 2;
     m->rc[ty] = (float*)malloc(sizeof(float) * (size_t)m->ctx_max * hh);
     m->rs[ty] = (float*)malloc(sizeof(float) * (size_t)m->ctx_max * hh);
     for (int p = 0; p < m->ctx_max; ++p)
       for (int j = 0; j < hh; ++j) {
-        const double inv = 1.0 / pow(theta, (2.0 * j) / m->HD);
+        const double inv = j < ra ? 1.0 / pow(theta, (2.0 * j) / hdt) : 0.0;
         const double ang = p * inv;
         m->rc[ty][(size_t)p * hh + j] = (float)cos(ang);
         m->rs[ty][(size_t)p * hh + j] = (float)sin(ang);
@@ -316,9 +332,9 @@ static void lin(Model* m, const Lin* w, const float* X, int M, float* Y, int for
 }
 
 /* non-split attention for row m: variant 0 = attn_tile (:1061-1083), 1 = per-(m,h) (:1337-1355) */
-static void attn_row(const Model* m, const uint16_t* Kc, const uint16_t* Vc, const float* q, int lo, int pos, int variant,
-                     float* out) {
-  const int hd = m->HD, len = pos - lo + 1;
+static void attn_row(const Model* m, const uint16_t* Kc, const uint16_t* Vc, int hd, const float* q, int lo, int pos,
+                     int variant, float* out) {
+  const int len = pos - lo + 1;
   float* sc = (float*)malloc(sizeof(float) * len);
   for (int h = 0; h < m->NQ; ++h) {
     const float* qh = q + (size_t)h * hd;
@@ -363,12 +379,12 @@ static void attn_row(const Model* m, const uint16_t* Kc, const uint16_t* Vc, con
 
 /* One target forward over M tokens at pos0 (fwd).  G[hf..] = greedy tokens, hbuf[hf..] = hidden. */
 static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf, int* G, float* hbuf) {
-  const int H = m->H, QD = m->NQ * m->HD, ldmax = QD + 2 * m->HD, hd = m->HD;
+  const int H = m->H, QDM = m->NQ * m->HDM, ldmax = QDM + 2 * m->HDM;
   const int I = m->IS > m->I ? m->IS : m->I; /* buffer width: the widest MLP */
   float* x = (float*)malloc(sizeof(float) * (size_t)M * H);
   float* a = (float*)malloc(sizeof(float) * (size_t)M * H);
   float* qkv = (float*)malloc(sizeof(float) * (size_t)M * ldmax);
-  float* att = (float*)malloc(sizeof(float) * (size_t)M * QD);
+  float* att = (float*)malloc(sizeof(float) * (size_t)M * QDM);
   float* o = (float*)malloc(sizeof(float) * (size_t)M * H);
   float* gu = (float*)malloc(sizeof(float) * (size_t)M * 2 * I);
   float* act = (float*)malloc(sizeof(float) * (size_t)M * I);
@@ -406,10 +422,11 @@ static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf
     TLayer* t = &m->L[l];
     const int ty = t->global ? 1 : 0;
     const int ld = t->qkv.N; /* QD + 2 hd, or QD for a KV-shared layer */
+    const int hd = hd_of(m, l), QD = m->NQ * hd;
     for (int r = 0; r < M; ++r) rmsnorm(x + (size_t)r * H, t->in_ln, H, a + (size_t)r * H, 0);
     lin(m, &t->qkv, a, M, qkv, 0);
-    uint16_t* Kc = m->Kc + (size_t)owner_of(m, l) * m->ctx_max * hd;
-    uint16_t* Vc = m->Vc + (size_t)owner_of(m, l) * m->ctx_max * hd;
+    uint16_t* Kc = m->Kc + (size_t)owner_of(m, l) * m->ctx_max * m->HDM;
+    uint16_t* Vc = m->Vc + (size_t)owner_of(m, l) * m->ctx_max * m->HDM;
     for (int r = 0; r < M; ++r) {
       const int pos = pos0 + r;
       const float* cs = m->rc[ty] + (size_t)pos * (hd / 2);
@@ -443,7 +460,7 @@ static void forward(Model* m, const int* toks, int M, int pos0, int want, int hf
 #pragma omp parallel for schedule(dynamic)
       for (int r = 0; r < M; ++r) {
         const int pos = pos0 + r, lo = t->global ? 0 : (pos - 511 > 0 ? pos - 511 : 0);
-        attn_row(m, Kc, Vc, qkv + (size_t)r * ld, lo, pos, variant, att + (size_t)r * QD);
+        attn_row(m, Kc, Vc, hd, qkv + (size_t)r * ld, lo, pos, variant, att + (size_t)r * QD);
       }
     }
     lin(m, &t->o, att, M, o, 0);
@@ -536,10 +553,10 @@ static int draft(Model* m, int tok, const float* h, int pos, int P, float* h_nex
     const int lo = t->global ? 0 : (pos - 511 > 0 ? pos - 511 : 0);
     int pp = P, ll = lo;
     if (m->hk.attn)
-      m->hk.attn(m->Kc + (size_t)tl * m->ctx_max * hd, m->Vc + (size_t)tl * m->ctx_max * hd, hd, m->NQ, 1, dq, &pp, &ll, lo, P,
+      m->hk.attn(m->Kc + (size_t)tl * m->ctx_max * m->HDM, m->Vc + (size_t)tl * m->ctx_max * m->HDM, hd, m->NQ, 1, dq, &pp, &ll, lo, P,
                  dopt);
     else
-      or_attn_splitkv(m->Kc + (size_t)tl * m->ctx_max * hd, m->Vc + (size_t)tl * m->ctx_max * hd, hd, m->NQ, 1, dq, &pp, &ll,
+      or_attn_splitkv(m->Kc + (size_t)tl * m->ctx_max * m->HDM, m->Vc + (size_t)tl * m->ctx_max * m->HDM, hd, m->NQ, 1, dq, &pp, &ll,
                       lo, P, m->attn_chunks, dopt);
     lin(m, &t->o, dopt, 1, da, 1);
     for (int i = 0; i < H; ++i) da[i] = or_r16(da[i]);
@@ -607,11 +624,11 @@ void or_e2e_fake_ctx(void* mp, int n) {
   Model* m = (Model*)mp;
   uint32_t rs = 12345;
   for (int l = 0; l < m->NL && owns(m, l); ++l) /* the owners' caches, one stream (:1249-1250) */
-    for (size_t i = 0; i < (size_t)n * m->HD; ++i) {
+    for (size_t i = 0; i < (size_t)n * hd_of(m, l); ++i) {
       rs = rs * 1664525u + 1013904223u;
-      m->Kc[(size_t)l * m->ctx_max * m->HD + i] = or_f2bf(((int)(rs >> 9) % 2001 - 1000) / 700.0f);
+      m->Kc[(size_t)l * m->ctx_max * m->HDM + i] = or_f2bf(((int)(rs >> 9) % 2001 - 1000) / 700.0f);
       rs = rs * 1664525u + 1013904223u;
-      m->Vc[(size_t)l * m->ctx_max * m->HD + i] = or_f2bf(((int)(rs >> 9) % 2001 - 1000) / 700.0f);
+      m->Vc[(size_t)l * m->ctx_max * m->HDM + i] = or_f2bf(((int)(rs >> 9) % 2001 - 1000) / 700.0f);
     }
   m->fake_n = n;
 }
@@ -673,7 +690,7 @@ int or_e2e_history(void* mp, int32_t* out, int cap, int* len, int* P) {
 int or_e2e_set_state(void* mp, const uint16_t* Kc, const uint16_t* Vc, int npos, const int32_t* seq, int seq_len,
                      const float* hprev, int P) {
   Model* m = (Model*)mp;
-  if (npos > m->ctx_max || seq_len < 1 || P + 1 > npos) return -1;
+  if (npos > m->ctx_max || seq_len < 1 || P + 1 > npos || m->HDM != m->HD) return -1; /* one head size only */
   for (int l = 0; l < m->NL; ++l) {
     memcpy(m->Kc + (size_t)l * m->ctx_max * m->HD, Kc + (size_t)l * npos * m->HD, sizeof(uint16_t) * (size_t)npos * m->HD);
     memcpy(m->Vc + (size_t)l * m->ctx_max * m->HD, Vc + (size_t)l * npos * m->HD, sizeof(uint16_t) * (size_t)npos * m->HD);
@@ -828,16 +845,17 @@ static void ck_add(CkOut* o, int* n, const char* name, const char* dtype, long l
 }
 int or_e2e_write_checkpoint(void* mp, const char* path, int packed_u8) {
   Model* m = (Model*)mp;
-  const int H = m->H, QD = m->NQ * m->HD, HD = m->HD;
+  const int H = m->H;
   const int per = 7 * 2 + 7 + 5;
   CkOut* o = (CkOut*)calloc((size_t)m->NL * per + 8, sizeof(CkOut));
-  uint16_t* bf = (uint16_t*)malloc(sizeof(uint16_t) * ((size_t)m->NL * (5 * H + 2 * HD + 1) + H + PLE_D));
+  uint16_t* bf = (uint16_t*)malloc(sizeof(uint16_t) * ((size_t)m->NL * (5 * H + 2 * m->HDM + 1) + H + PLE_D));
   size_t bo = 0;
   int n = 0;
   char nm[96];
   for (int l = 0; l < m->NL; ++l) {
     const TLayer* t = &m->L[l];
-    const int I = t->down.K; /* this layer's MLP width */
+    const int I = t->down.K;                     /* this layer's MLP width */
+    const int HD = hd_of(m, l), QD = m->NQ * HD; /* and head dim */
     struct { const char* name; const Lin* lin; int row0, rows; } lins[7] = {
         {"self_attn.q_proj", &t->qkv, 0, QD}, {"self_attn.k_proj", &t->qkv, QD, HD}, {"self_attn.v_proj", &t->qkv, QD + HD, HD},
         {"self_attn.o_proj", &t->o, 0, H},    {"mlp.gate_proj", &t->gu, 0, I},       {"mlp.up_proj", &t->gu, I, I},
@@ -888,6 +906,7 @@ int or_e2e_write_checkpoint(void* mp, const char* path, int packed_u8) {
   {
     uint16_t* dst = bf + bo;
     for (int i = 0; i < H; ++i) dst[i] = or_f2bf(m->fnorm[i]);
+    bo += H; /* the per-layer projection norm below goes after it */
     ck_add(o, &n, "norm.weight", "BF16", H, 0, 1, dst, sizeof(uint16_t) * (size_t)H);
   }
   ck_add(o, &n, "embed_tokens.weight", "BF16", m->V, H, 2, m->E, sizeof(uint16_t) * (size_t)m->V * H);
@@ -931,3 +950,27 @@ int or_e2e_write_checkpoint(void* mp, const char* path, int packed_u8) {
   free(o);
   return rc;
 }
+
+/* Test helper: zero the bf16 scales of one family of linears ("pg", "pp", "o" or "down" in layers
+ * [l0, l1), or the model's "plproj"), so that its output is exactly zero (isolates parts of the
+ * model when comparing against the reference engine on a checkpoint written afterwards).  Returns 0,
+ * or -1 for an unknown family, a bad range or a per-layer-embedding family in a model without
+ * per-layer embeddings. */
+int or_e2e_zero_scales_range(void* mp, const char* what, int l0, int l1) {
+  Model* m = (Model*)mp;
+  const int ple_part = !strcmp(what, "plproj") || !strcmp(what, "pg") || !strcmp(what, "pp");
+  if ((ple_part && !m->ple) || l0 < 0 || l1 > m->NL || l0 > l1) return -1;
+  if (!strcmp(what, "plproj")) {
+    memset(m->plproj.s, 0, sizeof(uint16_t) * (size_t)m->plproj.N * (m->plproj.K / 32));
+    return 0;
+  }
+  for (int l = l0; l < l1; ++l) {
+    TLayer* t = &m->L[l];
+    Lin* L = !strcmp(what, "pg") ? &t->pg : !strcmp(what, "pp") ? &t->pp : !strcmp(what, "o") ? &t->o
+           : !strcmp(what, "down") ? &t->down : NULL;
+    if (!L) return -1;
+    memset(L->s, 0, sizeof(uint16_t) * (size_t)L->N * (L->K / 32));
+  }
+  return 0;
+}
+int or_e2e_zero_scales(void* mp, const char* what) { return or_e2e_zero_scales_range(mp, what, 0, ((Model*)mp)->NL); }

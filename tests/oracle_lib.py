@@ -261,12 +261,13 @@ def or_calc_thr(L):
 # ---------------------------------------------------------------- end-to-end oracle
 class E2EConfig(ctypes.Structure):
     """The oracle's configuration: g4_engine_config's first fields (include/g4.h), then kv_owners,
-    mlp_shared and ple."""
+    mlp_shared, ple, hd_global (head dim of the global layers, 0 = 256) and rope_global_quarter
+    (proportional RoPE there)."""
     _fields_ = [(n, ctypes.c_int) for n in ("hidden", "n_layers", "mlp", "vocab", "ctx_max", "prefill_block", "k_draft",
                                             "ngram", "ngram_len", "prefill_int8", "decode_int8", "head_screen",
                                             "screen_lim", "attn_chunks", "att_par", "drafter")] + [
         ("seed", ctypes.c_ulonglong), ("kv_owners", ctypes.c_int), ("mlp_shared", ctypes.c_int),
-        ("ple", ctypes.c_int)]  # the oracle's own struct
+        ("ple", ctypes.c_int), ("hd_global", ctypes.c_int), ("rope_global_quarter", ctypes.c_int)]  # the oracle's own struct
 
 
 def e2e_config(**kw):
