@@ -11,13 +11,25 @@ engine`) on it with ENGINE_K=0 (plain greedy decode) and ENGINE_PREFILL_INT8=1 (
 and stores the prompts and the engine's GEN tokens in tests/golden/e2e_e2b_ref.npz (four prompts,
 one engine run each, so four first tokens of the full forward).  The oracle's own tokens for the
 same model are printed beside them and, as a check that the comparison can fail, the first tokens
-of the same model without its per-layer embeddings and with every layer scalar 1.  Needs ~16 GB of
-host memory and ~7 GB of temporary disk; run by hand:
+of the same model without its per-layer embeddings and with every layer scalar 1.
 
-    python tests/golden/make_golden_e2b.py
+A second case drives the speculative loop (run_req's draft-verify-accept rounds, :1616-1661) with
+prompt lookup as the only drafter: ENGINE_K=3 enters the loop, ENGINE_POLICY=0,0,0 caps the MTP
+drafter's steps at 0 (:1621), ENGINE_NGRAM=2 and ENGINE_NGLEN=3 copy up to three tokens after the
+latest earlier match of the last two (:1624-1628).  The prompts are 220 tokens long, so every verify
+pass of 2-4 rows runs the split-KV attention (M <= 4 past ENGINE_ATT_PAR = 192, :1305).  The engine
+loads a drafter checkpoint before it starts; a placeholder with the drafter's tensor names is
+written (its values are never read when no draft step runs).  The tokens and the engine's
+ngram_rounds / rounds counts go to tests/golden/e2e_e2b_spec_ref.npz.  Needs ~16 GB of host memory
+and ~7 GB of temporary disk; run by hand (both cases, or one of them):
+
+    python tests/golden/make_golden_e2b.py [greedy|spec]
 """
+import json
 import os
 import pathlib
+import re
+import struct
 import subprocess
 import sys
 import tempfile
@@ -39,6 +51,10 @@ E2B = dict(hidden=1536, n_layers=35, mlp=6144, mlp_shared=12288, vocab=262144, k
            rope_global_quarter=1, drafter=0, k_draft=0, ngram=0, prefill_int8=1, decode_int8=1, ctx_max=1024,
            prefill_block=32, seed=SEED)
 SCALARS = {3: 0.75, 14: 1.5, 22: 0.5, 34: 1.25}  # a few layer scalars other than 1 (bf16 values)
+# the speculative case: prompt lookup only (the oracle has no drafter here; the reference's is capped
+# at 0 steps), verify passes past the split-KV threshold
+SPEC = dict(ngram=2, ngram_len=3, k_draft=0)
+SPEC_PROMPT, SPEC_NEW, SPEC_REQ = 220, 24, 3
 
 
 def e2b_oracle(scalars=True, **over):
@@ -53,39 +69,64 @@ def prompts():
     return [make_prompt(SEED % 1000 + i, N_PROMPT) for i in range(N_REQ)]
 
 
-def main():
-    binary = ROOT / "oracle" / "_ref" / "gemma4_engine"
-    if not binary.exists():
-        sys.exit(f"{binary} missing: make -C oracle engine REF=<reference checkout>")
+def spec_prompts():
+    return [make_prompt(SEED % 1000 + 100 + i, SPEC_PROMPT) for i in range(SPEC_REQ)]
+
+
+def write_placeholder_drafter(d):
+    """A model.safetensors and index with the names the engine's drafter loader reads (:1519-1528):
+    tiny bf16 tensors (2-D where it takes a shape) and the int64 token ordering."""
+    d.mkdir(parents=True, exist_ok=True)
+    tensors = {}
+    for l in range(4):
+        p = f"model.layers.{l}."
+        for n in ("self_attn.q_proj", "self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"):
+            tensors[p + n + ".weight"] = ("BF16", (1, 8))
+        for n in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
+                  "post_feedforward_layernorm", "self_attn.q_norm"):
+            tensors[p + n + ".weight"] = ("BF16", (8,))
+        tensors[p + "layer_scalar"] = ("BF16", (1,))
+    for n in ("pre_projection.weight", "post_projection.weight", "masked_embedding.centroids.weight",
+              "model.embed_tokens.weight"):
+        tensors[n] = ("BF16", (1, 8))
+    tensors["model.norm.weight"] = ("BF16", (8,))
+    tensors["masked_embedding.token_ordering"] = ("I64", (16,))
+    hdr, off = {}, 0
+    for name, (dt, shape) in tensors.items():
+        nb = int(np.prod(shape)) * (2 if dt == "BF16" else 8)
+        hdr[name] = {"dtype": dt, "shape": list(shape), "data_offsets": [off, off + nb]}
+        off += nb
+    h = json.dumps(hdr).encode()
+    h += b" " * (-len(h) % 8)
+    (d / "model.safetensors").write_bytes(struct.pack("<Q", len(h)) + h + bytes(off))
+    make_index(d / "model.safetensors", d / "index.tsv")
+
+
+def run_engine(binary, d, prompt, n_new, env):
+    (d / "prompt.txt").write_text(" ".join(str(int(t)) for t in prompt))
+    proc = subprocess.run([str(binary), str(d), str(d / "index.tsv"), str(d / "prompt.txt"), str(n_new)],
+                          capture_output=True, text=True, env=env, timeout=3600)
+    if proc.returncode != 0:
+        sys.exit(proc.stderr[-3000:])
+    gen = next(ln for ln in proc.stdout.splitlines() if ln.startswith("GEN:"))
+    timing = next(ln for ln in proc.stdout.splitlines() if ln.startswith("TIMING"))
+    ng = re.search(r"ngram_rounds=(\d+)/(\d+)", timing)
+    return [int(x) for x in gen.split()[1:]], (int(ng.group(1)), int(ng.group(2)))
+
+
+def greedy(binary, d, m, env):
     ps = prompts()
-    t0 = time.time()
-    m = e2b_oracle()
-    print(f"oracle model built in {time.time() - t0:.0f} s", flush=True)
-    with tempfile.TemporaryDirectory() as d:
-        d = pathlib.Path(d)
-        m.write_checkpoint(d / "model.safetensors")
-        make_index(d / "model.safetensors", d / "index.tsv")
-        env = dict(os.environ, ENGINE_K="0", ENGINE_PREFILL_INT8="1", ENGINE_CTX="1024",
-                   ENGINE_CPUS=",".join(str(i) for i in range(min(8, os.cpu_count() or 1))))
-        gens = []
-        for i, p in enumerate(ps):  # one run per prompt: each prefill starts at position 0
-            (d / "prompt.txt").write_text(" ".join(str(int(t)) for t in p))
-            t1 = time.time()
-            proc = subprocess.run([str(binary), str(d), str(d / "index.tsv"), str(d / "prompt.txt"), str(N_NEW)],
-                                  capture_output=True, text=True, env=env, timeout=3600)
-            print(f"reference engine, prompt {i}: {time.time() - t1:.0f} s (rc {proc.returncode})", flush=True)
-            if proc.returncode != 0:
-                sys.exit(proc.stderr[-3000:])
-            gen = next(ln for ln in proc.stdout.splitlines() if ln.startswith("GEN:"))
-            gens.append([int(x) for x in gen.split()[1:]])
-    m.use_reference_kernels()
+    gens = []
+    for i, p in enumerate(ps):  # one run per prompt: each prefill starts at position 0
+        t1 = time.time()
+        gen, _ = run_engine(binary, d, p, N_NEW, dict(env, ENGINE_K="0"))
+        print(f"reference engine, prompt {i}: {time.time() - t1:.0f} s", flush=True)
+        gens.append(gen)
     ours = [[int(t) for t in m.generate(p, N_NEW)[0]] for p in ps]
-    m.close()
     for g, o in zip(gens, ours):
         print("reference:", g, "\noracle:   ", o)
     for name, over in (("without per-layer embeddings", dict(ple=0)), ("every layer scalar 1", dict(scalars=False))):
         v = e2b_oracle(**over)
-        v.use_reference_kernels()
         firsts = [int(v.generate(p, 1)[0][0]) for p in ps]
         v.close()
         print(f"first tokens {name}: {firsts} (reference: {[g[0] for g in gens]})")
@@ -96,7 +137,60 @@ def main():
     np.savez(HERE / "e2e_e2b_ref.npz", prompts=np.stack([np.asarray(p, np.int32) for p in ps]), tokens=tok, seed=SEED,
              n_new=N_NEW, scalar_layers=np.array(list(SCALARS), np.int32),
              scalar_values=np.array(list(SCALARS.values()), np.float32))
-    print("agree" if ours == gens else "DIFFER")
+    print("greedy: agree" if ours == gens else "greedy: DIFFER")
+
+
+def spec(binary, d, env):
+    ps = spec_prompts()
+    write_placeholder_drafter(d / "drafter")
+    env = dict(env, ENGINE_K="3", ENGINE_POLICY="0,0,0", ENGINE_NGRAM=str(SPEC["ngram"]),
+               ENGINE_NGLEN=str(SPEC["ngram_len"]), ENGINE_DRAFTER_DIR=str(d / "drafter"),
+               ENGINE_DRAFTER_INDEX=str(d / "drafter" / "index.tsv"))
+    gens, counts = [], []
+    for i, p in enumerate(ps):
+        t1 = time.time()
+        gen, ng = run_engine(binary, d, p, SPEC_NEW, env)
+        print(f"reference engine, speculative prompt {i}: {time.time() - t1:.0f} s, ngram_rounds/rounds {ng}", flush=True)
+        gens.append(gen)
+        counts.append(ng)
+    m = e2b_oracle(**SPEC)
+    ours, ocounts = [], []
+    for p in ps:
+        t, st = m.generate(p, SPEC_NEW)
+        ours.append([int(x) for x in t])
+        ocounts.append((st["ngram_rounds"], st["rounds"]))
+    m.close()
+    for g, o, c, oc in zip(gens, ours, counts, ocounts):
+        print("reference:", g, c, "\noracle:   ", o, oc)
+    width = max(len(g) for g in gens)
+    tok = np.full((SPEC_REQ, width), -1, np.int32)
+    for i, g in enumerate(gens):
+        tok[i, :len(g)] = g
+    np.savez(HERE / "e2e_e2b_spec_ref.npz", prompts=np.stack([np.asarray(p, np.int32) for p in ps]), tokens=tok,
+             seed=SEED, n_new=SPEC_NEW, ngram_rounds=np.array([c[0] for c in counts], np.int32),
+             rounds=np.array([c[1] for c in counts], np.int32))
+    print("speculative: agree" if (ours, ocounts) == (gens, counts) else "speculative: DIFFER")
+
+
+def main():
+    which = sys.argv[1] if len(sys.argv) > 1 else "all"
+    binary = ROOT / "oracle" / "_ref" / "gemma4_engine"
+    if not binary.exists():
+        sys.exit(f"{binary} missing: make -C oracle engine REF=<reference checkout>")
+    t0 = time.time()
+    m = e2b_oracle()
+    print(f"oracle model built in {time.time() - t0:.0f} s", flush=True)
+    env = dict(os.environ, ENGINE_PREFILL_INT8="1", ENGINE_CTX="1024",
+               ENGINE_CPUS=",".join(str(i) for i in range(min(8, os.cpu_count() or 1))))
+    with tempfile.TemporaryDirectory() as d:
+        d = pathlib.Path(d)
+        m.write_checkpoint(d / "model.safetensors")
+        make_index(d / "model.safetensors", d / "index.tsv")
+        if which in ("all", "greedy"):
+            greedy(binary, d, m, env)
+        m.close()
+        if which in ("all", "spec"):
+            spec(binary, d, env)
 
 
 if __name__ == "__main__":

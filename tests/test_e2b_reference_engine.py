@@ -9,7 +9,12 @@ checkpoint of the oracle's seeded E2B-shaped model (tests/golden/make_golden_e2b
 without any of the reference's kernels, must produce the same tokens; the script that made the
 fixture also showed that the same model without its per-layer embeddings, or with every layer
 scalar 1, gives other first tokens on two of the four prompts.  Needs about 8 GB of host memory and
-half a minute per prompt on eight cores; the two prompts that those variants change are checked."""
+half a minute per prompt on eight cores; the two prompts that those variants change are checked.
+
+tests/golden/e2e_e2b_spec_ref.npz holds the same engine's speculative rounds with prompt lookup as
+the drafter (the MTP drafter capped at 0 steps): 220-token prompts, so that every verify pass of 2-4
+rows runs the split-KV attention, 24 new tokens, and the engine's ngram_rounds / rounds counts.  One
+of its prompts is checked here, tokens and counts."""
 import pathlib
 import sys
 
@@ -22,6 +27,8 @@ sys.path.insert(0, str(HERE / "golden"))
 import make_golden_e2b as golden  # noqa: E402
 
 FIXTURE = HERE / "golden" / "e2e_e2b_ref.npz"
+SPEC_FIXTURE = HERE / "golden" / "e2e_e2b_spec_ref.npz"
+SPEC_CHECKED = 2  # its lookups are rejected once before the model settles
 CHECKED = (1, 2)  # the prompts whose first token moves without per-layer embeddings or scalars
 
 
@@ -46,5 +53,21 @@ def test_oracle_matches_the_reference_engine_on_e2b(fixture):
             want = [int(t) for t in fixture["tokens"][i] if t >= 0]
             got = [int(t) for t in m.generate(fixture["prompts"][i], golden.N_NEW)[0]]
             assert got == want, f"prompt {i}"
+    finally:
+        m.close()
+
+
+def test_oracle_matches_the_reference_engine_speculative():
+    g = np.load(SPEC_FIXTURE)
+    assert int(g["seed"]) == golden.SEED and int(g["n_new"]) == golden.SPEC_NEW
+    p = golden.spec_prompts()[SPEC_CHECKED]
+    assert np.array_equal(g["prompts"][SPEC_CHECKED], p)
+    m = golden.e2b_oracle(**golden.SPEC)
+    try:
+        toks, st = m.generate(p, golden.SPEC_NEW)
+        assert [int(t) for t in toks] == [int(t) for t in g["tokens"][SPEC_CHECKED] if t >= 0]
+        assert (st["ngram_rounds"], st["rounds"]) == (int(g["ngram_rounds"][SPEC_CHECKED]),
+                                                      int(g["rounds"][SPEC_CHECKED]))
+        assert st["ngram_rounds"] > 0 and st["accepted"] > 0  # lookups were drafted and accepted
     finally:
         m.close()
