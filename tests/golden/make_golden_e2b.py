@@ -19,8 +19,9 @@ drafter's steps at 0 (:1621), ENGINE_NGRAM=2 and ENGINE_NGLEN=3 copy up to three
 latest earlier match of the last two (:1624-1628).  The prompts are 220 tokens long, so every verify
 pass of 2-4 rows runs the split-KV attention (M <= 4 past ENGINE_ATT_PAR = 192, :1305).  The engine
 loads a drafter checkpoint before it starts; a placeholder with the drafter's tensor names is
-written (its values are never read when no draft step runs).  The tokens and the engine's
-ngram_rounds / rounds counts go to tests/golden/e2e_e2b_spec_ref.npz.  Needs ~16 GB of host memory
+written (its values are never read when no draft step runs).  It runs in both decode modes, the
+int8 verify passes and ENGINE_DECODE_INT8=0.  The tokens and the engine's ngram_rounds / rounds
+counts go to tests/golden/e2e_e2b_spec_ref.npz.  Needs ~16 GB of host memory
 and ~7 GB of temporary disk; run by hand (both cases, or one of them):
 
     python tests/golden/make_golden_e2b.py [greedy|spec]
@@ -141,35 +142,41 @@ def greedy(binary, d, m, env):
 
 
 def spec(binary, d, env):
+    """Both decode modes: int8 verify passes (the default) and ENGINE_DECODE_INT8=0 (:1600, the float
+    W4G32 path the reference's exactness claim is about); keys without and with the _dec0 suffix."""
     ps = spec_prompts()
     write_placeholder_drafter(d / "drafter")
     env = dict(env, ENGINE_K="3", ENGINE_POLICY="0,0,0", ENGINE_NGRAM=str(SPEC["ngram"]),
                ENGINE_NGLEN=str(SPEC["ngram_len"]), ENGINE_DRAFTER_DIR=str(d / "drafter"),
                ENGINE_DRAFTER_INDEX=str(d / "drafter" / "index.tsv"))
-    gens, counts = [], []
-    for i, p in enumerate(ps):
-        t1 = time.time()
-        gen, ng = run_engine(binary, d, p, SPEC_NEW, env)
-        print(f"reference engine, speculative prompt {i}: {time.time() - t1:.0f} s, ngram_rounds/rounds {ng}", flush=True)
-        gens.append(gen)
-        counts.append(ng)
-    m = e2b_oracle(**SPEC)
-    ours, ocounts = [], []
-    for p in ps:
-        t, st = m.generate(p, SPEC_NEW)
-        ours.append([int(x) for x in t])
-        ocounts.append((st["ngram_rounds"], st["rounds"]))
-    m.close()
-    for g, o, c, oc in zip(gens, ours, counts, ocounts):
-        print("reference:", g, c, "\noracle:   ", o, oc)
-    width = max(len(g) for g in gens)
-    tok = np.full((SPEC_REQ, width), -1, np.int32)
-    for i, g in enumerate(gens):
-        tok[i, :len(g)] = g
-    np.savez(HERE / "e2e_e2b_spec_ref.npz", prompts=np.stack([np.asarray(p, np.int32) for p in ps]), tokens=tok,
-             seed=SEED, n_new=SPEC_NEW, ngram_rounds=np.array([c[0] for c in counts], np.int32),
-             rounds=np.array([c[1] for c in counts], np.int32))
-    print("speculative: agree" if (ours, ocounts) == (gens, counts) else "speculative: DIFFER")
+    out = dict(prompts=np.stack([np.asarray(p, np.int32) for p in ps]), seed=SEED, n_new=SPEC_NEW)
+    for dec in (1, 0):
+        sfx = "" if dec else "_dec0"
+        gens, counts = [], []
+        for i, p in enumerate(ps):
+            t1 = time.time()
+            gen, ng = run_engine(binary, d, p, SPEC_NEW, dict(env, ENGINE_DECODE_INT8=str(dec)))
+            print(f"reference engine, speculative prompt {i}, decode int8 {dec}: {time.time() - t1:.0f} s, "
+                  f"ngram_rounds/rounds {ng}", flush=True)
+            gens.append(gen)
+            counts.append(ng)
+        m = e2b_oracle(decode_int8=dec, **SPEC)
+        ours, ocounts = [], []
+        for p in ps:
+            t, st = m.generate(p, SPEC_NEW)
+            ours.append([int(x) for x in t])
+            ocounts.append((st["ngram_rounds"], st["rounds"]))
+        m.close()
+        for g, o, c, oc in zip(gens, ours, counts, ocounts):
+            print("reference:", g, c, "\noracle:   ", o, oc)
+        tok = np.full((SPEC_REQ, max(len(g) for g in gens)), -1, np.int32)
+        for i, g in enumerate(gens):
+            tok[i, :len(g)] = g
+        out["tokens" + sfx] = tok
+        out["ngram_rounds" + sfx] = np.array([c[0] for c in counts], np.int32)
+        out["rounds" + sfx] = np.array([c[1] for c in counts], np.int32)
+        print(f"speculative, decode int8 {dec}: " + ("agree" if (ours, ocounts) == (gens, counts) else "DIFFER"))
+    np.savez(HERE / "e2e_e2b_spec_ref.npz", **out)
 
 
 def main():

@@ -13,8 +13,9 @@ half a minute per prompt on eight cores; the two prompts that those variants cha
 
 tests/golden/e2e_e2b_spec_ref.npz holds the same engine's speculative rounds with prompt lookup as
 the drafter (the MTP drafter capped at 0 steps): 220-token prompts, so that every verify pass of 2-4
-rows runs the split-KV attention, 24 new tokens, and the engine's ngram_rounds / rounds counts.  One
-of its prompts is checked here, tokens and counts."""
+rows runs the split-KV attention, 24 new tokens, and the engine's ngram_rounds / rounds counts, in
+both decode modes (int8 verify passes and ENGINE_DECODE_INT8=0).  One of its prompts is checked
+here in each mode, tokens and counts."""
 import pathlib
 import sys
 
@@ -57,17 +58,22 @@ def test_oracle_matches_the_reference_engine_on_e2b(fixture):
         m.close()
 
 
-def test_oracle_matches_the_reference_engine_speculative():
+@pytest.mark.parametrize("dec", [1, 0], ids=["int8", "decode_int8_0"])
+def test_oracle_matches_the_reference_engine_speculative(dec):
+    """dec 0 is ENGINE_DECODE_INT8=0 (gemma4_engine.cpp:1600): float verify passes.  On this prompt the
+    two modes give different tokens, and the oracle follows the engine in both."""
     g = np.load(SPEC_FIXTURE)
+    sfx = "" if dec else "_dec0"
     assert int(g["seed"]) == golden.SEED and int(g["n_new"]) == golden.SPEC_NEW
+    assert not np.array_equal(g["tokens"][SPEC_CHECKED], g["tokens_dec0"][SPEC_CHECKED])
     p = golden.spec_prompts()[SPEC_CHECKED]
     assert np.array_equal(g["prompts"][SPEC_CHECKED], p)
-    m = golden.e2b_oracle(**golden.SPEC)
+    m = golden.e2b_oracle(decode_int8=dec, **golden.SPEC)
     try:
         toks, st = m.generate(p, golden.SPEC_NEW)
-        assert [int(t) for t in toks] == [int(t) for t in g["tokens"][SPEC_CHECKED] if t >= 0]
-        assert (st["ngram_rounds"], st["rounds"]) == (int(g["ngram_rounds"][SPEC_CHECKED]),
-                                                      int(g["rounds"][SPEC_CHECKED]))
+        assert [int(t) for t in toks] == [int(t) for t in g["tokens" + sfx][SPEC_CHECKED] if t >= 0]
+        assert (st["ngram_rounds"], st["rounds"]) == (int(g["ngram_rounds" + sfx][SPEC_CHECKED]),
+                                                      int(g["rounds" + sfx][SPEC_CHECKED]))
         assert st["ngram_rounds"] > 0 and st["accepted"] > 0  # lookups were drafted and accepted
     finally:
         m.close()
