@@ -21,10 +21,18 @@ pass of 2-4 rows runs the split-KV attention (M <= 4 past ENGINE_ATT_PAR = 192, 
 loads a drafter checkpoint before it starts; a placeholder with the drafter's tensor names is
 written (its values are never read when no draft step runs).  It runs in both decode modes, the
 int8 verify passes and ENGINE_DECODE_INT8=0.  The tokens and the engine's ngram_rounds / rounds
-counts go to tests/golden/e2e_e2b_spec_ref.npz.  Needs ~16 GB of host memory
-and ~7 GB of temporary disk; run by hand (both cases, or one of them):
+counts go to tests/golden/e2e_e2b_spec_ref.npz.
 
-    python tests/golden/make_golden_e2b.py [greedy|spec]
+A third case runs the engine as a server (ENGINE_SERVE=1, one request per input line) through its
+prefix cache with three conversation slots (ENGINE_SLOTS=3, ENGINE_SLOT_MIN_REUSE=32, :1569-1613):
+continuation, switch, eviction and repeat (serve_requests).  Per request the tokens and TIMING's
+reused= and slot= go to tests/golden/e2e_e2b_serve_ref.npz, against tests/oracle_lib.py's
+OracleConversations, the restated policy the GPU request tests use.
+
+Needs ~16 GB of host memory (the serve case ~25 GB: one oracle model per slot) and ~7 GB of
+temporary disk; run by hand (every case, or one of them):
+
+    python tests/golden/make_golden_e2b.py [greedy|spec|serve]
 """
 import json
 import os
@@ -42,7 +50,7 @@ HERE = pathlib.Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
 sys.path.insert(0, str(HERE.parent))
 
-from oracle_lib import OracleModel, e2e_config, make_prompt  # noqa: E402
+from oracle_lib import OracleConversations, OracleModel, e2e_config, make_prompt  # noqa: E402
 from test_checkpoint import make_index  # noqa: E402
 
 SEED = 20261202
@@ -56,6 +64,8 @@ SCALARS = {3: 0.75, 14: 1.5, 22: 0.5, 34: 1.25}  # a few layer scalars other tha
 # at 0 steps), verify passes past the split-KV threshold
 SPEC = dict(ngram=2, ngram_len=3, k_draft=0)
 SPEC_PROMPT, SPEC_NEW, SPEC_REQ = 220, 24, 3
+# the serve case: conversation slots (ENGINE_SLOTS) and their reuse threshold (ENGINE_SLOT_MIN_REUSE)
+SERVE_SLOTS, SERVE_MIN_REUSE, SERVE_NEW = 3, 32, 4
 
 
 def e2b_oracle(scalars=True, **over):
@@ -72,6 +82,18 @@ def prompts():
 
 def spec_prompts():
     return [make_prompt(SEED % 1000 + 100 + i, SPEC_PROMPT) for i in range(SPEC_REQ)]
+
+
+def serve_requests():
+    """A session through the prefix cache: a new conversation, its continuation, an unrelated one
+    (a stored slot takes it), a return to the first sharing 50 tokens (switch), a prompt sharing
+    fewer than SERVE_MIN_REUSE tokens with everything (the least recently used slot is evicted),
+    and a repeat of the previous prompt (only its last token is re-run)."""
+    a = make_prompt(SEED % 1000 + 204, 60)  # seeds whose prompts do not lead to the random model's
+    b = make_prompt(SEED % 1000 + 207, 40)  # most frequent token (236283)
+    extra = make_prompt(SEED % 1000 + 203, 60)
+    return [a, np.concatenate([a, extra[:20]]), b, np.concatenate([a[:50], extra[20:30]]),
+            np.concatenate([a[:10], extra[30:60]]), np.concatenate([a[:10], extra[30:60]])]
 
 
 def write_placeholder_drafter(d):
@@ -179,6 +201,40 @@ def spec(binary, d, env):
     np.savez(HERE / "e2e_e2b_spec_ref.npz", **out)
 
 
+def serve(binary, d, env):
+    """ENGINE_SERVE=1: one engine process, one request per stdin line ("<n_new> <tokens>", :1681-1689);
+    per request the GEN tokens and TIMING's reused= and slot= fields."""
+    reqs = serve_requests()
+    env = dict(env, ENGINE_K="0", ENGINE_SERVE="1", ENGINE_SLOTS=str(SERVE_SLOTS),
+               ENGINE_SLOT_MIN_REUSE=str(SERVE_MIN_REUSE))
+    lines = "".join(f"{SERVE_NEW} " + " ".join(str(int(t)) for t in p) + "\n" for p in reqs)
+    t1 = time.time()
+    proc = subprocess.run([str(binary), str(d), str(d / "index.tsv"), "/dev/null", "0"], input=lines,
+                          capture_output=True, text=True, env=env, timeout=3600)
+    if proc.returncode != 0:
+        sys.exit(proc.stderr[-3000:])
+    gens = [[int(x) for x in ln.split()[1:]] for ln in proc.stdout.splitlines() if ln.startswith("GEN:")]
+    timing = [ln for ln in proc.stdout.splitlines() if ln.startswith("TIMING")]
+    reused = [int(re.search(r"reused=(\d+)", ln).group(1)) for ln in timing]
+    slots = [int(re.search(r"slot=(\d+)", ln).group(1)) for ln in timing]
+    print(f"reference engine, serve session: {time.time() - t1:.0f} s; reused {reused}, slots {slots}", flush=True)
+    conv = OracleConversations(e2b_oracle, SERVE_SLOTS, SERVE_MIN_REUSE)
+    ours = [conv.request(p, SERVE_NEW) for p in reqs]
+    conv.close()
+    for g, r, sl, o in zip(gens, reused, slots, ours):
+        print("reference:", g, r, sl, "\noracle:   ", o[0], o[1], o[2])
+    tok = np.full((len(reqs), SERVE_NEW), -1, np.int32)
+    req = np.full((len(reqs), max(len(p) for p in reqs)), -1, np.int32)
+    for i, (g, p) in enumerate(zip(gens, reqs)):
+        tok[i, :len(g)] = g
+        req[i, :len(p)] = p
+    np.savez(HERE / "e2e_e2b_serve_ref.npz", requests=req, tokens=tok, reused=np.array(reused, np.int32),
+             slot=np.array(slots, np.int32), seed=SEED, n_new=SERVE_NEW, slots=SERVE_SLOTS,
+             min_reuse=SERVE_MIN_REUSE)
+    same = [(o[0], o[1], o[2]) for o in ours] == list(zip(gens, reused, slots))
+    print("serve: agree" if same else "serve: DIFFER")
+
+
 def main():
     which = sys.argv[1] if len(sys.argv) > 1 else "all"
     binary = ROOT / "oracle" / "_ref" / "gemma4_engine"
@@ -198,6 +254,8 @@ def main():
         m.close()
         if which in ("all", "spec"):
             spec(binary, d, env)
+        if which in ("all", "serve"):
+            serve(binary, d, env)
 
 
 if __name__ == "__main__":

@@ -380,6 +380,84 @@ class OracleModel:
         return oracle().or_e2e_set_hooks(self.h, ctypes.cast(hooks, ctypes.c_void_p)) == 0
 
 
+STOP_TOKENS = (1, 106)  # is_stop (gemma4_engine.cpp)
+
+
+class OracleConversations:
+    """run_req's prefix cache (gemma4_engine.cpp:1569-1613) over oracle models, one per conversation
+    (each holds its own K/V and history, as a slot does): [model, keys, kv_len, stamp] per
+    conversation.  The longest shared prefix picks the conversation, a stored one that shares more
+    is switched in, a prompt that shares fewer than min_reuse tokens with every conversation evicts
+    the least recently used slot, and the prefill starts at min(shared, n - 1).  new_model() makes
+    each conversation's model."""
+
+    def __init__(self, new_model, slots, min_reuse):
+        self.min_reuse = min_reuse
+        self.active = [new_model(), [], 0, 0]
+        self.stored = [[new_model(), [], 0, 0] for _ in range(slots - 1)]
+        self.tick = 0
+
+    def close(self):
+        for c in [self.active] + self.stored:
+            c[0].close()
+
+    def set_k(self, k):
+        for c in [self.active] + self.stored:
+            c[0].set_k(k)
+
+    @staticmethod
+    def _lcp(keys, kv_len, prompt):
+        c = 0
+        while c < kv_len and c < len(prompt) and c < len(keys) and keys[c] == prompt[c]:
+            c += 1
+        return c
+
+    def _swap(self, i):
+        self.active, self.stored[i] = self.stored[i], self.active
+
+    def request(self, prompt, max_new):
+        prompt = [int(t) for t in prompt]
+        n = len(prompt)
+        common = self._lcp(self.active[1], self.active[2], prompt)
+        self.tick += 1
+        slot = 0
+        if self.stored:
+            best, bc = -1, common
+            for i, s in enumerate(self.stored):
+                c = self._lcp(s[1], s[2], prompt)
+                if c > bc:
+                    bc, best = c, i
+            if best >= 0:
+                self.active[3] = self.tick
+                self._swap(best)
+                slot, common = best + 1, bc
+            elif bc < self.min_reuse:
+                v = min(range(len(self.stored)), key=lambda i: self.stored[i][3])  # the first oldest
+                self.active[3] = self.tick
+                self._swap(v)
+                self.active[1], self.active[2] = [], 0
+                slot, common = v + 1, 0
+            self.active[3] = self.tick
+        start = min(common, n - 1)
+        m = self.active[0]
+        first = m.prefill(prompt, start)
+        if max_new <= 0:  # prefill only: the prompt is the conversation
+            self.active[1], self.active[2] = prompt, n
+            return [], start, slot
+        out = [first]
+        if max_new > 1 and out[0] not in STOP_TOKENS:
+            toks, _ = m.decode(1 << 30, max_new - 1)
+            out += [int(t) for t in toks]
+        for i, t in enumerate(out):
+            if t in STOP_TOKENS:
+                out = out[: i + 1]
+                break
+        seq, P = m.history()
+        self.active[1] = [int(t) for t in seq[: P + 1]]
+        self.active[2] = min(P + 1, len(self.active[1]))
+        return out, start, slot
+
+
 def gen_bytes(seed, tid, n):
     out = np.zeros(n, np.uint8)
     oracle().or_e2e_gen_bytes(seed, tid, n, ptr(out))

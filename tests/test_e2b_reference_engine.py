@@ -15,7 +15,8 @@ tests/golden/e2e_e2b_spec_ref.npz holds the same engine's speculative rounds wit
 the drafter (the MTP drafter capped at 0 steps): 220-token prompts, so that every verify pass of 2-4
 rows runs the split-KV attention, 24 new tokens, and the engine's ngram_rounds / rounds counts, in
 both decode modes (int8 verify passes and ENGINE_DECODE_INT8=0).  One of its prompts is checked
-here in each mode, tokens and counts."""
+here in each mode, tokens and counts.  tests/golden/e2e_e2b_serve_ref.npz holds a session of the
+engine as a server through its prefix cache, checked request by request."""
 import pathlib
 import sys
 
@@ -30,6 +31,7 @@ import make_golden_e2b as golden  # noqa: E402
 FIXTURE = HERE / "golden" / "e2e_e2b_ref.npz"
 SPEC_FIXTURE = HERE / "golden" / "e2e_e2b_spec_ref.npz"
 SPEC_CHECKED = 2  # its lookups are rejected once before the model settles
+SERVE_FIXTURE = HERE / "golden" / "e2e_e2b_serve_ref.npz"
 CHECKED = (1, 2)  # the prompts whose first token moves without per-layer embeddings or scalars
 
 
@@ -77,3 +79,25 @@ def test_oracle_matches_the_reference_engine_speculative(dec):
         assert st["ngram_rounds"] > 0 and st["accepted"] > 0  # lookups were drafted and accepted
     finally:
         m.close()
+
+
+def test_prefix_cache_slots_match_the_reference_engine_serving():
+    """tests/golden/e2e_e2b_serve_ref.npz: the engine as a server (ENGINE_SERVE=1) with three
+    conversation slots: continuation, switch, eviction and repeat.  OracleConversations, the
+    restated slot policy that the GPU request tests hold the CUDA engine to, gives the same tokens,
+    reused positions and slots for every request."""
+    from oracle_lib import OracleConversations
+    g = np.load(SERVE_FIXTURE)
+    assert int(g["seed"]) == golden.SEED and int(g["slots"]) == golden.SERVE_SLOTS
+    reqs = golden.serve_requests()
+    for i, p in enumerate(reqs):
+        assert np.array_equal(g["requests"][i][: len(p)], p) and (g["requests"][i][len(p):] == -1).all()
+    assert sorted(set(g["slot"].tolist())) == [0, 1, 2] and (g["reused"] > 0).sum() >= 3
+    conv = OracleConversations(golden.e2b_oracle, golden.SERVE_SLOTS, int(g["min_reuse"]))
+    try:
+        for i, p in enumerate(reqs):
+            toks, start, slot = conv.request(p, int(g["n_new"]))
+            assert toks == [int(t) for t in g["tokens"][i] if t >= 0], i
+            assert (start, slot) == (int(g["reused"][i]), int(g["slot"][i])), i
+    finally:
+        conv.close()

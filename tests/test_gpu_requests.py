@@ -1,14 +1,15 @@
 """Requests through the prefix cache (g4_engine_request: run_req and its conversation slots,
-gemma4_engine.cpp:1569-1613) against the same policy restated here over oracle models, one model
-per conversation (each holds its own K/V and history, as a slot does): the longest shared prefix
-picks the conversation, a stored one that shares more is switched in, a prompt that shares fewer
-than slot_min_reuse tokens with every conversation evicts the least recently used slot, and the
-prefill starts at min(shared, n - 1).  Tokens, reused positions and the slot used must equal the
+gemma4_engine.cpp:1569-1613) against the same policy restated over oracle models
+(oracle_lib.OracleConversations, itself pinned to the reference engine's serve mode on the E2B
+shape), one model per conversation (each holds its own K/V and history, as a slot does): the
+longest shared prefix picks the conversation, a stored one that shares more is switched in, a
+prompt that shares fewer than slot_min_reuse tokens with every conversation evicts the least
+recently used slot, and the prefill starts at min(shared, n - 1).  Tokens, reused positions and the slot used must equal the
 restatement's for every request."""
 import numpy as np
 import pytest
 
-from oracle_lib import OracleModel, e2e_config, make_prompt
+from oracle_lib import OracleConversations, OracleModel, e2e_config, make_prompt
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -16,77 +17,6 @@ pytestmark = pytest.mark.gpu
 from g4pkg import g4  # noqa: E402
 
 SMALL = dict(hidden=512, n_layers=5, mlp=1024, vocab=4096, ctx_max=1024)
-STOP = (1, 106)
-
-
-class OracleConversations:
-    """run_req's prefix cache over oracle models: [model, keys, kv_len, stamp] per conversation."""
-
-    def __init__(self, cfg, slots, min_reuse):
-        self.min_reuse = min_reuse
-        self.active = [OracleModel(e2e_config(**cfg)), [], 0, 0]
-        self.stored = [[OracleModel(e2e_config(**cfg)), [], 0, 0] for _ in range(slots - 1)]
-        self.tick = 0
-
-    def close(self):
-        for c in [self.active] + self.stored:
-            c[0].close()
-
-    def set_k(self, k):
-        for c in [self.active] + self.stored:
-            c[0].set_k(k)
-
-    @staticmethod
-    def _lcp(keys, kv_len, prompt):
-        c = 0
-        while c < kv_len and c < len(prompt) and c < len(keys) and keys[c] == prompt[c]:
-            c += 1
-        return c
-
-    def _swap(self, i):
-        self.active, self.stored[i] = self.stored[i], self.active
-
-    def request(self, prompt, max_new):
-        prompt = [int(t) for t in prompt]
-        n = len(prompt)
-        common = self._lcp(self.active[1], self.active[2], prompt)
-        self.tick += 1
-        slot = 0
-        if self.stored:
-            best, bc = -1, common
-            for i, s in enumerate(self.stored):
-                c = self._lcp(s[1], s[2], prompt)
-                if c > bc:
-                    bc, best = c, i
-            if best >= 0:
-                self.active[3] = self.tick
-                self._swap(best)
-                slot, common = best + 1, bc
-            elif bc < self.min_reuse:
-                v = min(range(len(self.stored)), key=lambda i: self.stored[i][3])  # the first oldest
-                self.active[3] = self.tick
-                self._swap(v)
-                self.active[1], self.active[2] = [], 0
-                slot, common = v + 1, 0
-            self.active[3] = self.tick
-        start = min(common, n - 1)
-        m = self.active[0]
-        first = m.prefill(prompt, start)
-        if max_new <= 0:  # prefill only: the prompt is the conversation
-            self.active[1], self.active[2] = prompt, n
-            return [], start, slot
-        out = [first]
-        if max_new > 1 and out[0] not in STOP:
-            toks, _ = m.decode(1 << 30, max_new - 1)
-            out += [int(t) for t in toks]
-        for i, t in enumerate(out):
-            if t in STOP:
-                out = out[: i + 1]
-                break
-        seq, P = m.history()
-        self.active[1] = [int(t) for t in seq[: P + 1]]
-        self.active[2] = min(P + 1, len(self.active[1]))
-        return out, start, slot
 
 
 def _prompts():
@@ -109,7 +39,7 @@ def _prompts():
 def test_requests_with_prefix_cache_match_the_restated_policy(slots):
     cfg = dict(SMALL)
     eng = g4.Engine(g4.engine_config(**cfg, slots=slots, slot_min_reuse=32))
-    ref = OracleConversations(cfg, slots, 32)
+    ref = OracleConversations(lambda: OracleModel(e2e_config(**cfg)), slots, 32)
     try:
         reused_any = False
         for i, p in enumerate(_prompts()):
