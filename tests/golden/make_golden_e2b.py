@@ -27,12 +27,14 @@ A third case runs the engine as a server (ENGINE_SERVE=1, one request per input 
 prefix cache with three conversation slots (ENGINE_SLOTS=3, ENGINE_SLOT_MIN_REUSE=32, :1569-1613):
 continuation, switch, eviction and repeat (serve_requests).  Per request the tokens and TIMING's
 reused= and slot= go to tests/golden/e2e_e2b_serve_ref.npz, against tests/oracle_lib.py's
-OracleConversations, the restated policy the GPU request tests use.
+OracleConversations, the restated policy the GPU request tests use.  A fourth case repeats the
+speculative one after ENGINE_FAKE_CTX=600 positions of the engine's seeded K/V (fake), into
+tests/golden/e2e_e2b_fake_ref.npz.
 
 Needs ~16 GB of host memory (the serve case ~25 GB: one oracle model per slot) and ~7 GB of
 temporary disk; run by hand (every case, or one of them):
 
-    python tests/golden/make_golden_e2b.py [greedy|spec|serve]
+    python tests/golden/make_golden_e2b.py [greedy|spec|serve|fake]
 """
 import json
 import os
@@ -64,6 +66,9 @@ SCALARS = {3: 0.75, 14: 1.5, 22: 0.5, 34: 1.25}  # a few layer scalars other tha
 # at 0 steps), verify passes past the split-KV threshold
 SPEC = dict(ngram=2, ngram_len=3, k_draft=0)
 SPEC_PROMPT, SPEC_NEW, SPEC_REQ = 220, 24, 3
+# the fake-context case: ENGINE_FAKE_CTX positions of seeded K/V before the prompt
+FAKE_N, FAKE_PROMPT, FAKE_NEW = 600, 60, 16
+FAKE_SEEDS = (204, 205)  # prompts that do not lead to the random model's most frequent token
 # the serve case: conversation slots (ENGINE_SLOTS) and their reuse threshold (ENGINE_SLOT_MIN_REUSE)
 SERVE_SLOTS, SERVE_MIN_REUSE, SERVE_NEW = 3, 32, 4
 
@@ -82,6 +87,10 @@ def prompts():
 
 def spec_prompts():
     return [make_prompt(SEED % 1000 + 100 + i, SPEC_PROMPT) for i in range(SPEC_REQ)]
+
+
+def fake_prompts():
+    return [make_prompt(SEED % 1000 + s, FAKE_PROMPT) for s in FAKE_SEEDS]
 
 
 def serve_requests():
@@ -235,6 +244,42 @@ def serve(binary, d, env):
     print("serve: agree" if same else "serve: DIFFER")
 
 
+def fake(binary, d, env):
+    """ENGINE_FAKE_CTX=600 (:1249-1250): the owners' K/V rows of positions 0..599 filled from the
+    engine's seeded LCG, the prompt at 600 on, speculative rounds with prompt lookup as above, so the
+    verify passes attend ~680 keys through the split-KV attention."""
+    ps = fake_prompts()
+    write_placeholder_drafter(d / "drafter")
+    env = dict(env, ENGINE_K="3", ENGINE_POLICY="0,0,0", ENGINE_NGRAM=str(SPEC["ngram"]),
+               ENGINE_NGLEN=str(SPEC["ngram_len"]), ENGINE_DRAFTER_DIR=str(d / "drafter"),
+               ENGINE_DRAFTER_INDEX=str(d / "drafter" / "index.tsv"), ENGINE_FAKE_CTX=str(FAKE_N))
+    gens, counts = [], []
+    for i, p in enumerate(ps):
+        t1 = time.time()
+        gen, ng = run_engine(binary, d, p, FAKE_NEW, env)
+        print(f"reference engine, fake-context prompt {i}: {time.time() - t1:.0f} s, ngram_rounds/rounds {ng}",
+              flush=True)
+        gens.append(gen)
+        counts.append(ng)
+    m = e2b_oracle(**SPEC)
+    m.fake_ctx(FAKE_N)
+    ours, ocounts = [], []
+    for p in ps:
+        t, st = m.generate(p, FAKE_NEW)
+        ours.append([int(x) for x in t])
+        ocounts.append((st["ngram_rounds"], st["rounds"]))
+    m.close()
+    for g, o, c, oc in zip(gens, ours, counts, ocounts):
+        print("reference:", g, c, "\noracle:   ", o, oc)
+    tok = np.full((len(ps), FAKE_NEW), -1, np.int32)
+    for i, g in enumerate(gens):
+        tok[i, :len(g)] = g
+    np.savez(HERE / "e2e_e2b_fake_ref.npz", prompts=np.stack([np.asarray(p, np.int32) for p in ps]), tokens=tok,
+             seed=SEED, n_new=FAKE_NEW, fake_n=FAKE_N, ngram_rounds=np.array([c[0] for c in counts], np.int32),
+             rounds=np.array([c[1] for c in counts], np.int32))
+    print("fake context: agree" if (ours, ocounts) == (gens, counts) else "fake context: DIFFER")
+
+
 def main():
     which = sys.argv[1] if len(sys.argv) > 1 else "all"
     binary = ROOT / "oracle" / "_ref" / "gemma4_engine"
@@ -256,6 +301,8 @@ def main():
             spec(binary, d, env)
         if which in ("all", "serve"):
             serve(binary, d, env)
+        if which in ("all", "fake"):
+            fake(binary, d, env)
 
 
 if __name__ == "__main__":

@@ -16,7 +16,8 @@ the drafter (the MTP drafter capped at 0 steps): 220-token prompts, so that ever
 rows runs the split-KV attention, 24 new tokens, and the engine's ngram_rounds / rounds counts, in
 both decode modes (int8 verify passes and ENGINE_DECODE_INT8=0).  One of its prompts is checked
 here in each mode, tokens and counts.  tests/golden/e2e_e2b_serve_ref.npz holds a session of the
-engine as a server through its prefix cache, checked request by request."""
+engine as a server through its prefix cache, checked request by request, and
+tests/golden/e2e_e2b_fake_ref.npz speculative rounds after ENGINE_FAKE_CTX=600 seeded positions."""
 import pathlib
 import sys
 
@@ -32,6 +33,7 @@ FIXTURE = HERE / "golden" / "e2e_e2b_ref.npz"
 SPEC_FIXTURE = HERE / "golden" / "e2e_e2b_spec_ref.npz"
 SPEC_CHECKED = 2  # its lookups are rejected once before the model settles
 SERVE_FIXTURE = HERE / "golden" / "e2e_e2b_serve_ref.npz"
+FAKE_FIXTURE = HERE / "golden" / "e2e_e2b_fake_ref.npz"
 CHECKED = (1, 2)  # the prompts whose first token moves without per-layer embeddings or scalars
 
 
@@ -101,3 +103,22 @@ def test_prefix_cache_slots_match_the_reference_engine_serving():
             assert (start, slot) == (int(g["reused"][i]), int(g["slot"][i])), i
     finally:
         conv.close()
+
+
+def test_fake_context_matches_the_reference_engine():
+    """tests/golden/e2e_e2b_fake_ref.npz: ENGINE_FAKE_CTX=600 (the engine's seeded K/V rows before the
+    prompt, gemma4_engine.cpp:1249-1250) and speculative rounds with prompt lookup; the oracle's
+    fake_ctx and decode give the engine's tokens and round counts."""
+    g = np.load(FAKE_FIXTURE)
+    assert int(g["seed"]) == golden.SEED and int(g["fake_n"]) == golden.FAKE_N
+    i = 1  # its tokens change three times
+    p = golden.fake_prompts()[i]
+    assert np.array_equal(g["prompts"][i], p)
+    m = golden.e2b_oracle(**golden.SPEC)
+    try:
+        m.fake_ctx(golden.FAKE_N)
+        toks, st = m.generate(p, int(g["n_new"]))
+        assert [int(t) for t in toks] == [int(t) for t in g["tokens"][i] if t >= 0]
+        assert (st["ngram_rounds"], st["rounds"]) == (int(g["ngram_rounds"][i]), int(g["rounds"][i]))
+    finally:
+        m.close()
