@@ -17,7 +17,9 @@ from g4pkg import g4
 from oracle_lib import OracleModel, e2e_config
 
 SMALL = dict(hidden=512, n_layers=5, mlp=1024, vocab=4096, ctx_max=1024)
-REFERENCE_TOOL = pathlib.Path("/root/reference/tools/make_index.py")
+# the reference checkout: G4_REFERENCE, else a "reference" directory beside this repository
+REFERENCE_TOOL = pathlib.Path(os.environ.get("G4_REFERENCE", str(pathlib.Path(__file__).resolve().parents[2] /
+                                                                  "reference"))) / "tools" / "make_index.py"
 
 
 def make_index(src, out):
