@@ -214,6 +214,29 @@ def test_ple_checkpoint(tmp_path):
         ck.close()
 
 
+def _bf16_tensor(path, name):
+    data = pathlib.Path(path).read_bytes()
+    n = struct.unpack("<Q", data[:8])[0]
+    a, b = json.loads(data[8:8 + n])[name]["data_offsets"]
+    return np.frombuffer(data[8 + n + a:8 + n + b], np.uint16)
+
+
+def test_ple_checkpoint_keeps_the_final_norm(tmp_path):
+    """The per-layer projection norm is written after norm.weight, not over it: norm.weight is the
+    same with and without per-layer embeddings (the final norm is generated independently of them)."""
+    for ple in (0, 1):
+        m = OracleModel(e2e_config(**SMALL, seed=780, ple=ple))
+        try:
+            m.write_checkpoint(tmp_path / f"ple{ple}.safetensors")
+        finally:
+            m.close()
+    a = _bf16_tensor(tmp_path / "ple0.safetensors", "norm.weight")
+    b = _bf16_tensor(tmp_path / "ple1.safetensors", "norm.weight")
+    c = _bf16_tensor(tmp_path / "ple1.safetensors", "per_layer_projection_norm.weight")
+    assert a.size == 512 and np.array_equal(a, b)
+    assert not np.array_equal(b[:256], c)
+
+
 def test_kv_shared_checkpoint(tmp_path):
     """Trailing layers without k/v projections (the E2B model's KV sharing, :1251): the config names
     the first of them as kv_owners and their (here doubled) MLP width as mlp_shared, and the shared
