@@ -122,3 +122,14 @@ def test_fake_context_matches_the_reference_engine():
         assert (st["ngram_rounds"], st["rounds"]) == (int(g["ngram_rounds"][i]), int(g["rounds"][i]))
     finally:
         m.close()
+
+
+def test_the_comparison_can_fail(fixture):
+    """Without its per-layer embeddings the same model gives another first token on a checked
+    prompt, so agreement above is not a property of every model of this shape."""
+    i = CHECKED[0]
+    m = golden.e2b_oracle(ple=0)
+    try:
+        assert int(m.generate(fixture["prompts"][i], 1)[0][0]) != int(fixture["tokens"][i][0])
+    finally:
+        m.close()
