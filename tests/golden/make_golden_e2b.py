@@ -11,7 +11,8 @@ engine`) on it with ENGINE_K=0 (plain greedy decode) and ENGINE_PREFILL_INT8=1 (
 and stores the prompts and the engine's GEN tokens in tests/golden/e2e_e2b_ref.npz (four prompts,
 one engine run each, so four first tokens of the full forward).  The oracle's own tokens for the
 same model are printed beside them and, as a check that the comparison can fail, the first tokens
-of the same model without its per-layer embeddings and with every layer scalar 1.
+of the same model without its per-layer embeddings and with every layer scalar 1.  The same prompts
+are also run on the float path (ENGINE_PREFILL_INT8=0, ENGINE_DECODE_INT8=0) into tokens_float.
 
 A second case drives the speculative loop (run_req's draft-verify-accept rounds, :1616-1661) with
 prompt lookup as the only drafter: ENGINE_K=3 enters the loop, ENGINE_POLICY=0,0,0 caps the MTP
@@ -162,14 +163,26 @@ def greedy(binary, d, m, env):
         firsts = [int(v.generate(p, 1)[0][0]) for p in ps]
         v.close()
         print(f"first tokens {name}: {firsts} (reference: {[g[0] for g in gens]})")
-    width = max(len(g) for g in gens)
-    tok = np.full((N_REQ, width), -1, np.int32)
-    for i, g in enumerate(gens):
-        tok[i, :len(g)] = g
-    np.savez(HERE / "e2e_e2b_ref.npz", prompts=np.stack([np.asarray(p, np.int32) for p in ps]), tokens=tok, seed=SEED,
-             n_new=N_NEW, scalar_layers=np.array(list(SCALARS), np.int32),
+    # the float path end to end: ENGINE_PREFILL_INT8=0 and ENGINE_DECODE_INT8=0 (the reference's
+    # fused float tasks for the MLP and the per-layer embeddings, :1267-1269, 1365-1366, 1380-1382)
+    fgens = [run_engine(binary, d, p, N_NEW, dict(env, ENGINE_K="0", ENGINE_PREFILL_INT8="0",
+                                                  ENGINE_DECODE_INT8="0"))[0] for p in ps]
+    f = e2b_oracle(prefill_int8=0, decode_int8=0)
+    fours = [[int(t) for t in f.generate(p, N_NEW)[0]] for p in ps]
+    f.close()
+    for g, o in zip(fgens, fours):
+        print("reference (float):", g, "\noracle (float):   ", o)
+
+    def pad(gs):
+        tok = np.full((N_REQ, max(len(g) for g in gs)), -1, np.int32)
+        for i, g in enumerate(gs):
+            tok[i, :len(g)] = g
+        return tok
+    np.savez(HERE / "e2e_e2b_ref.npz", prompts=np.stack([np.asarray(p, np.int32) for p in ps]), tokens=pad(gens),
+             tokens_float=pad(fgens), seed=SEED, n_new=N_NEW, scalar_layers=np.array(list(SCALARS), np.int32),
              scalar_values=np.array(list(SCALARS.values()), np.float32))
     print("greedy: agree" if ours == gens else "greedy: DIFFER")
+    print("greedy float: agree" if fours == fgens else "greedy float: DIFFER")
 
 
 def spec(binary, d, env):

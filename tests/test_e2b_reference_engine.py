@@ -133,3 +133,17 @@ def test_the_comparison_can_fail(fixture):
         assert int(m.generate(fixture["prompts"][i], 1)[0][0]) != int(fixture["tokens"][i][0])
     finally:
         m.close()
+
+
+def test_oracle_matches_the_reference_engine_on_the_float_path(fixture):
+    """ENGINE_PREFILL_INT8=0 and ENGINE_DECODE_INT8=0: the reference runs its fused float tasks for
+    the MLP and the per-layer embeddings; the oracle's float linears around the same element-wise
+    steps give the engine's tokens, which differ from the int8 path's on this prompt."""
+    i = CHECKED[0]
+    want = [int(t) for t in fixture["tokens_float"][i] if t >= 0]
+    assert want != [int(t) for t in fixture["tokens"][i] if t >= 0]
+    m = golden.e2b_oracle(prefill_int8=0, decode_int8=0)
+    try:
+        assert [int(t) for t in m.generate(fixture["prompts"][i], golden.N_NEW)[0]] == want
+    finally:
+        m.close()
